@@ -1,0 +1,201 @@
+/*
+ * mira_cuda.h - C ABI of libmira_cuda.so, the B200 (sm_100a) execution library behind MIRA's
+ * `cuda` target for the W8A8 path (`mira run ... -t cuda --quantize w8a8`).
+ *
+ * Every entry point takes plain pointers and sizes; device pointers come from mira_cuda_malloc.
+ * Every entry point returns 0 on success or a non-zero MIRA_CUDA_E* status; the message of the
+ * last failure on the calling thread is available through mira_cuda_last_error.  Launch entry
+ * points are asynchronous on the library's stream for the current device (mira_cuda_set_device);
+ * mira_cuda_sync waits for it and reports any error a kernel recorded on the device.
+ *
+ * The reference implements all of this in NumPy inside its op registry; each kernel entry point
+ * names the reference function (path within the myramay/MIRA project, file:line) it replaces.
+ *
+ * Layouts.  4-D activations live on the device as NHWC ("channels last") with the channel count
+ * padded to a multiple of 16 for int8 tensors (padding channels hold 0).  2-D int8 activations
+ * [M, K] have a row stride of round_up(K, 16) bytes, padding bytes hold 0.  int8 weights are
+ * K-major: qmatmul weights [N, Kp] (the transpose of the reference's [K, N] attr "q"), qconv2d
+ * weights [O, KH, KW, Cp] flattened to [O, Kp] with Kp = round_up(KH*KW*Cp, 16).
+ */
+#ifndef MIRA_CUDA_H
+#define MIRA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MIRA_CUDA_ABI_VERSION 1
+
+/* status codes */
+#define MIRA_CUDA_OK 0
+#define MIRA_CUDA_EINVAL 1      /* bad argument (shape, stride, alignment, unsupported case) */
+#define MIRA_CUDA_ECUDA 2       /* a CUDA runtime/driver call failed */
+#define MIRA_CUDA_ENODEV 3      /* no usable sm_100 device */
+#define MIRA_CUDA_EKERNEL 4     /* a kernel recorded an error (bounded wait expired, bad index) */
+
+/* epilogue step opcodes: reference ops.py:99-139 (UNARY/BINARY tables) restricted to
+ * passes.py:151-152 (FUSABLE_UNARY / FUSABLE_BINARY) */
+#define MIRA_EPI_RELU 1
+#define MIRA_EPI_GELU 2
+#define MIRA_EPI_SIGMOID 3
+#define MIRA_EPI_TANH 4
+#define MIRA_EPI_ADD 16
+#define MIRA_EPI_SUB 17
+#define MIRA_EPI_MUL 18
+#define MIRA_EPI_DIV 19
+#define MIRA_EPI_MAXIMUM 20
+#define MIRA_EPI_MINIMUM 21
+
+/* how a binary step's operand broadcasts against the [M, N] result (M = rows, N = channels) */
+#define MIRA_OPND_NONE 0        /* unary step */
+#define MIRA_OPND_SCALAR 1      /* one value: `scalar` */
+#define MIRA_OPND_CHANNEL 2     /* ptr[n], padded by the caller to a multiple of 256 floats */
+#define MIRA_OPND_FULL 3        /* ptr[m * ld + n] */
+#define MIRA_OPND_ROW 4         /* ptr[m] */
+
+#define MIRA_EPI_MAX_STEPS 8
+
+typedef struct mira_epi_step {
+  int32_t op;         /* MIRA_EPI_* */
+  int32_t operand;    /* MIRA_OPND_* */
+  int32_t swapped;    /* 1: f(operand, acc) instead of f(acc, operand) (reference ops.py:192-199) */
+  float scalar;       /* MIRA_OPND_SCALAR value */
+  const float* ptr;   /* device pointer for CHANNEL / FULL / ROW */
+  int64_t ld;         /* row stride (elements) for FULL */
+} mira_epi_step;
+
+/* The fused epilogue of a quantized matmul/conv.  The dequantized f32 value
+ * y = f32(f64(acc) * S) goes through the steps in order, then is written as f32 (out_f32) and/or
+ * requantized for the next int8 op: clip(round_half_even(f32(y / out_scale)), -127, 127) (out_i8). */
+typedef struct mira_epilogue {
+  int32_t n_steps;
+  mira_epi_step steps[MIRA_EPI_MAX_STEPS];
+  float* out_f32;     /* may be NULL */
+  int64_t ld_f32;     /* elements */
+  int8_t* out_i8;     /* may be NULL */
+  int64_t ld_i8;      /* bytes, multiple of 16; columns [N, ld_i8) are written as 0 */
+  float out_scale;    /* np.float32(x_scale) of the consumer of out_i8 */
+} mira_epilogue;
+
+/* Dequant scales.  Per-channel mode (qmatmul / qconv2d): S[n] = f64(x_scale) * f64(w_scale[n]),
+ * the reference's combined scale (ops.py:619, ops.py:633).  The caller passes it as device arrays
+ * padded to a multiple of 256 entries: scale64[n] = S[n] (double), scale_hi[n] = f32(S[n]) and
+ * scale_lo[n] = f32(S[n] - scale_hi[n]) (round-to-nearest conversions).  Row/column mode (the
+ * standalone GEMM sweep): S[m, n] = f64(row_scale[m]) * f64(col_scale[n]). */
+typedef struct mira_dequant {
+  const double* scale64;    /* per-channel mode when non-NULL */
+  const float* scale_hi;
+  const float* scale_lo;
+  const float* row_scale;   /* row/column mode */
+  const float* col_scale;
+} mira_dequant;
+
+/* ---------------------------------------------------------------- runtime */
+
+int mira_cuda_abi_version(void);
+/* Copies the message of the last failure on this thread into buf (always NUL-terminated). */
+int mira_cuda_last_error(char* buf, size_t n);
+/* Number of visible CUDA devices (0 without a GPU; never fails). */
+int mira_cuda_device_count(void);
+/* Selects the device for this thread and sets up its stream and helpers on first use. */
+int mira_cuda_set_device(int device);
+/* SM count and compute capability of the current device. */
+int mira_cuda_device_info(int* sm_count, int* cc_major, int* cc_minor);
+int mira_cuda_malloc(void** ptr, size_t bytes);
+int mira_cuda_free(void* ptr);
+int mira_cuda_host_alloc(void** ptr, size_t bytes);   /* pinned host memory */
+int mira_cuda_host_free(void* ptr);
+int mira_cuda_memset(void* dst, int value, size_t bytes);                 /* async */
+int mira_cuda_h2d(void* dst, const void* src, size_t bytes);               /* async */
+int mira_cuda_d2h(void* dst, const void* src, size_t bytes);               /* async */
+int mira_cuda_d2d(void* dst, const void* src, size_t bytes);               /* async */
+/* Waits for the current device's stream; returns MIRA_CUDA_EKERNEL if a kernel recorded an
+ * error since the last call (the record is cleared). */
+int mira_cuda_sync(void);
+/* The cudaStream_t of the current device, for callers that time with events on it. */
+int mira_cuda_get_stream(void** stream);
+/* Events on the library stream: create, record, elapsed milliseconds between two, destroy. */
+int mira_cuda_event_create(void** ev);
+int mira_cuda_event_record(void* ev);
+int mira_cuda_event_elapsed(void* start, void* end, float* ms);
+int mira_cuda_event_destroy(void* ev);
+/* CUDA graph capture of the launches issued on the library stream between begin and end. */
+int mira_cuda_graph_begin(void);
+int mira_cuda_graph_end(void** graph_exec);
+int mira_cuda_graph_launch(void* graph_exec);
+int mira_cuda_graph_destroy(void* graph_exec);
+/* Number of kernels this library launched on the current thread (all devices). */
+int64_t mira_cuda_launch_count(void);
+
+/* ---------------------------------------------------------------- kernels */
+
+/* Activation quantization, reference ops.py:602-603 (quantize_activation):
+ *   xq = clip(round_half_even(f32(x) / f32(scale)), -127, 127).
+ * x: f32 [rows, cols] with row stride ld_x (elements); xq: int8 [rows, ld_q], ld_q >= cols,
+ * columns [cols, ld_q) written as 0. */
+int mira_cuda_quantize_rows(const float* x, int64_t rows, int64_t cols, int64_t ld_x,
+                            float scale, int8_t* xq, int64_t ld_q);
+
+/* Quantization of an NCHW f32 tensor into NHWC int8 with Cp >= C channels (extra channels 0).
+ * Also reference ops.py:602-603; the layout change is this library's. */
+int mira_cuda_quantize_nchw_to_nhwc(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
+                                    float scale, int8_t* xq, int64_t cp);
+
+/* W8A8 matmul, reference ops.py:616-620 (_qmatmul_ref) with the epilogue of ops.py:192-199:
+ *   acc[m, n] = sum_k A[m, k] * B[n, k]   (exact int32)
+ *   y = epilogue(f32(f64(acc) * S))        (S from `dq`)
+ * A: int8 [M, lda] (lda = round_up(K, 16)); B: int8 [N, ldb] K-major (ldb = round_up(K, 16)).
+ * Runs on tcgen05.mma kind::i8 with TMEM accumulators and TMA-staged shared-memory tiles. */
+int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda,
+                    const int8_t* B, int64_t ldb, const mira_dequant* dq,
+                    const mira_epilogue* epi);
+
+/* W8A8 convolution as an implicit GEMM over NHWC int8, reference ops.py:630-634 (_qconv2d_ref,
+ * through _conv2d_ref ops.py:265-276 with groups = 1).
+ * x: int8 NHWC [n, h, w, cp] (cp multiple of 4; 16 unless cp == 4); weights: int8 [o, ldw] with
+ * k = (i * kw + j) * cp + c, ldw = round_up(kh*kw*cp, 16).  The result [n*oh*ow, o] (NHWC) goes
+ * through the same epilogue as mira_cuda_qgemm. */
+int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x,
+                      int64_t o, int64_t kh, int64_t kw, const int8_t* wq, int64_t ldw,
+                      int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                      int64_t dil_h, int64_t dil_w, const mira_dequant* dq,
+                      const mira_epilogue* epi);
+
+/* Max pooling over NHWC, reference ops.py:293-296 (maxpool2d) preceded by an optional constant
+ * pad (ops.py:469-470) of `pad` pixels holding `pad_value` (the -inf pad in front of ResNet's
+ * pool).  f32 in -> f32 out (out_f32) and/or int8 out; int8 in (x_i8 non-NULL) -> int8 out,
+ * which equals quantize(maxpool(x)) because quantization is monotone. */
+int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, int64_t n, int64_t h,
+                             int64_t w, int64_t c, int64_t ldc_in, int64_t size, int64_t stride,
+                             int64_t pad, float pad_value, float* out_f32, int64_t ldc_out_f32,
+                             int8_t* out_i8, int64_t ldc_out_i8, float out_scale);
+
+/* Mean over H and W of NHWC f32 (reference ops.py:318-343 reduce_mean over axes (2, 3)), summed
+ * in NumPy's pairwise order so the f32 result is bit-identical; optional f32 and int8 outputs
+ * [n, c] (int8 rows padded to ld_i8). */
+int mira_cuda_mean_hw_nhwc(const float* x, int64_t n, int64_t hw, int64_t c, int64_t ldc,
+                           float* out_f32, int8_t* out_i8, int64_t ld_i8, float out_scale);
+
+/* Depthwise f32 convolution over NHWC (reference ops.py:265-276 _conv2d_ref with
+ * groups == channels, which the reference never quantizes, quantize.py:105-106): per-tap f32
+ * products summed in (i, j) order from 0, then the epilogue on [n*oh*ow, c]. weights f32
+ * [kh*kw, c] (tap-major). */
+int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
+                            const float* wt, int64_t kh, int64_t kw, int64_t stride_h,
+                            int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h,
+                            int64_t dil_w, const mira_epilogue* epi);
+
+/* Layout changes between the reference's NCHW f32 tensors and the device's NHWC. */
+int mira_cuda_nchw_to_nhwc_f32(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
+                               float* y, int64_t ldc);
+int mira_cuda_nhwc_to_nchw_f32(const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
+                               int64_t ldc, float* y);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MIRA_CUDA_H */

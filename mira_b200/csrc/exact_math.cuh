@@ -1,0 +1,112 @@
+// Exact f32 arithmetic shared by the kernels, written so that results are bit-identical to the
+// reference's NumPy semantics:
+//   dequant      y  = float32(float64(acc) * S)          reference ops.py:619 and ops.py:633
+//   quantize     q  = clip(rint(float32(y / s)), -127, 127)   reference ops.py:602-603
+//   epilogue     NumPy float32 add/sub/mul/div/maximum/minimum   reference ops.py:192-199
+// No contraction: every operation below is an explicitly rounded intrinsic.
+#pragma once
+#include <cstdint>
+
+#include "../../include/mira_cuda.h"
+
+namespace mira {
+
+// float32(float64(acc) * S) without 64-bit conversions on the fast path.
+//
+// S (a double) is split as S = hi + lo + r with hi = f32(S), lo = f32(S - hi), |r| <= |S| 2^-48.
+// For |acc| < 2^22, a = float(acc) is exact (magic-number conversion) and
+//     D = a*hi + f32(a*lo)            (one FFMA: the product a*hi is exact inside the FMA)
+// is within |acc*S| 2^-46 of the true product X = acc*S.  float32(float64(X)) equals RN32(X)
+// unless an f32 rounding midpoint lies within |X| 2^-53 of X, and RN32(D) equals RN32(X) unless a
+// midpoint lies between D and X.  So if RN32(D - d) == RN32(D + d) with d = |a| hi 2^-40 (far
+// larger than both distances), no midpoint is near and RN32(D) is the exact answer.  Otherwise
+// (about 2 in 10^5 elements, or |acc| >= 2^22) the product is done in float64 like the reference.
+// Fast path of the above; returns false when the float64 product is needed.
+__device__ __forceinline__ bool dequant_fast(int32_t acc, float hi, float lo, float& y) {
+  const uint32_t biased = static_cast<uint32_t>(acc) + (1u << 22);
+  if (biased >= (1u << 23)) return false;
+  const float a = __fsub_rn(__int_as_float(0x4B400000 + acc), 12582912.0f);
+  const float p = __fmul_rn(a, lo);
+  const float d = __fmul_rn(fabsf(a), __fmul_rn(hi, 0x1p-40f));
+  const float y_lo = __fmaf_rn(a, hi, __fsub_rn(p, d));
+  const float y_hi = __fmaf_rn(a, hi, __fadd_rn(p, d));
+  y = y_lo;
+  return y_lo == y_hi;
+}
+
+// Row/column scales: S = f64(r) * f64(c) is exact in float64 (24 + 24 significant bits), and
+// so is its split hi = f32(r*c), lo = r*c - hi (the FMA residual).
+__device__ __forceinline__ void split_rowcol(float r, float c, float& hi, float& lo) {
+  hi = __fmul_rn(r, c);
+  lo = __fmaf_rn(r, c, -hi);
+}
+
+// RN32(y / s) from a precomputed correctly-rounded reciprocal rcp = RN32(1/s): q0 = RN(y*rcp) is
+// within one ulp, the residual y - q0*s is exact in one FMA, and RN(q0 + res*rcp) is the correctly
+// rounded quotient (Markstein's theorem).  y is first clamped to +-256 s, which cannot change a
+// result that is clipped to +-127 afterwards and keeps every intermediate finite.
+__device__ __forceinline__ float div_by_scale(float y, float s, float rcp, float lim) {
+  y = fminf(fmaxf(y, -lim), lim);
+  const float q0 = __fmul_rn(y, rcp);
+  const float res = __fmaf_rn(-q0, s, y);
+  return __fmaf_rn(res, rcp, q0);
+}
+
+// clip(rint(z), -127, 127) as an int8 in the low byte of the returned word: clipping before
+// rounding is equivalent because +-127 are integers; z + 1.5*2^23 rounds z half-to-even into the
+// low mantissa bits.
+__device__ __forceinline__ uint32_t round_clip_i8(float z) {
+  z = fminf(fmaxf(z, -127.0f), 127.0f);
+  return static_cast<uint32_t>(__float_as_int(__fadd_rn(z, 12582912.0f)));
+}
+
+__device__ __forceinline__ uint32_t pack4_i8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  const uint32_t ab = __byte_perm(a, b, 0x0040);
+  const uint32_t cd = __byte_perm(c, d, 0x0040);
+  return __byte_perm(ab, cd, 0x5410);
+}
+
+// NumPy float32 maximum/minimum (NaN propagates from either side).
+__device__ __forceinline__ float np_maximum(float a, float b) {
+  return (a >= b || a != a) ? a : b;
+}
+__device__ __forceinline__ float np_minimum(float a, float b) {
+  return (a <= b || a != a) ? a : b;
+}
+
+// Reference ops.py:94-96 (tanh form of GELU), evaluated in the same order in float32.  tanhf and
+// expf are CUDA's; NumPy's own float32 tanh/exp differ in the last bits, so steps that use them
+// match the reference within a tolerance, not bit for bit.
+__device__ __forceinline__ float gelu_f32(float x) {
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(0.044715f, x3)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+__device__ __forceinline__ float sigmoid_f32(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+}
+
+__device__ __forceinline__ float apply_unary(int op, float v) {
+  switch (op) {
+    case MIRA_EPI_RELU: return np_maximum(v, 0.0f);
+    case MIRA_EPI_GELU: return gelu_f32(v);
+    case MIRA_EPI_SIGMOID: return sigmoid_f32(v);
+    case MIRA_EPI_TANH: return tanhf(v);
+    default: return v;
+  }
+}
+
+__device__ __forceinline__ float apply_binary(int op, float a, float b) {
+  switch (op) {
+    case MIRA_EPI_ADD: return __fadd_rn(a, b);
+    case MIRA_EPI_SUB: return __fsub_rn(a, b);
+    case MIRA_EPI_MUL: return __fmul_rn(a, b);
+    case MIRA_EPI_DIV: return __fdiv_rn(a, b);
+    case MIRA_EPI_MAXIMUM: return np_maximum(a, b);
+    case MIRA_EPI_MINIMUM: return np_minimum(a, b);
+    default: return a;
+  }
+}
+
+}  // namespace mira

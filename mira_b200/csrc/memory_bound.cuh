@@ -1,0 +1,315 @@
+// K3/K4/K5: the memory-bound kernels around the int8 GEMMs: activation quantization (with the
+// NCHW -> NHWC layout change at graph inputs), max pooling, the global mean, the f32 depthwise
+// convolution, and the f32 layout changes at graph outputs.  All are 128-bit vectorised where the
+// layout allows and use the exact rounding helpers of exact_math.cuh.
+#pragma once
+#include <cstdint>
+
+#include "exact_math.cuh"
+
+namespace mira {
+
+struct QuantScale {
+  float s, rcp, lim;   // divisor, RN32(1/divisor), 256 * divisor
+};
+
+__device__ __forceinline__ uint32_t quant_byte(float x, const QuantScale& q) {
+  return round_clip_i8(div_by_scale(x, q.s, q.rcp, q.lim));
+}
+
+// ---------------------------------------------------------------- K3: quantize rows
+
+// One thread per 16 output bytes of a row: xq[r, c0:c0+16] from x[r, c0:c0+16] (0 past `cols`).
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t ld_x,
+                                     QuantScale q, int8_t* __restrict__ xq, int64_t ld_q) {
+  const int64_t groups = ld_q / 16;
+  const int64_t total = rows * groups;
+  const bool vec = (ld_x % 4) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / groups;
+    const int64_t c0 = (idx - r * groups) * 16;
+    const float* src = x + r * ld_x + c0;
+    float v[16];
+    if (vec && c0 + 16 <= cols) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(src) + k);
+        v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = (c0 + k < cols) ? src[k] : 0.0f;
+    }
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t b[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) b[e] = (c0 + 4 * k + e < cols) ? quant_byte(v[4 * k + e], q) : 0u;
+      w[k] = pack4_i8(b[0], b[1], b[2], b[3]);
+    }
+    *reinterpret_cast<uint4*>(xq + r * ld_q + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// ---------------------------------------------------------------- K3: quantize NCHW -> NHWC
+
+// One thread per (pixel, group of 4 output channels): reads are coalesced along W for each
+// channel plane, writes are one 32-bit word per thread.
+__global__ void quantize_nchw_nhwc_kernel(const float* __restrict__ x, int64_t n, int64_t c, int64_t hw,
+                                          QuantScale q, int8_t* __restrict__ xq, int64_t cp) {
+  const int64_t g4 = cp / 4;
+  const int64_t total = n * hw * g4;
+  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    // pixel-fastest order so neighbouring threads read neighbouring pixels
+    const int64_t pix_all = n * hw;
+    const int64_t grp = idx / pix_all;
+    const int64_t pix = idx - grp * pix_all;
+    const int64_t img = pix / hw;
+    const int64_t p = pix - img * hw;
+    uint32_t b[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int64_t ch = grp * 4 + e;
+      b[e] = ch < c ? quant_byte(__ldg(x + (img * c + ch) * hw + p), q) : 0u;
+    }
+    *reinterpret_cast<uint32_t*>(xq + pix * cp + grp * 4) = pack4_i8(b[0], b[1], b[2], b[3]);
+  }
+}
+
+// ---------------------------------------------------------------- K5: max pooling (NHWC)
+
+// f32 input: one thread per (output pixel, 4 channels).  Padding pixels take `pad_value` (the
+// reference pads with -inf before pooling).  Writes f32 and/or the quantized int8 value.
+__global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, int w, int c, int64_t ldc,
+                                   int size, int stride, int pad, float pad_value, int oh, int ow,
+                                   float* __restrict__ out, int64_t ldo, int8_t* __restrict__ out_i8,
+                                   int64_t ldo_i8, QuantScale q) {
+  const int c4 = (c + 3) / 4;
+  const int64_t total = int64_t(n) * oh * ow * c4;
+  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int cg = static_cast<int>(idx % c4);
+    const int64_t pix = idx / c4;
+    const int img = static_cast<int>(pix / (int64_t(oh) * ow));
+    const int rem = static_cast<int>(pix - int64_t(img) * oh * ow);
+    const int oy = rem / ow, ox = rem - (rem / ow) * ow;
+    float mx[4];
+    bool first = true;
+    for (int i = 0; i < size; ++i) {
+      const int iy = oy * stride + i - pad;
+      for (int j = 0; j < size; ++j) {
+        const int ix = ox * stride + j - pad;
+        float v[4];
+        if (iy < 0 || iy >= h || ix < 0 || ix >= w) {
+          v[0] = v[1] = v[2] = v[3] = pad_value;
+        } else {
+          const float* src = x + (int64_t(img) * h * w + int64_t(iy) * w + ix) * ldc + cg * 4;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = (cg * 4 + e < c) ? src[e] : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mx[e] = first ? v[e] : np_maximum(mx[e], v[e]);
+        first = false;
+      }
+    }
+    if (out != nullptr) {
+      float* dst = out + pix * ldo + cg * 4;
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (cg * 4 + e < c) dst[e] = mx[e];
+    }
+    if (out_i8 != nullptr) {
+      uint32_t b[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) b[e] = (cg * 4 + e < c) ? quant_byte(mx[e], q) : 0u;
+      *reinterpret_cast<uint32_t*>(out_i8 + pix * ldo_i8 + cg * 4) = pack4_i8(b[0], b[1], b[2], b[3]);
+    }
+  }
+}
+
+// int8 input (already quantized with the output's scale): quantize(max(x)) == max(quantize(x)),
+// so pooling the int8 values gives the reference's int8 result.  One thread per 16 channels.
+__global__ void maxpool_i8_kernel(const int8_t* __restrict__ x, int n, int h, int w, int64_t cp, int size,
+                                  int stride, int pad, int8_t pad_q, int oh, int ow, int8_t* __restrict__ out,
+                                  int64_t ldo) {
+  const int64_t c16 = cp / 16;
+  const int64_t total = int64_t(n) * oh * ow * c16;
+  const uint32_t padw = 0x01010101u * static_cast<uint8_t>(pad_q);
+  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t cg = idx % c16;
+    const int64_t pix = idx / c16;
+    const int img = static_cast<int>(pix / (int64_t(oh) * ow));
+    const int rem = static_cast<int>(pix - int64_t(img) * oh * ow);
+    const int oy = rem / ow, ox = rem - (rem / ow) * ow;
+    uint4 mx = make_uint4(0x81818181u, 0x81818181u, 0x81818181u, 0x81818181u);  // -127
+    for (int i = 0; i < size; ++i) {
+      const int iy = oy * stride + i - pad;
+      for (int j = 0; j < size; ++j) {
+        const int ix = ox * stride + j - pad;
+        uint4 v;
+        if (iy < 0 || iy >= h || ix < 0 || ix >= w) {
+          v = make_uint4(padw, padw, padw, padw);
+        } else {
+          v = __ldg(reinterpret_cast<const uint4*>(x + (int64_t(img) * h * w + int64_t(iy) * w + ix) * cp) + cg);
+        }
+        mx.x = __vmaxs4(mx.x, v.x);
+        mx.y = __vmaxs4(mx.y, v.y);
+        mx.z = __vmaxs4(mx.z, v.z);
+        mx.w = __vmaxs4(mx.w, v.w);
+      }
+    }
+    reinterpret_cast<uint4*>(out + pix * ldo)[cg] = mx;
+  }
+}
+
+// ---------------------------------------------------------------- K5: mean over H*W (NHWC)
+
+// NumPy's float32 pairwise summation (numpy/_core/src/umath/loops_utils.h.src, pairwise_sum):
+// below 8 elements a plain loop; up to 128 eight interleaved partial sums combined as
+// ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) plus a sequential tail; above 128 a split at
+// n/2 rounded down to a multiple of 8.
+__device__ float pairwise_block(const float* __restrict__ x, int n, int64_t stride) {
+  if (n < 8) {
+    float r = 0.0f;
+    for (int i = 0; i < n; ++i) r = __fadd_rn(r, x[i * stride]);
+    return r;
+  }
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = x[j * stride];
+  int i = 8;
+  for (; i < n - (n % 8); i += 8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], x[(i + j) * stride]);
+  }
+  float r = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])),
+                      __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7])));
+  for (; i < n; ++i) r = __fadd_rn(r, x[i * stride]);
+  return r;
+}
+
+__device__ float pairwise_sum(const float* __restrict__ x, int n, int64_t stride) {
+  if (n <= 128) return pairwise_block(x, n, stride);
+  int n2 = n / 2;
+  n2 -= n2 % 8;
+  return __fadd_rn(pairwise_sum(x, n2, stride), pairwise_sum(x + n2 * stride, n - n2, stride));
+}
+
+__global__ void mean_hw_kernel(const float* __restrict__ x, int n, int hw, int c, int64_t ldc,
+                               float* __restrict__ out, int8_t* __restrict__ out_i8, int64_t ld_i8, QuantScale q) {
+  const int64_t total = int64_t(n) * c;
+  const float count = static_cast<float>(hw);
+  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int img = static_cast<int>(idx / c);
+    const int ch = static_cast<int>(idx - int64_t(img) * c);
+    const float s = pairwise_sum(x + int64_t(img) * hw * ldc + ch, hw, ldc);
+    const float mean = __fdiv_rn(s, count);
+    if (out != nullptr) out[idx] = mean;
+    if (out_i8 != nullptr) out_i8[int64_t(img) * ld_i8 + ch] = static_cast<int8_t>(quant_byte(mean, q) & 0xff);
+  }
+}
+
+// zero the int8 padding columns [c, ld_i8) of each row
+__global__ void zero_pad_cols_kernel(int8_t* __restrict__ y, int64_t rows, int64_t c, int64_t ld) {
+  const int64_t w = ld - c;
+  const int64_t total = rows * w;
+  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / w;
+    y[r * ld + c + (idx - r * w)] = 0;
+  }
+}
+
+// ---------------------------------------------------------------- K4: depthwise f32 conv (NHWC)
+
+struct DwParams {
+  int n, h, w, c, oh, ow, kh, kw, sh, sw, ph, pw, dh, dw;
+  int n_steps;
+  mira_epi_step steps[MIRA_EPI_MAX_STEPS];
+  float* out_f32;
+  int64_t ld_f32;
+  int8_t* out_i8;
+  int64_t ld_i8;
+  QuantScale q;
+};
+
+// One thread per (output pixel, channel): per-tap products added in (i, j) order starting from
+// 0 (reference _conv2d_ref: one einsum term per tap, `acc +=`), padded taps skipped (they add
+// exact zeros), then the epilogue.  Threads run channel-fastest so x and w reads coalesce.
+__global__ void dwconv_kernel(const float* __restrict__ x, const float* __restrict__ wt, const __grid_constant__ DwParams p) {
+  const int64_t total = int64_t(p.n) * p.oh * p.ow * p.c;
+  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int ch = static_cast<int>(idx % p.c);
+    const int64_t pix = idx / p.c;
+    const int img = static_cast<int>(pix / (int64_t(p.oh) * p.ow));
+    const int rem = static_cast<int>(pix - int64_t(img) * p.oh * p.ow);
+    const int oy = rem / p.ow, ox = rem - (rem / p.ow) * p.ow;
+    float acc = 0.0f;
+    for (int i = 0; i < p.kh; ++i) {
+      const int iy = oy * p.sh - p.ph + i * p.dh;
+      for (int j = 0; j < p.kw; ++j) {
+        const int ix = ox * p.sw - p.pw + j * p.dw;
+        if (iy < 0 || iy >= p.h || ix < 0 || ix >= p.w) continue;
+        const float xv = __ldg(x + ((int64_t(img) * p.h + iy) * p.w + ix) * p.c + ch);
+        acc = __fadd_rn(acc, __fmul_rn(xv, __ldg(wt + (i * p.kw + j) * p.c + ch)));
+      }
+    }
+    float v = acc;
+    for (int s = 0; s < p.n_steps; ++s) {
+      const mira_epi_step& st = p.steps[s];
+      if (st.operand == MIRA_OPND_NONE) {
+        v = apply_unary(st.op, v);
+        continue;
+      }
+      float o;
+      if (st.operand == MIRA_OPND_SCALAR) o = st.scalar;
+      else if (st.operand == MIRA_OPND_CHANNEL) o = __ldg(st.ptr + ch);
+      else if (st.operand == MIRA_OPND_ROW) o = st.ptr[pix];
+      else o = st.ptr[pix * st.ld + ch];
+      v = st.swapped ? apply_binary(st.op, o, v) : apply_binary(st.op, v, o);
+    }
+    if (p.out_f32 != nullptr) p.out_f32[pix * p.ld_f32 + ch] = v;
+    if (p.out_i8 != nullptr) p.out_i8[pix * p.ld_i8 + ch] = static_cast<int8_t>(quant_byte(v, p.q) & 0xff);
+  }
+}
+
+// ---------------------------------------------------------------- layout changes (f32)
+
+// NCHW -> NHWC through a 32x32 shared-memory tile per (image, 32 channels, 32 pixels).
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int c, int hw, float* __restrict__ y, int64_t ldc) {
+  __shared__ float tile[32][33];
+  const int img = blockIdx.z;
+  const int c0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int ch = c0 + k, p = p0 + threadIdx.x;
+    tile[k][threadIdx.x] = (ch < c && p < hw) ? x[(int64_t(img) * c + ch) * hw + p] : 0.0f;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int p = p0 + k, ch = c0 + threadIdx.x;
+    if (p < hw && ch < c) y[(int64_t(img) * hw + p) * ldc + ch] = tile[threadIdx.x][k];
+  }
+}
+
+__global__ void nhwc_to_nchw_kernel(const float* __restrict__ x, int c, int hw, int64_t ldc, float* __restrict__ y) {
+  __shared__ float tile[32][33];
+  const int img = blockIdx.z;
+  const int c0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int p = p0 + k, ch = c0 + threadIdx.x;
+    tile[k][threadIdx.x] = (p < hw && ch < c) ? x[(int64_t(img) * hw + p) * ldc + ch] : 0.0f;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int ch = c0 + k, p = p0 + threadIdx.x;
+    if (ch < c && p < hw) y[(int64_t(img) * c + ch) * hw + p] = tile[threadIdx.x][k];
+  }
+}
+
+}  // namespace mira

@@ -1,0 +1,580 @@
+// libmira_cuda.so: the C ABI declared in include/mira_cuda.h.  One translation unit so that the
+// kernels, the device-side error record and the host wrappers share one module.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/mira_cuda.h"
+#include "memory_bound.cuh"
+#include "qgemm_sm100.cuh"
+#include "runtime.h"
+
+// Set by a kernel that gave up on a bounded wait or met an impossible index; read and cleared by
+// mira_cuda_sync.  One copy per device (module global).
+__device__ int g_mira_kernel_error;
+
+namespace mira {
+
+namespace {
+
+constexpr int kMaxDevices = 16;
+DeviceState g_devices[kMaxDevices];
+int* g_err_ptr[kMaxDevices];
+std::mutex g_init_mutex;
+thread_local int t_device = -1;
+thread_local std::string t_last_error;
+std::atomic<int64_t> g_launches{0};
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+
+int init_device(int d) {
+  std::lock_guard<std::mutex> lock(g_init_mutex);
+  DeviceState& st = g_devices[d];
+  if (st.ready) return MIRA_CUDA_OK;
+  MIRA_CUDA_TRY(cudaSetDevice(d), "cudaSetDevice");
+  cudaDeviceProp prop;
+  MIRA_CUDA_TRY(cudaGetDeviceProperties(&prop, d), "cudaGetDeviceProperties");
+  if (prop.major != 10) {
+    return set_error(MIRA_CUDA_ENODEV, "device " + std::to_string(d) + " is sm_" + std::to_string(prop.major) +
+                                           std::to_string(prop.minor) + "; this library is built for sm_100a");
+  }
+  st.device = d;
+  st.sm_count = prop.multiProcessorCount;
+  st.cc_major = prop.major;
+  st.cc_minor = prop.minor;
+  MIRA_CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  void* err_ptr = nullptr;
+  MIRA_CUDA_TRY(cudaGetSymbolAddress(&err_ptr, g_mira_kernel_error), "cudaGetSymbolAddress(error record)");
+  g_err_ptr[d] = static_cast<int*>(err_ptr);
+  const int zero = 0;
+  MIRA_CUDA_TRY(cudaMemcpyToSymbol(g_mira_kernel_error, &zero, sizeof(int)), "clear error record");
+  if (g_encode_tiled == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    MIRA_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q),
+                  "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+    if (q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  st.ready = true;
+  return MIRA_CUDA_OK;
+}
+
+}  // namespace
+
+DeviceState* current_device() {
+  if (t_device < 0) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return nullptr;
+    t_device = 0;
+  }
+  if (!g_devices[t_device].ready) {
+    if (init_device(t_device) != MIRA_CUDA_OK) return nullptr;
+  }
+  if (cudaSetDevice(t_device) != cudaSuccess) return nullptr;
+  return &g_devices[t_device];
+}
+
+int set_error(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  return set_error(MIRA_CUDA_ECUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int after_launch(const char* kernel) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, kernel);
+  count_launch();
+  return MIRA_CUDA_OK;
+}
+
+static int* device_err_ptr() { return g_err_ptr[t_device]; }
+
+static QuantScale make_qscale(float s) {
+  QuantScale q;
+  q.s = s;
+  q.rcp = 1.0f / s;          // correctly rounded (IEEE division on the host)
+  q.lim = 256.0f * s;        // exact (power of two)
+  return q;
+}
+
+// clip(rint(v / s), -127, 127) on the host, for constant pad values (-inf gives -127).
+static uint32_t quant_byte_host(float v, float s) {
+  float z = v / s;
+  if (z != z) z = 0.0f;
+  z = std::fmin(std::fmax(z, -127.0f), 127.0f);
+  return static_cast<uint32_t>(static_cast<int32_t>(std::nearbyint(z))) & 0xffu;
+}
+
+static int grid_for(const DeviceState* dev, int64_t work, int threads) {
+  int64_t blocks = (work + threads - 1) / threads;
+  const int64_t cap = int64_t(dev->sm_count) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+// ---------------------------------------------------------------- tensor maps
+
+static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t row_stride,
+                        uint32_t box_inner, uint32_t box_rows) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return set_error(MIRA_CUDA_EINVAL, "TMA base not 16-byte aligned");
+  if (row_stride % 16 != 0) return set_error(MIRA_CUDA_EINVAL, "TMA row stride not a multiple of 16 bytes");
+  const cuuint64_t dims[2] = {inner_bytes, rows};
+  const cuuint64_t strides[1] = {row_stride};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return MIRA_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- qgemm dispatch
+
+template <int BN, int STAGES, int AMODE, bool ROWCOL>
+static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, const QgParams& p) {
+  using Cfg = QgCfg<BN, STAGES, AMODE>;
+  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL>;
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[dev->device]) {
+    MIRA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM)),
+                  "cudaFuncSetAttribute(qgemm smem)");
+    attr_set[dev->device] = true;
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, dev->stream>>>(tmA, tmB, p);
+  return after_launch("qgemm_sm100_kernel");
+}
+
+template <int AMODE, bool ROWCOL>
+static int launch_qgemm_bn(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, QgParams& p, int bn) {
+  switch (bn) {
+    case 64: return launch_qgemm_cfg<64, 8, AMODE, ROWCOL>(dev, tmA, tmB, p);
+    case 128: return launch_qgemm_cfg<128, 6, AMODE, ROWCOL>(dev, tmA, tmB, p);
+    default: return launch_qgemm_cfg<256, 4, AMODE, ROWCOL>(dev, tmA, tmB, p);
+  }
+}
+
+static int pick_bn(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
+
+static int fill_epilogue(QgParams& p, const mira_dequant* dq, const mira_epilogue* epi) {
+  MIRA_CHECK_ARG(dq != nullptr && epi != nullptr, "dequant and epilogue descriptors are required");
+  MIRA_CHECK_ARG(epi->n_steps >= 0 && epi->n_steps <= MIRA_EPI_MAX_STEPS, "too many epilogue steps");
+  MIRA_CHECK_ARG(epi->out_f32 != nullptr || epi->out_i8 != nullptr, "epilogue has no output");
+  p.scale64 = dq->scale64;
+  p.scale_hi = dq->scale_hi;
+  p.scale_lo = dq->scale_lo;
+  p.row_scale = dq->row_scale;
+  p.col_scale = dq->col_scale;
+  if (dq->scale64 != nullptr) {
+    MIRA_CHECK_ARG(dq->scale_hi != nullptr && dq->scale_lo != nullptr, "per-channel scales need scale_hi/scale_lo");
+    MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(dq->scale_hi) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(dq->scale_lo) & 15) == 0,
+                   "scale arrays must be 16-byte aligned");
+  } else {
+    MIRA_CHECK_ARG(dq->row_scale != nullptr && dq->col_scale != nullptr, "no dequant scales given");
+  }
+  p.n_steps = epi->n_steps;
+  for (int s = 0; s < epi->n_steps; ++s) {
+    const mira_epi_step& st = epi->steps[s];
+    MIRA_CHECK_ARG((st.op >= MIRA_EPI_RELU && st.op <= MIRA_EPI_TANH) || (st.op >= MIRA_EPI_ADD && st.op <= MIRA_EPI_MINIMUM),
+                   "unknown epilogue op");
+    const bool unary = st.op < MIRA_EPI_ADD;
+    MIRA_CHECK_ARG(unary == (st.operand == MIRA_OPND_NONE), "epilogue operand kind does not match the op");
+    if (st.operand == MIRA_OPND_CHANNEL)
+      MIRA_CHECK_ARG(st.ptr != nullptr && (reinterpret_cast<uintptr_t>(st.ptr) & 15) == 0, "channel operand must be 16-byte aligned");
+    if (st.operand == MIRA_OPND_FULL || st.operand == MIRA_OPND_ROW)
+      MIRA_CHECK_ARG(st.ptr != nullptr, "operand pointer missing");
+    if (st.operand == MIRA_OPND_FULL)
+      MIRA_CHECK_ARG(st.ld % 4 != 0 || (reinterpret_cast<uintptr_t>(st.ptr) & 15) == 0, "full operand misaligned");
+    p.steps[s] = st;
+  }
+  p.out_f32 = epi->out_f32;
+  p.ld_f32 = epi->ld_f32;
+  p.out_i8 = epi->out_i8;
+  p.ld_i8 = epi->ld_i8;
+  if (epi->out_f32 != nullptr)
+    MIRA_CHECK_ARG(epi->ld_f32 % 4 != 0 || (reinterpret_cast<uintptr_t>(epi->out_f32) & 15) == 0, "f32 output misaligned");
+  if (epi->out_i8 != nullptr) {
+    MIRA_CHECK_ARG(epi->ld_i8 % 16 == 0 && (reinterpret_cast<uintptr_t>(epi->out_i8) & 15) == 0,
+                   "int8 output needs a 16-byte aligned base and a row stride multiple of 16");
+    MIRA_CHECK_ARG(epi->out_scale > 0.0f && std::isfinite(epi->out_scale), "requant scale must be positive");
+  }
+  const QuantScale q = make_qscale(epi->out_i8 != nullptr ? epi->out_scale : 1.0f);
+  p.q_scale = q.s;
+  p.q_rcp = q.rcp;
+  p.q_lim = q.lim;
+  p.err = device_err_ptr();
+  return MIRA_CUDA_OK;
+}
+
+}  // namespace mira
+
+using namespace mira;
+
+// ================================================================== C ABI: runtime
+
+extern "C" int mira_cuda_abi_version(void) { return MIRA_CUDA_ABI_VERSION; }
+
+extern "C" int mira_cuda_last_error(char* buf, size_t n) {
+  if (buf == nullptr || n == 0) return MIRA_CUDA_EINVAL;
+  std::snprintf(buf, n, "%s", t_last_error.c_str());
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+extern "C" int mira_cuda_set_device(int device) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return set_error(MIRA_CUDA_ENODEV, "no CUDA device");
+  if (device < 0 || device >= n || device >= kMaxDevices) return set_error(MIRA_CUDA_EINVAL, "device index out of range");
+  const int rc = init_device(device);
+  if (rc != MIRA_CUDA_OK) return rc;
+  t_device = device;
+  MIRA_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_device_info(int* sm_count, int* cc_major, int* cc_minor) {
+  MIRA_GET_DEVICE(dev);
+  if (sm_count) *sm_count = dev->sm_count;
+  if (cc_major) *cc_major = dev->cc_major;
+  if (cc_minor) *cc_minor = dev->cc_minor;
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_malloc(void** ptr, size_t bytes) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(ptr != nullptr, "null out pointer");
+  *ptr = nullptr;
+  MIRA_CUDA_TRY(cudaMalloc(ptr, bytes == 0 ? 16 : bytes), "cudaMalloc");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_free(void* ptr) {
+  MIRA_GET_DEVICE(dev);
+  if (ptr != nullptr) MIRA_CUDA_TRY(cudaFree(ptr), "cudaFree");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_host_alloc(void** ptr, size_t bytes) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(ptr != nullptr, "null out pointer");
+  MIRA_CUDA_TRY(cudaHostAlloc(ptr, bytes == 0 ? 16 : bytes, cudaHostAllocPortable), "cudaHostAlloc");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_host_free(void* ptr) {
+  if (ptr != nullptr) MIRA_CUDA_TRY(cudaFreeHost(ptr), "cudaFreeHost");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_memset(void* dst, int value, size_t bytes) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaMemsetAsync(dst, value, bytes, dev->stream), "cudaMemsetAsync");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_h2d(void* dst, const void* src, size_t bytes) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, dev->stream), "cudaMemcpyAsync H2D");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_d2h(void* dst, const void* src, size_t bytes) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, dev->stream), "cudaMemcpyAsync D2H");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_d2d(void* dst, const void* src, size_t bytes) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, dev->stream), "cudaMemcpyAsync D2D");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_sync(void) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaStreamSynchronize(dev->stream), "cudaStreamSynchronize");
+  int flag = 0;
+  MIRA_CUDA_TRY(cudaMemcpyFromSymbol(&flag, g_mira_kernel_error, sizeof(int)), "read kernel error record");
+  if (flag != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_mira_kernel_error, &zero, sizeof(int));
+    return set_error(MIRA_CUDA_EKERNEL, "a kernel gave up on a bounded wait (error record " + std::to_string(flag) + ")");
+  }
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_get_stream(void** stream) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(stream != nullptr, "null out pointer");
+  *stream = dev->stream;
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_event_create(void** ev) {
+  MIRA_GET_DEVICE(dev);
+  cudaEvent_t e;
+  MIRA_CUDA_TRY(cudaEventCreate(&e), "cudaEventCreate");
+  *ev = e;
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_event_record(void* ev) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(ev), dev->stream), "cudaEventRecord");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_event_elapsed(void* start, void* end, float* ms) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaEventSynchronize(static_cast<cudaEvent_t>(end)), "cudaEventSynchronize");
+  MIRA_CUDA_TRY(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(end)),
+                "cudaEventElapsedTime");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_event_destroy(void* ev) {
+  if (ev != nullptr) MIRA_CUDA_TRY(cudaEventDestroy(static_cast<cudaEvent_t>(ev)), "cudaEventDestroy");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_graph_begin(void) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaStreamBeginCapture(dev->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_graph_end(void** graph_exec) {
+  MIRA_GET_DEVICE(dev);
+  cudaGraph_t g = nullptr;
+  MIRA_CUDA_TRY(cudaStreamEndCapture(dev->stream, &g), "cudaStreamEndCapture");
+  cudaGraphExec_t ge = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGraphInstantiate");
+  *graph_exec = ge;
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_graph_launch(void* graph_exec) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), dev->stream), "cudaGraphLaunch");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_graph_destroy(void* graph_exec) {
+  if (graph_exec != nullptr) MIRA_CUDA_TRY(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec)), "cudaGraphExecDestroy");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int64_t mira_cuda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+// ================================================================== C ABI: kernels
+
+extern "C" int mira_cuda_quantize_rows(const float* x, int64_t rows, int64_t cols, int64_t ld_x, float scale,
+                                       int8_t* xq, int64_t ld_q) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(rows >= 0 && cols >= 0 && ld_x >= cols && ld_q >= cols, "bad quantize shape");
+  MIRA_CHECK_ARG(ld_q % 16 == 0 && (reinterpret_cast<uintptr_t>(xq) & 15) == 0, "int8 rows must be 16-byte aligned");
+  MIRA_CHECK_ARG(scale > 0.0f && std::isfinite(scale), "quantization scale must be positive");
+  if (rows == 0 || ld_q == 0) return MIRA_CUDA_OK;
+  const int threads = 256;
+  quantize_rows_kernel<<<grid_for(dev, rows * (ld_q / 16), threads), threads, 0, dev->stream>>>(
+      x, rows, cols, ld_x, make_qscale(scale), xq, ld_q);
+  return after_launch("quantize_rows_kernel");
+}
+
+extern "C" int mira_cuda_quantize_nchw_to_nhwc(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, float scale,
+                                               int8_t* xq, int64_t cp) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && c > 0 && h > 0 && w > 0 && cp >= c && cp % 4 == 0, "bad quantize_nchw shape");
+  MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(xq) & 3) == 0, "int8 output must be 4-byte aligned");
+  MIRA_CHECK_ARG(scale > 0.0f && std::isfinite(scale), "quantization scale must be positive");
+  if (n == 0) return MIRA_CUDA_OK;
+  const int threads = 256;
+  const int64_t work = n * h * w * (cp / 4);
+  quantize_nchw_nhwc_kernel<<<grid_for(dev, work, threads), threads, 0, dev->stream>>>(x, n, c, h * w,
+                                                                                       make_qscale(scale), xq, cp);
+  return after_launch("quantize_nchw_nhwc_kernel");
+}
+
+extern "C" int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda, const int8_t* B,
+                               int64_t ldb, const mira_dequant* dq, const mira_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad qgemm shape");
+  MIRA_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 24) && K < (int64_t(1) << 24), "qgemm shape too large");
+  MIRA_CHECK_ARG(K <= 133000, "K too large for exact int32 accumulation of int8 products");
+  MIRA_CHECK_ARG(lda >= round_up(K, 16) && lda % 16 == 0 && ldb >= round_up(K, 16) && ldb % 16 == 0,
+                 "int8 operands need row strides >= round_up(K, 16), multiples of 16");
+  if (M == 0) return MIRA_CUDA_OK;
+  QgParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int rc = fill_epilogue(p, dq, epi);
+  if (rc != MIRA_CUDA_OK) return rc;
+  const int bn = pick_bn(N);
+  p.M = int(M);
+  p.N = int(N);
+  p.K = int(K);
+  p.num_kb = int((K + QG_BK - 1) / QG_BK);
+  p.m_tiles = int((M + QG_BM - 1) / QG_BM);
+  p.n_tiles = int((N + bn - 1) / bn);
+  CUtensorMap tmA, tmB;
+  int r = encode_2d_i8(&tmA, A, uint64_t(lda), uint64_t(M), uint64_t(lda), QG_BK, QG_BM);
+  if (r != MIRA_CUDA_OK) return r;
+  r = encode_2d_i8(&tmB, B, uint64_t(ldb), uint64_t(N), uint64_t(ldb), QG_BK, uint32_t(bn));
+  if (r != MIRA_CUDA_OK) return r;
+  if (p.scale64 != nullptr) return launch_qgemm_bn<QG_A_TMA, false>(dev, tmA, tmB, p, bn);
+  return launch_qgemm_bn<QG_A_TMA, true>(dev, tmA, tmB, p, bn);
+}
+
+extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o, int64_t kh,
+                                 int64_t kw, const int8_t* wq, int64_t ldw, int64_t stride_h, int64_t stride_w,
+                                 int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w, const mira_dequant* dq,
+                                 const mira_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && h > 0 && w > 0 && o > 0 && kh > 0 && kw > 0, "bad qconv2d shape");
+  MIRA_CHECK_ARG(cp == 4 || (cp > 0 && cp % 16 == 0), "input channels must be padded to 4 or a multiple of 16");
+  MIRA_CHECK_ARG(stride_h > 0 && stride_w > 0 && dil_h > 0 && dil_w > 0 && pad_h >= 0 && pad_w >= 0, "bad conv geometry");
+  MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "conv input must be 16-byte aligned");
+  const int64_t oh = (h + 2 * pad_h - dil_h * (kh - 1) - 1) / stride_h + 1;
+  const int64_t ow = (w + 2 * pad_w - dil_w * (kw - 1) - 1) / stride_w + 1;
+  MIRA_CHECK_ARG(oh > 0 && ow > 0, "kernel larger than the padded input");
+  const int64_t K = kh * kw * cp;
+  MIRA_CHECK_ARG(K <= 133000, "K too large for exact int32 accumulation of int8 products");
+  MIRA_CHECK_ARG(ldw >= round_up(K, 16) && ldw % 16 == 0, "weight row stride must be >= round_up(kh*kw*cp, 16)");
+  const int64_t M = n * oh * ow;
+  MIRA_CHECK_ARG(M < (int64_t(1) << 31) && n * h * w * cp < (int64_t(1) << 40), "conv too large");
+  if (M == 0) return MIRA_CUDA_OK;
+  QgParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int rc = fill_epilogue(p, dq, epi);
+  if (rc != MIRA_CUDA_OK) return rc;
+  MIRA_CHECK_ARG(p.scale64 != nullptr, "convolutions use per-channel scales");
+  const int bn = pick_bn(o);
+  p.M = int(M);
+  p.N = int(o);
+  p.K = int(K);
+  p.num_kb = int((K + QG_BK - 1) / QG_BK);
+  p.m_tiles = int((M + QG_BM - 1) / QG_BM);
+  p.n_tiles = int((o + bn - 1) / bn);
+  p.A = x;
+  p.g = QgConv{int(n), int(h), int(w), int(cp), int(oh), int(ow), int(kh), int(kw), int(stride_h), int(stride_w),
+               int(pad_h), int(pad_w), int(dil_h), int(dil_w)};
+  CUtensorMap tmA, tmB;
+  std::memset(&tmA, 0, sizeof(tmA));
+  int r = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, uint32_t(bn));
+  if (r != MIRA_CUDA_OK) return r;
+  if (cp == 4) return launch_qgemm_bn<QG_A_GATHER4, false>(dev, tmA, tmB, p, bn);
+  return launch_qgemm_bn<QG_A_GATHER16, false>(dev, tmA, tmB, p, bn);
+}
+
+extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, int64_t n, int64_t h, int64_t w,
+                                        int64_t c, int64_t ldc_in, int64_t size, int64_t stride, int64_t pad,
+                                        float pad_value, float* out_f32, int64_t ldc_out_f32, int8_t* out_i8,
+                                        int64_t ldc_out_i8, float out_scale) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && h > 0 && w > 0 && c > 0 && size > 0 && stride > 0 && pad >= 0 && pad < size,
+                 "bad maxpool geometry");
+  const int64_t oh = (h + 2 * pad - size) / stride + 1, ow = (w + 2 * pad - size) / stride + 1;
+  MIRA_CHECK_ARG(oh > 0 && ow > 0, "pool window larger than the input");
+  if (n == 0) return MIRA_CUDA_OK;
+  const int threads = 256;
+  if (x_i8 != nullptr) {
+    MIRA_CHECK_ARG(out_f32 == nullptr && out_i8 != nullptr, "int8 pooling produces int8 only");
+    MIRA_CHECK_ARG(ldc_in % 16 == 0 && ldc_out_i8 == ldc_in, "int8 pooling keeps the padded channel stride");
+    MIRA_CHECK_ARG(out_scale > 0.0f, "requant scale must be positive");
+    const uint32_t pq = quant_byte_host(pad_value, out_scale);
+    const int64_t work = n * oh * ow * (ldc_in / 16);
+    maxpool_i8_kernel<<<grid_for(dev, work, threads), threads, 0, dev->stream>>>(
+        x_i8, int(n), int(h), int(w), ldc_in, int(size), int(stride), int(pad), static_cast<int8_t>(pq & 0xff),
+        int(oh), int(ow), out_i8, ldc_out_i8);
+    return after_launch("maxpool_i8_kernel");
+  }
+  MIRA_CHECK_ARG(x_f32 != nullptr && (out_f32 != nullptr || out_i8 != nullptr), "maxpool needs an input and an output");
+  if (out_i8 != nullptr) MIRA_CHECK_ARG(ldc_out_i8 % 4 == 0 && ldc_out_i8 >= c && out_scale > 0.0f, "bad int8 output");
+  const int64_t work = n * oh * ow * ((c + 3) / 4);
+  maxpool_f32_kernel<<<grid_for(dev, work, threads), threads, 0, dev->stream>>>(
+      x_f32, int(n), int(h), int(w), int(c), ldc_in, int(size), int(stride), int(pad), pad_value, int(oh), int(ow),
+      out_f32, ldc_out_f32, out_i8, ldc_out_i8, make_qscale(out_i8 != nullptr ? out_scale : 1.0f));
+  return after_launch("maxpool_f32_kernel");
+}
+
+extern "C" int mira_cuda_mean_hw_nhwc(const float* x, int64_t n, int64_t hw, int64_t c, int64_t ldc, float* out_f32,
+                                      int8_t* out_i8, int64_t ld_i8, float out_scale) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && hw > 0 && hw < (1 << 20) && c > 0 && ldc >= c, "bad mean shape");
+  MIRA_CHECK_ARG(out_f32 != nullptr || out_i8 != nullptr, "mean has no output");
+  if (out_i8 != nullptr) MIRA_CHECK_ARG(ld_i8 >= c && out_scale > 0.0f, "bad int8 output");
+  if (n == 0) return MIRA_CUDA_OK;
+  const int threads = 128;
+  mean_hw_kernel<<<grid_for(dev, n * c, threads), threads, 0, dev->stream>>>(
+      x, int(n), int(hw), int(c), ldc, out_f32, out_i8, ld_i8, make_qscale(out_i8 != nullptr ? out_scale : 1.0f));
+  return after_launch("mean_hw_kernel");
+}
+
+extern "C" int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int64_t w, int64_t c, const float* wt,
+                                       int64_t kh, int64_t kw, int64_t stride_h, int64_t stride_w, int64_t pad_h,
+                                       int64_t pad_w, int64_t dil_h, int64_t dil_w, const mira_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && h > 0 && w > 0 && c > 0 && kh > 0 && kw > 0, "bad dwconv shape");
+  MIRA_CHECK_ARG(stride_h > 0 && stride_w > 0 && dil_h > 0 && dil_w > 0 && pad_h >= 0 && pad_w >= 0, "bad dwconv geometry");
+  MIRA_CHECK_ARG(epi != nullptr && epi->n_steps >= 0 && epi->n_steps <= MIRA_EPI_MAX_STEPS, "bad epilogue");
+  MIRA_CHECK_ARG(epi->out_f32 != nullptr || epi->out_i8 != nullptr, "dwconv has no output");
+  const int64_t oh = (h + 2 * pad_h - dil_h * (kh - 1) - 1) / stride_h + 1;
+  const int64_t ow = (w + 2 * pad_w - dil_w * (kw - 1) - 1) / stride_w + 1;
+  MIRA_CHECK_ARG(oh > 0 && ow > 0, "kernel larger than the padded input");
+  if (n == 0) return MIRA_CUDA_OK;
+  DwParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.n = int(n); p.h = int(h); p.w = int(w); p.c = int(c); p.oh = int(oh); p.ow = int(ow);
+  p.kh = int(kh); p.kw = int(kw); p.sh = int(stride_h); p.sw = int(stride_w); p.ph = int(pad_h); p.pw = int(pad_w);
+  p.dh = int(dil_h); p.dw = int(dil_w);
+  p.n_steps = epi->n_steps;
+  for (int s = 0; s < epi->n_steps; ++s) p.steps[s] = epi->steps[s];
+  p.out_f32 = epi->out_f32; p.ld_f32 = epi->ld_f32; p.out_i8 = epi->out_i8; p.ld_i8 = epi->ld_i8;
+  p.q = make_qscale(epi->out_i8 != nullptr ? epi->out_scale : 1.0f);
+  const int threads = 256;
+  dwconv_kernel<<<grid_for(dev, n * oh * ow * c, threads), threads, 0, dev->stream>>>(x, wt, p);
+  return after_launch("dwconv_kernel");
+}
+
+extern "C" int mira_cuda_nchw_to_nhwc_f32(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, float* y,
+                                          int64_t ldc) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && c > 0 && h > 0 && w > 0 && ldc >= c && n < 65536, "bad layout-change shape");
+  if (n == 0) return MIRA_CUDA_OK;
+  const dim3 grid(unsigned((h * w + 31) / 32), unsigned((c + 31) / 32), unsigned(n));
+  nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(x, int(c), int(h * w), y, ldc);
+  return after_launch("nchw_to_nhwc_kernel");
+}
+
+extern "C" int mira_cuda_nhwc_to_nchw_f32(const float* x, int64_t n, int64_t h, int64_t w, int64_t c, int64_t ldc,
+                                          float* y) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && c > 0 && h > 0 && w > 0 && ldc >= c && n < 65536, "bad layout-change shape");
+  if (n == 0) return MIRA_CUDA_OK;
+  const dim3 grid(unsigned((h * w + 31) / 32), unsigned((c + 31) / 32), unsigned(n));
+  nhwc_to_nchw_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(x, int(c), int(h * w), ldc, y);
+  return after_launch("nhwc_to_nchw_kernel");
+}

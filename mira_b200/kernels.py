@@ -1,0 +1,180 @@
+"""Python-side launchers for the kernels of libmira_cuda.so.
+
+Each function takes device pointers (DeviceBuffer, int addresses) and plain sizes and fills the
+descriptor structs of include/mira_cuda.h.  Host-side preparation of constants (int8 weight
+re-layout, per-channel scale splits) lives here too, because it defines what the kernels expect.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from .device import ptr
+
+CHANNEL_PAD = 256    # per-channel arrays are padded to this many entries
+
+
+def round_up(x: int, m: int) -> int:
+    return (int(x) + m - 1) // m * m
+
+
+# ----------------------------------------------------------------------------- host preparation
+
+def scale_arrays(x_scale: float, w_scale: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """(scale64, scale_hi, scale_lo) for per-channel dequant, padded to a multiple of CHANNEL_PAD.
+    scale64 = float64(x_scale) * float64(w_scale), the reference's factor (ops.py:619, ops.py:633)."""
+    n = len(w_scale)
+    npad = round_up(max(n, 1), CHANNEL_PAD)
+    s64 = np.zeros(npad, np.float64)
+    s64[:n] = np.float64(x_scale) * np.asarray(w_scale).astype(np.float64)
+    hi = s64.astype(np.float32)
+    lo = (s64 - hi.astype(np.float64)).astype(np.float32)
+    return s64, hi, lo
+
+
+def pad_channels(v: np.ndarray) -> np.ndarray:
+    """f32 per-channel operand padded to a multiple of CHANNEL_PAD."""
+    v = np.asarray(v, np.float32).ravel()
+    out = np.zeros(round_up(max(len(v), 1), CHANNEL_PAD), np.float32)
+    out[:len(v)] = v
+    return out
+
+
+def matmul_weight(q_kn: np.ndarray) -> np.ndarray:
+    """Reference qmatmul weight int8 [K, N] -> K-major [N, round_up(K, 16)] (zero padded)."""
+    k, n = q_kn.shape
+    out = np.zeros((n, round_up(k, 16)), np.int8)
+    out[:, :k] = q_kn.T
+    return out
+
+
+def conv_channels(c: int) -> int:
+    """Padded channel count of an NHWC int8 activation: 4 for c <= 4, else a multiple of 16."""
+    return 4 if c <= 4 else round_up(c, 16)
+
+
+def conv_weight(q_oihw: np.ndarray) -> tuple[np.ndarray, int]:
+    """Reference qconv2d weight int8 [O, C, KH, KW] -> [O, round_up(KH*KW*Cp, 16)] with
+    k = (i * KW + j) * Cp + c (zero padded channels).  Returns (weights, Cp)."""
+    o, c, kh, kw = q_oihw.shape
+    cp = conv_channels(c)
+    t = np.zeros((o, kh, kw, cp), np.int8)
+    t[:, :, :, :c] = q_oihw.transpose(0, 2, 3, 1)
+    k = kh * kw * cp
+    out = np.zeros((o, round_up(k, 16)), np.int8)
+    out[:, :k] = t.reshape(o, k)
+    return out, cp
+
+
+# ----------------------------------------------------------------------------- epilogue descriptors
+
+@dataclass
+class Step:
+    """One fused epilogue step: `op` a reference UNARY/BINARY name, `operand` one of
+    "none" / "scalar" / "channel" / "full" / "row"."""
+    op: str
+    operand: str = "none"
+    swapped: bool = False
+    scalar: float = 0.0
+    ptr: object = None
+    ld: int = 0
+
+
+_OPND = {"none": _lib.OPND_NONE, "scalar": _lib.OPND_SCALAR, "channel": _lib.OPND_CHANNEL,
+         "full": _lib.OPND_FULL, "row": _lib.OPND_ROW}
+
+
+@dataclass
+class Epi:
+    steps: Sequence[Step] = field(default_factory=list)
+    out_f32: object = None
+    ld_f32: int = 0
+    out_i8: object = None
+    ld_i8: int = 0
+    out_scale: float = 1.0
+
+    def struct(self) -> _lib.Epilogue:
+        e = _lib.Epilogue()
+        if len(self.steps) > _lib.EPI_MAX_STEPS:
+            raise ValueError(f"at most {_lib.EPI_MAX_STEPS} fused epilogue steps")
+        e.n_steps = len(self.steps)
+        for i, s in enumerate(self.steps):
+            code = _lib.UNARY_CODES.get(s.op) or _lib.BINARY_CODES.get(s.op)
+            if code is None:
+                raise ValueError(f"epilogue op {s.op!r} has no device implementation")
+            e.steps[i].op = code
+            e.steps[i].operand = _OPND[s.operand]
+            e.steps[i].swapped = int(bool(s.swapped))
+            e.steps[i].scalar = float(np.float32(s.scalar))
+            e.steps[i].ptr = ptr(s.ptr).value or 0
+            e.steps[i].ld = int(s.ld)
+        e.out_f32 = ptr(self.out_f32).value or 0
+        e.ld_f32 = int(self.ld_f32)
+        e.out_i8 = ptr(self.out_i8).value or 0
+        e.ld_i8 = int(self.ld_i8)
+        e.out_scale = float(np.float32(self.out_scale))
+        return e
+
+
+def dequant_channel(scale64, scale_hi, scale_lo) -> _lib.Dequant:
+    d = _lib.Dequant()
+    d.scale64, d.scale_hi, d.scale_lo = ptr(scale64).value, ptr(scale_hi).value, ptr(scale_lo).value
+    return d
+
+
+def dequant_rowcol(row_scale, col_scale) -> _lib.Dequant:
+    d = _lib.Dequant()
+    d.row_scale, d.col_scale = ptr(row_scale).value, ptr(col_scale).value
+    return d
+
+
+# ----------------------------------------------------------------------------- launchers
+
+def quantize_rows(x, rows: int, cols: int, ld_x: int, scale: float, xq, ld_q: int) -> None:
+    _lib.call("mira_cuda_quantize_rows", ptr(x), rows, cols, ld_x, float(np.float32(scale)), ptr(xq), ld_q)
+
+
+def quantize_nchw_to_nhwc(x, n: int, c: int, h: int, w: int, scale: float, xq, cp: int) -> None:
+    _lib.call("mira_cuda_quantize_nchw_to_nhwc", ptr(x), n, c, h, w, float(np.float32(scale)), ptr(xq), cp)
+
+
+def qgemm(M: int, N: int, K: int, A, lda: int, B, ldb: int, dq: _lib.Dequant, epi: Epi) -> None:
+    e = epi.struct()
+    _lib.call("mira_cuda_qgemm", M, N, K, ptr(A), lda, ptr(B), ldb, C.byref(dq), C.byref(e))
+
+
+def qconv2d(n: int, h: int, w: int, cp: int, x, o: int, kh: int, kw: int, wq, ldw: int, stride, padding,
+            dilation, dq: _lib.Dequant, epi: Epi) -> None:
+    e = epi.struct()
+    _lib.call("mira_cuda_qconv2d", n, h, w, cp, ptr(x), o, kh, kw, ptr(wq), ldw, stride[0], stride[1],
+              padding[0], padding[1], dilation[0], dilation[1], C.byref(dq), C.byref(e))
+
+
+def maxpool2d(n, h, w, c, ldc_in, size, stride, pad, pad_value, x_f32=None, x_i8=None, out_f32=None,
+              ldc_out_f32=0, out_i8=None, ldc_out_i8=0, out_scale=1.0) -> None:
+    _lib.call("mira_cuda_maxpool2d_nhwc", ptr(x_f32), ptr(x_i8), n, h, w, c, ldc_in, size, stride, pad,
+              float(np.float32(pad_value)), ptr(out_f32), ldc_out_f32, ptr(out_i8), ldc_out_i8,
+              float(np.float32(out_scale)))
+
+
+def mean_hw(x, n, hw, c, ldc, out_f32=None, out_i8=None, ld_i8=0, out_scale=1.0) -> None:
+    _lib.call("mira_cuda_mean_hw_nhwc", ptr(x), n, hw, c, ldc, ptr(out_f32), ptr(out_i8), ld_i8,
+              float(np.float32(out_scale)))
+
+
+def dwconv2d(x, n, h, w, c, wt, kh, kw, stride, padding, dilation, epi: Epi) -> None:
+    e = epi.struct()
+    _lib.call("mira_cuda_dwconv2d_nhwc", ptr(x), n, h, w, c, ptr(wt), kh, kw, stride[0], stride[1],
+              padding[0], padding[1], dilation[0], dilation[1], C.byref(e))
+
+
+def nchw_to_nhwc(x, n, c, h, w, y, ldc) -> None:
+    _lib.call("mira_cuda_nchw_to_nhwc_f32", ptr(x), n, c, h, w, ptr(y), ldc)
+
+
+def nhwc_to_nchw(x, n, h, w, c, ldc, y) -> None:
+    _lib.call("mira_cuda_nhwc_to_nchw_f32", ptr(x), n, h, w, c, ldc, ptr(y))

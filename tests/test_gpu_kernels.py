@@ -1,0 +1,282 @@
+"""Per-kernel parity on the GPU: every kernel against the CPU oracle on identical seeded inputs.
+
+int8 activations and int32 accumulators must be bit-exact; f32 results must be bit-identical to
+the reference's NumPy arithmetic (tolerance 0) for the exact epilogue ops, and within 1e-5
+relative for the transcendental ones (gelu/sigmoid/tanh use CUDA's tanhf/expf).
+"""
+import numpy as np
+import pytest
+
+from oracle import w8a8 as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _k():
+    from mira_b200 import kernels as K
+    from mira_b200.device import DeviceBuffer
+    return K, DeviceBuffer
+
+
+def _same_f32(got, want):
+    got = np.asarray(got, np.float32)
+    want = np.asarray(want, np.float32)
+    assert got.shape == want.shape
+    bad = ~((got == want) | (np.isnan(got) & np.isnan(want)))
+    assert not bad.any(), f"{bad.sum()} of {bad.size} f32 values differ; first at {np.argwhere(bad)[:3].tolist()}"
+
+
+# ------------------------------------------------------------------------------ quantize
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 17), (64, 784), (257, 1000), (1000, 16)])
+def test_quantize_rows_matches_reference(cuda_device, rows, cols):
+    K, DB = _k()
+    rng = np.random.default_rng(rows * 7 + cols)
+    scale = float(rng.uniform(0.01, 0.1))
+    x = (rng.standard_normal((rows, cols)) * 60 * scale).astype(np.float32)
+    # exact ties k + 0.5 in the quotient and values beyond the clip range
+    x.ravel()[::7] = ((rng.integers(-140, 140, x.size)[::7] + 0.5) * np.float32(scale)).astype(np.float32)
+    x.ravel()[::11] = np.float32(1e30)
+    ldq = K.round_up(cols, 16)
+    xb = DB.from_array(x)
+    qb = DB(rows * ldq)
+    K.quantize_rows(xb, rows, cols, cols, scale, qb, ldq)
+    got = qb.download((rows, ldq), np.int8)
+    np.testing.assert_array_equal(got[:, :cols], ref.quantize_activation(x, scale))
+    assert not got[:, cols:].any()
+
+
+def test_quantize_nchw_to_nhwc(cuda_device):
+    K, DB = _k()
+    rng = np.random.default_rng(5)
+    n, c, h, w = 3, 3, 9, 11
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    scale = 0.0271
+    cp = K.conv_channels(c)
+    xb, qb = DB.from_array(x), DB(n * h * w * cp)
+    K.quantize_nchw_to_nhwc(xb, n, c, h, w, scale, qb, cp)
+    got = qb.download((n, h, w, cp), np.int8)
+    want = ref.quantize_activation(x, scale).transpose(0, 2, 3, 1)
+    np.testing.assert_array_equal(got[..., :c], want)
+    assert not got[..., c:].any()
+
+
+# ------------------------------------------------------------------------------ qgemm
+
+def _run_qgemm(M, N, K_, steps_spec, seed, want_i8=True, rowcol=False):
+    K, DB = _k()
+    rng = np.random.default_rng(seed)
+    x_scale = float(rng.uniform(0.005, 0.05))
+    xq = rng.integers(-127, 128, (M, K_)).astype(np.int8)
+    q = rng.integers(-127, 128, (K_, N)).astype(np.int8)
+    w_scale = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    lda = K.round_up(K_, 16)
+    A = np.zeros((M, lda), np.int8)
+    A[:, :K_] = xq
+    Ab, Bb = DB.from_array(A), DB.from_array(K.matmul_weight(q))
+    acc = ref.int_matmul(xq, q)
+    keep = []
+    if rowcol:
+        rs = rng.uniform(1e-3, 1e-2, M).astype(np.float32)
+        cs = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+        rb, cb = DB.from_array(rs), DB.from_array(cs)
+        keep += [rb, cb]
+        dq = K.dequant_rowcol(rb, cb)
+        y = (acc.astype(np.float64) * (rs.astype(np.float64)[:, None] * cs.astype(np.float64)[None, :])).astype(np.float32)
+    else:
+        s64, hi, lo = K.scale_arrays(x_scale, w_scale)
+        sb, hb, lb = DB.from_array(s64), DB.from_array(hi), DB.from_array(lo)
+        keep += [sb, hb, lb]
+        dq = K.dequant_channel(sb, hb, lb)
+        y = ref.dequant(acc, ref.combined_scale(x_scale, w_scale))
+    steps, ref_steps, operands = [], [], []
+    for kind in steps_spec:
+        if kind == "bias":
+            b = rng.standard_normal(N).astype(np.float32)
+            bb = DB.from_array(K.pad_channels(b))
+            keep.append(bb)
+            steps.append(K.Step("add", "channel", ptr=bb))
+            ref_steps.append(("add", len(operands), False))
+            operands.append(b)
+        elif kind == "residual":
+            r = rng.standard_normal((M, N)).astype(np.float32)
+            rb_ = DB.from_array(r)
+            keep.append(rb_)
+            steps.append(K.Step("add", "full", ptr=rb_, ld=N))
+            ref_steps.append(("add", len(operands), True))
+            steps[-1].swapped = True
+            operands.append(r)
+        elif kind in ("relu", "gelu", "tanh", "sigmoid"):
+            steps.append(K.Step(kind))
+            ref_steps.append((kind, None, False))
+        elif kind == "relu6":
+            steps += [K.Step("maximum", "scalar", scalar=0.0), K.Step("minimum", "scalar", scalar=6.0)]
+            operands += [np.float32(0.0), np.float32(6.0)]
+            ref_steps += [("maximum", len(operands) - 2, False), ("minimum", len(operands) - 1, False)]
+    y = ref.epilogue(y, operands, ref_steps).astype(np.float32)
+    out_scale = float(np.abs(y).max() / 127.0) or 1.0
+    yb = DB(M * N * 4)
+    ldi = K.round_up(N, 16)
+    qb = DB(M * ldi) if want_i8 else None
+    K.qgemm(M, N, K_, Ab, lda, Bb, lda, dq, K.Epi(steps, out_f32=yb, ld_f32=N, out_i8=qb, ld_i8=ldi, out_scale=out_scale))
+    got = yb.download((M, N), np.float32)
+    got_q = qb.download((M, ldi), np.int8) if want_i8 else None
+    return got, y, got_q, ref.quantize_activation(y, out_scale)
+
+
+@pytest.mark.parametrize("M,N,K_", [(128, 64, 128), (1, 10, 16), (37, 100, 100), (256, 512, 784),
+                                    (300, 300, 1000), (129, 256, 4096), (1024, 1000, 512)])
+def test_qgemm_bias_relu_exact(cuda_device, M, N, K_):
+    got, want, got_q, want_q = _run_qgemm(M, N, K_, ["bias", "relu"], seed=M + N + K_)
+    _same_f32(got, want)
+    np.testing.assert_array_equal(got_q[:, :N], want_q)
+    assert not got_q[:, N:].any()
+
+
+@pytest.mark.parametrize("spec", [[], ["relu"], ["bias", "residual", "relu"], ["bias", "relu6"]])
+def test_qgemm_epilogues_exact(cuda_device, spec):
+    got, want, got_q, want_q = _run_qgemm(200, 192, 576, spec, seed=11)
+    _same_f32(got, want)
+    np.testing.assert_array_equal(got_q[:, :192], want_q)
+
+
+@pytest.mark.parametrize("act", ["gelu", "tanh", "sigmoid"])
+def test_qgemm_transcendental_epilogue_close(cuda_device, act):
+    got, want, _, _ = _run_qgemm(130, 96, 256, ["bias", act], seed=3, want_i8=False)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("M,N,K_", [(256, 256, 256), (100, 130, 4096), (1, 4096, 4096), (16, 4096, 4096)])
+def test_qgemm_rowcol_sweep_semantics(cuda_device, M, N, K_):
+    got, want, _, _ = _run_qgemm(M, N, K_, ["bias"], seed=7, want_i8=False, rowcol=True)
+    _same_f32(got, want)
+
+
+# ------------------------------------------------------------------------------ qconv2d
+
+def _run_qconv(n, c, h, w, o, kh, kw, stride, pad, dil=(1, 1), spec=("bias", "relu"), seed=0):
+    K, DB = _k()
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    x_scale = float(np.abs(x).max() / 127.0)
+    wt = (rng.standard_normal((o, c, kh, kw)) / np.sqrt(c * kh * kw)).astype(np.float32)
+    q, w_scale = ref.quantize_array(wt, 0)
+    bias = rng.standard_normal((o, 1, 1)).astype(np.float32)
+    ref_steps, operands, steps, keep = [], [], [], []
+    if "bias" in spec:
+        bb = DB.from_array(K.pad_channels(bias))
+        keep.append(bb)
+        steps.append(K.Step("add", "channel", ptr=bb))
+        ref_steps.append(("add", 1, False))
+        operands.append(bias)
+    if "relu" in spec:
+        steps.append(K.Step("relu"))
+        ref_steps.append(("relu", None, False))
+    xq, acc, y = ref.qconv2d(x, q, w_scale, x_scale, stride, pad, dil, steps=ref_steps, operands=operands)
+    wq, cp = K.conv_weight(q)
+    xn = np.zeros((n, h, w, cp), np.int8)
+    xn[..., :c] = xq.transpose(0, 2, 3, 1)
+    oh, ow = y.shape[2:]
+    M = n * oh * ow
+    s64, hi, lo = K.scale_arrays(x_scale, w_scale)
+    sb, hb, lb = DB.from_array(s64), DB.from_array(hi), DB.from_array(lo)
+    xb, wb = DB.from_array(xn), DB.from_array(wq)
+    yb = DB(M * o * 4)
+    ldi = K.round_up(o, 16)
+    qb = DB(M * ldi)
+    out_scale = float(np.abs(y).max() / 127.0) or 1.0
+    K.qconv2d(n, h, w, cp, xb, o, kh, kw, wb, wq.shape[1], stride, pad, dil, K.dequant_channel(sb, hb, lb),
+              K.Epi(steps, out_f32=yb, ld_f32=o, out_i8=qb, ld_i8=ldi, out_scale=out_scale))
+    got = yb.download((n, oh, ow, o), np.float32).transpose(0, 3, 1, 2)
+    got_q = qb.download((n, oh, ow, ldi), np.int8)[..., :o].transpose(0, 3, 1, 2)
+    return got, y, got_q, ref.quantize_activation(y, out_scale)
+
+
+@pytest.mark.parametrize("case", [
+    dict(n=2, c=64, h=14, w=14, o=64, kh=3, kw=3, stride=(1, 1), pad=(1, 1)),
+    dict(n=2, c=64, h=15, w=13, o=128, kh=3, kw=3, stride=(2, 2), pad=(1, 1)),
+    dict(n=3, c=128, h=8, w=8, o=256, kh=1, kw=1, stride=(2, 2), pad=(0, 0)),
+    dict(n=2, c=3, h=32, w=32, o=64, kh=7, kw=7, stride=(2, 2), pad=(3, 3)),
+    dict(n=1, c=1, h=28, w=28, o=16, kh=3, kw=3, stride=(1, 1), pad=(1, 1)),
+    dict(n=2, c=16, h=14, w=14, o=32, kh=3, kw=3, stride=(1, 1), pad=(1, 1)),
+    dict(n=1, c=256, h=7, w=7, o=512, kh=3, kw=3, stride=(1, 1), pad=(1, 1)),
+    dict(n=2, c=32, h=10, w=10, o=48, kh=3, kw=3, stride=(1, 1), pad=(2, 2), dil=(2, 2)),
+    dict(n=2, c=40, h=9, w=9, o=24, kh=1, kw=1, stride=(1, 1), pad=(0, 0)),
+])
+def test_qconv2d_exact(cuda_device, case):
+    got, want, got_q, want_q = _run_qconv(**case, seed=sum(v if isinstance(v, int) else 0 for v in case.values()))
+    _same_f32(got, want)
+    np.testing.assert_array_equal(got_q, want_q)
+
+
+# ------------------------------------------------------------------------------ memory-bound ops
+
+def test_maxpool_f32_and_int8(cuda_device):
+    K, DB = _k()
+    rng = np.random.default_rng(2)
+    n, c, h, w = 2, 64, 15, 15
+    x = np.maximum(rng.standard_normal((n, c, h, w)), 0).astype(np.float32)
+    scale = float(np.abs(x).max() / 127)
+    want = ref.maxpool2d(x, 3, 2, 1)
+    xn = np.ascontiguousarray(x.transpose(0, 2, 3, 1))
+    oh = want.shape[2]
+    xb = DB.from_array(xn)
+    yb, qb = DB(n * oh * oh * c * 4), DB(n * oh * oh * c)
+    K.maxpool2d(n, h, w, c, c, 3, 2, 1, -np.inf, x_f32=xb, out_f32=yb, ldc_out_f32=c, out_i8=qb, ldc_out_i8=c,
+                out_scale=scale)
+    _same_f32(yb.download((n, oh, oh, c), np.float32).transpose(0, 3, 1, 2), want)
+    np.testing.assert_array_equal(qb.download((n, oh, oh, c), np.int8).transpose(0, 3, 1, 2),
+                                  ref.quantize_activation(want, scale))
+    # int8 path: pooling int8 equals quantizing the pooled f32 values
+    xq = DB.from_array(ref.quantize_activation(xn, scale))
+    q2 = DB(n * oh * oh * c)
+    K.maxpool2d(n, h, w, c, c, 3, 2, 1, -np.inf, x_i8=xq, out_i8=q2, ldc_out_i8=c, out_scale=scale)
+    np.testing.assert_array_equal(q2.download((n, oh, oh, c), np.int8).transpose(0, 3, 1, 2),
+                                  ref.quantize_activation(want, scale))
+
+
+@pytest.mark.parametrize("hw", [(7, 7), (1, 1), (14, 14), (3, 5)])
+def test_mean_hw_bit_exact(cuda_device, hw):
+    K, DB = _k()
+    rng = np.random.default_rng(hw[0] * 10 + hw[1])
+    n, c = 5, 96
+    x = (rng.standard_normal((n, c) + hw) * 3).astype(np.float32)
+    want = x.mean(axis=(2, 3))
+    xb = DB.from_array(np.ascontiguousarray(x.transpose(0, 2, 3, 1)))
+    yb, qb = DB(n * c * 4), DB(n * 112)
+    scale = float(np.abs(want).max() / 127)
+    K.mean_hw(xb, n, hw[0] * hw[1], c, c, out_f32=yb, out_i8=qb, ld_i8=112, out_scale=scale)
+    _same_f32(yb.download((n, c), np.float32), want)
+    np.testing.assert_array_equal(qb.download((n, 112), np.int8)[:, :c], ref.quantize_activation(want, scale))
+
+
+@pytest.mark.parametrize("stride", [1, 2])
+def test_dwconv_bit_exact(cuda_device, stride):
+    K, DB = _k()
+    rng = np.random.default_rng(stride)
+    n, c, h, w = 2, 96, 13, 13
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = rng.standard_normal((c, 1, 3, 3)).astype(np.float32)
+    bias = rng.standard_normal((c, 1, 1)).astype(np.float32)
+    want = ref.dwconv2d(x, wt, (stride, stride), (1, 1), steps=[("add", 2, False), ("maximum", 3, False),
+                                                                 ("minimum", 4, False)],
+                        operands=[bias, np.float32(0), np.float32(6)])
+    oh = want.shape[2]
+    xb = DB.from_array(np.ascontiguousarray(x.transpose(0, 2, 3, 1)))
+    wb = DB.from_array(np.ascontiguousarray(wt[:, 0].reshape(c, 9).T))
+    bb = DB.from_array(K.pad_channels(bias))
+    yb = DB(n * oh * oh * c * 4)
+    K.dwconv2d(xb, n, h, w, c, wb, 3, 3, (stride, stride), (1, 1), (1, 1),
+               K.Epi([K.Step("add", "channel", ptr=bb), K.Step("maximum", "scalar", scalar=0.0),
+                      K.Step("minimum", "scalar", scalar=6.0)], out_f32=yb, ld_f32=c))
+    _same_f32(yb.download((n, oh, oh, c), np.float32).transpose(0, 3, 1, 2), want)
+
+
+def test_layout_roundtrip(cuda_device):
+    K, DB = _k()
+    x = np.random.default_rng(0).standard_normal((3, 70, 9, 13)).astype(np.float32)
+    xb, yb, zb = DB.from_array(x), DB(x.nbytes), DB(x.nbytes)
+    K.nchw_to_nhwc(xb, 3, 70, 9, 13, yb, 70)
+    np.testing.assert_array_equal(yb.download((3, 9, 13, 70), np.float32), x.transpose(0, 2, 3, 1))
+    K.nhwc_to_nchw(yb, 3, 9, 13, 70, 70, zb)
+    np.testing.assert_array_equal(zb.download(x.shape, np.float32), x)
