@@ -1,0 +1,200 @@
+"""The benchmark workloads, built as MIRA IR graphs with the reference's own `ir.Graph` API
+(the reference's ONNX importer needs `onnx`, which is not installed; its BatchNorm lowering is
+replaced by folding BN into the conv weights and biases before quantization, as the configs ask).
+
+  mlp          784-512-512-10 ReLU MLP, Kaiming-normal weights, zero biases (config 1)
+  resnet18     torchvision ResNet-18 topology at 224x224, Kaiming-normal convs, BN folded (config 3)
+  mobilenet_v2 torchvision MobileNetV2 (width 1.0, ReLU6, inverted residuals), BN folded (config 4)
+
+Weights depend only on `seed`, not on the batch size, so a network built at two batch sizes is the
+same network.  `compile_w8a8` compiles through MIRA's own driver (mira/compiler.py compile_ir:
+optimize, fuse_epilogues, quantize_w8a8 with host calibration, partition, target compile).
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import numpy as np
+
+from .hostfw import import_mira
+from .plugin import install
+
+
+def _ir():
+    import_mira()
+    from mira import ir
+    from mira.types import TensorType
+    return ir, TensorType
+
+
+class _Net:
+    def __init__(self, name: str, input_shape: tuple, seed: int):
+        ir, TT = _ir()
+        self.ir = ir
+        self.x = ir.Value(TT("f32", tuple(input_shape)), name="x")
+        self.g = ir.Graph(name, [self.x], [], [])
+        self.rng = np.random.default_rng(seed)
+
+    def const(self, arr):
+        return self.g.const(np.asarray(arr, np.float32))
+
+    def op(self, kind, inputs, attrs=None):
+        return self.g.add(kind, list(inputs), attrs or {})
+
+    def bn_fold(self, w: np.ndarray, cout: int, randomize: bool):
+        """Fold an inference BatchNorm (eps 1e-5) into conv weights/bias."""
+        if randomize:
+            gamma = self.rng.uniform(0.7, 1.3, cout)
+            beta = self.rng.normal(0.0, 0.1, cout)
+            mean = self.rng.normal(0.0, 0.1, cout)
+            var = self.rng.uniform(0.7, 1.3, cout)
+        else:
+            gamma, beta, mean, var = np.ones(cout), np.zeros(cout), np.zeros(cout), np.ones(cout)
+        s = gamma / np.sqrt(var + 1e-5)
+        return (w * s[:, None, None, None]).astype(np.float32), (beta - mean * s).astype(np.float32)
+
+    def conv_bn(self, x, cin, cout, k, stride, pad, act=None, groups=1, randomize_bn=True):
+        fan_out = cout * k * k // groups
+        w = (self.rng.standard_normal((cout, cin // groups, k, k)) * np.sqrt(2.0 / fan_out)).astype(np.float32)
+        w, b = self.bn_fold(w, cout, randomize_bn)
+        attrs = {"stride": (stride, stride), "padding": (pad, pad)}
+        if groups != 1:
+            attrs["groups"] = groups
+        y = self.op("conv2d", [x, self.const(w)], attrs)
+        y = self.op("add", [y, self.const(b.reshape(cout, 1, 1))])
+        if act == "relu":
+            y = self.op("relu", [y])
+        elif act == "relu6":
+            y = self.op("maximum", [y, self.const(np.float32(0.0))])
+            y = self.op("minimum", [y, self.const(np.float32(6.0))])
+        return y
+
+    def linear(self, x, fin, fout, bias=True, std=None):
+        w = (self.rng.standard_normal((fin, fout)) * (std if std is not None else np.sqrt(2.0 / fin))).astype(np.float32)
+        y = self.op("matmul", [x, self.const(w)])
+        if bias:
+            y = self.op("add", [y, self.const(self.rng.normal(0.0, 0.05, fout).astype(np.float32))])
+        return y
+
+    def finish(self, out):
+        self.g.outputs = [out]
+        self.g.verify()
+        return self.g
+
+
+def mlp(batch: int = 256, seed: int = 0):
+    """Config 1: x f32[B, 784] -> 512 -> ReLU -> 512 -> ReLU -> 10, Kaiming-normal, zero biases
+    (MIRA's simplify pass deletes the zero-bias adds, reference passes.py:56-57)."""
+    n = _Net("mlp", (batch, 784), seed)
+    h = n.x
+    for fin, fout, act in ((784, 512, True), (512, 512, True), (512, 10, False)):
+        w = (n.rng.standard_normal((fin, fout)) * np.sqrt(2.0 / fin)).astype(np.float32)
+        h = n.op("matmul", [h, n.const(w)])
+        h = n.op("add", [h, n.const(np.zeros(fout, np.float32))])
+        if act:
+            h = n.op("relu", [h])
+    return n.finish(h)
+
+
+def resnet18(batch: int = 1, seed: int = 0, image: int = 224, num_classes: int = 1000):
+    """Config 3: ResNet-18 (BasicBlock x [2, 2, 2, 2]); stem 7x7/2 conv, -inf pad + 3x3/2 max pool,
+    global mean, FC.  BN (random inference statistics) folded into each conv."""
+    n = _Net("resnet18", (batch, 3, image, image), seed)
+    y = n.conv_bn(n.x, 3, 64, 7, 2, 3, act="relu")
+    y = n.op("pad", [y], {"pads": ((0, 0), (0, 0), (1, 1), (1, 1)), "value": -np.inf})
+    y = n.op("maxpool2d", [y], {"size": 3, "stride": 2})
+    cin = 64
+    for cout, stride in ((64, 1), (128, 2), (256, 2), (512, 2)):
+        for b in range(2):
+            s = stride if b == 0 else 1
+            out = n.conv_bn(y, cin, cout, 3, s, 1, act="relu")
+            out = n.conv_bn(out, cout, cout, 3, 1, 1)
+            short = n.conv_bn(y, cin, cout, 1, s, 0) if (s != 1 or cin != cout) else y
+            y = n.op("relu", [n.op("add", [out, short])])
+            cin = cout
+    y = n.op("reduce_mean", [y], {"axes": (2, 3), "keepdims": False})
+    y = n.linear(y, 512, num_classes, std=np.sqrt(1.0 / 512))
+    return n.finish(y)
+
+
+MBV2_SETTINGS = ((1, 16, 1, 1), (6, 24, 2, 2), (6, 32, 3, 2), (6, 64, 4, 2), (6, 96, 3, 1), (6, 160, 3, 2),
+                 (6, 320, 1, 1))
+
+
+def mobilenet_v2(batch: int = 1, seed: int = 0, image: int = 224, num_classes: int = 1000):
+    """Config 4: MobileNetV2 width 1.0: 3x3/2 stem, inverted residual blocks (expand 1x1, depthwise
+    3x3, project 1x1; residual when stride 1 and channels match), 1x1 to 1280, mean, FC.  ReLU6 is
+    maximum(., 0) then minimum(., 6), which MIRA fuses into the conv epilogues."""
+    n = _Net("mobilenet_v2", (batch, 3, image, image), seed)
+    y = n.conv_bn(n.x, 3, 32, 3, 2, 1, act="relu6")
+    cin = 32
+    for t, c, reps, s in MBV2_SETTINGS:
+        for r in range(reps):
+            stride = s if r == 0 else 1
+            hidden = cin * t
+            h = y
+            if t != 1:
+                h = n.conv_bn(h, cin, hidden, 1, 1, 0, act="relu6")
+            h = n.conv_bn(h, hidden, hidden, 3, stride, 1, act="relu6", groups=hidden)
+            h = n.conv_bn(h, hidden, c, 1, 1, 0)
+            y = n.op("add", [y, h]) if (stride == 1 and cin == c) else h
+            cin = c
+    y = n.conv_bn(y, cin, 1280, 1, 1, 0, act="relu6")
+    y = n.op("reduce_mean", [y], {"axes": (2, 3), "keepdims": False})
+    y = n.linear(y, 1280, num_classes, std=np.sqrt(1.0 / 1280))
+    return n.finish(y)
+
+
+BUILDERS: dict[str, Callable] = {"mlp": mlp, "resnet18": resnet18, "mobilenet_v2": mobilenet_v2}
+
+
+def random_inputs(graph, seed: int) -> dict:
+    """Seeded N(0, 1) f32 inputs keyed by input name (like the reference CLI's _inputs, cli.py:76-80)."""
+    rng = np.random.default_rng(seed)
+    return {v.name: rng.standard_normal(v.type.shape).astype(np.float32) for v in graph.inputs}
+
+
+def compile_w8a8(name: str, batch: int, target: str, *, seed: int = 0, n_calib: int = 4, calib_seed: int = 100,
+                 calib_batch: Optional[int] = None, **kw):
+    """Build workload `name` at `batch` and compile it W8A8 for `target` through MIRA's compile_ir.
+
+    Calibration feeds are `n_calib` seeded N(0, 1) batches.  With `calib_batch` (smaller than
+    `batch`), calibration runs on the same network built at `calib_batch` - the reference's own
+    _calibrate (quantize.py:73-92) over those feeds - and the resulting per-value peaks are carried
+    over to the large graph op by op, so large batches do not pay hours of host-side calibration."""
+    if target in ("cuda", "b200"):
+        install()
+    else:
+        import_mira()
+    from mira import compiler, passes
+    from mira import quantize as Q
+    build = BUILDERS[name]
+    g = build(batch, seed=seed)
+    if calib_batch is None or calib_batch == batch:
+        cal = [random_inputs(g, calib_seed + i) for i in range(n_calib)]
+        return compiler.compile_ir(g, target, quantize="w8a8", calibration=cal, precision=None, **kw)
+    small = build(calib_batch, seed=seed)
+    passes.optimize(small, precision=None)
+    passes.optimize(g, precision=None)
+
+    def candidates(graph):
+        return [op for op in graph.ops if op.kind in ("matmul", "conv2d") and Q._w8a8_weight(op) is not None]
+
+    cs, cb = candidates(small), candidates(g)
+    if len(cs) != len(cb):
+        raise RuntimeError("small and large graphs differ in structure")
+    cal = [random_inputs(small, calib_seed + i) for i in range(n_calib)]
+    peak_small = Q._calibrate(small, cal, {op.inputs[0] for op in cs})
+    pos_small = {v: i for i, v in enumerate(small.inputs + [r for op in small.ops for r in op.results])}
+    big_values = g.inputs + [r for op in g.ops for r in op.results]
+    peaks = {}
+    for s_op, b_op in zip(cs, cb):
+        peaks[b_op.inputs[0]] = peak_small[s_op.inputs[0]]
+        if pos_small.get(s_op.inputs[0]) is not None and big_values[pos_small[s_op.inputs[0]]] is not b_op.inputs[0]:
+            raise RuntimeError("calibrated value does not map onto the large graph")
+    original = Q._calibrate
+    Q._calibrate = lambda graph, feeds, watch: {v: peaks[v] for v in watch}
+    try:
+        return compiler.compile_ir(g, target, optimize=False, quantize="w8a8", calibration=[{}], precision=None, **kw)
+    finally:
+        Q._calibrate = original

@@ -57,11 +57,13 @@ def conv_channels(c: int) -> int:
     return 4 if c <= 4 else round_up(c, 16)
 
 
-def conv_weight(q_oihw: np.ndarray) -> tuple[np.ndarray, int]:
+def conv_weight(q_oihw: np.ndarray, cp: Optional[int] = None) -> tuple[np.ndarray, int]:
     """Reference qconv2d weight int8 [O, C, KH, KW] -> [O, round_up(KH*KW*Cp, 16)] with
-    k = (i * KW + j) * Cp + c (zero padded channels).  Returns (weights, Cp)."""
+    k = (i * KW + j) * Cp + c (zero padded channels; Cp defaults to conv_channels(C)).
+    Returns (weights, Cp)."""
     o, c, kh, kw = q_oihw.shape
-    cp = conv_channels(c)
+    cp = conv_channels(c) if cp is None else int(cp)
+    assert cp >= c
     t = np.zeros((o, kh, kw, cp), np.int8)
     t[:, :, :, :c] = q_oihw.transpose(0, 2, 3, 1)
     k = kh * kw * cp

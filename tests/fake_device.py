@@ -1,0 +1,151 @@
+"""A host-side stand-in for CudaDevice (test infrastructure).
+
+It executes the launch records of a Plan with the CPU oracle on NumPy buffers laid out exactly as
+the device buffers are (NHWC int8 with padded channels, K-major weights, padded per-channel
+arrays).  Driving MIRA programs through it checks the planner - representations, layouts, strides,
+epilogue operand classification - against the reference cpu target without a GPU.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from oracle import w8a8 as ref
+
+
+class FakeBuf:
+    def __init__(self, nbytes: int):
+        self.data = np.zeros(max(int(nbytes), 16), np.uint8)
+        self.nbytes = int(nbytes)
+
+    def view(self, dtype, shape):
+        n = int(np.prod(shape, dtype=np.int64))
+        return self.data[: n * np.dtype(dtype).itemsize].view(dtype).reshape(shape)
+
+
+class FakePinned(FakeBuf):
+    def view(self, shape, dtype):  # PinnedBuffer's argument order
+        return super().view(dtype, shape)
+
+
+class FakeDevice:
+    name = "fake"
+    index = 0
+
+    def __init__(self):
+        self.launched: list[str] = []
+
+    def activate(self):
+        pass
+
+    def alloc(self, nbytes, zero=False):
+        return FakeBuf(nbytes)
+
+    def upload(self, arr):
+        arr = np.ascontiguousarray(arr)
+        b = FakeBuf(arr.nbytes)
+        b.data[: arr.nbytes] = arr.reshape(-1).view(np.uint8)
+        return b
+
+    def pinned(self, nbytes):
+        return FakePinned(nbytes)
+
+    def h2d(self, dst, src, nbytes):
+        dst.data[:nbytes] = src.data[:nbytes]
+
+    def d2h(self, dst, src, nbytes):
+        dst.data[:nbytes] = src.data[:nbytes]
+
+    def sync(self):
+        pass
+
+    def thunk(self, launch):
+        fn = getattr(self, "_" + launch.kind)
+        return lambda: (self.launched.append(launch.kind), fn(**launch.args))
+
+    # ------------------------------------------------------------------ kernels
+
+    def _quantize_rows(self, x, rows, cols, ld_x, scale, xq, ld_q):
+        xv = x.view(np.float32, (rows, ld_x))[:, :cols]
+        q = xq.view(np.int8, (rows, ld_q))
+        q[:, :cols] = ref.quantize_activation(xv, scale)
+        q[:, cols:] = 0
+
+    def _quantize_nchw(self, x, n, c, h, w, scale, xq, cp):
+        q = xq.view(np.int8, (n, h, w, cp))
+        q[..., :c] = ref.quantize_activation(x.view(np.float32, (n, c, h, w)), scale).transpose(0, 2, 3, 1)
+        q[..., c:] = 0
+
+    def _nchw_to_nhwc(self, x, n, c, h, w, y, ldc):
+        y.view(np.float32, (n, h, w, ldc))[..., :c] = x.view(np.float32, (n, c, h, w)).transpose(0, 2, 3, 1)
+
+    def _nhwc_to_nchw(self, x, n, h, w, c, ldc, y):
+        y.view(np.float32, (n, c, h, w))[...] = x.view(np.float32, (n, h, w, ldc))[..., :c].transpose(0, 3, 1, 2)
+
+    def _copy(self, dst, src, nbytes):
+        dst.data[:nbytes] = src.data[:nbytes]
+
+    def _epi(self, y, epi, M, N):
+        """y: f32 [M, N] dequantized; applies steps and writes the outputs."""
+        for s in epi.steps:
+            if s.operand == "none":
+                y = ref.UNARY[s.op](y).astype(np.float32)
+                continue
+            if s.operand == "scalar":
+                o = np.float32(s.scalar)
+            elif s.operand == "channel":
+                o = s.ptr.view(np.float32, (N,))
+            elif s.operand == "full":
+                o = s.ptr.view(np.float32, (M, s.ld))[:, :N]
+            else:
+                o = s.ptr.view(np.float32, (M, 1))
+            y = (ref.BINARY[s.op](o, y) if s.swapped else ref.BINARY[s.op](y, o)).astype(np.float32)
+        if epi.out_f32 is not None:
+            epi.out_f32.view(np.float32, (M, epi.ld_f32))[:, :N] = y
+        if epi.out_i8 is not None:
+            q = epi.out_i8.view(np.int8, (M, epi.ld_i8))
+            q[:, :N] = ref.quantize_activation(y, epi.out_scale)
+            q[:, N:] = 0
+
+    def _dequant(self, acc, dq, N):
+        s64 = dq[0].view(np.float64, (N,))
+        return (acc.astype(np.float64) * s64).astype(np.float32)
+
+    def _qgemm(self, M, N, K, A, lda, B, ldb, dq, epi):
+        a = A.view(np.int8, (M, lda))[:, :K]
+        b = B.view(np.int8, (N, ldb))[:, :K]
+        acc = ref.int_matmul(a, b.T)
+        self._epi(self._dequant(acc, dq, N), epi, M, N)
+
+    def _qconv2d(self, n, h, w, cp, x, o, kh, kw, wq, ldw, stride, padding, dilation, dq, epi):
+        xn = x.view(np.int8, (n, h, w, cp)).transpose(0, 3, 1, 2)
+        wt = wq.view(np.int8, (o, ldw))[:, : kh * kw * cp].reshape(o, kh, kw, cp).transpose(0, 3, 1, 2)
+        acc = ref.int_conv2d(xn, wt, stride, padding, dilation)       # [n, o, oh, ow]
+        oh, ow = acc.shape[2:]
+        rows = acc.transpose(0, 2, 3, 1).reshape(n * oh * ow, o)
+        self._epi(self._dequant(rows, dq, o), epi, n * oh * ow, o)
+
+    def _maxpool(self, n, h, w, c, ldc, size, stride, pad, pad_value, x_f32=None, x_i8=None, out_f32=None, ldo=0,
+                 out_i8=None, ldo_i8=0, scale=1.0):
+        xv = x_f32.view(np.float32, (n, h, w, ldc))[..., :c].transpose(0, 3, 1, 2)
+        y = ref.maxpool2d(xv, size, stride, pad, pad_value)
+        oh, ow = y.shape[2:]
+        rows = y.transpose(0, 2, 3, 1).reshape(-1, c)
+        if out_f32 is not None:
+            out_f32.view(np.float32, (n * oh * ow, ldo))[:, :c] = rows
+        if out_i8 is not None:
+            out_i8.view(np.int8, (n * oh * ow, ldo_i8))[:, :c] = ref.quantize_activation(rows, scale)
+
+    def _mean_hw(self, x, n, hw, c, ldc, out_f32=None, out_i8=None, ld_i8=0, scale=1.0):
+        xv = x.view(np.float32, (n, hw, ldc))[..., :c].transpose(0, 2, 1)
+        m = ref.mean_hw(np.ascontiguousarray(xv).reshape(n, c, hw, 1))
+        if out_f32 is not None:
+            out_f32.view(np.float32, (n, c))[...] = m
+        if out_i8 is not None:
+            out_i8.view(np.int8, (n, ld_i8))[:, :c] = ref.quantize_activation(m, scale)
+
+    def _dwconv(self, x, n, h, w, c, wt, kh, kw, stride, padding, dilation, epi):
+        xn = x.view(np.float32, (n, h, w, c)).transpose(0, 3, 1, 2)
+        wk = wt.view(np.float32, (kh * kw, c)).T.reshape(c, 1, kh, kw)
+        y = ref.dwconv2d(xn, wk, stride, padding, dilation)
+        oh, ow = y.shape[2:]
+        self._epi(y.transpose(0, 2, 3, 1).reshape(-1, c), epi, n * oh * ow, c)

