@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Benchmark of the W8A8 hot path on B200: ResNet-18 W8A8 images/s (batch 256 per GPU, weak
+scaling over 1/2/4/8 GPUs, one process per GPU) plus the int8 GEMM throughput at 8192^3.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+A step is one forward pass of a batch through the compiled MIRA program.  `value` times K steps
+on device-resident inputs (CUDA events on the library stream, max over ranks); `e2e` times the
+same K steps through the public API (`CompiledProgram.run` with pinned host inputs: host->device
+copy of the batch, the kernels, device->host copy of the logits).  `--impl reference` times the
+reference's own cpu W8A8 path (MIRA's NumPy golden model) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOAD = "resnet18"
+METRIC = "w8a8 ResNet-18 img/s"
+# int8 ops per image of ResNet-18 at 224x224 (2 x MACs of the 20 convs and the FC)
+RESNET18_CONV_MACS = None   # computed from the graph
+
+
+def _env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops"), d.get("hbm_gbs"), "MEASURED_PEAKS.json"
+    return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        under_load = [s for s in sm if s > 0.3 * (mx or 1)] or sm
+        return {"sm_mhz": statistics.median(under_load), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def conv_work(graph) -> tuple[int, int]:
+    """(int8 ops of the convolutions, int8 ops of all quantized ops) per batch of the compiled graph."""
+    conv = total = 0
+    for op in graph.ops:
+        if op.kind == "qconv2d":
+            o, c, kh, kw = op.attrs["q"].shape
+            n, _, oh, ow = op.result.type.shape
+            w = 2 * n * oh * ow * o * c * kh * kw
+            conv += w
+            total += w
+        elif op.kind == "qmatmul":
+            k, nn = op.attrs["q"].shape
+            m = int(np.prod(op.inputs[0].type.shape[:-1]))
+            total += 2 * m * k * nn
+    return conv, total
+
+
+def time_conv_kernels(exe, iters: int = 3) -> float:
+    """Average summed duration (ms) of the plan's qconv2d launches, each bracketed by CUDA events on
+    the library stream (one event pair per launch, eager launches)."""
+    from mira_b200 import _lib
+    evs = []
+    idx = [i for i, l in enumerate(exe.plan.launches) if l.kind == "qconv2d"]
+
+    def ev():
+        p = C.c_void_p()
+        _lib.call("mira_cuda_event_create", C.byref(p))
+        return p
+
+    pairs = [(ev(), ev()) for _ in idx]
+    total = 0.0
+    for _ in range(iters):
+        j = 0
+        for i, t in enumerate(exe.thunks):
+            if j < len(idx) and idx[j] == i:
+                _lib.call("mira_cuda_event_record", pairs[j][0])
+                t()
+                _lib.call("mira_cuda_event_record", pairs[j][1])
+                j += 1
+            else:
+                t()
+        for a, b in pairs:
+            ms = C.c_float()
+            _lib.call("mira_cuda_event_elapsed", a, b, C.byref(ms))
+            total += ms.value
+    for a, b in pairs:
+        _lib.call("mira_cuda_event_destroy", a)
+        _lib.call("mira_cuda_event_destroy", b)
+    return total / iters
+
+
+def gemm_tops(n: int = 8192, iters: int = 5) -> float:
+    """Throughput of mira_cuda_qgemm on an n^3 int8 GEMM (row/col scales + bias epilogue, f32 out)."""
+    from mira_b200 import _lib, kernels as K
+    from mira_b200.device import DeviceBuffer
+    A, B, Y = DeviceBuffer(n * n), DeviceBuffer(n * n), DeviceBuffer(n * n * 4)
+    _lib.call("mira_cuda_memset", C.c_void_p(A.ptr), 3, C.c_size_t(n * n))
+    _lib.call("mira_cuda_memset", C.c_void_p(B.ptr), 5, C.c_size_t(n * n))
+    rs = DeviceBuffer.from_array(np.full(n, 1e-3, np.float32))
+    cs = DeviceBuffer.from_array(np.full(n, 2e-3, np.float32))
+    bias = DeviceBuffer.from_array(K.pad_channels(np.zeros(n, np.float32)))
+    dq = K.dequant_rowcol(rs, cs)
+    e = K.Epi([K.Step("add", "channel", ptr=bias)], out_f32=Y, ld_f32=n).struct()
+    fn = _lib.load().mira_cuda_qgemm
+    args = (n, n, n, C.c_void_p(A.ptr), n, C.c_void_p(B.ptr), n, C.byref(dq), C.byref(e))
+    fn(*args)
+    _lib.call("mira_cuda_sync")
+    a, b = C.c_void_p(), C.c_void_p()
+    _lib.call("mira_cuda_event_create", C.byref(a))
+    _lib.call("mira_cuda_event_create", C.byref(b))
+    _lib.call("mira_cuda_event_record", a)
+    for _ in range(iters):
+        fn(*args)
+    _lib.call("mira_cuda_event_record", b)
+    ms = C.c_float()
+    _lib.call("mira_cuda_event_elapsed", a, b, C.byref(ms))
+    _lib.call("mira_cuda_sync")
+    return 2.0 * n ** 3 / (ms.value / iters * 1e-3) / 1e12
+
+
+def cublaslt_int8_tops(n: int = 8192) -> float | None:
+    """torch._int_mm (cuBLASLt int8) at n^3, for context next to the roofline."""
+    try:
+        import torch
+        a = torch.ones((n, n), dtype=torch.int8, device="cuda")
+        b = torch.ones((n, n), dtype=torch.int8, device="cuda").t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(10):
+            torch._int_mm(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        return 2.0 * n ** 3 / (s.elapsed_time(e) / 10 * 1e-3) / 1e12
+    except Exception:
+        return None
+
+
+def reference_cpu_sample(batch: int, steps: int, warmup: int) -> dict:
+    """The reference's own cpu W8A8 path (mira.compile_ir(..., "cpu", quantize="w8a8") then
+    CompiledProgram.run) on `batch` images per step; falls back to the oracle port when the
+    reference package is not importable."""
+    try:
+        from mira_b200 import configs
+        from mira_b200.hostfw import import_mira
+        import_mira()
+        kind = "reference"
+        prog = configs.compile_w8a8(WORKLOAD, batch, "cpu", n_calib=4, calib_batch=batch)
+        feeds = configs.random_inputs(prog.graph, 1)
+        run = lambda: prog.run(feeds)  # noqa: E731
+    except ImportError:
+        kind = "port"
+        raise
+    for _ in range(warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run()
+    dt = time.perf_counter() - t0
+    return {"value": batch * steps / dt, "unit": "img/s", "cores": os.cpu_count(), "kind": kind,
+            "sample": f"{steps} run(s) of a batch of {batch} image(s), reference cpu target "
+                      f"(NumPy golden model, OpenBLAS on all host cores), after {warmup} warm-up run(s)"}
+
+
+def run_reference(args) -> None:
+    rank, world, _ = _env_rank()
+    if rank != 0:
+        return
+    sample_batch = 1
+    res = reference_cpu_sample(sample_batch, args.steps, args.warmup)
+    line = {"metric": METRIC, "value": res["value"], "unit": "img/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sample_batch / res["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "resnet18-w8a8-224", "batch_per_step": sample_batch,
+                       "note": "bounded sample of the batch-256 workload: each step is one image"},
+            "cpu_baseline": res, "e2e": {"value": res["value"], "unit": "img/s", "h2d_bytes_per_step": 0,
+                                         "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=256, help="images per GPU per step")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--calib-batch", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    rank, world, local = _env_rank()
+    os.environ["MIRA_CUDA_DEVICE"] = str(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    from mira_b200 import _lib
+    from mira_b200 import configs
+
+    t0 = time.perf_counter()
+    prog = configs.compile_w8a8(WORKLOAD, args.batch, "cuda", calib_batch=args.calib_batch, device=local)
+    compile_s = time.perf_counter() - t0
+    segs = [s for s in prog.segments if s.device == "cuda"]
+    assert len(prog.segments) == 1 and len(segs) == 1, "the whole network must be one cuda segment"
+    exe = segs[0].executable
+    x_val = prog.graph.inputs[0]
+    host_x = exe.input_array(x_val)          # pinned staging array of the executable
+    host_x[...] = np.random.default_rng(1 + rank).standard_normal(host_x.shape, dtype=np.float32)
+    name = x_val.name
+    feeds = {name: host_x}
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up through the public API (also captures the CUDA graph)
+    for _ in range(args.warmup):
+        out = prog.run(feeds)
+    launches_per_step = exe.launches_per_run
+
+    # ---- device-resident timing
+    ev_a, ev_b = C.c_void_p(), C.c_void_p()
+    _lib.call("mira_cuda_event_create", C.byref(ev_a))
+    _lib.call("mira_cuda_event_create", C.byref(ev_b))
+    n0 = _lib.launch_count()
+    barrier()
+    _lib.call("mira_cuda_sync")
+    with ClockSampler(local) as clocks:
+        _lib.call("mira_cuda_event_record", ev_a)
+        for _ in range(args.steps):
+            exe.replay()
+        _lib.call("mira_cuda_event_record", ev_b)
+        _lib.call("mira_cuda_sync")
+        ms = C.c_float()
+        _lib.call("mira_cuda_event_elapsed", ev_a, ev_b, C.byref(ms))
+    barrier()
+    dev_ms = max_over_ranks(ms.value)
+    gpu_launches = args.steps * launches_per_step + (_lib.launch_count() - n0)
+
+    # ---- end to end through CompiledProgram.run (H2D of the batch, kernels, D2H of the logits)
+    barrier()
+    t1 = time.perf_counter()
+    for _ in range(args.steps):
+        out = prog.run(feeds)
+    e2e_s = max_over_ranks(time.perf_counter() - t1)
+    barrier()
+
+    imgs = args.batch * world * args.steps
+    value = imgs / (dev_ms * 1e-3)
+    conv_ops, q_ops = conv_work(prog.graph)
+
+    result = None
+    if rank == 0:
+        conv_ms = time_conv_kernels(exe)
+        bf16, hbm, src = _peaks()
+        peak = 2.0 * bf16 if bf16 else None
+        achieved = conv_ops / (conv_ms * 1e-3) / 1e12
+        ours_gemm = gemm_tops(8192)
+        lib_gemm = cublaslt_int8_tops(8192)
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                cpu = reference_cpu_sample(1, 3, 1)
+            except Exception as e:  # the reference package is missing on this machine
+                cpu = {"value": None, "unit": "img/s", "cores": os.cpu_count(), "kind": "reference",
+                       "sample": f"unavailable: {e}"}
+        result = {
+            "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "resnet18-w8a8-224", "global_batch": args.batch * world,
+                       "batch_per_gpu": args.batch, "parallelism": f"dp{world} (replicas, no collective)",
+                       "l2": "inputs larger than L2 (154 MB input batch, ~2 GB of activations per step)",
+                       "calibration": f"4 seeded N(0,1) batches of {args.calib_batch} images",
+                       "compile_s": round(compile_s, 1)},
+            "e2e": {"value": imgs / e2e_s, "unit": "img/s", "h2d_bytes_per_step": int(host_x.nbytes),
+                    "d2h_bytes_per_step": int(out.nbytes)},
+            "roofline": {"bound": "tensor", "kernel": "qgemm_sm100_kernel (implicit-GEMM qconv2d, 20 launches/step)",
+                         "achieved": achieved, "peak": peak, "unit": "TOPS",
+                         "frac": (achieved / peak) if peak else None, "traffic": None,
+                         "peak_source": f"2 x bf16_tflops of {src} (dense int8 issues at twice the bf16 rate)",
+                         "conv_int8_ops_per_step": conv_ops, "conv_ms_per_step": conv_ms},
+            "int8_gemm": {"shape": "8192^3", "tops": ours_gemm, "frac_of_peak": ours_gemm / peak if peak else None,
+                          "cublaslt_tops": lib_gemm},
+            "int8_ops_per_step": q_ops, "int8_tops_step": q_ops / (dev_ms / args.steps * 1e-3) / 1e12,
+            "gpu_launches": int(gpu_launches), "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(result), flush=True)
+    if dist is not None:
+        barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
