@@ -164,6 +164,18 @@ int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t*
                       int64_t dil_h, int64_t dil_w, const mira_dequant* dq,
                       const mira_epilogue* epi);
 
+/* qconv2d followed by max pooling, fused: the reference's qconv2d (ops.py:630-634) with its
+ * epilogue, then pad (ops.py:469-470, `pool_pad` pixels of `pool_pad_value`) and maxpool2d
+ * (ops.py:293-296, window `pool_size`, stride `pool_stride`).  The conv outputs never leave the
+ * SM: each tile computes the conv pixels under a block of pooled outputs and pools them in shared
+ * memory; `epi`'s outputs are the pooled [n*ph*pw, o] f32 / int8 tensors.  o <= 64; epilogue
+ * operands must be scalar or per-channel. */
+int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o,
+                              int64_t kh, int64_t kw, const int8_t* wq, int64_t ldw, int64_t stride_h,
+                              int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
+                              int64_t pool_size, int64_t pool_stride, int64_t pool_pad, float pool_pad_value,
+                              const mira_dequant* dq, const mira_epilogue* epi);
+
 /* Max pooling over NHWC, reference ops.py:293-296 (maxpool2d) preceded by an optional constant
  * pad (ops.py:469-470) of `pad` pixels holding `pad_value` (the -inf pad in front of ResNet's
  * pool).  f32 in -> f32 out (out_f32) and/or int8 out; int8 in (x_i8 non-NULL) -> int8 out,

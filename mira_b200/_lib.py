@@ -72,6 +72,9 @@ SIGNATURES: dict[str, tuple] = {
     "mira_cuda_qgemm": (_i32, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, C.POINTER(Dequant), C.POINTER(Epilogue)]),
     "mira_cuda_qconv2d": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
                                  _i64, _i64, C.POINTER(Dequant), C.POINTER(Epilogue)]),
+    "mira_cuda_qconv2d_maxpool": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
+                                         _i64, _i64, _i64, _i64, _i64, _i64, _f32, C.POINTER(Dequant),
+                                         C.POINTER(Epilogue)]),
     "mira_cuda_maxpool2d_nhwc": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _i64,
                                         _vp, _i64, _f32]),
     "mira_cuda_mean_hw_nhwc": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _f32]),

@@ -20,18 +20,17 @@ namespace mira {
 // unless an f32 rounding midpoint lies within |X| 2^-53 of X, and RN32(D) equals RN32(X) unless a
 // midpoint lies between D and X.  So if RN32(D - d) == RN32(D + d) with d = |a| hi 2^-40 (far
 // larger than both distances), no midpoint is near and RN32(D) is the exact answer.  Otherwise
-// (about 2 in 10^5 elements, or |acc| >= 2^22) the product is done in float64 like the reference.
-// Fast path of the above; returns false when the float64 product is needed.
+// (about 2 in 10^5 elements, or |acc| >= 2^22) the product must be done in float64 like the
+// reference: this branch-free function writes the candidate and returns false in those cases.
 __device__ __forceinline__ bool dequant_fast(int32_t acc, float hi, float lo, float& y) {
-  const uint32_t biased = static_cast<uint32_t>(acc) + (1u << 22);
-  if (biased >= (1u << 23)) return false;
+  const bool in_range = static_cast<uint32_t>(acc) + (1u << 22) < (1u << 23);
   const float a = __fsub_rn(__int_as_float(0x4B400000 + acc), 12582912.0f);
   const float p = __fmul_rn(a, lo);
   const float d = __fmul_rn(fabsf(a), __fmul_rn(hi, 0x1p-40f));
   const float y_lo = __fmaf_rn(a, hi, __fsub_rn(p, d));
   const float y_hi = __fmaf_rn(a, hi, __fadd_rn(p, d));
   y = y_lo;
-  return y_lo == y_hi;
+  return in_range && (y_lo == y_hi);
 }
 
 // Row/column scales: S = f64(r) * f64(c) is exact in float64 (24 + 24 significant bits), and
@@ -66,12 +65,18 @@ __device__ __forceinline__ uint32_t pack4_i8(uint32_t a, uint32_t b, uint32_t c,
   return __byte_perm(ab, cd, 0x5410);
 }
 
-// NumPy float32 maximum/minimum (NaN propagates from either side).
+// NumPy float32 maximum/minimum: a NaN on either side propagates (PTX max.NaN / min.NaN).  The
+// one difference from NumPy is the sign of a zero result when +0.0 meets -0.0 (NumPy returns the
+// first operand); both quantize to 0.
 __device__ __forceinline__ float np_maximum(float a, float b) {
-  return (a >= b || a != a) ? a : b;
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 __device__ __forceinline__ float np_minimum(float a, float b) {
-  return (a <= b || a != a) ? a : b;
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 
 // Reference ops.py:94-96 (tanh form of GELU), evaluated in the same order in float32.  tanhf and

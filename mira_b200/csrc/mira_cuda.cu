@@ -145,10 +145,10 @@ static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes
 
 // ---------------------------------------------------------------- qgemm dispatch
 
-template <int BN, int STAGES, int AMODE, bool ROWCOL>
+template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false>
 static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, const QgParams& p) {
-  using Cfg = QgCfg<BN, STAGES, AMODE>;
-  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL>;
+  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL>;
+  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL>;
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[dev->device]) {
     MIRA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM)),
@@ -161,12 +161,22 @@ static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUte
   return after_launch("qgemm_sm100_kernel");
 }
 
+// Tile width BN and the epilogue/pipeline split: short reductions (at most 24 K-blocks of 128)
+// are epilogue-bound and get 16 epilogue warps (G = 4); long ones get 8 epilogue warps and the
+// shared memory goes to deeper operand pipelines.
 template <int AMODE, bool ROWCOL>
 static int launch_qgemm_bn(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, QgParams& p, int bn) {
+  const bool short_k = p.num_kb <= 24;
   switch (bn) {
-    case 64: return launch_qgemm_cfg<64, 8, AMODE, ROWCOL>(dev, tmA, tmB, p);
-    case 128: return launch_qgemm_cfg<128, 6, AMODE, ROWCOL>(dev, tmA, tmB, p);
-    default: return launch_qgemm_cfg<256, 4, AMODE, ROWCOL>(dev, tmA, tmB, p);
+    case 64:
+      return short_k ? launch_qgemm_cfg<64, 7, AMODE, ROWCOL, 4>(dev, tmA, tmB, p)
+                     : launch_qgemm_cfg<64, 8, AMODE, ROWCOL, 2>(dev, tmA, tmB, p);
+    case 128:
+      return short_k ? launch_qgemm_cfg<128, 5, AMODE, ROWCOL, 4>(dev, tmA, tmB, p)
+                     : launch_qgemm_cfg<128, 6, AMODE, ROWCOL, 2>(dev, tmA, tmB, p);
+    default:
+      return short_k ? launch_qgemm_cfg<256, 3, AMODE, ROWCOL, 4>(dev, tmA, tmB, p)
+                     : launch_qgemm_cfg<256, 4, AMODE, ROWCOL, 2>(dev, tmA, tmB, p);
   }
 }
 
@@ -448,45 +458,104 @@ extern "C" int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A,
   return launch_qgemm_bn<QG_A_TMA, true>(dev, tmA, tmB, p, bn);
 }
 
-extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o, int64_t kh,
-                                 int64_t kw, const int8_t* wq, int64_t ldw, int64_t stride_h, int64_t stride_w,
-                                 int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w, const mira_dequant* dq,
-                                 const mira_epilogue* epi) {
-  MIRA_GET_DEVICE(dev);
+// Shared argument checks and parameter setup of the implicit-GEMM convolutions.
+static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o, int64_t kh, int64_t kw,
+                      int64_t ldw, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h,
+                      int64_t dil_w, const mira_dequant* dq, const mira_epilogue* epi, QgParams& p, int64_t& oh,
+                      int64_t& ow) {
   MIRA_CHECK_ARG(n >= 0 && h > 0 && w > 0 && o > 0 && kh > 0 && kw > 0, "bad qconv2d shape");
   MIRA_CHECK_ARG(cp == 4 || (cp > 0 && cp % 16 == 0), "input channels must be padded to 4 or a multiple of 16");
   MIRA_CHECK_ARG(stride_h > 0 && stride_w > 0 && dil_h > 0 && dil_w > 0 && pad_h >= 0 && pad_w >= 0, "bad conv geometry");
+  MIRA_CHECK_ARG(kw <= 32, "kernel width above 32");
   MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "conv input must be 16-byte aligned");
-  const int64_t oh = (h + 2 * pad_h - dil_h * (kh - 1) - 1) / stride_h + 1;
-  const int64_t ow = (w + 2 * pad_w - dil_w * (kw - 1) - 1) / stride_w + 1;
+  oh = (h + 2 * pad_h - dil_h * (kh - 1) - 1) / stride_h + 1;
+  ow = (w + 2 * pad_w - dil_w * (kw - 1) - 1) / stride_w + 1;
   MIRA_CHECK_ARG(oh > 0 && ow > 0, "kernel larger than the padded input");
   const int64_t K = kh * kw * cp;
   MIRA_CHECK_ARG(K <= 133000, "K too large for exact int32 accumulation of int8 products");
   MIRA_CHECK_ARG(ldw >= round_up(K, 16) && ldw % 16 == 0, "weight row stride must be >= round_up(kh*kw*cp, 16)");
   const int64_t M = n * oh * ow;
   MIRA_CHECK_ARG(M < (int64_t(1) << 31) && n * h * w * cp < (int64_t(1) << 40), "conv too large");
-  if (M == 0) return MIRA_CUDA_OK;
-  QgParams p;
   std::memset(&p, 0, sizeof(p));
   const int rc = fill_epilogue(p, dq, epi);
   if (rc != MIRA_CUDA_OK) return rc;
   MIRA_CHECK_ARG(p.scale64 != nullptr, "convolutions use per-channel scales");
-  const int bn = pick_bn(o);
   p.M = int(M);
   p.N = int(o);
   p.K = int(K);
   p.num_kb = int((K + QG_BK - 1) / QG_BK);
-  p.m_tiles = int((M + QG_BM - 1) / QG_BM);
-  p.n_tiles = int((o + bn - 1) / bn);
   p.A = x;
   p.g = QgConv{int(n), int(h), int(w), int(cp), int(oh), int(ow), int(kh), int(kw), int(stride_h), int(stride_w),
                int(pad_h), int(pad_w), int(dil_h), int(dil_w)};
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o, int64_t kh,
+                                 int64_t kw, const int8_t* wq, int64_t ldw, int64_t stride_h, int64_t stride_w,
+                                 int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w, const mira_dequant* dq,
+                                 const mira_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  QgParams p;
+  int64_t oh, ow;
+  int rc = conv_setup(n, h, w, cp, x, o, kh, kw, ldw, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dq, epi, p, oh, ow);
+  if (rc != MIRA_CUDA_OK) return rc;
+  if (p.M == 0) return MIRA_CUDA_OK;
+  const int bn = pick_bn(o);
+  p.m_tiles = int((p.M + QG_BM - 1) / QG_BM);
+  p.n_tiles = int((o + bn - 1) / bn);
   CUtensorMap tmA, tmB;
   std::memset(&tmA, 0, sizeof(tmA));
-  int r = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, uint32_t(bn));
-  if (r != MIRA_CUDA_OK) return r;
+  rc = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, uint32_t(bn));
+  if (rc != MIRA_CUDA_OK) return rc;
   if (cp == 4) return launch_qgemm_bn<QG_A_GATHER4, false>(dev, tmA, tmB, p, bn);
   return launch_qgemm_bn<QG_A_GATHER16, false>(dev, tmA, tmB, p, bn);
+}
+
+extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o,
+                                         int64_t kh, int64_t kw, const int8_t* wq, int64_t ldw, int64_t stride_h,
+                                         int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
+                                         int64_t pool_size, int64_t pool_stride, int64_t pool_pad, float pool_pad_value,
+                                         const mira_dequant* dq, const mira_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  QgParams p;
+  int64_t oh, ow;
+  int rc = conv_setup(n, h, w, cp, x, o, kh, kw, ldw, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dq, epi, p, oh, ow);
+  if (rc != MIRA_CUDA_OK) return rc;
+  MIRA_CHECK_ARG(o <= 64, "fused pooling supports convolutions with at most 64 output channels");
+  MIRA_CHECK_ARG(pool_size > 0 && pool_stride > 0 && pool_pad >= 0 && pool_pad < pool_size, "bad pool geometry");
+  for (int s = 0; s < p.n_steps; ++s)
+    MIRA_CHECK_ARG(p.steps[s].operand == MIRA_OPND_NONE || p.steps[s].operand == MIRA_OPND_SCALAR ||
+                       p.steps[s].operand == MIRA_OPND_CHANNEL,
+                   "fused pooling supports scalar and per-channel epilogue operands only");
+  const int64_t ph = (oh + 2 * pool_pad - pool_size) / pool_stride + 1;
+  const int64_t pw = (ow + 2 * pool_pad - pool_size) / pool_stride + 1;
+  MIRA_CHECK_ARG(ph > 0 && pw > 0, "pool window larger than the conv output");
+  int T = 0;
+  for (int t = 1; t <= 16; ++t) {
+    const int64_t span = (t - 1) * pool_stride + pool_size;
+    if (span * span <= 96) T = t;   // QgCfg<...>::POOL_ROWS
+  }
+  MIRA_CHECK_ARG(T > 0, "pool window too large to fuse");
+  if (n == 0) return MIRA_CUDA_OK;
+  p.pool_p = int(pool_size);
+  p.pool_s = int(pool_stride);
+  p.pool_pad = int(pool_pad);
+  p.pool_t = T;
+  p.pool_span = int((T - 1) * pool_stride + pool_size);
+  p.ph_out = int(ph);
+  p.pw_out = int(pw);
+  p.tiles_y = int((ph + T - 1) / T);
+  p.tiles_x = int((pw + T - 1) / T);
+  p.pool_pad_value = pool_pad_value;
+  p.M = 0x7fffffff;
+  p.m_tiles = int(n * p.tiles_y * p.tiles_x);
+  p.n_tiles = 1;
+  CUtensorMap tmA, tmB;
+  std::memset(&tmA, 0, sizeof(tmA));
+  rc = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, 64u);
+  if (rc != MIRA_CUDA_OK) return rc;
+  if (cp == 4) return launch_qgemm_cfg<64, 7, QG_A_GATHER4, false, 4, true>(dev, tmA, tmB, p);
+  return launch_qgemm_cfg<64, 7, QG_A_GATHER16, false, 4, true>(dev, tmA, tmB, p);
 }
 
 extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, int64_t n, int64_t h, int64_t w,

@@ -48,6 +48,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread (up to `hint_ns`) until the phase completes, instead of
+// returning at once: waiting warps then stop taking issue slots from the working ones.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits until the phase with the given parity has completed.  Gives up after `timeout_ns` (or
 // as soon as another thread of the CTA raised *abort), sets *abort and returns false.  Every
 // wait in the kernels goes through here, so no kernel can spin forever.
@@ -56,9 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity, 1000000u)) return true;
     if (*abort) return false;
     if (globaltimer_ns() - t0 > timeout_ns) {
       *abort = 1;
@@ -96,6 +108,12 @@ __device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* src, 
 __device__ __forceinline__ void cp_async_4(uint32_t smem_dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_dst), "l"(src), "r"(src_bytes)
                : "memory");
+}
+
+// Arrives on `bar` once all cp.async copies this thread issued so far have landed; the arrival is
+// one of the barrier's expected arrivals (no pending-count increment).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }

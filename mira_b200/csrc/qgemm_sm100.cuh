@@ -5,11 +5,19 @@
 //               ring of shared-memory stages (128-byte swizzle, no multicast)
 //   warp 1      allocates TMEM (2 x BN columns: two accumulators) and issues the MMAs from one
 //               thread; tcgen05.commit frees a stage / publishes an accumulator
-//   warps 4-7   epilogue: tcgen05.ld of their 32 TMEM lanes (one output row per thread), exact
-//               dequant, the fused epilogue steps, f32 and/or requantized int8 stores
-//   warps 8-11  (convolutions only) im2col gather of A from NHWC int8 with cp.async, one output
-//               pixel (tile row) per thread, zero fill for padding
-// The two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1.
+//   warps 2 .. 2+4G-1
+//               epilogue: G groups of four warps (any four consecutive warps cover the four TMEM
+//               lane quarters, warp w reads lanes 32 * (w % 4) ...).  A group owns every G-th
+//               16-column chunk of a tile; one output row per thread: tcgen05.ld, exact dequant,
+//               the fused epilogue steps, requantized int8 stores, and f32 stores staged through
+//               shared memory so each store instruction writes whole 64-byte row segments
+//   next 4 warps (convolutions only) im2col gather of A from NHWC int8 with cp.async, one output
+//               pixel (tile row) per thread, zero fill for padding; each thread's copies arrive on
+//               the stage barrier when they land (cp.async.mbarrier.arrive.noinc), so the gather
+//               runs up to STAGES K-blocks ahead of the MMAs
+// The two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1.  The
+// epilogue is latency-bound at few warps per scheduler, so G = 4 (16 epilogue warps) is used
+// for short reductions and G = 2 with deeper operand pipelines for long ones.
 #pragma once
 #include <cuda.h>
 
@@ -50,176 +58,251 @@ struct QgParams {
   int64_t ld_i8;
   float q_scale, q_rcp, q_lim;   // requant divisor, RN32(1/divisor), 256 * divisor
   int* err;
+  // fused max pooling (POOL kernels only): window pool_p, stride pool_s, padding pool_pad holding
+  // pool_pad_value; a tile is pool_t x pool_t pooled pixels whose conv inputs form a
+  // pool_span x pool_span block (pool_span = (pool_t - 1) * pool_s + pool_p, pool_span^2 <= 128)
+  int pool_p, pool_s, pool_pad, pool_t, pool_span, ph_out, pw_out, tiles_y, tiles_x;
+  float pool_pad_value;
 };
 
-template <int BN, int STAGES, int AMODE>
+// Tile row r of a POOL tile (tile index t_m over images x tiles_y x tiles_x): the conv output
+// pixel it computes, and whether that pixel exists.
+__device__ __forceinline__ void pool_row_pixel(const QgParams& p, int t_m, int r, int& img, int& cy, int& cx,
+                                               int& ty, int& tx, bool& valid) {
+  const int per_img = p.tiles_y * p.tiles_x;
+  img = t_m / per_img;
+  const int rem = t_m - img * per_img;
+  ty = rem / p.tiles_x;
+  tx = rem - ty * p.tiles_x;
+  const int ry = r / p.pool_span, rx = r - ry * p.pool_span;
+  cy = ty * p.pool_t * p.pool_s - p.pool_pad + ry;
+  cx = tx * p.pool_t * p.pool_s - p.pool_pad + rx;
+  valid = r < p.pool_span * p.pool_span && cy >= 0 && cy < p.g.oh && cx >= 0 && cx < p.g.ow;
+}
+
+template <int BN, int STAGES, int AMODE, int G, bool POOL = false>
 struct QgCfg {
   static constexpr int A_BYTES = QG_BM * QG_BK;
   static constexpr int B_BYTES = BN * QG_BK;
-  static constexpr int THREADS = AMODE == QG_A_TMA ? 256 : 384;
+  static constexpr int CW = 16;                       // epilogue chunk width (columns)
+  static constexpr int EPI_WARP0 = 2;
+  static constexpr int EPI_WARPS = 4 * G;
+  static constexpr int GATHER_WARP0 = EPI_WARP0 + EPI_WARPS;
+  static constexpr int THREADS = 32 * (GATHER_WARP0 + (AMODE == QG_A_TMA ? 0 : 4));
+  static constexpr int EPI_THREADS = 32 * EPI_WARPS;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr int GATHER_LAG = STAGES > 3 ? 3 : STAGES - 1;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * (A_BYTES + B_BYTES) + 256;
+  // per epilogue warp: a 32-row x 16-column f32 staging block (row pitch 20 floats)
+  static constexpr int STAGE_PITCH = 20;
+  // POOL kernels instead keep two 128-row x BN conv-output tiles (row pitch BN + 4 floats)
+  static constexpr int POOL_PITCH = BN + 4;
+  static constexpr int POOL_ROWS = 96;
+  static constexpr int STAGING_BYTES = POOL ? 2 * POOL_ROWS * POOL_PITCH * 4 : EPI_WARPS * 32 * STAGE_PITCH * 4;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * (A_BYTES + B_BYTES) + STAGING_BYTES + 256;
+  static_assert(!POOL || (AMODE != 0 && BN == 64), "fused pooling: convolutions with at most 64 channels");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 // Bounded wait that ignores the abort flag: used only to let in-flight copies land before exit.
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_suspend(bar, parity, 1000000u)) {
     if (globaltimer_ns() - t0 > QG_TIMEOUT_NS) return;
   }
 }
 
-// ---------------------------------------------------------------- epilogue (one 32-column chunk)
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
 
-template <bool ROWCOL>
-__device__ __forceinline__ void qg_dequant_chunk(const QgParams& p, const uint32_t (&r)[32], int m, int nb,
-                                                 float (&v)[32]) {
-  if (!ROWCOL) {
-    const float4* hi4 = reinterpret_cast<const float4*>(p.scale_hi + nb);
-    const float4* lo4 = reinterpret_cast<const float4*>(p.scale_lo + nb);
+// ---------------------------------------------------------------- epilogue (one 16-column chunk)
+
+#define QG_APPLY_BINARY(EXPR)                          \
+  do {                                                 \
+    if (st.swapped) {                                  \
+      _Pragma("unroll") for (int j = 0; j < 16; ++j) { \
+        const float a = o[j], b = v[j];                \
+        v[j] = (EXPR);                                 \
+      }                                                \
+    } else {                                           \
+      _Pragma("unroll") for (int j = 0; j < 16; ++j) { \
+        const float a = v[j], b = o[j];                \
+        v[j] = (EXPR);                                 \
+      }                                                \
+    }                                                  \
+  } while (0)
+
+__device__ __forceinline__ void ld16(const float* src, float (&o)[16]) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 h = __ldg(hi4 + q), l = __ldg(lo4 + q);
-      const float hs[4] = {h.x, h.y, h.z, h.w}, ls[4] = {l.x, l.y, l.z, l.w};
+  for (int q = 0; q < 4; ++q) {
+    const float4 t = __ldg(s4 + q);
+    o[4 * q] = t.x; o[4 * q + 1] = t.y; o[4 * q + 2] = t.z; o[4 * q + 3] = t.w;
+  }
+}
+
+// Loads a binary step's operand for this thread's row and chunk columns [nb, nb + 16).
+__device__ __forceinline__ void qg_operand(const QgParams& p, const mira_epi_step& st, int m, bool row_ok, int nb,
+                                           bool full_chunk, float (&o)[16]) {
+  if (st.operand == MIRA_OPND_SCALAR) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = 4 * q + e;
-        float y;
-        if (!dequant_fast(static_cast<int32_t>(r[j]), hs[e], ls[e], y))
-          y = __double2float_rn(static_cast<double>(static_cast<int32_t>(r[j])) * p.scale64[nb + j]);
-        v[j] = y;
-      }
-    }
-  } else {
-    const float rs = p.row_scale[m];
+    for (int j = 0; j < 16; ++j) o[j] = st.scalar;
+  } else if (st.operand == MIRA_OPND_CHANNEL) {
+    ld16(st.ptr + nb, o);   // channel arrays are padded to a multiple of 256 entries
+  } else if (st.operand == MIRA_OPND_ROW) {
+    const float t = row_ok ? st.ptr[m] : 0.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float cs = (nb + j < p.N) ? __ldg(p.col_scale + nb + j) : 0.0f;
-      float hi, lo, y;
-      split_rowcol(rs, cs, hi, lo);
-      if (!dequant_fast(static_cast<int32_t>(r[j]), hi, lo, y))
-        y = __double2float_rn(static_cast<double>(static_cast<int32_t>(r[j])) *
-                              (static_cast<double>(rs) * static_cast<double>(cs)));
-      v[j] = y;
+    for (int j = 0; j < 16; ++j) o[j] = t;
+  } else {  // FULL
+    const float* src = st.ptr + static_cast<int64_t>(m) * st.ld + nb;
+    if (!row_ok) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = 0.0f;
+    } else if (full_chunk && (st.ld % 4) == 0) {
+      ld16(src, o);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = (nb + j < p.N) ? src[j] : 0.0f;
     }
   }
 }
 
-#define QG_APPLY_BINARY(EXPR)                         \
-  do {                                                \
-    if (st.swapped) {                                 \
-      _Pragma("unroll") for (int j = 0; j < 32; ++j) { \
-        const float a = o[j], b = v[j];               \
-        v[j] = (EXPR);                                \
-      }                                               \
-    } else {                                          \
-      _Pragma("unroll") for (int j = 0; j < 32; ++j) { \
-        const float a = v[j], b = o[j];               \
-        v[j] = (EXPR);                                \
-      }                                               \
-    }                                                 \
-  } while (0)
+__device__ __forceinline__ void qg_apply_step(const mira_epi_step& st, const float (&o)[16], float (&v)[16]) {
+  switch (st.op) {
+    case MIRA_EPI_ADD: QG_APPLY_BINARY(__fadd_rn(a, b)); break;
+    case MIRA_EPI_SUB: QG_APPLY_BINARY(__fsub_rn(a, b)); break;
+    case MIRA_EPI_MUL: QG_APPLY_BINARY(__fmul_rn(a, b)); break;
+    case MIRA_EPI_DIV: QG_APPLY_BINARY(__fdiv_rn(a, b)); break;
+    case MIRA_EPI_MAXIMUM: QG_APPLY_BINARY(np_maximum(a, b)); break;
+    case MIRA_EPI_MINIMUM: QG_APPLY_BINARY(np_minimum(a, b)); break;
+    default: break;
+  }
+}
 
-__device__ __forceinline__ void qg_epilogue_steps(const QgParams& p, int m, int nb, bool full_chunk,
-                                                  float (&v)[32]) {
+// The whole epilogue of one 16-column chunk of this warp's 32 rows.  Everything that does not
+// depend on the accumulator (dequant scales, the first binary operand) is loaded before the TMEM
+// read so the two latencies overlap.
+template <bool ROWCOL, int PITCH, bool POOL = false, int POOL_PITCH = 0>
+__device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t taddr, int m, bool row_ok, int m_warp0,
+                                                  int nb, float* stage, int lane, float* ptile_row = nullptr,
+                                                  int nb_local = 0) {
+  const bool full_chunk = nb + 16 <= p.N;
+  float hs[16], ls[16];
+  if (!ROWCOL) {
+    ld16(p.scale_hi + nb, hs);
+    ld16(p.scale_lo + nb, ls);
+  } else {
+    const float rs = row_ok ? p.row_scale[m] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float cs = (nb + j < p.N) ? __ldg(p.col_scale + nb + j) : 0.0f;
+      split_rowcol(rs, cs, hs[j], ls[j]);
+    }
+  }
+  int first = 0;
+  while (first < p.n_steps && p.steps[first].operand == MIRA_OPND_NONE) ++first;
+  float o[16];
+  if (first < p.n_steps) qg_operand(p, p.steps[first], m, row_ok, nb, full_chunk, o);
+
+  uint32_t r[16];
+  tmem_ld_32x32b_x16(taddr, r);
+  tmem_ld_wait();
+
+  float v[16];
+  uint32_t slow = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const bool ok = dequant_fast(static_cast<int32_t>(r[j]), hs[j], ls[j], v[j]);
+    slow |= ok ? 0u : (1u << j);
+  }
+  if (__any_sync(0xffffffffu, slow != 0)) {   // rare: about 2 elements in 10^5
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (slow & (1u << j)) {
+        const double s64 = ROWCOL ? static_cast<double>(row_ok ? p.row_scale[m] : 0.0f) *
+                                        static_cast<double>((nb + j < p.N) ? p.col_scale[nb + j] : 0.0f)
+                                  : p.scale64[nb + j];
+        v[j] = __double2float_rn(static_cast<double>(static_cast<int32_t>(r[j])) * s64);
+      }
+    }
+  }
+
   for (int s = 0; s < p.n_steps; ++s) {
     const mira_epi_step& st = p.steps[s];
     if (st.operand == MIRA_OPND_NONE) {
-      switch (st.op) {
-        case MIRA_EPI_RELU:
+      if (st.op == MIRA_EPI_RELU) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = np_maximum(v[j], 0.0f);
-          break;
-        default:
+        for (int j = 0; j < 16; ++j) v[j] = np_maximum(v[j], 0.0f);
+      } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = apply_unary(st.op, v[j]);
-          break;
+        for (int j = 0; j < 16; ++j) v[j] = apply_unary(st.op, v[j]);
       }
       continue;
     }
-    float o[32];
-    if (st.operand == MIRA_OPND_SCALAR) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[j] = st.scalar;
-    } else if (st.operand == MIRA_OPND_CHANNEL) {
-      const float4* c4 = reinterpret_cast<const float4*>(st.ptr + nb);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 t = __ldg(c4 + q);
-        o[4 * q] = t.x; o[4 * q + 1] = t.y; o[4 * q + 2] = t.z; o[4 * q + 3] = t.w;
-      }
-    } else if (st.operand == MIRA_OPND_ROW) {
-      const float t = st.ptr[m];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[j] = t;
-    } else {  // FULL
-      const float* src = st.ptr + static_cast<int64_t>(m) * st.ld + nb;
-      if (full_chunk && (st.ld % 4) == 0) {
-        const float4* s4 = reinterpret_cast<const float4*>(src);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 t = __ldg(s4 + q);
-          o[4 * q] = t.x; o[4 * q + 1] = t.y; o[4 * q + 2] = t.z; o[4 * q + 3] = t.w;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] = (nb + j < p.N) ? src[j] : 0.0f;
-      }
-    }
-    switch (st.op) {
-      case MIRA_EPI_ADD: QG_APPLY_BINARY(__fadd_rn(a, b)); break;
-      case MIRA_EPI_SUB: QG_APPLY_BINARY(__fsub_rn(a, b)); break;
-      case MIRA_EPI_MUL: QG_APPLY_BINARY(__fmul_rn(a, b)); break;
-      case MIRA_EPI_DIV: QG_APPLY_BINARY(__fdiv_rn(a, b)); break;
-      case MIRA_EPI_MAXIMUM: QG_APPLY_BINARY(np_maximum(a, b)); break;
-      case MIRA_EPI_MINIMUM: QG_APPLY_BINARY(np_minimum(a, b)); break;
-      default: break;
-    }
+    if (s != first) qg_operand(p, st, m, row_ok, nb, full_chunk, o);
+    qg_apply_step(st, o, v);
   }
-}
 
-__device__ __forceinline__ void qg_store_chunk(const QgParams& p, int m, int nb, bool full_chunk,
-                                               const float (&v)[32]) {
+  if (POOL) {
+    // conv outputs stay in shared memory; the pooling phase writes the results
+    if (ptile_row != nullptr) {
+      float4* d4 = reinterpret_cast<float4*>(ptile_row + nb_local);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    return;
+  }
   if (p.out_f32 != nullptr) {
-    float* dst = p.out_f32 + static_cast<int64_t>(m) * p.ld_f32 + nb;
     if (full_chunk && (p.ld_f32 % 4) == 0) {
-      float4* d4 = reinterpret_cast<float4*>(dst);
+      float4* srow = reinterpret_cast<float4*>(stage + lane * PITCH);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    } else {
+      for (int q = 0; q < 4; ++q) srow[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
+      for (int i = 0; i < 4; ++i) {
+        const int rr = i * 8 + (lane >> 2), qq = lane & 3;
+        const float4 t = reinterpret_cast<const float4*>(stage + rr * PITCH)[qq];
+        const int mm = m_warp0 + rr;
+        if (mm < p.M) reinterpret_cast<float4*>(p.out_f32 + static_cast<int64_t>(mm) * p.ld_f32 + nb)[qq] = t;
+      }
+      __syncwarp();
+    } else if (row_ok) {
+      float* dst = p.out_f32 + static_cast<int64_t>(m) * p.ld_f32 + nb;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
         if (nb + j < p.N) dst[j] = v[j];
     }
   }
-  if (p.out_i8 != nullptr) {
-    uint32_t w[8];
+  if (p.out_i8 != nullptr && row_ok && nb < p.ld_i8) {
+    uint32_t b[16];
+    if (full_chunk) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      uint32_t b[4];
+      for (int j = 0; j < 16; ++j) b[j] = round_clip_i8(div_by_scale(v[j], p.q_scale, p.q_rcp, p.q_lim));
+    } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = 4 * q + e;
-        b[e] = (nb + j < p.N) ? round_clip_i8(div_by_scale(v[j], p.q_scale, p.q_rcp, p.q_lim)) : 0u;
-      }
-      w[q] = pack4_i8(b[0], b[1], b[2], b[3]);
+      for (int j = 0; j < 16; ++j)
+        b[j] = (nb + j < p.N) ? round_clip_i8(div_by_scale(v[j], p.q_scale, p.q_rcp, p.q_lim)) : 0u;
     }
-    int8_t* dst = p.out_i8 + static_cast<int64_t>(m) * p.ld_i8 + nb;
-    const int64_t room = p.ld_i8 - nb;  // multiple of 16
-    if (room >= 16) reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    if (room >= 32) reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    *reinterpret_cast<uint4*>(p.out_i8 + static_cast<int64_t>(m) * p.ld_i8 + nb) =
+        make_uint4(pack4_i8(b[0], b[1], b[2], b[3]), pack4_i8(b[4], b[5], b[6], b[7]),
+                   pack4_i8(b[8], b[9], b[10], b[11]), pack4_i8(b[12], b[13], b[14], b[15]));
   }
 }
 
 // ---------------------------------------------------------------- the kernel
 
-template <int BN, int STAGES, int AMODE, bool ROWCOL>
-__global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE>::THREADS, 1)
+template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false>
+__global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
     qgemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ QgParams p) {
-  using Cfg = QgCfg<BN, STAGES, AMODE>;
+  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL>;
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
   constexpr uint32_t IDESC = idesc_i8(QG_BM, BN);
@@ -228,12 +311,14 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE>::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  float* staging = reinterpret_cast<float*>(sB + STAGES * B_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(staging) + Cfg::STAGING_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* pool_bar = drain + 1;   // [2]: all epilogue threads wrote the tile buffer
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pool_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -246,9 +331,11 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE>::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], Cfg::EPI_THREADS);
     }
     mbar_init(drain, 1);
+    mbar_init(&pool_bar[0], Cfg::EPI_THREADS);
+    mbar_init(&pool_bar[1], Cfg::EPI_THREADS);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmB);
@@ -306,6 +393,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE>::THREADS, 1)
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
+          if (AMODE != QG_A_TMA) fence_proxy_async_smem();  // A was written by cp.async (generic proxy)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
@@ -324,107 +412,173 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE>::THREADS, 1)
       mma_commit(drain);
       mbar_wait_drain(drain, 0);
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= Cfg::EPI_WARP0 && warp < Cfg::GATHER_WARP0) {
     // ------------------------------------------------ epilogue
-    const int ew = warp - 4;
+    const int ew = warp - Cfg::EPI_WARP0;
+    const int quarter = warp & 3;
+    const int group = ew >> 2;
+    float* stage = staging + ew * 32 * Cfg::STAGE_PITCH;
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       if (!mbar_wait(&tfull[acc], (it >> 1) & 1, abort_flag, QG_TIMEOUT_NS)) break;
       tc_fence_after();
-      const int m0 = (t / p.n_tiles) * QG_BM;
+      const int t_m = t / p.n_tiles;
       const int n0 = (t % p.n_tiles) * BN;
-      const int m = m0 + ew * 32 + lane;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      if (!POOL) {
+        const int m_warp0 = t_m * QG_BM + quarter * 32;
+        const int m = m_warp0 + lane;
+        const bool row_ok = m < p.M;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int nb = n0 + c * 32;
-        if (nb >= p.N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN + c * 32, r);
-        tmem_ld_wait();
-        if (m < p.M) {
-          const bool full_chunk = nb + 32 <= p.N;
-          float v[32];
-          qg_dequant_chunk<ROWCOL>(p, r, m, nb, v);
-          qg_epilogue_steps(p, m, nb, full_chunk, v);
-          qg_store_chunk(p, m, nb, full_chunk, v);
+        for (int c = group; c < BN / Cfg::CW; c += G) {
+          const int nb = n0 + c * Cfg::CW;
+          if (nb >= p.N) break;  // warp-uniform
+          qg_epilogue_chunk<ROWCOL, Cfg::STAGE_PITCH>(p, tbase + c * Cfg::CW, m, row_ok, m_warp0, nb, stage, lane);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      } else {
+        // conv outputs of the tile -> shared tile buffer (acc parity), then pool from it
+        const int r = quarter * 32 + lane;
+        int img, cy, cx, ty, tx;
+        bool valid;
+        pool_row_pixel(p, t_m, r, img, cy, cx, ty, tx, valid);
+        float* ptile = staging + acc * Cfg::POOL_ROWS * Cfg::POOL_PITCH;
+        float* prow = r < p.pool_span * p.pool_span ? ptile + r * Cfg::POOL_PITCH : nullptr;
+        const bool warp_used = quarter * 32 < p.pool_span * p.pool_span;   // warp-uniform
+#pragma unroll 1
+        for (int c = group; warp_used && c < BN / Cfg::CW; c += G) {
+          const int nb = n0 + c * Cfg::CW;
+          if (nb >= p.N) break;
+          qg_epilogue_chunk<false, Cfg::STAGE_PITCH, true>(p, tbase + c * Cfg::CW, 0, valid, 0, nb, stage, lane,
+                                                             prow, c * Cfg::CW);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        mbar_arrive(&pool_bar[acc]);
+        if (!mbar_wait(&pool_bar[acc], (it >> 1) & 1, abort_flag, QG_TIMEOUT_NS)) break;
+        // pooling: max over each window of the stored conv outputs; conv pixels outside the
+        // conv output (the pool's padding) take pool_pad_value
+        const int et = threadIdx.x - 32 * Cfg::EPI_WARP0;
+        const int T = p.pool_t, S = p.pool_s, P = p.pool_p, span = p.pool_span;
+        for (int o = et; o < T * T * BN; o += Cfg::EPI_THREADS) {
+          const int ch = o % BN, pp = o / BN;
+          const int py = pp / T, px = pp - (pp / T) * T;
+          const int gy = ty * T + py, gx = tx * T + px;
+          if (gy >= p.ph_out || gx >= p.pw_out) continue;
+          const int64_t orow = (static_cast<int64_t>(img) * p.ph_out + gy) * p.pw_out + gx;
+          const int col = n0 + ch;
+          if (col >= p.N) {
+            if (p.out_i8 != nullptr && col < p.ld_i8) p.out_i8[orow * p.ld_i8 + col] = 0;
+            continue;
+          }
+          float mx = 0.0f;
+          for (int dy = 0; dy < P; ++dy) {
+            const int cyy = ty * T * S - p.pool_pad + S * py + dy;
+            for (int dx = 0; dx < P; ++dx) {
+              const int cxx = tx * T * S - p.pool_pad + S * px + dx;
+              const bool inside = cyy >= 0 && cyy < p.g.oh && cxx >= 0 && cxx < p.g.ow;
+              const float v = inside ? ptile[((S * py + dy) * span + S * px + dx) * Cfg::POOL_PITCH + ch]
+                                     : p.pool_pad_value;
+              mx = (dy == 0 && dx == 0) ? v : np_maximum(mx, v);
+            }
+          }
+          if (p.out_f32 != nullptr) p.out_f32[orow * p.ld_f32 + col] = mx;
+          if (p.out_i8 != nullptr)
+            p.out_i8[orow * p.ld_i8 + col] =
+                static_cast<int8_t>(round_clip_i8(div_by_scale(mx, p.q_scale, p.q_rcp, p.q_lim)) & 0xff);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
     }
-  } else if (AMODE != QG_A_TMA && warp >= 8) {
+  } else if (AMODE != QG_A_TMA && warp >= Cfg::GATHER_WARP0) {
     // ------------------------------------------------ im2col gather of A (convolutions)
-    constexpr int LAG = Cfg::GATHER_LAG;
-    const int row = threadIdx.x - 256;
+    const int row = threadIdx.x - 32 * Cfg::GATHER_WARP0;
     const QgConv& g = p.g;
     int stage = 0;
     uint32_t phase = 0;
-    int ring[LAG];
-    int pending = 0, head = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      const int m = (t / p.n_tiles) * QG_BM + row;
-      const bool row_ok = m < p.M;
       int img = 0, oy = 0, ox = 0;
-      if (row_ok) {
-        img = m / (g.oh * g.ow);
-        const int rem = m - img * g.oh * g.ow;
-        oy = rem / g.ow;
-        ox = rem - oy * g.ow;
+      bool row_ok;
+      if (POOL) {
+        int ty, tx;
+        pool_row_pixel(p, t / p.n_tiles, row, img, oy, ox, ty, tx, row_ok);
+        if (!row_ok) img = oy = ox = 0;
+      } else {
+        const int m = (t / p.n_tiles) * QG_BM + row;
+        row_ok = m < p.M;
+        if (row_ok) {
+          img = m / (g.oh * g.ow);
+          const int rem = m - img * g.oh * g.ow;
+          oy = rem / g.ow;
+          ox = rem - oy * g.ow;
+        }
       }
       const int iy0 = oy * g.sh - g.ph;
       const int ix0 = ox * g.sw - g.pw;
       const int8_t* base = p.A + static_cast<int64_t>(img) * g.h * g.w * g.cp;
-      // reduction position k = (ti * kw + tj) * cp + ci, advanced incrementally
+      // which kernel columns land inside the image for this output pixel (kw <= 32)
+      uint32_t colmask = 0;
+      for (int j = 0; j < g.kw; ++j)
+        colmask |= (static_cast<unsigned>(ix0 + j * g.dw) < static_cast<unsigned>(g.w)) ? (1u << j) : 0u;
+      // current tap (ti, tj), channel offset ci within it, and the tap's source pixel
       int ti = 0, tj = 0, ci = 0;
+      int iy = iy0;
+      bool row_in = row_ok && static_cast<unsigned>(iy) < static_cast<unsigned>(g.h);
+      const int64_t tap_step = static_cast<int64_t>(g.dw) * g.cp;
+      const int8_t* tap_ptr = base + (static_cast<int64_t>(iy) * g.w + ix0) * g.cp;
+      const int swz = row & 7;
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
         const uint32_t dst_row = smem_u32(sA + stage * A_BYTES) + row * QG_BK;
+        const int kmax = p.K - kb * QG_BK;   // reduction bytes left from this K-block on
         if (AMODE == QG_A_GATHER16) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int k = kb * QG_BK + c * 16;
-            const int iy = iy0 + ti * g.dh, ix = ix0 + tj * g.dw;
-            const bool valid = row_ok && k < p.K && iy >= 0 && iy < g.h && ix >= 0 && ix < g.w;
-            const int8_t* src = valid ? base + (static_cast<int64_t>(iy) * g.w + ix) * g.cp + ci : p.A;
-            cp_async_16(dst_row + ((c ^ (row & 7)) << 4), src, valid ? 16u : 0u);
-            ci += 16;
+          int c = 0;
+          while (c < 8) {   // one tap (or what is left of it) per iteration
+            const bool tap_ok = row_in && ((colmask >> tj) & 1u);
+            int n_here = (g.cp - ci) >> 4;
+            if (n_here > 8 - c) n_here = 8 - c;
+            const int8_t* src = tap_ptr + ci;
+            for (int e = 0; e < n_here; ++e, ++c, src += 16) {
+              const bool v = tap_ok && (c * 16 < kmax);
+              cp_async_16(dst_row + ((c ^ swz) << 4), v ? src : p.A, v ? 16u : 0u);
+            }
+            ci += n_here * 16;
             if (ci == g.cp) {
               ci = 0;
-              if (++tj == g.kw) { tj = 0; ++ti; }
+              tap_ptr += tap_step;
+              if (++tj == g.kw) {
+                tj = 0;
+                ++ti;
+                iy += g.dh;
+                row_in = row_ok && static_cast<unsigned>(iy) < static_cast<unsigned>(g.h);
+                tap_ptr = base + (static_cast<int64_t>(iy) * g.w + ix0) * g.cp;
+              }
             }
           }
         } else {
 #pragma unroll 4
           for (int c = 0; c < 32; ++c) {
-            const int k = kb * QG_BK + c * 4;
-            const int iy = iy0 + ti * g.dh, ix = ix0 + tj * g.dw;
-            const bool valid = row_ok && k < p.K && iy >= 0 && iy < g.h && ix >= 0 && ix < g.w;
-            const int8_t* src = valid ? base + (static_cast<int64_t>(iy) * g.w + ix) * 4 : p.A;
-            cp_async_4(dst_row + (((c >> 2) ^ (row & 7)) << 4) + ((c & 3) << 2), src, valid ? 4u : 0u);
-            if (++tj == g.kw) { tj = 0; ++ti; }
+            const bool v = row_in && ((colmask >> tj) & 1u) && (c * 4 < kmax);
+            cp_async_4(dst_row + (((c >> 2) ^ swz) << 4) + ((c & 3) << 2), v ? tap_ptr : p.A, v ? 4u : 0u);
+            tap_ptr += tap_step;
+            if (++tj == g.kw) {
+              tj = 0;
+              ++ti;
+              iy += g.dh;
+              row_in = row_ok && static_cast<unsigned>(iy) < static_cast<unsigned>(g.h);
+              tap_ptr = base + (static_cast<int64_t>(iy) * g.w + ix0) * g.cp;
+            }
           }
         }
-        cp_async_commit();
-        ring[(head + pending) % LAG] = stage;
-        if (++pending == LAG) {
-          cp_async_wait<LAG - 1>();
-          fence_proxy_async_smem();
-          mbar_arrive(&full[ring[head]]);
-          head = (head + 1) % LAG;
-          --pending;
-        }
+        // the stage's barrier counts this thread's arrival when its copies have landed
+        cp_async_arrive_noinc(&full[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
+    // no copy may still be landing when the CTA exits
     cp_async_wait<0>();
-    fence_proxy_async_smem();
-    while (pending > 0) {
-      mbar_arrive(&full[ring[head]]);
-      head = (head + 1) % LAG;
-      --pending;
-    }
   }
 
   tc_fence_before();

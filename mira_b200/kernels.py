@@ -156,6 +156,15 @@ def qconv2d(n: int, h: int, w: int, cp: int, x, o: int, kh: int, kw: int, wq, ld
               padding[0], padding[1], dilation[0], dilation[1], C.byref(dq), C.byref(e))
 
 
+def qconv2d_maxpool(n: int, h: int, w: int, cp: int, x, o: int, kh: int, kw: int, wq, ldw: int, stride, padding,
+                    dilation, pool_size: int, pool_stride: int, pool_pad: int, pool_pad_value: float,
+                    dq: _lib.Dequant, epi: Epi) -> None:
+    e = epi.struct()
+    _lib.call("mira_cuda_qconv2d_maxpool", n, h, w, cp, ptr(x), o, kh, kw, ptr(wq), ldw, stride[0], stride[1],
+              padding[0], padding[1], dilation[0], dilation[1], pool_size, pool_stride, pool_pad,
+              float(np.float32(pool_pad_value)), C.byref(dq), C.byref(e))
+
+
 def maxpool2d(n, h, w, c, ldc_in, size, stride, pad, pad_value, x_f32=None, x_i8=None, out_f32=None,
               ldc_out_f32=0, out_i8=None, ldc_out_i8=0, out_scale=1.0) -> None:
     _lib.call("mira_cuda_maxpool2d_nhwc", ptr(x_f32), ptr(x_i8), n, h, w, c, ldc_in, size, stride, pad,

@@ -102,13 +102,19 @@ class CudaDevice:
         elif k == "nhwc_to_nchw":
             fn = L.mira_cuda_nhwc_to_nchw_f32
             args = (ptr(a["x"]), a["n"], a["h"], a["w"], a["c"], a["ldc"], ptr(a["y"]))
-        elif k in ("qgemm", "qconv2d"):
+        elif k in ("qgemm", "qconv2d", "qconv2d_pool"):
             dq = K.dequant_channel(*a["dq"]) if len(a["dq"]) == 3 else K.dequant_rowcol(*a["dq"])
             e = a["epi"].struct()
             keep += [dq, e]
             if k == "qgemm":
                 fn = L.mira_cuda_qgemm
                 args = (a["M"], a["N"], a["K"], ptr(a["A"]), a["lda"], ptr(a["B"]), a["ldb"], C.byref(dq), C.byref(e))
+            elif k == "qconv2d_pool":
+                fn = L.mira_cuda_qconv2d_maxpool
+                (sh, sw), (ph, pw), (dh, dw) = a["stride"], a["padding"], a["dilation"]
+                args = (a["n"], a["h"], a["w"], a["cp"], ptr(a["x"]), a["o"], a["kh"], a["kw"], ptr(a["wq"]), a["ldw"],
+                        sh, sw, ph, pw, dh, dw, a["pool_size"], a["pool_stride"], a["pool_pad"],
+                        float(np.float32(a["pool_pad_value"])), C.byref(dq), C.byref(e))
             else:
                 fn = L.mira_cuda_qconv2d
                 (sh, sw), (ph, pw), (dh, dw) = a["stride"], a["padding"], a["dilation"]
@@ -203,11 +209,13 @@ def _pad_hw(op) -> Optional[tuple[int, float]]:
 
 
 class Plan:
-    """Device buffers and launches for one segment graph."""
+    """Device buffers and launches for one segment graph.  fuse_pool: run a qconv2d whose only
+    consumer is a max pool inside the pooling kernel (mira_cuda_qconv2d_maxpool)."""
 
-    def __init__(self, g, device):
+    def __init__(self, g, device, fuse_pool: bool = False):
         self.g = g
         self.dev = device
+        self.fuse_pool = fuse_pool
         self.vals: dict = {}
         self.launches: list[Launch] = []
         self.inputs: list = []       # (value, device buffer in reference layout, nbytes)
@@ -248,17 +256,28 @@ class Plan:
     def _requirements(self):
         g = self.g
         users = g.users()
-        self.pad_into_pool = {}      # maxpool op -> (source value, pad, value)
+        self.pad_into_pool = {}      # maxpool op -> (source value, pad, pad value)
+        self.conv_into_pool = {}     # maxpool op -> qconv2d op computed inside the pooling kernel
         for op in g.ops:
-            if op.kind == "pad" and _pad_hw(op) is not None:
-                us = users.get(op.result, [])
-                if len(us) == 1 and us[0].kind == "maxpool2d" and op.result not in g.outputs:
-                    p, val = _pad_hw(op)
-                    self.pad_into_pool[us[0]] = (op.inputs[0], p, val)
-                    self.skipped.add(op)
+            if op.kind != "maxpool2d":
+                continue
+            src = op.inputs[0]
+            pad_op = src.producer
+            if (pad_op is not None and pad_op.kind == "pad" and _pad_hw(pad_op) is not None
+                    and users.get(src, []) == [op] and src not in g.outputs):
+                p, val = _pad_hw(pad_op)
+                self.pad_into_pool[op] = (pad_op.inputs[0], p, val)
+                self.skipped.add(pad_op)
+                src = pad_op.inputs[0]
+            conv = src.producer
+            if (self.fuse_pool and conv is not None and conv.kind == "qconv2d" and len(users.get(src, [])) == 1
+                    and src not in g.outputs and self._conv_pool_fusable(conv)):
+                self.conv_into_pool[op] = conv
+                self.skipped.add(conv)
+        fused_convs = set(self.conv_into_pool.values())
         need_f32, i8_req = set(), {}
         for op in g.ops:
-            if op.is_constant_like or op in self.skipped:
+            if op.is_constant_like or (op in self.skipped and op not in fused_convs):
                 continue
             if op.kind in QOPS:
                 x = op.inputs[0]
@@ -269,6 +288,8 @@ class Plan:
                     i8_req.setdefault(x, s)
                 for v in op.inputs[1:]:
                     need_f32.add(v)
+            elif op.kind == "maxpool2d" and op in self.conv_into_pool:
+                pass
             elif op.kind == "maxpool2d" and op in self.pad_into_pool:
                 need_f32.add(self.pad_into_pool[op][0])
             else:
@@ -277,6 +298,22 @@ class Plan:
         need_f32.update(g.outputs)
         self.need_f32 = {v for v in need_f32 if self._const(v) is None}
         self.i8_req = i8_req
+
+    def _conv_pool_fusable(self, conv) -> bool:
+        """A qconv2d whose only consumer is a max pool can run inside the pooling kernel when it has
+        at most 64 output channels and its epilogue operands are constant scalars or per-channel."""
+        _, _, _, groups = conv_attrs(conv.attrs)
+        o = np.asarray(conv.attrs["q"]).shape[0]
+        if groups != 1 or o > 64:
+            return False
+        probe = DVal(tuple(conv.result.type.shape), "nhwc")
+        for fn, idx, _ in conv.attrs.get("epilogue", ()):
+            if idx is None:
+                continue
+            val = self._const(conv.inputs[idx])
+            if val is None or not (val.size == 1 or self._is_channel(val.shape, probe)):
+                return False
+        return True
 
     # ------------------------------------------------------------------ build
 
@@ -468,12 +505,37 @@ class Plan:
             src, pad, pad_value = self.pad_into_pool[op]
         else:
             src, pad, pad_value = op.inputs[0], 0, float("-inf")
+        if op in self.conv_into_pool:
+            self._conv_pool(op, self.conv_into_pool[op], pad, pad_value)
+            return
         x = self.vals[src]
         n, c, h, w = x.shape
         out = self._new_out(op.result, "nhwc")
         self._launch("maxpool", x_f32=x.f32, n=n, h=h, w=w, c=c, ldc=c, size=op.attrs["size"],
                      stride=op.attrs["stride"], pad=pad, pad_value=pad_value, out_f32=out.f32, ldo=c,
                      out_i8=out.i8, ldo_i8=out.i8_ld, scale=out.i8_scale or 1.0)
+
+    def _conv_pool(self, pool, conv, pad: int, pad_value: float) -> None:
+        """qconv2d -> (pad) -> maxpool2d as one kernel: the conv epilogue runs on the conv outputs,
+        the pooled values are written (reference ops.py:630-634, then 469-470 and 293-296)."""
+        a = conv.attrs
+        stride, padding, dilation, _ = conv_attrs(a)
+        x = self.vals[conv.inputs[0]]
+        n, c, h, w = x.shape
+        q = np.asarray(a["q"])
+        o, _, kh, kw = q.shape
+        xi8, cp = self._i8_of(conv.inputs[0], _f32(a["x_scale"]))
+        wq, _ = K.conv_weight(q, cp)
+        out = self._new_out(pool.result, "nhwc")
+        probe = DVal(tuple(conv.result.type.shape), "nhwc")
+        epi = self._epilogue(conv, probe)
+        epi.out_f32, epi.ld_f32 = out.f32, out.cols
+        epi.out_i8, epi.ld_i8 = out.i8, out.i8_ld
+        epi.out_scale = out.i8_scale if out.i8 is not None else 1.0
+        self._launch("qconv2d_pool", n=n, h=h, w=w, cp=cp, x=xi8, o=o, kh=kh, kw=kw, wq=self._upload(wq),
+                     ldw=wq.shape[1], stride=stride, padding=padding, dilation=dilation,
+                     pool_size=pool.attrs["size"], pool_stride=pool.attrs["stride"], pool_pad=pad,
+                     pool_pad_value=pad_value, dq=self._scales(a["x_scale"], a["w_scale"]), epi=epi)
 
     def _op_pad(self, op) -> None:
         p, value = _pad_hw(op)
@@ -534,11 +596,11 @@ def supported_reason(op) -> Optional[str]:
 class CudaExecutable:
     """Runs one compiled segment (reference Executable protocol, base.py:13-16)."""
 
-    def __init__(self, g, device, use_graph: bool = True):
+    def __init__(self, g, device, use_graph: bool = True, fuse_pool: bool = False):
         self.g = g
         self.device = device
         t0 = time.perf_counter()
-        self.plan = Plan(g, device)
+        self.plan = Plan(g, device, fuse_pool=fuse_pool)
         self.thunks = [device.thunk(l) for l in self.plan.launches]
         self.pin_in = {v: device.pinned(nb) for v, _, nb in self.plan.inputs}
         self.pin_out = {v: device.pinned(nb) for v, _, nb in self.plan.outputs}
@@ -623,14 +685,17 @@ class CudaTarget:
 
     name = "cuda"
 
-    def __init__(self, device: Optional[int] = None, graphs: bool = True, executor=None, **_ignored):
+    def __init__(self, device: Optional[int] = None, graphs: bool = True, executor=None, fuse_pool: bool = False,
+                 **_ignored):
         """device: GPU index (default $MIRA_CUDA_DEVICE or 0).  graphs: replay launches from a CUDA
-        graph after the first run.  executor: an object with CudaDevice's interface to run the plan
-        on instead (host-side testing of the planner); options of other targets are ignored."""
+        graph after the first run.  fuse_pool: compute a qconv2d that only feeds a max pool inside
+        the pooling kernel.  executor: an object with CudaDevice's interface to run the plan on
+        instead (host-side testing of the planner); options of other targets are ignored."""
         if device is None:
             device = int(os.environ.get("MIRA_CUDA_DEVICE", "0"))
         self.device_index = int(device)
         self.graphs = graphs
+        self.fuse_pool = fuse_pool
         self._device = executor
 
     def check(self, op) -> Optional[str]:
@@ -639,4 +704,4 @@ class CudaTarget:
     def compile(self, g, compile_sub=None) -> CudaExecutable:
         if self._device is None:
             self._device = CudaDevice(self.device_index)
-        return CudaExecutable(g, self._device, use_graph=self.graphs)
+        return CudaExecutable(g, self._device, use_graph=self.graphs, fuse_pool=self.fuse_pool)

@@ -124,6 +124,29 @@ class FakeDevice:
         rows = acc.transpose(0, 2, 3, 1).reshape(n * oh * ow, o)
         self._epi(self._dequant(rows, dq, o), epi, n * oh * ow, o)
 
+    def _qconv2d_pool(self, n, h, w, cp, x, o, kh, kw, wq, ldw, stride, padding, dilation, pool_size, pool_stride,
+                      pool_pad, pool_pad_value, dq, epi):
+        xn = x.view(np.int8, (n, h, w, cp)).transpose(0, 3, 1, 2)
+        wt = wq.view(np.int8, (o, ldw))[:, : kh * kw * cp].reshape(o, kh, kw, cp).transpose(0, 3, 1, 2)
+        acc = ref.int_conv2d(xn, wt, stride, padding, dilation)
+        oh, ow = acc.shape[2:]
+        rows = self._dequant(acc.transpose(0, 2, 3, 1).reshape(-1, o), dq, o)
+        conv_out = FakeBuf(rows.size * 4)
+        import copy
+        inner = copy.copy(epi)
+        inner.out_f32, inner.ld_f32, inner.out_i8 = conv_out, o, None
+        self._epi(rows, inner, n * oh * ow, o)
+        y = conv_out.view(np.float32, (n, oh, ow, o)).transpose(0, 3, 1, 2)
+        pooled = ref.maxpool2d(y, pool_size, pool_stride, pool_pad, pool_pad_value)
+        ph, pw = pooled.shape[2:]
+        flat = pooled.transpose(0, 2, 3, 1).reshape(-1, o)
+        if epi.out_f32 is not None:
+            epi.out_f32.view(np.float32, (n * ph * pw, epi.ld_f32))[:, :o] = flat
+        if epi.out_i8 is not None:
+            q = epi.out_i8.view(np.int8, (n * ph * pw, epi.ld_i8))
+            q[:, :o] = ref.quantize_activation(flat, epi.out_scale)
+            q[:, o:] = 0
+
     def _maxpool(self, n, h, w, c, ldc, size, stride, pad, pad_value, x_f32=None, x_i8=None, out_f32=None, ldo=0,
                  out_i8=None, ldo_i8=0, scale=1.0):
         xv = x_f32.view(np.float32, (n, h, w, ldc))[..., :c].transpose(0, 3, 1, 2)

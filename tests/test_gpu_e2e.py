@@ -19,12 +19,12 @@ except ImportError:  # the host framework package is not on this machine
 needs_mira = pytest.mark.skipif(mira_missing, reason="MIRA host framework (package `mira`) not importable")
 
 
-def _pair(name, batch, n_calib=2, **kw):
+def _pair(name, batch, n_calib=2, fuse_pool=False, **kw):
     g_cpu = configs.BUILDERS[name](batch, **kw)
     g_cuda = configs.BUILDERS[name](batch, **kw)
     cal = [configs.random_inputs(g_cpu, 100 + i) for i in range(n_calib)]
     cpu = compiler.compile_ir(g_cpu, "cpu", quantize="w8a8", calibration=cal, precision=None)
-    cuda = compiler.compile_ir(g_cuda, "cuda", quantize="w8a8", calibration=cal)
+    cuda = compiler.compile_ir(g_cuda, "cuda", quantize="w8a8", calibration=cal, fuse_pool=fuse_pool)
     return cpu, cuda
 
 
@@ -52,6 +52,12 @@ def test_config1_mlp_batch256_bit_exact(cuda_device):
 def test_resnet18_bit_exact(cuda_device, batch, image):
     cpu, cuda = _pair("resnet18", batch, image=image)
     assert [s.device for s in cuda.segments] == ["cuda"]
+    _assert_same(cpu, cuda, seeds=(1,))
+
+
+@needs_mira
+def test_resnet18_fused_stem_pool_bit_exact(cuda_device):
+    cpu, cuda = _pair("resnet18", 2, fuse_pool=True, image=64)
     _assert_same(cpu, cuda, seeds=(1,))
 
 

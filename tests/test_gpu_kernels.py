@@ -280,3 +280,41 @@ def test_layout_roundtrip(cuda_device):
     np.testing.assert_array_equal(yb.download((3, 9, 13, 70), np.float32), x.transpose(0, 2, 3, 1))
     K.nhwc_to_nchw(yb, 3, 9, 13, 70, 70, zb)
     np.testing.assert_array_equal(zb.download(x.shape, np.float32), x)
+
+
+# ------------------------------------------------------------------------------ fused conv + max pool
+
+@pytest.mark.parametrize("case", [
+    dict(n=2, c=3, h=40, w=36, o=64, k=7, s=2, p=3, ps=3, pst=2, pp=1),     # ResNet stem + its pool
+    dict(n=3, c=1, h=28, w=28, o=16, k=3, s=1, p=1, ps=2, pst=2, pp=0),     # small CNN block
+    dict(n=2, c=16, h=14, w=14, o=32, k=3, s=1, p=1, ps=2, pst=2, pp=0),
+    dict(n=1, c=32, h=17, w=15, o=48, k=3, s=1, p=1, ps=3, pst=2, pp=1),
+])
+def test_qconv2d_maxpool_fused_exact(cuda_device, case):
+    K, DB = _k()
+    n, c, h, w, o, k = case["n"], case["c"], case["h"], case["w"], case["o"], case["k"]
+    rng = np.random.default_rng(n * 100 + c + o)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    x_scale = float(np.abs(x).max() / 127.0)
+    q, w_scale = ref.quantize_array(rng.standard_normal((o, c, k, k)).astype(np.float32), 0)
+    bias = rng.standard_normal((o, 1, 1)).astype(np.float32)
+    xq, _, y = ref.qconv2d(x, q, w_scale, x_scale, (case["s"],) * 2, (case["p"],) * 2,
+                           steps=[("add", 1, False), ("relu", None, False)], operands=[bias])
+    want = ref.maxpool2d(y, case["ps"], case["pst"], case["pp"], -np.inf)
+    wq, cp = K.conv_weight(q)
+    xn = np.zeros((n, h, w, cp), np.int8)
+    xn[..., :c] = xq.transpose(0, 2, 3, 1)
+    s64, hi, lo = K.scale_arrays(x_scale, w_scale)
+    bufs = [DB.from_array(a) for a in (xn, wq, s64, hi, lo, K.pad_channels(bias))]
+    ph, pw = want.shape[2:]
+    ldi = K.round_up(o, 16)
+    yb, qb = DB(n * ph * pw * o * 4), DB(n * ph * pw * ldi)
+    out_scale = float(np.abs(want).max() / 127.0)
+    K.qconv2d_maxpool(n, h, w, cp, bufs[0], o, k, k, bufs[1], wq.shape[1], (case["s"],) * 2, (case["p"],) * 2,
+                      (1, 1), case["ps"], case["pst"], case["pp"], -np.inf, K.dequant_channel(*bufs[2:5]),
+                      K.Epi([K.Step("add", "channel", ptr=bufs[5]), K.Step("relu")], out_f32=yb, ld_f32=o,
+                            out_i8=qb, ld_i8=ldi, out_scale=out_scale))
+    _same_f32(yb.download((n, ph, pw, o), np.float32).transpose(0, 3, 1, 2), want)
+    got_q = qb.download((n, ph, pw, ldi), np.int8)
+    np.testing.assert_array_equal(got_q[..., :o].transpose(0, 3, 1, 2), ref.quantize_activation(want, out_scale))
+    assert not got_q[..., o:].any()

@@ -11,7 +11,7 @@ mira = install()
 from mira import compiler  # noqa: E402
 
 
-def _pair(name, batch, **kw):
+def _pair(name, batch, fuse_pool=False, **kw):
     """(reference cpu W8A8 program, cuda program on the fake device) for the same network."""
     cal_seed = 100
     g_cpu = configs.BUILDERS[name](batch, **kw)
@@ -19,7 +19,7 @@ def _pair(name, batch, **kw):
     cal = [configs.random_inputs(g_cpu, cal_seed + i) for i in range(2)]
     cpu = compiler.compile_ir(g_cpu, "cpu", quantize="w8a8", calibration=cal, precision=None)
     dev = FakeDevice()
-    cuda = compiler.compile_ir(g_cuda, "cuda", quantize="w8a8", calibration=cal, executor=dev)
+    cuda = compiler.compile_ir(g_cuda, "cuda", quantize="w8a8", calibration=cal, executor=dev, fuse_pool=fuse_pool)
     return cpu, cuda, dev
 
 
@@ -44,6 +44,16 @@ def test_resnet18_small_plan_matches_cpu():
     assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
     _check_same(cpu, cuda)
     assert dev.launched.count("qconv2d") == 20 and dev.launched.count("qgemm") == 1
+    assert dev.launched.count("maxpool") == 1
+
+
+def test_resnet18_fused_stem_pool_plan_matches_cpu():
+    """With fuse_pool the stem conv runs inside the max-pool kernel (its f32 output never reaches
+    HBM)."""
+    cpu, cuda, dev = _pair("resnet18", 2, fuse_pool=True, image=32)
+    _check_same(cpu, cuda)
+    assert dev.launched.count("qconv2d_pool") == 1
+    assert dev.launched.count("qconv2d") == 19 and dev.launched.count("maxpool") == 0
 
 
 def test_mobilenet_v2_small_plan_matches_cpu():
