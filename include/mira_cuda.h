@@ -127,8 +127,12 @@ int mira_cuda_graph_begin(void);
 int mira_cuda_graph_end(void** graph_exec);
 int mira_cuda_graph_launch(void* graph_exec);
 int mira_cuda_graph_destroy(void* graph_exec);
-/* Number of kernels this library launched on the current thread (all devices). */
+/* Number of kernels this library launched (all threads, all devices). */
 int64_t mira_cuda_launch_count(void);
+/* Diagnostic: launches a kernel whose bounded wait on a barrier that nothing completes gives up
+ * after timeout_us (at most 1 s); the following mira_cuda_sync must return MIRA_CUDA_EKERNEL and
+ * leave the device usable.  No counterpart in the reference (it has no device code). */
+int mira_cuda_selftest_wait_timeout(int64_t timeout_us);
 
 /* ---------------------------------------------------------------- kernels */
 

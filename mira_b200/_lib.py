@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "mira_cuda_graph_launch": (_i32, [_vp]),
     "mira_cuda_graph_destroy": (_i32, [_vp]),
     "mira_cuda_launch_count": (_i64, []),
+    "mira_cuda_selftest_wait_timeout": (_i32, [_i64]),
     "mira_cuda_quantize_rows": (_i32, [_vp, _i64, _i64, _i64, _f32, _vp, _i64]),
     "mira_cuda_quantize_nchw_to_nhwc": (_i32, [_vp, _i64, _i64, _i64, _i64, _f32, _vp, _i64]),
     "mira_cuda_qgemm": (_i32, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, C.POINTER(Dequant), C.POINTER(Epilogue)]),

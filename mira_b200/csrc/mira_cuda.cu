@@ -233,6 +233,25 @@ static int fill_epilogue(QgParams& p, const mira_dequant* dq, const mira_epilogu
   return MIRA_CUDA_OK;
 }
 
+// Diagnostic kernel: waits on an mbarrier that nothing ever completes, with the kernels' usual
+// bounded wait shortened to `timeout_ns`; records error 2 when the wait gives up, as every kernel
+// here does on an expired wait.
+__global__ void selftest_wait_kernel(uint64_t timeout_ns, int* err) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!mbar_wait(&bar, 0, &abort_flag, timeout_ns)) atomicExch(err, 2);
+    mbar_arrive(&bar);   // complete the phase so the barrier is not left pending
+  }
+  __syncthreads();
+}
+
 }  // namespace mira
 
 using namespace mira;
@@ -399,6 +418,13 @@ extern "C" int mira_cuda_graph_destroy(void* graph_exec) {
 }
 
 extern "C" int64_t mira_cuda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+extern "C" int mira_cuda_selftest_wait_timeout(int64_t timeout_us) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(timeout_us > 0 && timeout_us <= 1000000, "timeout must be in (0, 1 s]");
+  selftest_wait_kernel<<<1, 32, 0, dev->stream>>>(uint64_t(timeout_us) * 1000u, device_err_ptr());
+  return after_launch("selftest_wait_kernel");
+}
 
 // ================================================================== C ABI: kernels
 

@@ -122,3 +122,15 @@ def test_small_batch_calibration_maps_onto_large_graph():
     full = compiler.compile_ir(g, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
     scales_full = [op.attrs["x_scale"] for op in full.graph.ops if op.kind == "qmatmul"]
     assert scales_small == scales_full
+
+
+@pytest.mark.parametrize("name", ["mlp", "resnet18", "mobilenet_v2"])
+def test_plan_matches_stored_reference_outputs(name):
+    """Against the reference's own outputs saved in tests/golden/programs.npz."""
+    from pathlib import Path
+    z = np.load(Path(__file__).resolve().parent / "golden" / "programs.npz")
+    batch, image, n_cal = int(z[f"{name}_batch"]), int(z[f"{name}_image"]), int(z[f"{name}_n_calib"])
+    g = configs.BUILDERS[name](batch, **({"image": image} if image else {}))
+    cal = [configs.random_inputs(g, 100 + i) for i in range(n_cal)]
+    prog = compiler.compile_ir(g, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
+    np.testing.assert_array_equal(prog.run({"x": z[f"{name}_x"]}), z[f"{name}_out"])
