@@ -10,6 +10,9 @@ Reference hooks (myramay/MIRA):
     cuda computes in f32 exactly like the cpu golden model, so "auto" becomes None for "cuda".
   * mira/partition.py:73-80         placement asks target.check(op); CudaTarget.check accepts every
     qmatmul/qconv2d, and compile_ir verifies afterwards that none landed on the CPU.
+  * mira/compiler.py:134-150        CompiledProgram.run validates the named inputs and converts each
+    with astype, which always copies; for cuda programs the same checks run but an input that
+    already has the IR dtype is passed on without a copy (the executable copies it to the device).
 """
 from __future__ import annotations
 
@@ -59,6 +62,32 @@ def install():
         return prog
 
     Cmp.compile_ir = compile_ir
+
+    original_run = Cmp.CompiledProgram.run
+
+    @functools.wraps(original_run)
+    def run(self, inputs):
+        if self.target not in ("cuda", "b200"):
+            return original_run(self, inputs)
+        import numpy as np
+        from mira.errors import MiraError
+        missing = [v.name for v in self.graph.inputs if v.name not in inputs]
+        if missing:
+            raise MiraError(f"missing input(s): {', '.join(missing)}")
+        extra = set(inputs) - {v.name for v in self.graph.inputs}
+        if extra:
+            raise MiraError(f"unknown input(s): {', '.join(sorted(extra))}")
+        feeds = {}
+        for v in self.graph.inputs:
+            arr = np.asarray(inputs[v.name])
+            if tuple(arr.shape) != v.type.shape:
+                raise MiraError(f"input '{v.name}' should have shape {list(v.type.shape)}, got {list(arr.shape)}")
+            feeds[v] = np.asarray(arr, dtype=v.type.np_dtype)
+        env = self.runner.run_env(feeds)
+        outs = [env[v] for v in self.graph.outputs]
+        return outs[0] if len(outs) == 1 else tuple(outs)
+
+    Cmp.CompiledProgram.run = run
     _installed = True
     return mira
 
