@@ -268,8 +268,11 @@ def main() -> None:
 
         import torch
         import torch.distributed as dist
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"      # keep stdout to the one JSON line
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
 
     from mira_b200 import _lib
     from mira_b200 import configs
@@ -355,7 +358,8 @@ def main() -> None:
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "resnet18-w8a8-224", "global_batch": args.batch * world,
                        "batch_per_gpu": args.batch, "parallelism": f"dp{world} (replicas, no collective)",
-                       "l2": "inputs larger than L2 (154 MB input batch, ~2 GB of activations per step)",
+                       "l2": (f"inputs larger than L2 ({host_x.nbytes / 1e6:.0f} MB input batch, activations "
+                              "of several GB per step)") if host_x.nbytes > 126e6 else "inputs smaller than L2",
                        "calibration": f"4 seeded N(0,1) batches of {args.calib_batch} images",
                        "compile_s": round(compile_s, 1)},
             "e2e": {"value": imgs / e2e_s, "unit": "img/s", "h2d_bytes_per_step": int(host_x.nbytes),

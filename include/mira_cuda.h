@@ -58,6 +58,13 @@ extern "C" {
 
 #define MIRA_EPI_MAX_STEPS 8
 
+/* int8 convolution input layouts */
+#define MIRA_LAYOUT_NHWC 0      /* [n, h, w, cp] */
+#define MIRA_LAYOUT_ROW4 1      /* row-expanded, for inputs of at most 4 channels: [n, h, entries, 16]
+                                   where entry e holds pixels e - pad_w .. e - pad_w + 3, 4 channels
+                                   each, 0 outside the image; weights [o, kh * 32] with
+                                   k = i * 32 + j * 4 + c (taps j >= kw and channels >= c are 0) */
+
 typedef struct mira_epi_step {
   int32_t op;         /* MIRA_EPI_* */
   int32_t operand;    /* MIRA_OPND_* */
@@ -148,6 +155,11 @@ int mira_cuda_quantize_rows(const float* x, int64_t rows, int64_t cols, int64_t 
 int mira_cuda_quantize_nchw_to_nhwc(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
                                     float scale, int8_t* xq, int64_t cp);
 
+/* The same quantization into the MIRA_LAYOUT_ROW4 layout (c <= 4): `row_entries` entries per image
+ * row, `pad` = the consumer convolution's horizontal padding. */
+int mira_cuda_quantize_nchw_to_row4(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
+                                    float scale, int8_t* xq, int64_t row_entries, int64_t pad);
+
 /* W8A8 matmul, reference ops.py:616-620 (_qmatmul_ref) with the epilogue of ops.py:192-199:
  *   acc[m, n] = sum_k A[m, k] * B[n, k]   (exact int32)
  *   y = epilogue(f32(f64(acc) * S))        (S from `dq`)
@@ -157,12 +169,14 @@ int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t ld
                     const int8_t* B, int64_t ldb, const mira_dequant* dq,
                     const mira_epilogue* epi);
 
-/* W8A8 convolution as an implicit GEMM over NHWC int8, reference ops.py:630-634 (_qconv2d_ref,
- * through _conv2d_ref ops.py:265-276 with groups = 1).
- * x: int8 NHWC [n, h, w, cp] (cp multiple of 4; 16 unless cp == 4); weights: int8 [o, ldw] with
- * k = (i * kw + j) * cp + c, ldw = round_up(kh*kw*cp, 16).  The result [n*oh*ow, o] (NHWC) goes
- * through the same epilogue as mira_cuda_qgemm. */
+/* W8A8 convolution as an implicit GEMM over int8 activations, reference ops.py:630-634
+ * (_qconv2d_ref, through _conv2d_ref ops.py:265-276 with groups = 1).
+ * x: MIRA_LAYOUT_NHWC int8 [n, h, w, cp] (cp 4 or a multiple of 16) with weights int8 [o, ldw],
+ * k = (i * kw + j) * cp + c, ldw = round_up(kh*kw*cp, 16); or MIRA_LAYOUT_ROW4 (x_row_entries
+ * entries per row) with its weight layout.  The result [n*oh*ow, o] (NHWC) goes through the same
+ * epilogue as mira_cuda_qgemm. */
 int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x,
+                      int64_t x_layout, int64_t x_row_entries,
                       int64_t o, int64_t kh, int64_t kw, const int8_t* wq, int64_t ldw,
                       int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
                       int64_t dil_h, int64_t dil_w, const mira_dequant* dq,
@@ -172,9 +186,12 @@ int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t*
  * epilogue, then pad (ops.py:469-470, `pool_pad` pixels of `pool_pad_value`) and maxpool2d
  * (ops.py:293-296, window `pool_size`, stride `pool_stride`).  The conv outputs never leave the
  * SM: each tile computes the conv pixels under a block of pooled outputs and pools them in shared
- * memory; `epi`'s outputs are the pooled [n*ph*pw, o] f32 / int8 tensors.  o <= 64; epilogue
- * operands must be scalar or per-channel. */
-int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o,
+ * memory; `epi`'s outputs are the pooled [n*ph*pw, o] f32 / int8 tensors.  o <= 64; the epilogue
+ * must be monotone non-decreasing (relu; add, non-swapped sub, maximum, minimum of scalar or
+ * per-channel constants) because the kernel pools the int32 accumulators and applies it to the
+ * pooled values; pool padding must be -inf. */
+int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x,
+                              int64_t x_layout, int64_t x_row_entries, int64_t o,
                               int64_t kh, int64_t kw, const int8_t* wq, int64_t ldw, int64_t stride_h,
                               int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
                               int64_t pool_size, int64_t pool_stride, int64_t pool_pad, float pool_pad_value,

@@ -17,6 +17,7 @@ OK, EINVAL, ECUDA, ENODEV, EKERNEL = 0, 1, 2, 3, 4
 EPI_RELU, EPI_GELU, EPI_SIGMOID, EPI_TANH = 1, 2, 3, 4
 EPI_ADD, EPI_SUB, EPI_MUL, EPI_DIV, EPI_MAXIMUM, EPI_MINIMUM = 16, 17, 18, 19, 20, 21
 OPND_NONE, OPND_SCALAR, OPND_CHANNEL, OPND_FULL, OPND_ROW = 0, 1, 2, 3, 4
+LAYOUT_NHWC, LAYOUT_ROW4 = 0, 1
 EPI_MAX_STEPS = 8
 
 UNARY_CODES = {"relu": EPI_RELU, "gelu": EPI_GELU, "sigmoid": EPI_SIGMOID, "tanh": EPI_TANH}
@@ -71,10 +72,11 @@ SIGNATURES: dict[str, tuple] = {
     "mira_cuda_quantize_rows": (_i32, [_vp, _i64, _i64, _i64, _f32, _vp, _i64]),
     "mira_cuda_quantize_nchw_to_nhwc": (_i32, [_vp, _i64, _i64, _i64, _i64, _f32, _vp, _i64]),
     "mira_cuda_qgemm": (_i32, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, C.POINTER(Dequant), C.POINTER(Epilogue)]),
-    "mira_cuda_qconv2d": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
-                                 _i64, _i64, C.POINTER(Dequant), C.POINTER(Epilogue)]),
-    "mira_cuda_qconv2d_maxpool": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
-                                         _i64, _i64, _i64, _i64, _i64, _i64, _f32, C.POINTER(Dequant),
+    "mira_cuda_quantize_nchw_to_row4": (_i32, [_vp, _i64, _i64, _i64, _i64, _f32, _vp, _i64, _i64]),
+    "mira_cuda_qconv2d": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64,
+                                 _i64, _i64, _i64, _i64, C.POINTER(Dequant), C.POINTER(Epilogue)]),
+    "mira_cuda_qconv2d_maxpool": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64,
+                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, C.POINTER(Dequant),
                                          C.POINTER(Epilogue)]),
     "mira_cuda_maxpool2d_nhwc": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _i64,
                                         _vp, _i64, _f32]),

@@ -79,6 +79,48 @@ __global__ void quantize_nchw_nhwc_kernel(const float* __restrict__ x, int64_t n
   }
 }
 
+// Quantization of an NCHW f32 image batch with at most 4 channels into the row-expanded int8
+// layout read by the ROW4 convolution gather: for every image row, `entries` 16-byte entries, entry
+// e holding pixels e - pad .. e - pad + 3 with 4 channels each (zero outside the image and for
+// channels >= c).  One thread per entry; neighbouring threads read neighbouring pixels.
+__global__ void quantize_nchw_row4_kernel(const float* __restrict__ x, int n, int c, int h, int w, QuantScale q,
+                                          int8_t* __restrict__ xq, int entries, int pad) {
+  // one warp per (image row, block of 32 entries); lane l quantizes pixel e0 - pad + l once (and
+  // lanes 0-2 the three pixels after the block) and the 4-pixel entries are assembled by shuffles
+  const int lane = threadIdx.x & 31;
+  const int blocks = (entries + 31) / 32;
+  const int64_t total_warps = int64_t(n) * h * blocks;
+  const int64_t warps_per_grid = int64_t(gridDim.x) * (blockDim.x / 32);
+  for (int64_t wi = blockIdx.x * int64_t(blockDim.x / 32) + (threadIdx.x >> 5); wi < total_warps;
+       wi += warps_per_grid) {
+    const int blk = static_cast<int>(wi % blocks);
+    const int64_t row = wi / blocks;               // n * h + y
+    const int img = static_cast<int>(row / h);
+    const int y = static_cast<int>(row - int64_t(img) * h);
+    const int e0 = blk * 32;
+    auto pixel_word = [&](int xx) -> uint32_t {
+      uint32_t b[4];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch)
+        b[ch] = (ch < c && xx >= 0 && xx < w) ? quant_byte(__ldg(x + ((int64_t(img) * c + ch) * h + y) * w + xx), q)
+                                              : 0u;
+      return pack4_i8(b[0], b[1], b[2], b[3]);
+    };
+    const uint32_t w0 = pixel_word(e0 - pad + lane);
+    const uint32_t w32 = lane < 3 ? pixel_word(e0 - pad + 32 + lane) : 0u;
+    uint32_t word[4];
+    word[0] = w0;
+#pragma unroll
+    for (int k = 1; k < 4; ++k) {
+      const uint32_t down = __shfl_down_sync(0xffffffffu, w0, k);
+      const uint32_t tail = __shfl_sync(0xffffffffu, w32, (lane + k - 32) & 31);
+      word[k] = lane + k < 32 ? down : tail;
+    }
+    if (e0 + lane < entries)
+      reinterpret_cast<uint4*>(xq)[row * entries + e0 + lane] = make_uint4(word[0], word[1], word[2], word[3]);
+  }
+}
+
 // ---------------------------------------------------------------- K5: max pooling (NHWC)
 
 // f32 input: one thread per (output pixel, 4 channels).  Padding pixels take `pad_value` (the
@@ -98,6 +140,7 @@ __global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, in
     const int oy = rem / ow, ox = rem - (rem / ow) * ow;
     float mx[4];
     bool first = true;
+    const bool vec = (c % 4) == 0 && (ldc % 4) == 0;
     for (int i = 0; i < size; ++i) {
       const int iy = oy * stride + i - pad;
       for (int j = 0; j < size; ++j) {
@@ -107,8 +150,13 @@ __global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, in
           v[0] = v[1] = v[2] = v[3] = pad_value;
         } else {
           const float* src = x + (int64_t(img) * h * w + int64_t(iy) * w + ix) * ldc + cg * 4;
+          if (vec) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(src));
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+          } else {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) v[e] = (cg * 4 + e < c) ? src[e] : 0.0f;
+            for (int e = 0; e < 4; ++e) v[e] = (cg * 4 + e < c) ? src[e] : 0.0f;
+          }
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) mx[e] = first ? v[e] : np_maximum(mx[e], v[e]);
@@ -117,9 +165,13 @@ __global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, in
     }
     if (out != nullptr) {
       float* dst = out + pix * ldo + cg * 4;
+      if (vec && (ldo % 4) == 0) {
+        *reinterpret_cast<float4*>(dst) = make_float4(mx[0], mx[1], mx[2], mx[3]);
+      } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (cg * 4 + e < c) dst[e] = mx[e];
+        for (int e = 0; e < 4; ++e)
+          if (cg * 4 + e < c) dst[e] = mx[e];
+      }
     }
     if (out_i8 != nullptr) {
       uint32_t b[4];

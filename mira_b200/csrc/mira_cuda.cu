@@ -455,6 +455,20 @@ extern "C" int mira_cuda_quantize_nchw_to_nhwc(const float* x, int64_t n, int64_
   return after_launch("quantize_nchw_nhwc_kernel");
 }
 
+extern "C" int mira_cuda_quantize_nchw_to_row4(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
+                                               float scale, int8_t* xq, int64_t row_entries, int64_t pad) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && c > 0 && c <= 4 && h > 0 && w > 0 && row_entries > 0 && pad >= 0, "bad quantize_row4 shape");
+  MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(xq) & 15) == 0, "int8 output must be 16-byte aligned");
+  MIRA_CHECK_ARG(scale > 0.0f && std::isfinite(scale), "quantization scale must be positive");
+  if (n == 0) return MIRA_CUDA_OK;
+  const int threads = 256;
+  quantize_nchw_row4_kernel<<<grid_for(dev, n * h * ((row_entries + 31) / 32) * 32, threads), threads, 0,
+                              dev->stream>>>(
+      x, int(n), int(c), int(h), int(w), make_qscale(scale), xq, int(row_entries), int(pad));
+  return after_launch("quantize_nchw_row4_kernel");
+}
+
 extern "C" int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda, const int8_t* B,
                                int64_t ldb, const mira_dequant* dq, const mira_epilogue* epi) {
   MIRA_GET_DEVICE(dev);
@@ -485,10 +499,10 @@ extern "C" int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A,
 }
 
 // Shared argument checks and parameter setup of the implicit-GEMM convolutions.
-static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o, int64_t kh, int64_t kw,
-                      int64_t ldw, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h,
-                      int64_t dil_w, const mira_dequant* dq, const mira_epilogue* epi, QgParams& p, int64_t& oh,
-                      int64_t& ow) {
+static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t x_layout,
+                      int64_t x_row_entries, int64_t o, int64_t kh, int64_t kw, int64_t ldw, int64_t stride_h,
+                      int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
+                      const mira_dequant* dq, const mira_epilogue* epi, QgParams& p, int64_t& oh, int64_t& ow) {
   MIRA_CHECK_ARG(n >= 0 && h > 0 && w > 0 && o > 0 && kh > 0 && kw > 0, "bad qconv2d shape");
   MIRA_CHECK_ARG(cp == 4 || (cp > 0 && cp % 16 == 0), "input channels must be padded to 4 or a multiple of 16");
   MIRA_CHECK_ARG(stride_h > 0 && stride_w > 0 && dil_h > 0 && dil_w > 0 && pad_h >= 0 && pad_w >= 0, "bad conv geometry");
@@ -497,9 +511,15 @@ static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t*
   oh = (h + 2 * pad_h - dil_h * (kh - 1) - 1) / stride_h + 1;
   ow = (w + 2 * pad_w - dil_w * (kw - 1) - 1) / stride_w + 1;
   MIRA_CHECK_ARG(oh > 0 && ow > 0, "kernel larger than the padded input");
-  const int64_t K = kh * kw * cp;
+  MIRA_CHECK_ARG(x_layout == MIRA_LAYOUT_NHWC || x_layout == MIRA_LAYOUT_ROW4, "unknown input layout");
+  if (x_layout == MIRA_LAYOUT_ROW4) {
+    MIRA_CHECK_ARG(cp == 4 && kw <= 8 && dil_h == 1 && dil_w == 1,
+                   "the row-expanded layout serves 4-channel inputs, kernel width <= 8, no dilation");
+    MIRA_CHECK_ARG(x_row_entries >= (ow - 1) * stride_w + 5, "row-expanded input has too few entries per row");
+  }
+  const int64_t K = x_layout == MIRA_LAYOUT_ROW4 ? kh * 32 : kh * kw * cp;
   MIRA_CHECK_ARG(K <= 133000, "K too large for exact int32 accumulation of int8 products");
-  MIRA_CHECK_ARG(ldw >= round_up(K, 16) && ldw % 16 == 0, "weight row stride must be >= round_up(kh*kw*cp, 16)");
+  MIRA_CHECK_ARG(ldw >= round_up(K, 16) && ldw % 16 == 0, "weight row stride must be >= round_up(K, 16)");
   const int64_t M = n * oh * ow;
   MIRA_CHECK_ARG(M < (int64_t(1) << 31) && n * h * w * cp < (int64_t(1) << 40), "conv too large");
   std::memset(&p, 0, sizeof(p));
@@ -512,18 +532,19 @@ static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t*
   p.num_kb = int((K + QG_BK - 1) / QG_BK);
   p.A = x;
   p.g = QgConv{int(n), int(h), int(w), int(cp), int(oh), int(ow), int(kh), int(kw), int(stride_h), int(stride_w),
-               int(pad_h), int(pad_w), int(dil_h), int(dil_w)};
+               int(pad_h), int(pad_w), int(dil_h), int(dil_w), int(x_row_entries)};
   return MIRA_CUDA_OK;
 }
 
-extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o, int64_t kh,
-                                 int64_t kw, const int8_t* wq, int64_t ldw, int64_t stride_h, int64_t stride_w,
-                                 int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w, const mira_dequant* dq,
-                                 const mira_epilogue* epi) {
+extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t x_layout,
+                                 int64_t x_row_entries, int64_t o, int64_t kh, int64_t kw, const int8_t* wq,
+                                 int64_t ldw, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                 int64_t dil_h, int64_t dil_w, const mira_dequant* dq, const mira_epilogue* epi) {
   MIRA_GET_DEVICE(dev);
   QgParams p;
   int64_t oh, ow;
-  int rc = conv_setup(n, h, w, cp, x, o, kh, kw, ldw, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dq, epi, p, oh, ow);
+  int rc = conv_setup(n, h, w, cp, x, x_layout, x_row_entries, o, kh, kw, ldw, stride_h, stride_w, pad_h, pad_w, dil_h,
+                      dil_w, dq, epi, p, oh, ow);
   if (rc != MIRA_CUDA_OK) return rc;
   if (p.M == 0) return MIRA_CUDA_OK;
   const int bn = pick_bn(o);
@@ -533,26 +554,38 @@ extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, co
   std::memset(&tmA, 0, sizeof(tmA));
   rc = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, uint32_t(bn));
   if (rc != MIRA_CUDA_OK) return rc;
+  if (x_layout == MIRA_LAYOUT_ROW4) return launch_qgemm_bn<QG_A_ROW4, false>(dev, tmA, tmB, p, bn);
   if (cp == 4) return launch_qgemm_bn<QG_A_GATHER4, false>(dev, tmA, tmB, p, bn);
   return launch_qgemm_bn<QG_A_GATHER16, false>(dev, tmA, tmB, p, bn);
 }
 
-extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t o,
-                                         int64_t kh, int64_t kw, const int8_t* wq, int64_t ldw, int64_t stride_h,
-                                         int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
-                                         int64_t pool_size, int64_t pool_stride, int64_t pool_pad, float pool_pad_value,
+extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x,
+                                         int64_t x_layout, int64_t x_row_entries, int64_t o, int64_t kh, int64_t kw,
+                                         const int8_t* wq, int64_t ldw, int64_t stride_h, int64_t stride_w,
+                                         int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w, int64_t pool_size,
+                                         int64_t pool_stride, int64_t pool_pad, float pool_pad_value,
                                          const mira_dequant* dq, const mira_epilogue* epi) {
   MIRA_GET_DEVICE(dev);
   QgParams p;
   int64_t oh, ow;
-  int rc = conv_setup(n, h, w, cp, x, o, kh, kw, ldw, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, dq, epi, p, oh, ow);
+  int rc = conv_setup(n, h, w, cp, x, x_layout, x_row_entries, o, kh, kw, ldw, stride_h, stride_w, pad_h, pad_w, dil_h,
+                      dil_w, dq, epi, p, oh, ow);
   if (rc != MIRA_CUDA_OK) return rc;
   MIRA_CHECK_ARG(o <= 64, "fused pooling supports convolutions with at most 64 output channels");
   MIRA_CHECK_ARG(pool_size > 0 && pool_stride > 0 && pool_pad >= 0 && pool_pad < pool_size, "bad pool geometry");
-  for (int s = 0; s < p.n_steps; ++s)
-    MIRA_CHECK_ARG(p.steps[s].operand == MIRA_OPND_NONE || p.steps[s].operand == MIRA_OPND_SCALAR ||
-                       p.steps[s].operand == MIRA_OPND_CHANNEL,
-                   "fused pooling supports scalar and per-channel epilogue operands only");
+  // the kernel pools the int32 accumulators and applies the epilogue to the pooled values, which
+  // equals pooling the epilogue's outputs when every step is monotone non-decreasing in its input
+  for (int s = 0; s < p.n_steps; ++s) {
+    const mira_epi_step& st = p.steps[s];
+    const bool monotone =
+        (st.operand == MIRA_OPND_NONE && st.op == MIRA_EPI_RELU) ||
+        ((st.operand == MIRA_OPND_SCALAR || st.operand == MIRA_OPND_CHANNEL) &&
+         (st.op == MIRA_EPI_ADD || st.op == MIRA_EPI_MAXIMUM || st.op == MIRA_EPI_MINIMUM ||
+          (st.op == MIRA_EPI_SUB && !st.swapped)));
+    MIRA_CHECK_ARG(monotone, "fused pooling needs a monotone epilogue (relu, add/sub/max/min of constants)");
+  }
+  MIRA_CHECK_ARG(pool_pad == 0 || std::isinf(pool_pad_value) && pool_pad_value < 0,
+                 "fused pooling pads with -inf only");
   const int64_t ph = (oh + 2 * pool_pad - pool_size) / pool_stride + 1;
   const int64_t pw = (ow + 2 * pool_pad - pool_size) / pool_stride + 1;
   MIRA_CHECK_ARG(ph > 0 && pw > 0, "pool window larger than the conv output");
@@ -580,6 +613,7 @@ extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_
   std::memset(&tmA, 0, sizeof(tmA));
   rc = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, 64u);
   if (rc != MIRA_CUDA_OK) return rc;
+  if (x_layout == MIRA_LAYOUT_ROW4) return launch_qgemm_cfg<64, 7, QG_A_ROW4, false, 4, true>(dev, tmA, tmB, p);
   if (cp == 4) return launch_qgemm_cfg<64, 7, QG_A_GATHER4, false, 4, true>(dev, tmA, tmB, p);
   return launch_qgemm_cfg<64, 7, QG_A_GATHER16, false, 4, true>(dev, tmA, tmB, p);
 }

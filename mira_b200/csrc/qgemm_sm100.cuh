@@ -11,7 +11,9 @@
 //               16-column chunk of a tile; one output row per thread: tcgen05.ld, exact dequant,
 //               the fused epilogue steps, requantized int8 stores, and f32 stores staged through
 //               shared memory so each store instruction writes whole 64-byte row segments
-//   next 4 warps (convolutions only) im2col gather of A from NHWC int8 with cp.async, one output
+//   next 4 warps (convolutions only) im2col gather of A from NHWC int8 (or, for inputs of at most
+//               4 channels, from the row-expanded layout: 16-byte entries holding 4 consecutive
+//               pixels, so a kernel row of up to 8 taps is two copies) with cp.async, one output
 //               pixel (tile row) per thread, zero fill for padding; each thread's copies arrive on
 //               the stage barrier when they land (cp.async.mbarrier.arrive.noinc), so the gather
 //               runs up to STAGES K-blocks ahead of the MMAs
@@ -31,12 +33,13 @@ constexpr int QG_BK = 128;               // K bytes per stage = one 128-byte swi
 constexpr int QG_UMMA_K = 32;            // K per tcgen05.mma kind::i8
 constexpr uint64_t QG_TIMEOUT_NS = 2000000000ull;
 
-enum QgAMode { QG_A_TMA = 0, QG_A_GATHER16 = 1, QG_A_GATHER4 = 2 };
+enum QgAMode { QG_A_TMA = 0, QG_A_GATHER16 = 1, QG_A_GATHER4 = 2, QG_A_ROW4 = 3 };
 
 struct QgConv {
   int n, h, w, cp;      // input NHWC (cp = padded channels)
   int oh, ow;
   int kh, kw, sh, sw, ph, pw, dh, dw;
+  int row_entries;      // QG_A_ROW4: 16-byte entries per image row (entry e = pixels e - pw .. e - pw + 3)
 };
 
 struct QgParams {
@@ -189,10 +192,9 @@ __device__ __forceinline__ void qg_apply_step(const mira_epi_step& st, const flo
 // The whole epilogue of one 16-column chunk of this warp's 32 rows.  Everything that does not
 // depend on the accumulator (dequant scales, the first binary operand) is loaded before the TMEM
 // read so the two latencies overlap.
-template <bool ROWCOL, int PITCH, bool POOL = false, int POOL_PITCH = 0>
+template <bool ROWCOL, int PITCH>
 __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t taddr, int m, bool row_ok, int m_warp0,
-                                                  int nb, float* stage, int lane, float* ptile_row = nullptr,
-                                                  int nb_local = 0) {
+                                                  int nb, float* stage, int lane) {
   const bool full_chunk = nb + 16 <= p.N;
   float hs[16], ls[16];
   if (!ROWCOL) {
@@ -250,15 +252,6 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
     qg_apply_step(st, o, v);
   }
 
-  if (POOL) {
-    // conv outputs stay in shared memory; the pooling phase writes the results
-    if (ptile_row != nullptr) {
-      float4* d4 = reinterpret_cast<float4*>(ptile_row + nb_local);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    }
-    return;
-  }
   if (p.out_f32 != nullptr) {
     if (full_chunk && (p.ld_f32 % 4) == 0) {
       float4* srow = reinterpret_cast<float4*>(stage + lane * PITCH);
@@ -439,29 +432,37 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
       } else {
-        // conv outputs of the tile -> shared tile buffer (acc parity), then pool from it
+        // The conv epilogue (dequant, then steps that the host checked are monotone non-decreasing)
+        // commutes with max, so the int32 accumulators are pooled first and the epilogue runs on the
+        // pooled values only: accumulators -> shared tile (acc parity) -> window max -> epilogue.
         const int r = quarter * 32 + lane;
         int img, cy, cx, ty, tx;
         bool valid;
         pool_row_pixel(p, t_m, r, img, cy, cx, ty, tx, valid);
-        float* ptile = staging + acc * Cfg::POOL_ROWS * Cfg::POOL_PITCH;
-        float* prow = r < p.pool_span * p.pool_span ? ptile + r * Cfg::POOL_PITCH : nullptr;
-        const bool warp_used = quarter * 32 < p.pool_span * p.pool_span;   // warp-uniform
+        int32_t* ptile = reinterpret_cast<int32_t*>(staging) + acc * Cfg::POOL_ROWS * Cfg::POOL_PITCH;
+        const int span = p.pool_span;
+        const bool warp_used = quarter * 32 < span * span;   // warp-uniform
 #pragma unroll 1
         for (int c = group; warp_used && c < BN / Cfg::CW; c += G) {
-          const int nb = n0 + c * Cfg::CW;
-          if (nb >= p.N) break;
-          qg_epilogue_chunk<false, Cfg::STAGE_PITCH, true>(p, tbase + c * Cfg::CW, 0, valid, 0, nb, stage, lane,
-                                                             prow, c * Cfg::CW);
+          if (n0 + c * Cfg::CW >= p.N) break;
+          uint32_t acc_r[16];
+          tmem_ld_32x32b_x16(tbase + c * Cfg::CW, acc_r);
+          tmem_ld_wait();
+          if (r < span * span) {
+            // conv pixels outside the conv output are the pool's -inf padding
+            uint4* d4 = reinterpret_cast<uint4*>(ptile + r * Cfg::POOL_PITCH + c * Cfg::CW);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              d4[q] = valid ? make_uint4(acc_r[4 * q], acc_r[4 * q + 1], acc_r[4 * q + 2], acc_r[4 * q + 3])
+                            : make_uint4(0x80000000u, 0x80000000u, 0x80000000u, 0x80000000u);
+          }
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
         mbar_arrive(&pool_bar[acc]);
         if (!mbar_wait(&pool_bar[acc], (it >> 1) & 1, abort_flag, QG_TIMEOUT_NS)) break;
-        // pooling: max over each window of the stored conv outputs; conv pixels outside the
-        // conv output (the pool's padding) take pool_pad_value
         const int et = threadIdx.x - 32 * Cfg::EPI_WARP0;
-        const int T = p.pool_t, S = p.pool_s, P = p.pool_p, span = p.pool_span;
+        const int T = p.pool_t, S = p.pool_s, P = p.pool_p;
         for (int o = et; o < T * T * BN; o += Cfg::EPI_THREADS) {
           const int ch = o % BN, pp = o / BN;
           const int py = pp / T, px = pp - (pp / T) * T;
@@ -473,21 +474,27 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
             if (p.out_i8 != nullptr && col < p.ld_i8) p.out_i8[orow * p.ld_i8 + col] = 0;
             continue;
           }
-          float mx = 0.0f;
+          int32_t mx = INT32_MIN;
           for (int dy = 0; dy < P; ++dy) {
-            const int cyy = ty * T * S - p.pool_pad + S * py + dy;
-            for (int dx = 0; dx < P; ++dx) {
-              const int cxx = tx * T * S - p.pool_pad + S * px + dx;
-              const bool inside = cyy >= 0 && cyy < p.g.oh && cxx >= 0 && cxx < p.g.ow;
-              const float v = inside ? ptile[((S * py + dy) * span + S * px + dx) * Cfg::POOL_PITCH + ch]
-                                     : p.pool_pad_value;
-              mx = (dy == 0 && dx == 0) ? v : np_maximum(mx, v);
+            const int32_t* prow = ptile + ((S * py + dy) * span + S * px) * Cfg::POOL_PITCH + ch;
+            for (int dx = 0; dx < P; ++dx) mx = max(mx, prow[dx * Cfg::POOL_PITCH]);
+          }
+          float y;
+          if (!dequant_fast(mx, __ldg(p.scale_hi + col), __ldg(p.scale_lo + col), y))
+            y = __double2float_rn(static_cast<double>(mx) * p.scale64[col]);
+          for (int s = 0; s < p.n_steps; ++s) {
+            const mira_epi_step& st = p.steps[s];
+            if (st.operand == MIRA_OPND_NONE) {
+              y = apply_unary(st.op, y);
+            } else {
+              const float opnd = st.operand == MIRA_OPND_SCALAR ? st.scalar : __ldg(st.ptr + col);
+              y = st.swapped ? apply_binary(st.op, opnd, y) : apply_binary(st.op, y, opnd);
             }
           }
-          if (p.out_f32 != nullptr) p.out_f32[orow * p.ld_f32 + col] = mx;
+          if (p.out_f32 != nullptr) p.out_f32[orow * p.ld_f32 + col] = y;
           if (p.out_i8 != nullptr)
             p.out_i8[orow * p.ld_i8 + col] =
-                static_cast<int8_t>(round_clip_i8(div_by_scale(mx, p.q_scale, p.q_rcp, p.q_lim)) & 0xff);
+                static_cast<int8_t>(round_clip_i8(div_by_scale(y, p.q_scale, p.q_rcp, p.q_lim)) & 0xff);
         }
       }
     }
@@ -556,6 +563,18 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
                 tap_ptr = base + (static_cast<int64_t>(iy) * g.w + ix0) * g.cp;
               }
             }
+          }
+        } else if (AMODE == QG_A_ROW4) {
+          // k = i * 32 + j * 4 + c: chunk (i, half) is entry (ox * sw + 4 * half) of input row iy0 + i
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int i = kb * 4 + (c >> 1);
+            const int iy = iy0 + i;
+            const bool v = row_ok && i < g.kh && static_cast<unsigned>(iy) < static_cast<unsigned>(g.h) &&
+                           (c * 16 < kmax);
+            const int8_t* src = p.A + ((static_cast<int64_t>(img) * g.h + iy) * g.row_entries +
+                                       ox * g.sw + 4 * (c & 1)) * 16;
+            cp_async_16(dst_row + ((c ^ swz) << 4), v ? src : p.A, v ? 16u : 0u);
           }
         } else {
 #pragma unroll 4

@@ -72,6 +72,21 @@ def conv_weight(q_oihw: np.ndarray, cp: Optional[int] = None) -> tuple[np.ndarra
     return out, cp
 
 
+def row4_entries(ow: int, stride_w: int) -> int:
+    """16-byte entries per image row of the row-expanded layout for a conv with output width ow."""
+    return (int(ow) - 1) * int(stride_w) + 5
+
+
+def conv_weight_row4(q_oihw: np.ndarray) -> np.ndarray:
+    """Reference qconv2d weight int8 [O, C<=4, KH, KW<=8] -> [O, KH*32] for MIRA_LAYOUT_ROW4 inputs:
+    k = i * 32 + j * 4 + c (taps j >= KW and channels c >= C are 0)."""
+    o, c, kh, kw = q_oihw.shape
+    assert c <= 4 and kw <= 8
+    t = np.zeros((o, kh, 8, 4), np.int8)
+    t[:, :, :kw, :c] = q_oihw.transpose(0, 2, 3, 1)
+    return t.reshape(o, kh * 32)
+
+
 # ----------------------------------------------------------------------------- epilogue descriptors
 
 @dataclass
@@ -149,20 +164,25 @@ def qgemm(M: int, N: int, K: int, A, lda: int, B, ldb: int, dq: _lib.Dequant, ep
     _lib.call("mira_cuda_qgemm", M, N, K, ptr(A), lda, ptr(B), ldb, C.byref(dq), C.byref(e))
 
 
+def quantize_nchw_to_row4(x, n: int, c: int, h: int, w: int, scale: float, xq, row_entries: int, pad: int) -> None:
+    _lib.call("mira_cuda_quantize_nchw_to_row4", ptr(x), n, c, h, w, float(np.float32(scale)), ptr(xq), row_entries,
+              pad)
+
+
 def qconv2d(n: int, h: int, w: int, cp: int, x, o: int, kh: int, kw: int, wq, ldw: int, stride, padding,
-            dilation, dq: _lib.Dequant, epi: Epi) -> None:
+            dilation, dq: _lib.Dequant, epi: Epi, layout: int = 0, row_entries: int = 0) -> None:
     e = epi.struct()
-    _lib.call("mira_cuda_qconv2d", n, h, w, cp, ptr(x), o, kh, kw, ptr(wq), ldw, stride[0], stride[1],
-              padding[0], padding[1], dilation[0], dilation[1], C.byref(dq), C.byref(e))
+    _lib.call("mira_cuda_qconv2d", n, h, w, cp, ptr(x), layout, row_entries, o, kh, kw, ptr(wq), ldw, stride[0],
+              stride[1], padding[0], padding[1], dilation[0], dilation[1], C.byref(dq), C.byref(e))
 
 
 def qconv2d_maxpool(n: int, h: int, w: int, cp: int, x, o: int, kh: int, kw: int, wq, ldw: int, stride, padding,
                     dilation, pool_size: int, pool_stride: int, pool_pad: int, pool_pad_value: float,
-                    dq: _lib.Dequant, epi: Epi) -> None:
+                    dq: _lib.Dequant, epi: Epi, layout: int = 0, row_entries: int = 0) -> None:
     e = epi.struct()
-    _lib.call("mira_cuda_qconv2d_maxpool", n, h, w, cp, ptr(x), o, kh, kw, ptr(wq), ldw, stride[0], stride[1],
-              padding[0], padding[1], dilation[0], dilation[1], pool_size, pool_stride, pool_pad,
-              float(np.float32(pool_pad_value)), C.byref(dq), C.byref(e))
+    _lib.call("mira_cuda_qconv2d_maxpool", n, h, w, cp, ptr(x), layout, row_entries, o, kh, kw, ptr(wq), ldw,
+              stride[0], stride[1], padding[0], padding[1], dilation[0], dilation[1], pool_size, pool_stride,
+              pool_pad, float(np.float32(pool_pad_value)), C.byref(dq), C.byref(e))
 
 
 def maxpool2d(n, h, w, c, ldc_in, size, stride, pad, pad_value, x_f32=None, x_i8=None, out_f32=None,

@@ -96,6 +96,10 @@ class CudaDevice:
         elif k == "quantize_nchw":
             fn = L.mira_cuda_quantize_nchw_to_nhwc
             args = (ptr(a["x"]), a["n"], a["c"], a["h"], a["w"], float(np.float32(a["scale"])), ptr(a["xq"]), a["cp"])
+        elif k == "quantize_row4":
+            fn = L.mira_cuda_quantize_nchw_to_row4
+            args = (ptr(a["x"]), a["n"], a["c"], a["h"], a["w"], float(np.float32(a["scale"])), ptr(a["xq"]),
+                    a["row_entries"], a["pad"])
         elif k == "nchw_to_nhwc":
             fn = L.mira_cuda_nchw_to_nhwc_f32
             args = (ptr(a["x"]), a["n"], a["c"], a["h"], a["w"], ptr(a["y"]), a["ldc"])
@@ -112,14 +116,15 @@ class CudaDevice:
             elif k == "qconv2d_pool":
                 fn = L.mira_cuda_qconv2d_maxpool
                 (sh, sw), (ph, pw), (dh, dw) = a["stride"], a["padding"], a["dilation"]
-                args = (a["n"], a["h"], a["w"], a["cp"], ptr(a["x"]), a["o"], a["kh"], a["kw"], ptr(a["wq"]), a["ldw"],
-                        sh, sw, ph, pw, dh, dw, a["pool_size"], a["pool_stride"], a["pool_pad"],
+                args = (a["n"], a["h"], a["w"], a["cp"], ptr(a["x"]), a["layout"], a["row_entries"], a["o"], a["kh"],
+                        a["kw"], ptr(a["wq"]), a["ldw"], sh, sw, ph, pw, dh, dw, a["pool_size"], a["pool_stride"],
+                        a["pool_pad"],
                         float(np.float32(a["pool_pad_value"])), C.byref(dq), C.byref(e))
             else:
                 fn = L.mira_cuda_qconv2d
                 (sh, sw), (ph, pw), (dh, dw) = a["stride"], a["padding"], a["dilation"]
-                args = (a["n"], a["h"], a["w"], a["cp"], ptr(a["x"]), a["o"], a["kh"], a["kw"], ptr(a["wq"]), a["ldw"],
-                        sh, sw, ph, pw, dh, dw, C.byref(dq), C.byref(e))
+                args = (a["n"], a["h"], a["w"], a["cp"], ptr(a["x"]), a["layout"], a["row_entries"], a["o"], a["kh"],
+                        a["kw"], ptr(a["wq"]), a["ldw"], sh, sw, ph, pw, dh, dw, C.byref(dq), C.byref(e))
         elif k == "maxpool":
             fn = L.mira_cuda_maxpool2d_nhwc
             args = (ptr(a.get("x_f32")), ptr(a.get("x_i8")), a["n"], a["h"], a["w"], a["c"], a["ldc"], a["size"],
@@ -161,6 +166,8 @@ class DVal:
     i8: object = None
     i8_scale: Optional[float] = None
     i8_ld: int = 0
+    i8_layout: str = "nhwc"      # or "row4" (MIRA_LAYOUT_ROW4, graph inputs of at most 4 channels)
+    row_entries: int = 0
 
     @property
     def rows(self) -> int:
@@ -256,6 +263,7 @@ class Plan:
     def _requirements(self):
         g = self.g
         users = g.users()
+        self.users = users
         self.pad_into_pool = {}      # maxpool op -> (source value, pad, pad value)
         self.conv_into_pool = {}     # maxpool op -> qconv2d op computed inside the pooling kernel
         for op in g.ops:
@@ -270,8 +278,9 @@ class Plan:
                 self.skipped.add(pad_op)
                 src = pad_op.inputs[0]
             conv = src.producer
-            if (self.fuse_pool and conv is not None and conv.kind == "qconv2d" and len(users.get(src, [])) == 1
-                    and src not in g.outputs and self._conv_pool_fusable(conv)):
+            pad_ok = op not in self.pad_into_pool or self.pad_into_pool[op][2] == float("-inf")
+            if (self.fuse_pool and pad_ok and conv is not None and conv.kind == "qconv2d"
+                    and len(users.get(src, [])) == 1 and src not in g.outputs and self._conv_pool_fusable(conv)):
                 self.conv_into_pool[op] = conv
                 self.skipped.add(conv)
         fused_convs = set(self.conv_into_pool.values())
@@ -301,15 +310,21 @@ class Plan:
 
     def _conv_pool_fusable(self, conv) -> bool:
         """A qconv2d whose only consumer is a max pool can run inside the pooling kernel when it has
-        at most 64 output channels and its epilogue operands are constant scalars or per-channel."""
+        at most 64 output channels and its epilogue is monotone non-decreasing (relu, and add /
+        non-swapped sub / maximum / minimum of constant scalars or per-channel values): the kernel
+        pools the int32 accumulators and applies the epilogue to the pooled values."""
         _, _, _, groups = conv_attrs(conv.attrs)
         o = np.asarray(conv.attrs["q"]).shape[0]
         if groups != 1 or o > 64:
             return False
         probe = DVal(tuple(conv.result.type.shape), "nhwc")
-        for fn, idx, _ in conv.attrs.get("epilogue", ()):
+        for fn, idx, swapped in conv.attrs.get("epilogue", ()):
             if idx is None:
+                if fn != "relu":
+                    return False
                 continue
+            if fn not in ("add", "maximum", "minimum", "sub") or (fn == "sub" and swapped):
+                return False
             val = self._const(conv.inputs[idx])
             if val is None or not (val.size == 1 or self._is_channel(val.shape, probe)):
                 return False
@@ -356,9 +371,17 @@ class Plan:
                     dv.f32 = self._alloc(dv.numel * 4)
                     self._launch("nchw_to_nhwc", x=buf, n=n, c=c, h=h, w=w, y=dv.f32, ldc=c)
             if v in self.i8_req:
-                cp = 4 if c <= 4 else K.round_up(c, 16)
-                dv.i8, dv.i8_scale, dv.i8_ld = self._alloc(n * h * w * cp, zero=True), self.i8_req[v], cp
-                self._launch("quantize_nchw", x=buf, n=n, c=c, h=h, w=w, scale=dv.i8_scale, xq=dv.i8, cp=cp)
+                row4 = self._row4_geometry(v)
+                dv.i8_scale = self.i8_req[v]
+                if row4 is not None:
+                    entries, pad = row4
+                    dv.i8, dv.i8_layout, dv.row_entries, dv.i8_ld = self._alloc(n * h * entries * 16), "row4", entries, 4
+                    self._launch("quantize_row4", x=buf, n=n, c=c, h=h, w=w, scale=dv.i8_scale, xq=dv.i8,
+                                 row_entries=entries, pad=pad)
+                else:
+                    cp = 4 if c <= 4 else K.round_up(c, 16)
+                    dv.i8, dv.i8_ld = self._alloc(n * h * w * cp, zero=True), cp
+                    self._launch("quantize_nchw", x=buf, n=n, c=c, h=h, w=w, scale=dv.i8_scale, xq=dv.i8, cp=cp)
         else:
             dv.f32 = buf
             if v in self.i8_req:
@@ -369,10 +392,46 @@ class Plan:
         self.vals[v] = dv
         return dv
 
+    def _row4_geometry(self, v):
+        """(entries, pad) when every consumer of the int8 value of `v` is a convolution that can read
+        the row-expanded layout (at most 4 channels, kernel width <= 8, no dilation) with one common
+        horizontal geometry; None otherwise."""
+        if v.type.shape[1] > 4:
+            return None
+        geo = None
+        for op in self.users.get(v, []):
+            if op.kind != "qconv2d":
+                if op.kind in QOPS:
+                    return None
+                continue
+            stride, padding, dilation, groups = conv_attrs(op.attrs)
+            kw = np.asarray(op.attrs["q"]).shape[3]
+            if groups != 1 or kw > 8 or tuple(dilation) != (1, 1) or op.inputs[0] is not v:
+                return None
+            ow = op.result.type.shape[3]
+            g = (K.row4_entries(ow, stride[1]), padding[1])
+            if geo is not None and g != geo:
+                return None
+            geo = g
+        return geo
+
+    def _conv_input(self, v, scale: float):
+        """(int8 buffer, channels per pixel, layout code, entries per row) of a conv input."""
+        dv = self.vals[v]
+        if dv.i8 is not None and dv.i8_scale == scale and dv.i8_layout == "row4":
+            return dv.i8, 4, _lib.LAYOUT_ROW4, dv.row_entries
+        buf, cp = self._i8_of(v, scale)
+        return buf, cp, _lib.LAYOUT_NHWC, 0
+
+    def _conv_weight(self, q, cp: int, layout: int) -> np.ndarray:
+        if layout == _lib.LAYOUT_ROW4:
+            return K.conv_weight_row4(q)
+        return K.conv_weight(q, cp)[0]
+
     def _i8_of(self, v, scale: float):
         """(int8 buffer, row stride) of `v` quantized with `scale`."""
         dv = self.vals[v]
-        if dv.i8 is not None and dv.i8_scale == scale:
+        if dv.i8 is not None and dv.i8_scale == scale and dv.i8_layout == "nhwc":
             return dv.i8, dv.i8_ld
         if dv.f32 is None:
             raise UnsupportedOnCuda("int8 operand without an f32 source")
@@ -480,11 +539,11 @@ class Plan:
         n, c, h, w = x.shape
         q = np.asarray(a["q"])
         o, _, kh, kw = q.shape
-        xi8, cp = self._i8_of(op.inputs[0], _f32(a["x_scale"]))
-        wq, _ = K.conv_weight(q, cp)
+        xi8, cp, layout, entries = self._conv_input(op.inputs[0], _f32(a["x_scale"]))
+        wq = self._conv_weight(q, cp, layout)
         out = self._new_out(op.result, "nhwc")
-        self._launch("qconv2d", n=n, h=h, w=w, cp=cp, x=xi8, o=o, kh=kh, kw=kw, wq=self._upload(wq), ldw=wq.shape[1],
-                     stride=stride, padding=padding, dilation=dilation,
+        self._launch("qconv2d", n=n, h=h, w=w, cp=cp, x=xi8, layout=layout, row_entries=entries, o=o, kh=kh, kw=kw,
+                     wq=self._upload(wq), ldw=wq.shape[1], stride=stride, padding=padding, dilation=dilation,
                      dq=self._scales(a["x_scale"], a["w_scale"]), epi=self._epilogue(op, out))
 
     def _op_conv2d(self, op) -> None:
@@ -524,15 +583,16 @@ class Plan:
         n, c, h, w = x.shape
         q = np.asarray(a["q"])
         o, _, kh, kw = q.shape
-        xi8, cp = self._i8_of(conv.inputs[0], _f32(a["x_scale"]))
-        wq, _ = K.conv_weight(q, cp)
+        xi8, cp, layout, entries = self._conv_input(conv.inputs[0], _f32(a["x_scale"]))
+        wq = self._conv_weight(q, cp, layout)
         out = self._new_out(pool.result, "nhwc")
         probe = DVal(tuple(conv.result.type.shape), "nhwc")
         epi = self._epilogue(conv, probe)
         epi.out_f32, epi.ld_f32 = out.f32, out.cols
         epi.out_i8, epi.ld_i8 = out.i8, out.i8_ld
         epi.out_scale = out.i8_scale if out.i8 is not None else 1.0
-        self._launch("qconv2d_pool", n=n, h=h, w=w, cp=cp, x=xi8, o=o, kh=kh, kw=kw, wq=self._upload(wq),
+        self._launch("qconv2d_pool", n=n, h=h, w=w, cp=cp, x=xi8, layout=layout, row_entries=entries, o=o, kh=kh,
+                     kw=kw, wq=self._upload(wq),
                      ldw=wq.shape[1], stride=stride, padding=padding, dilation=dilation,
                      pool_size=pool.attrs["size"], pool_stride=pool.attrs["stride"], pool_pad=pad,
                      pool_pad_value=pad_value, dq=self._scales(a["x_scale"], a["w_scale"]), epi=epi)

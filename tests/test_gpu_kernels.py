@@ -318,3 +318,48 @@ def test_qconv2d_maxpool_fused_exact(cuda_device, case):
     got_q = qb.download((n, ph, pw, ldi), np.int8)
     np.testing.assert_array_equal(got_q[..., :o].transpose(0, 3, 1, 2), ref.quantize_activation(want, out_scale))
     assert not got_q[..., o:].any()
+
+
+# ------------------------------------------------------------------------------ row-expanded inputs
+
+@pytest.mark.parametrize("case", [
+    dict(n=2, c=3, h=40, w=36, o=64, k=7, s=2, p=3),     # ResNet stem
+    dict(n=2, c=3, h=33, w=31, o=32, k=3, s=2, p=1),     # MobileNetV2 stem
+    dict(n=3, c=1, h=28, w=28, o=16, k=3, s=1, p=1),
+    dict(n=1, c=4, h=9, w=13, o=24, k=5, s=1, p=0),
+])
+@pytest.mark.parametrize("pool", [False, True])
+def test_row4_layout_conv_exact(cuda_device, case, pool):
+    K, DB = _k()
+    n, c, h, w, o, k, s, p = (case[key] for key in ("n", "c", "h", "w", "o", "k", "s", "p"))
+    rng = np.random.default_rng(n + c * 10 + o)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    x_scale = float(np.abs(x).max() / 127.0)
+    q, w_scale = ref.quantize_array(rng.standard_normal((o, c, k, k)).astype(np.float32), 0)
+    bias = rng.standard_normal((o, 1, 1)).astype(np.float32)
+    _, _, y = ref.qconv2d(x, q, w_scale, x_scale, (s, s), (p, p), steps=[("add", 1, False), ("relu", None, False)],
+                          operands=[bias])
+    if pool:
+        y = ref.maxpool2d(y, 3, 2, 1, -np.inf)
+    oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+    entries = K.row4_entries(ow, s)
+    xb, xq = DB.from_array(x), DB(n * h * entries * 16)
+    K.quantize_nchw_to_row4(xb, n, c, h, w, x_scale, xq, entries, p)
+    wq = K.conv_weight_row4(q)
+    s64, hi, lo = K.scale_arrays(x_scale, w_scale)
+    bufs = [DB.from_array(a) for a in (wq, s64, hi, lo, K.pad_channels(bias))]
+    ph, pw_ = y.shape[2:]
+    ldi = K.round_up(o, 16)
+    yb, qb = DB(n * ph * pw_ * o * 4), DB(n * ph * pw_ * ldi)
+    out_scale = float(np.abs(y).max() / 127.0)
+    epi = K.Epi([K.Step("add", "channel", ptr=bufs[4]), K.Step("relu")], out_f32=yb, ld_f32=o, out_i8=qb, ld_i8=ldi,
+                out_scale=out_scale)
+    if pool:
+        K.qconv2d_maxpool(n, h, w, 4, xq, o, k, k, bufs[0], wq.shape[1], (s, s), (p, p), (1, 1), 3, 2, 1, -np.inf,
+                          K.dequant_channel(*bufs[1:4]), epi, layout=1, row_entries=entries)
+    else:
+        K.qconv2d(n, h, w, 4, xq, o, k, k, bufs[0], wq.shape[1], (s, s), (p, p), (1, 1), K.dequant_channel(*bufs[1:4]),
+                  epi, layout=1, row_entries=entries)
+    _same_f32(yb.download((n, ph, pw_, o), np.float32).transpose(0, 3, 1, 2), y)
+    np.testing.assert_array_equal(qb.download((n, ph, pw_, ldi), np.int8)[..., :o].transpose(0, 3, 1, 2),
+                                  ref.quantize_activation(y, out_scale))

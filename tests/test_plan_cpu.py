@@ -45,6 +45,7 @@ def test_resnet18_small_plan_matches_cpu():
     _check_same(cpu, cuda)
     assert dev.launched.count("qconv2d") == 20 and dev.launched.count("qgemm") == 1
     assert dev.launched.count("maxpool") == 1
+    assert dev.launched.count("quantize_row4") == 1    # the 3-channel image feeds the stem row-expanded
 
 
 def test_resnet18_fused_stem_pool_plan_matches_cpu():
