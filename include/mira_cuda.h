@@ -227,6 +227,70 @@ int mira_cuda_nchw_to_nhwc_f32(const float* x, int64_t n, int64_t c, int64_t h, 
 int mira_cuda_nhwc_to_nchw_f32(const float* x, int64_t n, int64_t h, int64_t w, int64_t c,
                                int64_t ldc, float* y);
 
+/* ---------------------------------------------------------------- sequence (transformer) ops
+ *
+ * These cover the f32 ops between the quantized matmuls of a decoder-only transformer.  Tensors
+ * of rank <= 4 are addressed as views: a base pointer and element strides over four dimensions
+ * (batch0, batch1, row, col), lower ranks padded with leading size-1 dimensions, broadcast
+ * dimensions with stride 0.  Row kernels accept rows of at most MIRA_ROW_MAX elements. */
+
+#define MIRA_ROW_MAX 8192
+#define MIRA_OPND_VIEW 5        /* bmm epilogue operand read through a mira_view4 */
+
+typedef struct mira_view4 {
+  void* ptr;                /* device pointer (f32, or int8 for mira_bmm_epilogue.out_i8) */
+  int64_t stride[4];        /* element strides over (batch0, batch1, row, col) */
+} mira_view4;
+
+typedef struct mira_bmm_step {
+  int32_t op;               /* MIRA_EPI_* */
+  int32_t operand;          /* MIRA_OPND_NONE, MIRA_OPND_SCALAR or MIRA_OPND_VIEW */
+  int32_t swapped;          /* 1: f(operand, acc) */
+  float scalar;
+  mira_view4 view;          /* MIRA_OPND_VIEW operand, indexed like the output */
+} mira_bmm_step;
+
+typedef struct mira_bmm_epilogue {
+  int32_t n_steps;
+  mira_bmm_step steps[MIRA_EPI_MAX_STEPS];
+  mira_view4 out_f32;       /* ptr may be NULL */
+  mira_view4 out_i8;        /* ptr may be NULL: int8 requantized with out_scale */
+  float out_scale;
+} mira_bmm_epilogue;
+
+/* Batched f32 matmul C[b0, b1] = A[b0, b1] (M x K) @ B[b0, b1] (K x N) followed by an epilogue,
+ * reference ops.py:217-219 (_matmul_ref: np.matmul of f32 operands, then epilogue_ref,
+ * ops.py:192-199).  Products are accumulated in f32 in k order with fused multiply-adds, so
+ * results agree with the reference's BLAS matmul to f32 rounding, not bit for bit. */
+int mira_cuda_bmm_f32(int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,
+                      const mira_view4* a, const mira_view4* b, const mira_bmm_epilogue* epi);
+
+/* Layer normalization over the last axis of rows [rows, d] (row stride ld_x), reference
+ * ops.py:356-360 (_layernorm_ref): mean and variance in NumPy's pairwise summation order and
+ * float32 division by d, so the f32 result is bit-identical.  Optional outputs: f32 rows
+ * (out_f32, ld_f32) and int8 rows requantized with out_scale (out_i8, ld_i8 bytes). */
+int mira_cuda_layernorm_rows(const float* x, int64_t rows, int64_t d, int64_t ld_x, const float* gamma,
+                             const float* beta, float eps, float* out_f32, int64_t ld_f32, int8_t* out_i8,
+                             int64_t ld_i8, float out_scale);
+
+/* Softmax over the last axis of rows [rows, n], reference ops.py:310-313 (_softmax_ref):
+ * e = exp(x - max(x)), e / sum(e) with the sum in NumPy's pairwise order.  exp is CUDA's
+ * expf (NumPy's own float32 exp is not correctly rounded either), so results agree to a few
+ * units in the last place. */
+int mira_cuda_softmax_rows(const float* x, int64_t rows, int64_t n, int64_t ld_x, float* out, int64_t ld_out);
+
+/* Embedding rows: out[r, :] = table[idx[r], :] (+ addend[r % addend_rows, :] when addend is
+ * non-NULL), reference ops.py:482-487 (_gather_ref, np.take on axis 0) followed by an f32 add.
+ * Negative indices count from the end like np.take; an index outside [-vocab, vocab) writes 0
+ * and makes the next mira_cuda_sync fail (the reference raises IndexError). */
+int mira_cuda_embed_rows(const float* table, int64_t vocab, int64_t d, const int32_t* idx, int64_t rows,
+                         const float* addend, int64_t addend_rows, float* out, int64_t ld_out);
+
+/* Strided copy of a [n0, n1, n2, n3] f32 view into another view (the device form of the
+ * reference's transpose, ops.py:375, when a consumer needs the data in a new order). */
+int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* src,
+                            const mira_view4* dst);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,8 +17,10 @@ OK, EINVAL, ECUDA, ENODEV, EKERNEL = 0, 1, 2, 3, 4
 EPI_RELU, EPI_GELU, EPI_SIGMOID, EPI_TANH = 1, 2, 3, 4
 EPI_ADD, EPI_SUB, EPI_MUL, EPI_DIV, EPI_MAXIMUM, EPI_MINIMUM = 16, 17, 18, 19, 20, 21
 OPND_NONE, OPND_SCALAR, OPND_CHANNEL, OPND_FULL, OPND_ROW = 0, 1, 2, 3, 4
+OPND_VIEW = 5
 LAYOUT_NHWC, LAYOUT_ROW4 = 0, 1
 EPI_MAX_STEPS = 8
+ROW_MAX = 8192
 
 UNARY_CODES = {"relu": EPI_RELU, "gelu": EPI_GELU, "sigmoid": EPI_SIGMOID, "tanh": EPI_TANH}
 BINARY_CODES = {"add": EPI_ADD, "sub": EPI_SUB, "mul": EPI_MUL, "div": EPI_DIV,
@@ -38,6 +40,20 @@ class Epilogue(C.Structure):
 class Dequant(C.Structure):
     _fields_ = [("scale64", C.c_void_p), ("scale_hi", C.c_void_p), ("scale_lo", C.c_void_p),
                 ("row_scale", C.c_void_p), ("col_scale", C.c_void_p)]
+
+
+class View4(C.Structure):
+    _fields_ = [("ptr", C.c_void_p), ("stride", C.c_int64 * 4)]
+
+
+class BmmStep(C.Structure):
+    _fields_ = [("op", C.c_int32), ("operand", C.c_int32), ("swapped", C.c_int32), ("scalar", C.c_float),
+                ("view", View4)]
+
+
+class BmmEpilogue(C.Structure):
+    _fields_ = [("n_steps", C.c_int32), ("steps", BmmStep * EPI_MAX_STEPS), ("out_f32", View4), ("out_i8", View4),
+                ("out_scale", C.c_float)]
 
 
 _i64, _f32, _vp, _i32 = C.c_int64, C.c_float, C.c_void_p, C.c_int
@@ -85,6 +101,12 @@ SIGNATURES: dict[str, tuple] = {
                                        _i64, C.POINTER(Epilogue)]),
     "mira_cuda_nchw_to_nhwc_f32": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64]),
     "mira_cuda_nhwc_to_nchw_f32": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "mira_cuda_bmm_f32": (_i32, [_i64, _i64, _i64, _i64, _i64, C.POINTER(View4), C.POINTER(View4),
+                                 C.POINTER(BmmEpilogue)]),
+    "mira_cuda_layernorm_rows": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _f32, _vp, _i64, _vp, _i64, _f32]),
+    "mira_cuda_softmax_rows": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64]),
+    "mira_cuda_embed_rows": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64]),
+    "mira_cuda_copy_view_f32": (_i32, [_i64, _i64, _i64, _i64, C.POINTER(View4), C.POINTER(View4)]),
 }
 
 

@@ -5,6 +5,8 @@ replaced by folding BN into the conv weights and biases before quantization, as 
   mlp          784-512-512-10 ReLU MLP, Kaiming-normal weights, zero biases (config 1)
   resnet18     torchvision ResNet-18 topology at 224x224, Kaiming-normal convs, BN folded (config 3)
   mobilenet_v2 torchvision MobileNetV2 (width 1.0, ReLU6, inverted residuals), BN folded (config 4)
+  transformer  decoder-only pre-LayerNorm transformer prefill, 12 x (768, 12 heads, MLP 3072 GELU),
+               vocabulary 256 (config 5)
 
 Weights depend only on `seed`, not on the batch size, so a network built at two batch sizes is the
 same network.  `compile_w8a8` compiles through MIRA's own driver (mira/compiler.py compile_ir:
@@ -145,17 +147,88 @@ def mobilenet_v2(batch: int = 1, seed: int = 0, image: int = 224, num_classes: i
     return n.finish(y)
 
 
-BUILDERS: dict[str, Callable] = {"mlp": mlp, "resnet18": resnet18, "mobilenet_v2": mobilenet_v2}
+def transformer(batch: int = 1, seed: int = 0, seq: int = 1024, layers: int = 12, d_model: int = 768,
+                heads: int = 12, d_mlp: int = 3072, vocab: int = 256, max_seq: int = 1024):
+    """Config 5 prefill: decoder-only, pre-LayerNorm GPT block (the structure of the reference's
+    examples/gpt.mira `block`, with heads): token embedding gather + learned positions, per layer
+      x = layernorm(h); q, k, v = x @ Wq + bq, ...; heads via reshape/transpose;
+      p = softmax(q @ k^T * (1/sqrt(dh)) + causal_mask); h = h + (p @ v) @ Wo + bo;
+      h = h + gelu(layernorm(h) @ W1 + b1) @ W2 + b2,
+    then a final layernorm and the LM head.  Weights and biases N(0, 0.02), layernorm gains
+    1 + N(0, 0.02) and shifts N(0, 0.02); the mask is 0 on and below the diagonal and -10000 above
+    (gpt.mira causal_mask).  Tables are drawn at `max_seq` rows so every `seq` sees the same weights."""
+    ir, TT = _ir()
+    if d_model % heads:
+        raise ValueError("d_model must be a multiple of heads")
+    dh = d_model // heads
+    n = _Net.__new__(_Net)
+    n.ir = ir
+    n.x = ir.Value(TT("i32", (batch, seq)), name="tok")
+    n.g = ir.Graph("transformer", [n.x], [], [])
+    n.rng = np.random.default_rng(seed)
+    std = 0.02
+
+    def normal(*shape):
+        return (n.rng.standard_normal(shape) * std).astype(np.float32)
+
+    def ln(h):
+        g = (1.0 + normal(d_model)).astype(np.float32)
+        return n.op("layernorm", [h, n.const(g), n.const(normal(d_model))], {"eps": 1e-5})
+
+    def dense(x, fin, fout, bias=True):
+        y = n.op("matmul", [x, n.const(normal(fin, fout))])
+        return n.op("add", [y, n.const(normal(fout))]) if bias else y
+
+    emb = normal(vocab, d_model)
+    pos = normal(max_seq, d_model)[:seq]
+    mask = np.where(np.arange(seq)[:, None] >= np.arange(seq)[None, :], 0.0, -10000.0).astype(np.float32)
+    h = n.op("add", [n.op("gather", [n.const(emb), n.x], {"axis": 0}), n.const(pos)])
+    for _ in range(layers):
+        x = ln(h)
+        q, k, v = (dense(x, d_model, d_model) for _ in range(3))
+        split = lambda t: n.op("reshape", [t], {"shape": (batch, seq, heads, dh)})
+        qh = n.op("transpose", [split(q)], {"perm": (0, 2, 1, 3)})
+        kt = n.op("transpose", [split(k)], {"perm": (0, 2, 3, 1)})
+        vh = n.op("transpose", [split(v)], {"perm": (0, 2, 1, 3)})
+        s = n.op("matmul", [qh, kt])
+        s = n.op("mul", [s, n.const(np.float32(1.0 / np.sqrt(dh)))])
+        s = n.op("add", [s, n.const(mask)])
+        o = n.op("matmul", [n.op("softmax", [s], {"axis": -1}), vh])
+        o = n.op("reshape", [n.op("transpose", [o], {"perm": (0, 2, 1, 3)})], {"shape": (batch, seq, d_model)})
+        h = n.op("add", [dense(o, d_model, d_model), h])
+        m = n.op("gelu", [dense(ln(h), d_model, d_mlp)])
+        h = n.op("add", [dense(m, d_mlp, d_model), h])
+    logits = dense(ln(h), d_model, vocab, bias=False)
+    return n.finish(logits)
+
+
+BUILDERS: dict[str, Callable] = {"mlp": mlp, "resnet18": resnet18, "mobilenet_v2": mobilenet_v2,
+                                 "transformer": transformer}
+
+
+def _vocab_of(graph, v, default: int = 256) -> int:
+    """Rows of the embedding table that int32 input `v` indexes (by a gather), else `default`."""
+    for op in graph.ops:
+        if op.kind == "gather" and len(op.inputs) > 1 and op.inputs[1] is v:
+            return int(op.inputs[0].type.shape[0])
+    return default
 
 
 def random_inputs(graph, seed: int) -> dict:
-    """Seeded N(0, 1) f32 inputs keyed by input name (like the reference CLI's _inputs, cli.py:76-80)."""
+    """Seeded inputs keyed by input name: N(0, 1) for f32 (like the reference CLI's _inputs,
+    cli.py:76-80), token ids uniform in [0, vocab) for i32 inputs that index an embedding."""
     rng = np.random.default_rng(seed)
-    return {v.name: rng.standard_normal(v.type.shape).astype(np.float32) for v in graph.inputs}
+    out = {}
+    for v in graph.inputs:
+        if v.type.dtype == "i32":
+            out[v.name] = rng.integers(0, _vocab_of(graph, v), v.type.shape).astype(np.int32)
+        else:
+            out[v.name] = rng.standard_normal(v.type.shape).astype(np.float32)
+    return out
 
 
 def compile_w8a8(name: str, batch: int, target: str, *, seed: int = 0, n_calib: int = 4, calib_seed: int = 100,
-                 calib_batch: Optional[int] = None, **kw):
+                 calib_batch: Optional[int] = None, build_kw: Optional[dict] = None, **kw):
     """Build workload `name` at `batch` and compile it W8A8 for `target` through MIRA's compile_ir.
 
     Calibration feeds are `n_calib` seeded N(0, 1) batches.  With `calib_batch` (smaller than
@@ -169,6 +242,8 @@ def compile_w8a8(name: str, batch: int, target: str, *, seed: int = 0, n_calib: 
     from mira import compiler, passes
     from mira import quantize as Q
     build = BUILDERS[name]
+    if build_kw:
+        build = (lambda b, _f=build, **k: _f(b, **k, **build_kw))
     g = build(batch, seed=seed)
     if calib_batch is None or calib_batch == batch:
         cal = [random_inputs(g, calib_seed + i) for i in range(n_calib)]

@@ -15,6 +15,7 @@
 #include "memory_bound.cuh"
 #include "qgemm_sm100.cuh"
 #include "runtime.h"
+#include "sequence_ops.cuh"
 
 // Set by a kernel that gave up on a bounded wait or met an impossible index; read and cleared by
 // mira_cuda_sync.  One copy per device (module global).
@@ -349,6 +350,7 @@ extern "C" int mira_cuda_sync(void) {
   if (flag != 0) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_mira_kernel_error, &zero, sizeof(int));
+    if (flag == 2) return set_error(MIRA_CUDA_EKERNEL, "embedding row index out of range (error record 2)");
     return set_error(MIRA_CUDA_EKERNEL, "a kernel gave up on a bounded wait (error record " + std::to_string(flag) + ")");
   }
   return MIRA_CUDA_OK;
@@ -706,4 +708,143 @@ extern "C" int mira_cuda_nhwc_to_nchw_f32(const float* x, int64_t n, int64_t h, 
   const dim3 grid(unsigned((h * w + 31) / 32), unsigned((c + 31) / 32), unsigned(n));
   nhwc_to_nchw_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(x, int(c), int(h * w), ldc, y);
   return after_launch("nhwc_to_nchw_kernel");
+}
+
+// ---------------------------------------------------------------- sequence (transformer) ops
+
+namespace mira {
+
+static void pw_leaves_rec(int start, int n, PwLeaves& pw) {
+  if (n <= 128) {
+    pw.start[pw.count++] = start;
+    return;
+  }
+  int n2 = n / 2;
+  n2 -= n2 % 8;
+  pw_leaves_rec(start, n2, pw);
+  pw_leaves_rec(start + n2, n - n2, pw);
+}
+
+// NumPy's pairwise recursion cut into leaves of at most 128 elements (rows up to MIRA_ROW_MAX
+// give at most 128 leaves of more than 64 elements each).
+static void pw_leaves(int n, PwLeaves& pw) {
+  std::memset(&pw, 0, sizeof(pw));
+  pw.n = n;
+  if (n >= 8) pw_leaves_rec(0, n, pw);
+  pw.start[pw.count] = n;
+}
+
+static int row_grid(const DeviceState* dev, int64_t rows) {
+  int64_t blocks = (rows + ROW_WARPS - 1) / ROW_WARPS;
+  const int64_t cap = int64_t(dev->sm_count) * 8;
+  return static_cast<int>(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
+}
+
+}  // namespace mira
+
+extern "C" int mira_cuda_layernorm_rows(const float* x, int64_t rows, int64_t d, int64_t ld_x, const float* gamma,
+                                        const float* beta, float eps, float* out_f32, int64_t ld_f32, int8_t* out_i8,
+                                        int64_t ld_i8, float out_scale) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(rows >= 0 && d > 0 && d <= MIRA_ROW_MAX && ld_x >= d, "bad layernorm shape");
+  MIRA_CHECK_ARG(x != nullptr && gamma != nullptr && beta != nullptr, "layernorm needs x, gamma and beta");
+  MIRA_CHECK_ARG(out_f32 != nullptr || out_i8 != nullptr, "layernorm has no output");
+  if (out_f32 != nullptr) MIRA_CHECK_ARG(ld_f32 >= d, "bad f32 output stride");
+  if (out_i8 != nullptr) MIRA_CHECK_ARG(ld_i8 >= d && out_scale > 0.0f, "bad int8 output");
+  if (rows == 0) return MIRA_CUDA_OK;
+  LnParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.x = x; p.rows = rows; p.ld_x = ld_x; p.d = int(d); p.gamma = gamma; p.beta = beta; p.eps = eps;
+  p.out = out_f32; p.ld_out = ld_f32; p.out_i8 = out_i8; p.ld_i8 = ld_i8;
+  p.q = make_qscale(out_i8 != nullptr ? out_scale : 1.0f);
+  pw_leaves(int(d), p.pw);
+  layernorm_rows_kernel<<<row_grid(dev, rows), ROW_WARPS * 32, 0, dev->stream>>>(p);
+  return after_launch("layernorm_rows_kernel");
+}
+
+extern "C" int mira_cuda_softmax_rows(const float* x, int64_t rows, int64_t n, int64_t ld_x, float* out,
+                                      int64_t ld_out) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(rows >= 0 && n > 0 && n <= MIRA_ROW_MAX && ld_x >= n && ld_out >= n, "bad softmax shape");
+  MIRA_CHECK_ARG(x != nullptr && out != nullptr, "softmax needs an input and an output");
+  if (rows == 0) return MIRA_CUDA_OK;
+  SoftmaxParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.x = x; p.rows = rows; p.ld_x = ld_x; p.out = out; p.ld_out = ld_out;
+  pw_leaves(int(n), p.pw);
+  softmax_rows_kernel<<<row_grid(dev, rows), ROW_WARPS * 32, 0, dev->stream>>>(p);
+  return after_launch("softmax_rows_kernel");
+}
+
+extern "C" int mira_cuda_embed_rows(const float* table, int64_t vocab, int64_t d, const int32_t* idx, int64_t rows,
+                                    const float* addend, int64_t addend_rows, float* out, int64_t ld_out) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(vocab > 0 && d > 0 && rows >= 0 && ld_out >= d, "bad embedding shape");
+  MIRA_CHECK_ARG(table != nullptr && idx != nullptr && out != nullptr, "embedding needs a table, indices and an output");
+  if (addend != nullptr) MIRA_CHECK_ARG(addend_rows > 0, "addend needs at least one row");
+  if (rows == 0) return MIRA_CUDA_OK;
+  EmbedParams p;
+  p.table = table; p.vocab = vocab; p.d = d; p.idx = idx; p.rows = rows; p.addend = addend;
+  p.addend_rows = addend_rows; p.out = out; p.ld_out = ld_out; p.err = device_err_ptr();
+  const int threads = 256;
+  embed_rows_kernel<<<grid_for(dev, rows * d, threads), threads, 0, dev->stream>>>(p);
+  return after_launch("embed_rows_kernel");
+}
+
+extern "C" int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* src,
+                                       const mira_view4* dst) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n0 >= 0 && n1 >= 0 && n2 >= 0 && n3 >= 0, "bad view shape");
+  MIRA_CHECK_ARG(src != nullptr && dst != nullptr && src->ptr != nullptr && dst->ptr != nullptr, "null view");
+  const int64_t total = n0 * n1 * n2 * n3;
+  if (total == 0) return MIRA_CUDA_OK;
+  View4 v;
+  v.n[0] = n0; v.n[1] = n1; v.n[2] = n2; v.n[3] = n3;
+  v.src = static_cast<const float*>(src->ptr);
+  v.dst = static_cast<float*>(dst->ptr);
+  for (int i = 0; i < 4; ++i) { v.ss[i] = src->stride[i]; v.ds[i] = dst->stride[i]; }
+  const int threads = 256;
+  copy_view_kernel<<<grid_for(dev, total, threads), threads, 0, dev->stream>>>(v);
+  return after_launch("copy_view_kernel");
+}
+
+extern "C" int mira_cuda_bmm_f32(int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,
+                                 const mira_view4* a, const mira_view4* b, const mira_bmm_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(batch0 >= 0 && batch1 > 0 && m >= 0 && n >= 0 && k >= 0, "bad bmm shape");
+  MIRA_CHECK_ARG(a != nullptr && b != nullptr && epi != nullptr, "bmm needs a, b and an epilogue");
+  MIRA_CHECK_ARG(k == 0 || (a->ptr != nullptr && b->ptr != nullptr), "null bmm operand");
+  MIRA_CHECK_ARG(epi->n_steps >= 0 && epi->n_steps <= MIRA_EPI_MAX_STEPS, "bad epilogue");
+  MIRA_CHECK_ARG(epi->out_f32.ptr != nullptr || epi->out_i8.ptr != nullptr, "bmm has no output");
+  if (epi->out_i8.ptr != nullptr) MIRA_CHECK_ARG(epi->out_scale > 0.0f, "requant scale must be positive");
+  for (int s = 0; s < epi->n_steps; ++s) {
+    const mira_bmm_step& st = epi->steps[s];
+    MIRA_CHECK_ARG(st.operand == MIRA_OPND_NONE || st.operand == MIRA_OPND_SCALAR ||
+                       (st.operand == MIRA_OPND_VIEW && st.view.ptr != nullptr),
+                   "bmm epilogue operands are scalars or views");
+  }
+  const int64_t batches = batch0 * batch1;
+  if (batches == 0 || m == 0 || n == 0) return MIRA_CUDA_OK;
+  BmmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.batches = batches; p.batch1 = batch1; p.m = m; p.n = n; p.k = k;
+  p.a = static_cast<const float*>(a->ptr);
+  p.b = static_cast<const float*>(b->ptr);
+  for (int i = 0; i < 4; ++i) {
+    p.as[i] = a->stride[i]; p.bs[i] = b->stride[i];
+    p.os[i] = epi->out_f32.stride[i]; p.qs[i] = epi->out_i8.stride[i];
+  }
+  p.a_kfast = a->stride[3] == 1 || a->stride[2] != 1;
+  p.b_nfast = b->stride[3] == 1 || b->stride[2] != 1;
+  p.n_steps = epi->n_steps;
+  for (int s = 0; s < epi->n_steps; ++s) p.steps[s] = epi->steps[s];
+  p.out = static_cast<float*>(epi->out_f32.ptr);
+  p.out_i8 = static_cast<int8_t*>(epi->out_i8.ptr);
+  p.q = make_qscale(p.out_i8 != nullptr ? epi->out_scale : 1.0f);
+  const int64_t gy = (m + BMM_BM - 1) / BMM_BM, gx = (n + BMM_BN - 1) / BMM_BN;
+  MIRA_CHECK_ARG(gy <= 65535, "bmm has too many rows");
+  MIRA_CHECK_ARG(gx <= int64_t(INT32_MAX), "bmm has too many columns");
+  const dim3 grid(unsigned(gx), unsigned(gy), unsigned(batches < 65535 ? batches : 65535));
+  bmm_f32_kernel<<<grid, BMM_THREADS, 0, dev->stream>>>(p);
+  return after_launch("bmm_f32_kernel");
 }

@@ -103,10 +103,20 @@ class PinnedBuffer:
         self.close()
 
 
+class DeviceSlice:
+    """The memory of `parent` from byte `offset` on (keeps the parent allocation alive)."""
+
+    def __init__(self, parent, offset: int):
+        self.parent = parent
+        self.offset = int(offset)
+        self.ptr = int(parent.ptr) + self.offset
+        self.nbytes = parent.nbytes - self.offset
+
+
 def ptr(x) -> C.c_void_p:
-    """A C pointer from a DeviceBuffer, an int address or None."""
+    """A C pointer from a DeviceBuffer, a DeviceSlice, an int address or None."""
     if x is None:
         return C.c_void_p(0)
-    if isinstance(x, (DeviceBuffer, PinnedBuffer)):
+    if isinstance(x, (DeviceBuffer, PinnedBuffer, DeviceSlice)):
         return C.c_void_p(x.ptr)
     return C.c_void_p(int(x))

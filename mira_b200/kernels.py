@@ -209,3 +209,92 @@ def nchw_to_nhwc(x, n, c, h, w, y, ldc) -> None:
 
 def nhwc_to_nchw(x, n, h, w, c, ldc, y) -> None:
     _lib.call("mira_cuda_nhwc_to_nchw_f32", ptr(x), n, h, w, c, ldc, ptr(y))
+
+
+# ----------------------------------------------------------------------------- sequence (transformer) ops
+
+@dataclass
+class View:
+    """A view of at most 4 dimensions for the sequence kernels: buffer `buf` (a DeviceBuffer or
+    DeviceSlice), element `offset` and element `strides` over (batch0, batch1, row, col); broadcast
+    dimensions have stride 0."""
+    buf: object
+    strides: tuple
+    offset: int = 0
+    itemsize: int = 4
+
+    def struct(self) -> _lib.View4:
+        v = _lib.View4()
+        if self.buf is not None:
+            v.ptr = (ptr(self.buf).value or 0) + int(self.offset) * self.itemsize
+        for i, s in enumerate(self.strides):
+            v.stride[i] = int(s)
+        return v
+
+
+@dataclass
+class BmmStep:
+    """One epilogue step of the batched f32 matmul: operand "none", "scalar" or "view"."""
+    op: str
+    operand: str = "none"
+    swapped: bool = False
+    scalar: float = 0.0
+    view: Optional[View] = None
+
+
+_BMM_OPND = {"none": _lib.OPND_NONE, "scalar": _lib.OPND_SCALAR, "view": _lib.OPND_VIEW}
+
+
+@dataclass
+class BmmEpi:
+    steps: Sequence[BmmStep] = field(default_factory=list)
+    out: Optional[View] = None
+    out_i8: Optional[View] = None
+    out_scale: float = 1.0
+
+    def struct(self) -> _lib.BmmEpilogue:
+        e = _lib.BmmEpilogue()
+        if len(self.steps) > _lib.EPI_MAX_STEPS:
+            raise ValueError(f"at most {_lib.EPI_MAX_STEPS} fused epilogue steps")
+        e.n_steps = len(self.steps)
+        for i, s in enumerate(self.steps):
+            code = _lib.UNARY_CODES.get(s.op) or _lib.BINARY_CODES.get(s.op)
+            if code is None:
+                raise ValueError(f"epilogue op {s.op!r} has no device implementation")
+            e.steps[i].op = code
+            e.steps[i].operand = _BMM_OPND[s.operand]
+            e.steps[i].swapped = int(bool(s.swapped))
+            e.steps[i].scalar = float(np.float32(s.scalar))
+            if s.view is not None:
+                e.steps[i].view = s.view.struct()
+        if self.out is not None:
+            e.out_f32 = self.out.struct()
+        if self.out_i8 is not None:
+            e.out_i8 = self.out_i8.struct()
+        e.out_scale = float(np.float32(self.out_scale))
+        return e
+
+
+def bmm_f32(batch0: int, batch1: int, m: int, n: int, k: int, a: View, b: View, epi: BmmEpi) -> None:
+    av, bv, e = a.struct(), b.struct(), epi.struct()
+    _lib.call("mira_cuda_bmm_f32", batch0, batch1, m, n, k, C.byref(av), C.byref(bv), C.byref(e))
+
+
+def layernorm_rows(x, rows: int, d: int, ld_x: int, gamma, beta, eps: float, out_f32=None, ld_f32: int = 0,
+                   out_i8=None, ld_i8: int = 0, out_scale: float = 1.0) -> None:
+    _lib.call("mira_cuda_layernorm_rows", ptr(x), rows, d, ld_x, ptr(gamma), ptr(beta), float(np.float32(eps)),
+              ptr(out_f32), ld_f32, ptr(out_i8), ld_i8, float(np.float32(out_scale)))
+
+
+def softmax_rows(x, rows: int, n: int, ld_x: int, out, ld_out: int) -> None:
+    _lib.call("mira_cuda_softmax_rows", ptr(x), rows, n, ld_x, ptr(out), ld_out)
+
+
+def embed_rows(table, vocab: int, d: int, idx, rows: int, out, ld_out: int, addend=None, addend_rows: int = 0) -> None:
+    _lib.call("mira_cuda_embed_rows", ptr(table), vocab, d, ptr(idx), rows, ptr(addend), addend_rows, ptr(out), ld_out)
+
+
+def copy_view(shape4, src: View, dst: View) -> None:
+    s, d = src.struct(), dst.struct()
+    n0, n1, n2, n3 = (int(x) for x in shape4)
+    _lib.call("mira_cuda_copy_view_f32", n0, n1, n2, n3, C.byref(s), C.byref(d))

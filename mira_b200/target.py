@@ -25,7 +25,7 @@ import numpy as np
 
 from . import _lib
 from . import kernels as K
-from .device import DeviceBuffer, PinnedBuffer, ptr, set_device
+from .device import DeviceBuffer, DeviceSlice, PinnedBuffer, ptr, set_device
 
 QOPS = ("qmatmul", "qconv2d")
 
@@ -60,6 +60,9 @@ class CudaDevice:
 
     def pinned(self, nbytes: int) -> PinnedBuffer:
         return PinnedBuffer(nbytes)
+
+    def offset(self, buf, nbytes: int) -> DeviceSlice:
+        return DeviceSlice(buf, nbytes)
 
     def h2d(self, dst, src: PinnedBuffer, nbytes: int) -> None:
         _lib.call("mira_cuda_h2d", ptr(dst), ptr(src), C.c_size_t(nbytes))
@@ -144,6 +147,28 @@ class CudaDevice:
         elif k == "copy":
             fn = L.mira_cuda_d2d
             args = (ptr(a["dst"]), ptr(a["src"]), C.c_size_t(a["nbytes"]))
+        elif k == "bmm":
+            av, bv, e = a["a"].struct(), a["b"].struct(), a["epi"].struct()
+            keep += [av, bv, e]
+            fn = L.mira_cuda_bmm_f32
+            args = (a["batch0"], a["batch1"], a["m"], a["n"], a["k"], C.byref(av), C.byref(bv), C.byref(e))
+        elif k == "layernorm":
+            fn = L.mira_cuda_layernorm_rows
+            args = (ptr(a["x"]), a["rows"], a["d"], a["ld_x"], ptr(a["gamma"]), ptr(a["beta"]), _f32(a["eps"]),
+                    ptr(a.get("out_f32")), a.get("ld_f32", 0), ptr(a.get("out_i8")), a.get("ld_i8", 0),
+                    _f32(a.get("scale", 1.0)))
+        elif k == "softmax":
+            fn = L.mira_cuda_softmax_rows
+            args = (ptr(a["x"]), a["rows"], a["n"], a["ld_x"], ptr(a["out"]), a["ld_out"])
+        elif k == "embed":
+            fn = L.mira_cuda_embed_rows
+            args = (ptr(a["table"]), a["vocab"], a["d"], ptr(a["idx"]), a["rows"], ptr(a.get("addend")),
+                    a.get("addend_rows", 0), ptr(a["out"]), a["ld_out"])
+        elif k == "copy_view":
+            sv, dv = a["src"].struct(), a["dst"].struct()
+            keep += [sv, dv]
+            fn = L.mira_cuda_copy_view_f32
+            args = tuple(int(x) for x in a["shape"]) + (C.byref(sv), C.byref(dv))
         else:
             raise ValueError(f"unknown launch kind {k!r}")
 
@@ -168,6 +193,22 @@ class DVal:
     i8_ld: int = 0
     i8_layout: str = "nhwc"      # or "row4" (MIRA_LAYOUT_ROW4, graph inputs of at most 4 channels)
     row_entries: int = 0
+    i32: object = None           # int32 graph inputs (token ids)
+    strides: Optional[tuple] = None   # "rows" layout: element strides of the f32 view (None: row-major)
+    offset: int = 0                   # "rows" layout: element offset of the f32 view
+    contig: object = None             # row-major copy of a strided view, made on first need
+
+    @property
+    def f32_strides(self) -> tuple:
+        return self.strides if self.strides is not None else contiguous_strides(self.shape)
+
+    @property
+    def is_contiguous(self) -> bool:
+        if self.offset != 0:
+            return False
+        if self.strides is None:
+            return True
+        return all(d == 1 or s == c for d, s, c in zip(self.shape, self.strides, contiguous_strides(self.shape)))
 
     @property
     def rows(self) -> int:
@@ -187,8 +228,44 @@ class DVal:
         return int(np.prod(self.shape, dtype=np.int64))
 
 
-def _layout_for(shape) -> str:
-    return "nhwc" if len(shape) == 4 else "rows"
+def contiguous_strides(shape) -> tuple:
+    st, acc = [], 1
+    for d in reversed(tuple(shape)):
+        st.append(acc)
+        acc *= int(d)
+    return tuple(reversed(st))
+
+
+def view_strides(old_shape, old_strides, new_shape) -> Optional[tuple]:
+    """Strides that present the elements of a strided view in `new_shape` (row-major element order
+    kept), or None when the reshape needs a copy.  Dimensions are matched chunk by chunk: each run
+    of old dimensions that are contiguous with one another must be covered exactly by a run of new
+    dimensions."""
+    old_shape, old_strides, new_shape = tuple(old_shape), tuple(old_strides), tuple(new_shape)
+    if int(np.prod(new_shape, dtype=np.int64)) == 0 or not old_shape:
+        return contiguous_strides(new_shape)
+    new = [0] * len(new_shape)
+    view_d = len(new_shape) - 1
+    base = old_strides[-1]
+    tensor_numel = view_numel = 1
+    for d in range(len(old_shape) - 1, -1, -1):
+        tensor_numel *= old_shape[d]
+        if d == 0 or (old_shape[d - 1] != 1 and old_strides[d - 1] != tensor_numel * base):
+            while view_d >= 0 and (view_numel < tensor_numel or new_shape[view_d] == 1):
+                new[view_d] = view_numel * base
+                view_numel *= new_shape[view_d]
+                view_d -= 1
+            if view_numel != tensor_numel:
+                return None
+            if d > 0:
+                base = old_strides[d - 1]
+                tensor_numel = view_numel = 1
+    if view_d != -1:
+        return None
+    return tuple(new)
+
+
+IMAGE_OPS = ("qconv2d", "conv2d", "maxpool2d", "pad", "reduce_mean")
 
 
 def _f32(scale) -> float:
@@ -305,8 +382,58 @@ class Plan:
                 for v in op.inputs:
                     need_f32.add(v)
         need_f32.update(g.outputs)
-        self.need_f32 = {v for v in need_f32 if self._const(v) is None}
+        self.need_f32 = {v for v in need_f32 if self._const(v) is None and v.type.dtype == "f32"}
         self.i8_req = i8_req
+        self.image_values = set()
+        for op in g.ops:
+            if op.kind in IMAGE_OPS:
+                for v in list(op.inputs) + list(op.results):
+                    if v.type.rank == 4 and self._const(v) is None:
+                        self.image_values.add(v)
+        self._group_qmatmuls()
+
+    def _group_qmatmuls(self):
+        """Quantized matmuls that read the same int8 activation (same value, same x_scale) and
+        whose epilogues differ only in per-channel constants run as one GEMM over the concatenated
+        weights (the q/k/v projections of attention); their results are column slices of one
+        [M, sum(N)] buffer."""
+        self.qgroup: dict = {}       # first op of a group -> all ops of the group
+        self.qgrouped: set = set()   # later ops of a group (produced by the first)
+        by_key: dict = {}
+        for op in self.g.ops:
+            if op.kind != "qmatmul" or op in self.skipped or op.result in self.g.outputs:
+                continue
+            if op.result in self.i8_req or op.result not in self.need_f32:
+                continue
+            sig = self._epilogue_signature(op)
+            if sig is None:
+                continue
+            key = (op.inputs[0], _f32(op.attrs["x_scale"]), sig)
+            by_key.setdefault(key, []).append(op)
+        for ops in by_key.values():
+            if len(ops) > 1:
+                self.qgroup[ops[0]] = ops
+                self.qgrouped.update(ops[1:])
+
+    def _epilogue_signature(self, op):
+        """Hashable form of an epilogue whose operands are constant scalars or per-column
+        vectors (None for other epilogues)."""
+        n = np.asarray(op.attrs["q"]).shape[1]
+        sig = []
+        for fn, idx, swapped in op.attrs.get("epilogue", ()):
+            if idx is None:
+                sig.append((fn, None, False))
+                continue
+            val = self._const(op.inputs[idx])
+            if val is None:
+                return None
+            if val.size == 1:
+                sig.append((fn, ("scalar", float(np.float32(val.ravel()[0]))), bool(swapped)))
+            elif val.shape[-1] == n and val.size == n:
+                sig.append((fn, "channel", bool(swapped)))
+            else:
+                return None
+        return tuple(sig)
 
     def _conv_pool_fusable(self, conv) -> bool:
         """A qconv2d whose only consumer is a max pool can run inside the pooling kernel when it has
@@ -346,11 +473,15 @@ class Plan:
         for v in self.g.outputs:
             self._output(v)
 
-    def _new_out(self, v, layout: Optional[str] = None) -> DVal:
+    def _layout_of(self, v) -> str:
+        return "nhwc" if v.type.rank == 4 and v in self.image_values else "rows"
+
+    def _new_out(self, v, layout: Optional[str] = None, strides: Optional[tuple] = None) -> DVal:
         shape = tuple(v.type.shape)
-        dv = DVal(shape, layout or _layout_for(shape))
+        dv = DVal(shape, layout or self._layout_of(v))
         if v in self.need_f32:
             dv.f32 = self._alloc(dv.numel * 4)
+            dv.strides = strides
         if v in self.i8_req:
             dv.i8_scale = self.i8_req[v]
             dv.i8_ld = K.round_up(dv.cols, 16)
@@ -358,10 +489,54 @@ class Plan:
         self.vals[v] = dv
         return dv
 
+    # ------------------------------------------------------------------ views
+
+    def _at(self, buf, elem_offset: int, itemsize: int = 4):
+        return buf if not elem_offset else self.dev.offset(buf, int(elem_offset) * itemsize)
+
+    def _contiguous(self, dv: DVal):
+        """A row-major f32 buffer holding the elements of `dv` (a copy for strided views)."""
+        if dv.is_contiguous:
+            return dv.f32
+        if dv.contig is None:
+            shape4, view = self._view4(dv)
+            dv.contig = self._alloc(dv.numel * 4)
+            self._launch("copy_view", shape=shape4, src=view,
+                         dst=K.View(dv.contig, (0,) * (4 - len(dv.shape)) + contiguous_strides(dv.shape)))
+        return dv.contig
+
+    def _view4(self, dv: DVal):
+        shape, st = tuple(dv.shape), dv.f32_strides
+        if len(shape) > 4:
+            raise UnsupportedOnCuda("views of more than 4 dimensions")
+        pad = 4 - len(shape)
+        return (1,) * pad + shape, K.View(dv.f32, (0,) * pad + tuple(st), dv.offset)
+
+    def _rows_of(self, v):
+        """(f32 buffer, row stride) of `v` read as rows [prod(shape[:-1]), shape[-1]]; strided views
+        whose rows are not evenly spaced are copied first."""
+        dv = self.vals[v]
+        if dv.f32 is None:
+            raise UnsupportedOnCuda("value has no f32 representation")
+        if dv.layout != "rows":
+            return dv.f32, dv.cols
+        shape, st = tuple(dv.shape), dv.f32_strides
+        cols = shape[-1] if shape else 1
+        lead = [(d, x) for d, x in zip(shape[:-1], st[:-1]) if d != 1]
+        ok = not shape or cols == 1 or st[-1] == 1
+        ld = lead[-1][1] if lead else cols
+        expect = ld
+        for d, x in reversed(lead):
+            ok = ok and x == expect
+            expect = x * d
+        if ok and ld >= cols:
+            return self._at(dv.f32, dv.offset), ld
+        return self._contiguous(dv), cols
+
     def _from_reference_order(self, v, buf) -> DVal:
         """A DVal for `v` from an f32 buffer in the reference's element order (NCHW / row-major)."""
         shape = tuple(v.type.shape)
-        dv = DVal(shape, _layout_for(shape))
+        dv = DVal(shape, self._layout_of(v))
         if dv.layout == "nhwc":
             n, c, h, w = shape
             if v in self.need_f32:
@@ -437,17 +612,21 @@ class Plan:
             raise UnsupportedOnCuda("int8 operand without an f32 source")
         ld = K.round_up(dv.cols, 16)
         buf = self._alloc(dv.rows * ld, zero=True)
-        self._launch("quantize_rows", x=dv.f32, rows=dv.rows, cols=dv.cols, ld_x=dv.cols, scale=scale, xq=buf, ld_q=ld)
+        src, ld_x = self._rows_of(v)
+        self._launch("quantize_rows", x=src, rows=dv.rows, cols=dv.cols, ld_x=ld_x, scale=scale, xq=buf, ld_q=ld)
         if dv.i8 is None:
             dv.i8, dv.i8_scale, dv.i8_ld = buf, scale, ld
         return buf, ld
 
     def _input(self, v) -> None:
-        if v.type.dtype != "f32":
-            raise UnsupportedOnCuda(f"input {v!r} is {v.type.dtype}; the cuda target takes f32 inputs")
+        if v.type.dtype not in ("f32", "i32"):
+            raise UnsupportedOnCuda(f"input {v!r} is {v.type.dtype}; the cuda target takes f32 and i32 inputs")
         nbytes = v.type.numel * 4
         raw = self._alloc(nbytes)
         self.inputs.append((v, raw, nbytes))
+        if v.type.dtype == "i32":
+            self.vals[v] = DVal(tuple(v.type.shape), "rows", i32=raw)
+            return
         self._from_reference_order(v, raw)
 
     def _output(self, v) -> None:
@@ -461,6 +640,8 @@ class Plan:
             n, ch, h, w = dv.shape
             buf = self._alloc(nbytes)
             self._launch("nhwc_to_nchw", x=dv.f32, n=n, h=h, w=w, c=ch, ldc=ch, y=buf)
+        elif dv.layout == "rows":
+            buf = self._contiguous(dv)
         else:
             buf = dv.f32
         self.outputs.append((v, buf, nbytes))
@@ -494,10 +675,11 @@ class Plan:
         if dv.f32 is None:
             raise UnsupportedOnCuda("epilogue operand has no f32 representation")
         if tuple(dv.shape) == tuple(oshape) and dv.layout == out.layout:
-            return K.Step(fn, "full", swapped, ptr=dv.f32, ld=dv.cols)
+            src, ld = self._rows_of(v)
+            return K.Step(fn, "full", swapped, ptr=src, ld=ld)
         if self._is_channel(dv.shape, out):
             padded = self._alloc(K.round_up(max(out.cols, 1), K.CHANNEL_PAD) * 4, zero=True)
-            self._launch("copy", dst=padded, src=dv.f32, nbytes=out.cols * 4)
+            self._launch("copy", dst=padded, src=self._contiguous(dv), nbytes=out.cols * 4)
             return K.Step(fn, "channel", swapped, ptr=padded)
         raise UnsupportedOnCuda(f"runtime epilogue operand of shape {list(dv.shape)} against {list(oshape)}")
 
@@ -518,10 +700,15 @@ class Plan:
         return self._upload(s64), self._upload(hi), self._upload(lo)
 
     def _op_qmatmul(self, op) -> None:
+        if op in self.qgrouped:
+            return
         a = op.attrs
         x = self.vals[op.inputs[0]]
         if x.layout != "rows":
             raise UnsupportedOnCuda("qmatmul on a 4-D input")
+        if op in self.qgroup:
+            self._qmatmul_group(self.qgroup[op])
+            return
         q = np.asarray(a["q"])
         kdim, n = q.shape
         A, lda = self._i8_of(op.inputs[0], _f32(a["x_scale"]))
@@ -529,6 +716,40 @@ class Plan:
         out = self._new_out(op.result)
         self._launch("qgemm", M=x.rows, N=n, K=kdim, A=A, lda=lda, B=wq, ldb=K.round_up(kdim, 16),
                      dq=self._scales(a["x_scale"], a["w_scale"]), epi=self._epilogue(op, out))
+
+    def _qmatmul_group(self, ops) -> None:
+        """One GEMM for quantized matmuls sharing their int8 input: weights, scales and per-column
+        epilogue constants concatenated along N; every result is a column slice of the output."""
+        first = ops[0]
+        x = self.vals[first.inputs[0]]
+        qs = [np.asarray(op.attrs["q"]) for op in ops]
+        kdim = qs[0].shape[0]
+        widths = [q.shape[1] for q in qs]
+        total = int(sum(widths))
+        A, lda = self._i8_of(first.inputs[0], _f32(first.attrs["x_scale"]))
+        wq = self._upload(K.matmul_weight(np.concatenate(qs, axis=1)))
+        w_scale = np.concatenate([np.asarray(op.attrs["w_scale"], np.float32) for op in ops])
+        buf = self._alloc(x.rows * total * 4)
+        steps = []
+        for i, (fn, idx, swapped) in enumerate(first.attrs.get("epilogue", ())):
+            if idx is None:
+                steps.append(K.Step(fn))
+                continue
+            val = self._const(first.inputs[idx]).astype(np.float32)
+            if val.size == 1:
+                steps.append(K.Step(fn, "scalar", bool(swapped), scalar=float(val.ravel()[0])))
+                continue
+            cols = [self._const(op.inputs[op.attrs["epilogue"][i][1]]).astype(np.float32).ravel() for op in ops]
+            steps.append(K.Step(fn, "channel", bool(swapped), ptr=self._upload(K.pad_channels(np.concatenate(cols)))))
+        epi = K.Epi(steps, out_f32=buf, ld_f32=total)
+        self._launch("qgemm", M=x.rows, N=total, K=kdim, A=A, lda=lda, B=wq, ldb=K.round_up(kdim, 16),
+                     dq=self._scales(first.attrs["x_scale"], w_scale), epi=epi)
+        col = 0
+        for op, w in zip(ops, widths):
+            shape = tuple(op.result.type.shape)
+            st = tuple(c * total for c in contiguous_strides(shape[:-1])) + (1,)
+            self.vals[op.result] = DVal(shape, "rows", f32=buf, strides=st, offset=col)
+            col += w
 
     def _op_qconv2d(self, op) -> None:
         a = op.attrs
@@ -612,15 +833,177 @@ class Plan:
         self._launch("mean_hw", x=x.f32, n=n, hw=h * w, c=c, ldc=c, out_f32=out.f32, out_i8=out.i8, ld_i8=out.i8_ld,
                      scale=out.i8_scale or 1.0)
 
+    def _reference_order(self, dv: DVal):
+        """An f32 buffer with the elements of `dv` in the reference's row-major order."""
+        if dv.layout == "nhwc" and dv.shape[2] * dv.shape[3] > 1:
+            n, c, h, w = dv.shape
+            buf = self._alloc(dv.numel * 4)
+            self._launch("nhwc_to_nchw", x=dv.f32, n=n, h=h, w=w, c=c, ldc=c, y=buf)
+            return buf
+        if dv.layout == "nhwc":
+            return dv.f32
+        return self._contiguous(dv)
+
     def _op_reshape(self, op) -> None:
         x = self.vals[op.inputs[0]]
-        if x.layout == "nhwc" and x.shape[2] * x.shape[3] > 1:
-            n, c, h, w = x.shape
-            buf = self._alloc(x.numel * 4)
-            self._launch("nhwc_to_nchw", x=x.f32, n=n, h=h, w=w, c=c, ldc=c, y=buf)
+        shape = tuple(op.result.type.shape)
+        if x.layout == "rows" and self._layout_of(op.result) == "rows" and x.f32 is not None:
+            st = view_strides(x.shape, x.f32_strides, shape)
+            if st is not None:
+                dv = DVal(shape, "rows", f32=x.f32, strides=st, offset=x.offset)
+                self.vals[op.result] = dv
+                if op.result in self.i8_req:
+                    self._i8_of(op.result, self.i8_req[op.result])
+                return
+        self._from_reference_order(op.result, self._reference_order(x))
+
+    def _op_transpose(self, op) -> None:
+        """A strided view: the reference's np.transpose (ops.py:375) moves no data here; a consumer
+        that needs row-major data copies it (copy_view)."""
+        x = self.vals[op.inputs[0]]
+        perm = tuple(int(p) % max(len(x.shape), 1) for p in op.attrs["perm"])
+        if x.layout != "rows":
+            base = DVal(tuple(x.shape), "rows", f32=self._reference_order(x))
         else:
-            buf = x.f32
-        self._from_reference_order(op.result, buf)
+            base = x
+        st = base.f32_strides
+        dv = DVal(tuple(base.shape[p] for p in perm), "rows", f32=base.f32, strides=tuple(st[p] for p in perm),
+                  offset=base.offset)
+        self.vals[op.result] = dv
+        if op.result in self.i8_req:
+            self._i8_of(op.result, self.i8_req[op.result])
+
+    # ------------------------------------------------------------------ sequence (transformer) ops
+
+    def _f32_dval(self, v) -> DVal:
+        c = self._const(v)
+        if c is not None:
+            c = np.ascontiguousarray(c.astype(np.float32))
+            return DVal(tuple(c.shape), "rows", f32=self._upload(c))
+        return self.vals[v]
+
+    @staticmethod
+    def _broadcast_view(dv: DVal, out_shape) -> K.View:
+        """`dv` broadcast against `out_shape` (rank <= 4) as a 4-D view; size-1 dims get stride 0."""
+        r = len(out_shape)
+        shape = (1,) * (r - len(dv.shape)) + tuple(dv.shape)
+        st = (0,) * (r - len(dv.shape)) + tuple(dv.f32_strides)
+        st = tuple(0 if d == 1 else x for d, x in zip(shape, st))
+        return K.View(dv.f32, (0,) * (4 - r) + st, dv.offset)
+
+    def _op_matmul(self, op) -> None:
+        """f32 matmul with its fused epilogue (reference ops.py:217-219) on strided views: the
+        attention products q @ k^T and p @ v read the q/k/v projections where they lie."""
+        xa, wb = self._f32_dval(op.inputs[0]), self._f32_dval(op.inputs[1])
+        oshape = tuple(op.result.type.shape)
+        if len(oshape) > 4 or len(xa.shape) > 4 or len(wb.shape) > 4:
+            raise UnsupportedOnCuda("matmul of more than 4 dimensions")
+        m, kdim = xa.shape[-2:]
+        n = wb.shape[-1]
+        users = self.users.get(op.result, [])
+        strides = None
+        if len(users) == 1 and users[0].kind == "transpose" and op.result not in self.g.outputs:
+            # lay the result out so that its transpose is row-major
+            perm = tuple(int(p) % len(oshape) for p in users[0].attrs["perm"])
+            tst = contiguous_strides(tuple(oshape[p] for p in perm))
+            inv = [0] * len(oshape)
+            for i, p in enumerate(perm):
+                inv[p] = tst[i]
+            strides = tuple(inv)
+        out = self._new_out(op.result, strides=strides)
+        batch = (1,) * (4 - len(oshape)) + oshape[:-2]
+        steps = []
+        for fn, idx, swapped in op.attrs.get("epilogue", ()):
+            if idx is None:
+                steps.append(K.BmmStep(fn))
+                continue
+            val = self._const(op.inputs[idx])
+            if val is not None and val.size == 1:
+                steps.append(K.BmmStep(fn, "scalar", bool(swapped), scalar=float(np.float32(val.ravel()[0]))))
+                continue
+            ov = self._f32_dval(op.inputs[idx])
+            steps.append(K.BmmStep(fn, "view", bool(swapped), view=self._broadcast_view(ov, oshape)))
+        out_view = None
+        if out.f32 is not None:
+            out_view = self._broadcast_view(out, oshape)
+        out_i8 = None
+        if out.i8 is not None:
+            ist = tuple(c * out.i8_ld for c in contiguous_strides(oshape[:-1])) + (1,)
+            out_i8 = K.View(out.i8, (0,) * (4 - len(oshape)) + ist, itemsize=1)
+        self._launch("bmm", batch0=batch[0], batch1=batch[1], m=m, n=n, k=kdim,
+                     a=self._broadcast_view(xa, oshape[:-2] + (m, kdim)),
+                     b=self._broadcast_view(wb, oshape[:-2] + (kdim, n)),
+                     epi=K.BmmEpi(steps, out=out_view, out_i8=out_i8,
+                                  out_scale=out.i8_scale if out.i8 is not None else 1.0))
+
+    def _op_softmax(self, op) -> None:
+        x = self.vals[op.inputs[0]]
+        src, ld = self._rows_of(op.inputs[0])
+        out = self._new_out(op.result)
+        if out.f32 is None:
+            out.f32 = self._alloc(out.numel * 4)
+        self._launch("softmax", x=src, rows=x.rows, n=x.cols, ld_x=ld, out=out.f32, ld_out=out.cols)
+        self._fill_i8(op.result)
+
+    def _op_layernorm(self, op) -> None:
+        x = self.vals[op.inputs[0]]
+        src, ld = self._rows_of(op.inputs[0])
+        g, b = (self._const(v) for v in op.inputs[1:3])
+        if g is None or b is None:
+            raise UnsupportedOnCuda("layernorm with runtime gamma/beta")
+        out = self._new_out(op.result)
+        self._launch("layernorm", x=src, rows=x.rows, d=x.cols, ld_x=ld, gamma=self._upload(g.astype(np.float32)),
+                     beta=self._upload(b.astype(np.float32)), eps=op.attrs.get("eps", 1e-5), out_f32=out.f32,
+                     ld_f32=out.cols, out_i8=out.i8, ld_i8=out.i8_ld, scale=out.i8_scale or 1.0)
+
+    def _op_gather(self, op) -> None:
+        """Embedding lookup (reference ops.py:482-487) of int32 token ids, with a following add of
+        a constant table that repeats along the rows (learned positions) done in the same pass."""
+        table = self._const(op.inputs[0]).astype(np.float32)
+        idx = self.vals[op.inputs[1]]
+        vocab, d = table.shape
+        rows = int(np.prod(op.inputs[1].type.shape, dtype=np.int64))
+        add = self._embed_addend(op)
+        target = op.result
+        addend, period = None, 0
+        if add is not None:
+            add_op, val = add
+            self.skipped.add(add_op)
+            target = add_op.result
+            period = val.size // d
+            addend = self._upload(np.ascontiguousarray(val.reshape(period, d), np.float32))
+        out = self._new_out(target)
+        if out.f32 is None:
+            out.f32 = self._alloc(out.numel * 4)
+        self._launch("embed", table=self._upload(table), vocab=vocab, d=d, idx=idx.i32, rows=rows, out=out.f32,
+                     ld_out=d, addend=addend, addend_rows=period)
+        self._fill_i8(target)
+
+    def _embed_addend(self, op):
+        """(add op, constant) when the gather's only consumer adds a constant whose shape is a
+        suffix of the gathered shape (so it repeats with a period of whole rows)."""
+        uses = self.users.get(op.result, [])
+        if len(uses) != 1 or uses[0].kind != "add" or op.result in self.g.outputs:
+            return None
+        add = uses[0]
+        other = add.inputs[1] if add.inputs[0] is op.result else add.inputs[0]
+        val = self._const(other)
+        rshape = tuple(op.result.type.shape)
+        if val is None or other is op.result or tuple(add.result.type.shape) != rshape:
+            return None
+        vshape = tuple(val.shape)
+        while vshape and vshape[0] == 1:
+            vshape = vshape[1:]
+        if not vshape or vshape[-1] != rshape[-1] or rshape[len(rshape) - len(vshape):] != vshape:
+            return None
+        return add, val.astype(np.float32)
+
+    def _fill_i8(self, v) -> None:
+        dv = self.vals[v]
+        if dv.i8 is not None:
+            src, ld = self._rows_of(v)
+            self._launch("quantize_rows", x=src, rows=dv.rows, cols=dv.cols, ld_x=ld, scale=dv.i8_scale, xq=dv.i8,
+                         ld_q=dv.i8_ld)
 
 
 def supported_reason(op) -> Optional[str]:
@@ -630,6 +1013,13 @@ def supported_reason(op) -> Optional[str]:
         return None
     if op.is_control:
         return "control flow runs on the host"
+    if k == "gather":
+        table, idx = op.inputs[:2]
+        tp = table.producer
+        if (tp is None or not tp.is_constant_like or table.type.rank != 2 or table.type.dtype != "f32"
+                or idx.type.dtype != "i32" or op.attrs.get("axis", 0) not in (0, -2)):
+            return "gather: the cuda target looks up rows of a constant f32 table by int32 ids"
+        return None
     rank4 = op.inputs and op.inputs[0].type.rank == 4
     if any(v.type.dtype != "f32" for v in op.inputs) or op.result.type.dtype != "f32":
         return f"{k}: the cuda target computes in f32 (got {op.result.type.dtype})"
@@ -639,6 +1029,28 @@ def supported_reason(op) -> Optional[str]:
         return None
     if k == "reduce_mean" and rank4 and sorted(a % 4 for a in op.attrs["axes"]) == [2, 3]:
         return None
+    if k in ("reshape", "transpose"):
+        return None if op.result.type.rank <= 4 or k == "reshape" else f"{k}: at most 4 dimensions"
+    if k in ("layernorm", "softmax"):
+        x = op.inputs[0].type
+        if k == "softmax" and x.rank and op.attrs.get("axis", -1) % x.rank != x.rank - 1:
+            return "softmax: only over the last axis on cuda"
+        if k == "layernorm" and any(v.producer is None or not v.producer.is_constant_like for v in op.inputs[1:3]):
+            return "layernorm: gamma and beta must be constants on cuda"
+        if not x.rank or x.shape[-1] > _lib.ROW_MAX:
+            return f"{k}: rows of at most {_lib.ROW_MAX} elements on cuda"
+        return None
+    if k == "matmul":
+        if max(v.type.rank for v in op.inputs) > 4 or op.result.type.rank > 4:
+            return "matmul: at most 4 dimensions on cuda"
+        return None
+    if k == "add" and len(op.inputs) == 2:
+        a, b = op.inputs
+        for g_in, other in ((a, b), (b, a)):
+            if (g_in.producer is not None and g_in.producer.kind == "gather" and other.producer is not None
+                    and other.producer.is_constant_like):
+                return None
+        return "add: a standalone elementwise add runs on cuda only after an embedding gather"
     if k == "reshape":
         return None
     if k == "conv2d" and rank4:
@@ -672,7 +1084,7 @@ class CudaExecutable:
 
     # the pinned staging arrays: feeding these exact arrays skips a host copy
     def input_array(self, v) -> np.ndarray:
-        return self.pin_in[v].view(tuple(v.type.shape), np.float32)
+        return self.pin_in[v].view(tuple(v.type.shape), v.type.np_dtype)
 
     def _launch_all(self) -> None:
         if self.use_graph and self._runs >= 1:
@@ -706,7 +1118,7 @@ class CudaExecutable:
             view = self.input_array(v)
             arr = feeds[v]
             if not (isinstance(arr, np.ndarray) and arr.ctypes.data == view.ctypes.data):
-                np.copyto(view, np.asarray(arr, np.float32).reshape(view.shape))
+                np.copyto(view, np.asarray(arr, view.dtype).reshape(view.shape))
             self.device.h2d(raw, self.pin_in[v], nbytes)
         self._launch_all()
         for v, buf, nbytes in self.plan.outputs:

@@ -227,3 +227,64 @@ def mean_hw(x: np.ndarray) -> np.ndarray:
         for j in range(c):
             out[i, j] = np.float32(pairwise_sum_f32(flat[i, j]) / cnt)
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# f32 sequence ops of the transformer (reference ops.py:217-219, 310-313, 356-360, 482-487).
+# These restate the reference's NumPy expressions operation by operation; np.exp / np.tanh and
+# the BLAS matmul are NumPy's own, so the device kernels agree with these to f32 rounding while
+# layernorm (pairwise sums, IEEE divide and sqrt) agrees bit for bit.
+
+
+def layernorm(x: np.ndarray, gamma: np.ndarray, beta: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """Reference _layernorm_ref, ops.py:356-360."""
+    x, g, b = (np.asarray(v, np.float32) for v in (x, gamma, beta))
+    mu = x.mean(axis=-1, keepdims=True)
+    var = ((x - mu) ** 2).mean(axis=-1, keepdims=True)
+    return ((x - mu) / np.sqrt(var + eps) * g + b).astype(np.float32)
+
+
+def layernorm_rows_explicit(x: np.ndarray, gamma: np.ndarray, beta: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """layernorm written with pairwise_sum_f32 row by row (the device kernel's order); tests
+    check it equals `layernorm` bit for bit."""
+    x = np.asarray(x, np.float32)
+    rows = x.reshape(-1, x.shape[-1])
+    out = np.empty_like(rows)
+    d = np.float32(rows.shape[1])
+    e = np.float32(eps)
+    for r in range(rows.shape[0]):
+        mu = np.float32(pairwise_sum_f32(rows[r]) / d)
+        t = (rows[r] - mu).astype(np.float32)
+        var = np.float32(pairwise_sum_f32((t * t).astype(np.float32)) / d)
+        sd = np.sqrt(np.float32(var + e))
+        out[r] = (t / sd * np.asarray(gamma, np.float32) + np.asarray(beta, np.float32)).astype(np.float32)
+    return out.reshape(x.shape)
+
+
+def softmax(x: np.ndarray, axis: int = -1) -> np.ndarray:
+    """Reference _softmax_ref, ops.py:310-313."""
+    x = np.asarray(x, np.float32)
+    e = np.exp(x - x.max(axis=axis, keepdims=True))
+    return (e / e.sum(axis=axis, keepdims=True)).astype(np.float32)
+
+
+def matmul_f32(x: np.ndarray, w: np.ndarray, steps=(), operands=()) -> np.ndarray:
+    """Reference _matmul_ref, ops.py:217-219: np.matmul of f32 operands, then the epilogue."""
+    acc = np.matmul(np.asarray(x, np.float32), np.asarray(w, np.float32))
+    return epilogue(acc, list(operands), steps).astype(np.float32)
+
+
+def matmul_error_bound(x: np.ndarray, w: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """(exact float64 product, K * 2^-23 * |x| @ |w|): any f32 accumulation order of the K
+    products lies within the bound of the exact value (standard dot-product error analysis)."""
+    x64, w64 = np.asarray(x, np.float64), np.asarray(w, np.float64)
+    k = x64.shape[-1]
+    return np.matmul(x64, w64), (k + 2) * 2.0 ** -23 * np.matmul(np.abs(x64), np.abs(w64))
+
+
+def embed(table: np.ndarray, idx: np.ndarray, addend=None) -> np.ndarray:
+    """Reference _gather_ref, ops.py:482-487 (np.take on axis 0), then an optional f32 add."""
+    out = np.take(np.asarray(table, np.float32), np.asarray(idx), axis=0)
+    if addend is not None:
+        out = (out + np.asarray(addend, np.float32)).astype(np.float32)
+    return out

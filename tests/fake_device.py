@@ -22,6 +22,22 @@ class FakeBuf:
         return self.data[: n * np.dtype(dtype).itemsize].view(dtype).reshape(shape)
 
 
+class FakeSlice(FakeBuf):
+    """The bytes of a FakeBuf from an offset on (shares the parent's memory)."""
+
+    def __init__(self, parent, offset: int):
+        self.data = parent.data[int(offset):]
+        self.nbytes = parent.nbytes - int(offset)
+
+
+def _strided(view, shape4, dtype=np.float32):
+    """NumPy array over a kernels.View (element offset and strides) of a FakeBuf."""
+    item = np.dtype(dtype).itemsize
+    base = view.buf.data[int(view.offset) * item:].view(dtype)
+    return np.lib.stride_tricks.as_strided(base, tuple(int(d) for d in shape4),
+                                           tuple(int(s) * item for s in view.strides))
+
+
 class FakePinned(FakeBuf):
     def view(self, shape, dtype):  # PinnedBuffer's argument order
         return super().view(dtype, shape)
@@ -48,6 +64,9 @@ class FakeDevice:
 
     def pinned(self, nbytes):
         return FakePinned(nbytes)
+
+    def offset(self, buf, nbytes):
+        return FakeSlice(buf, nbytes)
 
     def h2d(self, dst, src, nbytes):
         dst.data[:nbytes] = src.data[:nbytes]
@@ -189,3 +208,41 @@ class FakeDevice:
         y = ref.dwconv2d(xn, wk, stride, padding, dilation)
         oh, ow = y.shape[2:]
         self._epi(y.transpose(0, 2, 3, 1).reshape(-1, c), epi, n * oh * ow, c)
+
+    # ------------------------------------------------------------------ sequence ops
+
+    def _bmm(self, batch0, batch1, m, n, k, a, b, epi):
+        av = _strided(a, (batch0, batch1, m, k))
+        bv = _strided(b, (batch0, batch1, k, n))
+        y = np.matmul(av.astype(np.float32), bv.astype(np.float32))
+        for st in epi.steps:
+            if st.operand == "none":
+                y = ref.UNARY[st.op](y).astype(np.float32)
+                continue
+            o = np.float32(st.scalar) if st.operand == "scalar" else _strided(st.view, (batch0, batch1, m, n))
+            y = (ref.BINARY[st.op](o, y) if st.swapped else ref.BINARY[st.op](y, o)).astype(np.float32)
+        if epi.out is not None:
+            _strided(epi.out, (batch0, batch1, m, n))[...] = y
+        if epi.out_i8 is not None:
+            _strided(epi.out_i8, (batch0, batch1, m, n), np.int8)[...] = ref.quantize_activation(y, epi.out_scale)
+
+    def _layernorm(self, x, rows, d, ld_x, gamma, beta, eps, out_f32=None, ld_f32=0, out_i8=None, ld_i8=0, scale=1.0):
+        xv = x.view(np.float32, (rows, ld_x))[:, :d]
+        y = ref.layernorm(xv, gamma.view(np.float32, (d,)), beta.view(np.float32, (d,)), eps)
+        if out_f32 is not None:
+            out_f32.view(np.float32, (rows, ld_f32))[:, :d] = y
+        if out_i8 is not None:
+            out_i8.view(np.int8, (rows, ld_i8))[:, :d] = ref.quantize_activation(y, scale)
+
+    def _softmax(self, x, rows, n, ld_x, out, ld_out):
+        out.view(np.float32, (rows, ld_out))[:, :n] = ref.softmax(x.view(np.float32, (rows, ld_x))[:, :n])
+
+    def _embed(self, table, vocab, d, idx, rows, out, ld_out, addend=None, addend_rows=0):
+        ids = idx.view(np.int32, (rows,))
+        add = None
+        if addend is not None:
+            add = np.tile(addend.view(np.float32, (addend_rows, d)), (rows // addend_rows, 1))
+        out.view(np.float32, (rows, ld_out))[:, :d] = ref.embed(table.view(np.float32, (vocab, d)), ids, add)
+
+    def _copy_view(self, shape, src, dst):
+        _strided(dst, shape)[...] = _strided(src, shape)

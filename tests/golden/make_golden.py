@@ -1,6 +1,7 @@
 """Generates the golden fixtures of tests/golden/ by running the reference itself (myramay/MIRA).
 
     python tests/golden/make_golden.py path/to/reference      (or set $MIRA_PATH)
+    python tests/golden/make_golden.py path/to/reference --only-sequence   (sequence.npz alone)
 
 The reference (a pure-Python package) is imported from the given checkout.  Every expected value comes from the
 reference's own code: mira.ops.evaluate for single ops (ops.py:602-634 quantized ops, 192-199
@@ -184,10 +185,55 @@ def main(ref_path: str) -> None:
                       f"{name}_batch": np.int64(batch), f"{name}_n_calib": np.int64(n_cal)})
         progs[f"{name}_image"] = np.int64(kw.get("image", 0))
     _save("programs", **progs)
+    sequence(ref_path)
+
+
+TINY_TRANSFORMER = dict(seq=16, layers=2, d_model=64, heads=4, d_mlp=128, vocab=32, max_seq=16)
+
+
+def sequence(ref_path: str) -> None:
+    """sequence.npz: the f32 ops of the transformer path through mira.ops.evaluate (layernorm
+    ops.py:356-360, softmax 310-313, matmul with epilogue 217-219, gather 482-487) and a small
+    W8A8 transformer program on the reference cpu target."""
+    mira, compiler, ir, O, Q = _import_reference(ref_path)
+    rng = np.random.default_rng(20261202)
+    out = {}
+    for d in (768, 100, 5):
+        x = (rng.standard_normal((6, d)) * rng.uniform(0.1, 5, (6, 1)) + rng.normal(0, 2, (6, 1))).astype(np.float32)
+        g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+        b = (0.1 * rng.standard_normal(d)).astype(np.float32)
+        out.update({f"ln{d}_x": x, f"ln{d}_g": g, f"ln{d}_b": b,
+                    f"ln{d}_y": O.evaluate("layernorm", [x, g, b], {"eps": 1e-5})})
+    s = (rng.standard_normal((6, 1024)) * 3).astype(np.float32)
+    s[:, 700:] -= np.float32(10000)
+    out.update({"sm_x": s, "sm_y": O.evaluate("softmax", [s], {"axis": -1})})
+    q = rng.standard_normal((2, 3, 16, 8)).astype(np.float32)
+    kt = rng.standard_normal((2, 3, 8, 16)).astype(np.float32)
+    mask = np.where(np.arange(16)[:, None] >= np.arange(16)[None, :], 0.0, -10000.0).astype(np.float32)
+    out.update({"mm_a": q, "mm_b": kt, "mm_mask": mask,
+                "mm_y": O.evaluate("matmul", [q, kt, np.float32(0.125), mask],
+                                   {"epilogue": (("mul", 2, False), ("add", 3, False))})})
+    table = rng.standard_normal((32, 16)).astype(np.float32)
+    idx = rng.integers(-32, 32, (2, 5)).astype(np.int32)
+    out.update({"ga_table": table, "ga_idx": idx, "ga_y": O.evaluate("gather", [table, idx], {"axis": 0})})
+
+    sys.path.insert(0, str(ROOT))
+    from mira_b200 import configs
+    g = configs.transformer(2, **TINY_TRANSFORMER)
+    cal = [configs.random_inputs(g, 100 + i) for i in range(2)]
+    prog = compiler.compile_ir(g, "cpu", quantize="w8a8", calibration=cal, precision=None)
+    feeds = configs.random_inputs(g, 1)
+    out.update({"tf_tok": feeds["tok"], "tf_out": prog.run(feeds),
+                "tf_x_scales": np.array([op.attrs["x_scale"] for op in prog.graph.ops if op.kind == "qmatmul"])})
+    _save("sequence", **out)
 
 
 if __name__ == "__main__":
-    path = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MIRA_PATH")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    path = args[0] if args else os.environ.get("MIRA_PATH")
     if not path:
-        raise SystemExit("usage: make_golden.py path/to/reference (or set MIRA_PATH)")
-    main(path)
+        raise SystemExit("usage: make_golden.py path/to/reference [--only-sequence] (or set MIRA_PATH)")
+    if "--only-sequence" in sys.argv:
+        sequence(path)
+    else:
+        main(path)

@@ -86,15 +86,18 @@ fn main(img: f32[16, 1, 28, 28],
 
 @needs_mira
 def test_mira_source_cnn_matches_cpu(cuda_device):
-    """A .mira CNN through compile_source: convs, pools, the flatten and the FC on cuda; the softmax
-    on the CPU (no cuda kernel), exactly like the reference's partitioned targets."""
+    """A .mira CNN through compile_source: convs, pools, the flatten, the FC and the final softmax
+    all on cuda.  Everything up to the softmax is exact; the softmax's exp is CUDA's expf against
+    NumPy's float32 exp (neither is correctly rounded), so the probabilities agree to a few ulp."""
     rng = np.random.default_rng(0)
     cal = [{"img": rng.standard_normal((16, 1, 28, 28)).astype(np.float32)} for _ in range(2)]
     cpu = mira.compile_source(CNN_SRC, "cpu", quantize="w8a8", calibration=cal, precision=None)
     cuda = mira.compile_source(CNN_SRC, "cuda", quantize="w8a8", calibration=cal)
     feeds = {"img": rng.standard_normal((16, 1, 28, 28)).astype(np.float32)}
-    np.testing.assert_array_equal(cuda.run(feeds), cpu.run(feeds))
-    assert "cuda" in [s.device for s in cuda.segments]
+    got, want = cuda.run(feeds), cpu.run(feeds)
+    ulps = np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32))
+    assert ulps.max() <= 8, int(ulps.max())
+    assert [s.device for s in cuda.segments] == ["cuda"]
 
 
 @needs_mira

@@ -118,3 +118,26 @@ def test_planted_error_is_caught():
     s, x, q = z["scales"][0], z["x"][0], z["q"][0]
     wrong = np.clip(np.sign(x) * np.floor(np.abs(x / np.float32(s)) + 0.5), -127, 127).astype(np.int8)
     assert not np.array_equal(wrong, q)
+
+
+@pytest.mark.parametrize("d", [1, 5, 8, 64, 100, 768, 1000])
+def test_layernorm_pairwise_restatement_is_numpy(d):
+    """The device layernorm's order (pairwise sums, f32 divide by d, IEEE sqrt) is NumPy's."""
+    rng = np.random.default_rng(d)
+    x = (rng.standard_normal((9, d)) * 3 + 1).astype(np.float32)
+    g, b = rng.standard_normal(d).astype(np.float32), rng.standard_normal(d).astype(np.float32)
+    a, e = ref.layernorm(x, g, b), ref.layernorm_rows_explicit(x, g, b)
+    assert np.array_equal(a.view(np.uint32), e.view(np.uint32))
+
+
+def test_sequence_ops_match_reference_fixtures():
+    """layernorm / gather bit for bit, softmax / f32 matmul to f32 rounding (NumPy's exp and BLAS
+    may differ between CPUs), against outputs of the reference's mira.ops.evaluate."""
+    z = np.load(GOLDEN / "sequence.npz")
+    for d in (768, 100, 5):
+        _same(ref.layernorm(z[f"ln{d}_x"], z[f"ln{d}_g"], z[f"ln{d}_b"]), z[f"ln{d}_y"])
+        _same(ref.layernorm_rows_explicit(z[f"ln{d}_x"], z[f"ln{d}_g"], z[f"ln{d}_b"]), z[f"ln{d}_y"])
+    np.testing.assert_allclose(ref.softmax(z["sm_x"]), z["sm_y"], rtol=1e-6, atol=1e-12)
+    y = ref.matmul_f32(z["mm_a"], z["mm_b"], (("mul", 0, False), ("add", 1, False)), (np.float32(0.125), z["mm_mask"]))
+    np.testing.assert_allclose(y, z["mm_y"], rtol=1e-6, atol=1e-5)
+    _same(ref.embed(z["ga_table"], z["ga_idx"]), z["ga_y"])

@@ -1,5 +1,7 @@
 """The cuda target's planner on the CPU: whole MIRA W8A8 programs compiled for `cuda` and executed
 by the host-side stand-in device must reproduce the reference cpu target bit for bit."""
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -74,20 +76,22 @@ fn main(img: f32[4, 1, 16, 16],
         const k2: f32[16, 8, 3, 3], const c2: f32[16, 1, 1],
         const wf: f32[256, 10],     const bf: f32[10]) -> f32[4, 10] {
   let h = block(block(img, k1, c1), k2, c2)
-  return softmax(flatten(h) @ wf + bf)
+  return TAIL(softmax(flatten(h) @ wf + bf))
 }
 """
 
 
-def test_mira_source_program_with_cpu_fallback_segment():
-    """A .mira program: the flatten (NHWC -> NCHW reorder) and the quantized FC run on cuda, the
-    softmax falls back to the CPU like any op the target does not run (reference partition.py)."""
+@pytest.mark.parametrize("tail, devices", [("", ["cuda"]), ("tanh", ["cuda", "cpu"])])
+def test_mira_source_program_placement(tail, devices):
+    """A .mira program: the flatten (NHWC -> NCHW reorder), the quantized FC and the softmax run on
+    cuda; a standalone tanh falls back to the CPU like any op the target does not run (reference
+    partition.py)."""
+    src = CNN_SRC.replace("TAIL", tail)
     rng = np.random.default_rng(0)
     cal = [{"img": rng.standard_normal((4, 1, 16, 16)).astype(np.float32)} for _ in range(2)]
-    cpu = mira.compile_source(CNN_SRC, "cpu", quantize="w8a8", calibration=cal, precision=None)
-    cuda = mira.compile_source(CNN_SRC, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
-    devices = [s.device for s in cuda.segments]
-    assert "cuda" in devices and devices[-1] == "cpu"
+    cpu = mira.compile_source(src, "cpu", quantize="w8a8", calibration=cal, precision=None)
+    cuda = mira.compile_source(src, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
+    assert [s.device for s in cuda.segments] == devices
     feeds = {"img": rng.standard_normal((4, 1, 16, 16)).astype(np.float32)}
     np.testing.assert_array_equal(cuda.run(feeds), cpu.run(feeds))
 
@@ -135,3 +139,54 @@ def test_plan_matches_stored_reference_outputs(name):
     cal = [configs.random_inputs(g, 100 + i) for i in range(n_cal)]
     prog = compiler.compile_ir(g, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
     np.testing.assert_array_equal(prog.run({"x": z[f"{name}_x"]}), z[f"{name}_out"])
+
+
+TINY_TF = dict(seq=16, layers=2, d_model=64, heads=4, d_mlp=128, vocab=32, max_seq=16)
+
+
+def test_transformer_small_plan_matches_cpu():
+    """Decoder-only transformer prefill: embedding, layernorm, fused q/k/v GEMM, attention on
+    strided views, softmax, GELU MLP, LM head, all in one cuda segment."""
+    cpu, cuda, dev = _pair("transformer", 2, **TINY_TF)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    _check_same(cpu, cuda)
+    counts = {k: dev.launched.count(k) for k in set(dev.launched)}
+    # per layer: one q/k/v GEMM, out-proj, two MLP GEMMs; plus the LM head
+    assert counts["qgemm"] == 4 * 2 + 1
+    assert counts["layernorm"] == 2 * 2 + 1 and counts["embed"] == 1
+    assert counts["bmm"] == 2 * 2 and counts["softmax"] == 2
+
+
+def test_view_strides_match_numpy_views():
+    from mira_b200.target import view_strides
+    rng = np.random.default_rng(0)
+    for _ in range(500):
+        r = int(rng.integers(1, 5))
+        shape = tuple(int(x) for x in rng.integers(1, 5, r))
+        base = np.arange(int(np.prod(shape)) * 3, dtype=np.float64)
+        v = base.reshape(shape + (3,))[..., 0].transpose(rng.permutation(r))
+        n, facs = v.size, []
+        while n > 1:
+            ds = [d for d in range(2, n + 1) if n % d == 0]
+            facs.append(ds[int(rng.integers(0, len(ds)))])
+            n //= facs[-1]
+        new = tuple(facs) or (1,)
+        got = view_strides(v.shape, tuple(s // 8 for s in v.strides), new)
+        if got is None:
+            w = v.view()
+            with pytest.raises(AttributeError):
+                w.shape = new          # NumPy cannot view it either
+            continue
+        w = np.lib.stride_tricks.as_strided(base, new, [g * 8 for g in got])
+        np.testing.assert_array_equal(w, v.reshape(new))
+
+
+def test_transformer_plan_matches_stored_reference_output():
+    """The small transformer against the reference cpu target's stored logits."""
+    z = np.load(Path(__file__).resolve().parent / "golden" / "sequence.npz")
+    g = configs.transformer(2, **TINY_TF)
+    cal = [configs.random_inputs(g, 100 + i) for i in range(2)]
+    prog = compiler.compile_ir(g, "cuda", quantize="w8a8", calibration=cal, executor=FakeDevice())
+    scales = np.array([op.attrs["x_scale"] for op in prog.graph.ops if op.kind == "qmatmul"])
+    np.testing.assert_array_equal(scales, z["tf_x_scales"])
+    np.testing.assert_allclose(prog.run({"tok": z["tf_tok"]}), z["tf_out"], rtol=1e-5, atol=1e-6)
