@@ -286,6 +286,35 @@ int mira_cuda_softmax_rows(const float* x, int64_t rows, int64_t n, int64_t ld_x
 int mira_cuda_embed_rows(const float* table, int64_t vocab, int64_t d, const int32_t* idx, int64_t rows,
                          const float* addend, int64_t addend_rows, float* out, int64_t ld_out);
 
+/* Fused attention, o = softmax((q @ k^T) <scale step> (+ mask), axis=-1) @ v: the reference's
+ * matmul with its fused epilogue (ops.py:217-219, 192-199), softmax (ops.py:310-313) and second
+ * matmul computed in one pass per block of 64 query rows without storing the scores (online
+ * softmax).  q [b0, b1, tq, dh], k [b0, b1, tk, dh] (keys as rows, i.e. the transpose of the
+ * reference's k^T operand), v [b0, b1, tk, dh], mask indexed [b0, b1, q, k].  A key tile whose
+ * mask entries are all <= -200 (tile_max, [ceil(tq/64)][ceil(tk/64)]) is skipped only when
+ * |scale| * ||q_i||_1 * max|k| + tile_max - m_i < -110 for every row (m_i the running row maximum,
+ * kmax from mira_cuda_absmax_f32), i.e. when the reference's exp gives exactly 0 on the whole
+ * tile.  Results agree with the reference to f32 rounding. */
+typedef struct mira_attention {
+  int64_t batch0, batch1, tq, tk, dh;   /* dh <= 128 */
+  mira_view4 q, k, v;
+  int32_t scale_op;         /* 0, MIRA_EPI_MUL or MIRA_EPI_DIV (applied before the mask) */
+  float scale;
+  mira_view4 mask;          /* ptr NULL: no mask */
+  const float* tile_max;    /* NULL: no skipping */
+  const float* kmax;        /* device scalar; NULL: no skipping */
+  const uint8_t* tile_zero; /* [ceil(tq/64)][ceil(tk/64)]: 1 where the mask tile is all +0 (its add
+                               is skipped); may be NULL */
+  mira_view4 out_f32;       /* ptr may be NULL */
+  mira_view4 out_i8;        /* ptr may be NULL: int8 requantized with out_scale */
+  float out_scale;
+} mira_attention;
+
+int mira_cuda_attention_f32(const mira_attention* a);
+
+/* *out = max |x| over a [n0, n1, n2, n3] f32 view (NaN counts as +inf); out is device memory. */
+int mira_cuda_absmax_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* x, float* out);
+
 /* Strided copy of a [n0, n1, n2, n3] f32 view into another view (the device form of the
  * reference's transpose, ops.py:375, when a consumer needs the data in a new order). */
 int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* src,

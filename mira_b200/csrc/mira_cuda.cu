@@ -714,15 +714,18 @@ extern "C" int mira_cuda_nhwc_to_nchw_f32(const float* x, int64_t n, int64_t h, 
 
 namespace mira {
 
-static void pw_leaves_rec(int start, int n, PwLeaves& pw) {
+static int pw_leaves_rec(int start, int n, PwLeaves& pw) {
   if (n <= 128) {
-    pw.start[pw.count++] = start;
-    return;
+    pw.start[pw.count] = start;
+    return pw.count++;
   }
   int n2 = n / 2;
   n2 -= n2 % 8;
-  pw_leaves_rec(start, n2, pw);
-  pw_leaves_rec(start + n2, n - n2, pw);
+  const int a = pw_leaves_rec(start, n2, pw);
+  const int b = pw_leaves_rec(start + n2, n - n2, pw);
+  pw.left[pw.nodes] = static_cast<uint8_t>(a);
+  pw.right[pw.nodes] = static_cast<uint8_t>(b);
+  return PW_MAX_LEAVES + pw.nodes++;
 }
 
 // NumPy's pairwise recursion cut into leaves of at most 128 elements (rows up to MIRA_ROW_MAX
@@ -758,6 +761,13 @@ extern "C" int mira_cuda_layernorm_rows(const float* x, int64_t rows, int64_t d,
   p.out = out_f32; p.ld_out = ld_f32; p.out_i8 = out_i8; p.ld_i8 = ld_i8;
   p.q = make_qscale(out_i8 != nullptr ? out_scale : 1.0f);
   pw_leaves(int(d), p.pw);
+  if (d >= 8 && p.pw.count <= 16) {
+    // leaves of at most 128 elements, 4 per round, chains of at most 16 in registers
+    if (p.pw.count <= 4) layernorm_rows_reg_kernel<1><<<row_grid(dev, rows), ROW_WARPS * 32, 0, dev->stream>>>(p);
+    else if (p.pw.count <= 8) layernorm_rows_reg_kernel<2><<<row_grid(dev, rows), ROW_WARPS * 32, 0, dev->stream>>>(p);
+    else layernorm_rows_reg_kernel<4><<<row_grid(dev, rows), ROW_WARPS * 32, 0, dev->stream>>>(p);
+    return after_launch("layernorm_rows_reg_kernel");
+  }
   layernorm_rows_kernel<<<row_grid(dev, rows), ROW_WARPS * 32, 0, dev->stream>>>(p);
   return after_launch("layernorm_rows_kernel");
 }
@@ -804,7 +814,7 @@ extern "C" int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64
   v.dst = static_cast<float*>(dst->ptr);
   for (int i = 0; i < 4; ++i) { v.ss[i] = src->stride[i]; v.ds[i] = dst->stride[i]; }
   const int threads = 256;
-  copy_view_kernel<<<grid_for(dev, total, threads), threads, 0, dev->stream>>>(v);
+  copy_view_kernel<<<grid_for(dev, (total / (n3 > 0 ? n3 : 1)) * 32, threads), threads, 0, dev->stream>>>(v);
   return after_launch("copy_view_kernel");
 }
 
@@ -847,4 +857,81 @@ extern "C" int mira_cuda_bmm_f32(int64_t batch0, int64_t batch1, int64_t m, int6
   const dim3 grid(unsigned(gx), unsigned(gy), unsigned(batches < 65535 ? batches : 65535));
   bmm_f32_kernel<<<grid, BMM_THREADS, 0, dev->stream>>>(p);
   return after_launch("bmm_f32_kernel");
+}
+
+namespace mira {
+
+template <int DH>
+static int launch_attention(DeviceState* dev, const AttnParams& p, int64_t b0, int64_t b1) {
+  const int smem = static_cast<int>(sizeof(AttnSmem<DH>));
+  static bool configured[64] = {};
+  if (!configured[dev->device & 63]) {
+    MIRA_CUDA_TRY(cudaFuncSetAttribute(attention_f32_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                  "cudaFuncSetAttribute(attention)");
+    configured[dev->device & 63] = true;
+  }
+  const dim3 grid(unsigned((p.tq + ATT_BQ - 1) / ATT_BQ), unsigned(b1), unsigned(b0));
+  attention_f32_kernel<DH><<<grid, ATT_THREADS, smem, dev->stream>>>(p);
+  return after_launch("attention_f32_kernel");
+}
+
+}  // namespace mira
+
+extern "C" int mira_cuda_attention_f32(const mira_attention* a) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(a != nullptr, "null attention descriptor");
+  MIRA_CHECK_ARG(a->batch0 >= 0 && a->batch1 >= 0 && a->tq >= 0 && a->tk > 0 && a->dh > 0 && a->dh <= 128,
+                 "bad attention shape (dh <= 128, at least one key)");
+  MIRA_CHECK_ARG(a->batch0 <= 65535 && a->batch1 <= 65535 && a->tq <= (int64_t(1) << 30) && a->tk <= (int64_t(1) << 30),
+                 "attention batch or sequence too large");
+  MIRA_CHECK_ARG(a->q.ptr != nullptr && a->k.ptr != nullptr && a->v.ptr != nullptr, "null attention operand");
+  MIRA_CHECK_ARG(a->out_f32.ptr != nullptr || a->out_i8.ptr != nullptr, "attention has no output");
+  MIRA_CHECK_ARG(a->scale_op == 0 || a->scale_op == MIRA_EPI_MUL || a->scale_op == MIRA_EPI_DIV, "bad scale step");
+  if (a->out_i8.ptr != nullptr) MIRA_CHECK_ARG(a->out_scale > 0.0f, "requant scale must be positive");
+  if (a->batch0 == 0 || a->batch1 == 0 || a->tq == 0) return MIRA_CUDA_OK;
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.tq = int(a->tq); p.tk = int(a->tk); p.dh = int(a->dh);
+  p.q = static_cast<const float*>(a->q.ptr);
+  p.k = static_cast<const float*>(a->k.ptr);
+  p.v = static_cast<const float*>(a->v.ptr);
+  for (int i = 0; i < 4; ++i) {
+    p.qs[i] = a->q.stride[i]; p.ks[i] = a->k.stride[i]; p.vs[i] = a->v.stride[i];
+    p.ms[i] = a->mask.stride[i]; p.os[i] = a->out_f32.stride[i]; p.is[i] = a->out_i8.stride[i];
+  }
+  const auto aligned16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  p.vec = a->dh % 4 == 0 && a->k.stride[3] == 1 && a->v.stride[3] == 1 && aligned16(a->k.ptr) && aligned16(a->v.ptr);
+  for (int i = 0; i < 3; ++i) p.vec = p.vec && a->k.stride[i] % 4 == 0 && a->v.stride[i] % 4 == 0;
+  p.scale_op = a->scale_op;
+  p.scale = a->scale;
+  const float s_abs = a->scale_op == MIRA_EPI_MUL ? std::fabs(a->scale)
+                      : (a->scale_op == MIRA_EPI_DIV ? 1.0f / std::fabs(a->scale) : 1.0f);
+  p.scale_abs = std::isfinite(s_abs) ? s_abs * 1.0001f : INFINITY;
+  p.mask = static_cast<const float*>(a->mask.ptr);
+  p.tile_max = a->tile_max;
+  p.tile_zero = a->tile_zero;
+  p.kmax = reinterpret_cast<const unsigned int*>(a->kmax);
+  p.out = static_cast<float*>(a->out_f32.ptr);
+  p.out_i8 = static_cast<int8_t*>(a->out_i8.ptr);
+  p.q8 = make_qscale(p.out_i8 != nullptr ? a->out_scale : 1.0f);
+  if (a->dh <= 32) return launch_attention<32>(dev, p, a->batch0, a->batch1);
+  if (a->dh <= 64) return launch_attention<64>(dev, p, a->batch0, a->batch1);
+  return launch_attention<128>(dev, p, a->batch0, a->batch1);
+}
+
+extern "C" int mira_cuda_absmax_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* x, float* out) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n0 >= 0 && n1 >= 0 && n2 >= 0 && n3 >= 0, "bad view shape");
+  MIRA_CHECK_ARG(x != nullptr && x->ptr != nullptr && out != nullptr, "null absmax operand");
+  MIRA_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(float), dev->stream), "cudaMemsetAsync(absmax)");
+  const int64_t total = n0 * n1 * n2 * n3;
+  if (total == 0) return MIRA_CUDA_OK;
+  AbsMaxParams p;
+  p.n[0] = n0; p.n[1] = n1; p.n[2] = n2; p.n[3] = n3;
+  p.x = static_cast<const float*>(x->ptr);
+  for (int i = 0; i < 4; ++i) p.s[i] = x->stride[i];
+  p.out = reinterpret_cast<unsigned int*>(out);
+  const int threads = 256;
+  absmax_view_kernel<<<grid_for(dev, (total / n3) * 32, threads), threads, 0, dev->stream>>>(p);
+  return after_launch("absmax_view_kernel");
 }

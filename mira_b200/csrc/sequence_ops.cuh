@@ -12,29 +12,32 @@
 
 #include "exact_math.cuh"
 #include "memory_bound.cuh"
+#include "ptx_sm100.cuh"
 
 namespace mira {
 
 constexpr int PW_MAX_LEAVES = 128;
 
-// Leaves of NumPy's pairwise recursion for rows of n elements (computed on the host).
+// Leaves of NumPy's pairwise recursion for rows of n elements and the additions that combine
+// them, in post order (computed on the host).  Value ids: leaves 0 .. count-1, the result of
+// addition t is PW_MAX_LEAVES + t.
 struct PwLeaves {
   int n;
   int count;
+  int nodes;
   int start[PW_MAX_LEAVES + 1];
+  uint8_t left[PW_MAX_LEAVES], right[PW_MAX_LEAVES];
 };
 
-__device__ float pw_tree(const float* leaf_sum, int n, int& k) {
-  if (n <= 128) return leaf_sum[k++];
-  int n2 = n / 2;
-  n2 -= n2 % 8;
-  const float a = pw_tree(leaf_sum, n2, k);
-  const float b = pw_tree(leaf_sum, n - n2, k);
-  return __fadd_rn(a, b);
+// Combines the leaf sums in buf[0 .. count) along the recursion (one lane; buf has
+// 2 * PW_MAX_LEAVES floats).
+__device__ __forceinline__ float pw_tree(const PwLeaves& pw, float* buf) {
+  for (int t = 0; t < pw.nodes; ++t) buf[PW_MAX_LEAVES + t] = __fadd_rn(buf[pw.left[t]], buf[pw.right[t]]);
+  return pw.nodes ? buf[PW_MAX_LEAVES + pw.nodes - 1] : buf[0];
 }
 
 // Sum of elem(0) .. elem(n-1) in NumPy's float32 pairwise order; every lane returns the total.
-// leaf_sum: PW_MAX_LEAVES floats of shared memory owned by this warp.
+// leaf_sum: 2 * PW_MAX_LEAVES floats of shared memory owned by this warp.
 template <class F>
 __device__ __forceinline__ float warp_pairwise_sum(const PwLeaves& pw, F elem, float* leaf_sum) {
   const int lane = threadIdx.x & 31;
@@ -66,10 +69,7 @@ __device__ __forceinline__ float warp_pairwise_sum(const PwLeaves& pw, F elem, f
   }
   __syncwarp();
   float total = 0.0f;
-  if (lane == 0) {
-    int k = 0;
-    total = pw_tree(leaf_sum, pw.n, k);
-  }
+  if (lane == 0) total = pw_tree(pw, leaf_sum);
   total = __shfl_sync(0xffffffffu, total, 0);
   __syncwarp();
   return total;
@@ -97,7 +97,7 @@ constexpr int ROW_WARPS = 8;
 // mu = mean(x), var = mean((x - mu)^2), y = (x - mu) / sqrt(var + eps) * gamma + beta, each step
 // one float32 rounding like the reference's NumPy expression.
 __global__ void __launch_bounds__(ROW_WARPS * 32) layernorm_rows_kernel(const LnParams p) {
-  __shared__ float leaf_sum[ROW_WARPS][PW_MAX_LEAVES];
+  __shared__ float leaf_sum[ROW_WARPS][2 * PW_MAX_LEAVES];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float dn = static_cast<float>(p.d);
   for (int64_t row = blockIdx.x * int64_t(ROW_WARPS) + warp; row < p.rows; row += int64_t(gridDim.x) * ROW_WARPS) {
@@ -117,6 +117,98 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) layernorm_rows_kernel(const Ln
   }
 }
 
+// Rows of at most 512 * ROUNDS elements with the row held in registers: lane (leaf 4r + lane/8,
+// chain lane % 8) keeps elements start + chain + 8i of its leaf, so every pairwise chain is
+// lane-local, all loads of a row are issued at once, and the three passes (sum, squared
+// deviations, output) read the row from DRAM once.
+template <int ROUNDS>
+__global__ void __launch_bounds__(ROW_WARPS * 32, ROUNDS == 1 ? 3 : (ROUNDS == 2 ? 2 : 1)) layernorm_rows_reg_kernel(const LnParams p) {
+  __shared__ float leaf_sum[ROW_WARPS][2 * PW_MAX_LEAVES];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7;
+  const float dn = static_cast<float>(p.d);
+  int start[ROUNDS], m8[ROUNDS], m[ROUNDS];
+#pragma unroll
+  for (int r = 0; r < ROUNDS; ++r) {
+    const int leaf = 4 * r + (lane >> 3);
+    const bool live = leaf < p.pw.count;
+    start[r] = live ? p.pw.start[leaf] : 0;
+    m[r] = live ? p.pw.start[leaf + 1] - start[r] : 0;
+    m8[r] = m[r] - m[r] % 8;
+  }
+  for (int64_t row = blockIdx.x * int64_t(ROW_WARPS) + warp; row < p.rows; row += int64_t(gridDim.x) * ROW_WARPS) {
+    const float* __restrict__ xr = p.x + row * p.ld_x;
+    float v[ROUNDS][16];
+#pragma unroll
+    for (int r = 0; r < ROUNDS; ++r)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[r][i] = (j + 8 * i < m8[r]) ? __ldg(xr + start[r] + j + 8 * i) : 0.0f;
+    float mu = 0.0f;
+    // pass 0: sum of x; pass 1: sum of (x - mu)^2
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll
+      for (int r = 0; r < ROUNDS; ++r) {
+        float acc = 0.0f;
+        if (m8[r] > 0) {
+          const float t0 = pass ? __fsub_rn(v[r][0], mu) : v[r][0];
+          acc = pass ? __fmul_rn(t0, t0) : t0;
+#pragma unroll
+          for (int i = 1; i < 16; ++i) {
+            if (j + 8 * i < m8[r]) {
+              const float t = pass ? __fsub_rn(v[r][i], mu) : v[r][i];
+              acc = __fadd_rn(acc, pass ? __fmul_rn(t, t) : t);
+            }
+          }
+        }
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+        if (j == 0 && m[r] > 0) {
+          for (int i = m8[r]; i < m[r]; ++i) {
+            const float t = pass ? __fsub_rn(__ldg(xr + start[r] + i), mu) : __ldg(xr + start[r] + i);
+            acc = __fadd_rn(acc, pass ? __fmul_rn(t, t) : t);
+          }
+          leaf_sum[warp][4 * r + (lane >> 3)] = acc;
+        }
+      }
+      __syncwarp();
+      float total = 0.0f;
+      if (lane == 0) total = pw_tree(p.pw, leaf_sum[warp]);
+      total = __fdiv_rn(__shfl_sync(0xffffffffu, total, 0), dn);
+      __syncwarp();
+      if (pass == 0) {
+        mu = total;
+      } else {
+        const float sd = __fsqrt_rn(__fadd_rn(total, p.eps));
+        const float rsd = __frcp_rn(sd);
+        auto emit = [&](int idx, float x) {
+          // (x - mu) / sd correctly rounded: Markstein's correction of RN(t * RN(1/sd)), exact for
+          // normal quotients (|t| / sd <= sqrt(d) here); tiny and zero t take the IEEE divide
+          const float t = __fsub_rn(x, mu);
+          float qt;
+          if (fabsf(t) >= 0x1p-100f) {
+            const float q0 = __fmul_rn(t, rsd);
+            qt = __fmaf_rn(__fmaf_rn(-q0, sd, t), rsd, q0);
+          } else {
+            qt = __fdiv_rn(t, sd);
+          }
+          const float y = __fadd_rn(__fmul_rn(qt, __ldg(p.gamma + idx)), __ldg(p.beta + idx));
+          if (p.out != nullptr) p.out[row * p.ld_out + idx] = y;
+          if (p.out_i8 != nullptr) p.out_i8[row * p.ld_i8 + idx] = static_cast<int8_t>(quant_byte(y, p.q) & 0xff);
+        };
+#pragma unroll
+        for (int r = 0; r < ROUNDS; ++r) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (j + 8 * i < m8[r]) emit(start[r] + j + 8 * i, v[r][i]);
+          if (j == 0)
+            for (int i = m8[r]; i < m[r]; ++i) emit(start[r] + i, __ldg(xr + start[r] + i));
+        }
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- softmax
 
 struct SoftmaxParams {
@@ -128,7 +220,7 @@ struct SoftmaxParams {
 };
 
 __global__ void __launch_bounds__(ROW_WARPS * 32) softmax_rows_kernel(const SoftmaxParams p) {
-  __shared__ float leaf_sum[ROW_WARPS][PW_MAX_LEAVES];
+  __shared__ float leaf_sum[ROW_WARPS][2 * PW_MAX_LEAVES];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = p.pw.n;
   for (int64_t row = blockIdx.x * int64_t(ROW_WARPS) + warp; row < p.rows; row += int64_t(gridDim.x) * ROW_WARPS) {
@@ -184,18 +276,17 @@ struct View4 {
   int64_t ds[4];
 };
 
+// One warp per innermost row (the index arithmetic of the outer dimensions once per row).
 __global__ void copy_view_kernel(const View4 v) {
-  const int64_t total = v.n[0] * v.n[1] * v.n[2] * v.n[3];
-  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
-    int64_t r = e;
-    const int64_t i3 = r % v.n[3];
-    r /= v.n[3];
-    const int64_t i2 = r % v.n[2];
-    r /= v.n[2];
-    const int64_t i1 = r % v.n[1];
-    const int64_t i0 = r / v.n[1];
-    v.dst[i0 * v.ds[0] + i1 * v.ds[1] + i2 * v.ds[2] + i3 * v.ds[3]] =
-        __ldg(v.src + i0 * v.ss[0] + i1 * v.ss[1] + i2 * v.ss[2] + i3 * v.ss[3]);
+  const int64_t rows = v.n[0] * v.n[1] * v.n[2];
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * int64_t(blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t i2 = row % v.n[2], i01 = row / v.n[2];
+    const int64_t i1 = i01 % v.n[1], i0 = i01 / v.n[1];
+    const float* src = v.src + i0 * v.ss[0] + i1 * v.ss[1] + i2 * v.ss[2];
+    float* dst = v.dst + i0 * v.ds[0] + i1 * v.ds[1] + i2 * v.ds[2];
+    for (int64_t i3 = lane; i3 < v.n[3]; i3 += 32) dst[i3 * v.ds[3]] = __ldg(src + i3 * v.ss[3]);
   }
 }
 
@@ -333,6 +424,316 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_f32_kernel(const BmmParams
     }
   }
   __syncthreads();   // the next batch entry refills the shared tiles
+  }
+}
+
+}  // namespace mira
+
+namespace mira {
+
+// ---------------------------------------------------------------- max |x| over a view
+
+struct AbsMaxParams {
+  int64_t n[4];
+  const float* x;
+  int64_t s[4];
+  unsigned int* out;      // float bits of the maximum (non-negative floats order like integers)
+};
+
+__global__ void absmax_view_kernel(const AbsMaxParams p) {
+  const int64_t rows = p.n[0] * p.n[1] * p.n[2];
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  float m = 0.0f;
+  for (int64_t row = blockIdx.x * int64_t(blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t i2 = row % p.n[2], i01 = row / p.n[2];
+    const int64_t i1 = i01 % p.n[1], i0 = i01 / p.n[1];
+    const float* x = p.x + i0 * p.s[0] + i1 * p.s[1] + i2 * p.s[2];
+    for (int64_t i3 = lane; i3 < p.n[3]; i3 += 32) {
+      float a = fabsf(__ldg(x + i3 * p.s[3]));
+      if (a != a) a = INFINITY;
+      m = fmaxf(m, a);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(p.out, __float_as_uint(m));
+}
+
+// ---------------------------------------------------------------- fused attention (f32)
+//
+// One chain of the reference, o = softmax((q @ k^T) * scale + mask, axis=-1) @ v, per (batch0,
+// batch1) and block of 64 query rows, without materializing the scores: the score tile lives in
+// registers, the softmax runs online (running row maximum and sum, earlier partial outputs
+// rescaled by exp(m_old - m_new)) and the probabilities go through shared memory into p @ v.
+//
+// Skipping key tiles.  A key tile whose mask entries are all strongly negative (tile_max from the
+// host) is left out only when, for every row i of the block,
+//   |scale| * ||q_i||_1 * max|k| + tile_max - m_i < -110,
+// where m_i is the running row maximum: then every score of the tile is below m_i - 110 and the
+// reference's exp(s - max) is exactly 0 for it, so its contribution to the sum and to p @ v is
+// exactly 0 there too.  Tiles that fail the test are processed like the others.
+
+constexpr int ATT_BQ = 64, ATT_BK = 64, ATT_THREADS = 256;
+
+struct AttnParams {
+  int tq, tk, dh;
+  const float* q;
+  int64_t qs[4];
+  const float* k;
+  int64_t ks[4];
+  const float* v;
+  int64_t vs[4];
+  int vec;                  // k and v rows load as 16-byte chunks (cp.async, double-buffered)
+  int scale_op;             // 0, MIRA_EPI_MUL or MIRA_EPI_DIV
+  float scale;
+  float scale_abs;          // an upper bound of |scale| (|1/scale| for DIV)
+  const float* mask;        // added after the scale step; NULL: none
+  int64_t ms[4];
+  const float* tile_max;    // [nqb][nkb] maximum mask value per tile; NULL: no skipping
+  const unsigned int* kmax; // max |k| (float bits); NULL: no skipping
+  const unsigned char* tile_zero;  // [nqb][nkb] 1 where every mask entry of the tile is +0; may be NULL
+  float* out;
+  int64_t os[4];
+  int8_t* out_i8;
+  int64_t is[4];
+  QuantScale q8;
+};
+
+// Row-major tiles with a 4-float pad: a thread reads rows ty + 16u of q and tx + 16v of k as
+// 16-byte vectors along d, which keeps every 8-thread phase of a 128-bit shared load on distinct
+// banks; k and v are double-buffered.
+template <int DH>
+struct AttnSmem {
+  float q[ATT_BQ][DH + 4];
+  float k[2][ATT_BK][DH + 4];
+  float v[2][ATT_BK][DH + 4];
+  float p[ATT_BQ][ATT_BK + 4];
+  float qn1[ATT_BQ];
+};
+
+template <int DH>
+__device__ __forceinline__ void attn_load_kv(const AttnParams& p, AttnSmem<DH>& sm, const float* kp, const float* vp,
+                                             int k0, int buf) {
+  const int tid = threadIdx.x;
+  if (p.vec) {
+    constexpr int CH = DH / 4;    // 16-byte chunks per row
+    for (int e = tid; e < ATT_BK * CH; e += ATT_THREADS) {
+      const int c = e / CH, d = (e - c * CH) * 4;
+      const bool ok = k0 + c < p.tk && d < p.dh;
+      const float* ks = ok ? kp + int64_t(k0 + c) * p.ks[2] + d : kp;
+      const float* vs = ok ? vp + int64_t(k0 + c) * p.vs[2] + d : vp;
+      cp_async_16(static_cast<uint32_t>(__cvta_generic_to_shared(&sm.k[buf][c][d])), ks, ok ? 16u : 0u);
+      cp_async_16(static_cast<uint32_t>(__cvta_generic_to_shared(&sm.v[buf][c][d])), vs, ok ? 16u : 0u);
+    }
+  } else {
+    for (int e = tid; e < ATT_BK * DH; e += ATT_THREADS) {
+      const int c = e / DH, d = e - c * DH;
+      const bool ok = k0 + c < p.tk && d < p.dh;
+      sm.k[buf][c][d] = ok ? __ldg(kp + int64_t(k0 + c) * p.ks[2] + int64_t(d) * p.ks[3]) : 0.0f;
+      sm.v[buf][c][d] = ok ? __ldg(vp + int64_t(k0 + c) * p.vs[2] + int64_t(d) * p.vs[3]) : 0.0f;
+    }
+  }
+}
+
+// One key tile: scores, online-softmax update, probabilities through shared memory, p @ v.
+template <int DH>
+__device__ __forceinline__ void attn_compute(const AttnParams& p, AttnSmem<DH>& sm, const float* mp, int q0, int k0,
+                                             int buf, float (&m)[4], float (&l)[4], float (&o)[4][DH / 16]) {
+  constexpr int CN = DH / 16;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  float s[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) s[u][v] = 0.0f;
+#pragma unroll 4
+  for (int d = 0; d < DH; d += 4) {
+    float4 a[4], b[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = *reinterpret_cast<const float4*>(&sm.q[ty + 16 * u][d]);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) b[v] = *reinterpret_cast<const float4*>(&sm.k[buf][tx + 16 * v][d]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        float t = fmaf(a[u].x, b[v].x, s[u][v]);
+        t = fmaf(a[u].y, b[v].y, t);
+        t = fmaf(a[u].z, b[v].z, t);
+        s[u][v] = fmaf(a[u].w, b[v].w, t);
+      }
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int r = q0 + ty + 16 * u;
+    float rmax = -INFINITY;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int c = k0 + tx + 16 * v;
+      float x = s[u][v];
+      if (p.scale_op == MIRA_EPI_MUL) x = __fmul_rn(x, p.scale);
+      else if (p.scale_op == MIRA_EPI_DIV) x = __fdiv_rn(x, p.scale);
+      if (mp != nullptr && r < p.tq && c < p.tk) x = __fadd_rn(x, __ldg(mp + int64_t(r) * p.ms[2] + int64_t(c) * p.ms[3]));
+      if (c >= p.tk) x = -INFINITY;
+      s[u][v] = x;
+      rmax = fmaxf(rmax, x);
+    }
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+    const float mnew = fmaxf(m[u], rmax);
+    const float corr = (mnew == -INFINITY) ? 1.0f : expf(m[u] - mnew);
+    float rsum = 0.0f;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const float e = (mnew == -INFINITY) ? 0.0f : expf(s[u][v] - mnew);
+      sm.p[ty + 16 * u][tx + 16 * v] = e;
+      rsum += e;
+    }
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, off);
+    l[u] = fmaf(l[u], corr, rsum);
+#pragma unroll
+    for (int c = 0; c < CN; ++c) o[u][c] *= corr;
+    m[u] = mnew;
+  }
+  __syncthreads();
+#pragma unroll 2
+  for (int j = 0; j < ATT_BK; j += 4) {
+    float4 pa[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) pa[u] = *reinterpret_cast<const float4*>(&sm.p[ty + 16 * u][j]);
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      float bv[CN];
+      if constexpr (CN % 4 == 0) {
+#pragma unroll
+        for (int c = 0; c < CN; c += 4) {
+          const float4 t = *reinterpret_cast<const float4*>(&sm.v[buf][j + jj][tx * CN + c]);
+          bv[c] = t.x; bv[c + 1] = t.y; bv[c + 2] = t.z; bv[c + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < CN; ++c) bv[c] = sm.v[buf][j + jj][tx * CN + c];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float pv = jj == 0 ? pa[u].x : (jj == 1 ? pa[u].y : (jj == 2 ? pa[u].z : pa[u].w));
+#pragma unroll
+        for (int c = 0; c < CN; ++c) o[u][c] = fmaf(pv, bv[c], o[u][c]);
+      }
+    }
+  }
+}
+
+template <int DH>
+__global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttnParams p) {
+  extern __shared__ __align__(16) unsigned char att_smem_raw[];
+  AttnSmem<DH>& sm = *reinterpret_cast<AttnSmem<DH>*>(att_smem_raw);
+  constexpr int CN = DH / 16;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int nqb = (p.tq + ATT_BQ - 1) / ATT_BQ, nkb = (p.tk + ATT_BK - 1) / ATT_BK;
+  const int qb = nqb - 1 - static_cast<int>(blockIdx.x);     // the longest rows first
+  const int q0 = qb * ATT_BQ;
+  const int64_t b1 = blockIdx.y, b0 = blockIdx.z;
+  const float* qp = p.q + b0 * p.qs[0] + b1 * p.qs[1];
+  const float* kp = p.k + b0 * p.ks[0] + b1 * p.ks[1];
+  const float* vp = p.v + b0 * p.vs[0] + b1 * p.vs[1];
+  const float* mp = p.mask != nullptr ? p.mask + b0 * p.ms[0] + b1 * p.ms[1] : nullptr;
+  const bool can_skip = p.tile_max != nullptr && p.kmax != nullptr;
+  const float* tmax = can_skip ? p.tile_max + int64_t(qb) * nkb : nullptr;
+  auto candidate = [&](int kb) { return can_skip && __ldg(tmax + kb) <= -200.0f; };
+  auto next_tile = [&](int kb) {
+    while (kb < nkb && candidate(kb)) ++kb;
+    return kb;
+  };
+
+  int cur = next_tile(0);
+  if (cur < nkb) attn_load_kv<DH>(p, sm, kp, vp, cur * ATT_BK, 0);
+  cp_async_commit();
+  for (int e = tid; e < ATT_BQ * DH; e += ATT_THREADS) {
+    const int r = e / DH, d = e - r * DH;
+    sm.q[r][d] = (q0 + r < p.tq && d < p.dh) ? __ldg(qp + int64_t(q0 + r) * p.qs[2] + int64_t(d) * p.qs[3]) : 0.0f;
+  }
+  __syncthreads();
+  {
+    // ||q_i||_1: four threads per row
+    const int r = tid >> 2, part = tid & 3;
+    float a = 0.0f;
+    for (int d = part; d < DH; d += 4) a += fabsf(sm.q[r][d]);
+    a += __shfl_xor_sync(0xffffffffu, a, 1);
+    a += __shfl_xor_sync(0xffffffffu, a, 2);
+    if (part == 0) sm.qn1[r] = a;
+  }
+  float m[4], l[4], o[4][CN];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    m[u] = -INFINITY;
+    l[u] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CN; ++c) o[u][c] = 0.0f;
+  }
+  int buf = 0;
+  while (cur < nkb) {
+    const int nxt = next_tile(cur + 1);
+    if (nxt < nkb) {
+      attn_load_kv<DH>(p, sm, kp, vp, nxt * ATT_BK, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    // a tile whose mask entries are all +0 adds nothing: x + 0 only turns -0 into +0, which
+    // leaves every exp(x - m) unchanged
+    const bool zero_mask = p.tile_zero != nullptr && __ldg(p.tile_zero + int64_t(qb) * nkb + cur) != 0;
+    attn_compute<DH>(p, sm, zero_mask ? nullptr : mp, q0, cur * ATT_BK, buf, m, l, o);
+    __syncthreads();
+    cur = nxt;
+    buf ^= 1;
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  if (can_skip) {
+    const float kmax = __uint_as_float(__ldg(p.kmax));
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (!candidate(kb)) continue;
+      const float tm = __ldg(tmax + kb);
+      bool ok = true;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int r = ty + 16 * u;
+        if (q0 + r < p.tq) {
+          // every score of this tile is at most this bound; the factor 1.001 and the margin
+          // cover the rounding of the products
+          const float bound = p.scale_abs * sm.qn1[r] * kmax * 1.001f + tm;
+          ok = ok && (bound - m[u] < -110.0f);
+        }
+      }
+      if (!__syncthreads_and(ok)) {
+        attn_load_kv<DH>(p, sm, kp, vp, kb * ATT_BK, 0);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        attn_compute<DH>(p, sm, mp, q0, kb * ATT_BK, 0, m, l, o);
+        __syncthreads();
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int r = q0 + ty + 16 * u;
+    if (r >= p.tq) continue;
+#pragma unroll
+    for (int c = 0; c < CN; ++c) {
+      const int col = tx * CN + c;
+      if (col >= p.dh) continue;
+      const float y = __fdiv_rn(o[u][c], l[u]);
+      if (p.out != nullptr) p.out[b0 * p.os[0] + b1 * p.os[1] + int64_t(r) * p.os[2] + int64_t(col) * p.os[3]] = y;
+      if (p.out_i8 != nullptr)
+        p.out_i8[b0 * p.is[0] + b1 * p.is[1] + int64_t(r) * p.is[2] + int64_t(col) * p.is[3]] =
+            static_cast<int8_t>(quant_byte(y, p.q8) & 0xff);
+    }
   }
 }
 

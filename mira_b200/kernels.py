@@ -298,3 +298,92 @@ def copy_view(shape4, src: View, dst: View) -> None:
     s, d = src.struct(), dst.struct()
     n0, n1, n2, n3 = (int(x) for x in shape4)
     _lib.call("mira_cuda_copy_view_f32", n0, n1, n2, n3, C.byref(s), C.byref(d))
+
+
+ATT_TILE = 64    # query and key rows per attention tile
+
+
+@dataclass
+class Attn:
+    """Descriptor of one fused attention launch (mira_attention): q/k/v views with keys as rows,
+    the scale step ("mul"/"div" or None), an optional mask view, tile maxima and a device scalar
+    max|k| for exact tile skipping, and f32 / int8 outputs."""
+    batch0: int
+    batch1: int
+    tq: int
+    tk: int
+    dh: int
+    q: View
+    k: View
+    v: View
+    scale_op: Optional[str] = None
+    scale: float = 1.0
+    mask: Optional[View] = None
+    tile_max: object = None
+    kmax: object = None
+    tile_zero: object = None
+    out: Optional[View] = None
+    out_i8: Optional[View] = None
+    out_scale: float = 1.0
+
+    def struct(self) -> _lib.Attention:
+        a = _lib.Attention()
+        a.batch0, a.batch1, a.tq, a.tk, a.dh = (int(x) for x in (self.batch0, self.batch1, self.tq, self.tk, self.dh))
+        a.q, a.k, a.v = self.q.struct(), self.k.struct(), self.v.struct()
+        a.scale_op = {None: 0, "mul": _lib.EPI_MUL, "div": _lib.EPI_DIV}[self.scale_op]
+        a.scale = float(np.float32(self.scale))
+        if self.mask is not None:
+            a.mask = self.mask.struct()
+        a.tile_max = ptr(self.tile_max).value or 0
+        a.kmax = ptr(self.kmax).value or 0
+        a.tile_zero = ptr(self.tile_zero).value or 0
+        if self.out is not None:
+            a.out_f32 = self.out.struct()
+        if self.out_i8 is not None:
+            a.out_i8 = self.out_i8.struct()
+        a.out_scale = float(np.float32(self.out_scale))
+        return a
+
+
+def mask_tile_max(mask: np.ndarray, tq: int, tk: int) -> np.ndarray:
+    """Maximum of each ATT_TILE x ATT_TILE tile of a [tq, tk] mask, [ceil(tq/64), ceil(tk/64)] f32."""
+    nq, nk = -(-tq // ATT_TILE), -(-tk // ATT_TILE)
+    padded = np.full((nq * ATT_TILE, nk * ATT_TILE), -np.inf, np.float32)
+    padded[:tq, :tk] = np.broadcast_to(np.asarray(mask, np.float32), (tq, tk))
+    return padded.reshape(nq, ATT_TILE, nk, ATT_TILE).max(axis=(1, 3)).astype(np.float32)
+
+
+def mask_tile_zero(mask: np.ndarray, tq: int, tk: int) -> np.ndarray:
+    """1 for each ATT_TILE x ATT_TILE tile of a [tq, tk] mask whose entries are all +0.0, as uint8."""
+    nq, nk = -(-tq // ATT_TILE), -(-tk // ATT_TILE)
+    m = np.broadcast_to(np.asarray(mask, np.float32), (tq, tk))
+    plus_zero = (m == 0) & ~np.signbit(m)
+    padded = np.ones((nq * ATT_TILE, nk * ATT_TILE), bool)
+    padded[:tq, :tk] = plus_zero
+    return padded.reshape(nq, ATT_TILE, nk, ATT_TILE).all(axis=(1, 3)).astype(np.uint8)
+
+
+def attention_f32(desc: Attn) -> None:
+    a = desc.struct()
+    _lib.call("mira_cuda_attention_f32", C.byref(a))
+
+
+def collapse_view(shape, strides) -> tuple[tuple, tuple]:
+    """An equivalent view of at most 4 dimensions with the fewest dimensions, for reductions whose
+    result does not depend on element order (dimensions reordered by stride and merged where
+    contiguous with each other), padded with leading size-1 dimensions."""
+    dims = sorted(((int(n), int(st)) for n, st in zip(shape, strides) if int(n) != 1), key=lambda t: -abs(t[1]))
+    out: list = []
+    for n, st in dims:
+        if out and out[-1][1] == st * n:
+            out[-1] = (out[-1][0] * n, st)
+        else:
+            out.append((n, st))
+    out = [(1, 0)] * (4 - len(out)) + out
+    return tuple(n for n, _ in out), tuple(st for _, st in out)
+
+
+def absmax_f32(shape4, x: View, out) -> None:
+    xv = x.struct()
+    n0, n1, n2, n3 = (int(v) for v in shape4)
+    _lib.call("mira_cuda_absmax_f32", n0, n1, n2, n3, C.byref(xv), ptr(out))

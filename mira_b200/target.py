@@ -164,6 +164,16 @@ class CudaDevice:
             fn = L.mira_cuda_embed_rows
             args = (ptr(a["table"]), a["vocab"], a["d"], ptr(a["idx"]), a["rows"], ptr(a.get("addend")),
                     a.get("addend_rows", 0), ptr(a["out"]), a["ld_out"])
+        elif k == "attention":
+            st = a["desc"].struct()
+            keep.append(st)
+            fn = L.mira_cuda_attention_f32
+            args = (C.byref(st),)
+        elif k == "absmax":
+            xv = a["x"].struct()
+            keep.append(xv)
+            fn = L.mira_cuda_absmax_f32
+            args = tuple(int(x) for x in a["shape"]) + (C.byref(xv), ptr(a["out"]))
         elif k == "copy_view":
             sv, dv = a["src"].struct(), a["dst"].struct()
             keep += [sv, dv]
@@ -308,6 +318,7 @@ class Plan:
         self.keep: list = []         # constant uploads
         self.skipped: set = set()
         self.kernel_counts: dict = {}
+        self._kmax = None            # device scalar max|k| shared by the attention launches
         self._build()
 
     # ------------------------------------------------------------------ helpers
@@ -391,6 +402,80 @@ class Plan:
                     if v.type.rank == 4 and self._const(v) is None:
                         self.image_values.add(v)
         self._group_qmatmuls()
+        self._find_attention()
+
+    def _find_attention(self):
+        """matmul(q, k^T) {scale, mask} -> softmax(axis=-1) -> matmul(., v) chains run as one fused
+        attention launch (the scores are never stored).  When the output only reaches quantized
+        matmuls through transpose(0, 2, 1, 3) + reshape (the heads merged back), the launch also
+        writes their int8 input rows directly."""
+        g, users = self.g, self.users
+        self.attention: dict = {}
+        for op in g.ops:
+            if op.kind != "matmul" or op in self.skipped or op.result in g.outputs:
+                continue
+            uses = users.get(op.result, [])
+            if len(uses) != 1 or uses[0].kind != "softmax" or uses[0].result in g.outputs:
+                continue
+            sm = uses[0]
+            rank = sm.result.type.rank
+            if rank < 2 or rank > 4 or sm.attrs.get("axis", -1) % rank != rank - 1:
+                continue
+            su = users.get(sm.result, [])
+            if len(su) != 1 or su[0].kind != "matmul" or su[0].inputs[0] is not sm.result or su[0].attrs.get("epilogue"):
+                continue
+            mm2 = su[0]
+            steps = list(op.attrs.get("epilogue", ()))
+            scale_op, scale, mask = None, 1.0, None
+            if steps and steps[0][0] in ("mul", "div") and steps[0][1] is not None:
+                fn, idx, swapped = steps[0]
+                val = self._const(op.inputs[idx])
+                if val is not None and val.size == 1 and not (fn == "div" and swapped):
+                    scale_op, scale = fn, float(np.float32(val.ravel()[0]))
+                    steps.pop(0)
+            if steps and steps[0][0] == "add" and steps[0][1] is not None:
+                mask = op.inputs[steps[0][1]]
+                steps.pop(0)
+            if steps:
+                continue
+            q, kt, v = op.inputs[0], op.inputs[1], mm2.inputs[1]
+            bshape = tuple(op.result.type.shape[:-2])
+            if any(tuple(x.type.shape[:-2]) != bshape for x in (q, kt, v)) or self._const(q) is not None:
+                continue
+            dh, dv = q.type.shape[-1], v.type.shape[-1]
+            if dh != dv or dh > 128 or kt.type.shape[-2] != dh:
+                continue
+            self.attention[op] = dict(softmax=sm, pv=mm2, scale_op=scale_op, scale=scale, mask=mask,
+                                      i8_chain=self._attention_i8_chain(mm2))
+            self.skipped.update((sm, mm2))
+            chain = self.attention[op]["i8_chain"]
+            if chain is not None:
+                self.skipped.update(chain[:2])
+
+    def _attention_i8_chain(self, mm2):
+        """(transpose op, reshape op) when the attention output [B, H, T, dv] only reaches
+        quantized matmuls as reshape(transpose(o, (0, 2, 1, 3)), [..., H * dv])."""
+        g, users = self.g, self.users
+        shape = tuple(mm2.result.type.shape)
+        if len(shape) != 4 or mm2.result in g.outputs:
+            return None
+        u = users.get(mm2.result, [])
+        if len(u) != 1 or u[0].kind != "transpose" or tuple(int(p) % 4 for p in u[0].attrs["perm"]) != (0, 2, 1, 3):
+            return None
+        tr = u[0]
+        u2 = users.get(tr.result, [])
+        if len(u2) != 1 or u2[0].kind != "reshape" or tr.result in g.outputs:
+            return None
+        rs = u2[0]
+        b, h, t, dv = shape
+        rshape = tuple(rs.result.type.shape)
+        if not rshape or rshape[-1] != h * dv or int(np.prod(rshape[:-1], dtype=np.int64)) != b * t:
+            return None
+        if rs.result in g.outputs or rs.result in self.need_f32 or rs.result not in self.i8_req:
+            return None
+        if any(c.kind != "qmatmul" or c.inputs[0] is not rs.result for c in users.get(rs.result, [])):
+            return None
+        return tr, rs
 
     def _group_qmatmuls(self):
         """Quantized matmuls that read the same int8 activation (same value, same x_scale) and
@@ -891,26 +976,88 @@ class Plan:
         st = tuple(0 if d == 1 else x for d, x in zip(shape, st))
         return K.View(dv.f32, (0,) * (4 - r) + st, dv.offset)
 
+    def _attention(self, op, info) -> None:
+        """One fused attention launch for matmul -> softmax -> matmul (see _find_attention)."""
+        mm2 = info["pv"]
+        qd, ktd, vd = (self._f32_dval(v) for v in (op.inputs[0], op.inputs[1], mm2.inputs[1]))
+        sshape = tuple(op.result.type.shape)
+        oshape = tuple(mm2.result.type.shape)
+        tq, tk, dh = sshape[-2], sshape[-1], qd.shape[-1]
+        batch = (1,) * (4 - len(oshape)) + oshape[:-2]
+        qv = self._broadcast_view(qd, oshape[:-2] + (tq, dh))
+        ktv = self._broadcast_view(ktd, oshape[:-2] + (dh, tk))
+        kv = K.View(ktv.buf, ktv.strides[:2] + (ktv.strides[3], ktv.strides[2]), ktv.offset)
+        vv = self._broadcast_view(vd, oshape[:-2] + (tk, dh))
+        mask_view, tile_max, kmax, tile_zero = None, None, None, None
+        if info["mask"] is not None:
+            mask_view = self._broadcast_view(self._f32_dval(info["mask"]), sshape)
+            mval = self._const(info["mask"])
+            if mval is not None:
+                m2 = np.broadcast_to(np.asarray(mval, np.float32), sshape)
+                m2 = m2.reshape(-1, tq, tk)
+                if all(np.array_equal(m2[0], m2[i]) for i in range(1, m2.shape[0])):
+                    tile_max = self._upload(K.mask_tile_max(m2[0], tq, tk))
+                    tile_zero = self._upload(K.mask_tile_zero(m2[0], tq, tk))
+        if tile_max is not None:
+            if self._kmax is None:
+                self._kmax = self._alloc(16, zero=True)
+            kmax = self._kmax
+            cshape, cst = K.collapse_view(batch + (tk, dh), kv.strides)
+            self._launch("absmax", shape=cshape, x=K.View(kv.buf, cst, kv.offset), out=kmax)
+        desc = K.Attn(batch[0], batch[1], tq, tk, dh, qv, kv, vv, info["scale_op"], info["scale"], mask_view,
+                      tile_max, kmax, tile_zero)
+        chain = info["i8_chain"]
+        if chain is not None:
+            rs = chain[1]
+            scale = self.i8_req[rs.result]
+            rshape = tuple(rs.result.type.shape)
+            dv_ = DVal(rshape, "rows", i8_scale=scale)
+            dv_.i8_ld = K.round_up(dv_.cols, 16)
+            dv_.i8 = self._alloc(dv_.rows * dv_.i8_ld, zero=True)
+            self.vals[rs.result] = dv_
+            b, h, t, d = oshape
+            desc.out_i8 = K.View(dv_.i8, (t * dv_.i8_ld, d, dv_.i8_ld, 1), itemsize=1)
+            desc.out_scale = scale
+        else:
+            strides = self._transposed_strides(mm2)
+            out = self._new_out(mm2.result, strides=strides)
+            if out.f32 is None:
+                out.f32 = self._alloc(out.numel * 4)
+                out.strides = strides
+            desc.out = self._broadcast_view(out, oshape)
+            if out.i8 is not None:
+                ist = tuple(c * out.i8_ld for c in contiguous_strides(oshape[:-1])) + (1,)
+                desc.out_i8 = K.View(out.i8, (0,) * (4 - len(oshape)) + ist, itemsize=1)
+                desc.out_scale = out.i8_scale
+        self._launch("attention", desc=desc)
+
+    def _transposed_strides(self, op) -> Optional[tuple]:
+        """Strides that make the transpose consuming `op`'s result row-major, if it has exactly
+        one consumer and that is a transpose."""
+        users = self.users.get(op.result, [])
+        if len(users) != 1 or users[0].kind != "transpose" or op.result in self.g.outputs:
+            return None
+        oshape = tuple(op.result.type.shape)
+        perm = tuple(int(p) % len(oshape) for p in users[0].attrs["perm"])
+        tst = contiguous_strides(tuple(oshape[p] for p in perm))
+        inv = [0] * len(oshape)
+        for i, p in enumerate(perm):
+            inv[p] = tst[i]
+        return tuple(inv)
+
     def _op_matmul(self, op) -> None:
         """f32 matmul with its fused epilogue (reference ops.py:217-219) on strided views: the
         attention products q @ k^T and p @ v read the q/k/v projections where they lie."""
+        if op in self.attention:
+            self._attention(op, self.attention[op])
+            return
         xa, wb = self._f32_dval(op.inputs[0]), self._f32_dval(op.inputs[1])
         oshape = tuple(op.result.type.shape)
         if len(oshape) > 4 or len(xa.shape) > 4 or len(wb.shape) > 4:
             raise UnsupportedOnCuda("matmul of more than 4 dimensions")
         m, kdim = xa.shape[-2:]
         n = wb.shape[-1]
-        users = self.users.get(op.result, [])
-        strides = None
-        if len(users) == 1 and users[0].kind == "transpose" and op.result not in self.g.outputs:
-            # lay the result out so that its transpose is row-major
-            perm = tuple(int(p) % len(oshape) for p in users[0].attrs["perm"])
-            tst = contiguous_strides(tuple(oshape[p] for p in perm))
-            inv = [0] * len(oshape)
-            for i, p in enumerate(perm):
-                inv[p] = tst[i]
-            strides = tuple(inv)
-        out = self._new_out(op.result, strides=strides)
+        out = self._new_out(op.result, strides=self._transposed_strides(op))
         batch = (1,) * (4 - len(oshape)) + oshape[:-2]
         steps = []
         for fn, idx, swapped in op.attrs.get("epilogue", ()):

@@ -246,3 +246,25 @@ class FakeDevice:
 
     def _copy_view(self, shape, src, dst):
         _strided(dst, shape)[...] = _strided(src, shape)
+
+    def _absmax(self, shape, x, out):
+        out.view(np.float32, (1,))[0] = np.abs(_strided(x, shape)).max() if np.prod(shape) else 0.0
+
+    def _attention(self, desc):
+        d = desc
+        q = _strided(d.q, (d.batch0, d.batch1, d.tq, d.dh))
+        k = _strided(d.k, (d.batch0, d.batch1, d.tk, d.dh))
+        v = _strided(d.v, (d.batch0, d.batch1, d.tk, d.dh))
+        steps, operands = [], []
+        if d.scale_op is not None:
+            steps.append((d.scale_op, len(operands), False))
+            operands.append(np.float32(d.scale))
+        if d.mask is not None:
+            steps.append(("add", len(operands), False))
+            operands.append(_strided(d.mask, (d.batch0, d.batch1, d.tq, d.tk)))
+        s = ref.matmul_f32(q, np.swapaxes(k, -1, -2), steps, operands)
+        o = ref.matmul_f32(ref.softmax(s), v)
+        if d.out is not None:
+            _strided(d.out, o.shape)[...] = o
+        if d.out_i8 is not None:
+            _strided(d.out_i8, o.shape, np.int8)[...] = ref.quantize_activation(o, d.out_scale)

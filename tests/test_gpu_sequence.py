@@ -156,9 +156,74 @@ def test_copy_view_transpose(cuda_device):
     rng = np.random.default_rng(4)
     x = rng.standard_normal((2, 7, 3, 5)).astype(np.float32)
     xb, yb = DB.from_array(x), DB(x.nbytes)
-    src = K.View(xb, (7 * 3 * 5, 5, 7 * 5, 1))            # x.transpose(0, 2, 1, 3) as a view
+    src = K.View(xb, (7 * 3 * 5, 5, 3 * 5, 1))            # x.transpose(0, 2, 1, 3) as a view
     K.copy_view((2, 3, 7, 5), src, K.View(yb, (3 * 7 * 5, 7 * 5, 5, 1)))
     _bits_equal(yb.download((2, 3, 7, 5), np.float32), x.transpose(0, 2, 1, 3))
+
+
+def _attention_case(K, DB, b0, b1, t, dh, seed, amp=1.0, mask=True, skip=True, scale_op="mul", i8_scale=None):
+    rng = np.random.default_rng(seed)
+    q = (rng.standard_normal((b0, b1, t, dh)) * amp).astype(np.float32)
+    k = (rng.standard_normal((b0, b1, t, dh)) * amp).astype(np.float32)
+    v = rng.standard_normal((b0, b1, t, dh)).astype(np.float32)
+    m = np.where(np.arange(t)[:, None] >= np.arange(t)[None, :], 0.0, -10000.0).astype(np.float32)
+    scale = 0.125 if scale_op == "mul" else 8.0
+    qb, kb, vb, mb = (DB.from_array(x) for x in (q, k, v, m))
+    st = (b1 * t * dh, t * dh, dh, 1)
+    ob = DB(q.nbytes)
+    tile_max = kmax = None
+    tile_zero = None
+    if mask and skip:
+        tile_max, kmax = DB.from_array(K.mask_tile_max(m, t, t)), DB(16, zero=True)
+        tile_zero = DB.from_array(K.mask_tile_zero(m, t, t))
+        K.absmax_f32((b0, b1, t, dh), K.View(kb, st), kmax)
+    desc = K.Attn(b0, b1, t, t, dh, K.View(qb, st), K.View(kb, st), K.View(vb, st), scale_op, scale,
+                  K.View(mb, (0, 0, t, 1)) if mask else None, tile_max, kmax, tile_zero, out=K.View(ob, st))
+    qi8 = None
+    if i8_scale is not None:
+        qi8 = DB(q.size, zero=True)
+        desc.out_i8, desc.out_scale = K.View(qi8, st, itemsize=1), i8_scale
+    K.attention_f32(desc)
+    steps, ops = [(scale_op, 0, False)], [np.float32(scale)]
+    if mask:
+        steps.append(("add", 1, False))
+        ops.append(m)
+    want = ref.matmul_f32(ref.softmax(ref.matmul_f32(q, np.swapaxes(k, -1, -2), steps, ops)), v)
+    got = ob.download(q.shape, np.float32)
+    i8 = qi8.download(q.shape, np.int8) if qi8 is not None else None
+    return got, want, v, i8
+
+
+@pytest.mark.parametrize("b0,b1,t,dh", [(2, 3, 100, 64), (1, 2, 64, 64), (1, 1, 1, 64), (2, 2, 200, 32), (1, 2, 70, 30),
+                                        (1, 2, 130, 128), (1, 4, 300, 48)])
+@pytest.mark.parametrize("skip", [True, False])
+def test_attention_matches_reference_chain(cuda_device, b0, b1, t, dh, skip):
+    """softmax(q @ k^T * s + causal mask) @ v against the reference's three ops."""
+    K, DB = _k()
+    got, want, v, _ = _attention_case(K, DB, b0, b1, t, dh, t + dh, skip=skip)
+    np.testing.assert_allclose(got, want, rtol=0, atol=3e-6 * np.abs(v).max())
+
+
+def test_attention_large_scores_are_not_skipped(cuda_device):
+    """With scores far beyond the mask (|q.k| * scale >> 10000) the masked entries do count in the
+    reference; the skip test must fail and every tile be processed."""
+    K, DB = _k()
+    got, want, v, _ = _attention_case(K, DB, 1, 2, 160, 64, 5, amp=60.0)
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-5 * np.abs(v).max())
+
+
+def test_attention_div_scale_no_mask(cuda_device):
+    K, DB = _k()
+    got, want, v, _ = _attention_case(K, DB, 2, 3, 90, 64, 6, mask=False, scale_op="div")
+    np.testing.assert_allclose(got, want, rtol=0, atol=3e-6 * np.abs(v).max())
+
+
+def test_attention_int8_output(cuda_device):
+    """The fused requantization equals quantize_activation of the kernel's own f32 output."""
+    K, DB = _k()
+    got, want, v, i8 = _attention_case(K, DB, 2, 2, 96, 64, 7, i8_scale=0.0123)
+    np.testing.assert_array_equal(i8, ref.quantize_activation(got, 0.0123))
+    assert np.abs(i8.astype(int) - ref.quantize_activation(want, 0.0123).astype(int)).max() <= 1
 
 
 # ------------------------------------------------------------------------------ end to end

@@ -154,7 +154,38 @@ def test_transformer_small_plan_matches_cpu():
     # per layer: one q/k/v GEMM, out-proj, two MLP GEMMs; plus the LM head
     assert counts["qgemm"] == 4 * 2 + 1
     assert counts["layernorm"] == 2 * 2 + 1 and counts["embed"] == 1
-    assert counts["bmm"] == 2 * 2 and counts["softmax"] == 2
+    # q @ k^T -> softmax -> @ v fused, writing the out-projection's int8 rows itself
+    assert counts["attention"] == 2 and counts["absmax"] == 2
+    assert "bmm" not in counts and "softmax" not in counts and "quantize_rows" not in counts
+
+
+def test_unfused_attention_ops_plan_matches_cpu():
+    """The generic kernels (strided bmm, softmax) when the chain does not have the fused form:
+    here the scores are also a graph output."""
+    from mira_b200.hostfw import import_mira
+    import_mira()
+    from mira import ir
+    from mira.types import TensorType as TT
+    rng = np.random.default_rng(2)
+    q = ir.Value(TT("f32", (2, 3, 8, 16)), name="q")
+    k = ir.Value(TT("f32", (2, 3, 16, 8)), name="k")
+    g = ir.Graph("attn", [q, k], [], [])
+    s = g.add("matmul", [q, k], {})
+    s = g.add("mul", [s, g.const(np.float32(0.25))], {})
+    p = g.add("softmax", [s], {"axis": -1})
+    o = g.add("matmul", [p, g.add("transpose", [k], {"perm": (0, 1, 3, 2)})], {})
+    g.outputs = [o, s]
+    g.verify()
+    feeds = {"q": rng.standard_normal((2, 3, 8, 16)).astype(np.float32),
+             "k": rng.standard_normal((2, 3, 16, 8)).astype(np.float32)}
+    cpu = compiler.compile_ir(g, "cpu", precision=None)
+    dev = FakeDevice()
+    cuda = compiler.compile_ir(g, "cuda", executor=dev)
+    assert [x.device for x in cuda.segments] == ["cuda"]
+    want, got = cpu.run(feeds), cuda.run(feeds)
+    for a, b in zip(want, got):
+        np.testing.assert_array_equal(a, b)
+    assert dev.launched.count("bmm") == 2 and dev.launched.count("softmax") == 1
 
 
 def test_view_strides_match_numpy_views():
