@@ -183,6 +183,51 @@ def gemm_tops(n: int = 8192, iters: int = 5) -> float:
     return 2.0 * n ** 3 / (ms.value / iters * 1e-3) / 1e12
 
 
+def skinny_gemm(m: int, n: int = 4096, k: int = 4096, iters: int = 50) -> dict:
+    """The GEMM sweep's skinny rows (config 2): M x 4096 x 4096 through mira_cuda_qgemm_splitk (split-K
+    with a workspace when the output tiles cannot fill the GPU); HBM-bound, so also GB/s of the
+    algorithmic bytes M*K + K*N + 4*M*N."""
+    from mira_b200 import _lib, kernels as K
+    from mira_b200.device import DeviceBuffer
+    A, B, Y = DeviceBuffer(m * k), DeviceBuffer(n * k), DeviceBuffer(m * n * 4)
+    _lib.call("mira_cuda_memset", C.c_void_p(A.ptr), 3, C.c_size_t(m * k))
+    _lib.call("mira_cuda_memset", C.c_void_p(B.ptr), 5, C.c_size_t(n * k))
+    rs = DeviceBuffer.from_array(np.full(m, 1e-3, np.float32))
+    cs = DeviceBuffer.from_array(np.full(n, 2e-3, np.float32))
+    bias = DeviceBuffer.from_array(K.pad_channels(np.zeros(n, np.float32)))
+    dq = K.dequant_rowcol(rs, cs)
+    e = K.Epi([K.Step("add", "channel", ptr=bias)], out_f32=Y, ld_f32=n).struct()
+    ws_bytes = K.qgemm_workspace(m, n, k)
+    ws = DeviceBuffer(max(ws_bytes, 16))
+    fn = _lib.load().mira_cuda_qgemm_splitk
+    args = (m, n, k, C.c_void_p(A.ptr), k, C.c_void_p(B.ptr), k, C.byref(dq), C.byref(e), C.c_void_p(ws.ptr), ws_bytes)
+    for _ in range(3):
+        fn(*args)
+    _lib.call("mira_cuda_sync")
+    # the launches replay from a CUDA graph, so the time is the device's, not the host's issue rate
+    _lib.call("mira_cuda_graph_begin")
+    try:
+        for _ in range(iters):
+            fn(*args)
+    finally:
+        g = C.c_void_p()
+        _lib.call("mira_cuda_graph_end", C.byref(g))
+    _lib.call("mira_cuda_graph_launch", g)
+    _lib.call("mira_cuda_sync")
+    a, b = C.c_void_p(), C.c_void_p()
+    _lib.call("mira_cuda_event_create", C.byref(a))
+    _lib.call("mira_cuda_event_create", C.byref(b))
+    _lib.call("mira_cuda_event_record", a)
+    _lib.call("mira_cuda_graph_launch", g)
+    _lib.call("mira_cuda_event_record", b)
+    ms = C.c_float()
+    _lib.call("mira_cuda_sync")
+    _lib.call("mira_cuda_event_elapsed", a, b, C.byref(ms))
+    _lib.call("mira_cuda_graph_destroy", g)
+    us = ms.value / iters * 1e3
+    return {"us": us, "gb_s": (m * k + k * n + 4 * m * n) / (us * 1e-6) / 1e9, "workspace_bytes": ws_bytes}
+
+
 def cublaslt_int8_tops(n: int = 8192) -> float | None:
     """torch._int_mm (cuBLASLt int8) at n^3, for context next to the roofline."""
     try:
@@ -345,6 +390,7 @@ def main() -> None:
         achieved = conv_ops / (conv_ms * 1e-3) / 1e12
         ours_gemm = gemm_tops(8192)
         lib_gemm = cublaslt_int8_tops(8192)
+        skinny = {str(m): skinny_gemm(m) for m in (1, 16, 128)}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             try:
@@ -370,7 +416,7 @@ def main() -> None:
                          "peak_source": f"2 x bf16_tflops of {src} (dense int8 issues at twice the bf16 rate)",
                          "conv_int8_ops_per_step": conv_ops, "conv_ms_per_step": conv_ms},
             "int8_gemm": {"shape": "8192^3", "tops": ours_gemm, "frac_of_peak": ours_gemm / peak if peak else None,
-                          "cublaslt_tops": lib_gemm},
+                          "cublaslt_tops": lib_gemm, "skinny_mx4096x4096": skinny},
             "int8_ops_per_step": q_ops, "int8_tops_step": q_ops / (dev_ms / args.steps * 1e-3) / 1e12,
             "gpu_launches": int(gpu_launches), "clocks": clocks.summary(),
             "cpu_baseline": cpu,

@@ -169,6 +169,19 @@ int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t ld
                     const int8_t* B, int64_t ldb, const mira_dequant* dq,
                     const mira_epilogue* epi);
 
+/* Bytes of workspace mira_cuda_qgemm_splitk needs for an M x N x K product on the current device;
+ * 0 when the output tiles already fill the GPU (then it runs like mira_cuda_qgemm). */
+int64_t mira_cuda_qgemm_workspace(int64_t M, int64_t N, int64_t K);
+
+/* mira_cuda_qgemm for shapes with few output tiles (small M, the skinny rows of the GEMM sweep and
+ * of decoding): the reduction is cut into K ranges processed by different CTAs, whose int32 partial
+ * sums go to `workspace` (device memory, 16-byte aligned, at least mira_cuda_qgemm_workspace()
+ * bytes); a second kernel adds them (exact in int32) and applies the same dequant and epilogue, so
+ * the results equal mira_cuda_qgemm's bit for bit.  Calls sharing a workspace must not overlap. */
+int mira_cuda_qgemm_splitk(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda,
+                           const int8_t* B, int64_t ldb, const mira_dequant* dq,
+                           const mira_epilogue* epi, void* workspace, int64_t workspace_bytes);
+
 /* W8A8 convolution as an implicit GEMM over int8 activations, reference ops.py:630-634
  * (_qconv2d_ref, through _conv2d_ref ops.py:265-276 with groups = 1).
  * x: MIRA_LAYOUT_NHWC int8 [n, h, w, cp] (cp 4 or a multiple of 16) with weights int8 [o, ldw],

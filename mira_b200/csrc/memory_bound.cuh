@@ -277,6 +277,70 @@ __global__ void zero_pad_cols_kernel(int8_t* __restrict__ y, int64_t rows, int64
   }
 }
 
+// ---------------------------------------------------------------- split-K finish
+
+// Adds the int32 partial sums of a split-K GEMM (exact: the full sum fits int32) and applies the
+// quantized matmul's epilogue element by element: exact dequant (f64 fallback), steps, f32 and
+// int8 outputs (int8 padding columns [N, ld_i8) written as 0).
+struct SplitkFinishParams {
+  const int32_t* ws;
+  int splits;
+  int64_t slice;            // elements per partial slice (M * N)
+  int M, N;
+  const double* scale64;
+  const float* scale_hi;
+  const float* scale_lo;
+  const float* row_scale;
+  const float* col_scale;
+  int n_steps;
+  mira_epi_step steps[MIRA_EPI_MAX_STEPS];
+  float* out_f32;
+  int64_t ld_f32;
+  int8_t* out_i8;
+  int64_t ld_i8;
+  QuantScale q;
+};
+
+__global__ void qgemm_splitk_finish_kernel(const SplitkFinishParams p) {
+  const int width = (p.out_i8 != nullptr && p.ld_i8 > p.N) ? static_cast<int>(p.ld_i8) : p.N;
+  const int64_t total = int64_t(p.M) * width;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(e / width), n = static_cast<int>(e - int64_t(m) * width);
+    if (n >= p.N) {
+      p.out_i8[int64_t(m) * p.ld_i8 + n] = 0;
+      continue;
+    }
+    const int64_t idx = int64_t(m) * p.N + n;
+    int32_t acc = 0;
+    for (int s = 0; s < p.splits; ++s) acc += __ldg(p.ws + s * p.slice + idx);
+    float y;
+    if (p.scale64 != nullptr) {
+      if (!dequant_fast(acc, __ldg(p.scale_hi + n), __ldg(p.scale_lo + n), y))
+        y = __double2float_rn(static_cast<double>(acc) * __ldg(p.scale64 + n));
+    } else {
+      const float rs = __ldg(p.row_scale + m), cs = __ldg(p.col_scale + n);
+      float hi, lo;
+      split_rowcol(rs, cs, hi, lo);
+      if (!dequant_fast(acc, hi, lo, y))
+        y = __double2float_rn(static_cast<double>(acc) * (static_cast<double>(rs) * static_cast<double>(cs)));
+    }
+    for (int s = 0; s < p.n_steps; ++s) {
+      const mira_epi_step& st = p.steps[s];
+      if (st.operand == MIRA_OPND_NONE) {
+        y = apply_unary(st.op, y);
+        continue;
+      }
+      float o = st.scalar;
+      if (st.operand == MIRA_OPND_CHANNEL) o = __ldg(st.ptr + n);
+      else if (st.operand == MIRA_OPND_ROW) o = __ldg(st.ptr + m);
+      else if (st.operand == MIRA_OPND_FULL) o = __ldg(st.ptr + int64_t(m) * st.ld + n);
+      y = st.swapped ? apply_binary(st.op, o, y) : apply_binary(st.op, y, o);
+    }
+    if (p.out_f32 != nullptr) p.out_f32[int64_t(m) * p.ld_f32 + n] = y;
+    if (p.out_i8 != nullptr) p.out_i8[int64_t(m) * p.ld_i8 + n] = static_cast<int8_t>(quant_byte(y, p.q) & 0xff);
+  }
+}
+
 // ---------------------------------------------------------------- K4: depthwise f32 conv (NHWC)
 
 struct DwParams {

@@ -147,7 +147,12 @@ static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes
 // ---------------------------------------------------------------- qgemm dispatch
 
 template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false>
-static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, const QgParams& p) {
+static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, const QgParams& p_in) {
+  QgParams p = p_in;
+  if (p.k_splits < 1) {   // no split: one K range per output tile
+    p.k_splits = 1;
+    p.kb_per_split = p.num_kb;
+  }
   using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL>;
   auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL>;
   static bool attr_set[kMaxDevices] = {};
@@ -156,7 +161,7 @@ static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUte
                   "cudaFuncSetAttribute(qgemm smem)");
     attr_set[dev->device] = true;
   }
-  const int tiles = p.m_tiles * p.n_tiles;
+  const int tiles = p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
   kern<<<grid, Cfg::THREADS, Cfg::SMEM, dev->stream>>>(tmA, tmB, p);
   return after_launch("qgemm_sm100_kernel");
@@ -350,7 +355,7 @@ extern "C" int mira_cuda_sync(void) {
   if (flag != 0) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_mira_kernel_error, &zero, sizeof(int));
-    if (flag == 2) return set_error(MIRA_CUDA_EKERNEL, "embedding row index out of range (error record 2)");
+    if (flag == 3) return set_error(MIRA_CUDA_EKERNEL, "embedding row index out of range (error record 3)");
     return set_error(MIRA_CUDA_EKERNEL, "a kernel gave up on a bounded wait (error record " + std::to_string(flag) + ")");
   }
   return MIRA_CUDA_OK;
@@ -471,15 +476,45 @@ extern "C" int mira_cuda_quantize_nchw_to_row4(const float* x, int64_t n, int64_
   return after_launch("quantize_nchw_row4_kernel");
 }
 
-extern "C" int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda, const int8_t* B,
-                               int64_t ldb, const mira_dequant* dq, const mira_epilogue* epi) {
-  MIRA_GET_DEVICE(dev);
+namespace mira {
+
+// Split-K plan for a GEMM whose output tiles cannot fill the GPU: the number of K ranges per
+// output tile (1: no split) and the K-blocks per range.  A split pays off when fewer than half
+// the SMs would get a tile and the reduction is long enough to cut into ranges of >= 4 blocks.
+static void splitk_plan(int64_t M, int64_t N, int64_t K, int sm_count, int& splits, int& kb_per) {
+  const int bn = pick_bn(N);
+  const int64_t tiles = ((M + QG_BM - 1) / QG_BM) * ((N + bn - 1) / bn);
+  const int num_kb = int((K + QG_BK - 1) / QG_BK);
+  splits = 1;
+  kb_per = num_kb;
+  if (tiles * 2 > sm_count || num_kb < 8) return;
+  int s = int(sm_count / tiles);
+  if (s > num_kb / 4) s = num_kb / 4;
+  if (s > 16) s = 16;
+  if (s < 2) return;
+  kb_per = (num_kb + s - 1) / s;
+  splits = (num_kb + kb_per - 1) / kb_per;
+  if (splits < 2) {
+    splits = 1;
+    kb_per = num_kb;
+  }
+}
+
+static int qgemm_check(int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb) {
   MIRA_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad qgemm shape");
   MIRA_CHECK_ARG(M < (int64_t(1) << 31) && N < (int64_t(1) << 24) && K < (int64_t(1) << 24), "qgemm shape too large");
   MIRA_CHECK_ARG(K <= 133000, "K too large for exact int32 accumulation of int8 products");
   MIRA_CHECK_ARG(lda >= round_up(K, 16) && lda % 16 == 0 && ldb >= round_up(K, 16) && ldb % 16 == 0,
                  "int8 operands need row strides >= round_up(K, 16), multiples of 16");
-  if (M == 0) return MIRA_CUDA_OK;
+  return MIRA_CUDA_OK;
+}
+
+// The quantized GEMM, optionally split over K: with splits > 1 the tcgen05 kernel stores each K
+// range's int32 sums to ws (splits x M x N) and qgemm_splitk_finish_kernel adds them and runs the
+// epilogue.
+static int qgemm_run(DeviceState* dev, int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda, const int8_t* B,
+                     int64_t ldb, const mira_dequant* dq, const mira_epilogue* epi, int splits, int kb_per,
+                     int32_t* ws) {
   QgParams p;
   std::memset(&p, 0, sizeof(p));
   const int rc = fill_epilogue(p, dq, epi);
@@ -491,13 +526,74 @@ extern "C" int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A,
   p.num_kb = int((K + QG_BK - 1) / QG_BK);
   p.m_tiles = int((M + QG_BM - 1) / QG_BM);
   p.n_tiles = int((N + bn - 1) / bn);
+  SplitkFinishParams f;
+  if (splits > 1) {
+    std::memset(&f, 0, sizeof(f));
+    f.ws = ws; f.splits = splits; f.slice = M * N; f.M = int(M); f.N = int(N);
+    f.scale64 = p.scale64; f.scale_hi = p.scale_hi; f.scale_lo = p.scale_lo;
+    f.row_scale = p.row_scale; f.col_scale = p.col_scale;
+    f.n_steps = p.n_steps;
+    for (int s = 0; s < p.n_steps; ++s) f.steps[s] = p.steps[s];
+    f.out_f32 = p.out_f32; f.ld_f32 = p.ld_f32; f.out_i8 = p.out_i8; f.ld_i8 = p.ld_i8;
+    f.q = make_qscale(p.out_i8 != nullptr ? epi->out_scale : 1.0f);
+    p.k_splits = splits;
+    p.kb_per_split = kb_per;
+    p.raw = 1;
+    p.split_stride = M * N;
+    p.out_f32 = reinterpret_cast<float*>(ws);
+    p.ld_f32 = N;
+    p.out_i8 = nullptr;
+    p.n_steps = 0;
+  }
   CUtensorMap tmA, tmB;
   int r = encode_2d_i8(&tmA, A, uint64_t(lda), uint64_t(M), uint64_t(lda), QG_BK, QG_BM);
   if (r != MIRA_CUDA_OK) return r;
   r = encode_2d_i8(&tmB, B, uint64_t(ldb), uint64_t(N), uint64_t(ldb), QG_BK, uint32_t(bn));
   if (r != MIRA_CUDA_OK) return r;
-  if (p.scale64 != nullptr) return launch_qgemm_bn<QG_A_TMA, false>(dev, tmA, tmB, p, bn);
-  return launch_qgemm_bn<QG_A_TMA, true>(dev, tmA, tmB, p, bn);
+  r = p.scale64 != nullptr ? launch_qgemm_bn<QG_A_TMA, false>(dev, tmA, tmB, p, bn)
+                           : launch_qgemm_bn<QG_A_TMA, true>(dev, tmA, tmB, p, bn);
+  if (r != MIRA_CUDA_OK || splits <= 1) return r;
+  const int threads = 256;
+  const int64_t width = (f.out_i8 != nullptr && f.ld_i8 > N) ? f.ld_i8 : N;
+  qgemm_splitk_finish_kernel<<<grid_for(dev, M * width, threads), threads, 0, dev->stream>>>(f);
+  return after_launch("qgemm_splitk_finish_kernel");
+}
+
+}  // namespace mira
+
+extern "C" int mira_cuda_qgemm(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda, const int8_t* B,
+                               int64_t ldb, const mira_dequant* dq, const mira_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  const int rc = qgemm_check(M, N, K, lda, ldb);
+  if (rc != MIRA_CUDA_OK) return rc;
+  if (M == 0) return MIRA_CUDA_OK;
+  return qgemm_run(dev, M, N, K, A, lda, B, ldb, dq, epi, 1, 0, nullptr);
+}
+
+extern "C" int64_t mira_cuda_qgemm_workspace(int64_t M, int64_t N, int64_t K) {
+  DeviceState* dev = current_device();
+  if (dev == nullptr || M <= 0 || N <= 0 || K <= 0) return 0;
+  int splits, kb_per;
+  splitk_plan(M, N, K, dev->sm_count, splits, kb_per);
+  return splits > 1 ? int64_t(splits) * M * N * int64_t(sizeof(int32_t)) : 0;
+}
+
+extern "C" int mira_cuda_qgemm_splitk(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda, const int8_t* B,
+                                      int64_t ldb, const mira_dequant* dq, const mira_epilogue* epi, void* workspace,
+                                      int64_t workspace_bytes) {
+  MIRA_GET_DEVICE(dev);
+  const int rc = qgemm_check(M, N, K, lda, ldb);
+  if (rc != MIRA_CUDA_OK) return rc;
+  if (M == 0) return MIRA_CUDA_OK;
+  int splits, kb_per;
+  splitk_plan(M, N, K, dev->sm_count, splits, kb_per);
+  if (splits > 1) {
+    const int64_t need = int64_t(splits) * M * N * int64_t(sizeof(int32_t));
+    MIRA_CHECK_ARG(workspace != nullptr && workspace_bytes >= need,
+                   "split-K workspace smaller than mira_cuda_qgemm_workspace() bytes");
+    MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, "split-K workspace must be 16-byte aligned");
+  }
+  return qgemm_run(dev, M, N, K, A, lda, B, ldb, dq, epi, splits, kb_per, static_cast<int32_t*>(workspace));
 }
 
 // Shared argument checks and parameter setup of the implicit-GEMM convolutions.

@@ -46,6 +46,12 @@ struct QgParams {
   int M, N, K;          // K = bytes of the reduction actually used
   int num_kb;           // ceil(K / QG_BK)
   int m_tiles, n_tiles;
+  // split-K (TMA mode): tile t covers output tile t % (m_tiles * n_tiles) and K-blocks
+  // [s * kb_per_split, (s + 1) * kb_per_split) with s = t / (m_tiles * n_tiles); with raw set the
+  // epilogue stores the int32 accumulators (as 4-byte words) to out_f32 + s * split_stride
+  int k_splits, kb_per_split;
+  int raw;
+  int64_t split_stride;
   const int8_t* A;      // gather modes: NHWC input
   QgConv g;
   const double* scale64;
@@ -177,6 +183,32 @@ __device__ __forceinline__ void qg_operand(const QgParams& p, const mira_epi_ste
   }
 }
 
+// Stores this thread's 16 values of a chunk: through the warp's staging block (coalesced 16-byte
+// stores of whole rows) when the chunk is full and rows are 16-byte aligned, else directly.
+template <int PITCH>
+__device__ __forceinline__ void qg_store_f32(const QgParams& p, const float (&v)[16], int m, bool row_ok, int m_warp0,
+                                             int nb, bool full_chunk, float* stage, int lane, float* out_f32) {
+  if (full_chunk && (p.ld_f32 % 4) == 0) {
+    float4* srow = reinterpret_cast<float4*>(stage + lane * PITCH);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) srow[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = i * 8 + (lane >> 2), qq = lane & 3;
+      const float4 t = reinterpret_cast<const float4*>(stage + rr * PITCH)[qq];
+      const int mm = m_warp0 + rr;
+      if (mm < p.M) reinterpret_cast<float4*>(out_f32 + static_cast<int64_t>(mm) * p.ld_f32 + nb)[qq] = t;
+    }
+    __syncwarp();
+  } else if (row_ok) {
+    float* dst = out_f32 + static_cast<int64_t>(m) * p.ld_f32 + nb;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (nb + j < p.N) dst[j] = v[j];
+  }
+}
+
 __device__ __forceinline__ void qg_apply_step(const mira_epi_step& st, const float (&o)[16], float (&v)[16]) {
   switch (st.op) {
     case MIRA_EPI_ADD: QG_APPLY_BINARY(__fadd_rn(a, b)); break;
@@ -191,11 +223,22 @@ __device__ __forceinline__ void qg_apply_step(const mira_epi_step& st, const flo
 
 // The whole epilogue of one 16-column chunk of this warp's 32 rows.  Everything that does not
 // depend on the accumulator (dequant scales, the first binary operand) is loaded before the TMEM
-// read so the two latencies overlap.
+// read so the two latencies overlap.  In raw mode (split-K partial sums) the int32 accumulators
+// are stored unchanged.
 template <bool ROWCOL, int PITCH>
 __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t taddr, int m, bool row_ok, int m_warp0,
-                                                  int nb, float* stage, int lane) {
+                                                  int nb, float* stage, int lane, float* out_f32) {
   const bool full_chunk = nb + 16 <= p.N;
+  if (p.raw) {
+    uint32_t r[16];
+    tmem_ld_32x32b_x16(taddr, r);
+    tmem_ld_wait();
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+    qg_store_f32<PITCH>(p, v, m, row_ok, m_warp0, nb, full_chunk, stage, lane, out_f32);
+    return;
+  }
   float hs[16], ls[16];
   if (!ROWCOL) {
     ld16(p.scale_hi + nb, hs);
@@ -252,27 +295,7 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
     qg_apply_step(st, o, v);
   }
 
-  if (p.out_f32 != nullptr) {
-    if (full_chunk && (p.ld_f32 % 4) == 0) {
-      float4* srow = reinterpret_cast<float4*>(stage + lane * PITCH);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) srow[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      __syncwarp();
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int rr = i * 8 + (lane >> 2), qq = lane & 3;
-        const float4 t = reinterpret_cast<const float4*>(stage + rr * PITCH)[qq];
-        const int mm = m_warp0 + rr;
-        if (mm < p.M) reinterpret_cast<float4*>(p.out_f32 + static_cast<int64_t>(mm) * p.ld_f32 + nb)[qq] = t;
-      }
-      __syncwarp();
-    } else if (row_ok) {
-      float* dst = p.out_f32 + static_cast<int64_t>(m) * p.ld_f32 + nb;
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (nb + j < p.N) dst[j] = v[j];
-    }
-  }
+  if (out_f32 != nullptr) qg_store_f32<PITCH>(p, v, m, row_ok, m_warp0, nb, full_chunk, stage, lane, out_f32);
   if (p.out_i8 != nullptr && row_ok && nb < p.ld_i8) {
     uint32_t b[16];
     if (full_chunk) {
@@ -343,7 +366,8 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_holder);
 
-  const int num_tiles = p.m_tiles * p.n_tiles;
+  const int mn_tiles = p.m_tiles * p.n_tiles;
+  const int num_tiles = mn_tiles * p.k_splits;
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
@@ -353,9 +377,11 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
       int issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t / p.n_tiles) * QG_BM;
-        const int n0 = (t % p.n_tiles) * BN;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int split = t / mn_tiles, t_mn = t - split * mn_tiles;
+        const int m0 = (t_mn / p.n_tiles) * QG_BM;
+        const int n0 = (t_mn % p.n_tiles) * BN;
+        const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], (AMODE == QG_A_TMA ? A_BYTES : 0) + B_BYTES);
           if (AMODE == QG_A_TMA) tma_load_2d(sA + stage * A_BYTES, &tmA, kb * QG_BK, m0, &full[stage]);
@@ -384,7 +410,9 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
         if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int split = t / mn_tiles;
+        const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
           if (AMODE != QG_A_TMA) fence_proxy_async_smem();  // A was written by cp.async (generic proxy)
           tc_fence_after();
@@ -394,7 +422,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
           const int nk = rem >= QG_BK ? QG_BK / QG_UMMA_K : (rem + QG_UMMA_K - 1) / QG_UMMA_K;
           for (int kk = 0; kk < nk; ++kk) {
             mma_i8(d_tmem, smem_desc_k_sw128(a_addr + kk * QG_UMMA_K), smem_desc_k_sw128(b_addr + kk * QG_UMMA_K),
-                   IDESC, (kb | kk) != 0 ? 1u : 0u);
+                   IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -416,8 +444,10 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
       const int acc = it & 1;
       if (!mbar_wait(&tfull[acc], (it >> 1) & 1, abort_flag, QG_TIMEOUT_NS)) break;
       tc_fence_after();
-      const int t_m = t / p.n_tiles;
-      const int n0 = (t % p.n_tiles) * BN;
+      const int split = t / mn_tiles, t_mn = t - split * mn_tiles;
+      const int t_m = t_mn / p.n_tiles;
+      const int n0 = (t_mn % p.n_tiles) * BN;
+      float* out_f32 = p.out_f32 != nullptr ? p.out_f32 + split * p.split_stride : nullptr;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       if (!POOL) {
         const int m_warp0 = t_m * QG_BM + quarter * 32;
@@ -427,7 +457,8 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
         for (int c = group; c < BN / Cfg::CW; c += G) {
           const int nb = n0 + c * Cfg::CW;
           if (nb >= p.N) break;  // warp-uniform
-          qg_epilogue_chunk<ROWCOL, Cfg::STAGE_PITCH>(p, tbase + c * Cfg::CW, m, row_ok, m_warp0, nb, stage, lane);
+          qg_epilogue_chunk<ROWCOL, Cfg::STAGE_PITCH>(p, tbase + c * Cfg::CW, m, row_ok, m_warp0, nb, stage, lane,
+                                                      out_f32);
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);

@@ -259,7 +259,7 @@ __global__ void embed_rows_kernel(const EmbedParams p) {
     if (t >= 0 && t < p.vocab) {
       v = __ldg(p.table + t * p.d + c);
     } else if (c == 0) {
-      atomicExch(p.err, 2);
+      atomicExch(p.err, 3);
     }
     if (p.addend != nullptr) v = __fadd_rn(v, __ldg(p.addend + (r % p.addend_rows) * p.d + c));
     p.out[r * p.ld_out + c] = v;

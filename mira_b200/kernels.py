@@ -164,6 +164,18 @@ def qgemm(M: int, N: int, K: int, A, lda: int, B, ldb: int, dq: _lib.Dequant, ep
     _lib.call("mira_cuda_qgemm", M, N, K, ptr(A), lda, ptr(B), ldb, C.byref(dq), C.byref(e))
 
 
+def qgemm_workspace(M: int, N: int, K: int) -> int:
+    """Workspace bytes of qgemm_splitk for this shape on the current device (0: no split)."""
+    return int(_lib.load().mira_cuda_qgemm_workspace(M, N, K))
+
+
+def qgemm_splitk(M: int, N: int, K: int, A, lda: int, B, ldb: int, dq: _lib.Dequant, epi: Epi, workspace,
+                 workspace_bytes: int) -> None:
+    e = epi.struct()
+    _lib.call("mira_cuda_qgemm_splitk", M, N, K, ptr(A), lda, ptr(B), ldb, C.byref(dq), C.byref(e), ptr(workspace),
+              workspace_bytes)
+
+
 def quantize_nchw_to_row4(x, n: int, c: int, h: int, w: int, scale: float, xq, row_entries: int, pad: int) -> None:
     _lib.call("mira_cuda_quantize_nchw_to_row4", ptr(x), n, c, h, w, float(np.float32(scale)), ptr(xq), row_entries,
               pad)

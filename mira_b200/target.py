@@ -64,6 +64,9 @@ class CudaDevice:
     def offset(self, buf, nbytes: int) -> DeviceSlice:
         return DeviceSlice(buf, nbytes)
 
+    def qgemm_workspace(self, m: int, n: int, k: int) -> int:
+        return K.qgemm_workspace(m, n, k)
+
     def h2d(self, dst, src: PinnedBuffer, nbytes: int) -> None:
         _lib.call("mira_cuda_h2d", ptr(dst), ptr(src), C.c_size_t(nbytes))
 
@@ -113,7 +116,11 @@ class CudaDevice:
             dq = K.dequant_channel(*a["dq"]) if len(a["dq"]) == 3 else K.dequant_rowcol(*a["dq"])
             e = a["epi"].struct()
             keep += [dq, e]
-            if k == "qgemm":
+            if k == "qgemm" and a.get("ws") is not None:
+                fn = L.mira_cuda_qgemm_splitk
+                args = (a["M"], a["N"], a["K"], ptr(a["A"]), a["lda"], ptr(a["B"]), a["ldb"], C.byref(dq), C.byref(e),
+                        ptr(a["ws"]), a["ws_bytes"])
+            elif k == "qgemm":
                 fn = L.mira_cuda_qgemm
                 args = (a["M"], a["N"], a["K"], ptr(a["A"]), a["lda"], ptr(a["B"]), a["ldb"], C.byref(dq), C.byref(e))
             elif k == "qconv2d_pool":
@@ -800,7 +807,16 @@ class Plan:
         wq = self._upload(K.matmul_weight(q))
         out = self._new_out(op.result)
         self._launch("qgemm", M=x.rows, N=n, K=kdim, A=A, lda=lda, B=wq, ldb=K.round_up(kdim, 16),
-                     dq=self._scales(a["x_scale"], a["w_scale"]), epi=self._epilogue(op, out))
+                     dq=self._scales(a["x_scale"], a["w_scale"]), epi=self._epilogue(op, out),
+                     **self._splitk_workspace(x.rows, n, kdim))
+
+    def _splitk_workspace(self, m: int, n: int, k: int) -> dict:
+        """Workspace arguments for a GEMM with too few output tiles to fill the GPU (split-K)."""
+        fn = getattr(self.dev, "qgemm_workspace", None)
+        nbytes = int(fn(m, n, k)) if fn is not None else 0
+        if nbytes <= 0:
+            return {}
+        return {"ws": self._alloc(nbytes), "ws_bytes": nbytes}
 
     def _qmatmul_group(self, ops) -> None:
         """One GEMM for quantized matmuls sharing their int8 input: weights, scales and per-column
@@ -828,7 +844,8 @@ class Plan:
             steps.append(K.Step(fn, "channel", bool(swapped), ptr=self._upload(K.pad_channels(np.concatenate(cols)))))
         epi = K.Epi(steps, out_f32=buf, ld_f32=total)
         self._launch("qgemm", M=x.rows, N=total, K=kdim, A=A, lda=lda, B=wq, ldb=K.round_up(kdim, 16),
-                     dq=self._scales(first.attrs["x_scale"], w_scale), epi=epi)
+                     dq=self._scales(first.attrs["x_scale"], w_scale), epi=epi,
+                     **self._splitk_workspace(x.rows, total, kdim))
         col = 0
         for op, w in zip(ops, widths):
             shape = tuple(op.result.type.shape)

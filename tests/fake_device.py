@@ -148,7 +148,23 @@ class FakeDevice:
         s64 = dq[0].view(np.float64, (N,))
         return (acc.astype(np.float64) * s64).astype(np.float32)
 
-    def _qgemm(self, M, N, K, A, lda, B, ldb, dq, epi):
+    def qgemm_workspace(self, M, N, K, sm_count=148):
+        """The library's split-K rule (mira_cuda.cu splitk_plan) for a 148-SM device."""
+        bn = 64 if N <= 64 else (128 if N <= 128 else 256)
+        tiles = -(-M // 128) * -(-N // bn)
+        num_kb = -(-K // 128)
+        if tiles * 2 > sm_count or num_kb < 8:
+            return 0
+        s = min(sm_count // tiles, num_kb // 4, 16)
+        if s < 2:
+            return 0
+        per = -(-num_kb // s)
+        s = -(-num_kb // per)
+        return s * M * N * 4 if s > 1 else 0
+
+    def _qgemm(self, M, N, K, A, lda, B, ldb, dq, epi, ws=None, ws_bytes=0):
+        if ws is not None:
+            assert ws_bytes == self.qgemm_workspace(M, N, K) and ws.nbytes >= ws_bytes
         a = A.view(np.int8, (M, lda))[:, :K]
         b = B.view(np.int8, (N, ldb))[:, :K]
         acc = ref.int_matmul(a, b.T)

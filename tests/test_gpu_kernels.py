@@ -63,7 +63,7 @@ def test_quantize_nchw_to_nhwc(cuda_device):
 
 # ------------------------------------------------------------------------------ qgemm
 
-def _run_qgemm(M, N, K_, steps_spec, seed, want_i8=True, rowcol=False):
+def _run_qgemm(M, N, K_, steps_spec, seed, want_i8=True, rowcol=False, splitk=False):
     K, DB = _k()
     rng = np.random.default_rng(seed)
     x_scale = float(rng.uniform(0.005, 0.05))
@@ -118,7 +118,14 @@ def _run_qgemm(M, N, K_, steps_spec, seed, want_i8=True, rowcol=False):
     yb = DB(M * N * 4)
     ldi = K.round_up(N, 16)
     qb = DB(M * ldi) if want_i8 else None
-    K.qgemm(M, N, K_, Ab, lda, Bb, lda, dq, K.Epi(steps, out_f32=yb, ld_f32=N, out_i8=qb, ld_i8=ldi, out_scale=out_scale))
+    epi = K.Epi(steps, out_f32=yb, ld_f32=N, out_i8=qb, ld_i8=ldi, out_scale=out_scale)
+    if splitk:
+        nbytes = K.qgemm_workspace(M, N, K_)
+        assert nbytes > 0, "shape expected to split"
+        ws = DB(nbytes)
+        K.qgemm_splitk(M, N, K_, Ab, lda, Bb, lda, dq, epi, ws, nbytes)
+    else:
+        K.qgemm(M, N, K_, Ab, lda, Bb, lda, dq, epi)
     got = yb.download((M, N), np.float32)
     got_q = qb.download((M, ldi), np.int8) if want_i8 else None
     return got, y, got_q, ref.quantize_activation(y, out_scale)
@@ -150,6 +157,26 @@ def test_qgemm_transcendental_epilogue_close(cuda_device, act):
 def test_qgemm_rowcol_sweep_semantics(cuda_device, M, N, K_):
     got, want, _, _ = _run_qgemm(M, N, K_, ["bias"], seed=7, want_i8=False, rowcol=True)
     _same_f32(got, want)
+
+
+@pytest.mark.parametrize("M,N,K_", [(1, 4096, 4096), (16, 4096, 4096), (128, 4096, 4096), (200, 300, 2048),
+                                    (3, 10, 1024), (64, 768, 3072)])
+@pytest.mark.parametrize("rowcol", [False, True])
+def test_qgemm_splitk_exact(cuda_device, M, N, K_, rowcol):
+    """Split-K (int32 partial sums per K range, added by a second kernel) gives the reference's
+    result bit for bit, like the unsplit GEMM."""
+    spec = ["bias", "relu"] if rowcol else ["bias", "residual", "relu"]
+    got, want, got_q, want_q = _run_qgemm(M, N, K_, spec, seed=M + K_, rowcol=rowcol, splitk=True)
+    _same_f32(got, want)
+    np.testing.assert_array_equal(got_q[:, :N], want_q)
+    assert not got_q[:, N:].any()
+
+
+def test_qgemm_splitk_workspace_rule(cuda_device):
+    K, _ = _k()
+    assert K.qgemm_workspace(65536, 768, 3072) == 0          # enough output tiles
+    assert K.qgemm_workspace(16, 4096, 512) == 0             # reduction too short to split
+    assert K.qgemm_workspace(1, 4096, 4096) > 0
 
 
 # ------------------------------------------------------------------------------ qconv2d

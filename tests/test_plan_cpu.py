@@ -221,3 +221,26 @@ def test_transformer_plan_matches_stored_reference_output():
     scales = np.array([op.attrs["x_scale"] for op in prog.graph.ops if op.kind == "qmatmul"])
     np.testing.assert_array_equal(scales, z["tf_x_scales"])
     np.testing.assert_allclose(prog.run({"tok": z["tf_tok"]}), z["tf_out"], rtol=1e-5, atol=1e-6)
+
+
+def test_skinny_qmatmul_plans_split_k():
+    """A quantized matmul with few output tiles and a long reduction gets a split-K workspace."""
+    from mira_b200.hostfw import import_mira
+    import_mira()
+    from mira import ir
+    from mira.types import TensorType as TT
+    rng = np.random.default_rng(4)
+    x = ir.Value(TT("f32", (4, 2048)), name="x")
+    g = ir.Graph("skinny", [x], [], [])
+    y = g.add("matmul", [x, g.const((rng.standard_normal((2048, 256)) * 0.02).astype(np.float32))], {})
+    y = g.add("relu", [g.add("add", [y, g.const(rng.standard_normal(256).astype(np.float32))], {})], {})
+    g.outputs = [y]
+    g.verify()
+    cal = [{"x": rng.standard_normal((4, 2048)).astype(np.float32)} for _ in range(2)]
+    cpu = compiler.compile_ir(g, "cpu", quantize="w8a8", calibration=cal, precision=None)
+    dev = FakeDevice()
+    cuda = compiler.compile_ir(g, "cuda", quantize="w8a8", calibration=cal, executor=dev)
+    launch = [l for l in cuda.segments[0].executable.plan.launches if l.kind == "qgemm"][0]
+    assert launch.args.get("ws") is not None and launch.args["ws_bytes"] > 0
+    feeds = {"x": rng.standard_normal((4, 2048)).astype(np.float32)}
+    np.testing.assert_array_equal(cuda.run(feeds), cpu.run(feeds))
