@@ -182,6 +182,17 @@ int mira_cuda_qgemm_splitk(int64_t M, int64_t N, int64_t K, const int8_t* A, int
                            const int8_t* B, int64_t ldb, const mira_dequant* dq,
                            const mira_epilogue* epi, void* workspace, int64_t workspace_bytes);
 
+/* mira_cuda_qgemm_splitk without a caller workspace and without allocating anything: the partial
+ * sums go to a fixed 8 MiB scratch array inside the library (one per device; its address is looked
+ * up once when the device is set up, so call mira_cuda_set_device before any stream capture).
+ * Shapes whose partial sums need more than 8 MiB (mira_cuda_qgemm_workspace() > 8 MiB) return
+ * MIRA_CUDA_EINVAL.  Nothing in the scratch has to start at zero.  All calls on a device share the
+ * scratch: calls that overlap in time (other streams, concurrently replayed graphs) race.
+ * No counterpart in the reference (it has no device memory). */
+int mira_cuda_qgemm_splitk_static(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda,
+                                  const int8_t* B, int64_t ldb, const mira_dequant* dq,
+                                  const mira_epilogue* epi);
+
 /* W8A8 convolution as an implicit GEMM over int8 activations, reference ops.py:630-634
  * (_qconv2d_ref, through _conv2d_ref ops.py:265-276 with groups = 1).
  * x: MIRA_LAYOUT_NHWC int8 [n, h, w, cp] (cp 4 or a multiple of 16) with weights int8 [o, ldw],

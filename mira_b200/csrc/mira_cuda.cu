@@ -21,6 +21,11 @@
 // mira_cuda_sync.  One copy per device (module global).
 __device__ int g_mira_kernel_error;
 
+// Scratch of mira_cuda_qgemm_splitk_static: the split-K partial sums of one call.  A fixed module
+// array (8 MiB), so that entry point allocates nothing; every call on the device shares it.
+constexpr int64_t kStaticSplitkBytes = int64_t(8) << 20;
+__device__ __align__(256) int32_t g_mira_splitk_scratch[kStaticSplitkBytes / sizeof(int32_t)];
+
 namespace mira {
 
 namespace {
@@ -28,6 +33,7 @@ namespace {
 constexpr int kMaxDevices = 16;
 DeviceState g_devices[kMaxDevices];
 int* g_err_ptr[kMaxDevices];
+int32_t* g_splitk_scratch[kMaxDevices];   // device address of g_mira_splitk_scratch, per device
 std::mutex g_init_mutex;
 thread_local int t_device = -1;
 thread_local std::string t_last_error;
@@ -53,6 +59,9 @@ int init_device(int d) {
   void* err_ptr = nullptr;
   MIRA_CUDA_TRY(cudaGetSymbolAddress(&err_ptr, g_mira_kernel_error), "cudaGetSymbolAddress(error record)");
   g_err_ptr[d] = static_cast<int*>(err_ptr);
+  void* scratch = nullptr;
+  MIRA_CUDA_TRY(cudaGetSymbolAddress(&scratch, g_mira_splitk_scratch), "cudaGetSymbolAddress(split-K scratch)");
+  g_splitk_scratch[d] = static_cast<int32_t*>(scratch);
   const int zero = 0;
   MIRA_CUDA_TRY(cudaMemcpyToSymbol(g_mira_kernel_error, &zero, sizeof(int)), "clear error record");
   if (g_encode_tiled == nullptr) {
@@ -1030,4 +1039,22 @@ extern "C" int mira_cuda_absmax_f32(int64_t n0, int64_t n1, int64_t n2, int64_t 
   const int threads = 256;
   absmax_view_kernel<<<grid_for(dev, (total / n3) * 32, threads), threads, 0, dev->stream>>>(p);
   return after_launch("absmax_view_kernel");
+}
+
+extern "C" int mira_cuda_qgemm_splitk_static(int64_t M, int64_t N, int64_t K, const int8_t* A, int64_t lda,
+                                             const int8_t* B, int64_t ldb, const mira_dequant* dq,
+                                             const mira_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  const int rc = qgemm_check(M, N, K, lda, ldb);
+  if (rc != MIRA_CUDA_OK) return rc;
+  if (M == 0) return MIRA_CUDA_OK;
+  int splits, kb_per;
+  splitk_plan(M, N, K, dev->sm_count, splits, kb_per);
+  const int64_t need = splits > 1 ? int64_t(splits) * M * N * int64_t(sizeof(int32_t)) : 0;
+  MIRA_CHECK_ARG(need <= kStaticSplitkBytes, "split-K partial sums exceed the 8 MiB static scratch");
+  int32_t* scratch = g_splitk_scratch[dev->device];
+  MIRA_CHECK_ARG(splits <= 1 || scratch != nullptr, "static split-K scratch not set up for this device");
+  // nothing in the scratch needs clearing: every K range writes its whole M x N slice before the
+  // finishing kernel reads it
+  return qgemm_run(dev, M, N, K, A, lda, B, ldb, dq, epi, splits, kb_per, scratch);
 }
