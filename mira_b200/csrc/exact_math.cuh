@@ -51,6 +51,87 @@ __device__ __forceinline__ float div_by_scale(float y, float s, float rcp, float
   return __fmaf_rn(res, rcp, q0);
 }
 
+// ---- packed f32x2 arithmetic (sm_100): two independent IEEE single-precision operations per
+// instruction, each rounded to nearest like the scalar __fadd_rn / __fmul_rn / __fmaf_rn.
+typedef unsigned long long f2_t;
+
+__device__ __forceinline__ f2_t f2(float lo, float hi) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(f2_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
+  f2_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_sub(f2_t a, f2_t b) {
+  f2_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_mul(f2_t a, f2_t b) {
+  f2_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
+  f2_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// The dequant of 4 accumulators, two per instruction: for each lane the same arithmetic as
+// dequant_fast with the uncertainty interval P +- A*hi*2^-40 (its sign only swaps the ends).
+// Sets bits of `slow` (shifted by `bit`) for elements that need the exact f64 path (|acc| >= 2^22,
+// or a result within the interval of an f32 rounding boundary); checked on 3e8 random cases on
+// the CPU.
+__device__ __forceinline__ void dequant4_x2(const uint32_t* r, const float4& hs, const float4& ls, float* v,
+                                            uint32_t& slow, int bit) {
+  const f2_t magic = f2(-12582912.0f, -12582912.0f);
+  const f2_t e40 = f2(0x1p-40f, 0x1p-40f), ne40 = f2(-0x1p-40f, -0x1p-40f);
+  const float hv[4] = {hs.x, hs.y, hs.z, hs.w}, lv[4] = {ls.x, ls.y, ls.z, ls.w};
+#pragma unroll
+  for (int j = 0; j < 4; j += 2) {
+    const f2_t a = f2_add(f2(__int_as_float(0x4B400000 + static_cast<int32_t>(r[j])),
+                             __int_as_float(0x4B400000 + static_cast<int32_t>(r[j + 1]))), magic);
+    const f2_t h = f2(hv[j], hv[j + 1]);
+    const f2_t pl = f2_mul(a, f2(lv[j], lv[j + 1]));
+    const f2_t yl = f2_fma(a, h, f2_fma(a, f2_mul(h, ne40), pl));
+    const f2_t yh = f2_fma(a, h, f2_fma(a, f2_mul(h, e40), pl));
+    float a0, a1, l0, l1, h0, h1;
+    f2_split(a, a0, a1);
+    f2_split(yl, l0, l1);
+    f2_split(yh, h0, h1);
+    v[j] = l0;
+    v[j + 1] = l1;
+    slow |= ((l0 == h0) && (fabsf(a0) < 0x1p22f)) ? 0u : (1u << (bit + j));
+    slow |= ((l1 == h1) && (fabsf(a1) < 0x1p22f)) ? 0u : (2u << (bit + j));
+  }
+}
+
+// Requantization of 16 values, two per instruction: clip(round_half_even(RN(y / s)), -127, 127)
+// as bytes.  y is clamped to +-c127 = +-RN(127 s) first, so every quotient lies in [-127, 127]
+// after rounding and no clip is needed afterwards (RN(c127 / s) rounds to 127; infinities map to
+// +-127); then Markstein's correction of RN(y * RN(1/s)) and the 1.5 * 2^23 rounding add.
+// Checked against the reference formula on 3e8 random cases (ties, values next to the clip).
+__device__ __forceinline__ void requant16_x2(const float (&v)[16], float s, float rcp, float c127, uint32_t (&b)[16]) {
+  const f2_t r2 = f2(rcp, rcp), ns = f2(-s, -s), magic = f2(12582912.0f, 12582912.0f);
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    const f2_t y = f2(fminf(fmaxf(v[j], -c127), c127), fminf(fmaxf(v[j + 1], -c127), c127));
+    const f2_t q0 = f2_mul(y, r2);
+    const f2_t z = f2_fma(f2_fma(q0, ns, y), r2, q0);
+    float t0, t1;
+    f2_split(f2_add(z, magic), t0, t1);
+    b[j] = static_cast<uint32_t>(__float_as_int(t0));
+    b[j + 1] = static_cast<uint32_t>(__float_as_int(t1));
+  }
+}
+
 // clip(rint(z), -127, 127) as an int8 in the low byte of the returned word: clipping before
 // rounding is equivalent because +-127 are integers; z + 1.5*2^23 rounds z half-to-even into the
 // low mantissa bits.

@@ -39,6 +39,7 @@ thread_local int t_device = -1;
 thread_local std::string t_last_error;
 std::atomic<int64_t> g_launches{0};
 PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+PFN_cuTensorMapEncodeIm2col_v12000 g_encode_im2col = nullptr;
 
 int init_device(int d) {
   std::lock_guard<std::mutex> lock(g_init_mutex);
@@ -72,6 +73,15 @@ int init_device(int d) {
     if (q != cudaDriverEntryPointSuccess || fn == nullptr)
       return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
     g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  if (g_encode_im2col == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    MIRA_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q),
+                  "cudaGetDriverEntryPoint(cuTensorMapEncodeIm2col)");
+    if (q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeIm2col is not available from the driver");
+    g_encode_im2col = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(fn);
   }
   st.ready = true;
   return MIRA_CUDA_OK;
@@ -138,8 +148,9 @@ static int grid_for(const DeviceState* dev, int64_t work, int threads) {
 
 // ---------------------------------------------------------------- tensor maps
 
-static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t row_stride,
-                        uint32_t box_inner, uint32_t box_rows) {
+// 2-D int8 tiles for TMA: box_inner bytes of box_rows rows, swizzled (128 or 64 bytes).
+static int encode_2d_i8_sw(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t row_stride,
+                           uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return set_error(MIRA_CUDA_EINVAL, "TMA base not 16-byte aligned");
   if (row_stride % 16 != 0) return set_error(MIRA_CUDA_EINVAL, "TMA row stride not a multiple of 16 bytes");
   const cuuint64_t dims[2] = {inner_bytes, rows};
@@ -147,23 +158,48 @@ static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes
   const cuuint32_t box[2] = {box_inner, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-                                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return MIRA_CUDA_OK;
 }
 
+// im2col tiles of an NHWC int8 tensor [n, h, w, cp] for a square kernel with symmetric padding:
+// each load brings `bk` channels of one tap for 128 consecutive output pixels (zeros outside the
+// image), the bounding box of the traversal being [-pad, dim - 1 + pad - (k - 1) * dil] per
+// spatial dimension with the convolution's strides as traversal steps.
+static int encode_im2col_i8(CUtensorMap* map, const void* base, int64_t n, int64_t h, int64_t w, int64_t cp,
+                            int64_t k, int64_t stride_h, int64_t stride_w, int64_t pad, int64_t dil, int bk) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return set_error(MIRA_CUDA_EINVAL, "TMA base not 16-byte aligned");
+  const cuuint64_t dims[4] = {uint64_t(cp), uint64_t(w), uint64_t(h), uint64_t(n)};
+  const cuuint64_t strides[3] = {uint64_t(cp), uint64_t(w * cp), uint64_t(h * w * cp)};
+  const int lower[2] = {int(-pad), int(-pad)};
+  const int upper[2] = {int(pad - (k - 1) * dil), int(pad - (k - 1) * dil)};
+  const cuuint32_t estr[4] = {1, uint32_t(stride_w), uint32_t(stride_h), 1};
+  const CUresult r = g_encode_im2col(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, lower,
+                                     upper, uint32_t(bk), uint32_t(QG_BM), estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                     bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeIm2col failed (" + std::to_string(r) + ")");
+  return MIRA_CUDA_OK;
+}
+
+static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t row_stride,
+                        uint32_t box_inner, uint32_t box_rows) {
+  return encode_2d_i8_sw(map, base, inner_bytes, rows, row_stride, box_inner, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 // ---------------------------------------------------------------- qgemm dispatch
 
-template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false>
+template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK>
 static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, const QgParams& p_in) {
   QgParams p = p_in;
   if (p.k_splits < 1) {   // no split: one K range per output tile
     p.k_splits = 1;
     p.kb_per_split = p.num_kb;
   }
-  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL>;
-  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL>;
+  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK>;
+  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL, BK>;
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[dev->device]) {
     MIRA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM)),
@@ -196,6 +232,37 @@ static int launch_qgemm_bn(DeviceState* dev, const CUtensorMap& tmA, const CUten
 }
 
 static int pick_bn(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
+
+// im2col convolutions: K-blocks of 64 bytes (64-channel inputs) or 128 bytes; the stages fill
+// about 144 KB, 16 epilogue warps for short reductions, 8 for long ones.
+static int launch_qgemm_im2col(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, QgParams& p, int bn,
+                               int bk) {
+  const bool short_k = p.num_kb * bk <= 24 * 128;
+  if (bk == 64) {
+    switch (bn) {
+      case 64:
+        return short_k ? launch_qgemm_cfg<64, 12, QG_A_IM2COL, false, 4, false, 64>(dev, tmA, tmB, p)
+                       : launch_qgemm_cfg<64, 14, QG_A_IM2COL, false, 2, false, 64>(dev, tmA, tmB, p);
+      case 128:
+        return short_k ? launch_qgemm_cfg<128, 9, QG_A_IM2COL, false, 4, false, 64>(dev, tmA, tmB, p)
+                       : launch_qgemm_cfg<128, 10, QG_A_IM2COL, false, 2, false, 64>(dev, tmA, tmB, p);
+      default:
+        return short_k ? launch_qgemm_cfg<256, 6, QG_A_IM2COL, false, 4, false, 64>(dev, tmA, tmB, p)
+                       : launch_qgemm_cfg<256, 7, QG_A_IM2COL, false, 2, false, 64>(dev, tmA, tmB, p);
+    }
+  }
+  switch (bn) {
+    case 64:
+      return short_k ? launch_qgemm_cfg<64, 7, QG_A_IM2COL, false, 4>(dev, tmA, tmB, p)
+                     : launch_qgemm_cfg<64, 8, QG_A_IM2COL, false, 2>(dev, tmA, tmB, p);
+    case 128:
+      return short_k ? launch_qgemm_cfg<128, 5, QG_A_IM2COL, false, 4>(dev, tmA, tmB, p)
+                     : launch_qgemm_cfg<128, 6, QG_A_IM2COL, false, 2>(dev, tmA, tmB, p);
+    default:
+      return short_k ? launch_qgemm_cfg<256, 3, QG_A_IM2COL, false, 4>(dev, tmA, tmB, p)
+                     : launch_qgemm_cfg<256, 4, QG_A_IM2COL, false, 2>(dev, tmA, tmB, p);
+  }
+}
 
 static int fill_epilogue(QgParams& p, const mira_dequant* dq, const mira_epilogue* epi) {
   MIRA_CHECK_ARG(dq != nullptr && epi != nullptr, "dequant and epilogue descriptors are required");
@@ -244,6 +311,7 @@ static int fill_epilogue(QgParams& p, const mira_dequant* dq, const mira_epilogu
   p.q_scale = q.s;
   p.q_rcp = q.rcp;
   p.q_lim = q.lim;
+  p.q_c127 = 127.0f * q.s;
   p.err = device_err_ptr();
   return MIRA_CUDA_OK;
 }
@@ -659,6 +727,18 @@ extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, co
   p.n_tiles = int((o + bn - 1) / bn);
   CUtensorMap tmA, tmB;
   std::memset(&tmA, 0, sizeof(tmA));
+  // TMA im2col for NHWC inputs of 64k channels and square, symmetric kernels
+  if (x_layout == MIRA_LAYOUT_NHWC && cp % 64 == 0 && kh == kw && pad_h == pad_w && dil_h == dil_w &&
+      pad_h <= 127 && (kw - 1) * dil_w - pad_w <= 128 && stride_h <= 8 && stride_w <= 8 && (kw - 1) * dil_w < 65536) {
+    const int bk = cp % 128 == 0 ? 128 : 64;
+    p.num_kb = int(p.K / bk);
+    rc = encode_im2col_i8(&tmA, x, n, h, w, cp, kw, stride_h, stride_w, pad_w, dil_w, bk);
+    if (rc != MIRA_CUDA_OK) return rc;
+    rc = encode_2d_i8_sw(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), uint32_t(bk), uint32_t(bn),
+                         bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != MIRA_CUDA_OK) return rc;
+    return launch_qgemm_im2col(dev, tmA, tmB, p, bn, bk);
+  }
   rc = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, uint32_t(bn));
   if (rc != MIRA_CUDA_OK) return rc;
   if (x_layout == MIRA_LAYOUT_ROW4) return launch_qgemm_bn<QG_A_ROW4, false>(dev, tmA, tmB, p, bn);

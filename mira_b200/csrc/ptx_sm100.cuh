@@ -81,6 +81,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 
 // ------------------------------------------------------------------ TMA (no multicast anywhere)
 
+// im2col load of a 4-D NHWC tensor: the pixels of one tap for pixelsPerColumn consecutive output
+// positions starting at traversal position (w, h, n), channels [c, c + channelsPerPixel), the tap
+// given as (off_w, off_h); positions outside the tensor read as 0.  c * 1 byte is a multiple of 16.
+__device__ __forceinline__ void tma_load_im2col_4d(void* smem_dst, const CUtensorMap* map, int32_t c, int32_t w,
+                                                   int32_t h, int32_t n, uint16_t off_w, uint16_t off_h,
+                                                   uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)), "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -197,6 +210,18 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
   d |= static_cast<uint64_t>(1024 >> 4) << 32;         // SBO            [32, 46)
   d |= static_cast<uint64_t>(1) << 46;                 // version        [46, 48)
   d |= static_cast<uint64_t>(2) << 61;                 // SWIZZLE_128B   [61, 64)
+  return d;
+}
+
+// The same for K-major operands in 64-byte rows with the 64-byte swizzle (8-row groups 512 bytes
+// apart): the A/B stages of 64-byte K-blocks.
+__device__ __forceinline__ uint64_t smem_desc_k_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);   // start address  [0, 14)
+  d |= static_cast<uint64_t>(1) << 16;                 // LBO            [16, 30)
+  d |= static_cast<uint64_t>(512 >> 4) << 32;          // SBO            [32, 46)
+  d |= static_cast<uint64_t>(1) << 46;                 // version        [46, 48)
+  d |= static_cast<uint64_t>(4) << 61;                 // SWIZZLE_64B    [61, 64)
   return d;
 }
 

@@ -33,7 +33,11 @@ constexpr int QG_BK = 128;               // K bytes per stage = one 128-byte swi
 constexpr int QG_UMMA_K = 32;            // K per tcgen05.mma kind::i8
 constexpr uint64_t QG_TIMEOUT_NS = 2000000000ull;
 
-enum QgAMode { QG_A_TMA = 0, QG_A_GATHER16 = 1, QG_A_GATHER4 = 2, QG_A_ROW4 = 3 };
+enum QgAMode { QG_A_TMA = 0, QG_A_GATHER16 = 1, QG_A_GATHER4 = 2, QG_A_ROW4 = 3, QG_A_IM2COL = 4 };
+
+// A operand comes from TMA (2-D tiles of a row-major matrix, or im2col tiles of an NHWC tensor)
+// rather than from the cp.async gather warps.
+constexpr bool qg_a_by_tma(int amode) { return amode == QG_A_TMA || amode == QG_A_IM2COL; }
 
 struct QgConv {
   int n, h, w, cp;      // input NHWC (cp = padded channels)
@@ -66,6 +70,7 @@ struct QgParams {
   int8_t* out_i8;
   int64_t ld_i8;
   float q_scale, q_rcp, q_lim;   // requant divisor, RN32(1/divisor), 256 * divisor
+  float q_c127;                  // RN32(127 * divisor): the clamp of the packed requantization
   int* err;
   // fused max pooling (POOL kernels only): window pool_p, stride pool_s, padding pool_pad holding
   // pool_pad_value; a tile is pool_t x pool_t pooled pixels whose conv inputs form a
@@ -89,15 +94,15 @@ __device__ __forceinline__ void pool_row_pixel(const QgParams& p, int t_m, int r
   valid = r < p.pool_span * p.pool_span && cy >= 0 && cy < p.g.oh && cx >= 0 && cx < p.g.ow;
 }
 
-template <int BN, int STAGES, int AMODE, int G, bool POOL = false>
+template <int BN, int STAGES, int AMODE, int G, bool POOL = false, int BK = QG_BK>
 struct QgCfg {
-  static constexpr int A_BYTES = QG_BM * QG_BK;
-  static constexpr int B_BYTES = BN * QG_BK;
+  static constexpr int A_BYTES = QG_BM * BK;
+  static constexpr int B_BYTES = BN * BK;
   static constexpr int CW = 16;                       // epilogue chunk width (columns)
   static constexpr int EPI_WARP0 = 2;
   static constexpr int EPI_WARPS = 4 * G;
   static constexpr int GATHER_WARP0 = EPI_WARP0 + EPI_WARPS;
-  static constexpr int THREADS = 32 * (GATHER_WARP0 + (AMODE == QG_A_TMA ? 0 : 4));
+  static constexpr int THREADS = 32 * (GATHER_WARP0 + (qg_a_by_tma(AMODE) ? 0 : 4));
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   // per epilogue warp: a 32-row x 16-column f32 staging block (row pitch 20 floats)
@@ -110,6 +115,7 @@ struct QgCfg {
   static_assert(!POOL || (AMODE != 0 && BN == 64), "fused pooling: convolutions with at most 64 channels");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(BK == 128 || (BK == 64 && AMODE == QG_A_IM2COL), "64-byte K-blocks: im2col convolutions only");
 };
 
 // Bounded wait that ignores the abort flag: used only to let in-flight copies land before exit.
@@ -221,6 +227,23 @@ __device__ __forceinline__ void qg_apply_step(const mira_epi_step& st, const flo
   }
 }
 
+// A binary step on 16 values: add/sub/mul two lanes per instruction, the others one by one.
+__device__ __forceinline__ void qg_apply_binary(const mira_epi_step& st, const float (&o)[16], float (&v)[16]) {
+  if (st.op == MIRA_EPI_ADD || st.op == MIRA_EPI_SUB || st.op == MIRA_EPI_MUL) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const f2_t x = f2(v[j], v[j + 1]), y = f2(o[j], o[j + 1]);
+      f2_t r;
+      if (st.op == MIRA_EPI_ADD) r = f2_add(x, y);                // commutative: swapped gives the same
+      else if (st.op == MIRA_EPI_MUL) r = f2_mul(x, y);
+      else r = st.swapped ? f2_sub(y, x) : f2_sub(x, y);
+      f2_split(r, v[j], v[j + 1]);
+    }
+    return;
+  }
+  qg_apply_step(st, o, v);
+}
+
 // The whole epilogue of one 16-column chunk of this warp's 32 rows.  Everything that does not
 // depend on the accumulator (dequant scales, the first binary operand) is loaded before the TMEM
 // read so the two latencies overlap.  In raw mode (split-K partial sums) the int32 accumulators
@@ -251,10 +274,20 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
       split_rowcol(rs, cs, hs[j], ls[j]);
     }
   }
-  int first = 0;
-  while (first < p.n_steps && p.steps[first].operand == MIRA_OPND_NONE) ++first;
-  float o[16];
-  if (first < p.n_steps) qg_operand(p, p.steps[first], m, row_ok, nb, full_chunk, o);
+  // one operand that reads memory is fetched before the accumulator so its latency overlaps the
+  // TMEM read: a full-tensor operand (a residual in DRAM) if there is one, else the first
+  // per-channel or per-row one
+  int mem0 = -1;
+  for (int s = 0; s < p.n_steps; ++s) {
+    const int kind = p.steps[s].operand;
+    if (kind == MIRA_OPND_FULL) {
+      mem0 = s;
+      break;
+    }
+    if (mem0 < 0 && (kind == MIRA_OPND_CHANNEL || kind == MIRA_OPND_ROW)) mem0 = s;
+  }
+  float o0[16];
+  if (mem0 >= 0) qg_operand(p, p.steps[mem0], m, row_ok, nb, full_chunk, o0);
 
   uint32_t r[16];
   tmem_ld_32x32b_x16(taddr, r);
@@ -263,10 +296,9 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
   float v[16];
   uint32_t slow = 0;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const bool ok = dequant_fast(static_cast<int32_t>(r[j]), hs[j], ls[j], v[j]);
-    slow |= ok ? 0u : (1u << j);
-  }
+  for (int q = 0; q < 4; ++q)
+    dequant4_x2(r + 4 * q, make_float4(hs[4 * q], hs[4 * q + 1], hs[4 * q + 2], hs[4 * q + 3]),
+                make_float4(ls[4 * q], ls[4 * q + 1], ls[4 * q + 2], ls[4 * q + 3]), v + 4 * q, slow, 4 * q);
   if (__any_sync(0xffffffffu, slow != 0)) {   // rare: about 2 elements in 10^5
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -291,20 +323,23 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
       }
       continue;
     }
-    if (s != first) qg_operand(p, st, m, row_ok, nb, full_chunk, o);
-    qg_apply_step(st, o, v);
+    if (s == mem0) {
+      qg_apply_binary(st, o0, v);
+    } else {
+      float o[16];
+      qg_operand(p, st, m, row_ok, nb, full_chunk, o);
+      qg_apply_binary(st, o, v);
+    }
   }
 
   if (out_f32 != nullptr) qg_store_f32<PITCH>(p, v, m, row_ok, m_warp0, nb, full_chunk, stage, lane, out_f32);
   if (p.out_i8 != nullptr && row_ok && nb < p.ld_i8) {
     uint32_t b[16];
-    if (full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) b[j] = round_clip_i8(div_by_scale(v[j], p.q_scale, p.q_rcp, p.q_lim));
-    } else {
+    requant16_x2(v, p.q_scale, p.q_rcp, p.q_c127, b);
+    if (!full_chunk) {
 #pragma unroll
       for (int j = 0; j < 16; ++j)
-        b[j] = (nb + j < p.N) ? round_clip_i8(div_by_scale(v[j], p.q_scale, p.q_rcp, p.q_lim)) : 0u;
+        if (nb + j >= p.N) b[j] = 0u;
     }
     *reinterpret_cast<uint4*>(p.out_i8 + static_cast<int64_t>(m) * p.ld_i8 + nb) =
         make_uint4(pack4_i8(b[0], b[1], b[2], b[3]), pack4_i8(b[4], b[5], b[6], b[7]),
@@ -314,11 +349,11 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
 
 // ---------------------------------------------------------------- the kernel
 
-template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false>
-__global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
+template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK>
+__global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS, 1)
     qgemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ QgParams p) {
-  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL>;
+  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK>;
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
   constexpr uint32_t IDESC = idesc_i8(QG_BM, BN);
@@ -342,7 +377,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], AMODE == QG_A_TMA ? 1 : 1 + 128);
+      mbar_init(&full[s], qg_a_by_tma(AMODE) ? 1 : 1 + 128);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -355,7 +390,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmB);
-    if (AMODE == QG_A_TMA) tma_prefetch_desc(&tmA);
+    if (qg_a_by_tma(AMODE)) tma_prefetch_desc(&tmA);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
@@ -381,11 +416,30 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
         const int m0 = (t_mn / p.n_tiles) * QG_BM;
         const int n0 = (t_mn % p.n_tiles) * BN;
         const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        // im2col: traversal position of the tile's first output pixel
+        int iw0 = 0, ih0 = 0, img0 = 0;
+        if (AMODE == QG_A_IM2COL) {
+          const int hw = p.g.oh * p.g.ow;
+          img0 = m0 / hw;
+          const int rem = m0 - img0 * hw;
+          const int oy = rem / p.g.ow;
+          iw0 = (rem - oy * p.g.ow) * p.g.sw - p.g.pw;
+          ih0 = oy * p.g.sh - p.g.ph;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], (AMODE == QG_A_TMA ? A_BYTES : 0) + B_BYTES);
-          if (AMODE == QG_A_TMA) tma_load_2d(sA + stage * A_BYTES, &tmA, kb * QG_BK, m0, &full[stage]);
-          tma_load_2d(sB + stage * B_BYTES, &tmB, kb * QG_BK, n0, &full[stage]);
+          mbar_arrive_expect_tx(&full[stage], (qg_a_by_tma(AMODE) ? A_BYTES : 0) + B_BYTES);
+          if (AMODE == QG_A_TMA) tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, m0, &full[stage]);
+          if (AMODE == QG_A_IM2COL) {
+            // K-block kb = channels [c0, c0 + BK) of tap (i, j): k = (i * kw + j) * cp + c
+            const int kbyte = kb * BK;
+            const int tap = kbyte / p.g.cp;
+            const int c0 = kbyte - tap * p.g.cp;
+            const int ti = tap / p.g.kw, tj = tap - ti * p.g.kw;
+            tma_load_im2col_4d(sA + stage * A_BYTES, &tmA, c0, iw0, ih0, img0, static_cast<uint16_t>(tj * p.g.dw),
+                               static_cast<uint16_t>(ti * p.g.dh), &full[stage]);
+          }
+          tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, n0, &full[stage]);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -414,14 +468,16 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
         const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
-          if (AMODE != QG_A_TMA) fence_proxy_async_smem();  // A was written by cp.async (generic proxy)
+          if (!qg_a_by_tma(AMODE)) fence_proxy_async_smem();  // A was written by cp.async (generic proxy)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
-          const int rem = p.K - kb * QG_BK;
-          const int nk = rem >= QG_BK ? QG_BK / QG_UMMA_K : (rem + QG_UMMA_K - 1) / QG_UMMA_K;
+          const int rem = p.K - kb * BK;
+          const int nk = rem >= BK ? BK / QG_UMMA_K : (rem + QG_UMMA_K - 1) / QG_UMMA_K;
           for (int kk = 0; kk < nk; ++kk) {
-            mma_i8(d_tmem, smem_desc_k_sw128(a_addr + kk * QG_UMMA_K), smem_desc_k_sw128(b_addr + kk * QG_UMMA_K),
+            const uint32_t ao = a_addr + kk * QG_UMMA_K, bo = b_addr + kk * QG_UMMA_K;
+            mma_i8(d_tmem, BK == 64 ? smem_desc_k_sw64(ao) : smem_desc_k_sw128(ao),
+                   BK == 64 ? smem_desc_k_sw64(bo) : smem_desc_k_sw128(bo),
                    IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
@@ -529,7 +585,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL>::THREADS, 1)
         }
       }
     }
-  } else if (AMODE != QG_A_TMA && warp >= Cfg::GATHER_WARP0) {
+  } else if (!qg_a_by_tma(AMODE) && warp >= Cfg::GATHER_WARP0) {
     // ------------------------------------------------ im2col gather of A (convolutions)
     const int row = threadIdx.x - 32 * Cfg::GATHER_WARP0;
     const QgConv& g = p.g;

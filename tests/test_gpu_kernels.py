@@ -229,6 +229,15 @@ def _run_qconv(n, c, h, w, o, kh, kw, stride, pad, dil=(1, 1), spec=("bias", "re
     dict(n=1, c=256, h=7, w=7, o=512, kh=3, kw=3, stride=(1, 1), pad=(1, 1)),
     dict(n=2, c=32, h=10, w=10, o=48, kh=3, kw=3, stride=(1, 1), pad=(2, 2), dil=(2, 2)),
     dict(n=2, c=40, h=9, w=9, o=24, kh=1, kw=1, stride=(1, 1), pad=(0, 0)),
+    # TMA im2col path (channels a multiple of 64, square kernels, symmetric padding)
+    dict(n=2, c=64, h=12, w=12, o=64, kh=3, kw=3, stride=(1, 1), pad=(2, 2), dil=(2, 2)),
+    dict(n=2, c=192, h=9, w=9, o=96, kh=3, kw=3, stride=(1, 1), pad=(1, 1)),
+    dict(n=3, c=128, h=11, w=11, o=64, kh=5, kw=5, stride=(2, 2), pad=(2, 2)),
+    dict(n=5, c=64, h=9, w=7, o=128, kh=1, kw=1, stride=(1, 1), pad=(0, 0)),
+    dict(n=2, c=512, h=7, w=7, o=256, kh=3, kw=3, stride=(2, 2), pad=(1, 1)),
+    dict(n=4, c=64, h=20, w=20, o=32, kh=3, kw=3, stride=(1, 1), pad=(0, 0)),
+    # non-square kernel with 64 channels: the cp.async gather
+    dict(n=2, c=64, h=10, w=10, o=64, kh=1, kw=3, stride=(1, 1), pad=(0, 1)),
 ])
 def test_qconv2d_exact(cuda_device, case):
     got, want, got_q, want_q = _run_qconv(**case, seed=sum(v if isinstance(v, int) else 0 for v in case.values()))
