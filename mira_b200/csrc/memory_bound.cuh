@@ -85,25 +85,23 @@ __global__ void quantize_nchw_nhwc_kernel(const float* __restrict__ x, int64_t n
 // channels >= c).  One thread per entry; neighbouring threads read neighbouring pixels.
 __global__ void quantize_nchw_row4_kernel(const float* __restrict__ x, int n, int c, int h, int w, QuantScale q,
                                           int8_t* __restrict__ xq, int entries, int pad) {
-  // one warp per (image row, block of 32 entries); lane l quantizes pixel e0 - pad + l once (and
-  // lanes 0-2 the three pixels after the block) and the 4-pixel entries are assembled by shuffles
+  // blockIdx.y: image rows (n * h, strided over gridDim.y); each warp of the block: 32 entries of the
+  // row, lane l quantizes pixel e0 - pad + l once (lanes 0-2 also the three pixels after the
+  // block) and the 4-pixel entries are assembled by shuffles.  No integer division per element.
   const int lane = threadIdx.x & 31;
-  const int blocks = (entries + 31) / 32;
-  const int64_t total_warps = int64_t(n) * h * blocks;
-  const int64_t warps_per_grid = int64_t(gridDim.x) * (blockDim.x / 32);
-  for (int64_t wi = blockIdx.x * int64_t(blockDim.x / 32) + (threadIdx.x >> 5); wi < total_warps;
-       wi += warps_per_grid) {
-    const int blk = static_cast<int>(wi % blocks);
-    const int64_t row = wi / blocks;               // n * h + y
+  const int e0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
+  if (e0 >= entries) return;   // warp-uniform
+  const int64_t rows = int64_t(n) * h;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
     const int img = static_cast<int>(row / h);
     const int y = static_cast<int>(row - int64_t(img) * h);
-    const int e0 = blk * 32;
+    const float* base = x + (int64_t(img) * c * h + y) * w;
+    const int64_t plane = int64_t(h) * w;
     auto pixel_word = [&](int xx) -> uint32_t {
       uint32_t b[4];
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch)
-        b[ch] = (ch < c && xx >= 0 && xx < w) ? quant_byte(__ldg(x + ((int64_t(img) * c + ch) * h + y) * w + xx), q)
-                                              : 0u;
+        b[ch] = (ch < c && xx >= 0 && xx < w) ? quant_byte(__ldg(base + ch * plane + xx), q) : 0u;
       return pack4_i8(b[0], b[1], b[2], b[3]);
     };
     const uint32_t w0 = pixel_word(e0 - pad + lane);
@@ -123,61 +121,64 @@ __global__ void quantize_nchw_row4_kernel(const float* __restrict__ x, int n, in
 
 // ---------------------------------------------------------------- K5: max pooling (NHWC)
 
-// f32 input: one thread per (output pixel, 4 channels).  Padding pixels take `pad_value` (the
-// reference pads with -inf before pooling).  Writes f32 and/or the quantized int8 value.
+// f32 input.  blockIdx.y: output rows (n * oh, strided over gridDim.y); threadIdx.x: groups of 4
+// channels (strided over blockDim.x), threadIdx.y + blockIdx.x * blockDim.y: the output column.
+// Padding pixels take `pad_value` (the reference pads with -inf before pooling).  Writes f32
+// and/or the quantized int8 value.
 __global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, int w, int c, int64_t ldc,
                                    int size, int stride, int pad, float pad_value, int oh, int ow,
                                    float* __restrict__ out, int64_t ldo, int8_t* __restrict__ out_i8,
                                    int64_t ldo_i8, QuantScale q) {
   const int c4 = (c + 3) / 4;
-  const int64_t total = int64_t(n) * oh * ow * c4;
-  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
-       idx += int64_t(gridDim.x) * blockDim.x) {
-    const int cg = static_cast<int>(idx % c4);
-    const int64_t pix = idx / c4;
-    const int img = static_cast<int>(pix / (int64_t(oh) * ow));
-    const int rem = static_cast<int>(pix - int64_t(img) * oh * ow);
-    const int oy = rem / ow, ox = rem - (rem / ow) * ow;
-    float mx[4];
-    bool first = true;
-    const bool vec = (c % 4) == 0 && (ldc % 4) == 0;
-    for (int i = 0; i < size; ++i) {
-      const int iy = oy * stride + i - pad;
-      for (int j = 0; j < size; ++j) {
-        const int ix = ox * stride + j - pad;
-        float v[4];
-        if (iy < 0 || iy >= h || ix < 0 || ix >= w) {
-          v[0] = v[1] = v[2] = v[3] = pad_value;
-        } else {
-          const float* src = x + (int64_t(img) * h * w + int64_t(iy) * w + ix) * ldc + cg * 4;
-          if (vec) {
-            const float4 t = __ldg(reinterpret_cast<const float4*>(src));
-            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  const int ox = blockIdx.x * blockDim.y + threadIdx.y;
+  if (ox >= ow) return;
+  const bool vec = (c % 4) == 0 && (ldc % 4) == 0;
+  const int64_t rows = int64_t(n) * oh;
+  for (int64_t orow = blockIdx.y; orow < rows; orow += gridDim.y) {
+    const int img = static_cast<int>(orow / oh);
+    const int oy = static_cast<int>(orow - int64_t(img) * oh);
+    const int64_t pix = orow * ow + ox;
+    for (int cg = threadIdx.x; cg < c4; cg += blockDim.x) {
+      float mx[4];
+      bool first = true;
+      for (int i = 0; i < size; ++i) {
+        const int iy = oy * stride + i - pad;
+        for (int j = 0; j < size; ++j) {
+          const int ix = ox * stride + j - pad;
+          float v[4];
+          if (iy < 0 || iy >= h || ix < 0 || ix >= w) {
+            v[0] = v[1] = v[2] = v[3] = pad_value;
           } else {
+            const float* src = x + (int64_t(img) * h * w + int64_t(iy) * w + ix) * ldc + cg * 4;
+            if (vec) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(src));
+              v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+            } else {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) v[e] = (cg * 4 + e < c) ? src[e] : 0.0f;
+              for (int e = 0; e < 4; ++e) v[e] = (cg * 4 + e < c) ? src[e] : 0.0f;
+            }
           }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) mx[e] = first ? v[e] : np_maximum(mx[e], v[e]);
+          first = false;
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) mx[e] = first ? v[e] : np_maximum(mx[e], v[e]);
-        first = false;
       }
-    }
-    if (out != nullptr) {
-      float* dst = out + pix * ldo + cg * 4;
-      if (vec && (ldo % 4) == 0) {
-        *reinterpret_cast<float4*>(dst) = make_float4(mx[0], mx[1], mx[2], mx[3]);
-      } else {
+      if (out != nullptr) {
+        float* dst = out + pix * ldo + cg * 4;
+        if (vec && (ldo % 4) == 0) {
+          *reinterpret_cast<float4*>(dst) = make_float4(mx[0], mx[1], mx[2], mx[3]);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (cg * 4 + e < c) dst[e] = mx[e];
+          for (int e = 0; e < 4; ++e)
+            if (cg * 4 + e < c) dst[e] = mx[e];
+        }
       }
-    }
-    if (out_i8 != nullptr) {
-      uint32_t b[4];
+      if (out_i8 != nullptr) {
+        uint32_t b[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) b[e] = (cg * 4 + e < c) ? quant_byte(mx[e], q) : 0u;
-      *reinterpret_cast<uint32_t*>(out_i8 + pix * ldo_i8 + cg * 4) = pack4_i8(b[0], b[1], b[2], b[3]);
+        for (int e = 0; e < 4; ++e) b[e] = (cg * 4 + e < c) ? quant_byte(mx[e], q) : 0u;
+        *reinterpret_cast<uint32_t*>(out_i8 + pix * ldo_i8 + cg * 4) = pack4_i8(b[0], b[1], b[2], b[3]);
+      }
     }
   }
 }

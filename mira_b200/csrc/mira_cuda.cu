@@ -546,10 +546,12 @@ extern "C" int mira_cuda_quantize_nchw_to_row4(const float* x, int64_t n, int64_
   MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(xq) & 15) == 0, "int8 output must be 16-byte aligned");
   MIRA_CHECK_ARG(scale > 0.0f && std::isfinite(scale), "quantization scale must be positive");
   if (n == 0) return MIRA_CUDA_OK;
-  const int threads = 256;
-  quantize_nchw_row4_kernel<<<grid_for(dev, n * h * ((row_entries + 31) / 32) * 32, threads), threads, 0,
-                              dev->stream>>>(
-      x, int(n), int(c), int(h), int(w), make_qscale(scale), xq, int(row_entries), int(pad));
+  MIRA_CHECK_ARG(row_entries < (int64_t(1) << 24), "rows too long");
+  const int threads = 256;   // 8 warps of 32 entries
+  const int64_t rows = n * h;
+  const dim3 grid(unsigned((row_entries + 255) / 256), unsigned(rows < 65535 ? rows : 65535));
+  quantize_nchw_row4_kernel<<<grid, threads, 0, dev->stream>>>(x, int(n), int(c), int(h), int(w), make_qscale(scale),
+                                                               xq, int(row_entries), int(pad));
   return after_launch("quantize_nchw_row4_kernel");
 }
 
@@ -829,8 +831,13 @@ extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, 
   }
   MIRA_CHECK_ARG(x_f32 != nullptr && (out_f32 != nullptr || out_i8 != nullptr), "maxpool needs an input and an output");
   if (out_i8 != nullptr) MIRA_CHECK_ARG(ldc_out_i8 % 4 == 0 && ldc_out_i8 >= c && out_scale > 0.0f, "bad int8 output");
-  const int64_t work = n * oh * ow * ((c + 3) / 4);
-  maxpool_f32_kernel<<<grid_for(dev, work, threads), threads, 0, dev->stream>>>(
+  // threads: x = groups of 4 channels (at most 64), y = output columns; blocks: columns x rows
+  const int c4 = int((c + 3) / 4);
+  const int tx = c4 < 64 ? c4 : 64;
+  const int ty = threads / tx < 1 ? 1 : threads / tx;
+  const int64_t orows = n * oh;
+  const dim3 grid(unsigned((ow + ty - 1) / ty), unsigned(orows < 65535 ? orows : 65535));
+  maxpool_f32_kernel<<<grid, dim3(tx, ty), 0, dev->stream>>>(
       x_f32, int(n), int(h), int(w), int(c), ldc_in, int(size), int(stride), int(pad), pad_value, int(oh), int(ow),
       out_f32, ldc_out_f32, out_i8, ldc_out_i8, make_qscale(out_i8 != nullptr ? out_scale : 1.0f));
   return after_launch("maxpool_f32_kernel");
