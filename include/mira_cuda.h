@@ -61,8 +61,9 @@ extern "C" {
 /* int8 convolution input layouts */
 #define MIRA_LAYOUT_NHWC 0      /* [n, h, w, cp] */
 #define MIRA_LAYOUT_ROW4 1      /* row-expanded, for inputs of at most 4 channels: [n, h, entries, 16]
-                                   where entry e holds pixels e - pad_w .. e - pad_w + 3, 4 channels
-                                   each, 0 outside the image; weights [o, kh * 32] with
+                                   where entry e holds pixels s*e - pad_w .. s*e - pad_w + 3, 4 channels
+                                   each, 0 outside the image, s = the horizontal stride of the
+                                   convolution that reads it (1, 2 or 4); weights [o, kh * 32] with
                                    k = i * 32 + j * 4 + c (taps j >= kw and channels >= c are 0) */
 
 typedef struct mira_epi_step {
@@ -156,9 +157,11 @@ int mira_cuda_quantize_nchw_to_nhwc(const float* x, int64_t n, int64_t c, int64_
                                     float scale, int8_t* xq, int64_t cp);
 
 /* The same quantization into the MIRA_LAYOUT_ROW4 layout (c <= 4): `row_entries` entries per image
- * row, `pad` = the consumer convolution's horizontal padding. */
+ * row, `pad` and `entry_stride` = the consumer convolution's horizontal padding and stride (1, 2 or
+ * 4; a convolution with output width ow reads ow + 4 / entry_stride entries per row). */
 int mira_cuda_quantize_nchw_to_row4(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
-                                    float scale, int8_t* xq, int64_t row_entries, int64_t pad);
+                                    float scale, int8_t* xq, int64_t row_entries, int64_t pad,
+                                    int64_t entry_stride);
 
 /* W8A8 matmul, reference ops.py:616-620 (_qmatmul_ref) with the epilogue of ops.py:192-199:
  *   acc[m, n] = sum_k A[m, k] * B[n, k]   (exact int32)

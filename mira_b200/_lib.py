@@ -101,7 +101,7 @@ SIGNATURES: dict[str, tuple] = {
                                       _vp, _i64]),
     "mira_cuda_qgemm_splitk_static": (_i32, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, C.POINTER(Dequant),
                                              C.POINTER(Epilogue)]),
-    "mira_cuda_quantize_nchw_to_row4": (_i32, [_vp, _i64, _i64, _i64, _i64, _f32, _vp, _i64, _i64]),
+    "mira_cuda_quantize_nchw_to_row4": (_i32, [_vp, _i64, _i64, _i64, _i64, _f32, _vp, _i64, _i64, _i64]),
     "mira_cuda_qconv2d": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64,
                                  _i64, _i64, _i64, _i64, C.POINTER(Dequant), C.POINTER(Epilogue)]),
     "mira_cuda_qconv2d_maxpool": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64,

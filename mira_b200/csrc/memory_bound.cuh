@@ -83,11 +83,14 @@ __global__ void quantize_nchw_nhwc_kernel(const float* __restrict__ x, int64_t n
 // layout read by the ROW4 convolution gather: for every image row, `entries` 16-byte entries, entry
 // e holding pixels e - pad .. e - pad + 3 with 4 channels each (zero outside the image and for
 // channels >= c).  One thread per entry; neighbouring threads read neighbouring pixels.
+template <int S>
 __global__ void quantize_nchw_row4_kernel(const float* __restrict__ x, int n, int c, int h, int w, QuantScale q,
                                           int8_t* __restrict__ xq, int entries, int pad) {
   // blockIdx.y: image rows (n * h, strided over gridDim.y); each warp of the block: 32 entries of the
-  // row, lane l quantizes pixel e0 - pad + l once (lanes 0-2 also the three pixels after the
-  // block) and the 4-pixel entries are assembled by shuffles.  No integer division per element.
+  // row.  Entry e holds pixels S*e - pad .. S*e - pad + 3: lane l quantizes the S pixels that start
+  // its entry (lanes 0 .. 4/S - 2 also those of the entries after the block) and the entries are
+  // assembled from 4/S neighbouring lanes by shuffles.  No integer division per element.
+  constexpr int L = 4 / S;
   const int lane = threadIdx.x & 31;
   const int e0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
   if (e0 >= entries) return;   // warp-uniform
@@ -104,15 +107,21 @@ __global__ void quantize_nchw_row4_kernel(const float* __restrict__ x, int n, in
         b[ch] = (ch < c && xx >= 0 && xx < w) ? quant_byte(__ldg(base + ch * plane + xx), q) : 0u;
       return pack4_i8(b[0], b[1], b[2], b[3]);
     };
-    const uint32_t w0 = pixel_word(e0 - pad + lane);
-    const uint32_t w32 = lane < 3 ? pixel_word(e0 - pad + 32 + lane) : 0u;
-    uint32_t word[4];
-    word[0] = w0;
+    uint32_t own[S], extra[S];
 #pragma unroll
-    for (int k = 1; k < 4; ++k) {
-      const uint32_t down = __shfl_down_sync(0xffffffffu, w0, k);
-      const uint32_t tail = __shfl_sync(0xffffffffu, w32, (lane + k - 32) & 31);
-      word[k] = lane + k < 32 ? down : tail;
+    for (int j = 0; j < S; ++j) {
+      own[j] = pixel_word(S * (e0 + lane) - pad + j);
+      extra[j] = lane < L - 1 ? pixel_word(S * (e0 + 32 + lane) - pad + j) : 0u;
+    }
+    uint32_t word[4];
+#pragma unroll
+    for (int k = 0; k < L; ++k) {
+#pragma unroll
+      for (int j = 0; j < S; ++j) {
+        const uint32_t down = __shfl_down_sync(0xffffffffu, own[j], k);
+        const uint32_t tail = __shfl_sync(0xffffffffu, extra[j], (lane + k - 32) & 31);
+        word[k * S + j] = lane + k < 32 ? down : tail;
+      }
     }
     if (e0 + lane < entries)
       reinterpret_cast<uint4*>(xq)[row * entries + e0 + lane] = make_uint4(word[0], word[1], word[2], word[3]);

@@ -540,18 +540,29 @@ extern "C" int mira_cuda_quantize_nchw_to_nhwc(const float* x, int64_t n, int64_
 }
 
 extern "C" int mira_cuda_quantize_nchw_to_row4(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
-                                               float scale, int8_t* xq, int64_t row_entries, int64_t pad) {
+                                               float scale, int8_t* xq, int64_t row_entries, int64_t pad,
+                                               int64_t entry_stride) {
   MIRA_GET_DEVICE(dev);
   MIRA_CHECK_ARG(n >= 0 && c > 0 && c <= 4 && h > 0 && w > 0 && row_entries > 0 && pad >= 0, "bad quantize_row4 shape");
   MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(xq) & 15) == 0, "int8 output must be 16-byte aligned");
   MIRA_CHECK_ARG(scale > 0.0f && std::isfinite(scale), "quantization scale must be positive");
   if (n == 0) return MIRA_CUDA_OK;
   MIRA_CHECK_ARG(row_entries < (int64_t(1) << 24), "rows too long");
-  const int threads = 256;   // 8 warps of 32 entries
+  MIRA_CHECK_ARG(entry_stride == 1 || entry_stride == 2 || entry_stride == 4, "entry stride must be 1, 2 or 4");
+  const int64_t warps = (row_entries + 31) / 32;
+  const int threads = int(32 * (warps < 8 ? warps : 8));
   const int64_t rows = n * h;
-  const dim3 grid(unsigned((row_entries + 255) / 256), unsigned(rows < 65535 ? rows : 65535));
-  quantize_nchw_row4_kernel<<<grid, threads, 0, dev->stream>>>(x, int(n), int(c), int(h), int(w), make_qscale(scale),
-                                                               xq, int(row_entries), int(pad));
+  const dim3 grid(unsigned((warps * 32 + threads - 1) / threads), unsigned(rows < 65535 ? rows : 65535));
+  const QuantScale qs = make_qscale(scale);
+  if (entry_stride == 1)
+    quantize_nchw_row4_kernel<1><<<grid, threads, 0, dev->stream>>>(x, int(n), int(c), int(h), int(w), qs, xq,
+                                                                    int(row_entries), int(pad));
+  else if (entry_stride == 2)
+    quantize_nchw_row4_kernel<2><<<grid, threads, 0, dev->stream>>>(x, int(n), int(c), int(h), int(w), qs, xq,
+                                                                    int(row_entries), int(pad));
+  else
+    quantize_nchw_row4_kernel<4><<<grid, threads, 0, dev->stream>>>(x, int(n), int(c), int(h), int(w), qs, xq,
+                                                                    int(row_entries), int(pad));
   return after_launch("quantize_nchw_row4_kernel");
 }
 
@@ -692,7 +703,8 @@ static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t*
   if (x_layout == MIRA_LAYOUT_ROW4) {
     MIRA_CHECK_ARG(cp == 4 && kw <= 8 && dil_h == 1 && dil_w == 1,
                    "the row-expanded layout serves 4-channel inputs, kernel width <= 8, no dilation");
-    MIRA_CHECK_ARG(x_row_entries >= (ow - 1) * stride_w + 5, "row-expanded input has too few entries per row");
+    MIRA_CHECK_ARG(stride_w == 1 || stride_w == 2 || stride_w == 4, "row-expanded inputs: horizontal stride 1, 2 or 4");
+    MIRA_CHECK_ARG(x_row_entries >= ow + 4 / stride_w, "row-expanded input has too few entries per row");
   }
   const int64_t K = x_layout == MIRA_LAYOUT_ROW4 ? kh * 32 : kh * kw * cp;
   MIRA_CHECK_ARG(K <= 133000, "K too large for exact int32 accumulation of int8 products");

@@ -43,7 +43,7 @@ struct QgConv {
   int n, h, w, cp;      // input NHWC (cp = padded channels)
   int oh, ow;
   int kh, kw, sh, sw, ph, pw, dh, dw;
-  int row_entries;      // QG_A_ROW4: 16-byte entries per image row (entry e = pixels e - pw .. e - pw + 3)
+  int row_entries;      // QG_A_ROW4: 16-byte entries per image row (entry e = pixels sw*e - pw .. sw*e - pw + 3)
 };
 
 struct QgParams {
@@ -652,7 +652,8 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
             }
           }
         } else if (AMODE == QG_A_ROW4) {
-          // k = i * 32 + j * 4 + c: chunk (i, half) is entry (ox * sw + 4 * half) of input row iy0 + i
+          // k = i * 32 + j * 4 + c: chunk (i, half) is entry ox + (4 / sw) * half of input row iy0 + i
+          // (entries are laid out at the convolution's horizontal stride)
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const int i = kb * 4 + (c >> 1);
@@ -660,7 +661,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
             const bool v = row_ok && i < g.kh && static_cast<unsigned>(iy) < static_cast<unsigned>(g.h) &&
                            (c * 16 < kmax);
             const int8_t* src = p.A + ((static_cast<int64_t>(img) * g.h + iy) * g.row_entries +
-                                       ox * g.sw + 4 * (c & 1)) * 16;
+                                       ox + (4 / g.sw) * (c & 1)) * 16;
             cp_async_16(dst_row + ((c ^ swz) << 4), v ? src : p.A, v ? 16u : 0u);
           }
         } else {

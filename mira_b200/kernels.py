@@ -73,8 +73,9 @@ def conv_weight(q_oihw: np.ndarray, cp: Optional[int] = None) -> tuple[np.ndarra
 
 
 def row4_entries(ow: int, stride_w: int) -> int:
-    """16-byte entries per image row of the row-expanded layout for a conv with output width ow."""
-    return (int(ow) - 1) * int(stride_w) + 5
+    """16-byte entries per image row of the row-expanded layout read by a conv with output width ow
+    and horizontal stride stride_w (1, 2 or 4; entries are laid out at that stride)."""
+    return int(ow) + 4 // int(stride_w)
 
 
 def conv_weight_row4(q_oihw: np.ndarray) -> np.ndarray:
@@ -176,9 +177,10 @@ def qgemm_splitk(M: int, N: int, K: int, A, lda: int, B, ldb: int, dq: _lib.Dequ
               workspace_bytes)
 
 
-def quantize_nchw_to_row4(x, n: int, c: int, h: int, w: int, scale: float, xq, row_entries: int, pad: int) -> None:
+def quantize_nchw_to_row4(x, n: int, c: int, h: int, w: int, scale: float, xq, row_entries: int, pad: int,
+                          entry_stride: int = 1) -> None:
     _lib.call("mira_cuda_quantize_nchw_to_row4", ptr(x), n, c, h, w, float(np.float32(scale)), ptr(xq), row_entries,
-              pad)
+              pad, entry_stride)
 
 
 def qconv2d(n: int, h: int, w: int, cp: int, x, o: int, kh: int, kw: int, wq, ldw: int, stride, padding,

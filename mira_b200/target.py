@@ -105,7 +105,7 @@ class CudaDevice:
         elif k == "quantize_row4":
             fn = L.mira_cuda_quantize_nchw_to_row4
             args = (ptr(a["x"]), a["n"], a["c"], a["h"], a["w"], float(np.float32(a["scale"])), ptr(a["xq"]),
-                    a["row_entries"], a["pad"])
+                    a["row_entries"], a["pad"], a["stride"])
         elif k == "nchw_to_nhwc":
             fn = L.mira_cuda_nchw_to_nhwc_f32
             args = (ptr(a["x"]), a["n"], a["c"], a["h"], a["w"], ptr(a["y"]), a["ldc"])
@@ -641,10 +641,10 @@ class Plan:
                 row4 = self._row4_geometry(v)
                 dv.i8_scale = self.i8_req[v]
                 if row4 is not None:
-                    entries, pad = row4
+                    entries, pad, stride = row4
                     dv.i8, dv.i8_layout, dv.row_entries, dv.i8_ld = self._alloc(n * h * entries * 16), "row4", entries, 4
                     self._launch("quantize_row4", x=buf, n=n, c=c, h=h, w=w, scale=dv.i8_scale, xq=dv.i8,
-                                 row_entries=entries, pad=pad)
+                                 row_entries=entries, pad=pad, stride=stride)
                 else:
                     cp = 4 if c <= 4 else K.round_up(c, 16)
                     dv.i8, dv.i8_ld = self._alloc(n * h * w * cp, zero=True), cp
@@ -660,9 +660,9 @@ class Plan:
         return dv
 
     def _row4_geometry(self, v):
-        """(entries, pad) when every consumer of the int8 value of `v` is a convolution that can read
-        the row-expanded layout (at most 4 channels, kernel width <= 8, no dilation) with one common
-        horizontal geometry; None otherwise."""
+        """(entries, pad, stride) when every consumer of the int8 value of `v` is a convolution that can
+        read the row-expanded layout (at most 4 channels, kernel width <= 8, no dilation, horizontal
+        stride 1, 2 or 4) with one common horizontal geometry; None otherwise."""
         if v.type.shape[1] > 4:
             return None
         geo = None
@@ -673,10 +673,10 @@ class Plan:
                 continue
             stride, padding, dilation, groups = conv_attrs(op.attrs)
             kw = np.asarray(op.attrs["q"]).shape[3]
-            if groups != 1 or kw > 8 or tuple(dilation) != (1, 1) or op.inputs[0] is not v:
+            if groups != 1 or kw > 8 or tuple(dilation) != (1, 1) or op.inputs[0] is not v or stride[1] not in (1, 2, 4):
                 return None
             ow = op.result.type.shape[3]
-            g = (K.row4_entries(ow, stride[1]), padding[1])
+            g = (K.row4_entries(ow, stride[1]), padding[1], stride[1])
             if geo is not None and g != geo:
                 return None
             geo = g

@@ -94,19 +94,24 @@ class FakeDevice:
         q[..., :c] = ref.quantize_activation(x.view(np.float32, (n, c, h, w)), scale).transpose(0, 2, 3, 1)
         q[..., c:] = 0
 
-    def _quantize_row4(self, x, n, c, h, w, scale, xq, row_entries, pad):
-        q = np.zeros((n, h, w + 16 + 2 * pad, 4), np.int8)
+    def _quantize_row4(self, x, n, c, h, w, scale, xq, row_entries, pad, stride=1):
+        """Entry e of a row holds pixels stride*e - pad .. stride*e - pad + 3 (4 channels each)."""
+        q = np.zeros((n, h, stride * row_entries + 4 + 2 * pad, 4), np.int8)
         q[:, :, pad:pad + w, :c] = ref.quantize_activation(x.view(np.float32, (n, c, h, w)), scale).transpose(0, 2, 3, 1)
         out = xq.view(np.int8, (n, h, row_entries, 16))
+        first = stride * np.arange(row_entries)            # index of pixel stride*e - pad in q
         for k in range(4):
-            out[..., 4 * k:4 * k + 4] = q[:, :, k:k + row_entries, :]
+            out[..., 4 * k:4 * k + 4] = q[:, :, first + k, :]
 
     @staticmethod
-    def _conv_operands(x, n, h, w, cp, layout, row_entries, wq, o, kh, kw, ldw, pad_w):
+    def _conv_operands(x, n, h, w, cp, layout, row_entries, wq, o, kh, kw, ldw, pad_w, stride_w=1):
         """NCHW int8 input and OIHW weights, whatever the device layout."""
         if layout == 1:
             rows = x.view(np.int8, (n, h, row_entries, 16))
-            xn = rows[:, :, pad_w:pad_w + w, 0:4].transpose(0, 3, 1, 2)
+            full = np.zeros((n, h, stride_w * row_entries + 4, 4), np.int8)
+            for k in range(4):             # pixel stride*e - pad + k is byte group k of entry e
+                full[:, :, stride_w * np.arange(row_entries) + k, :] = rows[..., 4 * k:4 * k + 4]
+            xn = full[:, :, pad_w:pad_w + w, :].transpose(0, 3, 1, 2)
             wt = wq.view(np.int8, (o, ldw))[:, : kh * 32].reshape(o, kh, 8, 4)[:, :, :kw, :].transpose(0, 3, 1, 2)
             return xn, wt
         xn = x.view(np.int8, (n, h, w, cp)).transpose(0, 3, 1, 2)
@@ -171,7 +176,7 @@ class FakeDevice:
         self._epi(self._dequant(acc, dq, N), epi, M, N)
 
     def _qconv2d(self, n, h, w, cp, x, o, kh, kw, wq, ldw, stride, padding, dilation, dq, epi, layout=0, row_entries=0):
-        xn, wt = self._conv_operands(x, n, h, w, cp, layout, row_entries, wq, o, kh, kw, ldw, padding[1])
+        xn, wt = self._conv_operands(x, n, h, w, cp, layout, row_entries, wq, o, kh, kw, ldw, padding[1], stride[1])
         acc = ref.int_conv2d(xn, wt, stride, padding, dilation)       # [n, o, oh, ow]
         oh, ow = acc.shape[2:]
         rows = acc.transpose(0, 2, 3, 1).reshape(n * oh * ow, o)
@@ -179,7 +184,7 @@ class FakeDevice:
 
     def _qconv2d_pool(self, n, h, w, cp, x, o, kh, kw, wq, ldw, stride, padding, dilation, pool_size, pool_stride,
                       pool_pad, pool_pad_value, dq, epi, layout=0, row_entries=0):
-        xn, wt = self._conv_operands(x, n, h, w, cp, layout, row_entries, wq, o, kh, kw, ldw, padding[1])
+        xn, wt = self._conv_operands(x, n, h, w, cp, layout, row_entries, wq, o, kh, kw, ldw, padding[1], stride[1])
         acc = ref.int_conv2d(xn, wt, stride, padding, dilation)
         oh, ow = acc.shape[2:]
         rows = self._dequant(acc.transpose(0, 2, 3, 1).reshape(-1, o), dq, o)

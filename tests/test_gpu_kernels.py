@@ -363,6 +363,7 @@ def test_qconv2d_maxpool_fused_exact(cuda_device, case):
     dict(n=2, c=3, h=33, w=31, o=32, k=3, s=2, p=1),     # MobileNetV2 stem
     dict(n=3, c=1, h=28, w=28, o=16, k=3, s=1, p=1),
     dict(n=1, c=4, h=9, w=13, o=24, k=5, s=1, p=0),
+    dict(n=2, c=3, h=21, w=30, o=16, k=3, s=4, p=1),     # entries laid out at stride 4
 ])
 @pytest.mark.parametrize("pool", [False, True])
 def test_row4_layout_conv_exact(cuda_device, case, pool):
@@ -380,7 +381,7 @@ def test_row4_layout_conv_exact(cuda_device, case, pool):
     oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
     entries = K.row4_entries(ow, s)
     xb, xq = DB.from_array(x), DB(n * h * entries * 16)
-    K.quantize_nchw_to_row4(xb, n, c, h, w, x_scale, xq, entries, p)
+    K.quantize_nchw_to_row4(xb, n, c, h, w, x_scale, xq, entries, p, s)
     wq = K.conv_weight_row4(q)
     s64, hi, lo = K.scale_arrays(x_scale, w_scale)
     bufs = [DB.from_array(a) for a in (wq, s64, hi, lo, K.pad_channels(bias))]
