@@ -191,15 +191,17 @@ static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes
 
 // ---------------------------------------------------------------- qgemm dispatch
 
-template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK>
+template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK, int RKB = 0>
 static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, const QgParams& p_in) {
   QgParams p = p_in;
   if (p.k_splits < 1) {   // no split: one K range per output tile
     p.k_splits = 1;
     p.kb_per_split = p.num_kb;
   }
-  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK>;
-  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL, BK>;
+  if (RKB > 0 && (p.n_tiles != 1 || p.k_splits != 1 || p.num_kb > RKB))
+    return set_error(MIRA_CUDA_EINVAL, "resident-weight kernel used for a shape it does not cover");
+  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>;
+  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL, BK, RKB>;
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[dev->device]) {
     MIRA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM)),
@@ -241,6 +243,9 @@ static int launch_qgemm_im2col(DeviceState* dev, const CUtensorMap& tmA, const C
   if (bk == 64) {
     switch (bn) {
       case 64:
+        // one column tile of weights (N <= 64) of at most 16 K-blocks stays in shared memory
+        if (p.n_tiles == 1 && p.num_kb <= 16 && short_k)
+          return launch_qgemm_cfg<64, 12, QG_A_IM2COL, false, 4, false, 64, 16>(dev, tmA, tmB, p);
         return short_k ? launch_qgemm_cfg<64, 12, QG_A_IM2COL, false, 4, false, 64>(dev, tmA, tmB, p)
                        : launch_qgemm_cfg<64, 14, QG_A_IM2COL, false, 2, false, 64>(dev, tmA, tmB, p);
       case 128:
@@ -755,7 +760,11 @@ extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, co
   }
   rc = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, uint32_t(bn));
   if (rc != MIRA_CUDA_OK) return rc;
-  if (x_layout == MIRA_LAYOUT_ROW4) return launch_qgemm_bn<QG_A_ROW4, false>(dev, tmA, tmB, p, bn);
+  if (x_layout == MIRA_LAYOUT_ROW4) {
+    if (bn == 64 && p.n_tiles == 1 && p.num_kb <= 2)   // the stem's weights stay in shared memory
+      return launch_qgemm_cfg<64, 7, QG_A_ROW4, false, 4, false, QG_BK, 2>(dev, tmA, tmB, p);
+    return launch_qgemm_bn<QG_A_ROW4, false>(dev, tmA, tmB, p, bn);
+  }
   if (cp == 4) return launch_qgemm_bn<QG_A_GATHER4, false>(dev, tmA, tmB, p, bn);
   return launch_qgemm_bn<QG_A_GATHER16, false>(dev, tmA, tmB, p, bn);
 }

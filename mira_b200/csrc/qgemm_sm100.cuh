@@ -94,7 +94,9 @@ __device__ __forceinline__ void pool_row_pixel(const QgParams& p, int t_m, int r
   valid = r < p.pool_span * p.pool_span && cy >= 0 && cy < p.g.oh && cx >= 0 && cx < p.g.ow;
 }
 
-template <int BN, int STAGES, int AMODE, int G, bool POOL = false, int BK = QG_BK>
+// RKB > 0: the whole B operand (at most RKB K-blocks) stays in shared memory for the CTA's lifetime
+// (one output column tile, loaded once); the stages then carry A only.
+template <int BN, int STAGES, int AMODE, int G, bool POOL = false, int BK = QG_BK, int RKB = 0>
 struct QgCfg {
   static constexpr int A_BYTES = QG_BM * BK;
   static constexpr int B_BYTES = BN * BK;
@@ -111,7 +113,8 @@ struct QgCfg {
   static constexpr int POOL_PITCH = BN + 4;
   static constexpr int POOL_ROWS = 96;
   static constexpr int STAGING_BYTES = POOL ? 2 * POOL_ROWS * POOL_PITCH * 4 : EPI_WARPS * 32 * STAGE_PITCH * 4;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * (A_BYTES + B_BYTES) + STAGING_BYTES + 256;
+  static constexpr int B_REGION = RKB > 0 ? RKB * B_BYTES : STAGES * B_BYTES;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * A_BYTES + B_REGION + STAGING_BYTES + 256;
   static_assert(!POOL || (AMODE != 0 && BN == 64), "fused pooling: convolutions with at most 64 channels");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(SMEM <= 232448, "shared memory budget");
@@ -349,11 +352,11 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
 
 // ---------------------------------------------------------------- the kernel
 
-template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK>
-__global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS, 1)
+template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK, int RKB = 0>
+__global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::THREADS, 1)
     qgemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ QgParams p) {
-  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK>;
+  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>;
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
   constexpr uint32_t IDESC = idesc_i8(QG_BM, BN);
@@ -362,14 +365,15 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  float* staging = reinterpret_cast<float*>(sB + STAGES * B_BYTES);
+  float* staging = reinterpret_cast<float*>(sB + Cfg::B_REGION);
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(staging) + Cfg::STAGING_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* pool_bar = drain + 1;   // [2]: all epilogue threads wrote the tile buffer
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pool_bar + 2);
+  uint64_t* bres = pool_bar + 2;    // resident B landed (RKB > 0)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bres + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -387,6 +391,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
     mbar_init(drain, 1);
     mbar_init(&pool_bar[0], Cfg::EPI_THREADS);
     mbar_init(&pool_bar[1], Cfg::EPI_THREADS);
+    mbar_init(bres, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmB);
@@ -411,6 +416,11 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
+      if (RKB > 0 && blockIdx.x < num_tiles) {
+        // the whole B operand (one column tile, checked by the host) once for the CTA
+        mbar_arrive_expect_tx(bres, p.num_kb * B_BYTES);
+        for (int kb = 0; kb < p.num_kb; ++kb) tma_load_2d(sB + kb * B_BYTES, &tmB, kb * BK, 0, bres);
+      }
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const int split = t / mn_tiles, t_mn = t - split * mn_tiles;
         const int m0 = (t_mn / p.n_tiles) * QG_BM;
@@ -428,7 +438,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
         }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], (qg_a_by_tma(AMODE) ? A_BYTES : 0) + B_BYTES);
+          mbar_arrive_expect_tx(&full[stage], (qg_a_by_tma(AMODE) ? A_BYTES : 0) + (RKB > 0 ? 0 : B_BYTES));
           if (AMODE == QG_A_TMA) tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, m0, &full[stage]);
           if (AMODE == QG_A_IM2COL) {
             // K-block kb = channels [c0, c0 + BK) of tap (i, j): k = (i * kw + j) * cp + c
@@ -439,7 +449,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
             tma_load_im2col_4d(sA + stage * A_BYTES, &tmA, c0, iw0, ih0, img0, static_cast<uint16_t>(tj * p.g.dw),
                                static_cast<uint16_t>(ti * p.g.dh), &full[stage]);
           }
-          tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, n0, &full[stage]);
+          if (RKB == 0) tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, n0, &full[stage]);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -451,6 +461,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
           mbar_wait_drain(&full[idx % STAGES], (idx / STAGES) & 1);
         }
       }
+      if (RKB > 0 && blockIdx.x < num_tiles) mbar_wait_drain(bres, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
@@ -459,6 +470,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
+      if (RKB > 0 && blockIdx.x < num_tiles && !mbar_wait(bres, 0, abort_flag, QG_TIMEOUT_NS)) ok = false;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
         const int acc = it & 1;
         if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) break;
@@ -471,7 +483,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK>::THREADS
           if (!qg_a_by_tma(AMODE)) fence_proxy_async_smem();  // A was written by cp.async (generic proxy)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          const uint32_t b_addr = smem_u32(sB + (RKB > 0 ? kb : stage) * B_BYTES);
           const int rem = p.K - kb * BK;
           const int nk = rem >= BK ? BK / QG_UMMA_K : (rem + QG_UMMA_K - 1) / QG_UMMA_K;
           for (int kk = 0; kk < nk; ++kk) {
