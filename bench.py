@@ -183,6 +183,12 @@ def gemm_tops(n: int = 8192, iters: int = 5) -> float:
     return 2.0 * n ** 3 / (ms.value / iters * 1e-3) / 1e12
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the 20 convolution launches of one
+# batch-256 ResNet-18 pass, from one ncu capture of the current kernels: the denominator's traffic
+# counterpart of `achieved` (which is also per pass of those 20 launches).
+CONV_DRAM_BYTES_PER_PASS = 2.535e9
+
+
 def skinny_gemm(m: int, n: int = 4096, k: int = 4096, iters: int = 50) -> dict:
     """The GEMM sweep's skinny rows (config 2): M x 4096 x 4096 through mira_cuda_qgemm_splitk (split-K
     with a workspace when the output tiles cannot fill the GPU); HBM-bound, so also GB/s of the
@@ -412,7 +418,8 @@ def main() -> None:
                     "d2h_bytes_per_step": int(out.nbytes)},
             "roofline": {"bound": "tensor", "kernel": "qgemm_sm100_kernel (implicit-GEMM qconv2d, 20 launches/step)",
                          "achieved": achieved, "peak": peak, "unit": "TOPS",
-                         "frac": (achieved / peak) if peak else None, "traffic": None,
+                         "frac": (achieved / peak) if peak else None, "traffic": CONV_DRAM_BYTES_PER_PASS,
+                         "traffic_unit": "bytes per pass of the 20 conv launches (batch 256)",
                          "peak_source": f"2 x bf16_tflops of {src} (dense int8 issues at twice the bf16 rate)",
                          "conv_int8_ops_per_step": conv_ops, "conv_ms_per_step": conv_ms},
             "int8_gemm": {"shape": "8192^3", "tops": ours_gemm, "frac_of_peak": ours_gemm / peak if peak else None,
