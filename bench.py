@@ -3,6 +3,11 @@
 scaling over 1/2/4/8 GPUs, one process per GPU) plus the int8 GEMM throughput at 8192^3.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+                  [--workload resnet18|mobilenet_v2|mlp|transformer]
+
+The default workload is the headline (ResNet-18); the others are the remaining configurations of
+the same path (MobileNetV2 images/s, the MLP's samples/s, the transformer prefill's tokens/s) with
+the same JSON line.
 
 A step is one forward pass of a batch through the compiled MIRA program.  `value` times K steps
 on device-resident inputs (CUDA events on the library stream, max over ranks); `e2e` times the
@@ -28,10 +33,29 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# name -> metric, unit, config name, default batch, calibration (batch, count), items per batch row,
+# and the bounded sample the reference cpu path is timed on (builder options, batch, and the factor
+# that scales its rate to the full network: the transformer sample runs 1 of the 12 layers)
+WORKLOADS = {
+    "resnet18": dict(metric="w8a8 ResNet-18 img/s", unit="img/s", config="resnet18-w8a8-224", batch=256,
+                     calib_batch=8, n_calib=4, items_per_row=1, build_kw={}, cpu_batch=1, cpu_build_kw={},
+                     cpu_scale=1.0, cpu_note="one image per step"),
+    "mobilenet_v2": dict(metric="w8a8 MobileNetV2 img/s", unit="img/s", config="mobilenet_v2-w8a8-224", batch=256,
+                         calib_batch=8, n_calib=4, items_per_row=1, build_kw={}, cpu_batch=1, cpu_build_kw={},
+                         cpu_scale=1.0, cpu_note="one image per step"),
+    "mlp": dict(metric="w8a8 MLP samples/s", unit="samples/s", config="mlp-784-512-512-10", batch=256,
+                calib_batch=256, n_calib=8, items_per_row=1, build_kw={}, cpu_batch=256, cpu_build_kw={},
+                cpu_scale=1.0, cpu_note="one batch of 256 per step"),
+    "transformer": dict(metric="w8a8 transformer prefill tokens/s", unit="tokens/s",
+                        config="decoder-12x768-h12-mlp3072-vocab256-seq1024", batch=64, calib_batch=1, n_calib=4,
+                        items_per_row=1024, build_kw={}, cpu_batch=1, cpu_build_kw=dict(layers=1, seq=128),
+                        cpu_scale=1.0 / 12,
+                        cpu_note="one sequence of 128 tokens through 1 of the 12 layers per step; tokens/s "
+                                 "divided by 12 (layers; attention cost per token grows with the sequence, so "
+                                 "this overestimates the reference at 1024)"),
+}
 WORKLOAD = "resnet18"
-METRIC = "w8a8 ResNet-18 img/s"
-# int8 ops per image of ResNet-18 at 224x224 (2 x MACs of the 20 convs and the FC)
-RESNET18_CONV_MACS = None   # computed from the graph
+METRIC = WORKLOADS[WORKLOAD]["metric"]
 
 
 def _env_rank():
@@ -120,12 +144,13 @@ def conv_work(graph) -> tuple[int, int]:
     return conv, total
 
 
-def time_conv_kernels(exe, iters: int = 3) -> float:
-    """Average summed duration (ms) of the plan's qconv2d launches, each bracketed by CUDA events on
-    the library stream (one event pair per launch, eager launches)."""
+def time_kernels(exe, kinds, iters: int = 3) -> tuple[float, int]:
+    """(average summed duration in ms, count) of the plan's launches of the given kinds, each
+    bracketed by CUDA events on the library stream (one event pair per launch, eager launches)."""
     from mira_b200 import _lib
-    evs = []
-    idx = [i for i, l in enumerate(exe.plan.launches) if l.kind == "qconv2d"]
+    idx = [i for i, l in enumerate(exe.plan.launches) if l.kind in kinds]
+    if not idx:
+        return 0.0, 0
 
     def ev():
         p = C.c_void_p()
@@ -151,7 +176,7 @@ def time_conv_kernels(exe, iters: int = 3) -> float:
     for a, b in pairs:
         _lib.call("mira_cuda_event_destroy", a)
         _lib.call("mira_cuda_event_destroy", b)
-    return total / iters
+    return total / iters, len(idx)
 
 
 def gemm_tops(n: int = 8192, iters: int = 5) -> float:
@@ -254,43 +279,42 @@ def cublaslt_int8_tops(n: int = 8192) -> float | None:
         return None
 
 
-def reference_cpu_sample(batch: int, steps: int, warmup: int) -> dict:
+def reference_cpu_sample(steps: int, warmup: int, workload: str = WORKLOAD) -> dict:
     """The reference's own cpu W8A8 path (mira.compile_ir(..., "cpu", quantize="w8a8") then
-    CompiledProgram.run) on `batch` images per step; falls back to the oracle port when the
-    reference package is not importable."""
-    try:
-        from mira_b200 import configs
-        from mira_b200.hostfw import import_mira
-        import_mira()
-        kind = "reference"
-        prog = configs.compile_w8a8(WORKLOAD, batch, "cpu", n_calib=4, calib_batch=batch)
-        feeds = configs.random_inputs(prog.graph, 1)
-        run = lambda: prog.run(feeds)  # noqa: E731
-    except ImportError:
-        kind = "port"
-        raise
+    CompiledProgram.run) on the workload's bounded sample."""
+    w = WORKLOADS[workload]
+    from mira_b200 import configs
+    from mira_b200.hostfw import import_mira
+    import_mira()
+    batch = w["cpu_batch"]
+    prog = configs.compile_w8a8(workload, batch, "cpu", n_calib=w["n_calib"], calib_batch=batch,
+                                build_kw=w["cpu_build_kw"] or None)
+    feeds = configs.random_inputs(prog.graph, 1)
+    rows = int(prog.graph.inputs[0].type.shape[0])
+    items = rows * (prog.graph.inputs[0].type.shape[1] if w["items_per_row"] > 1 else 1)
     for _ in range(warmup):
-        run()
+        prog.run(feeds)
     t0 = time.perf_counter()
     for _ in range(steps):
-        run()
+        prog.run(feeds)
     dt = time.perf_counter() - t0
-    return {"value": batch * steps / dt, "unit": "img/s", "cores": os.cpu_count(), "kind": kind,
-            "sample": f"{steps} run(s) of a batch of {batch} image(s), reference cpu target "
-                      f"(NumPy golden model, OpenBLAS on all host cores), after {warmup} warm-up run(s)"}
+    return {"value": items * steps / dt * w["cpu_scale"], "unit": w["unit"], "cores": os.cpu_count(),
+            "kind": "reference", "ms_per_step": dt / steps * 1e3,
+            "sample": f"{steps} run(s) after {warmup} warm-up run(s), {w['cpu_note']}; reference cpu target "
+                      f"(NumPy golden model, OpenBLAS on all host cores)"}
 
 
 def run_reference(args) -> None:
     rank, world, _ = _env_rank()
     if rank != 0:
         return
-    sample_batch = 1
-    res = reference_cpu_sample(sample_batch, args.steps, args.warmup)
-    line = {"metric": METRIC, "value": res["value"], "unit": "img/s", "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sample_batch / res["value"],
+    w = WORKLOADS[args.workload]
+    res = reference_cpu_sample(args.steps, args.warmup, args.workload)
+    line = {"metric": w["metric"], "value": res["value"], "unit": w["unit"], "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "resnet18-w8a8-224", "batch_per_step": sample_batch,
-                       "note": "bounded sample of the batch-256 workload: each step is one image"},
+            "config": {"workload": w["config"], "batch_per_step": w["cpu_batch"],
+                       "note": f"bounded sample of the workload: {w['cpu_note']}"},
             "cpu_baseline": res, "e2e": {"value": res["value"], "unit": "img/s", "h2d_bytes_per_step": 0,
                                          "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -301,12 +325,16 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=256, help="images per GPU per step")
+    ap.add_argument("--batch", type=int, default=None, help="batch rows per GPU per step (workload default)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--calib-batch", type=int, default=8)
+    ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--calib-batch", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    wl = WORKLOADS[args.workload]
+    args.batch = args.batch or wl["batch"]
+    args.calib_batch = args.calib_batch or wl["calib_batch"]
     if args.impl == "reference":
         run_reference(args)
         return
@@ -329,14 +357,19 @@ def main() -> None:
     from mira_b200 import configs
 
     t0 = time.perf_counter()
-    prog = configs.compile_w8a8(WORKLOAD, args.batch, "cuda", calib_batch=args.calib_batch, device=local)
+    prog = configs.compile_w8a8(args.workload, args.batch, "cuda", calib_batch=args.calib_batch, device=local,
+                                n_calib=wl["n_calib"], build_kw=wl["build_kw"] or None)
     compile_s = time.perf_counter() - t0
     segs = [s for s in prog.segments if s.device == "cuda"]
     assert len(prog.segments) == 1 and len(segs) == 1, "the whole network must be one cuda segment"
     exe = segs[0].executable
     x_val = prog.graph.inputs[0]
     host_x = exe.input_array(x_val)          # pinned staging array of the executable
-    host_x[...] = np.random.default_rng(1 + rank).standard_normal(host_x.shape, dtype=np.float32)
+    rng = np.random.default_rng(1 + rank)
+    if host_x.dtype == np.int32:             # token ids
+        host_x[...] = rng.integers(0, configs._vocab_of(prog.graph, x_val), host_x.shape)
+    else:
+        host_x[...] = rng.standard_normal(host_x.shape, dtype=np.float32)
     name = x_val.name
     feeds = {name: host_x}
 
@@ -384,50 +417,69 @@ def main() -> None:
     e2e_s = max_over_ranks(time.perf_counter() - t1)
     barrier()
 
-    imgs = args.batch * world * args.steps
-    value = imgs / (dev_ms * 1e-3)
+    items = args.batch * wl["items_per_row"] * world * args.steps
+    value = items / (dev_ms * 1e-3)
     conv_ops, q_ops = conv_work(prog.graph)
+    headline = args.workload == WORKLOAD
 
     result = None
     if rank == 0:
-        conv_ms = time_conv_kernels(exe)
         bf16, hbm, src = _peaks()
         peak = 2.0 * bf16 if bf16 else None
-        achieved = conv_ops / (conv_ms * 1e-3) / 1e12
-        ours_gemm = gemm_tops(8192)
-        lib_gemm = cublaslt_int8_tops(8192)
-        skinny = {str(m): skinny_gemm(m) for m in (1, 16, 128)}
+        # roofline of the int8 tensor-core kernels: the convolutions (ResNet-18, MobileNetV2) or all
+        # quantized matmuls (MLP, transformer)
+        kinds = ("qconv2d",) if conv_ops else ("qgemm",)
+        fam_ops = conv_ops if conv_ops else q_ops
+        fam_ms, fam_n = time_kernels(exe, kinds)
+        achieved = fam_ops / (fam_ms * 1e-3) / 1e12
+        other = {}
+        if not headline:
+            for kind in ("attention", "layernorm", "dwconv", "qconv2d", "qgemm"):
+                ms_k, n_k = time_kernels(exe, (kind,))
+                if n_k:
+                    other[kind] = {"launches": n_k, "ms_per_step": ms_k}
+        gemm = None
+        if headline:
+            ours_gemm = gemm_tops(8192)
+            gemm = {"shape": "8192^3", "tops": ours_gemm, "frac_of_peak": ours_gemm / peak if peak else None,
+                    "cublaslt_tops": cublaslt_int8_tops(8192),
+                    "skinny_mx4096x4096": {str(m): skinny_gemm(m) for m in (1, 16, 128)}}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             try:
-                cpu = reference_cpu_sample(1, 3, 1)
+                cpu = reference_cpu_sample(3, 1, args.workload)
             except Exception as e:  # the reference package is missing on this machine
-                cpu = {"value": None, "unit": "img/s", "cores": os.cpu_count(), "kind": "reference",
+                cpu = {"value": None, "unit": wl["unit"], "cores": os.cpu_count(), "kind": "reference",
                        "sample": f"unavailable: {e}"}
+        in_desc = (f"{host_x.nbytes / 1e6:.0f} MB input batch") if host_x.nbytes > 1e6 else "small input batch"
         result = {
-            "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
+            "metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "resnet18-w8a8-224", "global_batch": args.batch * world,
+            "config": {"workload": wl["config"], "global_batch": args.batch * world,
                        "batch_per_gpu": args.batch, "parallelism": f"dp{world} (replicas, no collective)",
-                       "l2": (f"inputs larger than L2 ({host_x.nbytes / 1e6:.0f} MB input batch, activations "
-                              "of several GB per step)") if host_x.nbytes > 126e6 else "inputs smaller than L2",
-                       "calibration": f"4 seeded N(0,1) batches of {args.calib_batch} images",
+                       "l2": (f"inputs larger than L2 ({in_desc}, activations of several GB per step)")
+                       if host_x.nbytes > 126e6 or args.workload == "transformer"
+                       else f"working set near L2 ({in_desc})",
+                       "calibration": f"{wl['n_calib']} seeded batches of {args.calib_batch}",
                        "compile_s": round(compile_s, 1)},
-            "e2e": {"value": imgs / e2e_s, "unit": "img/s", "h2d_bytes_per_step": int(host_x.nbytes),
+            "e2e": {"value": items / e2e_s, "unit": wl["unit"], "h2d_bytes_per_step": int(host_x.nbytes),
                     "d2h_bytes_per_step": int(out.nbytes)},
-            "roofline": {"bound": "tensor", "kernel": "qgemm_sm100_kernel (implicit-GEMM qconv2d, 20 launches/step)",
+            "roofline": {"bound": "tensor", "kernel": f"qgemm_sm100_kernel ({'/'.join(kinds)}, {fam_n} launches/step)",
                          "achieved": achieved, "peak": peak, "unit": "TOPS",
-                         "frac": (achieved / peak) if peak else None, "traffic": CONV_DRAM_BYTES_PER_PASS,
-                         "traffic_unit": "bytes per pass of the 20 conv launches (batch 256)",
+                         "frac": (achieved / peak) if peak else None,
+                         "traffic": CONV_DRAM_BYTES_PER_PASS if headline else None,
+                         "traffic_unit": "bytes per pass of the 20 conv launches (batch 256)" if headline else None,
                          "peak_source": f"2 x bf16_tflops of {src} (dense int8 issues at twice the bf16 rate)",
-                         "conv_int8_ops_per_step": conv_ops, "conv_ms_per_step": conv_ms},
-            "int8_gemm": {"shape": "8192^3", "tops": ours_gemm, "frac_of_peak": ours_gemm / peak if peak else None,
-                          "cublaslt_tops": lib_gemm, "skinny_mx4096x4096": skinny},
+                         "int8_ops_per_step": fam_ops, "ms_per_step": fam_ms},
             "int8_ops_per_step": q_ops, "int8_tops_step": q_ops / (dev_ms / args.steps * 1e-3) / 1e12,
             "gpu_launches": int(gpu_launches), "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
+        if gemm is not None:
+            result["int8_gemm"] = gemm
+        if other:
+            result["kernels"] = other
         print(json.dumps(result), flush=True)
     if dist is not None:
         barrier()
