@@ -52,7 +52,10 @@ __device__ __forceinline__ float div_by_scale(float y, float s, float rcp, float
 }
 
 // ---- packed f32x2 arithmetic (sm_100): two independent IEEE single-precision operations per
-// instruction, each rounded to nearest like the scalar __fadd_rn / __fmul_rn / __fmaf_rn.
+// instruction, each rounded to nearest like the scalar __fadd_rn / __fmul_rn / __fmaf_rn.  Unlike
+// the scalar forms, ptxas contracts f2_mul followed by an f2_add/f2_sub of its result into one
+// fma.rn.f32x2 (measured on sm_100a): never feed an f2_mul into an f2_add or f2_sub where the
+// product must be rounded on its own.
 typedef unsigned long long f2_t;
 
 __device__ __forceinline__ f2_t f2(float lo, float hi) {

@@ -365,8 +365,9 @@ struct DwParams {
 };
 
 // One thread per (output pixel, channel): per-tap products added in (i, j) order starting from
-// 0 (reference _conv2d_ref: one einsum term per tap, `acc +=`), padded taps skipped (they add
-// exact zeros), then the epilogue.  Threads run channel-fastest so x and w reads coalesce.
+// 0 (reference _conv2d_ref ops.py:272-275: one einsum term per tap over the zero-padded input,
+// `acc +=`), then the epilogue.  Threads run channel-fastest so x and w reads coalesce.  This is the
+// path for channel counts that are not a multiple of 4 and for unaligned buffers.
 __global__ void dwconv_kernel(const float* __restrict__ x, const float* __restrict__ wt, const __grid_constant__ DwParams p) {
   const int64_t total = int64_t(p.n) * p.oh * p.ow * p.c;
   for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
@@ -381,8 +382,9 @@ __global__ void dwconv_kernel(const float* __restrict__ x, const float* __restri
       const int iy = oy * p.sh - p.ph + i * p.dh;
       for (int j = 0; j < p.kw; ++j) {
         const int ix = ox * p.sw - p.pw + j * p.dw;
-        if (iy < 0 || iy >= p.h || ix < 0 || ix >= p.w) continue;
-        const float xv = __ldg(x + ((int64_t(img) * p.h + iy) * p.w + ix) * p.c + ch);
+        // a padded tap still adds 0 * w, as the zero-padded reference does (NaN for an inf weight)
+        const bool in = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
+        const float xv = in ? __ldg(x + ((int64_t(img) * p.h + iy) * p.w + ix) * p.c + ch) : 0.0f;
         acc = __fadd_rn(acc, __fmul_rn(xv, __ldg(wt + (i * p.kw + j) * p.c + ch)));
       }
     }
@@ -402,6 +404,69 @@ __global__ void dwconv_kernel(const float* __restrict__ x, const float* __restri
     }
     if (p.out_f32 != nullptr) p.out_f32[pix * p.ld_f32 + ch] = v;
     if (p.out_i8 != nullptr) p.out_i8[pix * p.ld_i8 + ch] = static_cast<int8_t>(quant_byte(v, p.q) & 0xff);
+  }
+}
+
+// Four channels per thread (c % 4 == 0): blockIdx.y walks output rows (n * oh, strided over
+// gridDim.y), threadIdx.x groups of 4 channels (strided over blockDim.x), threadIdx.y +
+// blockIdx.x * blockDim.y the output column.  Inputs, weights and operands move as 16-byte vectors;
+// the per-tap sums run two channels per packed f32x2 add, each lane rounded like the scalar kernel
+// (product, then sum, per tap in (i, j) order, padded taps as 0 * w).
+__global__ void dwconv4_kernel(const float* __restrict__ x, const float* __restrict__ wt, const __grid_constant__ DwParams p) {
+  const int c4 = p.c >> 2;
+  const int ox = blockIdx.x * blockDim.y + threadIdx.y;
+  if (ox >= p.ow) return;
+  const int64_t rows = int64_t(p.n) * p.oh;
+  for (int64_t orow = blockIdx.y; orow < rows; orow += gridDim.y) {
+    const int img = static_cast<int>(orow / p.oh);
+    const int oy = static_cast<int>(orow - int64_t(img) * p.oh);
+    const int64_t pix = orow * p.ow + ox;
+    for (int cg = threadIdx.x; cg < c4; cg += blockDim.x) {
+      f2_t a01 = f2(0.0f, 0.0f), a23 = f2(0.0f, 0.0f);
+      for (int i = 0; i < p.kh; ++i) {
+        const int iy = oy * p.sh - p.ph + i * p.dh;
+        const bool row_in = iy >= 0 && iy < p.h;
+        const float* xrow = x + ((int64_t(img) * p.h + (row_in ? iy : 0)) * p.w) * p.c + 4 * cg;
+        const float* wrow = wt + int64_t(i) * p.kw * p.c + 4 * cg;
+        for (int j = 0; j < p.kw; ++j) {
+          const int ix = ox * p.sw - p.pw + j * p.dw;
+          const float4 xv = row_in && ix >= 0 && ix < p.w ? __ldg(reinterpret_cast<const float4*>(xrow + int64_t(ix) * p.c))
+                                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          const float4 wv = __ldg(reinterpret_cast<const float4*>(wrow + int64_t(j) * p.c));
+          // scalar products (a packed mul.rn.f32x2 would be fused with the packed add into an fma)
+          a01 = f2_add(a01, f2(__fmul_rn(xv.x, wv.x), __fmul_rn(xv.y, wv.y)));
+          a23 = f2_add(a23, f2(__fmul_rn(xv.z, wv.z), __fmul_rn(xv.w, wv.w)));
+        }
+      }
+      float v[4];
+      f2_split(a01, v[0], v[1]);
+      f2_split(a23, v[2], v[3]);
+      for (int s = 0; s < p.n_steps; ++s) {
+        const mira_epi_step& st = p.steps[s];
+        if (st.operand == MIRA_OPND_NONE) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = apply_unary(st.op, v[e]);
+          continue;
+        }
+        float o[4];
+        if (st.operand == MIRA_OPND_SCALAR) {
+          o[0] = o[1] = o[2] = o[3] = st.scalar;
+        } else if (st.operand == MIRA_OPND_ROW) {
+          o[0] = o[1] = o[2] = o[3] = st.ptr[pix];
+        } else {
+          const float* src = st.operand == MIRA_OPND_CHANNEL ? st.ptr + 4 * cg : st.ptr + pix * st.ld + 4 * cg;
+          const float4 t = __ldg(reinterpret_cast<const float4*>(src));
+          o[0] = t.x; o[1] = t.y; o[2] = t.z; o[3] = t.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = st.swapped ? apply_binary(st.op, o[e], v[e]) : apply_binary(st.op, v[e], o[e]);
+      }
+      if (p.out_f32 != nullptr)
+        *reinterpret_cast<float4*>(p.out_f32 + pix * p.ld_f32 + 4 * cg) = make_float4(v[0], v[1], v[2], v[3]);
+      if (p.out_i8 != nullptr)
+        *reinterpret_cast<uint32_t*>(p.out_i8 + pix * p.ld_i8 + 4 * cg) =
+            pack4_i8(quant_byte(v[0], p.q), quant_byte(v[1], p.q), quant_byte(v[2], p.q), quant_byte(v[3], p.q));
+    }
   }
 }
 

@@ -744,6 +744,10 @@ extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, co
   const int bn = pick_bn(o);
   p.m_tiles = int((p.M + QG_BM - 1) / QG_BM);
   p.n_tiles = int((o + bn - 1) / bn);
+  // a 1x1 stride-1 convolution without padding is a GEMM over the NHWC activation matrix [n*h*w, cp]
+  if (x_layout == MIRA_LAYOUT_NHWC && kh == 1 && kw == 1 && stride_h == 1 && stride_w == 1 && pad_h == 0 &&
+      pad_w == 0 && cp % 16 == 0)
+    return qgemm_run(dev, p.M, o, cp, x, cp, wq, ldw, dq, epi, 1, 0, nullptr);
   CUtensorMap tmA, tmB;
   std::memset(&tmA, 0, sizeof(tmA));
   // TMA im2col for NHWC inputs of 64k channels and square, symmetric kernels
@@ -899,6 +903,23 @@ extern "C" int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int
   p.out_f32 = epi->out_f32; p.ld_f32 = epi->ld_f32; p.out_i8 = epi->out_i8; p.ld_i8 = epi->ld_i8;
   p.q = make_qscale(epi->out_i8 != nullptr ? epi->out_scale : 1.0f);
   const int threads = 256;
+  bool vec = c % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(wt) & 15) == 0;
+  if (epi->out_f32 != nullptr) vec = vec && epi->ld_f32 % 4 == 0 && (reinterpret_cast<uintptr_t>(epi->out_f32) & 15) == 0;
+  if (epi->out_i8 != nullptr) vec = vec && epi->ld_i8 % 4 == 0 && (reinterpret_cast<uintptr_t>(epi->out_i8) & 3) == 0;
+  for (int s = 0; s < epi->n_steps; ++s) {
+    const mira_epi_step& st = epi->steps[s];
+    if (st.operand == MIRA_OPND_CHANNEL || st.operand == MIRA_OPND_FULL)
+      vec = vec && (reinterpret_cast<uintptr_t>(st.ptr) & 15) == 0 && (st.operand != MIRA_OPND_FULL || st.ld % 4 == 0);
+  }
+  if (vec) {
+    const int c4 = int(c / 4);
+    const int tx = c4 < 32 ? c4 : 32;
+    const int ty = threads / tx;
+    const int64_t orows = n * oh;
+    const dim3 grid(unsigned((ow + ty - 1) / ty), unsigned(orows < 65535 ? orows : 65535));
+    dwconv4_kernel<<<grid, dim3(tx, ty), 0, dev->stream>>>(x, wt, p);
+    return after_launch("dwconv4_kernel");
+  }
   dwconv_kernel<<<grid_for(dev, n * oh * ow * c, threads), threads, 0, dev->stream>>>(x, wt, p);
   return after_launch("dwconv_kernel");
 }

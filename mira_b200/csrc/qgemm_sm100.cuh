@@ -230,15 +230,17 @@ __device__ __forceinline__ void qg_apply_step(const mira_epi_step& st, const flo
   }
 }
 
-// A binary step on 16 values: add/sub/mul two lanes per instruction, the others one by one.
+// A binary step on 16 values: add/sub two lanes per instruction, the others one by one.  A
+// multiply stays scalar: ptxas fuses a packed mul.rn.f32x2 with a following packed add into one
+// fma (measured on sm_100a), which would round a mul step and the next add step once instead of
+// twice; the scalar mul.rn.f32 with its explicit rounding mode is never fused.
 __device__ __forceinline__ void qg_apply_binary(const mira_epi_step& st, const float (&o)[16], float (&v)[16]) {
-  if (st.op == MIRA_EPI_ADD || st.op == MIRA_EPI_SUB || st.op == MIRA_EPI_MUL) {
+  if (st.op == MIRA_EPI_ADD || st.op == MIRA_EPI_SUB) {
 #pragma unroll
     for (int j = 0; j < 16; j += 2) {
       const f2_t x = f2(v[j], v[j + 1]), y = f2(o[j], o[j + 1]);
       f2_t r;
       if (st.op == MIRA_EPI_ADD) r = f2_add(x, y);                // commutative: swapped gives the same
-      else if (st.op == MIRA_EPI_MUL) r = f2_mul(x, y);
       else r = st.swapped ? f2_sub(y, x) : f2_sub(x, y);
       f2_split(r, v[j], v[j + 1]);
     }

@@ -106,6 +106,18 @@ def _run_qgemm(M, N, K_, steps_spec, seed, want_i8=True, rowcol=False, splitk=Fa
             ref_steps.append(("add", len(operands), True))
             steps[-1].swapped = True
             operands.append(r)
+        elif kind == "scale":            # a per-channel multiply (an unfolded batch norm's scale)
+            g = rng.uniform(0.5, 2.0, N).astype(np.float32)
+            gb = DB.from_array(K.pad_channels(g))
+            keep.append(gb)
+            steps.append(K.Step("mul", "channel", ptr=gb))
+            ref_steps.append(("mul", len(operands), False))
+            operands.append(g)
+        elif kind == "rsub":             # 0.25 - y
+            steps.append(K.Step("sub", "scalar", scalar=0.25))
+            steps[-1].swapped = True
+            ref_steps.append(("sub", len(operands), True))
+            operands.append(np.float32(0.25))
         elif kind in ("relu", "gelu", "tanh", "sigmoid"):
             steps.append(K.Step(kind))
             ref_steps.append((kind, None, False))
@@ -140,8 +152,10 @@ def test_qgemm_bias_relu_exact(cuda_device, M, N, K_):
     assert not got_q[:, N:].any()
 
 
-@pytest.mark.parametrize("spec", [[], ["relu"], ["bias", "residual", "relu"], ["bias", "relu6"]])
+@pytest.mark.parametrize("spec", [[], ["relu"], ["bias", "residual", "relu"], ["bias", "relu6"],
+                                  ["scale", "bias", "relu"], ["scale", "rsub", "scale", "residual"]])
 def test_qgemm_epilogues_exact(cuda_device, spec):
+    """Each step rounded on its own; a mul step followed by add/sub must not fuse into one fma."""
     got, want, got_q, want_q = _run_qgemm(200, 192, 576, spec, seed=11)
     _same_f32(got, want)
     np.testing.assert_array_equal(got_q[:, :192], want_q)
@@ -170,6 +184,13 @@ def test_qgemm_splitk_exact(cuda_device, M, N, K_, rowcol):
     _same_f32(got, want)
     np.testing.assert_array_equal(got_q[:, :N], want_q)
     assert not got_q[:, N:].any()
+
+
+@pytest.mark.parametrize("M", [1, 16])
+def test_qgemm_splitk_mul_step_exact(cuda_device, M):
+    got, want, got_q, want_q = _run_qgemm(M, 4096, 4096, ["scale", "rsub", "bias"], seed=M, splitk=True)
+    _same_f32(got, want)
+    np.testing.assert_array_equal(got_q[:, :4096], want_q)
 
 
 def test_qgemm_splitk_workspace_rule(cuda_device):
@@ -234,6 +255,7 @@ def _run_qconv(n, c, h, w, o, kh, kw, stride, pad, dil=(1, 1), spec=("bias", "re
     dict(n=2, c=192, h=9, w=9, o=96, kh=3, kw=3, stride=(1, 1), pad=(1, 1)),
     dict(n=3, c=128, h=11, w=11, o=64, kh=5, kw=5, stride=(2, 2), pad=(2, 2)),
     dict(n=5, c=64, h=9, w=7, o=128, kh=1, kw=1, stride=(1, 1), pad=(0, 0)),
+    dict(n=4, c=320, h=7, w=7, o=1280, kh=1, kw=1, stride=(1, 1), pad=(0, 0)),   # 1x1 as a 2-D TMA GEMM
     dict(n=2, c=512, h=7, w=7, o=256, kh=3, kw=3, stride=(2, 2), pad=(1, 1)),
     dict(n=4, c=64, h=20, w=20, o=32, kh=3, kw=3, stride=(1, 1), pad=(0, 0)),
     # non-square kernel with 64 channels: the cp.async gather
@@ -286,26 +308,44 @@ def test_mean_hw_bit_exact(cuda_device, hw):
     np.testing.assert_array_equal(qb.download((n, 112), np.int8)[:, :c], ref.quantize_activation(want, scale))
 
 
-@pytest.mark.parametrize("stride", [1, 2])
-def test_dwconv_bit_exact(cuda_device, stride):
+@pytest.mark.parametrize("stride,c,inf_weight", [(1, 96, False), (2, 96, False), (1, 30, False), (2, 960, False),
+                                                (1, 96, True), (1, 30, True)])
+def test_dwconv_bit_exact(cuda_device, stride, c, inf_weight):
+    """Four-channel vector kernel (c % 4 == 0, c / 4 above one warp for 960) and the scalar kernel
+    (c = 30), with f32 and int8 outputs.  An inf weight makes every output that reads a padded tap
+    through it NaN in the zero-padded reference (0 * inf), and the kernels must agree."""
     K, DB = _k()
-    rng = np.random.default_rng(stride)
-    n, c, h, w = 2, 96, 13, 13
+    rng = np.random.default_rng(stride + c)
+    n, h, w = 2, 13, 13
     x = rng.standard_normal((n, c, h, w)).astype(np.float32)
     wt = rng.standard_normal((c, 1, 3, 3)).astype(np.float32)
+    if inf_weight:
+        wt[3, 0, 0, 0] = np.inf
+        wt[5, 0, 2, 1] = -np.inf
     bias = rng.standard_normal((c, 1, 1)).astype(np.float32)
-    want = ref.dwconv2d(x, wt, (stride, stride), (1, 1), steps=[("add", 2, False), ("maximum", 3, False),
-                                                                 ("minimum", 4, False)],
-                        operands=[bias, np.float32(0), np.float32(6)])
+    with np.errstate(invalid="ignore", over="ignore"):
+        want = ref.dwconv2d(x, wt, (stride, stride), (1, 1), steps=[("add", 2, False), ("maximum", 3, False),
+                                                                     ("minimum", 4, False)],
+                            operands=[bias, np.float32(0), np.float32(6)])
+    if inf_weight:
+        assert np.isnan(want).any()
     oh = want.shape[2]
     xb = DB.from_array(np.ascontiguousarray(x.transpose(0, 2, 3, 1)))
     wb = DB.from_array(np.ascontiguousarray(wt[:, 0].reshape(c, 9).T))
     bb = DB.from_array(K.pad_channels(bias))
     yb = DB(n * oh * oh * c * 4)
+    ldq = K.round_up(c, 16)
+    qb = DB(n * oh * oh * ldq, zero=True)
+    scale = 6.0 / 127
     K.dwconv2d(xb, n, h, w, c, wb, 3, 3, (stride, stride), (1, 1), (1, 1),
                K.Epi([K.Step("add", "channel", ptr=bb), K.Step("maximum", "scalar", scalar=0.0),
-                      K.Step("minimum", "scalar", scalar=6.0)], out_f32=yb, ld_f32=c))
-    _same_f32(yb.download((n, oh, oh, c), np.float32).transpose(0, 3, 1, 2), want)
+                      K.Step("minimum", "scalar", scalar=6.0)], out_f32=yb, ld_f32=c, out_i8=qb, ld_i8=ldq,
+                     out_scale=scale))
+    got = yb.download((n, oh, oh, c), np.float32).transpose(0, 3, 1, 2)
+    _same_f32(got, want)
+    if not inf_weight:
+        q = qb.download((n, oh, oh, ldq), np.int8)[..., :c].transpose(0, 3, 1, 2)
+        np.testing.assert_array_equal(q, ref.quantize_activation(want, scale))
 
 
 def test_layout_roundtrip(cuda_device):
