@@ -121,10 +121,12 @@ __device__ __forceinline__ void dequant4_x2(const uint32_t* r, const float4& hs,
 // after rounding and no clip is needed afterwards (RN(c127 / s) rounds to 127; infinities map to
 // +-127); then Markstein's correction of RN(y * RN(1/s)) and the 1.5 * 2^23 rounding add.
 // Checked against the reference formula on 3e8 random cases (ties, values next to the clip).
-__device__ __forceinline__ void requant16_x2(const float (&v)[16], float s, float rcp, float c127, uint32_t (&b)[16]) {
+template <int N>
+__device__ __forceinline__ void requant_x2(const float (&v)[N], float s, float rcp, float c127, uint32_t (&b)[N]) {
+  static_assert(N % 2 == 0, "values come in pairs");
   const f2_t r2 = f2(rcp, rcp), ns = f2(-s, -s), magic = f2(12582912.0f, 12582912.0f);
 #pragma unroll
-  for (int j = 0; j < 16; j += 2) {
+  for (int j = 0; j < N; j += 2) {
     const f2_t y = f2(fminf(fmaxf(v[j], -c127), c127), fminf(fmaxf(v[j + 1], -c127), c127));
     const f2_t q0 = f2_mul(y, r2);
     const f2_t z = f2_fma(f2_fma(q0, ns, y), r2, q0);
@@ -133,6 +135,9 @@ __device__ __forceinline__ void requant16_x2(const float (&v)[16], float s, floa
     b[j] = static_cast<uint32_t>(__float_as_int(t0));
     b[j + 1] = static_cast<uint32_t>(__float_as_int(t1));
   }
+}
+__device__ __forceinline__ void requant16_x2(const float (&v)[16], float s, float rcp, float c127, uint32_t (&b)[16]) {
+  requant_x2<16>(v, s, rcp, c127, b);
 }
 
 // clip(rint(z), -127, 127) as an int8 in the low byte of the returned word: clipping before

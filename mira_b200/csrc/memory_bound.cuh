@@ -11,6 +11,7 @@ namespace mira {
 
 struct QuantScale {
   float s, rcp, lim;   // divisor, RN32(1/divisor), 256 * divisor
+  float c127;          // RN32(127 * divisor): the clamp of the packed requantization (requant_x2)
 };
 
 __device__ __forceinline__ uint32_t quant_byte(float x, const QuantScale& q) {
@@ -407,6 +408,83 @@ __global__ void dwconv_kernel(const float* __restrict__ x, const float* __restri
   }
 }
 
+// Apply `expr` (of a, the value, and b, the operand) to every value of a thread's tile, with
+// the operand order of step `st` (b op a when swapped).
+#define DW_BINARY(SWAP, expr)                                                             \
+  _Pragma("unroll") for (int t = 0; t < T; ++t) _Pragma("unroll") for (int e = 0; e < 4; ++e) { \
+    const float a = (SWAP) ? o[t][e] : v[t][e];                                           \
+    const float b = (SWAP) ? v[t][e] : o[t][e];                                           \
+    v[t][e] = (expr);                                                                     \
+  }
+
+// The epilogue of T adjacent output pixels (pix0 ...) x 4 channels (4 * cg ...) and the 16-byte
+// f32 / 4-byte int8 stores of the first `nvalid` pixels.  Each step's operand kind and op are
+// decoded once for the whole tile (they are uniform across the grid), not per value.
+template <int T>
+__device__ __forceinline__ void dw_epilogue_tile(const DwParams& p, int64_t pix0, int cg, int nvalid,
+                                                 float (&v)[T][4]) {
+  for (int s = 0; s < p.n_steps; ++s) {
+    const mira_epi_step& st = p.steps[s];
+    if (st.operand == MIRA_OPND_NONE) {
+      if (st.op == MIRA_EPI_RELU) {
+#pragma unroll
+        for (int t = 0; t < T; ++t)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[t][e] = np_maximum(v[t][e], 0.0f);
+      } else {
+#pragma unroll
+        for (int t = 0; t < T; ++t)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[t][e] = apply_unary(st.op, v[t][e]);
+      }
+      continue;
+    }
+    float o[T][4];
+    if (st.operand == MIRA_OPND_SCALAR || st.operand == MIRA_OPND_CHANNEL) {
+      float4 c4 = make_float4(st.scalar, st.scalar, st.scalar, st.scalar);
+      if (st.operand == MIRA_OPND_CHANNEL) c4 = __ldg(reinterpret_cast<const float4*>(st.ptr + 4 * cg));
+#pragma unroll
+      for (int t = 0; t < T; ++t) { o[t][0] = c4.x; o[t][1] = c4.y; o[t][2] = c4.z; o[t][3] = c4.w; }
+    } else {
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        const int64_t pix = pix0 + (t < nvalid ? t : 0);
+        if (st.operand == MIRA_OPND_ROW) {
+          o[t][0] = o[t][1] = o[t][2] = o[t][3] = st.ptr[pix];
+        } else {
+          const float4 f = __ldg(reinterpret_cast<const float4*>(st.ptr + pix * st.ld + 4 * cg));
+          o[t][0] = f.x; o[t][1] = f.y; o[t][2] = f.z; o[t][3] = f.w;
+        }
+      }
+    }
+    // add, mul, maximum and minimum are commutative (np_maximum/np_minimum up to the sign of a
+    // zero, which quantizes alike), so only sub and div look at the operand order
+    const bool sw = st.swapped != 0;
+    switch (st.op) {
+      case MIRA_EPI_ADD: DW_BINARY(false, __fadd_rn(a, b)); break;
+      case MIRA_EPI_SUB: if (sw) { DW_BINARY(true, __fsub_rn(a, b)); } else { DW_BINARY(false, __fsub_rn(a, b)); } break;
+      case MIRA_EPI_MUL: DW_BINARY(false, __fmul_rn(a, b)); break;
+      case MIRA_EPI_DIV: if (sw) { DW_BINARY(true, __fdiv_rn(a, b)); } else { DW_BINARY(false, __fdiv_rn(a, b)); } break;
+      case MIRA_EPI_MAXIMUM: DW_BINARY(false, np_maximum(a, b)); break;
+      case MIRA_EPI_MINIMUM: DW_BINARY(false, np_minimum(a, b)); break;
+      default: break;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < T; ++t) {
+    if (t >= nvalid) break;
+    const int64_t pix = pix0 + t;
+    if (p.out_f32 != nullptr)
+      *reinterpret_cast<float4*>(p.out_f32 + pix * p.ld_f32 + 4 * cg) = make_float4(v[t][0], v[t][1], v[t][2], v[t][3]);
+    if (p.out_i8 != nullptr) {
+      uint32_t b[4];
+      requant_x2<4>(v[t], p.q.s, p.q.rcp, p.q.c127, b);
+      *reinterpret_cast<uint32_t*>(p.out_i8 + pix * p.ld_i8 + 4 * cg) = pack4_i8(b[0], b[1], b[2], b[3]);
+    }
+  }
+}
+#undef DW_BINARY
+
 // Four channels per thread (c % 4 == 0): blockIdx.y walks output rows (n * oh, strided over
 // gridDim.y), threadIdx.x groups of 4 channels (strided over blockDim.x), threadIdx.y +
 // blockIdx.x * blockDim.y the output column.  Inputs, weights and operands move as 16-byte vectors;
@@ -438,34 +516,66 @@ __global__ void dwconv4_kernel(const float* __restrict__ x, const float* __restr
           a23 = f2_add(a23, f2(__fmul_rn(xv.z, wv.z), __fmul_rn(xv.w, wv.w)));
         }
       }
-      float v[4];
-      f2_split(a01, v[0], v[1]);
-      f2_split(a23, v[2], v[3]);
-      for (int s = 0; s < p.n_steps; ++s) {
-        const mira_epi_step& st = p.steps[s];
-        if (st.operand == MIRA_OPND_NONE) {
+      float v[1][4];
+      f2_split(a01, v[0][0], v[0][1]);
+      f2_split(a23, v[0][2], v[0][3]);
+      dw_epilogue_tile<1>(p, pix, cg, 1, v);
+    }
+  }
+}
+
+// 3x3 depthwise, dilation 1, stride S (1 or 2), c % 4 == 0: each thread computes OXT adjacent
+// output columns of one output row for 4 channels.  The taps are unrolled so one input row's
+// (OXT - 1) * S + 3 16-byte loads are in flight together, and each loaded column feeds every
+// output column whose window covers it.  Per output the order is the reference's: (i, j) taps
+// ascending, each product rounded, then added to the running sum from 0; padded taps add 0 * w.
+template <int S, int OXT>
+__global__ void __launch_bounds__(256) dwconv3x3_kernel(const float* __restrict__ x, const float* __restrict__ wt,
+                                                        const __grid_constant__ DwParams p) {
+  constexpr int NIN = (OXT - 1) * S + 3;
+  const int c4 = p.c >> 2;
+  const int ox0 = (blockIdx.x * blockDim.y + threadIdx.y) * OXT;
+  if (ox0 >= p.ow) return;
+  const int64_t rows = int64_t(p.n) * p.oh;
+  for (int64_t orow = blockIdx.y; orow < rows; orow += gridDim.y) {
+    const int img = static_cast<int>(orow / p.oh);
+    const int oy = static_cast<int>(orow - int64_t(img) * p.oh);
+    for (int cg = threadIdx.x; cg < c4; cg += blockDim.x) {
+      f2_t acc[OXT][2];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) v[e] = apply_unary(st.op, v[e]);
-          continue;
-        }
-        float o[4];
-        if (st.operand == MIRA_OPND_SCALAR) {
-          o[0] = o[1] = o[2] = o[3] = st.scalar;
-        } else if (st.operand == MIRA_OPND_ROW) {
-          o[0] = o[1] = o[2] = o[3] = st.ptr[pix];
-        } else {
-          const float* src = st.operand == MIRA_OPND_CHANNEL ? st.ptr + 4 * cg : st.ptr + pix * st.ld + 4 * cg;
-          const float4 t = __ldg(reinterpret_cast<const float4*>(src));
-          o[0] = t.x; o[1] = t.y; o[2] = t.z; o[3] = t.w;
-        }
+      for (int t = 0; t < OXT; ++t) acc[t][0] = acc[t][1] = f2(0.0f, 0.0f);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = st.swapped ? apply_binary(st.op, o[e], v[e]) : apply_binary(st.op, v[e], o[e]);
+      for (int i = 0; i < 3; ++i) {
+        const int iy = oy * S - p.ph + i;
+        const bool row_in = iy >= 0 && iy < p.h;
+        const float* xrow = x + ((int64_t(img) * p.h + (row_in ? iy : 0)) * p.w) * p.c + 4 * cg;
+        float4 xin[NIN];
+#pragma unroll
+        for (int u = 0; u < NIN; ++u) {
+          const int ix = ox0 * S - p.pw + u;
+          xin[u] = row_in && ix >= 0 && ix < p.w ? __ldg(reinterpret_cast<const float4*>(xrow + int64_t(ix) * p.c))
+                                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        float4 wv[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(wt + (i * 3 + j) * p.c + 4 * cg));
+#pragma unroll
+        for (int t = 0; t < OXT; ++t)
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            const float4 xv = xin[t * S + j];
+            // scalar products (a packed mul.rn.f32x2 would be fused with the packed add into an fma)
+            acc[t][0] = f2_add(acc[t][0], f2(__fmul_rn(xv.x, wv[j].x), __fmul_rn(xv.y, wv[j].y)));
+            acc[t][1] = f2_add(acc[t][1], f2(__fmul_rn(xv.z, wv[j].z), __fmul_rn(xv.w, wv[j].w)));
+          }
       }
-      if (p.out_f32 != nullptr)
-        *reinterpret_cast<float4*>(p.out_f32 + pix * p.ld_f32 + 4 * cg) = make_float4(v[0], v[1], v[2], v[3]);
-      if (p.out_i8 != nullptr)
-        *reinterpret_cast<uint32_t*>(p.out_i8 + pix * p.ld_i8 + 4 * cg) =
-            pack4_i8(quant_byte(v[0], p.q), quant_byte(v[1], p.q), quant_byte(v[2], p.q), quant_byte(v[3], p.q));
+      float v[OXT][4];
+#pragma unroll
+      for (int t = 0; t < OXT; ++t) {
+        f2_split(acc[t][0], v[t][0], v[t][1]);
+        f2_split(acc[t][1], v[t][2], v[t][3]);
+      }
+      dw_epilogue_tile<OXT>(p, orow * p.ow + ox0, cg, p.ow - ox0 < OXT ? p.ow - ox0 : OXT, v);
     }
   }
 }

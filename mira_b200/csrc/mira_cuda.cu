@@ -127,6 +127,7 @@ static QuantScale make_qscale(float s) {
   q.s = s;
   q.rcp = 1.0f / s;          // correctly rounded (IEEE division on the host)
   q.lim = 256.0f * s;        // exact (power of two)
+  q.c127 = 127.0f * s;       // correctly rounded product
   return q;
 }
 
@@ -910,6 +911,21 @@ extern "C" int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int
     const mira_epi_step& st = epi->steps[s];
     if (st.operand == MIRA_OPND_CHANNEL || st.operand == MIRA_OPND_FULL)
       vec = vec && (reinterpret_cast<uintptr_t>(st.ptr) & 15) == 0 && (st.operand != MIRA_OPND_FULL || st.ld % 4 == 0);
+  }
+  if (vec && kh == 3 && kw == 3 && dil_h == 1 && dil_w == 1 && stride_h == stride_w && stride_h <= 2) {
+    // threadIdx.x: 4-channel groups (all of them up to 256 threads), threadIdx.y: groups of
+    // output columns, so narrow late layers with many channels keep every thread busy
+    const int oxt = stride_h == 1 ? 4 : 2;
+    const int c4 = int(c / 4);
+    const int64_t col_groups = (ow + oxt - 1) / oxt;
+    const int tx = c4 < threads ? c4 : threads;
+    const int ty_max = threads / tx;
+    const int ty = int(col_groups < ty_max ? col_groups : ty_max);
+    const int64_t orows = n * oh;
+    const dim3 grid(unsigned((col_groups + ty - 1) / ty), unsigned(orows < 65535 ? orows : 65535));
+    if (stride_h == 1) dwconv3x3_kernel<1, 4><<<grid, dim3(tx, ty), 0, dev->stream>>>(x, wt, p);
+    else dwconv3x3_kernel<2, 2><<<grid, dim3(tx, ty), 0, dev->stream>>>(x, wt, p);
+    return after_launch("dwconv3x3_kernel");
   }
   if (vec) {
     const int c4 = int(c / 4);

@@ -348,6 +348,27 @@ def test_dwconv_bit_exact(cuda_device, stride, c, inf_weight):
         np.testing.assert_array_equal(q, ref.quantize_activation(want, scale))
 
 
+@pytest.mark.parametrize("n,c,h,w,k,stride,pad,dil", [
+    (2, 64, 11, 9, 5, 1, 2, 1),      # 5x5: the general 4-channel kernel
+    (2, 32, 12, 12, 3, 1, 2, 2),     # dilated 3x3: the general 4-channel kernel
+    (2, 36, 9, 10, 3, 2, 0, 1),      # unpadded, ragged output width
+    (600, 8, 112, 5, 3, 1, 1, 1),    # 67200 output rows: more than one grid row per block
+    (1, 1024, 3, 3, 3, 1, 1, 1),     # channels beyond one block's 256 threads
+])
+def test_dwconv_geometries_bit_exact(cuda_device, n, c, h, w, k, stride, pad, dil):
+    K, DB = _k()
+    rng = np.random.default_rng(n + c + k)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = rng.standard_normal((c, 1, k, k)).astype(np.float32)
+    want = ref.dwconv2d(x, wt, (stride, stride), (pad, pad), (dil, dil))
+    oh, ow = want.shape[2:]
+    xb = DB.from_array(np.ascontiguousarray(x.transpose(0, 2, 3, 1)))
+    wb = DB.from_array(np.ascontiguousarray(wt[:, 0].reshape(c, k * k).T))
+    yb = DB(n * oh * ow * c * 4)
+    K.dwconv2d(xb, n, h, w, c, wb, k, k, (stride, stride), (pad, pad), (dil, dil), K.Epi([], out_f32=yb, ld_f32=c))
+    _same_f32(yb.download((n, oh, ow, c), np.float32).transpose(0, 3, 1, 2), want)
+
+
 def test_layout_roundtrip(cuda_device):
     K, DB = _k()
     x = np.random.default_rng(0).standard_normal((3, 70, 9, 13)).astype(np.float32)
