@@ -292,6 +292,16 @@ typedef struct mira_bmm_epilogue {
 int mira_cuda_bmm_f32(int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,
                       const mira_view4* a, const mira_view4* b, const mira_bmm_epilogue* epi);
 
+/* Weight-only int8 matmul (reference `quantize="int8"`: quantize.py:45-68 turns a [K, N] matmul
+ * weight into a `dequantize` constant, ops.py:583-587, feeding the f32 matmul of ops.py:217-219).
+ * Like mira_cuda_bmm_f32, but b_i8 views the int8 weights q (element strides) and b_scale holds
+ * the f32 scale of each of the n columns; every weight is rebuilt as RN(f32(q[k, n]) * b_scale[n]),
+ * the reference's own rounding, while it is staged into shared memory, so the weights stay int8 in
+ * device memory. */
+int mira_cuda_bmm_f32_w8(int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,
+                         const mira_view4* a, const mira_view4* b_i8, const float* b_scale,
+                         const mira_bmm_epilogue* epi);
+
 /* Layer normalization over the last axis of rows [rows, d] (row stride ld_x), reference
  * ops.py:356-360 (_layernorm_ref): mean and variance in NumPy's pairwise summation order and
  * float32 division by d, so the f32 result is bit-identical.  Optional outputs: f32 rows

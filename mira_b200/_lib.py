@@ -116,6 +116,8 @@ SIGNATURES: dict[str, tuple] = {
     "mira_cuda_nhwc_to_nchw_f32": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mira_cuda_bmm_f32": (_i32, [_i64, _i64, _i64, _i64, _i64, C.POINTER(View4), C.POINTER(View4),
                                  C.POINTER(BmmEpilogue)]),
+    "mira_cuda_bmm_f32_w8": (_i32, [_i64, _i64, _i64, _i64, _i64, C.POINTER(View4), C.POINTER(View4), _vp,
+                                    C.POINTER(BmmEpilogue)]),
     "mira_cuda_layernorm_rows": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _f32, _vp, _i64, _vp, _i64, _f32]),
     "mira_cuda_softmax_rows": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64]),
     "mira_cuda_embed_rows": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64]),

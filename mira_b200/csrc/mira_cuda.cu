@@ -1068,9 +1068,12 @@ extern "C" int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64
   return after_launch("copy_view_kernel");
 }
 
-extern "C" int mira_cuda_bmm_f32(int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,
-                                 const mira_view4* a, const mira_view4* b, const mira_bmm_epilogue* epi) {
-  MIRA_GET_DEVICE(dev);
+namespace mira {
+
+// The f32 batched matmul behind mira_cuda_bmm_f32 (b_scale == nullptr: b holds f32) and
+// mira_cuda_bmm_f32_w8 (b holds int8 weights, dequantized with b_scale[n] as tiles are loaded).
+static int bmm_launch(DeviceState* dev, int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,
+                      const mira_view4* a, const mira_view4* b, const float* b_scale, const mira_bmm_epilogue* epi) {
   MIRA_CHECK_ARG(batch0 >= 0 && batch1 > 0 && m >= 0 && n >= 0 && k >= 0, "bad bmm shape");
   MIRA_CHECK_ARG(a != nullptr && b != nullptr && epi != nullptr, "bmm needs a, b and an epilogue");
   MIRA_CHECK_ARG(k == 0 || (a->ptr != nullptr && b->ptr != nullptr), "null bmm operand");
@@ -1089,7 +1092,12 @@ extern "C" int mira_cuda_bmm_f32(int64_t batch0, int64_t batch1, int64_t m, int6
   std::memset(&p, 0, sizeof(p));
   p.batches = batches; p.batch1 = batch1; p.m = m; p.n = n; p.k = k;
   p.a = static_cast<const float*>(a->ptr);
-  p.b = static_cast<const float*>(b->ptr);
+  if (b_scale != nullptr) {
+    p.b_i8 = static_cast<const int8_t*>(b->ptr);
+    p.b_scale = b_scale;
+  } else {
+    p.b = static_cast<const float*>(b->ptr);
+  }
   for (int i = 0; i < 4; ++i) {
     p.as[i] = a->stride[i]; p.bs[i] = b->stride[i];
     p.os[i] = epi->out_f32.stride[i]; p.qs[i] = epi->out_i8.stride[i];
@@ -1107,6 +1115,22 @@ extern "C" int mira_cuda_bmm_f32(int64_t batch0, int64_t batch1, int64_t m, int6
   const dim3 grid(unsigned(gx), unsigned(gy), unsigned(batches < 65535 ? batches : 65535));
   bmm_f32_kernel<<<grid, BMM_THREADS, 0, dev->stream>>>(p);
   return after_launch("bmm_f32_kernel");
+}
+
+}  // namespace mira
+
+extern "C" int mira_cuda_bmm_f32(int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,
+                                 const mira_view4* a, const mira_view4* b, const mira_bmm_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  return bmm_launch(dev, batch0, batch1, m, n, k, a, b, nullptr, epi);
+}
+
+extern "C" int mira_cuda_bmm_f32_w8(int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,
+                                    const mira_view4* a, const mira_view4* b_i8, const float* b_scale,
+                                    const mira_bmm_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(b_scale != nullptr, "weight-only bmm needs the per-column scales");
+  return bmm_launch(dev, batch0, batch1, m, n, k, a, b_i8, b_scale, epi);
 }
 
 namespace mira {

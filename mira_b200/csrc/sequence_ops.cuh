@@ -302,6 +302,10 @@ struct BmmParams {
   int64_t as[4];
   const float* b;
   int64_t bs[4];
+  // weight-only int8 B (b == nullptr): element (k, n) is RN(f32(b_i8[k, n]) * b_scale[n]), the
+  // reference's dequantize (ops.py:583-587) of a [K, N] weight with one scale per column
+  const int8_t* b_i8;
+  const float* b_scale;
   bool a_kfast, b_nfast;
   int n_steps;
   mira_bmm_step steps[MIRA_EPI_MAX_STEPS];
@@ -312,7 +316,7 @@ struct BmmParams {
   QuantScale q;
 };
 
-__device__ __forceinline__ void bmm_load_tiles(const BmmParams& p, const float* a, const float* b, int64_t m0,
+__device__ __forceinline__ void bmm_load_tiles(const BmmParams& p, const float* a, int64_t boff, int64_t m0,
                                                int64_t n0, int64_t k0, float (&ra)[8], float (&rb)[4]) {
   const int t = threadIdx.x;
 #pragma unroll
@@ -329,7 +333,11 @@ __device__ __forceinline__ void bmm_load_tiles(const BmmParams& p, const float* 
     int nn, kk;
     if (p.b_nfast) { nn = idx % BMM_BN; kk = idx / BMM_BN; } else { kk = idx % BMM_BK; nn = idx / BMM_BK; }
     const int64_t gn = n0 + nn, gk = k0 + kk;
-    rb[r] = (gn < p.n && gk < p.k) ? __ldg(b + gk * p.bs[2] + gn * p.bs[3]) : 0.0f;
+    const int64_t off = boff + gk * p.bs[2] + gn * p.bs[3];
+    if (p.b_i8 != nullptr)
+      rb[r] = (gn < p.n && gk < p.k) ? __fmul_rn(static_cast<float>(__ldg(p.b_i8 + off)), __ldg(p.b_scale + gn)) : 0.0f;
+    else
+      rb[r] = (gn < p.n && gk < p.k) ? __ldg(p.b + off) : 0.0f;
   }
 }
 
@@ -360,7 +368,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_f32_kernel(const BmmParams
   for (int64_t bz = blockIdx.z; bz < p.batches; bz += gridDim.z) {
   const int64_t b0 = bz / p.batch1, b1 = bz - b0 * p.batch1;
   const float* a = p.a + b0 * p.as[0] + b1 * p.as[1];
-  const float* b = p.b + b0 * p.bs[0] + b1 * p.bs[1];
+  const int64_t boff = b0 * p.bs[0] + b1 * p.bs[1];
   const int64_t m0 = int64_t(blockIdx.y) * BMM_BM, n0 = int64_t(blockIdx.x) * BMM_BN;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
 
@@ -371,13 +379,13 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_f32_kernel(const BmmParams
     for (int j = 0; j < BMM_TN; ++j) acc[i][j] = 0.0f;
 
   float ra[8], rb[4];
-  bmm_load_tiles(p, a, b, m0, n0, 0, ra, rb);
+  bmm_load_tiles(p, a, boff, m0, n0, 0, ra, rb);
   bmm_store_tiles(p, As[0], Bs[0], ra, rb);
   __syncthreads();
   const int nk = static_cast<int>((p.k + BMM_BK - 1) / BMM_BK);
   for (int kt = 0; kt < nk; ++kt) {
     const int cur = kt & 1;
-    if (kt + 1 < nk) bmm_load_tiles(p, a, b, m0, n0, int64_t(kt + 1) * BMM_BK, ra, rb);
+    if (kt + 1 < nk) bmm_load_tiles(p, a, boff, m0, n0, int64_t(kt + 1) * BMM_BK, ra, rb);
 #pragma unroll
     for (int kk = 0; kk < BMM_BK; ++kk) {
       const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][kk][ty * BMM_TM]);

@@ -294,6 +294,12 @@ def bmm_f32(batch0: int, batch1: int, m: int, n: int, k: int, a: View, b: View, 
     _lib.call("mira_cuda_bmm_f32", batch0, batch1, m, n, k, C.byref(av), C.byref(bv), C.byref(e))
 
 
+def bmm_f32_w8(batch0: int, batch1: int, m: int, n: int, k: int, a: View, b_i8: View, b_scale, epi: BmmEpi) -> None:
+    """bmm_f32 with int8 weights: b_i8 views q (itemsize 1), b_scale holds one f32 scale per column."""
+    av, bv, e = a.struct(), b_i8.struct(), epi.struct()
+    _lib.call("mira_cuda_bmm_f32_w8", batch0, batch1, m, n, k, C.byref(av), C.byref(bv), ptr(b_scale), C.byref(e))
+
+
 def layernorm_rows(x, rows: int, d: int, ld_x: int, gamma, beta, eps: float, out_f32=None, ld_f32: int = 0,
                    out_i8=None, ld_i8: int = 0, out_scale: float = 1.0) -> None:
     _lib.call("mira_cuda_layernorm_rows", ptr(x), rows, d, ld_x, ptr(gamma), ptr(beta), float(np.float32(eps)),

@@ -157,8 +157,13 @@ class CudaDevice:
         elif k == "bmm":
             av, bv, e = a["a"].struct(), a["b"].struct(), a["epi"].struct()
             keep += [av, bv, e]
-            fn = L.mira_cuda_bmm_f32
-            args = (a["batch0"], a["batch1"], a["m"], a["n"], a["k"], C.byref(av), C.byref(bv), C.byref(e))
+            if a.get("b_scale") is not None:
+                fn = L.mira_cuda_bmm_f32_w8
+                args = (a["batch0"], a["batch1"], a["m"], a["n"], a["k"], C.byref(av), C.byref(bv),
+                        ptr(a["b_scale"]), C.byref(e))
+            else:
+                fn = L.mira_cuda_bmm_f32
+                args = (a["batch0"], a["batch1"], a["m"], a["n"], a["k"], C.byref(av), C.byref(bv), C.byref(e))
         elif k == "layernorm":
             fn = L.mira_cuda_layernorm_rows
             args = (ptr(a["x"]), a["rows"], a["d"], a["ld_x"], ptr(a["gamma"]), ptr(a["beta"]), _f32(a["eps"]),
@@ -326,6 +331,7 @@ class Plan:
         self.skipped: set = set()
         self.kernel_counts: dict = {}
         self._kmax = None            # device scalar max|k| shared by the attention launches
+        self.w8_cache: dict = {}     # weight-only int8 matmul weights: value -> (int8 DVal, scales)
         self._build()
 
     # ------------------------------------------------------------------ helpers
@@ -1068,7 +1074,9 @@ class Plan:
         if op in self.attention:
             self._attention(op, self.attention[op])
             return
-        xa, wb = self._f32_dval(op.inputs[0]), self._f32_dval(op.inputs[1])
+        xa = self._f32_dval(op.inputs[0])
+        w8 = self._w8_weight(op.inputs[1])
+        wb = w8[0] if w8 is not None else self._f32_dval(op.inputs[1])
         oshape = tuple(op.result.type.shape)
         if len(oshape) > 4 or len(xa.shape) > 4 or len(wb.shape) > 4:
             raise UnsupportedOnCuda("matmul of more than 4 dimensions")
@@ -1094,11 +1102,32 @@ class Plan:
         if out.i8 is not None:
             ist = tuple(c * out.i8_ld for c in contiguous_strides(oshape[:-1])) + (1,)
             out_i8 = K.View(out.i8, (0,) * (4 - len(oshape)) + ist, itemsize=1)
+        bview = self._broadcast_view(wb, oshape[:-2] + (kdim, n))
+        if w8 is not None:
+            bview.itemsize = 1
         self._launch("bmm", batch0=batch[0], batch1=batch[1], m=m, n=n, k=kdim,
-                     a=self._broadcast_view(xa, oshape[:-2] + (m, kdim)),
-                     b=self._broadcast_view(wb, oshape[:-2] + (kdim, n)),
+                     a=self._broadcast_view(xa, oshape[:-2] + (m, kdim)), b=bview,
+                     b_scale=w8[1] if w8 is not None else None,
                      epi=K.BmmEpi(steps, out=out_view, out_i8=out_i8,
                                   out_scale=out.i8_scale if out.i8 is not None else 1.0))
+
+    def _w8_weight(self, v):
+        """(int8 DVal, per-column f32 scales) for a matmul weight that the reference stores as a
+        `dequantize` constant with one scale per output column (quantize.py:45-68 with axis = last,
+        ops.py:583-587): the int8 values and the scales are uploaded once and the matmul rebuilds
+        each weight as RN(f32(q) * scale) while staging it.  None for anything else."""
+        p = v.producer
+        if p is None or p.kind != "dequantize" or v.type.dtype != "f32":
+            return None
+        q = np.asarray(p.attrs["q"])
+        if q.dtype != np.int8 or q.ndim < 2 or p.attrs["axis"] % q.ndim != q.ndim - 1:
+            return None
+        hit = self.w8_cache.get(v)
+        if hit is None:
+            scale = np.ascontiguousarray(np.asarray(p.attrs["scale"], np.float32).reshape(-1))
+            hit = (DVal(tuple(q.shape), "rows", f32=self._upload(np.ascontiguousarray(q))), self._upload(scale))
+            self.w8_cache[v] = hit
+        return hit
 
     def _op_softmax(self, op) -> None:
         x = self.vals[op.inputs[0]]

@@ -37,6 +37,14 @@ def quantize_array(w: np.ndarray, axis: int) -> tuple[np.ndarray, np.ndarray]:
     return q, scale
 
 
+def dequantize(q: np.ndarray, scale: np.ndarray, axis: int) -> np.ndarray:
+    """The weight-only int8 constant: f32(q) * scale broadcast along `axis`, one f32 rounding per
+    weight.  Reference ops.py:583-587 (with dtype f32)."""
+    shape = [1] * q.ndim
+    shape[axis] = -1
+    return q.astype(np.float32) * np.asarray(scale, np.float32).reshape(shape)
+
+
 def combined_scale(x_scale: float, w_scale: np.ndarray) -> np.ndarray:
     """float64 x_scale * w_scale[c], the dequant factor of ops.py:619 / ops.py:633."""
     return np.float64(x_scale) * np.asarray(w_scale).astype(np.float64)

@@ -232,9 +232,12 @@ class FakeDevice:
 
     # ------------------------------------------------------------------ sequence ops
 
-    def _bmm(self, batch0, batch1, m, n, k, a, b, epi):
+    def _bmm(self, batch0, batch1, m, n, k, a, b, epi, b_scale=None):
         av = _strided(a, (batch0, batch1, m, k))
-        bv = _strided(b, (batch0, batch1, k, n))
+        if b_scale is None:
+            bv = _strided(b, (batch0, batch1, k, n))
+        else:                        # int8 weights, one scale per column (the reference's dequantize)
+            bv = _strided(b, (batch0, batch1, k, n), np.int8).astype(np.float32) * b_scale.view(np.float32, (n,))
         y = np.matmul(av.astype(np.float32), bv.astype(np.float32))
         for st in epi.steps:
             if st.operand == "none":

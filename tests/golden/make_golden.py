@@ -2,6 +2,7 @@
 
     python tests/golden/make_golden.py path/to/reference      (or set $MIRA_PATH)
     python tests/golden/make_golden.py path/to/reference --only-sequence   (sequence.npz alone)
+    python tests/golden/make_golden.py path/to/reference --only-weight-only   (weight_only.npz alone)
 
 The reference (a pure-Python package) is imported from the given checkout.  Every expected value comes from the
 reference's own code: mira.ops.evaluate for single ops (ops.py:602-634 quantized ops, 192-199
@@ -186,6 +187,7 @@ def main(ref_path: str) -> None:
         progs[f"{name}_image"] = np.int64(kw.get("image", 0))
     _save("programs", **progs)
     sequence(ref_path)
+    weight_only(ref_path)
 
 
 TINY_TRANSFORMER = dict(seq=16, layers=2, d_model=64, heads=4, d_mlp=128, vocab=32, max_seq=16)
@@ -228,12 +230,39 @@ def sequence(ref_path: str) -> None:
     _save("sequence", **out)
 
 
+def weight_only(ref_path: str) -> None:
+    """weight_only.npz: the `dequantize` constant (ops.py:583-587) of weights quantized by
+    quantize_array (quantize.py:24-31) along either axis, and whole programs compiled with
+    quantize="int8" (quantize.py:45-68) on the reference cpu target."""
+    mira, compiler, ir, O, Q = _import_reference(ref_path)
+    rng = np.random.default_rng(20261203)
+    out = {}
+    w = (rng.standard_normal((96, 40)) * rng.uniform(0.01, 3, (1, 40))).astype(np.float32)
+    w[:, 7] = 0.0                                    # an all-zero column: scale 1.0
+    for axis in (0, 1):
+        q, s = Q.quantize_array(w, axis)
+        out.update({f"q_axis{axis}": q, f"s_axis{axis}": s,
+                    f"w_axis{axis}": O.evaluate("dequantize", [], {"q": q, "scale": s, "axis": axis, "dtype": "f32"})})
+    sys.path.insert(0, str(ROOT))
+    from mira_b200 import configs
+    for name, batch, kw in (("mlp", 8, {}), ("transformer", 2, TINY_TRANSFORMER)):
+        g = configs.BUILDERS[name](batch, **kw)
+        prog = compiler.compile_ir(g, "cpu", quantize="int8", precision=None)
+        feeds = configs.random_inputs(g, 1)
+        key = next(iter(feeds))
+        out.update({f"{name}_in": feeds[key], f"{name}_out": prog.run(feeds),
+                    f"{name}_n_dequantize": np.int64(sum(op.kind == "dequantize" for op in prog.graph.ops))})
+    _save("weight_only", **out)
+
+
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     path = args[0] if args else os.environ.get("MIRA_PATH")
     if not path:
-        raise SystemExit("usage: make_golden.py path/to/reference [--only-sequence] (or set MIRA_PATH)")
+        raise SystemExit("usage: make_golden.py path/to/reference [--only-sequence|--only-weight-only] (or set MIRA_PATH)")
     if "--only-sequence" in sys.argv:
         sequence(path)
+    elif "--only-weight-only" in sys.argv:
+        weight_only(path)
     else:
         main(path)

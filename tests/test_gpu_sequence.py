@@ -110,6 +110,36 @@ def test_bmm_f32_within_error_bound(cuda_device, shape, a_t, b_t):
     assert np.all(np.abs(got - blas) <= 2 * bound + 1e-30)
 
 
+@pytest.mark.parametrize("b0,b1,m,n,k", [(1, 1, 64, 300, 200), (2, 3, 17, 96, 64), (1, 1, 1, 4096, 768),
+                                         (1, 1, 130, 10, 1000)])
+def test_bmm_f32_w8_equals_f32_bmm_on_dequantized_weights(cuda_device, b0, b1, m, n, k):
+    """Weight-only int8 B (one [K, N] weight broadcast over the batch, per-column scales): the
+    staged weights are the reference's dequantized values exactly, so the product is bit-identical
+    to the f32 bmm over those values, and within the f32 error bound of the exact product."""
+    K, DB = _k()
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((b0, b1, m, k)).astype(np.float32)
+    q, scale = ref.quantize_array((rng.standard_normal((k, n)) * rng.uniform(0.01, 2, (1, n))).astype(np.float32), 1)
+    w = ref.dequantize(q, scale, 1)
+    ab, qb, sb, wb = DB.from_array(a), DB.from_array(q), DB.from_array(scale), DB.from_array(w)
+    bias = rng.standard_normal(n).astype(np.float32)
+    biasb = DB.from_array(bias)
+    av = K.View(ab, (b1 * m * k, m * k, k, 1))
+    outs = []
+    for w8 in (True, False):
+        yb = DB(b0 * b1 * m * n * 4)
+        epi = K.BmmEpi([K.BmmStep("add", "view", view=K.View(biasb, (0, 0, 0, 1)))],
+                       out=K.View(yb, (b1 * m * n, m * n, n, 1)))
+        if w8:
+            K.bmm_f32_w8(b0, b1, m, n, k, av, K.View(qb, (0, 0, n, 1), itemsize=1), sb, epi)
+        else:
+            K.bmm_f32(b0, b1, m, n, k, av, K.View(wb, (0, 0, n, 1)), epi)
+        outs.append(yb.download((b0, b1, m, n), np.float32))
+    _bits_equal(outs[0], outs[1])
+    exact, bound = ref.matmul_error_bound(a, np.broadcast_to(w, (b0, b1, k, n)))
+    assert np.all(np.abs(outs[0] - (exact + bias)) <= bound + np.abs(exact + bias) * 2 ** -23 + 1e-30)
+
+
 def test_bmm_attention_scores_epilogue(cuda_device):
     """q @ k^T * (1/8) + causal mask, the mask broadcast over batch and heads (stride-0 view)."""
     K, DB = _k()
@@ -259,3 +289,22 @@ def test_transformer_prefill_matches_cpu(cuda_device, kw, batch):
         # a flipped int8 activation moves a logit by about one quantization step of one input
         assert err.max() <= 0.05 * scale
         assert close.mean() >= 0.5
+
+
+@pytest.mark.skipif(mira_missing, reason="MIRA host framework (package `mira`) not importable")
+@pytest.mark.parametrize("name,batch,kw", [("mlp", 64, {}),
+                                           ("transformer", 2, dict(seq=64, layers=2, d_model=128, heads=4,
+                                                                   d_mlp=256, vocab=64, max_seq=64))])
+def test_weight_only_int8_matches_cpu(cuda_device, name, batch, kw):
+    """`quantize="int8"`: int8 weights on the device, f32 activations; against the reference cpu
+    target within f32 tolerance (no int8 activation rounding to flip)."""
+    g_cpu, g_cuda = configs.BUILDERS[name](batch, **kw), configs.BUILDERS[name](batch, **kw)
+    cpu = compiler.compile_ir(g_cpu, "cpu", quantize="int8", precision=None)
+    cuda = compiler.compile_ir(g_cuda, "cuda", quantize="int8")
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    feeds = configs.random_inputs(g_cpu, 1)
+    want = cpu.run(feeds)
+    for _ in range(2):
+        got = cuda.run(feeds)
+        assert got.shape == want.shape and got.dtype == want.dtype
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * np.abs(want).max())

@@ -141,3 +141,18 @@ def test_sequence_ops_match_reference_fixtures():
     y = ref.matmul_f32(z["mm_a"], z["mm_b"], (("mul", 0, False), ("add", 1, False)), (np.float32(0.125), z["mm_mask"]))
     np.testing.assert_allclose(y, z["mm_y"], rtol=1e-6, atol=1e-5)
     _same(ref.embed(z["ga_table"], z["ga_idx"]), z["ga_y"])
+
+
+def test_weight_only_dequantize_golden():
+    """quantize_array along both axes (an all-zero column gets scale 1) and the dequantize constant,
+    bit for bit against the reference's own quantize_array and ops.evaluate("dequantize")."""
+    z = _load("weight_only")
+    w = z["w_axis1"]
+    for axis in (0, 1):
+        q, s = z[f"q_axis{axis}"], z[f"s_axis{axis}"]
+        d = ref.dequantize(q, s, axis)
+        assert d.dtype == np.float32
+        assert np.array_equal(d.view(np.uint32), z[f"w_axis{axis}"].view(np.uint32))
+    assert z["s_axis0"].shape == (96,) and z["s_axis1"].shape == (40,) and z["s_axis1"][7] == 1.0
+    assert not z["q_axis1"][:, 7].any()
+    assert w.shape == (96, 40)

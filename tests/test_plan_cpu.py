@@ -159,6 +159,37 @@ def test_transformer_small_plan_matches_cpu():
     assert "bmm" not in counts and "softmax" not in counts and "quantize_rows" not in counts
 
 
+@pytest.mark.parametrize("name,batch,kw", [("mlp", 8, {}), ("transformer", 2, TINY_TF)])
+def test_weight_only_int8_plan_matches_cpu(name, batch, kw):
+    """`quantize="int8"` (weight-only): every large matmul weight becomes a `dequantize` constant;
+    on cuda they stay int8 on the device and feed the weight-only bmm, whole graph in one segment."""
+    g_cpu, g_cuda = configs.BUILDERS[name](batch, **kw), configs.BUILDERS[name](batch, **kw)
+    cpu = compiler.compile_ir(g_cpu, "cpu", quantize="int8", precision=None)
+    dev = FakeDevice()
+    cuda = compiler.compile_ir(g_cuda, "cuda", quantize="int8", executor=dev)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    deq = [op for op in cuda.graph.ops if op.kind == "dequantize"]
+    assert deq and all(np.asarray(op.attrs["q"]).dtype == np.int8 for op in deq)
+    plan = cuda.segments[0].executable.plan
+    w8 = [l for l in plan.launches if l.kind == "bmm" and l.args.get("b_scale") is not None]
+    assert len(w8) == len(deq)
+    feeds = configs.random_inputs(cpu.graph, 1)
+    want = cpu.run(feeds)
+    got = cuda.run(feeds)
+    assert got.shape == want.shape and got.dtype == want.dtype
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("name,batch,kw,key", [("mlp", 8, {}, "x"), ("transformer", 2, TINY_TF, "tok")])
+def test_weight_only_int8_plan_matches_stored_reference_output(name, batch, kw, key):
+    """Weight-only programs against the reference cpu target's stored outputs."""
+    z = np.load(Path(__file__).resolve().parent / "golden" / "weight_only.npz")
+    g = configs.BUILDERS[name](batch, **kw)
+    prog = compiler.compile_ir(g, "cuda", quantize="int8", executor=FakeDevice())
+    assert sum(op.kind == "dequantize" for op in prog.graph.ops) == int(z[f"{name}_n_dequantize"])
+    np.testing.assert_allclose(prog.run({key: z[f"{name}_in"]}), z[f"{name}_out"], rtol=1e-4, atol=1e-4)
+
+
 def test_unfused_attention_ops_plan_matches_cpu():
     """The generic kernels (strided bmm, softmax) when the chain does not have the fused form:
     here the scores are also a graph output."""
