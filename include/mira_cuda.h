@@ -357,6 +357,20 @@ int mira_cuda_absmax_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const m
 int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* src,
                             const mira_view4* dst);
 
+/* Slices at runtime positions (reference dynamic_slice / dynamic_update_slice, ops.py:533-576),
+ * for 4-byte elements (f32 or i32) in views of at most 4 dimensions (shapes padded with leading 1s
+ * to 4).  `start` is DEVICE memory holding `rank` int32 start entries for the last `rank`
+ * dimensions (the leading ones start at 0 and must be taken whole); every entry is clamped to
+ * [0, dims - window] like the reference's _clamped_starts (ops.py:536-537).  Reading the start on
+ * the device keeps a captured CUDA graph valid while the position changes between steps.
+ *   dynamic_slice:        out[e] = x[start + e] for e < size.
+ *   dynamic_update_slice: x[start + e] = upd[e] for e < upd_dims, in place (the reference returns an
+ *                         updated copy; a caller that needs the old x copies it first). */
+int mira_cuda_dynamic_slice(const mira_view4* x, const int64_t* x_dims, const int32_t* start, int64_t rank,
+                            const int64_t* size, const mira_view4* out);
+int mira_cuda_dynamic_update_slice(const mira_view4* x, const int64_t* x_dims, const mira_view4* upd,
+                                   const int64_t* upd_dims, const int32_t* start, int64_t rank);
+
 #ifdef __cplusplus
 }
 #endif

@@ -157,14 +157,42 @@ def transformer(batch: int = 1, seed: int = 0, seq: int = 1024, layers: int = 12
     then a final layernorm and the LM head.  Weights and biases N(0, 0.02), layernorm gains
     1 + N(0, 0.02) and shifts N(0, 0.02); the mask is 0 on and below the diagonal and -10000 above
     (gpt.mira causal_mask).  Tables are drawn at `max_seq` rows so every `seq` sees the same weights."""
+    return _gpt(batch, seed, seq, layers, d_model, heads, d_mlp, vocab, max_seq, step=False)
+
+
+def transformer_step(batch: int = 1, seed: int = 0, layers: int = 12, d_model: int = 768, heads: int = 12,
+                     d_mlp: int = 3072, vocab: int = 256, max_seq: int = 1024):
+    """One decode step of the config-5 transformer (same weights as `transformer` with the same
+    seed): one new token per sequence at a runtime position p, with a key/value cache per layer.
+
+    Inputs: tok i32[B, 1]; pos2 i32[2] = (p, 0) and pos4 i32[4] = (0, 0, p, 0), the start vectors
+    of the reference's runtime-position slices (ops.py:533-576); then k0, v0, k1, v1, ... f32[B,
+    heads, max_seq, d_head], the caches holding positions < p.  The step reads the position row and
+    the causal-mask row p with dynamic_slice, writes the new key and value at row p with
+    dynamic_update_slice, and attends over all max_seq cache rows (rows after p are masked to
+    -10000 like the prefill's upper triangle).  Outputs: logits f32[B, 1, vocab], then the
+    updated caches in input order."""
+    return _gpt(batch, seed, 1, layers, d_model, heads, d_mlp, vocab, max_seq, step=True)
+
+
+def _gpt(batch, seed, seq, layers, d_model, heads, d_mlp, vocab, max_seq, step):
     ir, TT = _ir()
     if d_model % heads:
         raise ValueError("d_model must be a multiple of heads")
+    if seq > max_seq:
+        raise ValueError("seq must not exceed max_seq")
     dh = d_model // heads
     n = _Net.__new__(_Net)
     n.ir = ir
     n.x = ir.Value(TT("i32", (batch, seq)), name="tok")
-    n.g = ir.Graph("transformer", [n.x], [], [])
+    inputs = [n.x]
+    if step:
+        pos2 = ir.Value(TT("i32", (2,)), name="pos2")
+        pos4 = ir.Value(TT("i32", (4,)), name="pos4")
+        caches = [ir.Value(TT("f32", (batch, heads, max_seq, dh)), name=f"{kv}{l}")
+                  for l in range(layers) for kv in ("k", "v")]
+        inputs += [pos2, pos4] + caches
+    n.g = ir.Graph("transformer_step" if step else "transformer", inputs, [], [])
     n.rng = np.random.default_rng(seed)
     std = 0.02
 
@@ -180,26 +208,43 @@ def transformer(batch: int = 1, seed: int = 0, seq: int = 1024, layers: int = 12
         return n.op("add", [y, n.const(normal(fout))]) if bias else y
 
     emb = normal(vocab, d_model)
-    pos = normal(max_seq, d_model)[:seq]
-    mask = np.where(np.arange(seq)[:, None] >= np.arange(seq)[None, :], 0.0, -10000.0).astype(np.float32)
-    h = n.op("add", [n.op("gather", [n.const(emb), n.x], {"axis": 0}), n.const(pos)])
-    for _ in range(layers):
+    pos_table = normal(max_seq, d_model)
+    if step:
+        causal = np.where(np.arange(max_seq)[:, None] >= np.arange(max_seq)[None, :], 0.0, -10000.0)
+        pos = n.op("dynamic_slice", [n.const(pos_table), pos2], {"size": (1, d_model)})
+        mask = n.op("dynamic_slice", [n.const(causal.astype(np.float32)), pos2], {"size": (1, max_seq)})
+    else:
+        pos = n.const(pos_table[:seq])
+        mask = n.const(np.where(np.arange(seq)[:, None] >= np.arange(seq)[None, :], 0.0, -10000.0).astype(np.float32))
+    h = n.op("add", [n.op("gather", [n.const(emb), n.x], {"axis": 0}), pos])
+    new_caches = []
+    for layer in range(layers):
         x = ln(h)
         q, k, v = (dense(x, d_model, d_model) for _ in range(3))
         split = lambda t: n.op("reshape", [t], {"shape": (batch, seq, heads, dh)})
         qh = n.op("transpose", [split(q)], {"perm": (0, 2, 1, 3)})
-        kt = n.op("transpose", [split(k)], {"perm": (0, 2, 3, 1)})
-        vh = n.op("transpose", [split(v)], {"perm": (0, 2, 1, 3)})
+        if step:
+            kc = n.op("dynamic_update_slice",
+                      [caches[2 * layer], n.op("transpose", [split(k)], {"perm": (0, 2, 1, 3)}), pos4])
+            vh = n.op("dynamic_update_slice",
+                      [caches[2 * layer + 1], n.op("transpose", [split(v)], {"perm": (0, 2, 1, 3)}), pos4])
+            kt = n.op("transpose", [kc], {"perm": (0, 1, 3, 2)})
+            new_caches += [kc, vh]
+        else:
+            kt = n.op("transpose", [split(k)], {"perm": (0, 2, 3, 1)})
+            vh = n.op("transpose", [split(v)], {"perm": (0, 2, 1, 3)})
         s = n.op("matmul", [qh, kt])
         s = n.op("mul", [s, n.const(np.float32(1.0 / np.sqrt(dh)))])
-        s = n.op("add", [s, n.const(mask)])
+        s = n.op("add", [s, mask])
         o = n.op("matmul", [n.op("softmax", [s], {"axis": -1}), vh])
         o = n.op("reshape", [n.op("transpose", [o], {"perm": (0, 2, 1, 3)})], {"shape": (batch, seq, d_model)})
         h = n.op("add", [dense(o, d_model, d_model), h])
         m = n.op("gelu", [dense(ln(h), d_model, d_mlp)])
         h = n.op("add", [dense(m, d_mlp, d_model), h])
     logits = dense(ln(h), d_model, vocab, bias=False)
-    return n.finish(logits)
+    n.g.outputs = [logits] + new_caches
+    n.g.verify()
+    return n.g
 
 
 BUILDERS: dict[str, Callable] = {"mlp": mlp, "resnet18": resnet18, "mobilenet_v2": mobilenet_v2,

@@ -1070,6 +1070,49 @@ extern "C" int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64
 
 namespace mira {
 
+static int dyn_window(DeviceState* dev, const mira_view4* src, const mira_view4* dst, const int64_t* n,
+                      const int64_t* dims, const int32_t* start, int64_t rank, int update) {
+  MIRA_CHECK_ARG(src != nullptr && dst != nullptr && n != nullptr && dims != nullptr, "null argument");
+  MIRA_CHECK_ARG(rank >= 0 && rank <= 4 && (rank == 0 || start != nullptr), "start vector: rank 0..4, device i32");
+  int64_t total = 1;
+  for (int i = 0; i < 4; ++i) {
+    MIRA_CHECK_ARG(n[i] >= 0 && n[i] <= dims[i], "the window must fit in the full shape");
+    MIRA_CHECK_ARG(i >= 4 - rank || n[i] == dims[i], "dimensions without a start entry are copied whole");
+    total *= n[i];
+  }
+  if (total == 0) return MIRA_CUDA_OK;
+  MIRA_CHECK_ARG(src->ptr != nullptr && dst->ptr != nullptr, "null view");
+  DynWindowParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.src = static_cast<const uint32_t*>(src->ptr);
+  p.dst = static_cast<uint32_t*>(dst->ptr);
+  for (int i = 0; i < 4; ++i) {
+    p.ss[i] = src->stride[i]; p.ds[i] = dst->stride[i]; p.n[i] = n[i]; p.dims[i] = dims[i];
+  }
+  p.start = start;
+  p.rank = int(rank);
+  p.update = update;
+  const int threads = 256;
+  dyn_window_kernel<<<grid_for(dev, (total / (n[3] > 0 ? n[3] : 1)) * 32, threads), threads, 0, dev->stream>>>(p);
+  return after_launch("dyn_window_kernel");
+}
+
+}  // namespace mira
+
+extern "C" int mira_cuda_dynamic_slice(const mira_view4* x, const int64_t* x_dims, const int32_t* start, int64_t rank,
+                                       const int64_t* size, const mira_view4* out) {
+  MIRA_GET_DEVICE(dev);
+  return dyn_window(dev, x, out, size, x_dims, start, rank, 0);
+}
+
+extern "C" int mira_cuda_dynamic_update_slice(const mira_view4* x, const int64_t* x_dims, const mira_view4* upd,
+                                              const int64_t* upd_dims, const int32_t* start, int64_t rank) {
+  MIRA_GET_DEVICE(dev);
+  return dyn_window(dev, upd, x, upd_dims, x_dims, start, rank, 1);
+}
+
+namespace mira {
+
 // The f32 batched matmul behind mira_cuda_bmm_f32 (b_scale == nullptr: b holds f32) and
 // mira_cuda_bmm_f32_w8 (b holds int8 weights, dequantized with b_scale[n] as tiles are loaded).
 static int bmm_launch(DeviceState* dev, int64_t batch0, int64_t batch1, int64_t m, int64_t n, int64_t k,

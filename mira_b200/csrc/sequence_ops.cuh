@@ -290,6 +290,56 @@ __global__ void copy_view_kernel(const View4 v) {
   }
 }
 
+// ---------------------------------------------------------------- slices at runtime positions
+
+// The reference's dynamic_slice / dynamic_update_slice (ops.py:533-576): a window of shape n at a
+// start position read from device memory (so a captured CUDA graph stays valid while the position
+// changes), each start clamped to [0, dims - n] like _clamped_starts (ops.py:536-537).  The start
+// vector has `rank` entries for the last `rank` of the 4 dimensions; the others start at 0.
+// update == 0: dst[e] = src[start + e] (slice); update == 1: dst[start + e] = src[e] (update).
+// Elements are 4 bytes (f32 or i32), copied as bits.
+struct DynWindowParams {
+  const uint32_t* src;
+  int64_t ss[4];
+  uint32_t* dst;
+  int64_t ds[4];
+  int64_t n[4];       // window shape
+  int64_t dims[4];    // full shape of the windowed side
+  const int32_t* start;
+  int rank;
+  int update;
+};
+
+// One warp per innermost window row.
+__global__ void dyn_window_kernel(const DynWindowParams p) {
+  __shared__ int64_t s[4];
+  if (threadIdx.x < 4) {
+    const int d = threadIdx.x, j = d - (4 - p.rank);
+    int64_t v = 0;
+    if (j >= 0) {
+      v = __ldg(p.start + j);
+      v = v < 0 ? 0 : v;
+      v = v > p.dims[d] - p.n[d] ? p.dims[d] - p.n[d] : v;
+    }
+    s[d] = v;
+  }
+  __syncthreads();
+  const int64_t ws0 = p.update ? 0 : s[0], ws1 = p.update ? 0 : s[1], ws2 = p.update ? 0 : s[2],
+                ws3 = p.update ? 0 : s[3];
+  const int64_t wd0 = p.update ? s[0] : 0, wd1 = p.update ? s[1] : 0, wd2 = p.update ? s[2] : 0,
+                wd3 = p.update ? s[3] : 0;
+  const int64_t rows = p.n[0] * p.n[1] * p.n[2];
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * int64_t(blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t i2 = row % p.n[2], i01 = row / p.n[2];
+    const int64_t i1 = i01 % p.n[1], i0 = i01 / p.n[1];
+    const uint32_t* src = p.src + (ws0 + i0) * p.ss[0] + (ws1 + i1) * p.ss[1] + (ws2 + i2) * p.ss[2] + ws3 * p.ss[3];
+    uint32_t* dst = p.dst + (wd0 + i0) * p.ds[0] + (wd1 + i1) * p.ds[1] + (wd2 + i2) * p.ds[2] + wd3 * p.ds[3];
+    for (int64_t i3 = lane; i3 < p.n[3]; i3 += 32) dst[i3 * p.ds[3]] = src[i3 * p.ss[3]];
+  }
+}
+
 // ---------------------------------------------------------------- batched f32 matmul
 
 constexpr int BMM_BM = 128, BMM_BN = 64, BMM_BK = 16, BMM_THREADS = 256;

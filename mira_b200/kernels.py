@@ -294,6 +294,27 @@ def bmm_f32(batch0: int, batch1: int, m: int, n: int, k: int, a: View, b: View, 
     _lib.call("mira_cuda_bmm_f32", batch0, batch1, m, n, k, C.byref(av), C.byref(bv), C.byref(e))
 
 
+def dims4(shape) -> "C.Array":
+    """A shape of at most 4 dimensions padded with leading 1s, as the int64[4] the C-ABI takes."""
+    shape = tuple(int(d) for d in shape)
+    if len(shape) > 4:
+        raise ValueError("at most 4 dimensions")
+    return (C.c_int64 * 4)(*((1,) * (4 - len(shape)) + shape))
+
+
+def dynamic_slice(x: View, x_shape, start, rank: int, size, out: View) -> None:
+    """out = x[start : start + size] with the start vector (int32, `rank` entries) in device memory."""
+    xv, ov = x.struct(), out.struct()
+    _lib.call("mira_cuda_dynamic_slice", C.byref(xv), dims4(x_shape), ptr(start), rank, dims4(size), C.byref(ov))
+
+
+def dynamic_update_slice(x: View, x_shape, upd: View, upd_shape, start, rank: int) -> None:
+    """x[start : start + upd_shape] = upd in place, start vector in device memory."""
+    xv, uv = x.struct(), upd.struct()
+    _lib.call("mira_cuda_dynamic_update_slice", C.byref(xv), dims4(x_shape), C.byref(uv), dims4(upd_shape),
+              ptr(start), rank)
+
+
 def bmm_f32_w8(batch0: int, batch1: int, m: int, n: int, k: int, a: View, b_i8: View, b_scale, epi: BmmEpi) -> None:
     """bmm_f32 with int8 weights: b_i8 views q (itemsize 1), b_scale holds one f32 scale per column."""
     av, bv, e = a.struct(), b_i8.struct(), epi.struct()

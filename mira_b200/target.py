@@ -76,6 +76,9 @@ class CudaDevice:
     def sync(self) -> None:
         _lib.call("mira_cuda_sync")
 
+    def zero(self, buf, nbytes: int) -> None:
+        _lib.call("mira_cuda_memset", ptr(buf), 0, C.c_size_t(nbytes))
+
     def graph_begin(self) -> None:
         _lib.call("mira_cuda_graph_begin")
 
@@ -164,6 +167,16 @@ class CudaDevice:
             else:
                 fn = L.mira_cuda_bmm_f32
                 args = (a["batch0"], a["batch1"], a["m"], a["n"], a["k"], C.byref(av), C.byref(bv), C.byref(e))
+        elif k == "dyn_slice":
+            xv, ov, xd, sz = a["x"].struct(), a["out"].struct(), K.dims4(a["x_shape"]), K.dims4(a["size"])
+            keep += [xv, ov, xd, sz]
+            fn = L.mira_cuda_dynamic_slice
+            args = (C.byref(xv), xd, ptr(a["start"]), a["rank"], sz, C.byref(ov))
+        elif k == "dyn_update":
+            xv, uv, xd, ud = a["x"].struct(), a["upd"].struct(), K.dims4(a["x_shape"]), K.dims4(a["upd_shape"])
+            keep += [xv, uv, xd, ud]
+            fn = L.mira_cuda_dynamic_update_slice
+            args = (C.byref(xv), xd, C.byref(uv), ud, ptr(a["start"]), a["rank"])
         elif k == "layernorm":
             fn = L.mira_cuda_layernorm_rows
             args = (ptr(a["x"]), a["rows"], a["d"], a["ld_x"], ptr(a["gamma"]), ptr(a["beta"]), _f32(a["eps"]),
@@ -332,6 +345,7 @@ class Plan:
         self.kernel_counts: dict = {}
         self._kmax = None            # device scalar max|k| shared by the attention launches
         self.w8_cache: dict = {}     # weight-only int8 matmul weights: value -> (int8 DVal, scales)
+        self.aliases: dict = {}      # dynamic_update_slice result -> the graph input it updated in place
         self._build()
 
     # ------------------------------------------------------------------ helpers
@@ -1129,6 +1143,70 @@ class Plan:
             self.w8_cache[v] = hit
         return hit
 
+    # ------------------------------------------------------------------ runtime-position slices
+
+    def _start_buf(self, v):
+        """Device int32 start vector of a dynamic slice: a graph input, or an uploaded constant."""
+        c = self._const(v)
+        if c is not None:
+            return self._upload(np.ascontiguousarray(np.asarray(c, np.int32).reshape(-1)))
+        dv = self.vals[v]
+        if dv.i32 is None:
+            raise UnsupportedOnCuda("dynamic slice start vectors must be graph inputs or constants on cuda")
+        return dv.i32
+
+    def _data_view(self, v) -> K.View:
+        """4-D view of the 4-byte elements of `v` (an uploaded constant or a value on the device)."""
+        c = self._const(v)
+        r = v.type.rank
+        if c is not None:
+            c = np.ascontiguousarray(np.asarray(c, v.type.np_dtype))
+            return K.View(self._upload(c), (0,) * (4 - r) + contiguous_strides(tuple(c.shape)))
+        dv = self.vals[v]
+        if dv.i32 is not None:
+            return K.View(dv.i32, (0,) * (4 - r) + contiguous_strides(tuple(dv.shape)))
+        if dv.f32 is None or dv.layout != "rows":
+            raise UnsupportedOnCuda("dynamic slice of a value without a row-major f32 form")
+        return self._view4(dv)[1]
+
+    def _op_dynamic_slice(self, op) -> None:
+        """Reference ops.py:550-553: the window at the clamped runtime start, copied on the device."""
+        x, start = op.inputs
+        size = tuple(int(n) for n in op.attrs["size"])
+        rank = x.type.rank
+        dv = DVal(size, "rows", f32=self._alloc(max(int(np.prod(size, dtype=np.int64)), 1) * 4))
+        self.vals[op.result] = dv
+        self._launch("dyn_slice", x=self._data_view(x), x_shape=tuple(x.type.shape), start=self._start_buf(start),
+                     rank=rank, size=size, out=K.View(dv.f32, (0,) * (4 - rank) + contiguous_strides(size)))
+        if op.result in self.i8_req:
+            dv.i8_scale = self.i8_req[op.result]
+            dv.i8_ld = K.round_up(dv.cols, 16)
+            dv.i8 = self._alloc(dv.rows * dv.i8_ld, zero=True)
+            self._fill_i8(op.result)
+
+    def _op_dynamic_update_slice(self, op) -> None:
+        """Reference ops.py:565-570.  When x is a graph input used by nothing else (a key/value
+        cache fed back each step) the update is written into x's own device buffer, so the result
+        aliases the input; otherwise x is copied first."""
+        x, upd, start = op.inputs
+        shape = tuple(x.type.shape)
+        rank = len(shape)
+        xdv = self.vals.get(x)
+        in_place = (x in self.g.inputs and self.users.get(x, []) == [op] and x not in self.g.outputs
+                    and xdv is not None and xdv.f32 is not None and xdv.layout == "rows" and xdv.is_contiguous
+                    and not xdv.offset)
+        if in_place:
+            buf = xdv.f32
+        else:
+            buf = self._alloc(max(int(np.prod(shape, dtype=np.int64)), 1) * 4)
+            self._launch("copy_view", shape=(1,) * (4 - rank) + shape, src=self._data_view(x),
+                         dst=K.View(buf, (0,) * (4 - rank) + contiguous_strides(shape)))
+        self.vals[op.result] = DVal(shape, "rows", f32=buf)
+        self.aliases[op.result] = x if in_place else None
+        self._launch("dyn_update", x=K.View(buf, (0,) * (4 - rank) + contiguous_strides(shape)), x_shape=shape,
+                     upd=self._data_view(upd), upd_shape=tuple(upd.type.shape), start=self._start_buf(start),
+                     rank=rank)
+
     def _op_softmax(self, op) -> None:
         x = self.vals[op.inputs[0]]
         src, ld = self._rows_of(op.inputs[0])
@@ -1163,8 +1241,11 @@ class Plan:
             add_op, val = add
             self.skipped.add(add_op)
             target = add_op.result
-            period = val.size // d
-            addend = self._upload(np.ascontiguousarray(val.reshape(period, d), np.float32))
+            if isinstance(val, DVal):         # a row sliced at a runtime position, already on the device
+                period, addend = val.numel // d, val.f32
+            else:
+                period = val.size // d
+                addend = self._upload(np.ascontiguousarray(val.reshape(period, d), np.float32))
         out = self._new_out(target)
         if out.f32 is None:
             out.f32 = self._alloc(out.numel * 4)
@@ -1182,8 +1263,18 @@ class Plan:
         other = add.inputs[1] if add.inputs[0] is op.result else add.inputs[0]
         val = self._const(other)
         rshape = tuple(op.result.type.shape)
+        if val is None and _const_row_slice(other) and other in self.vals:
+            dv = self.vals[other]
+            if dv.f32 is not None and dv.is_contiguous and not dv.offset:
+                val = dv
         if val is None or other is op.result or tuple(add.result.type.shape) != rshape:
             return None
+        if isinstance(val, DVal):
+            vshape = tuple(val.shape)
+            while vshape and vshape[0] == 1:
+                vshape = vshape[1:]
+            ok = vshape and vshape[-1] == rshape[-1] and rshape[len(rshape) - len(vshape):] == vshape
+            return (add, val) if ok else None
         vshape = tuple(val.shape)
         while vshape and vshape[0] == 1:
             vshape = vshape[1:]
@@ -1199,6 +1290,13 @@ class Plan:
                          ld_q=dv.i8_ld)
 
 
+def _const_row_slice(v) -> bool:
+    """v is a dynamic_slice of a constant table (a position-embedding row read at runtime)."""
+    p = v.producer
+    return (p is not None and p.kind == "dynamic_slice" and p.inputs[0].producer is not None
+            and p.inputs[0].producer.is_constant_like)
+
+
 def supported_reason(op) -> Optional[str]:
     """None if the cuda target runs `op`, else why not (reference Target.check, base.py:22-23)."""
     k = op.kind
@@ -1212,6 +1310,13 @@ def supported_reason(op) -> Optional[str]:
         if (tp is None or not tp.is_constant_like or table.type.rank != 2 or table.type.dtype != "f32"
                 or idx.type.dtype != "i32" or op.attrs.get("axis", 0) not in (0, -2)):
             return "gather: the cuda target looks up rows of a constant f32 table by int32 ids"
+        return None
+    if k in ("dynamic_slice", "dynamic_update_slice"):
+        x, start = op.inputs[0], op.inputs[-1]
+        if x.type.rank > 4 or x.type.dtype not in ("f32", "i32") or start.type.dtype != "i32":
+            return f"{k}: 4-byte elements, at most 4 dimensions, int32 starts on cuda"
+        if start.producer is not None and not start.producer.is_constant_like:
+            return f"{k}: the start vector must be a graph input or a constant on cuda"
         return None
     rank4 = op.inputs and op.inputs[0].type.rank == 4
     if any(v.type.dtype != "f32" for v in op.inputs) or op.result.type.dtype != "f32":
@@ -1241,7 +1346,7 @@ def supported_reason(op) -> Optional[str]:
         a, b = op.inputs
         for g_in, other in ((a, b), (b, a)):
             if (g_in.producer is not None and g_in.producer.kind == "gather" and other.producer is not None
-                    and other.producer.is_constant_like):
+                    and (other.producer.is_constant_like or _const_row_slice(other))):
                 return None
         return "add: a standalone elementwise add runs on cuda only after an embedding gather"
     if k == "reshape":
@@ -1270,6 +1375,8 @@ class CudaExecutable:
         self.pin_in = {v: device.pinned(nb) for v, _, nb in self.plan.inputs}
         self.pin_out = {v: device.pinned(nb) for v, _, nb in self.plan.outputs}
         self.use_graph = use_graph and hasattr(device, "graph_begin")
+        self.resident_in: set = set()
+        self.resident_out: set = set()
         self._graph = None
         self._runs = 0
         self.compile_seconds = time.perf_counter() - t0
@@ -1304,21 +1411,69 @@ class CudaExecutable:
     def launches_per_run(self) -> int:
         return len(self.thunks)
 
+    # ---- device-resident state (an extension beyond the reference's Executable protocol)
+
+    def state_pairs(self) -> list:
+        """(graph input, graph output) pairs whose output is the input updated in place on the
+        device (dynamic_update_slice of a cache fed back every step)."""
+        return [(x, y) for y, x in self.plan.aliases.items() if x is not None and y in self.g.outputs]
+
+    def keep_resident(self, pairs=None) -> None:
+        """From now on run() leaves these inputs on the device unless a feed names them, and does
+        not copy these outputs back (read them with state_read)."""
+        pairs = self.state_pairs() if pairs is None else list(pairs)
+        known = set(self.state_pairs())
+        for p in pairs:
+            if tuple(p) not in known:
+                raise ValueError(f"{p} is not an input/output pair updated in place")
+        self.resident_in = {x for x, _ in pairs}
+        self.resident_out = {y for _, y in pairs}
+
+    def _raw(self, v):
+        for u, raw, nbytes in self.plan.inputs:
+            if u is v:
+                return raw, nbytes
+        raise KeyError(v)
+
+    def state_write(self, v, arr: np.ndarray) -> None:
+        """Copies a host array into resident input `v`."""
+        raw, nbytes = self._raw(v)
+        self.device.activate()
+        view = self.input_array(v)
+        np.copyto(view, np.asarray(arr, view.dtype).reshape(view.shape))
+        self.device.h2d(raw, self.pin_in[v], nbytes)
+        self.device.sync()
+
+    def state_zero(self, v) -> None:
+        raw, nbytes = self._raw(v)
+        self.device.activate()
+        self.device.zero(raw, nbytes)
+
+    def state_read(self, v) -> np.ndarray:
+        raw, nbytes = self._raw(v)
+        self.device.activate()
+        self.device.d2h(self.pin_in[v], raw, nbytes)
+        self.device.sync()
+        return self.input_array(v).copy()
+
     def run(self, feeds: dict) -> dict:
         t0 = time.perf_counter()
         self.device.activate()
         for v, raw, nbytes in self.plan.inputs:
+            if v in self.resident_in and v not in feeds:
+                continue
             view = self.input_array(v)
             arr = feeds[v]
             if not (isinstance(arr, np.ndarray) and arr.ctypes.data == view.ctypes.data):
                 np.copyto(view, np.asarray(arr, view.dtype).reshape(view.shape))
             self.device.h2d(raw, self.pin_in[v], nbytes)
         self._launch_all()
-        for v, buf, nbytes in self.plan.outputs:
+        outs = [(v, buf, nbytes) for v, buf, nbytes in self.plan.outputs if v not in self.resident_out]
+        for v, buf, nbytes in outs:
             self.device.d2h(self.pin_out[v], buf, nbytes)
         self.device.sync()
         self._runs += 1
-        out = {v: self.pin_out[v].view(tuple(v.type.shape), np.float32).copy() for v, _, _ in self.plan.outputs}
+        out = {v: self.pin_out[v].view(tuple(v.type.shape), np.float32).copy() for v, _, _ in outs}
         out.update({v: c.copy() for v, c in self.plan.const_outputs.items()})
         self.last_seconds = time.perf_counter() - t0
         return out

@@ -38,6 +38,11 @@ def _strided(view, shape4, dtype=np.float32):
                                            tuple(int(s) * item for s in view.strides))
 
 
+def _pad4(shape) -> tuple:
+    shape = tuple(int(d) for d in shape)
+    return (1,) * (4 - len(shape)) + shape
+
+
 class FakePinned(FakeBuf):
     def view(self, shape, dtype):  # PinnedBuffer's argument order
         return super().view(dtype, shape)
@@ -76,6 +81,9 @@ class FakeDevice:
 
     def sync(self):
         pass
+
+    def zero(self, buf, nbytes):
+        buf.data[:nbytes] = 0
 
     def thunk(self, launch):
         fn = getattr(self, "_" + launch.kind)
@@ -267,6 +275,24 @@ class FakeDevice:
         if addend is not None:
             add = np.tile(addend.view(np.float32, (addend_rows, d)), (rows // addend_rows, 1))
         out.view(np.float32, (rows, ld_out))[:, :d] = ref.embed(table.view(np.float32, (vocab, d)), ids, add)
+
+    @staticmethod
+    def _window(start, rank, dims, n):
+        """Clamped starts over 4 dimensions (reference _clamped_starts, ops.py:536-537)."""
+        st = [0] * 4
+        vals = start.view(np.int32, (rank,)) if rank else []
+        for j in range(rank):
+            d = 4 - rank + j
+            st[d] = int(min(max(int(vals[j]), 0), dims[d] - n[d]))
+        return tuple(slice(s, s + k) for s, k in zip(st, n))
+
+    def _dyn_slice(self, x, x_shape, start, rank, size, out):
+        dims, n = _pad4(x_shape), _pad4(size)
+        _strided(out, n)[...] = _strided(x, dims)[self._window(start, rank, dims, n)]
+
+    def _dyn_update(self, x, x_shape, upd, upd_shape, start, rank):
+        dims, n = _pad4(x_shape), _pad4(upd_shape)
+        _strided(x, dims)[self._window(start, rank, dims, n)] = _strided(upd, n)
 
     def _copy_view(self, shape, src, dst):
         _strided(dst, shape)[...] = _strided(src, shape)
