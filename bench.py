@@ -3,7 +3,7 @@
 scaling over 1/2/4/8 GPUs, one process per GPU) plus the int8 GEMM throughput at 8192^3.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
-                  [--workload resnet18|mobilenet_v2|mlp|transformer]
+                  [--workload resnet18|mobilenet_v2|mlp|transformer|decode]
 
 The default workload is the headline (ResNet-18); the others are the remaining configurations of
 the same path (MobileNetV2 images/s, the MLP's samples/s, the transformer prefill's tokens/s) with
@@ -56,6 +56,12 @@ WORKLOADS = {
 }
 WORKLOAD = "resnet18"
 METRIC = WORKLOADS[WORKLOAD]["metric"]
+
+# config-5 decode: one new token for each of `batch` sequences per step, key/value caches of max_seq
+# positions resident on the device (mira_b200.decode); the reference cpu sample runs the same
+# quantized step graph at batch 1
+DECODE = dict(metric="w8a8 transformer decode tokens/s", unit="tokens/s",
+              config="decoder-12x768-h12-mlp3072-vocab256-kv1024-step", batch=64, max_seq=1024, vocab=256)
 
 
 def _env_rank():
@@ -304,9 +310,51 @@ def reference_cpu_sample(steps: int, warmup: int, workload: str = WORKLOAD) -> d
                       f"(NumPy golden model, OpenBLAS on all host cores)"}
 
 
+def _decode_programs(batch: int, target: str, device: int = 0):
+    """(prefill program on the host, used for its activation scales; W8A8 step program for target)."""
+    from mira_b200 import configs, decode
+    pre = configs.compile_w8a8("transformer", 1, "cpu", n_calib=4, calib_batch=1)
+    opts = {"device": device} if target == "cuda" else {}
+    return pre, decode.compile_step(configs.transformer_step(batch, max_seq=DECODE["max_seq"]), pre, target, **opts)
+
+
+def reference_decode_sample(steps: int, warmup: int) -> dict:
+    """The reference cpu target running the quantized step graph (batch 1, caches through the host)."""
+    _, prog = _decode_programs(1, "cpu")
+    g = prog.graph
+    names = [v.name for v in g.inputs[3:]]
+    caches = {n: np.zeros(v.type.shape, np.float32) for n, v in zip(names, g.inputs[3:])}
+    tok = np.zeros((1, 1), np.int32)
+    dt = 0.0
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        out = prog.run({"tok": tok, "pos2": np.array([i, 0], np.int32), "pos4": np.array([0, 0, i, 0], np.int32),
+                        **caches})
+        if i >= warmup:
+            dt += time.perf_counter() - t0
+        caches = dict(zip(names, out[1:]))
+        tok = out[0][:, 0].argmax(axis=1).astype(np.int32).reshape(1, 1)
+    return {"value": steps / dt, "unit": DECODE["unit"], "cores": os.cpu_count(), "kind": "reference",
+            "ms_per_step": dt / steps * 1e3,
+            "sample": f"{steps} step(s) after {warmup} warm-up step(s) of one sequence (batch 1) through the W8A8 "
+                      f"step graph, caches through the host; reference cpu target (NumPy golden model, OpenBLAS "
+                      f"on all host cores)"}
+
+
 def run_reference(args) -> None:
     rank, world, _ = _env_rank()
     if rank != 0:
+        return
+    if args.workload == "decode":
+        res = reference_decode_sample(args.steps, args.warmup)
+        line = {"metric": DECODE["metric"], "value": res["value"], "unit": DECODE["unit"], "impl": "reference",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic", "config": {"workload": DECODE["config"], "batch_per_step": 1,
+                                                "note": "bounded sample: one sequence per step"},
+                "cpu_baseline": res, "e2e": {"value": res["value"], "unit": DECODE["unit"], "h2d_bytes_per_step": 0,
+                                             "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     w = WORKLOADS[args.workload]
     res = reference_cpu_sample(args.steps, args.warmup, args.workload)
@@ -315,9 +363,110 @@ def run_reference(args) -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": w["config"], "batch_per_step": w["cpu_batch"],
                        "note": f"bounded sample of the workload: {w['cpu_note']}"},
-            "cpu_baseline": res, "e2e": {"value": res["value"], "unit": "img/s", "h2d_bytes_per_step": 0,
+            "cpu_baseline": res, "e2e": {"value": res["value"], "unit": w["unit"], "h2d_bytes_per_step": 0,
                                          "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def run_decode(args, rank: int, world: int, local: int, dist) -> None:
+    """Config-5 decode: `batch` sequences per GPU, one token each per step, caches resident.
+
+    value: tokens/s over K steps replayed on the device (each step attends over all max_seq cache
+    rows, so every position costs the same); e2e: K Decoder.step calls (token ids and start
+    vectors to the device, logits back, positions advancing).  HBM-bound: the roofline counts the
+    int8 weights and the whole key/value cache read each step."""
+    from mira_b200 import _lib, decode
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    batch = args.batch
+    if args.warmup + 2 * args.steps > DECODE["max_seq"]:
+        raise SystemExit(f"warmup + 2 * steps must stay within the {DECODE['max_seq']} cache positions")
+    t0 = time.perf_counter()
+    _, step = _decode_programs(batch, "cuda", local)
+    compile_s = time.perf_counter() - t0
+    dec = decode.Decoder(step)
+    exe = dec.exe
+    rng = np.random.default_rng(1 + rank)
+    toks = rng.integers(0, DECODE["vocab"], (batch, args.warmup + 2 * args.steps)).astype(np.int32)
+    dec.reset()
+    for i in range(args.warmup):           # eager first step, then the captured CUDA graph
+        logits = dec.step(toks[:, i])
+
+    ev_a, ev_b = C.c_void_p(), C.c_void_p()
+    _lib.call("mira_cuda_event_create", C.byref(ev_a))
+    _lib.call("mira_cuda_event_create", C.byref(ev_b))
+    n0 = _lib.launch_count()
+    barrier()
+    _lib.call("mira_cuda_sync")
+    with ClockSampler(local) as clocks:
+        _lib.call("mira_cuda_event_record", ev_a)
+        for _ in range(args.steps):
+            exe.replay()
+        _lib.call("mira_cuda_event_record", ev_b)
+        _lib.call("mira_cuda_sync")
+        ms = C.c_float()
+        _lib.call("mira_cuda_event_elapsed", ev_a, ev_b, C.byref(ms))
+    barrier()
+    dev_ms = max_over_ranks(ms.value)
+    gpu_launches = args.steps * exe.launches_per_run + (_lib.launch_count() - n0)
+
+    barrier()
+    t1 = time.perf_counter()
+    for i in range(args.steps):
+        logits = dec.step(toks[:, args.warmup + i])
+    e2e_s = max_over_ranks(time.perf_counter() - t1)
+    barrier()
+
+    if rank == 0:
+        bf16, hbm, src = _peaks()
+        g = exe.g
+        weight_bytes = sum(np.asarray(op.attrs["q"]).nbytes + 4 * np.asarray(op.attrs["w_scale"]).size
+                           for op in g.ops if op.kind == "qmatmul")
+        cache_bytes = sum(v.type.numel * 4 for v in dec.caches)
+        step_bytes = weight_bytes + cache_bytes
+        step_ms = dev_ms / args.steps
+        kernels = {}
+        for kind in ("attention", "qgemm", "layernorm", "dyn_update", "dyn_slice", "embed"):
+            ms_k, n_k = time_kernels(exe, (kind,))
+            if n_k:
+                kernels[kind] = {"launches": n_k, "ms_per_step": ms_k}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = reference_decode_sample(3, 1)
+        items = batch * world * args.steps
+        result = {
+            "metric": DECODE["metric"], "value": items / (dev_ms * 1e-3), "unit": DECODE["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": DECODE["config"], "global_batch": batch * world, "batch_per_gpu": batch,
+                       "parallelism": f"dp{world} (replicas, no collective)",
+                       "l2": f"inputs larger than L2 ({cache_bytes / 1e9:.1f} GB key/value cache read per step)",
+                       "calibration": "prefill activation scales (4 seeded sequences of 1024 tokens)",
+                       "compile_s": round(compile_s, 1)},
+            "e2e": {"value": items / e2e_s, "unit": DECODE["unit"], "h2d_bytes_per_step": batch * 4 + 8 + 16,
+                    "d2h_bytes_per_step": int(logits.nbytes)},
+            "roofline": {"bound": "hbm", "kernel": "whole step (int8 weights + key/value cache reads)",
+                         "achieved": step_bytes / (step_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": (step_bytes / (step_ms * 1e-3) / 1e9 / hbm) if hbm else None, "traffic": None,
+                         "algorithmic_bytes_per_step": step_bytes, "weight_bytes": weight_bytes,
+                         "cache_bytes": cache_bytes, "peak_source": f"hbm_gbs of {src}"},
+            "kernels": kernels, "gpu_launches": int(gpu_launches), "clocks": clocks.summary(), "cpu_baseline": cpu,
+        }
+        print(json.dumps(result), flush=True)
+    if dist is not None:
+        barrier()
+        dist.destroy_process_group()
 
 
 def main() -> None:
@@ -327,11 +476,29 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=None, help="batch rows per GPU per step (workload default)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS) + ["decode"])
     ap.add_argument("--calib-batch", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "decode":
+        args.batch = args.batch or DECODE["batch"]
+        if args.impl == "reference":
+            run_reference(args)
+            return
+        rank, world, local = _env_rank()
+        os.environ["MIRA_CUDA_DEVICE"] = str(local)
+        dist = None
+        if world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+        run_decode(args, rank, world, local, dist)
+        return
     wl = WORKLOADS[args.workload]
     args.batch = args.batch or wl["batch"]
     args.calib_batch = args.calib_batch or wl["calib_batch"]

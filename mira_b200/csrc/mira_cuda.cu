@@ -1231,6 +1231,13 @@ extern "C" int mira_cuda_attention_f32(const mira_attention* a) {
   p.out = static_cast<float*>(a->out_f32.ptr);
   p.out_i8 = static_cast<int8_t*>(a->out_i8.ptr);
   p.q8 = make_qscale(p.out_i8 != nullptr ? a->out_scale : 1.0f);
+  if (p.tq == 1 && p.vec) {       // one query row (a decode step): stream the keys and values once
+    const dim3 grid(unsigned(a->batch1), unsigned(a->batch0));
+    if (a->dh <= 32) attention_q1_kernel<32><<<grid, ATT1_WARPS * 32, 0, dev->stream>>>(p);
+    else if (a->dh <= 64) attention_q1_kernel<64><<<grid, ATT1_WARPS * 32, 0, dev->stream>>>(p);
+    else attention_q1_kernel<128><<<grid, ATT1_WARPS * 32, 0, dev->stream>>>(p);
+    return after_launch("attention_q1_kernel");
+  }
   if (a->dh <= 32) return launch_attention<32>(dev, p, a->batch0, a->batch1);
   if (a->dh <= 64) return launch_attention<64>(dev, p, a->batch0, a->batch1);
   return launch_attention<128>(dev, p, a->batch0, a->batch1);

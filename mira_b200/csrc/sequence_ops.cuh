@@ -795,4 +795,100 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttnPa
   }
 }
 
+// ---------------------------------------------------------------- single-query attention (decode)
+
+constexpr int ATT1_WARPS = 8;
+constexpr int ATT1_UNROLL = 4;     // keys per lane group in flight
+
+// One query row per (batch0, batch1) entry against tk keys: the decode step, where a key/value
+// cache of tk rows is read once and nothing is reused.  One CTA per entry; each warp is split into
+// groups of DH/4 lanes, a group holds one key at a time (every lane 4 of its DH values, 16-byte
+// loads of k and v rows), the warps stride over the keys.  Each group keeps its own online softmax
+// state with the arithmetic of attn_compute (scale step, mask add, expf(s - m), rescaled sums);
+// the groups are merged in shared memory at the end, then o / l (rounded division) and the
+// optional int8 requantization like attention_f32_kernel.  Needs tq == 1 and vec (contiguous
+// 16-byte aligned k and v rows).
+template <int DH>
+__global__ void __launch_bounds__(ATT1_WARPS * 32) attention_q1_kernel(const AttnParams p) {
+  constexpr int G = DH / 4;              // lanes per key
+  constexpr int KPW = 32 / G;            // keys per warp per round
+  constexpr int NGRP = ATT1_WARPS * KPW;
+  __shared__ float s_m[NGRP], s_l[NGRP];
+  __shared__ __align__(16) float s_o[NGRP][DH];
+  const int64_t b0 = blockIdx.y, b1 = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane % G, slot = lane / G, grp = warp * KPW + slot;
+  const int d0 = 4 * sub;
+  const bool dim_ok = d0 < p.dh;
+  const float* qp = p.q + b0 * p.qs[0] + b1 * p.qs[1];
+  float4 q4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (dim_ok) {
+    q4.x = __ldg(qp + int64_t(d0) * p.qs[3]);
+    q4.y = __ldg(qp + int64_t(d0 + 1) * p.qs[3]);
+    q4.z = __ldg(qp + int64_t(d0 + 2) * p.qs[3]);
+    q4.w = __ldg(qp + int64_t(d0 + 3) * p.qs[3]);
+  }
+  const float* kp = p.k + b0 * p.ks[0] + b1 * p.ks[1];
+  const float* vp = p.v + b0 * p.vs[0] + b1 * p.vs[1];
+  const float* mp = p.mask != nullptr ? p.mask + b0 * p.ms[0] + b1 * p.ms[1] : nullptr;
+  float m = -INFINITY, l = 0.0f;
+  float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const int stride = NGRP * ATT1_UNROLL;
+  // the loop bound is the warp's first key, the same for all 32 lanes, so every lane reaches the
+  // full-mask shuffles below; keys past tk enter the softmax as -inf
+  for (int jw = warp * KPW * ATT1_UNROLL; jw < p.tk; jw += stride) {
+    const int j0 = jw + slot * ATT1_UNROLL;
+    float4 kv[ATT1_UNROLL], vv[ATT1_UNROLL];
+#pragma unroll
+    for (int u = 0; u < ATT1_UNROLL; ++u) {
+      const int j = j0 + u;
+      const bool ok = j < p.tk && dim_ok;
+      kv[u] = ok ? __ldg(reinterpret_cast<const float4*>(kp + int64_t(j) * p.ks[2] + d0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      vv[u] = ok ? __ldg(reinterpret_cast<const float4*>(vp + int64_t(j) * p.vs[2] + d0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < ATT1_UNROLL; ++u) {
+      const int j = j0 + u;
+      float t = fmaf(q4.x, kv[u].x, 0.0f);
+      t = fmaf(q4.y, kv[u].y, t);
+      t = fmaf(q4.z, kv[u].z, t);
+      t = fmaf(q4.w, kv[u].w, t);
+#pragma unroll
+      for (int off = 1; off < G; off <<= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+      float x = t;
+      if (p.scale_op == MIRA_EPI_MUL) x = __fmul_rn(x, p.scale);
+      else if (p.scale_op == MIRA_EPI_DIV) x = __fdiv_rn(x, p.scale);
+      if (mp != nullptr && j < p.tk) x = __fadd_rn(x, __ldg(mp + int64_t(j) * p.ms[3]));
+      if (j >= p.tk) x = -INFINITY;
+      const float mnew = fmaxf(m, x);
+      const float corr = (mnew == -INFINITY) ? 1.0f : expf(m - mnew);
+      const float e = (mnew == -INFINITY) ? 0.0f : expf(x - mnew);
+      l = fmaf(l, corr, e);
+      o.x = fmaf(e, vv[u].x, o.x * corr);
+      o.y = fmaf(e, vv[u].y, o.y * corr);
+      o.z = fmaf(e, vv[u].z, o.z * corr);
+      o.w = fmaf(e, vv[u].w, o.w * corr);
+      m = mnew;
+    }
+  }
+  if (sub == 0) { s_m[grp] = m; s_l[grp] = l; }
+  if (dim_ok) *reinterpret_cast<float4*>(&s_o[grp][d0]) = o;
+  __syncthreads();
+  for (int d = threadIdx.x; d < p.dh; d += blockDim.x) {
+    float mt = -INFINITY;
+    for (int g = 0; g < NGRP; ++g) mt = fmaxf(mt, s_m[g]);
+    float lt = 0.0f, ot = 0.0f;
+    for (int g = 0; g < NGRP; ++g) {
+      if (s_m[g] == -INFINITY) continue;
+      const float c = expf(s_m[g] - mt);
+      lt = fmaf(s_l[g], c, lt);
+      ot = fmaf(s_o[g][d], c, ot);
+    }
+    const float y = __fdiv_rn(ot, lt);
+    if (p.out != nullptr) p.out[b0 * p.os[0] + b1 * p.os[1] + int64_t(d) * p.os[3]] = y;
+    if (p.out_i8 != nullptr)
+      p.out_i8[b0 * p.is[0] + b1 * p.is[1] + int64_t(d) * p.is[3]] = static_cast<int8_t>(quant_byte(y, p.q8) & 0xff);
+  }
+}
+
 }  // namespace mira

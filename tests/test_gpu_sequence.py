@@ -234,6 +234,36 @@ def test_attention_matches_reference_chain(cuda_device, b0, b1, t, dh, skip):
     np.testing.assert_allclose(got, want, rtol=0, atol=3e-6 * np.abs(v).max())
 
 
+@pytest.mark.parametrize("b0,b1,tk,dh,scale_op", [(4, 12, 1024, 64, "mul"), (2, 3, 1000, 32, "div"),
+                                                 (1, 2, 77, 128, "mul"), (3, 2, 300, 48, "mul"), (1, 1, 5, 64, "div")])
+def test_single_query_attention_matches_reference_chain(cuda_device, b0, b1, tk, dh, scale_op):
+    """The decode form: one query row per (batch, head) against a key/value cache of tk rows, the
+    mask a runtime row (0 up to the position, -10000 after it) shared by every batch and head;
+    f32 and int8 outputs."""
+    K, DB = _k()
+    rng = np.random.default_rng(tk + dh)
+    q = rng.standard_normal((b0, b1, 1, dh)).astype(np.float32)
+    k = rng.standard_normal((b0, b1, tk, dh)).astype(np.float32)
+    v = rng.standard_normal((b0, b1, tk, dh)).astype(np.float32)
+    pos = int(rng.integers(0, tk))
+    m = np.where(np.arange(tk) <= pos, 0.0, -10000.0).astype(np.float32).reshape(1, tk)
+    scale = 0.125 if scale_op == "mul" else 8.0
+    qb, kb, vb, mb = (DB.from_array(x) for x in (q, k, v, m))
+    kst = (b1 * tk * dh, tk * dh, dh, 1)
+    qst = (b1 * dh, dh, dh, 1)
+    ob, ib = DB(q.nbytes), DB(q.size, zero=True)
+    desc = K.Attn(b0, b1, 1, tk, dh, K.View(qb, qst), K.View(kb, kst), K.View(vb, kst), scale_op, scale,
+                  K.View(mb, (0, 0, 0, 1)), None, None, None, out=K.View(ob, qst))
+    out_scale = 0.02
+    desc.out_i8, desc.out_scale = K.View(ib, qst, itemsize=1), out_scale
+    K.attention_f32(desc)
+    want = ref.matmul_f32(ref.softmax(ref.matmul_f32(q, np.swapaxes(k, -1, -2), [(scale_op, 0, False), ("add", 1, False)],
+                                                     [np.float32(scale), m])), v)
+    got = ob.download(q.shape, np.float32)
+    np.testing.assert_allclose(got, want, rtol=0, atol=3e-6 * np.abs(v).max())
+    np.testing.assert_array_equal(ib.download(q.shape, np.int8), ref.quantize_activation(got, out_scale))
+
+
 def test_attention_large_scores_are_not_skipped(cuda_device):
     """With scores far beyond the mask (|q.k| * scale >> 10000) the masked entries do count in the
     reference; the skip test must fail and every tile be processed."""
