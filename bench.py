@@ -77,7 +77,8 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
+    """SM clock and throttle reasons sampled during the timed region: NVML read every 5 ms from a
+    thread (read-only queries, so regions of a few ms still get samples), else nvidia-smi every 200 ms."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -87,8 +88,33 @@ class ClockSampler:
         self.gpu = gpu
         self.proc = None
         self.lines: list[str] = []
+        self.nvml_samples: list[tuple[float, int]] = []
+        self.nvml_max = None
+        self._stop = None
+
+    def _poll_nvml(self, nv, h):
+        while True:
+            try:
+                self.nvml_samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                          int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+            except Exception:
+                return
+            if self._stop.wait(0.005):
+                return
 
     def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.nvml_max = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._nv = nv
+            self._stop = threading.Event()
+            self.t = threading.Thread(target=self._poll_nvml, args=(nv, h), daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self._stop = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -104,6 +130,10 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self._stop is not None:
+            self._stop.set()
+            self.t.join(timeout=5)
+            return
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -112,6 +142,19 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        if self._stop is not None:
+            nv = self._nv
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            sm = [c for c, _ in self.nvml_samples]
+            if not sm:
+                return {"sm_mhz": None, "sm_max_mhz": self.nvml_max, "reasons": [], "samples": 0, "source": "nvml"}
+            reasons = sorted(n for n, b in bits.items() if any(r & b for _, r in self.nvml_samples))
+            under_load = [c for c in sm if c > 0.3 * (self.nvml_max or 1)] or sm
+            return {"sm_mhz": statistics.median(under_load), "sm_max_mhz": self.nvml_max, "reasons": reasons,
+                    "samples": len(sm), "source": "nvml, every 5 ms"}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
@@ -212,6 +255,78 @@ def gemm_tops(n: int = 8192, iters: int = 5) -> float:
     _lib.call("mira_cuda_event_elapsed", a, b, C.byref(ms))
     _lib.call("mira_cuda_sync")
     return 2.0 * n ** 3 / (ms.value / iters * 1e-3) / 1e12
+
+
+PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows")
+
+
+def profile_case(name: str, reps: int = 3) -> None:
+    """One kernel on a bounded, seeded case, launched `reps` times, for ncu captures (the inputs are
+    larger than L2 where the kernel is HBM-bound; a few hundred MB on the device):
+      gemm8192      mira_cuda_qgemm 8192^3, row/col scales + bias, f32 out (config 2)
+      conv_l1       ResNet-18 layer-1 3x3 conv, batch 256, 56x56x64 -> 64, bias + relu, int8 + f32 out
+      dwconv_l1     MobileNetV2's first depthwise layer, batch 96, 112x112x32, bias + relu6, int8 out
+      attention_q1  a decode step's attention: 64 sequences x 12 heads, 1024 cached rows, d_head 64
+      quantize_rows the transformer's activation quantization, 65536 x 768 f32 -> int8"""
+    from mira_b200 import _lib, kernels as K
+    from mira_b200.device import DeviceBuffer as DB
+    rng = np.random.default_rng(0)
+    if name == "gemm8192":
+        n = 8192
+        A, B, Y = DB(n * n), DB(n * n), DB(n * n * 4)
+        _lib.call("mira_cuda_memset", C.c_void_p(A.ptr), 3, C.c_size_t(n * n))
+        _lib.call("mira_cuda_memset", C.c_void_p(B.ptr), 5, C.c_size_t(n * n))
+        rs, cs = DB.from_array(np.full(n, 1e-3, np.float32)), DB.from_array(np.full(n, 2e-3, np.float32))
+        bias = DB.from_array(K.pad_channels(np.zeros(n, np.float32)))
+        epi = K.Epi([K.Step("add", "channel", ptr=bias)], out_f32=Y, ld_f32=n)
+        for _ in range(reps):
+            K.qgemm(n, n, n, A, n, B, n, K.dequant_rowcol(rs, cs), epi)
+    elif name == "conv_l1":
+        n, h, c, o = 256, 56, 64, 64
+        x = DB.from_array(rng.integers(-127, 128, (n, h, h, c)).astype(np.int8))
+        wq, cp = K.conv_weight(rng.integers(-127, 128, (o, c, 3, 3)).astype(np.int8))
+        s64, hi, lo = K.scale_arrays(0.02, rng.uniform(1e-3, 1e-2, o).astype(np.float32))
+        keep = [DB.from_array(a) for a in (s64, hi, lo)]
+        bias = DB.from_array(K.pad_channels(rng.standard_normal(o).astype(np.float32)))
+        y, yq = DB(n * h * h * o * 4), DB(n * h * h * o)
+        epi = K.Epi([K.Step("add", "channel", ptr=bias), K.Step("relu")], out_f32=y, ld_f32=o, out_i8=yq, ld_i8=o,
+                    out_scale=0.05)
+        wb = DB.from_array(wq)
+        for _ in range(reps):
+            K.qconv2d(n, h, h, cp, x, o, 3, 3, wb, wq.shape[1], (1, 1), (1, 1), (1, 1), K.dequant_channel(*keep), epi,
+                      layout=0)
+    elif name == "dwconv_l1":
+        n, h, c = 96, 112, 32
+        x = DB.from_array(rng.standard_normal((n, h, h, c), dtype=np.float32))
+        wt = DB.from_array(rng.standard_normal((9, c)).astype(np.float32))
+        bias = DB.from_array(K.pad_channels(rng.standard_normal(c).astype(np.float32)))
+        q = DB(n * h * h * K.round_up(c, 16))
+        epi = K.Epi([K.Step("add", "channel", ptr=bias), K.Step("maximum", "scalar", scalar=0.0),
+                     K.Step("minimum", "scalar", scalar=6.0)], out_i8=q, ld_i8=K.round_up(c, 16), out_scale=6.0 / 127)
+        for _ in range(reps):
+            K.dwconv2d(x, n, h, h, c, wt, 3, 3, (1, 1), (1, 1), (1, 1), epi)
+    elif name == "attention_q1":
+        b, hd, tk, dh = 64, 12, 1024, 64
+        q = DB.from_array(rng.standard_normal((b, hd, 1, dh), dtype=np.float32))
+        k = DB.from_array(rng.standard_normal((b, hd, tk, dh), dtype=np.float32))
+        v = DB.from_array(rng.standard_normal((b, hd, tk, dh), dtype=np.float32))
+        m = DB.from_array(np.where(np.arange(tk) <= 700, 0.0, -10000.0).astype(np.float32))
+        out = DB(b * hd * dh * 4)
+        st, qst = (hd * tk * dh, tk * dh, dh, 1), (hd * dh, dh, dh, 1)
+        desc = K.Attn(b, hd, 1, tk, dh, K.View(q, qst), K.View(k, st), K.View(v, st), "mul", 0.125,
+                      K.View(m, (0, 0, 0, 1)), out=K.View(out, qst))
+        for _ in range(reps):
+            K.attention_f32(desc)
+    elif name == "quantize_rows":
+        rows, cols = 65536, 768
+        x = DB.from_array(rng.standard_normal((rows, cols), dtype=np.float32))
+        xq = DB(rows * cols)
+        for _ in range(reps):
+            K.quantize_rows(x, rows, cols, cols, 0.03, xq, cols)
+    else:
+        raise SystemExit(f"unknown profile case {name}; one of {', '.join(PROFILE_CASES)}")
+    _lib.call("mira_cuda_sync")
+    print(f"profile case {name}: {reps} launches ok", flush=True)
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the 20 convolution launches of one
@@ -479,7 +594,12 @@ def main() -> None:
     ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS) + ["decode"])
     ap.add_argument("--calib-batch", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=PROFILE_CASES, default=None,
+                    help="launch one kernel on a bounded case a few times (for ncu) and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     args.warmup = max(args.warmup, 3)
     if args.workload == "decode":
         args.batch = args.batch or DECODE["batch"]
