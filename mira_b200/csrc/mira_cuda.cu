@@ -6,6 +6,7 @@
 
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -14,6 +15,7 @@
 #include "../../include/mira_cuda.h"
 #include "memory_bound.cuh"
 #include "qgemm_sm100.cuh"
+#include "qgemm_pair_sm100.cuh"
 #include "runtime.h"
 #include "sequence_ops.cuh"
 
@@ -235,6 +237,46 @@ static int launch_qgemm_bn(DeviceState* dev, const CUtensorMap& tmA, const CUten
 }
 
 static int pick_bn(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
+
+// CTA-pair GEMM (256 x 256 tiles over two SMs): on unless MIRA_CUDA_PAIR_GEMM=0.
+static bool pair_gemm_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("MIRA_CUDA_PAIR_GEMM");
+    return e == nullptr || std::strcmp(e, "0") != 0;
+  }();
+  return on;
+}
+
+template <int BN, int STAGES, bool ROWCOL, int G>
+static int launch_qgemm_pair_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                                 const QgParams& p_in) {
+  QgParams p = p_in;
+  p.k_splits = 1;
+  p.kb_per_split = p.num_kb;
+  using Cfg = Qg2Cfg<BN, STAGES, G>;
+  auto kern = qgemm_pair_kernel<BN, STAGES, ROWCOL, G>;
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[dev->device]) {
+    MIRA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM)),
+                  "cudaFuncSetAttribute(qgemm pair smem)");
+    attr_set[dev->device] = true;
+  }
+  const int tiles = int((p.M + 2 * QG_BM - 1) / (2 * QG_BM)) * p.n_tiles;
+  const int pairs = dev->sm_count / 2;
+  const int grid = 2 * (tiles < pairs ? tiles : pairs);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, dev->stream>>>(tmA, tmB, p);
+  return after_launch("qgemm_pair_kernel");
+}
+
+// Whether a GEMM of this shape runs on CTA pairs: wide enough for 256-column tiles, unsplit, a
+// long reduction (more than 24 K-blocks of 128: with shorter ones the tile is epilogue-bound and
+// the single-CTA kernel with 16 epilogue warps is faster), and at least one 256 x 256 tile per SM
+// pair.
+static bool use_pair_gemm(const DeviceState* dev, int64_t M, int64_t N, int64_t K, int splits) {
+  if (!pair_gemm_enabled() || splits > 1 || N < 256 || (K + QG_BK - 1) / QG_BK <= 24) return false;
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  return tiles >= dev->sm_count / 2;
+}
 
 // im2col convolutions: K-blocks of 64 bytes (64-channel inputs) or 128 bytes; the stages fill
 // about 144 KB, 16 epilogue warps for short reductions, 8 for long ones.
@@ -644,6 +686,14 @@ static int qgemm_run(DeviceState* dev, int64_t M, int64_t N, int64_t K, const in
   CUtensorMap tmA, tmB;
   int r = encode_2d_i8(&tmA, A, uint64_t(lda), uint64_t(M), uint64_t(lda), QG_BK, QG_BM);
   if (r != MIRA_CUDA_OK) return r;
+  if (use_pair_gemm(dev, M, N, K, splits)) {
+    // each CTA of a pair stages 128 of the tile's 256 columns of B
+    r = encode_2d_i8(&tmB, B, uint64_t(ldb), uint64_t(N), uint64_t(ldb), QG_BK, 128);
+    if (r != MIRA_CUDA_OK) return r;
+    p.n_tiles = int((N + 255) / 256);
+    return p.scale64 != nullptr ? launch_qgemm_pair_cfg<256, 6, false, 2>(dev, tmA, tmB, p)
+                                : launch_qgemm_pair_cfg<256, 6, true, 2>(dev, tmA, tmB, p);
+  }
   r = encode_2d_i8(&tmB, B, uint64_t(ldb), uint64_t(N), uint64_t(ldb), QG_BK, uint32_t(bn));
   if (r != MIRA_CUDA_OK) return r;
   r = p.scale64 != nullptr ? launch_qgemm_bn<QG_A_TMA, false>(dev, tmA, tmB, p, bn)

@@ -152,6 +152,20 @@ def test_qgemm_bias_relu_exact(cuda_device, M, N, K_):
     assert not got_q[:, N:].any()
 
 
+@pytest.mark.parametrize("M,N,K_,rowcol", [(4096, 4096, 4096, False), (4100, 3000, 3200, False),
+                                           (2304, 2304, 4096, True), (8192, 2560, 3080, True)])
+def test_qgemm_cta_pair_exact(cuda_device, M, N, K_, rowcol):
+    """Long reductions with at least one 256 x 256 tile per SM pair run on CTA pairs (tcgen05.mma.cta_group::2):
+    bit-exact like every GEMM, including ragged M (a last row tile whose odd CTA is all padding), N
+    (a partial column half) and K."""
+    spec = ["bias", "relu"] if rowcol else ["bias", "residual", "relu"]
+    got, want, got_q, want_q = _run_qgemm(M, N, K_, spec, seed=M + N + K_, want_i8=not rowcol, rowcol=rowcol)
+    _same_f32(got, want)
+    if not rowcol:
+        np.testing.assert_array_equal(got_q[:, :N], want_q)
+        assert not got_q[:, N:].any()
+
+
 @pytest.mark.parametrize("spec", [[], ["relu"], ["bias", "residual", "relu"], ["bias", "relu6"],
                                   ["scale", "bias", "relu"], ["scale", "rsub", "scale", "residual"]])
 def test_qgemm_epilogues_exact(cuda_device, spec):
