@@ -120,7 +120,19 @@ int mira_cuda_memset(void* dst, int value, size_t bytes);                 /* asy
 int mira_cuda_h2d(void* dst, const void* src, size_t bytes);               /* async */
 int mira_cuda_d2h(void* dst, const void* src, size_t bytes);               /* async */
 int mira_cuda_d2d(void* dst, const void* src, size_t bytes);               /* async */
-/* Waits for the current device's stream; returns MIRA_CUDA_EKERNEL if a kernel recorded an
+/* Copies that overlap the kernels: the device keeps a second stream for host<->device copies.
+ * mira_cuda_h2d_copy_stream queues an H2D copy there (host memory pinned for overlap);
+ * mira_cuda_copy_stream_record / mira_cuda_copy_stream_wait record an event on / make that stream
+ * wait for an event; mira_cuda_stream_wait makes the kernel stream wait for an event;
+ * mira_cuda_event_sync blocks the host until an event completed.  mira_cuda_sync waits for both
+ * streams.  (No counterpart in the reference, which runs on the host.) */
+int mira_cuda_h2d_copy_stream(void* dst, const void* src, size_t bytes);
+int mira_cuda_copy_stream_record(void* event);
+int mira_cuda_copy_stream_wait(void* event);
+int mira_cuda_stream_wait(void* event);
+int mira_cuda_event_sync(void* event);
+
+/* Waits for the current device's streams; returns MIRA_CUDA_EKERNEL if a kernel recorded an
  * error since the last call (the record is cleared). */
 int mira_cuda_sync(void);
 /* The cudaStream_t of the current device, for callers that time with events on it. */

@@ -78,6 +78,11 @@ SIGNATURES: dict[str, tuple] = {
     "mira_cuda_host_alloc": (_i32, [C.POINTER(_vp), C.c_size_t]),
     "mira_cuda_host_free": (_i32, [_vp]),
     "mira_cuda_memset": (_i32, [_vp, _i32, C.c_size_t]),
+    "mira_cuda_h2d_copy_stream": (_i32, [_vp, _vp, C.c_size_t]),
+    "mira_cuda_copy_stream_record": (_i32, [_vp]),
+    "mira_cuda_copy_stream_wait": (_i32, [_vp]),
+    "mira_cuda_stream_wait": (_i32, [_vp]),
+    "mira_cuda_event_sync": (_i32, [_vp]),
     "mira_cuda_h2d": (_i32, [_vp, _vp, C.c_size_t]),
     "mira_cuda_d2h": (_i32, [_vp, _vp, C.c_size_t]),
     "mira_cuda_d2d": (_i32, [_vp, _vp, C.c_size_t]),

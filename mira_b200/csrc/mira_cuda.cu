@@ -59,6 +59,7 @@ int init_device(int d) {
   st.cc_major = prop.major;
   st.cc_minor = prop.minor;
   MIRA_CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  MIRA_CUDA_TRY(cudaStreamCreateWithFlags(&st.copy_stream, cudaStreamNonBlocking), "cudaStreamCreate(copy)");
   void* err_ptr = nullptr;
   MIRA_CUDA_TRY(cudaGetSymbolAddress(&err_ptr, g_mira_kernel_error), "cudaGetSymbolAddress(error record)");
   g_err_ptr[d] = static_cast<int*>(err_ptr);
@@ -472,8 +473,40 @@ extern "C" int mira_cuda_d2d(void* dst, const void* src, size_t bytes) {
   return MIRA_CUDA_OK;
 }
 
+extern "C" int mira_cuda_h2d_copy_stream(void* dst, const void* src, size_t bytes) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, dev->copy_stream),
+                "cudaMemcpyAsync H2D (copy stream)");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_copy_stream_record(void* ev) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(ev), dev->copy_stream), "cudaEventRecord(copy stream)");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_copy_stream_wait(void* ev) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaStreamWaitEvent(dev->copy_stream, static_cast<cudaEvent_t>(ev), 0), "cudaStreamWaitEvent(copy)");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_stream_wait(void* ev) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaStreamWaitEvent(dev->stream, static_cast<cudaEvent_t>(ev), 0), "cudaStreamWaitEvent");
+  return MIRA_CUDA_OK;
+}
+
+extern "C" int mira_cuda_event_sync(void* ev) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaEventSynchronize(static_cast<cudaEvent_t>(ev)), "cudaEventSynchronize");
+  return MIRA_CUDA_OK;
+}
+
 extern "C" int mira_cuda_sync(void) {
   MIRA_GET_DEVICE(dev);
+  MIRA_CUDA_TRY(cudaStreamSynchronize(dev->copy_stream), "cudaStreamSynchronize(copy)");
   MIRA_CUDA_TRY(cudaStreamSynchronize(dev->stream), "cudaStreamSynchronize");
   int flag = 0;
   MIRA_CUDA_TRY(cudaMemcpyFromSymbol(&flag, g_mira_kernel_error, sizeof(int)), "read kernel error record");

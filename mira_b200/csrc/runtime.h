@@ -16,6 +16,7 @@ struct DeviceState {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
   cudaStream_t stream = nullptr;
+  cudaStream_t copy_stream = nullptr;   // host<->device copies that overlap the kernels on `stream`
 };
 
 // State of the calling thread's current device (set up by mira_cuda_set_device; device 0 is

@@ -79,6 +79,36 @@ class CudaDevice:
     def zero(self, buf, nbytes: int) -> None:
         _lib.call("mira_cuda_memset", ptr(buf), 0, C.c_size_t(nbytes))
 
+    # ---- the copy stream and events (run_many's overlap of input copies with kernels)
+    def event(self):
+        ev = C.c_void_p()
+        _lib.call("mira_cuda_event_create", C.byref(ev))
+        return ev
+
+    def event_destroy(self, ev) -> None:
+        _lib.call("mira_cuda_event_destroy", ev)
+
+    def event_record(self, ev) -> None:
+        _lib.call("mira_cuda_event_record", ev)
+
+    def event_sync(self, ev) -> None:
+        _lib.call("mira_cuda_event_sync", ev)
+
+    def wait(self, ev) -> None:
+        _lib.call("mira_cuda_stream_wait", ev)
+
+    def copy_record(self, ev) -> None:
+        _lib.call("mira_cuda_copy_stream_record", ev)
+
+    def copy_wait(self, ev) -> None:
+        _lib.call("mira_cuda_copy_stream_wait", ev)
+
+    def h2d_copy(self, dst, src: PinnedBuffer, nbytes: int) -> None:
+        _lib.call("mira_cuda_h2d_copy_stream", ptr(dst), ptr(src), C.c_size_t(nbytes))
+
+    def d2d(self, dst, src, nbytes: int) -> None:
+        _lib.call("mira_cuda_d2d", ptr(dst), ptr(src), C.c_size_t(nbytes))
+
     def graph_begin(self) -> None:
         _lib.call("mira_cuda_graph_begin")
 
@@ -1377,6 +1407,7 @@ class CudaExecutable:
         self.use_graph = use_graph and hasattr(device, "graph_begin")
         self.resident_in: set = set()
         self.resident_out: set = set()
+        self._many = None            # run_many's second input buffers, pinned rings and events
         self._graph = None
         self._runs = 0
         self.compile_seconds = time.perf_counter() - t0
@@ -1478,6 +1509,79 @@ class CudaExecutable:
         self.last_seconds = time.perf_counter() - t0
         return out
 
+    def run_many(self, feeds_list) -> list:
+        """Runs one step per feeds dict, like run() each (same results), but queues step i+1's
+        host-to-device input copies on the copy stream while step i's kernels run: the copies go
+        to a second device buffer per input, which a device-to-device copy moves into the plan's
+        input buffer at the start of the next step.  Outputs are read back through a two-slot
+        pinned ring.  Inputs fed as the executable's own pinned arrays (input_array) are copied
+        without a host copy; other arrays are staged through pinned buffers."""
+        dev = self.device
+        dev.activate()
+        feeds_list = list(feeds_list)
+        if not feeds_list:
+            return []
+        ins = [(v, raw, nb) for v, raw, nb in self.plan.inputs if v not in self.resident_in]
+        outs = [(v, buf, nb) for v, buf, nb in self.plan.outputs if v not in self.resident_out]
+        if self._many is None:
+            self._many = {
+                "in2": {v: dev.alloc(nb) for v, _, nb in ins},
+                "stage": {v: [dev.pinned(nb), dev.pinned(nb)] for v, _, nb in ins},
+                "out": {v: [self.pin_out[v], dev.pinned(nb)] for v, _, nb in outs},
+                "ev": {k: [dev.event(), dev.event()] for k in ("h2d", "d2d", "done")},
+            }
+        m = self._many
+        ev = m["ev"]
+        results: list = [None] * len(feeds_list)
+
+        def enqueue(i: int) -> None:
+            slot = i % 2
+            feeds = feeds_list[i]
+            srcs = {}
+            for v, _, nb in ins:
+                arr = feeds[v]
+                own = self.input_array(v)
+                if isinstance(arr, np.ndarray) and arr.ctypes.data == own.ctypes.data:
+                    srcs[v] = self.pin_in[v]
+                    continue
+                if i >= 2:
+                    dev.event_sync(ev["h2d"][slot])     # the slot's previous copy has been read
+                st = m["stage"][v][slot]
+                view = st.view(tuple(v.type.shape), v.type.np_dtype)
+                np.copyto(view, np.asarray(arr, view.dtype).reshape(view.shape))
+                srcs[v] = st
+            if i >= 1:
+                dev.copy_wait(ev["d2d"][(i - 1) % 2])   # the previous step took its input out
+            for v, _, nb in ins:
+                dev.h2d_copy(m["in2"][v], srcs[v], nb)
+            dev.copy_record(ev["h2d"][slot])
+            dev.wait(ev["h2d"][slot])
+            for v, raw, nb in ins:
+                dev.d2d(raw, m["in2"][v], nb)
+            dev.event_record(ev["d2d"][slot])
+            self._launch_all()
+            self._runs += 1
+            for v, buf, nb in outs:
+                dev.d2h(m["out"][v][slot], buf, nb)
+            dev.event_record(ev["done"][slot])
+
+        def collect(i: int) -> None:
+            slot = i % 2
+            dev.event_sync(ev["done"][slot])
+            r = {v: m["out"][v][slot].view(tuple(v.type.shape), np.float32).copy() for v, _, _ in outs}
+            r.update({v: c.copy() for v, c in self.plan.const_outputs.items()})
+            results[i] = r
+
+        t0 = time.perf_counter()
+        for i in range(len(feeds_list)):
+            enqueue(i)
+            if i >= 1:
+                collect(i - 1)
+        collect(len(feeds_list) - 1)
+        dev.sync()
+        self.last_seconds = time.perf_counter() - t0
+        return results
+
     def device_of(self, v) -> Optional[str]:
         return f"cuda:{self.device.index}" if hasattr(self.device, "index") else "cuda"
 
@@ -1489,6 +1593,14 @@ class CudaExecutable:
                 f"{nq} in int8 on tcgen05; kernels: {counts}; {mode}")
 
     def close(self) -> None:
+        if self._many is not None:
+            for pair in self._many["ev"].values():
+                for e in pair:
+                    try:
+                        self.device.event_destroy(e)
+                    except Exception:
+                        pass
+            self._many = None
         if self._graph is not None:
             try:
                 self.device.graph_destroy(self._graph)

@@ -85,6 +85,34 @@ class FakeDevice:
     def zero(self, buf, nbytes):
         buf.data[:nbytes] = 0
 
+    # the copy stream and events: everything here completes at once, in program order
+    def event(self):
+        return object()
+
+    def event_destroy(self, ev):
+        pass
+
+    def event_record(self, ev):
+        pass
+
+    def event_sync(self, ev):
+        pass
+
+    def wait(self, ev):
+        pass
+
+    def copy_record(self, ev):
+        pass
+
+    def copy_wait(self, ev):
+        pass
+
+    def h2d_copy(self, dst, src, nbytes):
+        dst.data[:nbytes] = src.data[:nbytes]
+
+    def d2d(self, dst, src, nbytes):
+        dst.data[:nbytes] = src.data[:nbytes]
+
     def thunk(self, launch):
         fn = getattr(self, "_" + launch.kind)
         return lambda: (self.launched.append(launch.kind), fn(**launch.args))

@@ -111,3 +111,23 @@ def test_w8a8_accuracy_against_f32_like_reference_test(cuda_device):
     got = compiler.compile_ir(configs.mlp(64), "cuda", quantize="w8a8", calibration=cal).run(feeds)
     assert (got.argmax(1) == ref.argmax(1)).mean() >= 0.9
     assert np.abs(got - ref).max() < 0.1 * np.abs(ref).max()
+
+
+@needs_mira
+def test_run_many_overlapped_copies_bit_exact(cuda_device):
+    """run_many (each step's input copy on the copy stream overlapping the previous step's kernels,
+    a second device input buffer, a two-slot output ring) against the reference cpu target step by
+    step, with the executable's own pinned input array and with ordinary arrays."""
+    cpu, cuda = _pair("resnet18", 4, image=64)
+    exe = cuda.segments[0].executable
+    x = exe.g.inputs[0]
+    feeds = [configs.random_inputs(cpu.graph, 20 + i) for i in range(6)]
+    want = [cpu.run(f) for f in feeds]
+    own = exe.input_array(x)
+    own[...] = feeds[3]["x"]
+    steps = [{x: own} if i == 3 else {x: f["x"]} for i, f in enumerate(feeds)]
+    for _ in range(2):                  # the first call captures the CUDA graph on its second step
+        got = exe.run_many(steps)
+        for w, g_ in zip(want, got):
+            out = g_[exe.g.outputs[0]]
+            assert out.shape == w.shape and not (out != w).any()

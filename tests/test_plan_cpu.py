@@ -275,3 +275,23 @@ def test_skinny_qmatmul_plans_split_k():
     assert launch.args.get("ws") is not None and launch.args["ws_bytes"] > 0
     feeds = {"x": rng.standard_normal((4, 2048)).astype(np.float32)}
     np.testing.assert_array_equal(cuda.run(feeds), cpu.run(feeds))
+
+
+@pytest.mark.parametrize("name,batch,kw", [("mlp", 8, {}), ("resnet18", 2, {"image": 32})])
+def test_run_many_matches_run_step_by_step(name, batch, kw):
+    """run_many (input copies of the next step overlapped with the kernels of this one) returns
+    what run() returns for each step, whether the inputs come in the executable's pinned arrays
+    (the same array refilled between calls would race, so only fresh arrays are mixed in here) or
+    as ordinary arrays."""
+    cpu, cuda, _ = _pair(name, batch, **kw)
+    exe = cuda.segments[0].executable
+    x = exe.g.inputs[0]
+    feeds = [{x: configs.random_inputs(cpu.graph, 10 + i)[x.name]} for i in range(5)]
+    want = [exe.run({x: f[x].copy()})[exe.g.outputs[0]] for f in feeds]
+    own = exe.input_array(x)          # run() staged every feed through this array: refill it last
+    own[...] = feeds[2][x]
+    feeds[2] = {x: own}
+    got = exe.run_many(feeds)
+    assert len(got) == 5
+    for w, g_ in zip(want, got):
+        np.testing.assert_array_equal(g_[exe.g.outputs[0]], w)
