@@ -257,7 +257,7 @@ def gemm_tops(n: int = 8192, iters: int = 5) -> float:
     return 2.0 * n ** 3 / (ms.value / iters * 1e-3) / 1e12
 
 
-PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows")
+PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem")
 
 
 def profile_case(name: str, reps: int = 3) -> None:
@@ -267,7 +267,11 @@ def profile_case(name: str, reps: int = 3) -> None:
       conv_l1       ResNet-18 layer-1 3x3 conv, batch 256, 56x56x64 -> 64, bias + relu, int8 + f32 out
       dwconv_l1     MobileNetV2's first depthwise layer, batch 96, 112x112x32, bias + relu6, int8 out
       attention_q1  a decode step's attention: 64 sequences x 12 heads, 1024 cached rows, d_head 64
-      quantize_rows the transformer's activation quantization, 65536 x 768 f32 -> int8"""
+      quantize_rows the transformer's activation quantization, 65536 x 768 f32 -> int8
+      stem          ResNet-18's stem: NCHW f32 64 x 3 x 224 x 224 quantized into the row-expanded layout,
+                    then the 7x7/2 conv to 64 channels, bias + relu, f32 out (205 MB)
+      maxpool_stem  ResNet-18's -inf pad + 3x3/2 max pool on the stem output, 64 x 112 x 112 x 64 f32,
+                    f32 and int8 out"""
     from mira_b200 import _lib, kernels as K
     from mira_b200.device import DeviceBuffer as DB
     rng = np.random.default_rng(0)
@@ -323,6 +327,31 @@ def profile_case(name: str, reps: int = 3) -> None:
         xq = DB(rows * cols)
         for _ in range(reps):
             K.quantize_rows(x, rows, cols, cols, 0.03, xq, cols)
+    elif name == "stem":
+        n, h, o = 64, 224, 64
+        x = DB.from_array(rng.standard_normal((n, 3, h, h), dtype=np.float32))
+        ow = (h + 2 * 3 - 7) // 2 + 1
+        entries = K.row4_entries(ow, 2)
+        xq = DB(n * h * entries * 16)
+        wq = K.conv_weight_row4(rng.integers(-127, 128, (o, 3, 7, 7)).astype(np.int8))
+        s64, hi, lo = K.scale_arrays(0.03, rng.uniform(1e-3, 1e-2, o).astype(np.float32))
+        keep = [DB.from_array(a) for a in (s64, hi, lo)]
+        bias = DB.from_array(K.pad_channels(rng.standard_normal(o).astype(np.float32)))
+        y = DB(n * ow * ow * o * 4)
+        epi = K.Epi([K.Step("add", "channel", ptr=bias), K.Step("relu")], out_f32=y, ld_f32=o)
+        wb = DB.from_array(wq)
+        for _ in range(reps):
+            K.quantize_nchw_to_row4(x, n, 3, h, h, 0.03, xq, entries, 3, 2)
+            K.qconv2d(n, h, h, 4, xq, o, 7, 7, wb, wq.shape[1], (2, 2), (3, 3), (1, 1), K.dequant_channel(*keep), epi,
+                      layout=_lib.LAYOUT_ROW4, row_entries=entries)
+    elif name == "maxpool_stem":
+        n, h, c = 64, 112, 64
+        x = DB.from_array(np.maximum(rng.standard_normal((n, h, h, c), dtype=np.float32), 0))
+        oh = (h + 2 - 3) // 2 + 1
+        y, yq = DB(n * oh * oh * c * 4), DB(n * oh * oh * c)
+        for _ in range(reps):
+            K.maxpool2d(n, h, h, c, c, 3, 2, 1, -np.inf, x_f32=x, out_f32=y, ldc_out_f32=c, out_i8=yq, ldc_out_i8=c,
+                        out_scale=0.05)
     else:
         raise SystemExit(f"unknown profile case {name}; one of {', '.join(PROFILE_CASES)}")
     _lib.call("mira_cuda_sync")

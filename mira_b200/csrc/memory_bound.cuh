@@ -193,6 +193,67 @@ __global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, in
   }
 }
 
+// 3x3 windows, 4 channels per thread (c % 4 == 0, 16-byte aligned rows): the same maxima as
+// maxpool_f32_kernel with far fewer instructions (the general kernel spends most of its issue
+// slots on per-tap 64-bit index arithmetic and checks): three row pointers computed once, no
+// bounds checks for windows inside the image, the nine 16-byte loads in flight together, and
+// the packed requantization.  max.NaN is commutative (NaN wins, +0 over -0), so the order of the
+// maxima cannot change a result.
+__global__ void maxpool3_f32_kernel(const float* __restrict__ x, int n, int h, int w, int c, int64_t ldc, int stride,
+                                    int pad, float pad_value, int oh, int ow, float* __restrict__ out, int64_t ldo,
+                                    int8_t* __restrict__ out_i8, int64_t ldo_i8, QuantScale q) {
+  const int c4 = c >> 2;
+  const int ox = blockIdx.x * blockDim.y + threadIdx.y;
+  if (ox >= ow) return;
+  const int ix0 = ox * stride - pad;
+  const bool cols_in = ix0 >= 0 && ix0 + 2 < w;
+  const int64_t rows = int64_t(n) * oh;
+  for (int64_t orow = blockIdx.y; orow < rows; orow += gridDim.y) {
+    const int img = static_cast<int>(orow / oh);
+    const int oy = static_cast<int>(orow - int64_t(img) * oh);
+    const int iy0 = oy * stride - pad;
+    const bool inside = cols_in && iy0 >= 0 && iy0 + 2 < h;
+    const float* r0 = x + (int64_t(img) * h + iy0) * w * ldc + int64_t(ix0) * ldc;   // window's top-left pixel
+    const int64_t rs = int64_t(w) * ldc;
+    float* q0 = out != nullptr ? out + (orow * ow + ox) * ldo : nullptr;
+    int8_t* q8 = out_i8 != nullptr ? out_i8 + (orow * ow + ox) * ldo_i8 : nullptr;
+    for (int cg = threadIdx.x; cg < c4; cg += blockDim.x) {
+      float4 t[9];
+      if (inside) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+          for (int j = 0; j < 3; ++j)
+            t[3 * i + j] = __ldg(reinterpret_cast<const float4*>(r0 + i * rs + j * ldc + 4 * cg));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            const bool in = iy0 + i >= 0 && iy0 + i < h && ix0 + j >= 0 && ix0 + j < w;
+            t[3 * i + j] = in ? __ldg(reinterpret_cast<const float4*>(r0 + i * rs + j * ldc + 4 * cg))
+                              : make_float4(pad_value, pad_value, pad_value, pad_value);
+          }
+      }
+      float mx[4] = {t[0].x, t[0].y, t[0].z, t[0].w};
+#pragma unroll
+      for (int k = 1; k < 9; ++k) {
+        mx[0] = np_maximum(mx[0], t[k].x);
+        mx[1] = np_maximum(mx[1], t[k].y);
+        mx[2] = np_maximum(mx[2], t[k].z);
+        mx[3] = np_maximum(mx[3], t[k].w);
+      }
+      if (q0 != nullptr)
+        *reinterpret_cast<float4*>(q0 + 4 * cg) = make_float4(mx[0], mx[1], mx[2], mx[3]);
+      if (q8 != nullptr) {
+        uint32_t b[4];
+        requant_x2<4>(mx, q.s, q.rcp, q.c127, b);
+        *reinterpret_cast<uint32_t*>(q8 + 4 * cg) = pack4_i8(b[0], b[1], b[2], b[3]);
+      }
+    }
+  }
+}
+
 // int8 input (already quantized with the output's scale): quantize(max(x)) == max(quantize(x)),
 // so pooling the int8 values gives the reference's int8 result.  One thread per 16 channels.
 __global__ void maxpool_i8_kernel(const int8_t* __restrict__ x, int n, int h, int w, int64_t cp, int size,

@@ -940,6 +940,20 @@ extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, 
   }
   MIRA_CHECK_ARG(x_f32 != nullptr && (out_f32 != nullptr || out_i8 != nullptr), "maxpool needs an input and an output");
   if (out_i8 != nullptr) MIRA_CHECK_ARG(ldc_out_i8 % 4 == 0 && ldc_out_i8 >= c && out_scale > 0.0f, "bad int8 output");
+  const auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  if (size == 3 && c % 4 == 0 && ldc_in % 4 == 0 && a16(x_f32) &&
+      (out_f32 == nullptr || (ldc_out_f32 % 4 == 0 && a16(out_f32))) &&
+      (out_i8 == nullptr || (ldc_out_i8 % 4 == 0 && (reinterpret_cast<uintptr_t>(out_i8) & 3u) == 0))) {
+    const int c4 = int(c / 4);
+    const int tx = c4 < 64 ? c4 : 64;
+    const int ty = threads / tx < 1 ? 1 : threads / tx;
+    const int64_t orows = n * oh;
+    const dim3 grid(unsigned((ow + ty - 1) / ty), unsigned(orows < 65535 ? orows : 65535));
+    maxpool3_f32_kernel<<<grid, dim3(tx, ty), 0, dev->stream>>>(
+        x_f32, int(n), int(h), int(w), int(c), ldc_in, int(stride), int(pad), pad_value, int(oh), int(ow), out_f32,
+        ldc_out_f32, out_i8, ldc_out_i8, make_qscale(out_i8 != nullptr ? out_scale : 1.0f));
+    return after_launch("maxpool3_f32_kernel");
+  }
   // threads: x = groups of 4 channels (at most 64), y = output columns; blocks: columns x rows
   const int c4 = int((c + 3) / 4);
   const int tx = c4 < 64 ? c4 : 64;
