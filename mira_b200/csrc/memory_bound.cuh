@@ -101,18 +101,29 @@ __global__ void quantize_nchw_row4_kernel(const float* __restrict__ x, int n, in
     const int y = static_cast<int>(row - int64_t(img) * h);
     const float* base = x + (int64_t(img) * c * h + y) * w;
     const int64_t plane = int64_t(h) * w;
-    auto pixel_word = [&](int xx) -> uint32_t {
-      uint32_t b[4];
+    // the S pixels from x0 on, 4 channels each (0 outside the image and for channels >= c, which
+    // quantizes to 0), quantized two values per packed instruction
+    auto pixel_words = [&](int x0, uint32_t (&out)[S]) {
+      float v[4 * S];
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch)
-        b[ch] = (ch < c && xx >= 0 && xx < w) ? quant_byte(__ldg(base + ch * plane + xx), q) : 0u;
-      return pack4_i8(b[0], b[1], b[2], b[3]);
+      for (int j = 0; j < S; ++j)
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          const int xx = x0 + j;
+          v[4 * j + ch] = (ch < c && xx >= 0 && xx < w) ? __ldg(base + ch * plane + xx) : 0.0f;
+        }
+      uint32_t b[4 * S];
+      requant_x2<4 * S>(v, q.s, q.rcp, q.c127, b);
+#pragma unroll
+      for (int j = 0; j < S; ++j) out[j] = pack4_i8(b[4 * j], b[4 * j + 1], b[4 * j + 2], b[4 * j + 3]);
     };
     uint32_t own[S], extra[S];
+    pixel_words(S * (e0 + lane) - pad, own);
+    if (lane < L - 1) {
+      pixel_words(S * (e0 + 32 + lane) - pad, extra);
+    } else {
 #pragma unroll
-    for (int j = 0; j < S; ++j) {
-      own[j] = pixel_word(S * (e0 + lane) - pad + j);
-      extra[j] = lane < L - 1 ? pixel_word(S * (e0 + 32 + lane) - pad + j) : 0u;
+      for (int j = 0; j < S; ++j) extra[j] = 0u;
     }
     uint32_t word[4];
 #pragma unroll
