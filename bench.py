@@ -257,7 +257,8 @@ def gemm_tops(n: int = 8192, iters: int = 5) -> float:
     return 2.0 * n ** 3 / (ms.value / iters * 1e-3) / 1e12
 
 
-PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem")
+PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem",
+                 "decode_step")
 
 
 def profile_case(name: str, reps: int = 3) -> None:
@@ -271,7 +272,9 @@ def profile_case(name: str, reps: int = 3) -> None:
       stem          ResNet-18's stem: NCHW f32 64 x 3 x 224 x 224 quantized into the row-expanded layout,
                     then the 7x7/2 conv to 64 channels, bias + relu, f32 out (205 MB)
       maxpool_stem  ResNet-18's -inf pad + 3x3/2 max pool on the stem output, 64 x 112 x 112 x 64 f32,
-                    f32 and int8 out"""
+                    f32 and int8 out
+      decode_step   `reps` eager steps of the config-5 decode (batch 64, 1024-row caches): every
+                    launch of a step, for a launch list"""
     from mira_b200 import _lib, kernels as K
     from mira_b200.device import DeviceBuffer as DB
     rng = np.random.default_rng(0)
@@ -344,6 +347,16 @@ def profile_case(name: str, reps: int = 3) -> None:
             K.quantize_nchw_to_row4(x, n, 3, h, h, 0.03, xq, entries, 3, 2)
             K.qconv2d(n, h, h, 4, xq, o, 7, 7, wb, wq.shape[1], (2, 2), (3, 3), (1, 1), K.dequant_channel(*keep), epi,
                       layout=_lib.LAYOUT_ROW4, row_entries=entries)
+    elif name == "decode_step":
+        from mira_b200 import decode
+        _, step = _decode_programs(DECODE["batch"], "cuda")
+        exe = step.segments[0].executable
+        exe.use_graph = False             # eager launches, so every kernel shows up individually
+        dec = decode.Decoder(step)
+        dec.reset()
+        for i in range(reps):
+            dec.step(np.full(DECODE["batch"], i % DECODE["vocab"], np.int32))
+        print(f"decode step: {exe.launches_per_run} launches per step", flush=True)
     elif name == "maxpool_stem":
         n, h, c = 64, 112, 64
         x = DB.from_array(np.maximum(rng.standard_normal((n, h, h, c), dtype=np.float32), 0))

@@ -652,15 +652,23 @@ namespace mira {
 // Split-K plan for a GEMM whose output tiles cannot fill the GPU: the number of K ranges per
 // output tile (1: no split) and the K-blocks per range.  A split pays off when fewer than half
 // the SMs would get a tile and the reduction is long enough to cut into ranges of >= 4 blocks.
+// Tile width of a GEMM: one row tile (M <= 128, the skinny shapes of decode steps and small
+// batches) gets 64-column tiles so that more CTAs share the weight reads; otherwise by N.
+static int pick_bn_gemm(int64_t M, int64_t N) { return M <= QG_BM ? 64 : pick_bn(N); }
+
+// Split-K for GEMMs whose output tiles cannot fill the GPU: a single row tile splits its K-blocks
+// over up to sm_count / tiles CTAs per tile (one K-block each at least); taller shapes need 8
+// K-blocks and keep at least 4 per split.
 static void splitk_plan(int64_t M, int64_t N, int64_t K, int sm_count, int& splits, int& kb_per) {
-  const int bn = pick_bn(N);
+  const int bn = pick_bn_gemm(M, N);
   const int64_t tiles = ((M + QG_BM - 1) / QG_BM) * ((N + bn - 1) / bn);
   const int num_kb = int((K + QG_BK - 1) / QG_BK);
+  const bool one_row = M <= QG_BM;
   splits = 1;
   kb_per = num_kb;
-  if (tiles * 2 > sm_count || num_kb < 8) return;
+  if (tiles * 2 > sm_count || (!one_row && num_kb < 8)) return;
   int s = int(sm_count / tiles);
-  if (s > num_kb / 4) s = num_kb / 4;
+  if (s > (one_row ? num_kb : num_kb / 4)) s = one_row ? num_kb : num_kb / 4;
   if (s > 16) s = 16;
   if (s < 2) return;
   kb_per = (num_kb + s - 1) / s;
@@ -690,7 +698,7 @@ static int qgemm_run(DeviceState* dev, int64_t M, int64_t N, int64_t K, const in
   std::memset(&p, 0, sizeof(p));
   const int rc = fill_epilogue(p, dq, epi);
   if (rc != MIRA_CUDA_OK) return rc;
-  const int bn = pick_bn(N);
+  const int bn = pick_bn_gemm(M, N);
   p.M = int(M);
   p.N = int(N);
   p.K = int(K);

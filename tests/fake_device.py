@@ -191,12 +191,13 @@ class FakeDevice:
 
     def qgemm_workspace(self, M, N, K, sm_count=148):
         """The library's split-K rule (mira_cuda.cu splitk_plan) for a 148-SM device."""
-        bn = 64 if N <= 64 else (128 if N <= 128 else 256)
+        one_row = M <= 128
+        bn = 64 if (one_row or N <= 64) else (128 if N <= 128 else 256)
         tiles = -(-M // 128) * -(-N // bn)
         num_kb = -(-K // 128)
-        if tiles * 2 > sm_count or num_kb < 8:
+        if tiles * 2 > sm_count or (not one_row and num_kb < 8):
             return 0
-        s = min(sm_count // tiles, num_kb // 4, 16)
+        s = min(sm_count // tiles, num_kb if one_row else num_kb // 4, 16)
         if s < 2:
             return 0
         per = -(-num_kb // s)

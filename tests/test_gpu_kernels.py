@@ -210,8 +210,10 @@ def test_qgemm_splitk_mul_step_exact(cuda_device, M):
 def test_qgemm_splitk_workspace_rule(cuda_device):
     K, _ = _k()
     assert K.qgemm_workspace(65536, 768, 3072) == 0          # enough output tiles
-    assert K.qgemm_workspace(16, 4096, 512) == 0             # reduction too short to split
+    assert K.qgemm_workspace(300, 4096, 512) == 0            # taller shapes: reduction too short to split
     assert K.qgemm_workspace(1, 4096, 4096) > 0
+    # one row tile (a decode step's projections): 64-column tiles, K split down to one K-block
+    assert K.qgemm_workspace(64, 768, 768) == 6 * 64 * 768 * 4
 
 
 # ------------------------------------------------------------------------------ qconv2d

@@ -67,7 +67,7 @@ def test_static_scratch_rejects_shapes_beyond_its_size(cuda_device):
     from mira_b200 import _lib
     from mira_b200 import kernels as K
     from mira_b200.device import DeviceBuffer as DB
-    M, N, Kd = 128, 4096, 4096           # 8 K ranges x 128 x 4096 int32 = 16 MiB of partial sums
+    M, N, Kd = 256, 1024, 8192           # 16 K ranges x 256 x 1024 int32 = 16 MiB of partial sums
     assert K.qgemm_workspace(M, N, Kd) > 8 << 20
     bufs, lda, _, out_scale = _case(K, DB, M, N, Kd, 3)
     with pytest.raises(_lib.CudaError) as e:
