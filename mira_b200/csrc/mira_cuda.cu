@@ -652,15 +652,35 @@ namespace mira {
 // Split-K plan for a GEMM whose output tiles cannot fill the GPU: the number of K ranges per
 // output tile (1: no split) and the K-blocks per range.  A split pays off when fewer than half
 // the SMs would get a tile and the reduction is long enough to cut into ranges of >= 4 blocks.
-// Tile width of a GEMM: one row tile (M <= 128, the skinny shapes of decode steps and small
-// batches) gets 64-column tiles so that more CTAs share the weight reads; otherwise by N.
-static int pick_bn_gemm(int64_t M, int64_t N) { return M <= QG_BM ? 64 : pick_bn(N); }
+// Tile width of a GEMM.  One row tile (M <= 128: the skinny shapes of decode steps and small
+// batches) takes the widest tile, no wider than N needs, whose split-K plan (below) still puts
+// CTAs on three quarters of the SMs, else the width with the most CTAs: long reductions keep wide
+// tiles with long K ranges, short ones (K of a few K-blocks) narrow tiles.  Otherwise by N.
+static int pick_bn_gemm(int64_t M, int64_t N, int64_t K, int sm_count) {
+  if (M > QG_BM) return pick_bn(N);
+  const int64_t num_kb = (K + QG_BK - 1) / QG_BK;
+  int best_bn = 64;
+  int64_t best = -1;
+  for (int bn = pick_bn(N); bn >= 64; bn /= 2) {
+    const int64_t tiles = (N + bn - 1) / bn;
+    int64_t s = tiles * 2 > sm_count ? 1 : sm_count / tiles;
+    if (s > num_kb) s = num_kb;
+    if (s > 16) s = 16;
+    const int64_t ctas = tiles * (s < 1 ? 1 : s);
+    if (ctas * 4 >= int64_t(sm_count) * 3) return bn;
+    if (ctas > best) {
+      best = ctas;
+      best_bn = bn;
+    }
+  }
+  return best_bn;
+}
 
 // Split-K for GEMMs whose output tiles cannot fill the GPU: a single row tile splits its K-blocks
 // over up to sm_count / tiles CTAs per tile (one K-block each at least); taller shapes need 8
 // K-blocks and keep at least 4 per split.
 static void splitk_plan(int64_t M, int64_t N, int64_t K, int sm_count, int& splits, int& kb_per) {
-  const int bn = pick_bn_gemm(M, N);
+  const int bn = pick_bn_gemm(M, N, K, sm_count);
   const int64_t tiles = ((M + QG_BM - 1) / QG_BM) * ((N + bn - 1) / bn);
   const int num_kb = int((K + QG_BK - 1) / QG_BK);
   const bool one_row = M <= QG_BM;
@@ -698,7 +718,7 @@ static int qgemm_run(DeviceState* dev, int64_t M, int64_t N, int64_t K, const in
   std::memset(&p, 0, sizeof(p));
   const int rc = fill_epilogue(p, dq, epi);
   if (rc != MIRA_CUDA_OK) return rc;
-  const int bn = pick_bn_gemm(M, N);
+  const int bn = pick_bn_gemm(M, N, K, dev->sm_count);
   p.M = int(M);
   p.N = int(N);
   p.K = int(K);

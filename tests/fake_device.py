@@ -192,9 +192,21 @@ class FakeDevice:
     def qgemm_workspace(self, M, N, K, sm_count=148):
         """The library's split-K rule (mira_cuda.cu splitk_plan) for a 148-SM device."""
         one_row = M <= 128
-        bn = 64 if (one_row or N <= 64) else (128 if N <= 128 else 256)
-        tiles = -(-M // 128) * -(-N // bn)
         num_kb = -(-K // 128)
+        bn = 64 if N <= 64 else (128 if N <= 128 else 256)
+        if one_row:                    # the widest tile whose split plan fills 3/4 of the SMs
+            best, best_bn, w = -1, 64, bn
+            while w >= 64:
+                t = -(-N // w)
+                sp = 1 if t * 2 > sm_count else min(sm_count // t, num_kb, 16)
+                if t * max(sp, 1) * 4 >= sm_count * 3:
+                    best_bn = w
+                    break
+                if t * max(sp, 1) > best:
+                    best, best_bn = t * max(sp, 1), w
+                w //= 2
+            bn = best_bn
+        tiles = -(-M // 128) * -(-N // bn)
         if tiles * 2 > sm_count or (not one_row and num_kb < 8):
             return 0
         s = min(sm_count // tiles, num_kb if one_row else num_kb // 4, 16)
