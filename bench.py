@@ -258,7 +258,7 @@ def gemm_tops(n: int = 8192, iters: int = 5) -> float:
 
 
 PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem",
-                 "decode_step")
+                 "decode_step", "attention_prefill", "layernorm_decode")
 
 
 def profile_case(name: str, reps: int = 3) -> None:
@@ -274,7 +274,10 @@ def profile_case(name: str, reps: int = 3) -> None:
       maxpool_stem  ResNet-18's -inf pad + 3x3/2 max pool on the stem output, 64 x 112 x 112 x 64 f32,
                     f32 and int8 out
       decode_step   `reps` eager steps of the config-5 decode (batch 64, 1024-row caches): every
-                    launch of a step, for a launch list"""
+                    launch of a step, for a launch list
+      attention_prefill  the prefill's fused attention: 8 sequences x 12 heads x 1024 tokens, d_head 64,
+                    causal mask with exact tile skipping
+      layernorm_decode  a decode step's layernorm: 64 rows x 768, f32 and int8 out"""
     from mira_b200 import _lib, kernels as K
     from mira_b200.device import DeviceBuffer as DB
     rng = np.random.default_rng(0)
@@ -347,6 +350,27 @@ def profile_case(name: str, reps: int = 3) -> None:
             K.quantize_nchw_to_row4(x, n, 3, h, h, 0.03, xq, entries, 3, 2)
             K.qconv2d(n, h, h, 4, xq, o, 7, 7, wb, wq.shape[1], (2, 2), (3, 3), (1, 1), K.dequant_channel(*keep), epi,
                       layout=_lib.LAYOUT_ROW4, row_entries=entries)
+    elif name == "attention_prefill":
+        b0, b1, t, dh = 8, 12, 1024, 64
+        q, k, v = (DB.from_array(rng.standard_normal((b0, b1, t, dh), dtype=np.float32)) for _ in range(3))
+        m = np.where(np.arange(t)[:, None] >= np.arange(t)[None, :], 0.0, -10000.0).astype(np.float32)
+        mb = DB.from_array(m)
+        st = (b1 * t * dh, t * dh, dh, 1)
+        out = DB(b0 * b1 * t * dh * 4)
+        tm, km, tz = DB.from_array(K.mask_tile_max(m, t, t)), DB(16, zero=True), DB.from_array(K.mask_tile_zero(m, t, t))
+        K.absmax_f32((b0, b1, t, dh), K.View(k, st), km)
+        desc = K.Attn(b0, b1, t, t, dh, K.View(q, st), K.View(k, st), K.View(v, st), "mul", 0.125,
+                      K.View(mb, (0, 0, t, 1)), tm, km, tz, out=K.View(out, st))
+        for _ in range(reps):
+            K.attention_f32(desc)
+    elif name == "layernorm_decode":
+        rows, d = 64, 768
+        x = DB.from_array(rng.standard_normal((rows, d), dtype=np.float32))
+        g = DB.from_array((1 + 0.02 * rng.standard_normal(d)).astype(np.float32))
+        bta = DB.from_array((0.02 * rng.standard_normal(d)).astype(np.float32))
+        y, yq = DB(rows * d * 4), DB(rows * d)
+        for _ in range(reps):
+            K.layernorm_rows(x, rows, d, d, g, bta, 1e-5, out_f32=y, ld_f32=d, out_i8=yq, ld_i8=d, out_scale=0.03)
     elif name == "decode_step":
         from mira_b200 import decode
         _, step = _decode_programs(DECODE["batch"], "cuda")
