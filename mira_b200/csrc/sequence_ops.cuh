@@ -181,6 +181,12 @@ __global__ void __launch_bounds__(ROW_WARPS * 32, ROUNDS == 1 ? 3 : (ROUNDS == 2
       } else {
         const float sd = __fsqrt_rn(__fadd_rn(total, p.eps));
         const float rsd = __frcp_rn(sd);
+        // no output aliases gamma or beta: the unrolled loop below may then issue every gamma and
+        // beta load ahead of the stores instead of one round trip per element
+        const float* __restrict__ gam = p.gamma;
+        const float* __restrict__ bet = p.beta;
+        float* __restrict__ yout = p.out;
+        int8_t* __restrict__ qout = p.out_i8;
         auto emit = [&](int idx, float x) {
           // (x - mu) / sd correctly rounded: Markstein's correction of RN(t * RN(1/sd)), exact for
           // normal quotients (|t| / sd <= sqrt(d) here); tiny and zero t take the IEEE divide
@@ -192,9 +198,9 @@ __global__ void __launch_bounds__(ROW_WARPS * 32, ROUNDS == 1 ? 3 : (ROUNDS == 2
           } else {
             qt = __fdiv_rn(t, sd);
           }
-          const float y = __fadd_rn(__fmul_rn(qt, __ldg(p.gamma + idx)), __ldg(p.beta + idx));
-          if (p.out != nullptr) p.out[row * p.ld_out + idx] = y;
-          if (p.out_i8 != nullptr) p.out_i8[row * p.ld_i8 + idx] = static_cast<int8_t>(quant_byte(y, p.q) & 0xff);
+          const float y = __fadd_rn(__fmul_rn(qt, __ldg(gam + idx)), __ldg(bet + idx));
+          if (yout != nullptr) yout[row * p.ld_out + idx] = y;
+          if (qout != nullptr) qout[row * p.ld_i8 + idx] = static_cast<int8_t>(quant_byte(y, p.q) & 0xff);
         };
 #pragma unroll
         for (int r = 0; r < ROUNDS; ++r) {
