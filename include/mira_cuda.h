@@ -251,6 +251,15 @@ int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, int64_t n, 
 int mira_cuda_mean_hw_nhwc(const float* x, int64_t n, int64_t hw, int64_t c, int64_t ldc,
                            float* out_f32, int8_t* out_i8, int64_t ld_i8, float out_scale);
 
+/* Patch matrix of a general f32 convolution (reference _conv2d_ref with groups = 1, ops.py:265-276,
+ * taps from _taps 256-263): x NHWC f32 [n, h, w, c] with pixel stride ldc; out [n * oh * ow, ld_out]
+ * with row m = output pixel and column (i * kw + j) * c + ch the input value under tap (i, j), 0 in
+ * the zero padding.  The convolution is the f32 matmul of out with the weights reshaped to
+ * [kh * kw * c, o] (mira_cuda_bmm_f32, or mira_cuda_bmm_f32_w8 for weight-only int8 weights). */
+int mira_cuda_im2col_f32(const float* x, int64_t n, int64_t h, int64_t w, int64_t c, int64_t ldc, int64_t kh,
+                         int64_t kw, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                         int64_t dil_h, int64_t dil_w, float* out, int64_t ld_out);
+
 /* Depthwise f32 convolution over NHWC (reference ops.py:265-276 _conv2d_ref with
  * groups == channels, which the reference never quantizes, quantize.py:105-106): per-tap f32
  * products summed in (i, j) order from 0, then the epilogue on [n*oh*ow, c]. weights f32

@@ -655,6 +655,38 @@ __global__ void __launch_bounds__(256, 4) dwconv3x3_kernel(const float* __restri
   }
 }
 
+// ---------------------------------------------------------------- K4b: general f32 convolution
+
+// The patch matrix of an f32 convolution over an NHWC input: row m = output pixel (img, oy, ox),
+// column (i * kw + j) * c + ch = x[img, oy * sh - ph + i * dh, ox * sw - pw + j * dw, ch], 0 in the
+// padding (the reference pads with zeros, ops.py:256-263).  One warp per (pixel, tap) row of c
+// values; the convolution is then the f32 matmul of this matrix with the [kh * kw * c, o] weights.
+__global__ void im2col_f32_kernel(const float* __restrict__ x, int n, int h, int w, int c, int64_t ldc, int kh,
+                                  int kw, int sh, int sw, int ph, int pw, int dh, int dw, int oh, int ow,
+                                  float* __restrict__ out, int64_t ld_out) {
+  const int lane = threadIdx.x & 31;
+  const int taps = kh * kw;
+  const int64_t rows = int64_t(n) * oh * ow * taps;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * int64_t(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const int tap = static_cast<int>(r % taps);
+    const int64_t pix = r / taps;
+    const int ox = static_cast<int>(pix % ow);
+    const int64_t t2 = pix / ow;
+    const int oy = static_cast<int>(t2 % oh);
+    const int img = static_cast<int>(t2 / oh);
+    const int i = tap / kw, j = tap - (tap / kw) * kw;
+    const int iy = oy * sh - ph + i * dh, ix = ox * sw - pw + j * dw;
+    float* dst = out + pix * ld_out + int64_t(tap) * c;
+    if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
+      const float* src = x + ((int64_t(img) * h + iy) * w + ix) * ldc;
+      for (int ch = lane; ch < c; ch += 32) dst[ch] = __ldg(src + ch);
+    } else {
+      for (int ch = lane; ch < c; ch += 32) dst[ch] = 0.0f;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- layout changes (f32)
 
 // NCHW -> NHWC through a 32x32 shared-memory tile per (image, 32 channels, 32 pixels).

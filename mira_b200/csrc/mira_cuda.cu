@@ -1007,6 +1007,25 @@ extern "C" int mira_cuda_mean_hw_nhwc(const float* x, int64_t n, int64_t hw, int
   return after_launch("mean_hw_kernel");
 }
 
+extern "C" int mira_cuda_im2col_f32(const float* x, int64_t n, int64_t h, int64_t w, int64_t c, int64_t ldc, int64_t kh,
+                                    int64_t kw, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                    int64_t dil_h, int64_t dil_w, float* out, int64_t ld_out) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && h > 0 && w > 0 && c > 0 && ldc >= c && kh > 0 && kw > 0, "bad im2col shape");
+  MIRA_CHECK_ARG(stride_h > 0 && stride_w > 0 && dil_h > 0 && dil_w > 0 && pad_h >= 0 && pad_w >= 0, "bad im2col geometry");
+  MIRA_CHECK_ARG(ld_out >= kh * kw * c, "im2col rows hold kh * kw * c values");
+  MIRA_CHECK_ARG(x != nullptr && out != nullptr, "im2col needs an input and an output");
+  const int64_t oh = (h + 2 * pad_h - dil_h * (kh - 1) - 1) / stride_h + 1;
+  const int64_t ow = (w + 2 * pad_w - dil_w * (kw - 1) - 1) / stride_w + 1;
+  MIRA_CHECK_ARG(oh > 0 && ow > 0, "kernel larger than the padded input");
+  if (n == 0) return MIRA_CUDA_OK;
+  const int threads = 256;
+  im2col_f32_kernel<<<grid_for(dev, n * oh * ow * kh * kw * 32, threads), threads, 0, dev->stream>>>(
+      x, int(n), int(h), int(w), int(c), ldc, int(kh), int(kw), int(stride_h), int(stride_w), int(pad_h), int(pad_w),
+      int(dil_h), int(dil_w), int(oh), int(ow), out, ld_out);
+  return after_launch("im2col_f32_kernel");
+}
+
 extern "C" int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int64_t w, int64_t c, const float* wt,
                                        int64_t kh, int64_t kw, int64_t stride_h, int64_t stride_w, int64_t pad_h,
                                        int64_t pad_w, int64_t dil_h, int64_t dil_w, const mira_epilogue* epi) {

@@ -217,6 +217,13 @@ def dwconv2d(x, n, h, w, c, wt, kh, kw, stride, padding, dilation, epi: Epi) -> 
               padding[0], padding[1], dilation[0], dilation[1], C.byref(e))
 
 
+def im2col_f32(x, n: int, h: int, w: int, c: int, ldc: int, kh: int, kw: int, stride, padding, dilation, out,
+               ld_out: int) -> None:
+    """Patch matrix [n * oh * ow, kh * kw * c] of an NHWC f32 input (column (i * kw + j) * c + ch)."""
+    _lib.call("mira_cuda_im2col_f32", ptr(x), n, h, w, c, ldc, kh, kw, stride[0], stride[1], padding[0], padding[1],
+              dilation[0], dilation[1], ptr(out), ld_out)
+
+
 def nchw_to_nhwc(x, n, c, h, w, y, ldc) -> None:
     _lib.call("mira_cuda_nchw_to_nhwc_f32", ptr(x), n, c, h, w, ptr(y), ldc)
 

@@ -197,6 +197,11 @@ class CudaDevice:
             else:
                 fn = L.mira_cuda_bmm_f32
                 args = (a["batch0"], a["batch1"], a["m"], a["n"], a["k"], C.byref(av), C.byref(bv), C.byref(e))
+        elif k == "im2col":
+            fn = L.mira_cuda_im2col_f32
+            (sh, sw), (ph, pw), (dh, dw) = a["stride"], a["padding"], a["dilation"]
+            args = (ptr(a["x"]), a["n"], a["h"], a["w"], a["c"], a["ldc"], a["kh"], a["kw"], sh, sw, ph, pw, dh, dw,
+                    ptr(a["out"]), a["ld_out"])
         elif k == "dyn_slice":
             xv, ov, xd, sz = a["x"].struct(), a["out"].struct(), K.dims4(a["x_shape"]), K.dims4(a["size"])
             keep += [xv, ov, xd, sz]
@@ -923,14 +928,70 @@ class Plan:
         stride, padding, dilation, groups = conv_attrs(op.attrs)
         x = self.vals[op.inputs[0]]
         n, c, h, w = x.shape
+        if groups == 1:
+            self._conv2d_general(op, x, stride, padding, dilation)
+            return
         wt = self._const(op.inputs[1])
         if wt is None or groups != c or wt.shape[0] != c or wt.shape[1] != 1:
-            raise UnsupportedOnCuda("only depthwise f32 conv2d with constant weights runs on cuda")
+            raise UnsupportedOnCuda("only depthwise or ungrouped f32 conv2d with constant weights runs on cuda")
         kh, kw = wt.shape[2:]
         wtap = np.ascontiguousarray(wt[:, 0].reshape(c, kh * kw).T.astype(np.float32))
         out = self._new_out(op.result, "nhwc")
         self._launch("dwconv", x=x.f32, n=n, h=h, w=w, c=c, wt=self._upload(wtap), kh=kh, kw=kw, stride=stride,
                      padding=padding, dilation=dilation, epi=self._epilogue(op, out))
+
+    def _conv2d_general(self, op, x: DVal, stride, padding, dilation) -> None:
+        """An ungrouped f32 convolution (reference _conv2d_ref, ops.py:265-276) as the f32 matmul of its
+        patch matrix (im2col over the NHWC input) with the weights reshaped to [kh * kw * c, o], the
+        epilogue fused into the matmul.  A weight-only int8 weight (a `dequantize` constant with one
+        scale per output channel, quantize.py:38-41) stays int8 and is rebuilt as RN(f32(q) * scale)
+        while the matmul stages it.  Like the reference's per-tap f32 sums, the result is exact to
+        f32 rounding, not bit for bit."""
+        n, c, h, w = x.shape
+        wv = op.inputs[1]
+        p = wv.producer
+        o, cin, kh, kw = wv.type.shape
+        oh, ow = op.result.type.shape[2:]
+        rows, kdim = n * oh * ow, kh * kw * cin
+        if x.f32 is None or x.layout != "nhwc":
+            raise UnsupportedOnCuda("conv2d input without an NHWC f32 form")
+        patches = self._alloc(max(rows * kdim, 1) * 4)
+        self._launch("im2col", x=x.f32, n=n, h=h, w=w, c=c, ldc=x.cols, kh=kh, kw=kw, stride=stride,
+                     padding=padding, dilation=dilation, out=patches, ld_out=kdim)
+        b_scale = None
+        if p is not None and p.kind == "dequantize" and p.attrs["axis"] % 4 == 0 and wv.type.dtype == "f32":
+            q = np.asarray(p.attrs["q"])
+            bmat = self._upload(np.ascontiguousarray(q.transpose(2, 3, 1, 0).reshape(kdim, o)))
+            b_scale = self._upload(np.ascontiguousarray(np.asarray(p.attrs["scale"], np.float32).reshape(-1)))
+        else:
+            wt = self._const(wv)
+            if wt is None:
+                raise UnsupportedOnCuda("conv2d with runtime weights")
+            bmat = self._upload(np.ascontiguousarray(wt.astype(np.float32).transpose(2, 3, 1, 0).reshape(kdim, o)))
+        out = self._new_out(op.result, "nhwc")
+        if out.f32 is None and out.i8 is None:
+            out.f32 = self._alloc(out.numel * 4)
+        bview = K.View(bmat, (0, 0, o, 1), itemsize=1 if b_scale is not None else 4)
+        self._launch("bmm", batch0=1, batch1=1, m=rows, n=o, k=kdim, a=K.View(patches, (0, 0, kdim, 1)), b=bview,
+                     b_scale=b_scale, epi=self._as_bmm_epi(self._epilogue(op, out)))
+
+    @staticmethod
+    def _as_bmm_epi(epi: K.Epi) -> K.BmmEpi:
+        """A conv-style epilogue over [rows, cols] outputs as the f32 matmul's view-based one: per-channel
+        operands are rows of stride 0, full operands rows of stride ld, per-row operands columns of
+        stride 0."""
+        steps = []
+        for st in epi.steps:
+            if st.operand == "none":
+                steps.append(K.BmmStep(st.op, swapped=st.swapped))
+            elif st.operand == "scalar":
+                steps.append(K.BmmStep(st.op, "scalar", st.swapped, scalar=st.scalar))
+            else:
+                strides = {"channel": (0, 0, 0, 1), "full": (0, 0, st.ld, 1), "row": (0, 0, 1, 0)}[st.operand]
+                steps.append(K.BmmStep(st.op, "view", st.swapped, view=K.View(st.ptr, strides)))
+        out = K.View(epi.out_f32, (0, 0, epi.ld_f32, 1)) if epi.out_f32 is not None else None
+        out_i8 = K.View(epi.out_i8, (0, 0, epi.ld_i8, 1), itemsize=1) if epi.out_i8 is not None else None
+        return K.BmmEpi(steps, out=out, out_i8=out_i8, out_scale=epi.out_scale)
 
     def _op_maxpool2d(self, op) -> None:
         if op in self.pad_into_pool:
@@ -1385,9 +1446,11 @@ def supported_reason(op) -> Optional[str]:
         _, _, _, groups = conv_attrs(op.attrs)
         c = op.inputs[0].type.shape[1]
         w = op.inputs[1]
-        if groups == c and w.type.shape[0] == c and w.producer is not None and w.producer.is_constant_like:
+        if w.producer is None or not w.producer.is_constant_like:
+            return "conv2d: the cuda target takes constant weights"
+        if groups == 1 or (groups == c and w.type.shape[0] == c):
             return None
-        return "conv2d: only depthwise convolutions with constant weights run on cuda in f32"
+        return "conv2d: grouped convolutions other than depthwise run on the host"
     return f"{k} has no cuda kernel"
 
 

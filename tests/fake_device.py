@@ -272,6 +272,18 @@ class FakeDevice:
         if out_i8 is not None:
             out_i8.view(np.int8, (n, ld_i8))[:, :c] = ref.quantize_activation(m, scale)
 
+    def _im2col(self, x, n, h, w, c, ldc, kh, kw, stride, padding, dilation, out, ld_out):
+        (sh, sw), (ph, pw), (dh, dw) = stride, padding, dilation
+        xp = np.zeros((n, h + 2 * ph, w + 2 * pw, c), np.float32)
+        xp[:, ph:ph + h, pw:pw + w, :] = x.view(np.float32, (n, h, w, ldc))[..., :c]
+        oh = (h + 2 * ph - dh * (kh - 1) - 1) // sh + 1
+        ow = (w + 2 * pw - dw * (kw - 1) - 1) // sw + 1
+        cols = []
+        for i in range(kh):
+            for j in range(kw):
+                cols.append(xp[:, i * dh:i * dh + sh * (oh - 1) + 1:sh, j * dw:j * dw + sw * (ow - 1) + 1:sw, :])
+        out.view(np.float32, (n * oh * ow, ld_out))[:, :kh * kw * c] = np.concatenate(cols, axis=-1).reshape(-1, kh * kw * c)
+
     def _dwconv(self, x, n, h, w, c, wt, kh, kw, stride, padding, dilation, epi):
         xn = x.view(np.float32, (n, h, w, c)).transpose(0, 3, 1, 2)
         wk = wt.view(np.float32, (kh * kw, c)).T.reshape(c, 1, kh, kw)

@@ -131,3 +131,19 @@ def test_run_many_overlapped_copies_bit_exact(cuda_device):
         for w, g_ in zip(want, got):
             out = g_[exe.g.outputs[0]]
             assert out.shape == w.shape and not (out != w).any()
+
+
+@needs_mira
+@pytest.mark.parametrize("quantize", [None, "int8"])
+def test_f32_and_weight_only_resnet18_close_to_cpu(cuda_device, quantize):
+    """f32 (no quantization) and weight-only int8 ResNet-18: ungrouped convolutions through im2col and
+    the f32 matmul, all on the device; f32 tolerance against the reference cpu target."""
+    g_cpu, g_cuda = configs.resnet18(2, image=64), configs.resnet18(2, image=64)
+    cpu = compiler.compile_ir(g_cpu, "cpu", quantize=quantize, precision=None)
+    cuda = compiler.compile_ir(g_cuda, "cuda", quantize=quantize)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    feeds = configs.random_inputs(g_cpu, 1)
+    want = cpu.run(feeds)
+    for _ in range(2):
+        got = cuda.run(feeds)
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * np.abs(want).max())

@@ -477,3 +477,34 @@ def test_row4_layout_conv_exact(cuda_device, case, pool):
     _same_f32(yb.download((n, ph, pw_, o), np.float32).transpose(0, 3, 1, 2), y)
     np.testing.assert_array_equal(qb.download((n, ph, pw_, ldi), np.int8)[..., :o].transpose(0, 3, 1, 2),
                                   ref.quantize_activation(y, out_scale))
+
+
+@pytest.mark.parametrize("n,c,h,w,o,k,stride,pad,dil", [(2, 3, 17, 15, 16, 3, 1, 1, 1), (1, 64, 14, 14, 32, 3, 2, 1, 1),
+                                                       (2, 5, 12, 12, 7, 5, 1, 4, 2), (3, 16, 9, 9, 24, 1, 1, 0, 1)])
+def test_f32_conv_im2col_within_error_bound(cuda_device, n, c, h, w, o, k, stride, pad, dil):
+    """General f32 convolution = patch matrix (im2col) times [k*k*c, o] weights in the f32 matmul:
+    within the f32 error bound of the exact (float64) convolution, bias added in the epilogue."""
+    K, DB = _k()
+    rng = np.random.default_rng(n + c + k)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = rng.standard_normal((o, c, k, k)).astype(np.float32)
+    bias = rng.standard_normal(o).astype(np.float32)
+    oh = (h + 2 * pad - dil * (k - 1) - 1) // stride + 1
+    ow = (w + 2 * pad - dil * (k - 1) - 1) // stride + 1
+    rows, kdim = n * oh * ow, k * k * c
+    xb = DB.from_array(np.ascontiguousarray(x.transpose(0, 2, 3, 1)))
+    pb = DB(rows * kdim * 4)
+    K.im2col_f32(xb, n, h, w, c, c, k, k, (stride, stride), (pad, pad), (dil, dil), pb, kdim)
+    patches = pb.download((rows, kdim), np.float32)
+    xp = np.pad(x.transpose(0, 2, 3, 1), ((0, 0), (pad, pad), (pad, pad), (0, 0)))
+    want_p = np.concatenate([xp[:, i * dil:i * dil + stride * (oh - 1) + 1:stride, j * dil:j * dil + stride * (ow - 1) + 1:stride]
+                             for i in range(k) for j in range(k)], axis=-1).reshape(rows, kdim)
+    np.testing.assert_array_equal(patches, want_p)
+    bmat = np.ascontiguousarray(wt.transpose(2, 3, 1, 0).reshape(kdim, o))
+    bb, biasb, yb = DB.from_array(bmat), DB.from_array(bias), DB(rows * o * 4)
+    K.bmm_f32(1, 1, rows, o, kdim, K.View(pb, (0, 0, kdim, 1)), K.View(bb, (0, 0, o, 1)),
+              K.BmmEpi([K.BmmStep("add", "view", view=K.View(biasb, (0, 0, 0, 1)))], out=K.View(yb, (0, 0, o, 1))))
+    got = yb.download((rows, o), np.float32)
+    exact = want_p.astype(np.float64) @ bmat.astype(np.float64) + bias.astype(np.float64)
+    bound = (np.abs(want_p).astype(np.float64) @ np.abs(bmat).astype(np.float64) + np.abs(bias)) * (kdim + 2) * 2.0 ** -24
+    assert np.all(np.abs(got - exact) <= bound + 1e-30)

@@ -295,3 +295,24 @@ def test_run_many_matches_run_step_by_step(name, batch, kw):
     assert len(got) == 5
     for w, g_ in zip(want, got):
         np.testing.assert_array_equal(g_[exe.g.outputs[0]], w)
+
+
+@pytest.mark.parametrize("quantize", [None, "int8"])
+def test_f32_and_weight_only_cnn_plan_matches_cpu(quantize):
+    """Ungrouped f32 convolutions (im2col + the f32 matmul, weight-only int8 weights kept int8) put a
+    whole f32 or `quantize="int8"` ResNet-18 in one cuda segment; f32 tolerance against the cpu target
+    (the reference's per-tap einsum sums in another order)."""
+    g_cpu, g_cuda = configs.resnet18(2, image=32), configs.resnet18(2, image=32)
+    cpu = compiler.compile_ir(g_cpu, "cpu", quantize=quantize, precision=None)
+    dev = FakeDevice()
+    cuda = compiler.compile_ir(g_cuda, "cuda", quantize=quantize, executor=dev)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    plan = cuda.segments[0].executable.plan
+    convs = [l for l in plan.launches if l.kind == "im2col"]
+    assert len(convs) == sum(op.kind == "conv2d" for op in cuda.graph.ops) == 20
+    if quantize == "int8":
+        assert all(l.args.get("b_scale") is not None for l in plan.launches if l.kind == "bmm")
+    feeds = configs.random_inputs(cpu.graph, 1)
+    want = cpu.run(feeds)
+    got = cuda.run(feeds)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * np.abs(want).max())
