@@ -378,6 +378,14 @@ int mira_cuda_absmax_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const m
 int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* src,
                             const mira_view4* dst);
 
+/* A standalone f32 element-wise op (reference UNARY / BINARY, ops.py:99-139, when no matmul or
+ * convolution epilogue absorbed it): op a unary MIRA_EPI_* code (out = f(a); b, scalar ignored) or a
+ * binary one (out = f(a, B), or f(B, a) when swapped, with B the view b or, when b is NULL, the
+ * scalar).  [n0, n1, n2, n3] through element-stride views (0 for broadcast dimensions); the same
+ * arithmetic as the epilogue steps, so add/sub/mul/div/maximum/minimum match NumPy bit for bit. */
+int mira_cuda_elementwise_f32(int32_t op, int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* a,
+                              const mira_view4* b, float scalar, int32_t swapped, const mira_view4* out);
+
 /* Slices at runtime positions (reference dynamic_slice / dynamic_update_slice, ops.py:533-576),
  * for 4-byte elements (f32 or i32) in views of at most 4 dimensions (shapes padded with leading 1s
  * to 4).  `start` is DEVICE memory holding `rank` int32 start entries for the last `rank`

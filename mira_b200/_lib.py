@@ -125,6 +125,8 @@ SIGNATURES: dict[str, tuple] = {
                                        C.POINTER(View4)]),
     "mira_cuda_dynamic_update_slice": (_i32, [C.POINTER(View4), C.POINTER(_i64), C.POINTER(View4),
                                               C.POINTER(_i64), _vp, _i64]),
+    "mira_cuda_elementwise_f32": (_i32, [_i32, _i64, _i64, _i64, _i64, C.POINTER(View4), C.POINTER(View4), _f32, _i32,
+                                         C.POINTER(View4)]),
     "mira_cuda_im2col_f32": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                     _vp, _i64]),
     "mira_cuda_bmm_f32_w8": (_i32, [_i64, _i64, _i64, _i64, _i64, C.POINTER(View4), C.POINTER(View4), _vp,

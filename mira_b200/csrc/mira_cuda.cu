@@ -1212,6 +1212,35 @@ extern "C" int mira_cuda_copy_view_f32(int64_t n0, int64_t n1, int64_t n2, int64
   return after_launch("copy_view_kernel");
 }
 
+extern "C" int mira_cuda_elementwise_f32(int32_t op, int64_t n0, int64_t n1, int64_t n2, int64_t n3,
+                                         const mira_view4* a, const mira_view4* b, float scalar, int32_t swapped,
+                                         const mira_view4* out) {
+  MIRA_GET_DEVICE(dev);
+  const bool unary = op >= MIRA_EPI_RELU && op <= MIRA_EPI_TANH;
+  MIRA_CHECK_ARG(unary || (op >= MIRA_EPI_ADD && op <= MIRA_EPI_MINIMUM), "unknown element-wise op");
+  MIRA_CHECK_ARG(n0 >= 0 && n1 >= 0 && n2 >= 0 && n3 >= 0, "bad element-wise shape");
+  MIRA_CHECK_ARG(a != nullptr && out != nullptr, "element-wise op needs an input and an output view");
+  const int64_t total = n0 * n1 * n2 * n3;
+  if (total == 0) return MIRA_CUDA_OK;
+  MIRA_CHECK_ARG(a->ptr != nullptr && out->ptr != nullptr && (b == nullptr || b->ptr != nullptr), "null view");
+  EltParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.n[0] = n0; p.n[1] = n1; p.n[2] = n2; p.n[3] = n3;
+  p.a = static_cast<const float*>(a->ptr);
+  p.b = (!unary && b != nullptr) ? static_cast<const float*>(b->ptr) : nullptr;
+  p.out = static_cast<float*>(out->ptr);
+  for (int i = 0; i < 4; ++i) {
+    p.as[i] = a->stride[i]; p.os[i] = out->stride[i]; p.bs[i] = p.b != nullptr ? b->stride[i] : 0;
+  }
+  p.scalar = scalar;
+  p.op = op;
+  p.unary = unary ? 1 : 0;
+  p.swapped = swapped ? 1 : 0;
+  const int threads = 256;
+  elementwise_f32_kernel<<<grid_for(dev, (total / (n3 > 0 ? n3 : 1)) * 32, threads), threads, 0, dev->stream>>>(p);
+  return after_launch("elementwise_f32_kernel");
+}
+
 namespace mira {
 
 static int dyn_window(DeviceState* dev, const mira_view4* src, const mira_view4* dst, const int64_t* n,

@@ -296,6 +296,48 @@ __global__ void copy_view_kernel(const View4 v) {
   }
 }
 
+// ---------------------------------------------------------------- standalone element-wise ops
+
+// out = f(a) for the unary MIRA_EPI_* ops, or f(a, b) / f(b, a) (swapped) for the binary ones, b a
+// view or a scalar; [n0, n1, n2, n3] through 4-D views (broadcast dims have stride 0), one warp per
+// innermost row.  The arithmetic is the epilogue's (apply_unary / apply_binary): the reference's
+// UNARY / BINARY ops (ops.py:99-139) with IEEE rounding for the binary ones.
+struct EltParams {
+  int64_t n[4];
+  const float* a;
+  int64_t as[4];
+  const float* b;
+  int64_t bs[4];
+  float scalar;
+  int op, unary, swapped;
+  float* out;
+  int64_t os[4];
+};
+
+__global__ void elementwise_f32_kernel(const EltParams p) {
+  const int64_t rows = p.n[0] * p.n[1] * p.n[2];
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * int64_t(blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t i2 = row % p.n[2], i01 = row / p.n[2];
+    const int64_t i1 = i01 % p.n[1], i0 = i01 / p.n[1];
+    const float* a = p.a + i0 * p.as[0] + i1 * p.as[1] + i2 * p.as[2];
+    const float* b = p.b != nullptr ? p.b + i0 * p.bs[0] + i1 * p.bs[1] + i2 * p.bs[2] : nullptr;
+    float* o = p.out + i0 * p.os[0] + i1 * p.os[1] + i2 * p.os[2];
+    for (int64_t i3 = lane; i3 < p.n[3]; i3 += 32) {
+      const float x = __ldg(a + i3 * p.as[3]);
+      float y;
+      if (p.unary) {
+        y = apply_unary(p.op, x);
+      } else {
+        const float v = b != nullptr ? __ldg(b + i3 * p.bs[3]) : p.scalar;
+        y = p.swapped ? apply_binary(p.op, v, x) : apply_binary(p.op, x, v);
+      }
+      o[i3 * p.os[3]] = y;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- slices at runtime positions
 
 // The reference's dynamic_slice / dynamic_update_slice (ops.py:533-576): a window of shape n at a

@@ -217,6 +217,19 @@ def dwconv2d(x, n, h, w, c, wt, kh, kw, stride, padding, dilation, epi: Epi) -> 
               padding[0], padding[1], dilation[0], dilation[1], C.byref(e))
 
 
+def elementwise_f32(op: str, shape4, a: View, out: View, b: Optional[View] = None, scalar: float = 0.0,
+                    swapped: bool = False) -> None:
+    """out = op(a) (unary) or op(a, b-or-scalar) (op(b, a) when swapped) over a 4-D shape."""
+    code = _lib.UNARY_CODES.get(op) or _lib.BINARY_CODES.get(op)
+    if code is None:
+        raise ValueError(f"no element-wise kernel for {op}")
+    av, ov = a.struct(), out.struct()
+    bv = b.struct() if b is not None else None
+    n = tuple(int(d) for d in shape4)
+    _lib.call("mira_cuda_elementwise_f32", code, *n, C.byref(av), C.byref(bv) if bv is not None else None,
+              float(np.float32(scalar)), int(bool(swapped)), C.byref(ov))
+
+
 def im2col_f32(x, n: int, h: int, w: int, c: int, ldc: int, kh: int, kw: int, stride, padding, dilation, out,
                ld_out: int) -> None:
     """Patch matrix [n * oh * ow, kh * kw * c] of an NHWC f32 input (column (i * kw + j) * c + ch)."""

@@ -197,6 +197,14 @@ class CudaDevice:
             else:
                 fn = L.mira_cuda_bmm_f32
                 args = (a["batch0"], a["batch1"], a["m"], a["n"], a["k"], C.byref(av), C.byref(bv), C.byref(e))
+        elif k == "elementwise":
+            av, ov = a["a"].struct(), a["out"].struct()
+            bv = a["b"].struct() if a.get("b") is not None else None
+            n4 = tuple(int(d) for d in a["shape"])
+            keep += [av, ov, bv]
+            fn = L.mira_cuda_elementwise_f32
+            args = (a["code"], *n4, C.byref(av), C.byref(bv) if bv is not None else None, _f32(a.get("scalar", 0.0)),
+                    int(bool(a.get("swapped"))), C.byref(ov))
         elif k == "im2col":
             fn = L.mira_cuda_im2col_f32
             (sh, sw), (ph, pw), (dh, dw) = a["stride"], a["padding"], a["dilation"]
@@ -1298,6 +1306,57 @@ class Plan:
                      upd=self._data_view(upd), upd_shape=tuple(upd.type.shape), start=self._start_buf(start),
                      rank=rank)
 
+    def _logical_view(self, dv: DVal, out_shape) -> K.View:
+        """4-D view of `dv` in the reference's element order (NCHW for image values, whose buffer is
+        NHWC), broadcast against `out_shape`."""
+        if dv.layout != "nhwc":
+            return self._broadcast_view(dv, out_shape)
+        n, c, h, w = dv.shape
+        st = (h * w * c, 1, w * c, c)
+        return K.View(dv.f32, tuple(0 if d == 1 else x for d, x in zip(dv.shape, st)), dv.offset)
+
+    def _op_elementwise(self, op) -> None:
+        """A unary or binary f32 op the reference's epilogue fusion left standalone (ops.py:99-139):
+        one strided element-wise launch; scalar constants are passed as scalars."""
+        oshape = tuple(op.result.type.shape)
+        if len(oshape) > 4:
+            raise UnsupportedOnCuda("element-wise ops of more than 4 dimensions")
+        shape4 = (1,) * (4 - len(oshape)) + oshape
+        unary = op.kind in _lib.UNARY_CODES
+        code = _lib.UNARY_CODES.get(op.kind) or _lib.BINARY_CODES[op.kind]
+
+        def operand(v):
+            c = self._const(v)
+            if c is not None and c.size == 1:
+                return None, float(np.float32(np.asarray(c).ravel()[0]))
+            if c is not None:
+                c = np.ascontiguousarray(np.asarray(c, np.float32))
+                return self._broadcast_view(DVal(tuple(c.shape), "rows", f32=self._upload(c)), oshape), None
+            dv = self.vals[v]
+            if dv.f32 is None:
+                raise UnsupportedOnCuda("element-wise operand without an f32 form")
+            return self._logical_view(dv, oshape), None
+
+        a, a_s = operand(op.inputs[0])
+        b, b_s, swapped = None, 0.0, False
+        if not unary:
+            b, b_s = operand(op.inputs[1])
+            if a is None:                 # scalar op tensor: f(scalar, tensor)
+                if b is None:
+                    raise UnsupportedOnCuda("element-wise op of two scalars")
+                a, b, b_s, swapped = b, None, a_s, True
+        elif a is None:
+            raise UnsupportedOnCuda("element-wise op of a scalar")
+        out = self._new_out(op.result)
+        if out.f32 is None:
+            out.f32 = self._alloc(max(out.numel, 1) * 4)
+        self._launch("elementwise", code=code, shape=shape4, a=a, b=b, scalar=b_s, swapped=swapped,
+                     out=self._logical_view(out, oshape))
+        self._fill_i8(op.result)
+
+    _op_relu = _op_gelu = _op_sigmoid = _op_tanh = _op_elementwise
+    _op_add = _op_sub = _op_mul = _op_div = _op_maximum = _op_minimum = _op_elementwise
+
     def _op_softmax(self, op) -> None:
         x = self.vals[op.inputs[0]]
         src, ld = self._rows_of(op.inputs[0])
@@ -1433,13 +1492,10 @@ def supported_reason(op) -> Optional[str]:
         if max(v.type.rank for v in op.inputs) > 4 or op.result.type.rank > 4:
             return "matmul: at most 4 dimensions on cuda"
         return None
-    if k == "add" and len(op.inputs) == 2:
-        a, b = op.inputs
-        for g_in, other in ((a, b), (b, a)):
-            if (g_in.producer is not None and g_in.producer.kind == "gather" and other.producer is not None
-                    and (other.producer.is_constant_like or _const_row_slice(other))):
-                return None
-        return "add: a standalone elementwise add runs on cuda only after an embedding gather"
+    if k in _lib.UNARY_CODES or k in _lib.BINARY_CODES:
+        if op.result.type.rank > 4:
+            return f"{k}: at most 4 dimensions on cuda"
+        return None
     if k == "reshape":
         return None
     if k == "conv2d" and rank4:

@@ -272,6 +272,18 @@ class FakeDevice:
         if out_i8 is not None:
             out_i8.view(np.int8, (n, ld_i8))[:, :c] = ref.quantize_activation(m, scale)
 
+    def _elementwise(self, code, shape, a, out, b=None, scalar=0.0, swapped=False):
+        from mira_b200 import _lib
+        names = {v: k for k, v in {**_lib.UNARY_CODES, **_lib.BINARY_CODES}.items()}
+        op = names[code]
+        x = _strided(a, shape).astype(np.float32)
+        if op in ref.UNARY:
+            y = ref.UNARY[op](x)
+        else:
+            o = _strided(b, shape) if b is not None else np.float32(scalar)
+            y = ref.BINARY[op](o, x) if swapped else ref.BINARY[op](x, o)
+        _strided(out, shape)[...] = np.asarray(y, np.float32)
+
     def _im2col(self, x, n, h, w, c, ldc, kh, kw, stride, padding, dilation, out, ld_out):
         (sh, sw), (ph, pw), (dh, dw) = stride, padding, dilation
         xp = np.zeros((n, h + 2 * ph, w + 2 * pw, c), np.float32)

@@ -147,3 +147,16 @@ def test_f32_and_weight_only_resnet18_close_to_cpu(cuda_device, quantize):
     for _ in range(2):
         got = cuda.run(feeds)
         np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * np.abs(want).max())
+
+
+@needs_mira
+def test_unfused_f32_resnet18_close_to_cpu(cuda_device):
+    """fuse=False: every bias add, residual add and ReLU a standalone element-wise launch over NHWC
+    image values; f32 tolerance against the reference cpu target."""
+    g_cpu, g_cuda = configs.resnet18(2, image=64), configs.resnet18(2, image=64)
+    cpu = compiler.compile_ir(g_cpu, "cpu", fuse=False, precision=None)
+    cuda = compiler.compile_ir(g_cuda, "cuda", fuse=False)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    feeds = configs.random_inputs(g_cpu, 1)
+    want = cpu.run(feeds)
+    np.testing.assert_allclose(cuda.run(feeds), want, rtol=1e-4, atol=1e-4 * np.abs(want).max())

@@ -508,3 +508,31 @@ def test_f32_conv_im2col_within_error_bound(cuda_device, n, c, h, w, o, k, strid
     exact = want_p.astype(np.float64) @ bmat.astype(np.float64) + bias.astype(np.float64)
     bound = (np.abs(want_p).astype(np.float64) @ np.abs(bmat).astype(np.float64) + np.abs(bias)) * (kdim + 2) * 2.0 ** -24
     assert np.all(np.abs(got - exact) <= bound + 1e-30)
+
+
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div", "maximum", "minimum", "relu", "gelu", "sigmoid", "tanh"])
+def test_elementwise_f32(cuda_device, op):
+    """Standalone element-wise op over a transposed view with a broadcast operand: IEEE binary ops
+    and relu bit for bit against NumPy, the transcendental ones within f32 tolerance."""
+    K, DB = _k()
+    rng = np.random.default_rng(len(op))
+    a = (rng.standard_normal((2, 3, 7, 40)) * 3).astype(np.float32)
+    b = rng.standard_normal((1, 3, 1, 40)).astype(np.float32)
+    a_t = np.ascontiguousarray(a.transpose(0, 1, 3, 2))          # stored [.., 40, 7], read as [.., 7, 40]
+    ab, bb, ob = DB.from_array(a_t), DB.from_array(b), DB(a.nbytes)
+    av = K.View(ab, (3 * 40 * 7, 40 * 7, 1, 7))
+    out = K.View(ob, (3 * 7 * 40, 7 * 40, 40, 1))
+    unary = op in ("relu", "gelu", "sigmoid", "tanh")
+    K.elementwise_f32(op, a.shape, av, out, b=None if unary else K.View(bb, (0, 40, 0, 1)))
+    got = ob.download(a.shape, np.float32)
+    want = (ref.UNARY[op](a) if unary else ref.BINARY[op](a, b)).astype(np.float32)
+    if op in ("gelu", "sigmoid", "tanh"):
+        # CUDA's tanhf/expf against NumPy's: relative near 1, absolute where GELU tends to 0
+        np.testing.assert_allclose(got, want, rtol=2e-6, atol=1e-6)
+    else:
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # a scalar on the left: 0.75 op a
+    if not unary:
+        K.elementwise_f32(op, a.shape, av, out, scalar=0.75, swapped=True)
+        want = ref.BINARY[op](np.float32(0.75), a).astype(np.float32)
+        assert np.array_equal(ob.download(a.shape, np.float32).view(np.uint32), want.view(np.uint32))

@@ -81,11 +81,11 @@ fn main(img: f32[4, 1, 16, 16],
 """
 
 
-@pytest.mark.parametrize("tail, devices", [("", ["cuda"]), ("tanh", ["cuda", "cpu"])])
+@pytest.mark.parametrize("tail, devices", [("", ["cuda"]), ("exp", ["cuda", "cpu"])])
 def test_mira_source_program_placement(tail, devices):
     """A .mira program: the flatten (NHWC -> NCHW reorder), the quantized FC and the softmax run on
-    cuda; a standalone tanh falls back to the CPU like any op the target does not run (reference
-    partition.py)."""
+    cuda; a standalone exp (no cuda kernel) falls back to the CPU like any op the target does not
+    run (reference partition.py)."""
     src = CNN_SRC.replace("TAIL", tail)
     rng = np.random.default_rng(0)
     cal = [{"img": rng.standard_normal((4, 1, 16, 16)).astype(np.float32)} for _ in range(2)]
@@ -316,3 +316,46 @@ def test_f32_and_weight_only_cnn_plan_matches_cpu(quantize):
     want = cpu.run(feeds)
     got = cuda.run(feeds)
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * np.abs(want).max())
+
+
+def test_standalone_elementwise_ops_plan_matches_cpu():
+    """With the reference's epilogue fusion off (fuse=False) every bias add, residual add and ReLU of
+    an f32 ResNet-18 is a standalone op: strided element-wise launches over NHWC image values and
+    broadcast constants, all in one cuda segment; f32 tolerance against the cpu target."""
+    g_cpu, g_cuda = configs.resnet18(2, image=32), configs.resnet18(2, image=32)
+    cpu = compiler.compile_ir(g_cpu, "cpu", fuse=False, precision=None)
+    dev = FakeDevice()
+    cuda = compiler.compile_ir(g_cuda, "cuda", fuse=False, executor=dev)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    kinds = [l.kind for l in cuda.segments[0].executable.plan.launches]
+    assert kinds.count("elementwise") >= 40
+    feeds = configs.random_inputs(cpu.graph, 1)
+    want = cpu.run(feeds)
+    np.testing.assert_allclose(cuda.run(feeds), want, rtol=1e-4, atol=1e-4 * np.abs(want).max())
+
+
+def test_elementwise_graph_with_scalars_and_broadcasting_plan_matches_cpu():
+    """Standalone ops on rank-3 values: a scalar on the left (2 - x), tensor-tensor broadcasting,
+    division, the transcendental unaries; all on cuda."""
+    from mira_b200.hostfw import import_mira
+    import_mira()
+    from mira import ir
+    from mira.types import TensorType as TT
+
+    def build():                      # compiling rewrites the graph: one per target
+        x = ir.Value(TT("f32", (2, 3, 5)), name="x")
+        y = ir.Value(TT("f32", (1, 3, 1)), name="y")
+        g = ir.Graph("elt", [x, y], [], [])
+        t = g.add("sub", [g.const(np.float32(2.0)), x], {})
+        t = g.add("maximum", [t, y], {})
+        t = g.add("div", [t, g.add("add", [g.add("sigmoid", [x], {}), g.const(np.float32(0.5))], {})], {})
+        t = g.add("mul", [g.add("tanh", [t], {}), g.const(np.linspace(-1, 1, 5).astype(np.float32))], {})
+        g.outputs = [g.add("gelu", [t], {})]
+        return g
+
+    feeds = {"x": np.random.default_rng(0).standard_normal((2, 3, 5)).astype(np.float32),
+             "y": np.random.default_rng(1).standard_normal((1, 3, 1)).astype(np.float32)}
+    cpu = compiler.compile_ir(build(), "cpu", fuse=False, precision=None)
+    cuda = compiler.compile_ir(build(), "cuda", fuse=False, executor=FakeDevice(), cost_model=False)
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    np.testing.assert_allclose(cuda.run(feeds), cpu.run(feeds), rtol=1e-6, atol=1e-6)
