@@ -258,7 +258,7 @@ def gemm_tops(n: int = 8192, iters: int = 5) -> float:
 
 
 PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem",
-                 "decode_step", "attention_prefill", "layernorm_decode")
+                 "decode_step", "attention_prefill", "layernorm_decode", "layernorm_prefill")
 
 
 def profile_case(name: str, reps: int = 3) -> None:
@@ -277,7 +277,8 @@ def profile_case(name: str, reps: int = 3) -> None:
                     launch of a step, for a launch list
       attention_prefill  the prefill's fused attention: 8 sequences x 12 heads x 1024 tokens, d_head 64,
                     causal mask with exact tile skipping
-      layernorm_decode  a decode step's layernorm: 64 rows x 768, f32 and int8 out"""
+      layernorm_decode  a decode step's layernorm: 64 rows x 768, f32 and int8 out
+      layernorm_prefill a prefill layernorm: 65536 rows x 768 (201 MB), int8 out"""
     from mira_b200 import _lib, kernels as K
     from mira_b200.device import DeviceBuffer as DB
     rng = np.random.default_rng(0)
@@ -363,14 +364,16 @@ def profile_case(name: str, reps: int = 3) -> None:
                       K.View(mb, (0, 0, t, 1)), tm, km, tz, out=K.View(out, st))
         for _ in range(reps):
             K.attention_f32(desc)
-    elif name == "layernorm_decode":
-        rows, d = 64, 768
+    elif name in ("layernorm_decode", "layernorm_prefill"):
+        rows, d = (64, 768) if name == "layernorm_decode" else (65536, 768)
         x = DB.from_array(rng.standard_normal((rows, d), dtype=np.float32))
         g = DB.from_array((1 + 0.02 * rng.standard_normal(d)).astype(np.float32))
         bta = DB.from_array((0.02 * rng.standard_normal(d)).astype(np.float32))
-        y, yq = DB(rows * d * 4), DB(rows * d)
+        y = DB(rows * d * 4) if name == "layernorm_decode" else None
+        yq = DB(rows * d)
         for _ in range(reps):
-            K.layernorm_rows(x, rows, d, d, g, bta, 1e-5, out_f32=y, ld_f32=d, out_i8=yq, ld_i8=d, out_scale=0.03)
+            K.layernorm_rows(x, rows, d, d, g, bta, 1e-5, out_f32=y, ld_f32=d if y is not None else 0, out_i8=yq,
+                             ld_i8=d, out_scale=0.03)
     elif name == "decode_step":
         from mira_b200 import decode
         _, step = _decode_programs(DECODE["batch"], "cuda")
