@@ -1131,6 +1131,24 @@ static void pw_leaves(int n, PwLeaves& pw) {
   pw.start[pw.count] = n;
 }
 
+// Whether NumPy's pairwise recursion over d elements is a perfect binary tree of NL leaves of L
+// elements (layernorm_tree_kernel): NL a power of two up to 16, L a multiple of 8 of at most 128,
+// and more than 64 when the range is split (halves of multiples of 8 split exactly).
+static bool ln_tree_shape(int64_t d, int& L, int& NL) {
+  for (int nl = 1; nl <= 16; nl *= 2) {
+    if (d % nl != 0) continue;
+    const int64_t l = d / nl;
+    if (l % 8 == 0 && l <= 128 && (nl == 1 ? l >= 8 : l > 64)) {
+      L = int(l);
+      NL = nl;
+      return true;
+    }
+  }
+  return false;
+}
+
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
 static int row_grid(const DeviceState* dev, int64_t rows) {
   int64_t blocks = (rows + ROW_WARPS - 1) / ROW_WARPS;
   const int64_t cap = int64_t(dev->sm_count) * 8;
@@ -1155,6 +1173,27 @@ extern "C" int mira_cuda_layernorm_rows(const float* x, int64_t rows, int64_t d,
   p.out = out_f32; p.ld_out = ld_f32; p.out_i8 = out_i8; p.ld_i8 = ld_i8;
   p.q = make_qscale(out_i8 != nullptr ? out_scale : 1.0f);
   pw_leaves(int(d), p.pw);
+  int L = 0, NL = 0;
+  if (ln_tree_shape(d, L, NL) && (L == 96 || L == 128) && aligned16(x) && ld_x % 4 == 0 && aligned16(gamma) &&
+      aligned16(beta) && (out_f32 == nullptr || (aligned16(out_f32) && ld_f32 % 4 == 0)) &&
+      (out_i8 == nullptr || ((reinterpret_cast<uintptr_t>(out_i8) & 3u) == 0 && ld_i8 % 4 == 0))) {
+    const int64_t rows_per_block = (LN_TREE_THREADS / 32) * (32 / (2 * NL));
+    const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
+    const int64_t cap = int64_t(dev->sm_count) * 16;
+    const int grid = int(blocks < cap ? blocks : cap);
+    auto kern = L == 96 ? (NL == 1   ? layernorm_tree_kernel<96, 1>
+                           : NL == 2 ? layernorm_tree_kernel<96, 2>
+                           : NL == 4 ? layernorm_tree_kernel<96, 4>
+                           : NL == 8 ? layernorm_tree_kernel<96, 8>
+                                     : layernorm_tree_kernel<96, 16>)
+                        : (NL == 1   ? layernorm_tree_kernel<128, 1>
+                           : NL == 2 ? layernorm_tree_kernel<128, 2>
+                           : NL == 4 ? layernorm_tree_kernel<128, 4>
+                           : NL == 8 ? layernorm_tree_kernel<128, 8>
+                                     : layernorm_tree_kernel<128, 16>);
+    kern<<<grid, LN_TREE_THREADS, 0, dev->stream>>>(p);
+    return after_launch("layernorm_tree_kernel");
+  }
   if (d >= 8 && p.pw.count <= 16) {
     // leaves of at most 128 elements, 4 per round, chains of at most 16 in registers
     if (p.pw.count <= 4) layernorm_rows_reg_kernel<1><<<row_grid(dev, rows), ROW_WARPS * 32, 0, dev->stream>>>(p);

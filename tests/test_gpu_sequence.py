@@ -33,8 +33,10 @@ def _ulps(a, b):
     return np.abs(a - b)
 
 
+# d = 768, 96, 256, 512, 1024 and 2048 take layernorm_tree_kernel (NumPy's pairwise tree over 8, 1, 2,
+# 4, 8 and 16 leaves), with rows that leave lanes of the last warp idle; the others the general kernels
 @pytest.mark.parametrize("rows,d", [(1, 768), (37, 768), (1000, 768), (5, 100), (9, 5), (3, 8), (17, 3072),
-                                    (4, 8192)])
+                                    (4, 8192), (3, 96), (70, 256), (33, 512), (9, 1024), (5, 2048)])
 def test_layernorm_rows_bit_exact(cuda_device, rows, d):
     K, DB = _k()
     rng = np.random.default_rng(rows * 31 + d)
@@ -50,6 +52,22 @@ def test_layernorm_rows_bit_exact(cuda_device, rows, d):
     want = ref.layernorm(x, g, b)
     _bits_equal(yb.download((rows, d), np.float32), want)
     np.testing.assert_array_equal(qb.download((rows, ld_i8), np.int8)[:, :d], ref.quantize_activation(want, scale))
+
+
+@pytest.mark.parametrize("ld_x", [768, 770])
+def test_layernorm_int8_only(cuda_device, ld_x):
+    """The prefill form: int8 output only; a row stride that is not a multiple of 4 floats takes the
+    general kernel, the aligned one the tree kernel, with the same bytes."""
+    K, DB = _k()
+    rng = np.random.default_rng(ld_x)
+    rows, d = 301, 768
+    full = (rng.standard_normal((rows, ld_x)) * 2 + 0.5).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    xb, gb, bb, qb = DB.from_array(full), DB.from_array(g), DB.from_array(b), DB(rows * d)
+    K.layernorm_rows(xb, rows, d, ld_x, gb, bb, 1e-5, out_i8=qb, ld_i8=d, out_scale=0.02)
+    want = ref.quantize_activation(ref.layernorm(full[:, :d], g, b), 0.02)
+    np.testing.assert_array_equal(qb.download((rows, d), np.int8), want)
 
 
 def test_layernorm_strided_rows(cuda_device):
