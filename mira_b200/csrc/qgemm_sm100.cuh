@@ -114,10 +114,13 @@ struct QgCfg {
   static constexpr int POOL_ROWS = 96;
   static constexpr int STAGING_BYTES = POOL ? 2 * POOL_ROWS * POOL_PITCH * 4 : EPI_WARPS * 32 * STAGE_PITCH * 4;
   static constexpr int B_REGION = RKB > 0 ? RKB * B_BYTES : STAGES * B_BYTES;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * A_BYTES + B_REGION + STAGING_BYTES + 256;
+  // the barrier region after the staging: 2 * STAGES + 8 mbarriers, the TMEM address, the abort flag
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 8) + 8 <= 256 ? 256 : 512;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * A_BYTES + B_REGION + STAGING_BYTES + BAR_BYTES;
   static_assert(!POOL || (AMODE != 0 && BN == 64), "fused pooling: convolutions with at most 64 channels");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(8 * (2 * STAGES + 8) + 8 <= BAR_BYTES, "barrier region");
   static_assert(BK == 128 || (BK == 64 && AMODE == QG_A_IM2COL), "64-byte K-blocks: im2col convolutions only");
 };
 

@@ -207,6 +207,16 @@ def test_qgemm_splitk_mul_step_exact(cuda_device, M):
     np.testing.assert_array_equal(got_q[:, :4096], want_q)
 
 
+def test_qgemm_splitk_shapes_in_sequence(cuda_device):
+    """Split-K shapes of different tile counts and splits one after another (a decode step's mix),
+    each sharing nothing but the device: all bit-exact."""
+    for M, N, K_ in [(64, 768, 768), (64, 3072, 768), (64, 768, 768), (16, 4096, 4096), (64, 768, 3072),
+                     (64, 3072, 768)]:
+        got, want, got_q, want_q = _run_qgemm(M, N, K_, ["bias", "residual"], seed=N + K_, splitk=True)
+        _same_f32(got, want)
+        np.testing.assert_array_equal(got_q[:, :N], want_q)
+
+
 def test_qgemm_splitk_workspace_rule(cuda_device):
     K, _ = _k()
     assert K.qgemm_workspace(65536, 768, 3072) == 0          # enough output tiles
