@@ -1177,20 +1177,22 @@ extern "C" int mira_cuda_layernorm_rows(const float* x, int64_t rows, int64_t d,
   if (ln_tree_shape(d, L, NL) && (L == 96 || L == 128) && aligned16(x) && ld_x % 4 == 0 && aligned16(gamma) &&
       aligned16(beta) && (out_f32 == nullptr || (aligned16(out_f32) && ld_f32 % 4 == 0)) &&
       (out_i8 == nullptr || ((reinterpret_cast<uintptr_t>(out_i8) & 3u) == 0 && ld_i8 % 4 == 0))) {
-    const int64_t rows_per_block = (LN_TREE_THREADS / 32) * (32 / (2 * NL));
+    // 2 chains per lane (4 lanes per leaf) while a row fits a warp, else 4
+    const int lanes_per_row = NL <= 8 ? 4 * NL : 2 * NL;
+    const int64_t rows_per_block = (LN_TREE_THREADS / 32) * (32 / lanes_per_row);
     const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
     const int64_t cap = int64_t(dev->sm_count) * 16;
     const int grid = int(blocks < cap ? blocks : cap);
-    auto kern = L == 96 ? (NL == 1   ? layernorm_tree_kernel<96, 1>
-                           : NL == 2 ? layernorm_tree_kernel<96, 2>
-                           : NL == 4 ? layernorm_tree_kernel<96, 4>
-                           : NL == 8 ? layernorm_tree_kernel<96, 8>
-                                     : layernorm_tree_kernel<96, 16>)
-                        : (NL == 1   ? layernorm_tree_kernel<128, 1>
-                           : NL == 2 ? layernorm_tree_kernel<128, 2>
-                           : NL == 4 ? layernorm_tree_kernel<128, 4>
-                           : NL == 8 ? layernorm_tree_kernel<128, 8>
-                                     : layernorm_tree_kernel<128, 16>);
+    auto kern = L == 96 ? (NL == 1   ? layernorm_tree_kernel<96, 1, 2>
+                           : NL == 2 ? layernorm_tree_kernel<96, 2, 2>
+                           : NL == 4 ? layernorm_tree_kernel<96, 4, 2>
+                           : NL == 8 ? layernorm_tree_kernel<96, 8, 2>
+                                     : layernorm_tree_kernel<96, 16, 4>)
+                        : (NL == 1   ? layernorm_tree_kernel<128, 1, 2>
+                           : NL == 2 ? layernorm_tree_kernel<128, 2, 2>
+                           : NL == 4 ? layernorm_tree_kernel<128, 4, 2>
+                           : NL == 8 ? layernorm_tree_kernel<128, 8, 2>
+                                     : layernorm_tree_kernel<128, 16, 4>);
     kern<<<grid, LN_TREE_THREADS, 0, dev->stream>>>(p);
     return after_launch("layernorm_tree_kernel");
   }

@@ -217,12 +217,13 @@ __global__ void __launch_bounds__(ROW_WARPS * 32, ROUNDS == 1 ? 3 : (ROUNDS == 2
 
 // Rows whose NumPy pairwise recursion is a perfect binary tree: d = NL * L with NL a power of two
 // (at most 16) and L a multiple of 8, L <= 128 and, when NL > 1, L > 64 (every split halves the
-// range exactly and stops at leaves of L elements: d = 768 is 8 leaves of 96).  2 * NL lanes
-// hold a row: the two lanes of a leaf take alternate groups of 4 elements (16-byte loads), so
-// lane half h accumulates chains 4h .. 4h + 3 of NumPy's 8-way unrolled leaf in element order;
-// one shuffle joins the halves ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)) and xor shuffles
-// over the leaf bits add the leaves up the tree.  Same arithmetic as layernorm_rows_reg_kernel,
-// with 32 / (2 * NL) rows per warp and no per-element bounds or shared-memory tree.
+// range exactly and stops at leaves of L elements: d = 768 is 8 leaves of 96).  A leaf's 8 chains
+// (NumPy's 8-way unrolled sum) go to 8 / CPL lanes, CPL chains each: lane q of a leaf loads
+// elements CPL*q .. CPL*q + CPL - 1 of every 8 (one 16-byte load for CPL = 4, 8-byte for CPL = 2)
+// and accumulates them in element order; lane sums and xor shuffles then rebuild
+// ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)) and add the leaves up the tree.  Same
+// arithmetic as layernorm_rows_reg_kernel, with 32 / (NL * 8 / CPL) rows per warp and no per-element
+// bounds or shared-memory tree.  CPL = 2 halves the registers and the serial work per lane.
 constexpr int LN_TREE_THREADS = 128;
 
 __device__ __forceinline__ float ln_divide(float t, float sd, float rsd) {
@@ -235,35 +236,57 @@ __device__ __forceinline__ float ln_divide(float t, float sd, float rsd) {
   return __fdiv_rn(t, sd);
 }
 
-template <int L, int NL>
+template <int CPL>
+struct LnVec;
+template <>
+struct LnVec<4> {
+  using T = float4;
+  static __device__ __forceinline__ void get(const T& v, float (&e)[4]) { e[0] = v.x; e[1] = v.y; e[2] = v.z; e[3] = v.w; }
+  static __device__ __forceinline__ T make(const float (&e)[4]) { return make_float4(e[0], e[1], e[2], e[3]); }
+  static __device__ __forceinline__ T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+};
+template <>
+struct LnVec<2> {
+  using T = float2;
+  static __device__ __forceinline__ void get(const T& v, float (&e)[2]) { e[0] = v.x; e[1] = v.y; }
+  static __device__ __forceinline__ T make(const float (&e)[2]) { return make_float2(e[0], e[1]); }
+  static __device__ __forceinline__ T zero() { return make_float2(0.f, 0.f); }
+};
+
+template <int L, int NL, int CPL>
 __global__ void __launch_bounds__(LN_TREE_THREADS) layernorm_tree_kernel(const LnParams p) {
-  constexpr int LPR = 2 * NL;   // lanes per row
-  constexpr int RPW = 32 / LPR; // rows per warp
-  constexpr int V = L / 8;      // 16-byte groups per lane
+  using Vec = LnVec<CPL>;
+  using VT = typename Vec::T;
+  constexpr int LPL = 8 / CPL;        // lanes per leaf
+  constexpr int LPR = NL * LPL;       // lanes per row
+  static_assert(LPR <= 32, "a row fits a warp");
+  constexpr int RPW = 32 / LPR;       // rows per warp
+  constexpr int V = L / 8;            // vectors per lane
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR;
-  const int h = sub & 1;
-  const int col0 = (sub >> 1) * L + 4 * h;   // first element of this lane; then every 8
+  const int col0 = (sub / LPL) * L + CPL * (sub % LPL);   // first element of this lane; then every 8
   const float dn = static_cast<float>(p.d);
-  const float4* __restrict__ gam = reinterpret_cast<const float4*>(p.gamma + col0);
-  const float4* __restrict__ bet = reinterpret_cast<const float4*>(p.beta + col0);
+  const VT* __restrict__ gam = reinterpret_cast<const VT*>(p.gamma + col0);
+  const VT* __restrict__ bet = reinterpret_cast<const VT*>(p.beta + col0);
+  constexpr int STEP = 8 / CPL;       // vectors between a lane's consecutive loads
   const int64_t warps = int64_t(gridDim.x) * (LN_TREE_THREADS / 32);
   for (int64_t w = (int64_t(blockIdx.x) * LN_TREE_THREADS + threadIdx.x) >> 5; w * RPW < p.rows; w += warps) {
     const int64_t row = w * RPW + lane / LPR;
     const bool live = row < p.rows;
-    const float4* __restrict__ xr = reinterpret_cast<const float4*>(p.x + (live ? row : 0) * p.ld_x + col0);
-    float4 v[V];
+    const VT* __restrict__ xr = reinterpret_cast<const VT*>(p.x + (live ? row : 0) * p.ld_x + col0);
+    VT v[V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) v[i] = live ? __ldg(xr + 2 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < V; ++i) v[i] = live ? __ldg(xr + STEP * i) : Vec::zero();
     float mu = 0.0f, sd = 0.0f, rsd = 0.0f;
 #pragma unroll
     for (int pass = 0; pass < 2; ++pass) {
-      float r[4];
+      float r[CPL];
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        float e[CPL];
+        Vec::get(v[i], e);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < CPL; ++k) {
           float t = e[k];
           if (pass) {
             t = __fsub_rn(t, mu);
@@ -272,10 +295,11 @@ __global__ void __launch_bounds__(LN_TREE_THREADS) layernorm_tree_kernel(const L
           r[k] = i == 0 ? t : __fadd_rn(r[k], t);
         }
       }
-      float s = __fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3]));
-      s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+      float s;
+      if constexpr (CPL == 4) s = __fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3]));
+      else s = __fadd_rn(r[0], r[1]);
 #pragma unroll
-      for (int m = 2; m < LPR; m <<= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, m));
+      for (int m = 1; m < LPR; m <<= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, m));
       const float total = __fdiv_rn(s, dn);
       if (pass == 0) {
         mu = total;
@@ -285,21 +309,25 @@ __global__ void __launch_bounds__(LN_TREE_THREADS) layernorm_tree_kernel(const L
       }
     }
     if (!live) continue;
-    float4* __restrict__ yout = p.out != nullptr ? reinterpret_cast<float4*>(p.out + row * p.ld_out + col0) : nullptr;
-    uint32_t* __restrict__ qout =
-        p.out_i8 != nullptr ? reinterpret_cast<uint32_t*>(p.out_i8 + row * p.ld_i8 + col0) : nullptr;
+    VT* __restrict__ yout = p.out != nullptr ? reinterpret_cast<VT*>(p.out + row * p.ld_out + col0) : nullptr;
+    int8_t* __restrict__ qout = p.out_i8 != nullptr ? p.out_i8 + row * p.ld_i8 + col0 : nullptr;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      const float4 g = __ldg(gam + 2 * i), b = __ldg(bet + 2 * i);
-      float4 y;
-      y.x = __fadd_rn(__fmul_rn(ln_divide(__fsub_rn(v[i].x, mu), sd, rsd), g.x), b.x);
-      y.y = __fadd_rn(__fmul_rn(ln_divide(__fsub_rn(v[i].y, mu), sd, rsd), g.y), b.y);
-      y.z = __fadd_rn(__fmul_rn(ln_divide(__fsub_rn(v[i].z, mu), sd, rsd), g.z), b.z);
-      y.w = __fadd_rn(__fmul_rn(ln_divide(__fsub_rn(v[i].w, mu), sd, rsd), g.w), b.w);
-      if (yout != nullptr) yout[2 * i] = y;
-      if (qout != nullptr)
-        qout[2 * i] = (quant_byte(y.x, p.q) & 0xffu) | ((quant_byte(y.y, p.q) & 0xffu) << 8) |
-                      ((quant_byte(y.z, p.q) & 0xffu) << 16) | ((quant_byte(y.w, p.q) & 0xffu) << 24);
+      float x[CPL], g[CPL], b[CPL], y[CPL];
+      Vec::get(v[i], x);
+      Vec::get(__ldg(gam + STEP * i), g);
+      Vec::get(__ldg(bet + STEP * i), b);
+      uint32_t packed = 0;
+#pragma unroll
+      for (int k = 0; k < CPL; ++k) {
+        y[k] = __fadd_rn(__fmul_rn(ln_divide(__fsub_rn(x[k], mu), sd, rsd), g[k]), b[k]);
+        packed |= (quant_byte(y[k], p.q) & 0xffu) << (8 * k);
+      }
+      if (yout != nullptr) yout[STEP * i] = Vec::make(y);
+      if (qout != nullptr) {
+        if constexpr (CPL == 4) *reinterpret_cast<uint32_t*>(qout + 8 * i) = packed;
+        else *reinterpret_cast<uint16_t*>(qout + 8 * i) = static_cast<uint16_t>(packed);
+      }
     }
   }
 }
