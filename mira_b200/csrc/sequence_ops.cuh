@@ -770,7 +770,7 @@ __device__ __forceinline__ void attn_compute(const AttnParams& p, AttnSmem<DH>& 
   for (int u = 0; u < 4; ++u)
 #pragma unroll
     for (int v = 0; v < 4; ++v) s[u][v] = 0.0f;
-#pragma unroll 4
+#pragma unroll
   for (int d = 0; d < DH; d += 4) {
     float4 a[4], b[4];
 #pragma unroll
@@ -821,7 +821,7 @@ __device__ __forceinline__ void attn_compute(const AttnParams& p, AttnSmem<DH>& 
     m[u] = mnew;
   }
   __syncthreads();
-#pragma unroll 2
+#pragma unroll 4
   for (int j = 0; j < ATT_BK; j += 4) {
     float4 pa[4];
 #pragma unroll
