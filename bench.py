@@ -228,33 +228,150 @@ def time_kernels(exe, kinds, iters: int = 3) -> tuple[float, int]:
     return total / iters, len(idx)
 
 
-def gemm_tops(n: int = 8192, iters: int = 5) -> float:
-    """Throughput of mira_cuda_qgemm on an n^3 int8 GEMM (row/col scales + bias epilogue, f32 out)."""
+GEMM_SQUARE = (1024, 2048, 4096, 8192, 16384)
+GEMM_SKINNY = (1, 16, 128)
+GEMM_ITERS = 50
+ROTATE_BYTES = 320e6     # operands + output cycled between timed GEMMs: more than twice the 126 MB L2
+
+
+def gemm_operands(m: int, n: int, k: int, seed: int):
+    """Config 2's operands: A int8 [m, k] and B int8 [n, k] (K-major, the transposed [k, n] weight)
+    uniform in [-127, 127], row and column scales f32 U(1e-3, 1e-2), bias f32 N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    return (rng.integers(-127, 128, (m, k), dtype=np.int8), rng.integers(-127, 128, (n, k), dtype=np.int8),
+            rng.uniform(1e-3, 1e-2, m).astype(np.float32), rng.uniform(1e-3, 1e-2, n).astype(np.float32),
+            rng.standard_normal(n).astype(np.float32))
+
+
+def _rotation(m: int, n: int, k: int) -> int:
+    """Operand sets to cycle through so consecutive timed GEMMs never find their inputs in L2."""
+    return max(1, int(np.ceil(ROTATE_BYTES / (m * k + n * k + 4 * m * n))))
+
+
+def _graph_us(fns, iters: int) -> float:
+    """Device time per call of `iters` calls cycling over fns: captured into one CUDA graph on the
+    library stream, replayed once untimed, then once between CUDA events."""
+    from mira_b200 import _lib
+    for f in fns:
+        f()
+    _lib.call("mira_cuda_sync")
+    _lib.call("mira_cuda_graph_begin")
+    try:
+        for i in range(iters):
+            fns[i % len(fns)]()
+    finally:
+        g = C.c_void_p()
+        _lib.call("mira_cuda_graph_end", C.byref(g))
+    try:
+        _lib.call("mira_cuda_graph_launch", g)
+        _lib.call("mira_cuda_sync")
+        a, b = C.c_void_p(), C.c_void_p()
+        _lib.call("mira_cuda_event_create", C.byref(a))
+        _lib.call("mira_cuda_event_create", C.byref(b))
+        _lib.call("mira_cuda_event_record", a)
+        _lib.call("mira_cuda_graph_launch", g)
+        _lib.call("mira_cuda_event_record", b)
+        _lib.call("mira_cuda_sync")
+        ms = C.c_float()
+        _lib.call("mira_cuda_event_elapsed", a, b, C.byref(ms))
+        _lib.call("mira_cuda_event_destroy", a)
+        _lib.call("mira_cuda_event_destroy", b)
+    finally:
+        _lib.call("mira_cuda_graph_destroy", g)
+    return ms.value / iters * 1e3
+
+
+def _ours_gemm(m: int, n: int, k: int, seed: int, splitk: bool):
+    """Device buffers and launch closures of mira_cuda_qgemm (or _splitk) on config-2 operand sets."""
     from mira_b200 import _lib, kernels as K
-    from mira_b200.device import DeviceBuffer
-    A, B, Y = DeviceBuffer(n * n), DeviceBuffer(n * n), DeviceBuffer(n * n * 4)
-    _lib.call("mira_cuda_memset", C.c_void_p(A.ptr), 3, C.c_size_t(n * n))
-    _lib.call("mira_cuda_memset", C.c_void_p(B.ptr), 5, C.c_size_t(n * n))
-    rs = DeviceBuffer.from_array(np.full(n, 1e-3, np.float32))
-    cs = DeviceBuffer.from_array(np.full(n, 2e-3, np.float32))
-    bias = DeviceBuffer.from_array(K.pad_channels(np.zeros(n, np.float32)))
-    dq = K.dequant_rowcol(rs, cs)
-    e = K.Epi([K.Step("add", "channel", ptr=bias)], out_f32=Y, ld_f32=n).struct()
-    fn = _lib.load().mira_cuda_qgemm
-    args = (n, n, n, C.c_void_p(A.ptr), n, C.c_void_p(B.ptr), n, C.byref(dq), C.byref(e))
-    fn(*args)
-    _lib.call("mira_cuda_sync")
-    a, b = C.c_void_p(), C.c_void_p()
-    _lib.call("mira_cuda_event_create", C.byref(a))
-    _lib.call("mira_cuda_event_create", C.byref(b))
-    _lib.call("mira_cuda_event_record", a)
-    for _ in range(iters):
-        fn(*args)
-    _lib.call("mira_cuda_event_record", b)
-    ms = C.c_float()
-    _lib.call("mira_cuda_event_elapsed", a, b, C.byref(ms))
-    _lib.call("mira_cuda_sync")
-    return 2.0 * n ** 3 / (ms.value / iters * 1e-3) / 1e12
+    from mira_b200.device import DeviceBuffer as DB
+    keep, fns = [], []
+    lib = _lib.load()
+    for s in range(_rotation(m, n, k)):
+        A, B, rs, cs, bias = gemm_operands(m, n, k, seed + s)
+        bufs = [DB.from_array(A), DB.from_array(B), DB.from_array(rs), DB.from_array(cs),
+                DB.from_array(K.pad_channels(bias)), DB(m * n * 4)]
+        dq = K.dequant_rowcol(bufs[2], bufs[3])
+        e = K.Epi([K.Step("add", "channel", ptr=bufs[4])], out_f32=bufs[5], ld_f32=n).struct()
+        keep += bufs + [dq, e]
+        if splitk:
+            ws_bytes = K.qgemm_workspace(m, n, k)
+            ws = DB(max(ws_bytes, 16))
+            keep.append(ws)
+            args = (m, n, k, C.c_void_p(bufs[0].ptr), k, C.c_void_p(bufs[1].ptr), k, C.byref(dq), C.byref(e),
+                    C.c_void_p(ws.ptr), ws_bytes)
+            fn = lib.mira_cuda_qgemm_splitk
+        else:
+            args = (m, n, k, C.c_void_p(bufs[0].ptr), k, C.c_void_p(bufs[1].ptr), k, C.byref(dq), C.byref(e))
+            fn = lib.mira_cuda_qgemm
+
+        def call(fn=fn, args=args):
+            rc = fn(*args)
+            if rc != _lib.OK:
+                raise _lib.CudaError(rc, _lib.last_error())
+        fns.append(call)
+    return keep, fns
+
+
+def cublaslt_us(m: int, n: int, k: int, seed: int, iters: int = GEMM_ITERS) -> float | None:
+    """torch._int_mm (cuBLASLt int8 x int8 -> int32) on the same operand sets and rotation, for
+    context: device time per call of `iters` calls replayed from a CUDA graph."""
+    try:
+        import torch
+        sets = []
+        for s in range(_rotation(m, n, k)):
+            A, B, *_ = gemm_operands(m, n, k, seed + s)
+            sets.append((torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda().t()))
+        for a, b in sets:
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(iters):
+                a, b = sets[i % len(sets)]
+                torch._int_mm(a, b)
+        g.replay()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        g.replay()
+        s1.record()
+        torch.cuda.synchronize()
+        us = s0.elapsed_time(s1) / iters * 1e3
+        del g, sets
+        torch.cuda.empty_cache()
+        return us
+    except Exception:
+        return None
+
+
+def gemm_sweep(peak_tops: float | None) -> dict:
+    """Config 2 (the int8 GEMM sweep) through mira_cuda_qgemm: square M = N = K in GEMM_SQUARE and
+    skinny M x 4096 x 4096 (split-K), row x column scales + bias, f32 out; operands per config 2,
+    cycled so no timed GEMM finds its inputs in L2; GEMM_ITERS calls replayed from a CUDA graph.
+    cuBLASLt's int8 GEMM (int32 out, no epilogue) on the same data beside each square size."""
+    square = {}
+    for n in GEMM_SQUARE:
+        keep, fns = _ours_gemm(n, n, n, 1000 + n, splitk=False)
+        us = _graph_us(fns, GEMM_ITERS)
+        del keep, fns
+        tops = 2.0 * n ** 3 / (us * 1e-6) / 1e12
+        lt = cublaslt_us(n, n, n, 1000 + n)
+        lt_tops = 2.0 * n ** 3 / (lt * 1e-6) / 1e12 if lt else None
+        square[str(n)] = {"us": us, "tops": tops, "frac_of_2x_bf16": tops / peak_tops if peak_tops else None,
+                          "cublaslt_tops": lt_tops, "frac_of_cublaslt": tops / lt_tops if lt_tops else None,
+                          "operand_sets": _rotation(n, n, n)}
+    skinny = {}
+    for m in GEMM_SKINNY:
+        n = k = 4096
+        keep, fns = _ours_gemm(m, n, k, 2000 + m, splitk=True)
+        us = _graph_us(fns, GEMM_ITERS)
+        del keep, fns
+        nbytes = m * k + k * n + 4 * m * n + 4 * (m + 2 * n)
+        skinny[str(m)] = {"us": us, "gb_s": nbytes / (us * 1e-6) / 1e9, "algorithmic_bytes": nbytes}
+    return {"square": square, "skinny_mx4096x4096": skinny, "iters": GEMM_ITERS,
+            "data": "config 2: A, B int8 uniform [-127, 127], row/col scales U(1e-3, 1e-2), bias N(0, 1), "
+                    "seeded; operand sets cycled (more than twice L2 between reuses)"}
 
 
 PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem",
@@ -264,7 +381,7 @@ PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_r
 def profile_case(name: str, reps: int = 3) -> None:
     """One kernel on a bounded, seeded case, launched `reps` times, for ncu captures (the inputs are
     larger than L2 where the kernel is HBM-bound; a few hundred MB on the device):
-      gemm8192      mira_cuda_qgemm 8192^3, row/col scales + bias, f32 out (config 2)
+      gemm8192      mira_cuda_qgemm 8192^3 on config-2 operands, row/col scales + bias, f32 out
       conv_l1       ResNet-18 layer-1 3x3 conv, batch 256, 56x56x64 -> 64, bias + relu, int8 + f32 out
       dwconv_l1     MobileNetV2's first depthwise layer, batch 96, 112x112x32, bias + relu6, int8 out
       attention_q1  a decode step's attention: 64 sequences x 12 heads, 1024 cached rows, d_head 64
@@ -284,11 +401,10 @@ def profile_case(name: str, reps: int = 3) -> None:
     rng = np.random.default_rng(0)
     if name == "gemm8192":
         n = 8192
-        A, B, Y = DB(n * n), DB(n * n), DB(n * n * 4)
-        _lib.call("mira_cuda_memset", C.c_void_p(A.ptr), 3, C.c_size_t(n * n))
-        _lib.call("mira_cuda_memset", C.c_void_p(B.ptr), 5, C.c_size_t(n * n))
-        rs, cs = DB.from_array(np.full(n, 1e-3, np.float32)), DB.from_array(np.full(n, 2e-3, np.float32))
-        bias = DB.from_array(K.pad_channels(np.zeros(n, np.float32)))
+        a, b, r, c, bi = gemm_operands(n, n, n, 1000 + n)
+        A, B, Y = DB.from_array(a), DB.from_array(b), DB(n * n * 4)
+        rs, cs = DB.from_array(r), DB.from_array(c)
+        bias = DB.from_array(K.pad_channels(bi))
         epi = K.Epi([K.Step("add", "channel", ptr=bias)], out_f32=Y, ld_f32=n)
         for _ in range(reps):
             K.qgemm(n, n, n, A, n, B, n, K.dequant_rowcol(rs, cs), epi)
@@ -404,74 +520,84 @@ def profile_case(name: str, reps: int = 3) -> None:
 CONV_DRAM_BYTES_PER_PASS = 2.535e9
 
 
-def skinny_gemm(m: int, n: int = 4096, k: int = 4096, iters: int = 50) -> dict:
-    """The GEMM sweep's skinny rows (config 2): M x 4096 x 4096 through mira_cuda_qgemm_splitk (split-K
-    with a workspace when the output tiles cannot fill the GPU); HBM-bound, so also GB/s of the
-    algorithmic bytes M*K + K*N + 4*M*N."""
-    from mira_b200 import _lib, kernels as K
-    from mira_b200.device import DeviceBuffer
-    A, B, Y = DeviceBuffer(m * k), DeviceBuffer(n * k), DeviceBuffer(m * n * 4)
-    _lib.call("mira_cuda_memset", C.c_void_p(A.ptr), 3, C.c_size_t(m * k))
-    _lib.call("mira_cuda_memset", C.c_void_p(B.ptr), 5, C.c_size_t(n * k))
-    rs = DeviceBuffer.from_array(np.full(m, 1e-3, np.float32))
-    cs = DeviceBuffer.from_array(np.full(n, 2e-3, np.float32))
-    bias = DeviceBuffer.from_array(K.pad_channels(np.zeros(n, np.float32)))
-    dq = K.dequant_rowcol(rs, cs)
-    e = K.Epi([K.Step("add", "channel", ptr=bias)], out_f32=Y, ld_f32=n).struct()
-    ws_bytes = K.qgemm_workspace(m, n, k)
-    ws = DeviceBuffer(max(ws_bytes, 16))
-    fn = _lib.load().mira_cuda_qgemm_splitk
-    args = (m, n, k, C.c_void_p(A.ptr), k, C.c_void_p(B.ptr), k, C.byref(dq), C.byref(e), C.c_void_p(ws.ptr), ws_bytes)
-    for _ in range(3):
-        fn(*args)
-    _lib.call("mira_cuda_sync")
-    # the launches replay from a CUDA graph, so the time is the device's, not the host's issue rate
-    _lib.call("mira_cuda_graph_begin")
-    try:
-        for _ in range(iters):
-            fn(*args)
-    finally:
-        g = C.c_void_p()
-        _lib.call("mira_cuda_graph_end", C.byref(g))
-    _lib.call("mira_cuda_graph_launch", g)
-    _lib.call("mira_cuda_sync")
-    a, b = C.c_void_p(), C.c_void_p()
-    _lib.call("mira_cuda_event_create", C.byref(a))
-    _lib.call("mira_cuda_event_create", C.byref(b))
-    _lib.call("mira_cuda_event_record", a)
-    _lib.call("mira_cuda_graph_launch", g)
-    _lib.call("mira_cuda_event_record", b)
-    ms = C.c_float()
-    _lib.call("mira_cuda_sync")
-    _lib.call("mira_cuda_event_elapsed", a, b, C.byref(ms))
-    _lib.call("mira_cuda_graph_destroy", g)
-    us = ms.value / iters * 1e3
-    return {"us": us, "gb_s": (m * k + k * n + 4 * m * n) / (us * 1e-6) / 1e9, "workspace_bytes": ws_bytes}
+def pass_bytes(graph) -> dict:
+    """Algorithmic HBM bytes of one forward pass of the compiled graph, in this target's
+    representations: every activation is written once per representation it needs (int8, 1 byte
+    per element, when a quantized op reads it; f32 otherwise) and read once by each op that uses
+    it; weights and the graph input are read once.  Views (reshape/transpose) and the padding that
+    the max pool reads through cost nothing."""
+    QO = ("qconv2d", "qmatmul")
+    FREE = ("reshape", "transpose", "pad", "const")
+    users: dict = {}
+    for op in graph.ops:
+        for i, v in enumerate(op.inputs):
+            users.setdefault(v, []).append((op, i))
+
+    def root(v):
+        p = v.producer
+        while p is not None and p.kind in FREE[:3]:
+            v = p.inputs[0]
+            p = v.producer
+        return v
+
+    def numel(v):
+        return int(np.prod(v.type.shape, dtype=np.int64))
+
+    def is_const(v):
+        p = v.producer
+        return p is not None and p.kind in ("const", "dequantize")
+
+    reads = writes = weights = 0
+    reps: dict = {}
+    for op in graph.ops:
+        if op.kind in FREE or op.is_constant_like:
+            continue
+        for i, v in enumerate(op.inputs):
+            if is_const(v):
+                continue
+            r = root(v)
+            kind = "i8" if (op.kind in QO and i == 0) else "f32"
+            reps.setdefault(r, set()).add(kind)
+            reads += numel(r) * (1 if kind == "i8" else 4)
+        if op.kind in QO:
+            weights += int(np.asarray(op.attrs["q"]).nbytes)
+    for v, kinds in reps.items():
+        if v in graph.inputs:
+            continue
+        writes += numel(v) * sum(1 if k == "i8" else 4 for k in kinds)
+    for v in graph.outputs:
+        writes += numel(v) * 4
+    x_bytes = sum(numel(v) * 4 for v in graph.inputs)
+    reads_no_input = reads - sum(numel(v) * 4 for v in graph.inputs if v in reps)
+    total = reads_no_input + x_bytes + writes + weights
+    return {"bytes": total, "activation_reads": reads_no_input, "activation_writes": writes,
+            "weights": weights, "input": x_bytes}
 
 
-def cublaslt_int8_tops(n: int = 8192) -> float | None:
-    """torch._int_mm (cuBLASLt int8) at n^3, for context next to the roofline."""
-    try:
-        import torch
-        a = torch.ones((n, n), dtype=torch.int8, device="cuda")
-        b = torch.ones((n, n), dtype=torch.int8, device="cuda").t()
-        for _ in range(3):
-            torch._int_mm(a, b)
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(10):
-            torch._int_mm(a, b)
-        e.record()
-        torch.cuda.synchronize()
-        return 2.0 * n ** 3 / (s.elapsed_time(e) / 10 * 1e-3) / 1e12
-    except Exception:
-        return None
+def parity_check(workload: str, batch: int, out: np.ndarray, x: np.ndarray, calib_batch: int, n_calib: int,
+                 n_images: int = 4) -> dict:
+    """The timed program's own output rows against the reference cpu target (MIRA's NumPy golden
+    model) run on the same input rows, bit for bit: a batch-1 (MLP: full-batch) cpu program compiled
+    with the same calibration, so every activation scale is identical.  Images: first, last and a
+    seeded middle pair."""
+    from mira_b200 import configs
+    if workload == "mlp":
+        cpu = configs.compile_w8a8(workload, batch, "cpu", calib_batch=calib_batch, n_calib=n_calib)
+        want = cpu.run({"x": x})
+        bad = int((want != out).any(axis=1).sum())
+        return {"images": int(batch), "mismatches": bad, "oracle": "reference cpu target, whole batch"}
+    cpu = configs.compile_w8a8(workload, 1, "cpu", calib_batch=calib_batch, n_calib=n_calib)
+    rng = np.random.default_rng(7)
+    idx = sorted({0, batch - 1, *(int(i) for i in rng.choice(batch, size=max(0, n_images - 2), replace=False))})
+    bad = [i for i in idx if not np.array_equal(cpu.run({"x": x[i:i + 1]}), out[i:i + 1])]
+    return {"images": len(idx), "mismatches": len(bad), "rows": idx,
+            "oracle": "reference cpu target (batch-1 program, same calibration), bit for bit"}
 
 
-def reference_cpu_sample(steps: int, warmup: int, workload: str = WORKLOAD) -> dict:
+def reference_cpu_sample(steps: int, warmup: int, workload: str = WORKLOAD, max_seconds: float = 60.0) -> dict:
     """The reference's own cpu W8A8 path (mira.compile_ir(..., "cpu", quantize="w8a8") then
-    CompiledProgram.run) on the workload's bounded sample."""
+    CompiledProgram.run) on the workload's bounded sample: `steps` runs, or fewer when they would
+    take longer than `max_seconds` (the rate is over the runs done)."""
     w = WORKLOADS[workload]
     from mira_b200 import configs
     from mira_b200.hostfw import import_mira
@@ -485,12 +611,15 @@ def reference_cpu_sample(steps: int, warmup: int, workload: str = WORKLOAD) -> d
     for _ in range(warmup):
         prog.run(feeds)
     t0 = time.perf_counter()
-    for _ in range(steps):
+    done = 0
+    while done < steps and (done == 0 or time.perf_counter() - t0 < max_seconds):
         prog.run(feeds)
+        done += 1
     dt = time.perf_counter() - t0
-    return {"value": items * steps / dt * w["cpu_scale"], "unit": w["unit"], "cores": os.cpu_count(),
-            "kind": "reference", "ms_per_step": dt / steps * 1e3,
-            "sample": f"{steps} run(s) after {warmup} warm-up run(s), {w['cpu_note']}; reference cpu target "
+    return {"value": items * done / dt * w["cpu_scale"], "unit": w["unit"], "cores": os.cpu_count(),
+            "kind": "reference", "ms_per_step": dt / done * 1e3, "steps_run": done,
+            "sample": f"{done} run(s) after {warmup} warm-up run(s) (at most {steps}, stopped after "
+                      f"{max_seconds:.0f} s), {w['cpu_note']}; reference cpu target "
                       f"(NumPy golden model, OpenBLAS on all host cores)"}
 
 
@@ -502,25 +631,30 @@ def _decode_programs(batch: int, target: str, device: int = 0):
     return pre, decode.compile_step(configs.transformer_step(batch, max_seq=DECODE["max_seq"]), pre, target, **opts)
 
 
-def reference_decode_sample(steps: int, warmup: int) -> dict:
-    """The reference cpu target running the quantized step graph (batch 1, caches through the host)."""
+def reference_decode_sample(steps: int, warmup: int, max_seconds: float = 60.0) -> dict:
+    """The reference cpu target running the quantized step graph (batch 1, caches through the host),
+    `steps` steps or as many as fit in `max_seconds`."""
     _, prog = _decode_programs(1, "cpu")
     g = prog.graph
     names = [v.name for v in g.inputs[3:]]
     caches = {n: np.zeros(v.type.shape, np.float32) for n, v in zip(names, g.inputs[3:])}
     tok = np.zeros((1, 1), np.int32)
     dt = 0.0
+    done = 0
     for i in range(warmup + steps):
+        if i >= warmup and done > 0 and dt > max_seconds:
+            break
         t0 = time.perf_counter()
         out = prog.run({"tok": tok, "pos2": np.array([i, 0], np.int32), "pos4": np.array([0, 0, i, 0], np.int32),
                         **caches})
         if i >= warmup:
             dt += time.perf_counter() - t0
+            done += 1
         caches = dict(zip(names, out[1:]))
         tok = out[0][:, 0].argmax(axis=1).astype(np.int32).reshape(1, 1)
-    return {"value": steps / dt, "unit": DECODE["unit"], "cores": os.cpu_count(), "kind": "reference",
-            "ms_per_step": dt / steps * 1e3,
-            "sample": f"{steps} step(s) after {warmup} warm-up step(s) of one sequence (batch 1) through the W8A8 "
+    return {"value": done / dt, "unit": DECODE["unit"], "cores": os.cpu_count(), "kind": "reference",
+            "ms_per_step": dt / done * 1e3, "steps_run": done,
+            "sample": f"{done} step(s) after {warmup} warm-up step(s) of one sequence (batch 1) through the W8A8 "
                       f"step graph, caches through the host; reference cpu target (NumPy golden model, OpenBLAS "
                       f"on all host cores)"}
 
@@ -532,7 +666,7 @@ def run_reference(args) -> None:
     if args.workload == "decode":
         res = reference_decode_sample(args.steps, args.warmup)
         line = {"metric": DECODE["metric"], "value": res["value"], "unit": DECODE["unit"], "impl": "reference",
-                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+                "n_gpus": args.gpus, "steps": res["steps_run"], "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
                 "data": "synthetic", "config": {"workload": DECODE["config"], "batch_per_step": 1,
                                                 "note": "bounded sample: one sequence per step"},
@@ -543,7 +677,7 @@ def run_reference(args) -> None:
     w = WORKLOADS[args.workload]
     res = reference_cpu_sample(args.steps, args.warmup, args.workload)
     line = {"metric": w["metric"], "value": res["value"], "unit": w["unit"], "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+            "steps": res["steps_run"], "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": w["config"], "batch_per_step": w["cpu_batch"],
                        "note": f"bounded sample of the workload: {w['cpu_note']}"},
@@ -653,16 +787,54 @@ def run_decode(args, rank: int, world: int, local: int, dist) -> None:
         dist.destroy_process_group()
 
 
+def _init_dist(local: int):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+        os.environ["NCCL_DEBUG"] = "WARN"      # keep stdout to the one JSON line
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return dist
+
+
+def _device_timed(exe, steps: int, barrier, max_over_ranks, local: int, sample_clocks: bool = True):
+    """(max over ranks of the CUDA-event ms of `steps` device-resident replays, launches, clocks)."""
+    from mira_b200 import _lib
+    ev_a, ev_b = C.c_void_p(), C.c_void_p()
+    _lib.call("mira_cuda_event_create", C.byref(ev_a))
+    _lib.call("mira_cuda_event_create", C.byref(ev_b))
+    n0 = _lib.launch_count()
+    barrier()
+    _lib.call("mira_cuda_sync")
+    with ClockSampler(local) as clocks:
+        _lib.call("mira_cuda_event_record", ev_a)
+        for _ in range(steps):
+            exe.replay()
+        _lib.call("mira_cuda_event_record", ev_b)
+        _lib.call("mira_cuda_sync")
+        ms = C.c_float()
+        _lib.call("mira_cuda_event_elapsed", ev_a, ev_b, C.byref(ms))
+    barrier()
+    launches = steps * exe.launches_per_run + (_lib.launch_count() - n0)
+    _lib.call("mira_cuda_event_destroy", ev_a)
+    _lib.call("mira_cuda_event_destroy", ev_b)
+    return max_over_ranks(ms.value), launches, clocks
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=None, help="batch rows per GPU per step (workload default)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS) + ["decode"])
     ap.add_argument("--calib-batch", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", action="store_true", help="skip the parity check of the timed output")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM sweep of the headline line")
     ap.add_argument("--profile-case", choices=PROFILE_CASES, default=None,
                     help="launch one kernel on a bounded case a few times (for ncu) and exit")
     args = ap.parse_args()
@@ -672,20 +844,13 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.workload == "decode":
         args.batch = args.batch or DECODE["batch"]
+        args.steps = min(args.steps, (DECODE["max_seq"] - args.warmup) // 2)
         if args.impl == "reference":
             run_reference(args)
             return
         rank, world, local = _env_rank()
         os.environ["MIRA_CUDA_DEVICE"] = str(local)
-        dist = None
-        if world > 1:
-            import datetime
-
-            import torch
-            import torch.distributed as dist
-            torch.cuda.set_device(local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                    device_id=torch.device("cuda", local))
+        dist = _init_dist(local) if world > 1 else None
         run_decode(args, rank, world, local, dist)
         return
     wl = WORKLOADS[args.workload]
@@ -697,19 +862,8 @@ def main() -> None:
 
     rank, world, local = _env_rank()
     os.environ["MIRA_CUDA_DEVICE"] = str(local)
-    dist = None
-    if world > 1:
-        import datetime
+    dist = _init_dist(local) if world > 1 else None
 
-        import torch
-        import torch.distributed as dist
-        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"      # keep stdout to the one JSON line
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-
-    from mira_b200 import _lib
     from mira_b200 import configs
 
     t0 = time.perf_counter()
@@ -721,11 +875,15 @@ def main() -> None:
     exe = segs[0].executable
     x_val = prog.graph.inputs[0]
     host_x = exe.input_array(x_val)          # pinned staging array of the executable
-    rng = np.random.default_rng(1 + rank)
-    if host_x.dtype == np.int32:             # token ids
-        host_x[...] = rng.integers(0, configs._vocab_of(prog.graph, x_val), host_x.shape)
-    else:
-        host_x[...] = rng.standard_normal(host_x.shape, dtype=np.float32)
+
+    def fill_input(arr, r):
+        rng = np.random.default_rng(1 + r)
+        if arr.dtype == np.int32:             # token ids
+            arr[...] = rng.integers(0, configs._vocab_of(prog.graph, x_val), arr.shape)
+        else:
+            arr[...] = rng.standard_normal(arr.shape, dtype=np.float32)
+
+    fill_input(host_x, rank)
     name = x_val.name
     feeds = {name: host_x}
 
@@ -744,42 +902,62 @@ def main() -> None:
     # ---- warm-up through the public API (also captures the CUDA graph)
     for _ in range(args.warmup):
         out = prog.run(feeds)
-    launches_per_step = exe.launches_per_run
 
     # ---- device-resident timing
-    ev_a, ev_b = C.c_void_p(), C.c_void_p()
-    _lib.call("mira_cuda_event_create", C.byref(ev_a))
-    _lib.call("mira_cuda_event_create", C.byref(ev_b))
-    n0 = _lib.launch_count()
-    barrier()
-    _lib.call("mira_cuda_sync")
-    with ClockSampler(local) as clocks:
-        _lib.call("mira_cuda_event_record", ev_a)
-        for _ in range(args.steps):
-            exe.replay()
-        _lib.call("mira_cuda_event_record", ev_b)
-        _lib.call("mira_cuda_sync")
-        ms = C.c_float()
-        _lib.call("mira_cuda_event_elapsed", ev_a, ev_b, C.byref(ms))
-    barrier()
-    dev_ms = max_over_ranks(ms.value)
-    gpu_launches = args.steps * launches_per_step + (_lib.launch_count() - n0)
+    dev_ms, gpu_launches, clocks = _device_timed(exe, args.steps, barrier, max_over_ranks, local)
 
     # ---- end to end, K steps with host buffers: through the executable's streaming call run_many
-    # (each step's input copy overlaps the previous step's kernels) and through the reference's
-    # blocking CompiledProgram.run (copy in, kernels, copy out, one step at a time)
-    exe.run_many([{x_val: host_x}] * 2)    # first use allocates the second input buffers and events
+    # (each step's input copy overlaps the previous step's kernels; with several GPUs the final
+    # gather of the logits to rank 0 runs on the device after each step's kernels) and through the
+    # reference's blocking CompiledProgram.run (copy in, kernels, copy out, one step at a time)
+    gather = None
+    if dist is not None:
+        from mira_b200.shard import DeviceGather
+        gather = DeviceGather(exe, world, rank)
+    exe.run_many([{x_val: host_x}] * 2, gather=gather)   # first use allocates the second buffers, events
     barrier()
     t1 = time.perf_counter()
-    outs = exe.run_many([{x_val: host_x}] * args.steps)
+    outs = exe.run_many([{x_val: host_x}] * args.steps, gather=gather)
     e2e_s = max_over_ranks(time.perf_counter() - t1)
-    out = outs[-1][exe.g.outputs[0]]
     barrier()
+    out_global = outs[-1].get(exe.g.outputs[0]) if outs[-1] else None
     t1 = time.perf_counter()
     for _ in range(args.steps):
-        prog.run(feeds)
+        out = prog.run(feeds)
     e2e_blocking_s = max_over_ranks(time.perf_counter() - t1)
     barrier()
+
+    # ---- multi-GPU checks and strong scaling (untimed: after the timed regions)
+    multi = None
+    if dist is not None:
+        check = None
+        if rank == 0:
+            # another rank's shard, recomputed on this GPU, against the gathered rows of that rank
+            other = world - 1
+            x_other = np.empty_like(host_x)
+            fill_input(x_other, other)
+            mine = prog.run({name: x_other})
+            rows = out_global[other * args.batch:(other + 1) * args.batch]
+            own = out_global[:args.batch]
+            check = {"rank_recomputed_on_rank0": other, "rows": int(args.batch),
+                     "mismatches": int((rows != mine).any(axis=1).sum()),
+                     "rank0_rows_match_local_run": bool(np.array_equal(own, out))}
+        strong_batch = max(1, 256 // world) if args.workload in ("resnet18", "mobilenet_v2") else None
+        strong = None
+        if strong_batch is not None:
+            sprog = configs.compile_w8a8(args.workload, strong_batch, "cuda", calib_batch=args.calib_batch,
+                                         device=local, n_calib=wl["n_calib"], build_kw=wl["build_kw"] or None)
+            sexe = sprog.segments[0].executable
+            sx = sexe.input_array(sprog.graph.inputs[0])
+            fill_input(sx, rank)
+            for _ in range(args.warmup):
+                sprog.run({name: sx})
+            s_ms, _, _ = _device_timed(sexe, args.steps, barrier, max_over_ranks, local)
+            strong = {"global_batch": strong_batch * world, "batch_per_gpu": strong_batch,
+                      "value": strong_batch * world * args.steps / (s_ms * 1e-3), "ms_per_step": s_ms / args.steps}
+        multi = {"gather": "NCCL gather of the logits to rank 0 on the device after every e2e step "
+                           "(mira_b200.shard.DeviceGather), then one device-to-host copy on rank 0",
+                 "check": check, "strong_scaling": strong}
 
     items = args.batch * wl["items_per_row"] * world * args.steps
     value = items / (dev_ms * 1e-3)
@@ -797,17 +975,24 @@ def main() -> None:
         fam_ms, fam_n = time_kernels(exe, kinds)
         achieved = fam_ops / (fam_ms * 1e-3) / 1e12
         other = {}
-        if not headline:
-            for kind in ("attention", "layernorm", "dwconv", "qconv2d", "qgemm"):
-                ms_k, n_k = time_kernels(exe, (kind,))
-                if n_k:
-                    other[kind] = {"launches": n_k, "ms_per_step": ms_k}
+        for kind in sorted(set(l.kind for l in exe.plan.launches)):
+            ms_k, n_k = time_kernels(exe, (kind,))
+            if n_k:
+                other[kind] = {"launches": n_k, "ms_per_step": ms_k}
+        step_ms = dev_ms / args.steps
+        pb = pass_bytes(prog.graph)
+        hbm_pass = {"bound": "hbm", "kernel": "whole pass (every launch of one step)",
+                    "achieved": pb["bytes"] / (step_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                    "frac": pb["bytes"] / (step_ms * 1e-3) / 1e9 / hbm if hbm else None,
+                    "algorithmic_bytes_per_step": pb, "peak_source": f"hbm_gbs of {src}"}
         gemm = None
-        if headline:
-            ours_gemm = gemm_tops(8192)
-            gemm = {"shape": "8192^3", "tops": ours_gemm, "frac_of_peak": ours_gemm / peak if peak else None,
-                    "cublaslt_tops": cublaslt_int8_tops(8192),
-                    "skinny_mx4096x4096": {str(m): skinny_gemm(m) for m in (1, 16, 128)}}
+        if headline and world == 1 and not args.no_gemm:
+            gemm = gemm_sweep(peak)
+            g8 = gemm["square"]["8192"]
+            gemm.update({"shape": "8192^3", "tops": g8["tops"], "frac_of_peak": g8["frac_of_2x_bf16"],
+                         "cublaslt_tops": g8["cublaslt_tops"], "frac_of_cublaslt": g8["frac_of_cublaslt"],
+                         "frac_of_larger_peak": g8["tops"] / max(peak or 0, g8["cublaslt_tops"] or 0)
+                         if (peak or g8["cublaslt_tops"]) else None})
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             try:
@@ -815,42 +1000,58 @@ def main() -> None:
             except Exception as e:  # the reference package is missing on this machine
                 cpu = {"value": None, "unit": wl["unit"], "cores": os.cpu_count(), "kind": "reference",
                        "sample": f"unavailable: {e}"}
+        parity = None
+        if not args.no_check and args.workload != "transformer":
+            try:
+                parity = parity_check(args.workload, args.batch, outs[-1][exe.g.outputs[0]][:args.batch],
+                                      host_x, args.calib_batch, wl["n_calib"])
+            except ImportError as e:
+                parity = {"unavailable": str(e)}
         in_desc = (f"{host_x.nbytes / 1e6:.0f} MB input batch") if host_x.nbytes > 1e6 else "small input batch"
+        h2d = int(host_x.nbytes)
         result = {
             "metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": wl["config"], "global_batch": args.batch * world,
-                       "batch_per_gpu": args.batch, "parallelism": f"dp{world} (replicas, no collective)",
+                       "batch_per_gpu": args.batch, "parallelism": f"dp{world} (replicas, no collective in "
+                                                                   f"the device-timed step)",
                        "l2": (f"inputs larger than L2 ({in_desc}, activations of several GB per step)")
                        if host_x.nbytes > 126e6 or args.workload == "transformer"
                        else f"working set near L2 ({in_desc})",
                        "calibration": f"{wl['n_calib']} seeded batches of {args.calib_batch}",
                        "compile_s": round(compile_s, 1)},
-            "e2e": {"value": items / e2e_s, "unit": wl["unit"], "h2d_bytes_per_step": int(host_x.nbytes),
-                    "d2h_bytes_per_step": int(out.nbytes),
+            "e2e": {"value": items / e2e_s, "unit": wl["unit"], "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": int(out.nbytes) * world,
+                    "h2d_gb_s_per_gpu": h2d * args.steps / e2e_s / 1e9,
                     "call": "CudaExecutable.run_many: host batch (pinned) copied in and logits read back every "
-                            "step, the next step's copy overlapping this step's kernels"},
+                            "step, the next step's copy overlapping this step's kernels"
+                            + ("; logits gathered to rank 0 on the device every step" if world > 1 else "")},
             "e2e_blocking": {"value": items / e2e_blocking_s, "unit": wl["unit"],
                              "call": "CompiledProgram.run, one step at a time (copy in, kernels, copy out)"},
             "roofline": {"bound": "tensor", "kernel": f"qgemm_sm100_kernel ({'/'.join(kinds)}, {fam_n} launches/step)",
                          "achieved": achieved, "peak": peak, "unit": "TOPS",
                          "frac": (achieved / peak) if peak else None,
                          "traffic": CONV_DRAM_BYTES_PER_PASS if headline else None,
-                         "traffic_unit": "bytes per pass of the 20 conv launches (batch 256)" if headline else None,
+                         "traffic_unit": "DRAM bytes per pass of the 20 conv launches (batch-32 capture x 8)"
+                         if headline else None,
                          "peak_source": f"2 x bf16_tflops of {src} (dense int8 issues at twice the bf16 rate)",
                          "int8_ops_per_step": fam_ops, "ms_per_step": fam_ms},
-            "int8_ops_per_step": q_ops, "int8_tops_step": q_ops / (dev_ms / args.steps * 1e-3) / 1e12,
+            "roofline_hbm_pass": hbm_pass,
+            "int8_ops_per_step": q_ops, "int8_tops_step": q_ops / (step_ms * 1e-3) / 1e12,
             "gpu_launches": int(gpu_launches), "clocks": clocks.summary(),
-            "cpu_baseline": cpu,
+            "cpu_baseline": cpu, "kernels": other,
         }
+        if parity is not None:
+            result["parity"] = parity
         if gemm is not None:
             result["int8_gemm"] = gemm
-        if other:
-            result["kernels"] = other
+        if multi is not None:
+            result["multi_gpu"] = multi
         print(json.dumps(result), flush=True)
     if dist is not None:
         barrier()
+        del gather
         dist.destroy_process_group()
 
 

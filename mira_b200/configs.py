@@ -272,14 +272,22 @@ def random_inputs(graph, seed: int) -> dict:
     return out
 
 
+# per-value calibration peaks of a (workload, seed, calibration batch/count/seed, builder options),
+# in the order of the graph's quantizable ops: programs of one workload compiled at different batch
+# sizes (or for different targets) with the same calibration share them, so their activation scales
+# are identical and every per-image row of their outputs can be compared bit for bit
+_PEAKS: dict = {}
+
+
 def compile_w8a8(name: str, batch: int, target: str, *, seed: int = 0, n_calib: int = 4, calib_seed: int = 100,
                  calib_batch: Optional[int] = None, build_kw: Optional[dict] = None, **kw):
     """Build workload `name` at `batch` and compile it W8A8 for `target` through MIRA's compile_ir.
 
-    Calibration feeds are `n_calib` seeded N(0, 1) batches.  With `calib_batch` (smaller than
-    `batch`), calibration runs on the same network built at `calib_batch` - the reference's own
+    Calibration feeds are `n_calib` seeded N(0, 1) batches.  With `calib_batch` (usually smaller
+    than `batch`), calibration runs on the same network built at `calib_batch` - the reference's own
     _calibrate (quantize.py:73-92) over those feeds - and the resulting per-value peaks are carried
-    over to the large graph op by op, so large batches do not pay hours of host-side calibration."""
+    over to the large graph op by op, so large batches do not pay hours of host-side calibration.
+    Those peaks are computed once per process and calibration setting (`_PEAKS`)."""
     if target in ("cuda", "b200"):
         install()
     else:
@@ -290,7 +298,7 @@ def compile_w8a8(name: str, batch: int, target: str, *, seed: int = 0, n_calib: 
     if build_kw:
         build = (lambda b, _f=build, **k: _f(b, **k, **build_kw))
     g = build(batch, seed=seed)
-    if calib_batch is None or calib_batch == batch:
+    if calib_batch is None:
         cal = [random_inputs(g, calib_seed + i) for i in range(n_calib)]
         return compiler.compile_ir(g, target, quantize="w8a8", calibration=cal, precision=None, **kw)
     small = build(calib_batch, seed=seed)
@@ -303,13 +311,16 @@ def compile_w8a8(name: str, batch: int, target: str, *, seed: int = 0, n_calib: 
     cs, cb = candidates(small), candidates(g)
     if len(cs) != len(cb):
         raise RuntimeError("small and large graphs differ in structure")
-    cal = [random_inputs(small, calib_seed + i) for i in range(n_calib)]
-    peak_small = Q._calibrate(small, cal, {op.inputs[0] for op in cs})
+    key = (name, seed, calib_batch, n_calib, calib_seed, tuple(sorted((build_kw or {}).items())))
+    if key not in _PEAKS:
+        cal = [random_inputs(small, calib_seed + i) for i in range(n_calib)]
+        peak_small = Q._calibrate(small, cal, {op.inputs[0] for op in cs})
+        _PEAKS[key] = [peak_small[op.inputs[0]] for op in cs]
     pos_small = {v: i for i, v in enumerate(small.inputs + [r for op in small.ops for r in op.results])}
     big_values = g.inputs + [r for op in g.ops for r in op.results]
     peaks = {}
-    for s_op, b_op in zip(cs, cb):
-        peaks[b_op.inputs[0]] = peak_small[s_op.inputs[0]]
+    for s_op, b_op, pk in zip(cs, cb, _PEAKS[key]):
+        peaks[b_op.inputs[0]] = pk
         if pos_small.get(s_op.inputs[0]) is not None and big_values[pos_small[s_op.inputs[0]]] is not b_op.inputs[0]:
             raise RuntimeError("calibrated value does not map onto the large graph")
     original = Q._calibrate

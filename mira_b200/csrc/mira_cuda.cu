@@ -678,7 +678,8 @@ static int pick_bn_gemm(int64_t M, int64_t N, int64_t K, int sm_count) {
 
 // Split-K for GEMMs whose output tiles cannot fill the GPU: a single row tile splits its K-blocks
 // over up to sm_count / tiles CTAs per tile (one K-block each at least); taller shapes need 8
-// K-blocks and keep at least 4 per split.
+// K-blocks and keep at least 4 per split.  splits = ceil(num_kb / kb_per), so every split covers at
+// least one K-block: mira_cuda_qgemm_splitk_static relies on that (it never clears its scratch).
 static void splitk_plan(int64_t M, int64_t N, int64_t K, int sm_count, int& splits, int& kb_per) {
   const int bn = pick_bn_gemm(M, N, K, sm_count);
   const int64_t tiles = ((M + QG_BM - 1) / QG_BM) * ((N + bn - 1) / bn);
@@ -1488,6 +1489,9 @@ extern "C" int mira_cuda_qgemm_splitk_static(int64_t M, int64_t N, int64_t K, co
   int32_t* scratch = g_splitk_scratch[dev->device];
   MIRA_CHECK_ARG(splits <= 1 || scratch != nullptr, "static split-K scratch not set up for this device");
   // nothing in the scratch needs clearing: every K range writes its whole M x N slice before the
-  // finishing kernel reads it
+  // finishing kernel reads it, which holds because no range is empty (a plan with an empty range
+  // would leave the previous call's partial sums in its slice)
+  const int64_t num_kb = (K + QG_BK - 1) / QG_BK;
+  MIRA_CHECK_ARG(splits <= 1 || int64_t(splits - 1) * kb_per < num_kb, "split-K plan with an empty K range");
   return qgemm_run(dev, M, N, K, A, lda, B, ldb, dq, epi, splits, kb_per, scratch);
 }

@@ -1628,13 +1628,18 @@ class CudaExecutable:
         self.last_seconds = time.perf_counter() - t0
         return out
 
-    def run_many(self, feeds_list) -> list:
+    def run_many(self, feeds_list, gather=None) -> list:
         """Runs one step per feeds dict, like run() each (same results), but queues step i+1's
         host-to-device input copies on the copy stream while step i's kernels run: the copies go
         to a second device buffer per input, which a device-to-device copy moves into the plan's
         input buffer at the start of the next step.  Outputs are read back through a two-slot
         pinned ring.  Inputs fed as the executable's own pinned arrays (input_array) are copied
-        without a host copy; other arrays are staged through pinned buffers."""
+        without a host copy; other arrays are staged through pinned buffers.
+
+        gather: for batch-sharded runs (mira_b200.shard.DeviceGather): called after each step's
+        kernels are queued, it queues the collective on the device; the step then reads back
+        `gather.outputs` ((value, device buffer, bytes, shape): the gathered global batch on the
+        rank that receives it, nothing on the others) instead of the plan's outputs."""
         dev = self.device
         dev.activate()
         feeds_list = list(feeds_list)
@@ -1642,15 +1647,25 @@ class CudaExecutable:
             return []
         ins = [(v, raw, nb) for v, raw, nb in self.plan.inputs if v not in self.resident_in]
         outs = [(v, buf, nb) for v, buf, nb in self.plan.outputs if v not in self.resident_out]
+        shapes = {v: tuple(v.type.shape) for v, _, _ in outs}
         if self._many is None:
             self._many = {
                 "in2": {v: dev.alloc(nb) for v, _, nb in ins},
                 "stage": {v: [dev.pinned(nb), dev.pinned(nb)] for v, _, nb in ins},
                 "out": {v: [self.pin_out[v], dev.pinned(nb)] for v, _, nb in outs},
                 "ev": {k: [dev.event(), dev.event()] for k in ("h2d", "d2d", "done")},
+                "gout": {},
             }
         m = self._many
         ev = m["ev"]
+        ring = m["out"]
+        if gather is not None:
+            outs = [(v, buf, nb) for v, buf, nb, _ in gather.outputs]
+            shapes = {v: tuple(shape) for v, _, _, shape in gather.outputs}
+            for v, _, nb in outs:
+                if (v, nb) not in m["gout"]:
+                    m["gout"][(v, nb)] = [dev.pinned(nb), dev.pinned(nb)]
+            ring = {v: m["gout"][(v, nb)] for v, _, nb in outs}
         results: list = [None] * len(feeds_list)
 
         def enqueue(i: int) -> None:
@@ -1680,14 +1695,16 @@ class CudaExecutable:
             dev.event_record(ev["d2d"][slot])
             self._launch_all()
             self._runs += 1
+            if gather is not None:
+                gather()
             for v, buf, nb in outs:
-                dev.d2h(m["out"][v][slot], buf, nb)
+                dev.d2h(ring[v][slot], buf, nb)
             dev.event_record(ev["done"][slot])
 
         def collect(i: int) -> None:
             slot = i % 2
             dev.event_sync(ev["done"][slot])
-            r = {v: m["out"][v][slot].view(tuple(v.type.shape), np.float32).copy() for v, _, _ in outs}
+            r = {v: ring[v][slot].view(shapes[v], np.float32).copy() for v, _, _ in outs}
             r.update({v: c.copy() for v, c in self.plan.const_outputs.items()})
             results[i] = r
 

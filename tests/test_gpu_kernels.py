@@ -546,3 +546,28 @@ def test_elementwise_f32(cuda_device, op):
         K.elementwise_f32(op, a.shape, av, out, scalar=0.75, swapped=True)
         want = ref.BINARY[op](np.float32(0.75), a).astype(np.float32)
         assert np.array_equal(ob.download(a.shape, np.float32).view(np.uint32), want.view(np.uint32))
+
+
+def test_qgemm_config2_8192_cubed_exact(cuda_device):
+    """The GEMM sweep's headline shape exactly as bench.py times it: M = N = K = 8192 on config-2
+    operands (A, B uniform int8 in [-127, 127], row and column scales U(1e-3, 1e-2), bias N(0, 1)),
+    which takes the CTA-pair kernel; every output against the oracle's exact restatement
+    (float64 sums of int8 products are exact here)."""
+    from mira_b200 import _lib
+    K, DB = _k()
+    n = 8192
+    rng = np.random.default_rng(1000 + n)
+    a = rng.integers(-127, 128, (n, n), dtype=np.int8)
+    b = rng.integers(-127, 128, (n, n), dtype=np.int8)          # K-major: row j holds column j of B
+    rs = rng.uniform(1e-3, 1e-2, n).astype(np.float32)
+    cs = rng.uniform(1e-3, 1e-2, n).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    Ab, Bb, rb, cb = DB.from_array(a), DB.from_array(b), DB.from_array(rs), DB.from_array(cs)
+    biasb, yb = DB.from_array(K.pad_channels(bias)), DB(n * n * 4)
+    n0 = _lib.launch_count()
+    K.qgemm(n, n, n, Ab, n, Bb, n, K.dequant_rowcol(rb, cb),
+            K.Epi([K.Step("add", "channel", ptr=biasb)], out_f32=yb, ld_f32=n))
+    assert _lib.launch_count() - n0 == 1
+    got = yb.download((n, n), np.float32)
+    _, want = ref.qgemm_rowcol(a, b.T, rs, cs, bias)
+    _same_f32(got, want)
