@@ -374,7 +374,7 @@ def gemm_sweep(peak_tops: float | None) -> dict:
                     "seeded; operand sets cycled (more than twice L2 between reuses)"}
 
 
-PROFILE_CASES = ("gemm8192", "conv_l1", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem",
+PROFILE_CASES = ("gemm8192", "conv_l1", "conv_l1_cp", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem",
                  "decode_step", "attention_prefill", "layernorm_decode", "layernorm_prefill")
 
 
@@ -383,6 +383,7 @@ def profile_case(name: str, reps: int = 3) -> None:
     larger than L2 where the kernel is HBM-bound; a few hundred MB on the device):
       gemm8192      mira_cuda_qgemm 8192^3 on config-2 operands, row/col scales + bias, f32 out
       conv_l1       ResNet-18 layer-1 3x3 conv, batch 256, 56x56x64 -> 64, bias + relu, int8 + f32 out
+      conv_l1_cp    the same conv reading and writing int8 in the chunk-planar layout (MIRA_LAYOUT_CP)
       dwconv_l1     MobileNetV2's first depthwise layer, batch 96, 112x112x32, bias + relu6, int8 out
       attention_q1  a decode step's attention: 64 sequences x 12 heads, 1024 cached rows, d_head 64
       quantize_rows the transformer's activation quantization, 65536 x 768 f32 -> int8
@@ -422,6 +423,21 @@ def profile_case(name: str, reps: int = 3) -> None:
         for _ in range(reps):
             K.qconv2d(n, h, h, cp, x, o, 3, 3, wb, wq.shape[1], (1, 1), (1, 1), (1, 1), K.dequant_channel(*keep), epi,
                       layout=0)
+    elif name == "conv_l1_cp":
+        n, h, c, o = 256, 56, 64, 64
+        xq = rng.integers(-127, 128, (n, h, h, c)).astype(np.int8)
+        x = DB.from_array(K.to_cp(xq))
+        wq, cp = K.conv_weight(rng.integers(-127, 128, (o, c, 3, 3)).astype(np.int8))
+        s64, hi, lo = K.scale_arrays(0.02, rng.uniform(1e-3, 1e-2, o).astype(np.float32))
+        keep = [DB.from_array(a) for a in (s64, hi, lo)]
+        bias = DB.from_array(K.pad_channels(rng.standard_normal(o).astype(np.float32)))
+        y, yq = DB(n * h * h * o * 4), DB(K.cp_bytes(n, h, h, o), zero=True)
+        epi = K.Epi([K.Step("add", "channel", ptr=bias), K.Step("relu")], out_f32=y, ld_f32=o, out_i8=yq, ld_i8=o,
+                    out_scale=0.05, i8_layout=_lib.LAYOUT_CP)
+        wb = DB.from_array(wq)
+        for _ in range(reps):
+            K.qconv2d(n, h, h, cp, x, o, 3, 3, wb, wq.shape[1], (1, 1), (1, 1), (1, 1), K.dequant_channel(*keep), epi,
+                      layout=_lib.LAYOUT_CP)
     elif name == "dwconv_l1":
         n, h, c = 96, 112, 32
         x = DB.from_array(rng.standard_normal((n, h, h, c), dtype=np.float32))

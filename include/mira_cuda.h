@@ -65,6 +65,15 @@ extern "C" {
                                    each, 0 outside the image, s = the horizontal stride of the
                                    convolution that reads it (1, 2 or 4); weights [o, kh * 32] with
                                    k = i * 32 + j * 4 + c (taps j >= kw and channels >= c are 0) */
+#define MIRA_LAYOUT_CP 2        /* chunk-planar, zero-padded: for [n, h, w, cp] with cp % 16 == 0,
+                                   cp / 16 planes of n * (h + 2) * (w + 2) slots of 16 bytes; slot
+                                   (c16, img, y, x) = G + c16 * plane + (img * (h + 2) + y + 1) *
+                                   (w + 2) + x + 1 holds channels [16 c16, 16 c16 + 16) of pixel
+                                   (img, y, x); G = round_up(w + 3, 8) guard slots come first and
+                                   G + 128 after the last plane; every other slot (the padding ring
+                                   of each image, the guards) is 0.  Bytes: mira_cuda_cp_bytes().
+                                   Read by 3x3, stride-1, pad-1 convolutions of cp % 64 == 0 input
+                                   channels, which then fetch each tile's input halo once */
 
 typedef struct mira_epi_step {
   int32_t op;         /* MIRA_EPI_* */
@@ -86,6 +95,8 @@ typedef struct mira_epilogue {
   int8_t* out_i8;     /* may be NULL */
   int64_t ld_i8;      /* bytes, multiple of 16; columns [N, ld_i8) are written as 0 */
   float out_scale;    /* np.float32(x_scale) of the consumer of out_i8 */
+  int32_t i8_layout;  /* MIRA_LAYOUT_NHWC (rows of ld_i8 bytes), or MIRA_LAYOUT_CP for convolutions:
+                         out_i8 in the chunk-planar layout of the conv output [n, oh, ow, ld_i8] */
 } mira_epilogue;
 
 /* Dequant scales.  Per-channel mode (qmatmul / qconv2d): S[n] = f64(x_scale) * f64(w_scale[n]),
@@ -212,8 +223,9 @@ int mira_cuda_qgemm_splitk_static(int64_t M, int64_t N, int64_t K, const int8_t*
  * (_qconv2d_ref, through _conv2d_ref ops.py:265-276 with groups = 1).
  * x: MIRA_LAYOUT_NHWC int8 [n, h, w, cp] (cp 4 or a multiple of 16) with weights int8 [o, ldw],
  * k = (i * kw + j) * cp + c, ldw = round_up(kh*kw*cp, 16); or MIRA_LAYOUT_ROW4 (x_row_entries
- * entries per row) with its weight layout.  The result [n*oh*ow, o] (NHWC) goes through the same
- * epilogue as mira_cuda_qgemm. */
+ * entries per row) with its weight layout; or MIRA_LAYOUT_CP (3x3, stride 1, pad 1, no dilation,
+ * cp % 64 == 0) with the NHWC weight layout.  The result [n*oh*ow, o] (NHWC) goes through the same
+ * epilogue as mira_cuda_qgemm; its int8 output may be MIRA_LAYOUT_CP (epi->i8_layout). */
 int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x,
                       int64_t x_layout, int64_t x_row_entries,
                       int64_t o, int64_t kh, int64_t kw, const int8_t* wq, int64_t ldw,
@@ -244,6 +256,14 @@ int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, int64_t n, 
                              int64_t w, int64_t c, int64_t ldc_in, int64_t size, int64_t stride,
                              int64_t pad, float pad_value, float* out_f32, int64_t ldc_out_f32,
                              int8_t* out_i8, int64_t ldc_out_i8, float out_scale);
+/* The same with the int8 output's layout chosen: MIRA_LAYOUT_NHWC as above, or MIRA_LAYOUT_CP
+ * (f32 input only; ldc_out_i8 = the padded channel count, a multiple of 16). */
+int mira_cuda_maxpool2d_nhwc_ex(const float* x_f32, const int8_t* x_i8, int64_t n, int64_t h,
+                                int64_t w, int64_t c, int64_t ldc_in, int64_t size, int64_t stride,
+                                int64_t pad, float pad_value, float* out_f32, int64_t ldc_out_f32,
+                                int8_t* out_i8, int64_t ldc_out_i8, float out_scale, int64_t i8_layout);
+/* Bytes of an int8 activation [n, h, w, cp] in MIRA_LAYOUT_CP (0 for bad sizes). */
+int64_t mira_cuda_cp_bytes(int64_t n, int64_t h, int64_t w, int64_t cp);
 
 /* Mean over H and W of NHWC f32 (reference ops.py:318-343 reduce_mean over axes (2, 3)), summed
  * in NumPy's pairwise order so the f32 result is bit-identical; optional f32 and int8 outputs

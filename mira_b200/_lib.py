@@ -18,7 +18,7 @@ EPI_RELU, EPI_GELU, EPI_SIGMOID, EPI_TANH = 1, 2, 3, 4
 EPI_ADD, EPI_SUB, EPI_MUL, EPI_DIV, EPI_MAXIMUM, EPI_MINIMUM = 16, 17, 18, 19, 20, 21
 OPND_NONE, OPND_SCALAR, OPND_CHANNEL, OPND_FULL, OPND_ROW = 0, 1, 2, 3, 4
 OPND_VIEW = 5
-LAYOUT_NHWC, LAYOUT_ROW4 = 0, 1
+LAYOUT_NHWC, LAYOUT_ROW4, LAYOUT_CP = 0, 1, 2
 EPI_MAX_STEPS = 8
 ROW_MAX = 8192
 
@@ -34,7 +34,8 @@ class EpiStep(C.Structure):
 
 class Epilogue(C.Structure):
     _fields_ = [("n_steps", C.c_int32), ("steps", EpiStep * EPI_MAX_STEPS), ("out_f32", C.c_void_p),
-                ("ld_f32", C.c_int64), ("out_i8", C.c_void_p), ("ld_i8", C.c_int64), ("out_scale", C.c_float)]
+                ("ld_f32", C.c_int64), ("out_i8", C.c_void_p), ("ld_i8", C.c_int64), ("out_scale", C.c_float),
+                ("i8_layout", C.c_int32)]
 
 
 class Dequant(C.Structure):
@@ -114,6 +115,9 @@ SIGNATURES: dict[str, tuple] = {
                                          C.POINTER(Epilogue)]),
     "mira_cuda_maxpool2d_nhwc": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _i64,
                                         _vp, _i64, _f32]),
+    "mira_cuda_maxpool2d_nhwc_ex": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp,
+                                           _i64, _vp, _i64, _f32, _i64]),
+    "mira_cuda_cp_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "mira_cuda_mean_hw_nhwc": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _f32]),
     "mira_cuda_dwconv2d_nhwc": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, C.POINTER(Epilogue)]),

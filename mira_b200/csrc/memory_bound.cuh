@@ -142,14 +142,28 @@ __global__ void quantize_nchw_row4_kernel(const float* __restrict__ x, int n, in
 
 // ---------------------------------------------------------------- K5: max pooling (NHWC)
 
+// Where an output pixel's int8 channels go: rows of `ld` bytes (cp == 0), or the chunk-planar,
+// zero-padded layout (MIRA_LAYOUT_CP) of an [n, oh, ow, c] activation, `chunk` bytes apart per
+// 16 channels.
+struct I8Dst {
+  int8_t* base;
+  int64_t ld;
+  int cp, guard;
+  int64_t chunk;
+  __device__ __forceinline__ int8_t* pixel(int img, int oy, int ox, int oh, int ow, int64_t pix) const {
+    return base + (cp ? (guard + (static_cast<int64_t>(img) * (oh + 2) + oy + 1) * (ow + 2) + ox + 1) * 16 : pix * ld);
+  }
+  // byte offset of channel ch (a multiple of 4 stays inside one 16-byte chunk with its 3 followers)
+  __device__ __forceinline__ int64_t channel(int ch) const { return static_cast<int64_t>(ch >> 4) * chunk + (ch & 15); }
+};
+
 // f32 input.  blockIdx.y: output rows (n * oh, strided over gridDim.y); threadIdx.x: groups of 4
 // channels (strided over blockDim.x), threadIdx.y + blockIdx.x * blockDim.y: the output column.
 // Padding pixels take `pad_value` (the reference pads with -inf before pooling).  Writes f32
 // and/or the quantized int8 value.
 __global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, int w, int c, int64_t ldc,
                                    int size, int stride, int pad, float pad_value, int oh, int ow,
-                                   float* __restrict__ out, int64_t ldo, int8_t* __restrict__ out_i8,
-                                   int64_t ldo_i8, QuantScale q) {
+                                   float* __restrict__ out, int64_t ldo, I8Dst o8, QuantScale q) {
   const int c4 = (c + 3) / 4;
   const int ox = blockIdx.x * blockDim.y + threadIdx.y;
   if (ox >= ow) return;
@@ -194,11 +208,12 @@ __global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, in
             if (cg * 4 + e < c) dst[e] = mx[e];
         }
       }
-      if (out_i8 != nullptr) {
+      if (o8.base != nullptr) {
         uint32_t b[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) b[e] = (cg * 4 + e < c) ? quant_byte(mx[e], q) : 0u;
-        *reinterpret_cast<uint32_t*>(out_i8 + pix * ldo_i8 + cg * 4) = pack4_i8(b[0], b[1], b[2], b[3]);
+        *reinterpret_cast<uint32_t*>(o8.pixel(img, oy, ox, oh, ow, pix) + o8.channel(cg * 4)) =
+            pack4_i8(b[0], b[1], b[2], b[3]);
       }
     }
   }
@@ -212,7 +227,7 @@ __global__ void maxpool_f32_kernel(const float* __restrict__ x, int n, int h, in
 // maxima cannot change a result.
 __global__ void maxpool3_f32_kernel(const float* __restrict__ x, int n, int h, int w, int c, int64_t ldc, int stride,
                                     int pad, float pad_value, int oh, int ow, float* __restrict__ out, int64_t ldo,
-                                    int8_t* __restrict__ out_i8, int64_t ldo_i8, QuantScale q) {
+                                    I8Dst o8, QuantScale q) {
   const int c4 = c >> 2;
   const int ox = blockIdx.x * blockDim.y + threadIdx.y;
   if (ox >= ow) return;
@@ -227,7 +242,7 @@ __global__ void maxpool3_f32_kernel(const float* __restrict__ x, int n, int h, i
     const float* r0 = x + (int64_t(img) * h + iy0) * w * ldc + int64_t(ix0) * ldc;   // window's top-left pixel
     const int64_t rs = int64_t(w) * ldc;
     float* q0 = out != nullptr ? out + (orow * ow + ox) * ldo : nullptr;
-    int8_t* q8 = out_i8 != nullptr ? out_i8 + (orow * ow + ox) * ldo_i8 : nullptr;
+    int8_t* q8 = o8.base != nullptr ? o8.pixel(img, oy, ox, oh, ow, orow * ow + ox) : nullptr;
     for (int cg = threadIdx.x; cg < c4; cg += blockDim.x) {
       float4 t[9];
       if (inside) {
@@ -259,7 +274,7 @@ __global__ void maxpool3_f32_kernel(const float* __restrict__ x, int n, int h, i
       if (q8 != nullptr) {
         uint32_t b[4];
         requant_x2<4>(mx, q.s, q.rcp, q.c127, b);
-        *reinterpret_cast<uint32_t*>(q8 + 4 * cg) = pack4_i8(b[0], b[1], b[2], b[3]);
+        *reinterpret_cast<uint32_t*>(q8 + o8.channel(4 * cg)) = pack4_i8(b[0], b[1], b[2], b[3]);
       }
     }
   }

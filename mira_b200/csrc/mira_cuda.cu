@@ -195,7 +195,8 @@ static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes
 
 // ---------------------------------------------------------------- qgemm dispatch
 
-template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK, int RKB = 0>
+template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK, int RKB = 0,
+          int PATCH = 0>
 static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, const QgParams& p_in) {
   QgParams p = p_in;
   if (p.k_splits < 1) {   // no split: one K range per output tile
@@ -204,8 +205,8 @@ static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUte
   }
   if (RKB > 0 && (p.n_tiles != 1 || p.k_splits != 1 || p.num_kb > RKB))
     return set_error(MIRA_CUDA_EINVAL, "resident-weight kernel used for a shape it does not cover");
-  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>;
-  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL, BK, RKB>;
+  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PATCH>;
+  auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL, BK, RKB, PATCH>;
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[dev->device]) {
     MIRA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM)),
@@ -313,6 +314,58 @@ static int launch_qgemm_im2col(DeviceState* dev, const CUtensorMap& tmA, const C
   }
 }
 
+// 3x3 stride-1 convolutions over the chunk-planar layout (QG_A_PATCH): per tile one bulk copy per
+// 16-channel plane brings the whole input halo (w + 3 slots either side of the tile's 128 output
+// slots) into one of two shared-memory buffers, and the nine taps are views of it shifted by whole
+// slots; weights stream through the ring, or stay resident for a 64 x 64 conv.  Halo buffer sizes
+// per input channel count (the largest image width each serves): 64 -> 16 KB (w <= 56),
+// 128 -> 24 KB (w <= 28), 256 -> 41 KB (w <= 14), 512 -> 74 KB (w <= 7).
+static int patch_cap(int cp) {
+  switch (cp) {
+    case 64: return 16384;
+    case 128: return 24576;
+    case 256: return 41984;
+    case 512: return 75776;
+    default: return 0;
+  }
+}
+
+static int launch_qgemm_patch(DeviceState* dev, const int8_t* wq, int64_t ldw, int64_t o, QgParams& p) {
+  const int cp = p.g.cp;
+  const int64_t halo = int64_t(p.g.patch_slots) * cp;
+  MIRA_CHECK_ARG(patch_cap(cp) > 0 && halo <= patch_cap(cp),
+                 "no chunk-planar conv kernel for this channel count and image width");
+  const int bk = cp == 64 ? 64 : 128;
+  int bn = o <= 64 ? 64 : (o <= 128 ? 128 : 256);
+  if (cp >= 256 && bn == 64) bn = 128;
+  if (cp == 512) bn = 128;
+  p.num_kb = 9 * cp / bk;
+  p.m_tiles = int((p.M + QG_BM - 1) / QG_BM);
+  p.n_tiles = int((o + bn - 1) / bn);
+  CUtensorMap tmA, tmB;
+  std::memset(&tmA, 0, sizeof(tmA));
+  int rc = encode_2d_i8_sw(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), uint32_t(bk), uint32_t(bn),
+                           bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != MIRA_CUDA_OK) return rc;
+  switch (cp) {
+    case 64:
+      if (bn == 64 && p.n_tiles == 1)
+        return launch_qgemm_cfg<64, 1, QG_A_PATCH, false, 4, false, 64, 9, 16384>(dev, tmA, tmB, p);
+      if (bn == 64) return launch_qgemm_cfg<64, 8, QG_A_PATCH, false, 4, false, 64, 0, 16384>(dev, tmA, tmB, p);
+      if (bn == 128) return launch_qgemm_cfg<128, 8, QG_A_PATCH, false, 4, false, 64, 0, 16384>(dev, tmA, tmB, p);
+      return launch_qgemm_cfg<256, 6, QG_A_PATCH, false, 4, false, 64, 0, 16384>(dev, tmA, tmB, p);
+    case 128:
+      if (bn == 64) return launch_qgemm_cfg<64, 8, QG_A_PATCH, false, 4, false, 128, 0, 24576>(dev, tmA, tmB, p);
+      if (bn == 128) return launch_qgemm_cfg<128, 6, QG_A_PATCH, false, 4, false, 128, 0, 24576>(dev, tmA, tmB, p);
+      return launch_qgemm_cfg<256, 3, QG_A_PATCH, false, 4, false, 128, 0, 24576>(dev, tmA, tmB, p);
+    case 256:
+      if (bn == 128) return launch_qgemm_cfg<128, 5, QG_A_PATCH, false, 4, false, 128, 0, 41984>(dev, tmA, tmB, p);
+      return launch_qgemm_cfg<256, 3, QG_A_PATCH, false, 2, false, 128, 0, 41984>(dev, tmA, tmB, p);
+    default:
+      return launch_qgemm_cfg<128, 3, QG_A_PATCH, false, 2, false, 128, 0, 75776>(dev, tmA, tmB, p);
+  }
+}
+
 static int fill_epilogue(QgParams& p, const mira_dequant* dq, const mira_epilogue* epi) {
   MIRA_CHECK_ARG(dq != nullptr && epi != nullptr, "dequant and epilogue descriptors are required");
   MIRA_CHECK_ARG(epi->n_steps >= 0 && epi->n_steps <= MIRA_EPI_MAX_STEPS, "too many epilogue steps");
@@ -356,12 +409,31 @@ static int fill_epilogue(QgParams& p, const mira_dequant* dq, const mira_epilogu
                    "int8 output needs a 16-byte aligned base and a row stride multiple of 16");
     MIRA_CHECK_ARG(epi->out_scale > 0.0f && std::isfinite(epi->out_scale), "requant scale must be positive");
   }
+  MIRA_CHECK_ARG(epi->i8_layout == MIRA_LAYOUT_NHWC || epi->i8_layout == MIRA_LAYOUT_CP, "unknown int8 output layout");
+  p.i8_cp = 0;
+  p.i8_guard = 0;
+  p.i8_chunk = 16;   // rows layout: the next 16 channels are the next 16 bytes (set_i8_layout for CP)
   const QuantScale q = make_qscale(epi->out_i8 != nullptr ? epi->out_scale : 1.0f);
   p.q_scale = q.s;
   p.q_rcp = q.rcp;
   p.q_lim = q.lim;
   p.q_c127 = 127.0f * q.s;
   p.err = device_err_ptr();
+  return MIRA_CUDA_OK;
+}
+
+// Guard slots in front of the chunk-planar layout's planes (MIRA_LAYOUT_CP) for image width w: a
+// tile's halo starts w + 3 slots before its first output slot.
+static int64_t cp_guard(int64_t w) { return round_up(w + 3, 8); }
+
+// The int8 output of a convolution with output [n, oh, ow] in the chunk-planar layout when the
+// epilogue asks for it.
+static int set_i8_layout(QgParams& p, const mira_epilogue* epi, int64_t n, int64_t oh, int64_t ow) {
+  if (epi->out_i8 == nullptr || epi->i8_layout != MIRA_LAYOUT_CP) return MIRA_CUDA_OK;
+  MIRA_CHECK_ARG(n * (oh + 2) * (ow + 2) * 16 < (int64_t(1) << 40), "chunk-planar output too large");
+  p.i8_cp = 1;
+  p.i8_guard = int(cp_guard(ow));
+  p.i8_chunk = n * (oh + 2) * (ow + 2) * 16;
   return MIRA_CUDA_OK;
 }
 
@@ -719,6 +791,8 @@ static int qgemm_run(DeviceState* dev, int64_t M, int64_t N, int64_t K, const in
   std::memset(&p, 0, sizeof(p));
   const int rc = fill_epilogue(p, dq, epi);
   if (rc != MIRA_CUDA_OK) return rc;
+  MIRA_CHECK_ARG(epi->out_i8 == nullptr || epi->i8_layout == MIRA_LAYOUT_NHWC,
+                 "the chunk-planar int8 output is for convolutions");
   const int bn = pick_bn_gemm(M, N, K, dev->sm_count);
   p.M = int(M);
   p.N = int(N);
@@ -817,7 +891,12 @@ static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t*
   oh = (h + 2 * pad_h - dil_h * (kh - 1) - 1) / stride_h + 1;
   ow = (w + 2 * pad_w - dil_w * (kw - 1) - 1) / stride_w + 1;
   MIRA_CHECK_ARG(oh > 0 && ow > 0, "kernel larger than the padded input");
-  MIRA_CHECK_ARG(x_layout == MIRA_LAYOUT_NHWC || x_layout == MIRA_LAYOUT_ROW4, "unknown input layout");
+  MIRA_CHECK_ARG(x_layout == MIRA_LAYOUT_NHWC || x_layout == MIRA_LAYOUT_ROW4 || x_layout == MIRA_LAYOUT_CP,
+                 "unknown input layout");
+  if (x_layout == MIRA_LAYOUT_CP)
+    MIRA_CHECK_ARG(cp % 64 == 0 && kh == 3 && kw == 3 && stride_h == 1 && stride_w == 1 && pad_h == 1 && pad_w == 1 &&
+                       dil_h == 1 && dil_w == 1,
+                   "the chunk-planar layout feeds 3x3, stride-1, pad-1 convolutions of 64k input channels");
   if (x_layout == MIRA_LAYOUT_ROW4) {
     MIRA_CHECK_ARG(cp == 4 && kw <= 8 && dil_h == 1 && dil_w == 1,
                    "the row-expanded layout serves 4-channel inputs, kernel width <= 8, no dilation");
@@ -839,8 +918,17 @@ static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t*
   p.num_kb = int((K + QG_BK - 1) / QG_BK);
   p.A = x;
   p.g = QgConv{int(n), int(h), int(w), int(cp), int(oh), int(ow), int(kh), int(kw), int(stride_h), int(stride_w),
-               int(pad_h), int(pad_w), int(dil_h), int(dil_w), int(x_row_entries)};
-  return MIRA_CUDA_OK;
+               int(pad_h), int(pad_w), int(dil_h), int(dil_w), int(x_row_entries), 0, 0, 0};
+  if (x_layout == MIRA_LAYOUT_CP) {
+    // GEMM rows = every slot of the zero-padded output plane (same geometry as the input)
+    const int64_t plane = n * (h + 2) * (w + 2);
+    MIRA_CHECK_ARG(plane < (int64_t(1) << 31) - 256, "conv too large for the chunk-planar layout");
+    p.M = int(plane);
+    p.g.guard = int(cp_guard(w));
+    p.g.patch_slots = int(QG_BM + 2 * (w + 3));
+    p.g.plane = plane;
+  }
+  return set_i8_layout(p, epi, n, oh, ow);
 }
 
 extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x, int64_t x_layout,
@@ -857,9 +945,10 @@ extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, co
   const int bn = pick_bn(o);
   p.m_tiles = int((p.M + QG_BM - 1) / QG_BM);
   p.n_tiles = int((o + bn - 1) / bn);
+  if (x_layout == MIRA_LAYOUT_CP) return launch_qgemm_patch(dev, wq, ldw, o, p);
   // a 1x1 stride-1 convolution without padding is a GEMM over the NHWC activation matrix [n*h*w, cp]
   if (x_layout == MIRA_LAYOUT_NHWC && kh == 1 && kw == 1 && stride_h == 1 && stride_w == 1 && pad_h == 0 &&
-      pad_w == 0 && cp % 16 == 0)
+      pad_w == 0 && cp % 16 == 0 && (epi->out_i8 == nullptr || epi->i8_layout == MIRA_LAYOUT_NHWC))
     return qgemm_run(dev, p.M, o, cp, x, cp, wq, ldw, dq, epi, 1, 0, nullptr);
   CUtensorMap tmA, tmB;
   std::memset(&tmA, 0, sizeof(tmA));
@@ -899,6 +988,8 @@ extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_
                       dil_w, dq, epi, p, oh, ow);
   if (rc != MIRA_CUDA_OK) return rc;
   MIRA_CHECK_ARG(o <= 64, "fused pooling supports convolutions with at most 64 output channels");
+  MIRA_CHECK_ARG(x_layout != MIRA_LAYOUT_CP && (epi->out_i8 == nullptr || epi->i8_layout == MIRA_LAYOUT_NHWC),
+                 "fused pooling reads and writes the NHWC / row-expanded layouts");
   MIRA_CHECK_ARG(pool_size > 0 && pool_stride > 0 && pool_pad >= 0 && pool_pad < pool_size, "bad pool geometry");
   // the kernel pools the int32 accumulators and applies the epilogue to the pooled values, which
   // equals pooling the epilogue's outputs when every step is monotone non-decreasing in its input
@@ -949,7 +1040,22 @@ extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, 
                                         int64_t c, int64_t ldc_in, int64_t size, int64_t stride, int64_t pad,
                                         float pad_value, float* out_f32, int64_t ldc_out_f32, int8_t* out_i8,
                                         int64_t ldc_out_i8, float out_scale) {
+  return mira_cuda_maxpool2d_nhwc_ex(x_f32, x_i8, n, h, w, c, ldc_in, size, stride, pad, pad_value, out_f32,
+                                     ldc_out_f32, out_i8, ldc_out_i8, out_scale, MIRA_LAYOUT_NHWC);
+}
+
+extern "C" int64_t mira_cuda_cp_bytes(int64_t n, int64_t h, int64_t w, int64_t cp) {
+  if (n < 0 || h <= 0 || w <= 0 || cp <= 0 || cp % 16 != 0) return 0;
+  return (2 * mira::cp_guard(w) + QG_BM + (cp / 16) * n * (h + 2) * (w + 2)) * 16;
+}
+
+extern "C" int mira_cuda_maxpool2d_nhwc_ex(const float* x_f32, const int8_t* x_i8, int64_t n, int64_t h, int64_t w,
+                                           int64_t c, int64_t ldc_in, int64_t size, int64_t stride, int64_t pad,
+                                           float pad_value, float* out_f32, int64_t ldc_out_f32, int8_t* out_i8,
+                                           int64_t ldc_out_i8, float out_scale, int64_t i8_layout) {
   MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(i8_layout == MIRA_LAYOUT_NHWC || (i8_layout == MIRA_LAYOUT_CP && x_i8 == nullptr && ldc_out_i8 % 16 == 0),
+                 "chunk-planar int8 output: f32 input, padded channel count a multiple of 16");
   MIRA_CHECK_ARG(n >= 0 && h > 0 && w > 0 && c > 0 && size > 0 && stride > 0 && pad >= 0 && pad < size,
                  "bad maxpool geometry");
   const int64_t oh = (h + 2 * pad - size) / stride + 1, ow = (w + 2 * pad - size) / stride + 1;
@@ -969,6 +1075,12 @@ extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, 
   }
   MIRA_CHECK_ARG(x_f32 != nullptr && (out_f32 != nullptr || out_i8 != nullptr), "maxpool needs an input and an output");
   if (out_i8 != nullptr) MIRA_CHECK_ARG(ldc_out_i8 % 4 == 0 && ldc_out_i8 >= c && out_scale > 0.0f, "bad int8 output");
+  I8Dst o8{out_i8, ldc_out_i8, 0, 0, 16};
+  if (out_i8 != nullptr && i8_layout == MIRA_LAYOUT_CP) {
+    o8.cp = 1;
+    o8.guard = int(cp_guard(ow));
+    o8.chunk = n * (oh + 2) * (ow + 2) * 16;
+  }
   const auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   if (size == 3 && c % 4 == 0 && ldc_in % 4 == 0 && a16(x_f32) &&
       (out_f32 == nullptr || (ldc_out_f32 % 4 == 0 && a16(out_f32))) &&
@@ -980,7 +1092,7 @@ extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, 
     const dim3 grid(unsigned((ow + ty - 1) / ty), unsigned(orows < 65535 ? orows : 65535));
     maxpool3_f32_kernel<<<grid, dim3(tx, ty), 0, dev->stream>>>(
         x_f32, int(n), int(h), int(w), int(c), ldc_in, int(stride), int(pad), pad_value, int(oh), int(ow), out_f32,
-        ldc_out_f32, out_i8, ldc_out_i8, make_qscale(out_i8 != nullptr ? out_scale : 1.0f));
+        ldc_out_f32, o8, make_qscale(out_i8 != nullptr ? out_scale : 1.0f));
     return after_launch("maxpool3_f32_kernel");
   }
   // threads: x = groups of 4 channels (at most 64), y = output columns; blocks: columns x rows
@@ -991,7 +1103,7 @@ extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, 
   const dim3 grid(unsigned((ow + ty - 1) / ty), unsigned(orows < 65535 ? orows : 65535));
   maxpool_f32_kernel<<<grid, dim3(tx, ty), 0, dev->stream>>>(
       x_f32, int(n), int(h), int(w), int(c), ldc_in, int(size), int(stride), int(pad), pad_value, int(oh), int(ow),
-      out_f32, ldc_out_f32, out_i8, ldc_out_i8, make_qscale(out_i8 != nullptr ? out_scale : 1.0f));
+      out_f32, ldc_out_f32, o8, make_qscale(out_i8 != nullptr ? out_scale : 1.0f));
   return after_launch("maxpool_f32_kernel");
 }
 

@@ -109,6 +109,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Contiguous bulk copy global -> this CTA's shared memory (no tensor map, no multicast): `bytes`
+// (a multiple of 16) from a 16-byte aligned source, completion counted in bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ------------------------------------------------------------------ cp.async (im2col gathers)
 
 // 16-byte copy; src_bytes == 0 writes 16 zero bytes without reading src.
@@ -223,6 +233,18 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw64(uint32_t saddr) {
   d |= static_cast<uint64_t>(1) << 46;                 // version        [46, 48)
   d |= static_cast<uint64_t>(4) << 61;                 // SWIZZLE_64B    [61, 64)
   return d;
+}
+
+// K-major operand without swizzle: core matrices of 8 rows x 16 bytes stored contiguously (rows
+// 16 bytes apart), the next 16 bytes of K `lbo` bytes further, the next 8 rows `sbo` bytes further.
+// Any 16-byte aligned start address is valid, so a tile can begin at any row of a larger array.
+__device__ __forceinline__ uint64_t smem_desc_k_none(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);          // start address  [0, 14)
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;      // LBO (K step)   [16, 30)
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;      // SBO (8 rows)   [32, 46)
+  d |= static_cast<uint64_t>(1) << 46;                        // version        [46, 48)
+  return d;                                                   // SWIZZLE_NONE   [61, 64) = 0
 }
 
 // ------------------------------------------------------------------ CTA pairs (cta_group::2)

@@ -192,13 +192,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Qg2Cfg<BN, STAGES, G
       const int n0 = t_n * BN;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       const int m_warp0 = t_m * 2 * QG_BM + int(rank) * QG_BM + quarter * 32;
-      const int m = m_warp0 + lane;
-      const bool row_ok = m < p.M;
+      const QgRow row = qg_row<QG_A_TMA>(p, m_warp0 + lane);
 #pragma unroll 1
       for (int c = group; c < BN / Cfg::CW; c += G) {
         const int nb = n0 + c * Cfg::CW;
         if (nb >= p.N) break;  // warp-uniform
-        qg_epilogue_chunk<ROWCOL, Cfg::STAGE_PITCH>(p, tbase + c * Cfg::CW, m, row_ok, m_warp0, nb, stage, lane,
+        qg_epilogue_chunk<ROWCOL, Cfg::STAGE_PITCH>(p, tbase + c * Cfg::CW, row, m_warp0, nb, stage, lane,
                                                     p.out_f32);
       }
       tc_fence_before();

@@ -33,17 +33,25 @@ constexpr int QG_BK = 128;               // K bytes per stage = one 128-byte swi
 constexpr int QG_UMMA_K = 32;            // K per tcgen05.mma kind::i8
 constexpr uint64_t QG_TIMEOUT_NS = 2000000000ull;
 
-enum QgAMode { QG_A_TMA = 0, QG_A_GATHER16 = 1, QG_A_GATHER4 = 2, QG_A_ROW4 = 3, QG_A_IM2COL = 4 };
+enum QgAMode { QG_A_TMA = 0, QG_A_GATHER16 = 1, QG_A_GATHER4 = 2, QG_A_ROW4 = 3, QG_A_IM2COL = 4, QG_A_PATCH = 5 };
 
 // A operand comes from TMA (2-D tiles of a row-major matrix, or im2col tiles of an NHWC tensor)
-// rather than from the cp.async gather warps.
+// into the stages of the operand ring, rather than from the cp.async gather warps.
 constexpr bool qg_a_by_tma(int amode) { return amode == QG_A_TMA || amode == QG_A_IM2COL; }
+// A operand is a tile's whole input halo, bulk-copied once per tile from the chunk-planar layout
+// (3x3 stride-1 convolutions): no gather warps, the ring stages carry weights only.
+constexpr bool qg_a_patch(int amode) { return amode == QG_A_PATCH; }
+constexpr bool qg_a_async(int amode) { return qg_a_by_tma(amode) || qg_a_patch(amode); }
 
 struct QgConv {
   int n, h, w, cp;      // input NHWC (cp = padded channels)
   int oh, ow;
   int kh, kw, sh, sw, ph, pw, dh, dw;
   int row_entries;      // QG_A_ROW4: 16-byte entries per image row (entry e = pixels sw*e - pw .. sw*e - pw + 3)
+  // QG_A_PATCH (chunk-planar input, 3x3 stride 1 pad 1): guard slots, slots per chunk plane, and
+  // the slots of one tile's halo (128 + 2 (w + 3)); GEMM rows are the padded output slots
+  int guard, patch_slots;
+  int64_t plane;
 };
 
 struct QgParams {
@@ -71,6 +79,10 @@ struct QgParams {
   int64_t ld_i8;
   float q_scale, q_rcp, q_lim;   // requant divisor, RN32(1/divisor), 256 * divisor
   float q_c127;                  // RN32(127 * divisor): the clamp of the packed requantization
+  // int8 output layout: rows of ld_i8 bytes (i8_cp = 0, i8_chunk = 16), or chunk-planar for a
+  // convolution's output (i8_cp = 1: slot guard + c16 * plane + padded pixel, i8_chunk = plane * 16)
+  int i8_cp, i8_guard;
+  int64_t i8_chunk;
   int* err;
   // fused max pooling (POOL kernels only): window pool_p, stride pool_s, padding pool_pad holding
   // pool_pad_value; a tile is pool_t x pool_t pooled pixels whose conv inputs form a
@@ -96,15 +108,17 @@ __device__ __forceinline__ void pool_row_pixel(const QgParams& p, int t_m, int r
 
 // RKB > 0: the whole B operand (at most RKB K-blocks) stays in shared memory for the CTA's lifetime
 // (one output column tile, loaded once); the stages then carry A only.
-template <int BN, int STAGES, int AMODE, int G, bool POOL = false, int BK = QG_BK, int RKB = 0>
+// PATCH > 0 (QG_A_PATCH): bytes of one of the two halo buffers that replace the A stages.
+template <int BN, int STAGES, int AMODE, int G, bool POOL = false, int BK = QG_BK, int RKB = 0, int PATCH = 0>
 struct QgCfg {
   static constexpr int A_BYTES = QG_BM * BK;
+  static constexpr int A_REGION = qg_a_patch(AMODE) ? 2 * PATCH : STAGES * A_BYTES;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int CW = 16;                       // epilogue chunk width (columns)
   static constexpr int EPI_WARP0 = 2;
   static constexpr int EPI_WARPS = 4 * G;
   static constexpr int GATHER_WARP0 = EPI_WARP0 + EPI_WARPS;
-  static constexpr int THREADS = 32 * (GATHER_WARP0 + (qg_a_by_tma(AMODE) ? 0 : 4));
+  static constexpr int THREADS = 32 * (GATHER_WARP0 + (qg_a_async(AMODE) ? 0 : 4));
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   // per epilogue warp: a 32-row x 16-column f32 staging block (row pitch 20 floats)
@@ -114,14 +128,16 @@ struct QgCfg {
   static constexpr int POOL_ROWS = 96;
   static constexpr int STAGING_BYTES = POOL ? 2 * POOL_ROWS * POOL_PITCH * 4 : EPI_WARPS * 32 * STAGE_PITCH * 4;
   static constexpr int B_REGION = RKB > 0 ? RKB * B_BYTES : STAGES * B_BYTES;
-  // the barrier region after the staging: 2 * STAGES + 8 mbarriers, the TMEM address, the abort flag
-  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 8) + 8 <= 256 ? 256 : 512;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * A_BYTES + B_REGION + STAGING_BYTES + BAR_BYTES;
+  // the barrier region after the staging: 2 * STAGES + 12 mbarriers, the TMEM address, the abort flag
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 12) + 8 <= 256 ? 256 : 512;
+  static constexpr size_t SMEM = 1024 + size_t(A_REGION) + B_REGION + STAGING_BYTES + BAR_BYTES;
   static_assert(!POOL || (AMODE != 0 && BN == 64), "fused pooling: convolutions with at most 64 channels");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(8 * (2 * STAGES + 8) + 8 <= BAR_BYTES, "barrier region");
-  static_assert(BK == 128 || (BK == 64 && AMODE == QG_A_IM2COL), "64-byte K-blocks: im2col convolutions only");
+  static_assert(8 * (2 * STAGES + 12) + 8 <= BAR_BYTES, "barrier region");
+  static_assert(BK == 128 || (BK == 64 && (AMODE == QG_A_IM2COL || AMODE == QG_A_PATCH)),
+                "64-byte K-blocks: convolutions with 64-channel inputs only");
+  static_assert(qg_a_patch(AMODE) == (PATCH > 0) && PATCH % 1024 == 0, "halo buffers: PATCH mode only");
 };
 
 // Bounded wait that ignores the abort flag: used only to let in-flight copies land before exit.
@@ -144,6 +160,39 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 }
 
 // ---------------------------------------------------------------- epilogue (one 16-column chunk)
+
+// Where GEMM row m of a tile goes: the f32 row (output pixel; operands with rows are read there
+// too), the byte offset of its int8 output row, and whether the row exists.  Plain GEMMs and the
+// convolutions other than PATCH have row m = pixel m; PATCH convolutions compute every slot of the
+// zero-padded output plane, and the padding slots are not written.
+struct QgRow {
+  int64_t pix;
+  int64_t i8;
+  bool ok;
+};
+
+template <int AMODE>
+__device__ __forceinline__ QgRow qg_row(const QgParams& p, int m) {
+  QgRow r;
+  if (AMODE == QG_A_PATCH) {
+    const int pw = p.g.ow + 2, pimg = (p.g.oh + 2) * pw;
+    const int img = m / pimg, rem = m - img * pimg, yy = rem / pw, xx = rem - yy * pw;
+    r.ok = m < p.M && yy >= 1 && yy <= p.g.oh && xx >= 1 && xx <= p.g.ow;
+    r.pix = r.ok ? (static_cast<int64_t>(img) * p.g.oh + yy - 1) * p.g.ow + xx - 1 : 0;
+    r.i8 = p.i8_cp ? (static_cast<int64_t>(p.i8_guard) + m) * 16 : r.pix * p.ld_i8;
+  } else {
+    r.ok = m < p.M;
+    r.pix = m;
+    r.i8 = static_cast<int64_t>(m) * p.ld_i8;
+    if (p.i8_cp && r.ok) {
+      const int hw = p.g.oh * p.g.ow;
+      const int img = m / hw, rem = m - img * hw, y = rem / p.g.ow, x = rem - y * p.g.ow;
+      r.i8 = (static_cast<int64_t>(p.i8_guard) +
+              (static_cast<int64_t>(img) * (p.g.oh + 2) + y + 1) * (p.g.ow + 2) + x + 1) * 16;
+    }
+  }
+  return r;
+}
 
 #define QG_APPLY_BINARY(EXPR)                          \
   do {                                                 \
@@ -170,7 +219,7 @@ __device__ __forceinline__ void ld16(const float* src, float (&o)[16]) {
 }
 
 // Loads a binary step's operand for this thread's row and chunk columns [nb, nb + 16).
-__device__ __forceinline__ void qg_operand(const QgParams& p, const mira_epi_step& st, int m, bool row_ok, int nb,
+__device__ __forceinline__ void qg_operand(const QgParams& p, const mira_epi_step& st, int64_t m, bool row_ok, int nb,
                                            bool full_chunk, float (&o)[16]) {
   if (st.operand == MIRA_OPND_SCALAR) {
 #pragma unroll
@@ -182,7 +231,7 @@ __device__ __forceinline__ void qg_operand(const QgParams& p, const mira_epi_ste
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j] = t;
   } else {  // FULL
-    const float* src = st.ptr + static_cast<int64_t>(m) * st.ld + nb;
+    const float* src = st.ptr + m * st.ld + nb;
     if (!row_ok) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) o[j] = 0.0f;
@@ -196,9 +245,10 @@ __device__ __forceinline__ void qg_operand(const QgParams& p, const mira_epi_ste
 }
 
 // Stores this thread's 16 values of a chunk: through the warp's staging block (coalesced 16-byte
-// stores of whole rows) when the chunk is full and rows are 16-byte aligned, else directly.
-template <int PITCH>
-__device__ __forceinline__ void qg_store_f32(const QgParams& p, const float (&v)[16], int m, bool row_ok, int m_warp0,
+// stores of whole rows) when the chunk is full and rows are 16-byte aligned, else directly.  With
+// MAPPED rows the other rows' pixels come from their lanes.
+template <int PITCH, bool MAPPED>
+__device__ __forceinline__ void qg_store_f32(const QgParams& p, const float (&v)[16], const QgRow& row, int m_warp0,
                                              int nb, bool full_chunk, float* stage, int lane, float* out_f32) {
   if (full_chunk && (p.ld_f32 % 4) == 0) {
     float4* srow = reinterpret_cast<float4*>(stage + lane * PITCH);
@@ -209,12 +259,20 @@ __device__ __forceinline__ void qg_store_f32(const QgParams& p, const float (&v)
     for (int i = 0; i < 4; ++i) {
       const int rr = i * 8 + (lane >> 2), qq = lane & 3;
       const float4 t = reinterpret_cast<const float4*>(stage + rr * PITCH)[qq];
-      const int mm = m_warp0 + rr;
-      if (mm < p.M) reinterpret_cast<float4*>(out_f32 + static_cast<int64_t>(mm) * p.ld_f32 + nb)[qq] = t;
+      int64_t pr;
+      bool okr;
+      if (MAPPED) {
+        pr = __shfl_sync(0xffffffffu, row.pix, rr);
+        okr = __shfl_sync(0xffffffffu, row.ok ? 1 : 0, rr) != 0;
+      } else {
+        pr = m_warp0 + rr;
+        okr = pr < p.M;
+      }
+      if (okr) reinterpret_cast<float4*>(out_f32 + pr * p.ld_f32 + nb)[qq] = t;
     }
     __syncwarp();
-  } else if (row_ok) {
-    float* dst = out_f32 + static_cast<int64_t>(m) * p.ld_f32 + nb;
+  } else if (row.ok) {
+    float* dst = out_f32 + row.pix * p.ld_f32 + nb;
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (nb + j < p.N) dst[j] = v[j];
@@ -256,10 +314,12 @@ __device__ __forceinline__ void qg_apply_binary(const mira_epi_step& st, const f
 // depend on the accumulator (dequant scales, the first binary operand) is loaded before the TMEM
 // read so the two latencies overlap.  In raw mode (split-K partial sums) the int32 accumulators
 // are stored unchanged.
-template <bool ROWCOL, int PITCH>
-__device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t taddr, int m, bool row_ok, int m_warp0,
+template <bool ROWCOL, int PITCH, bool MAPPED = false>
+__device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t taddr, const QgRow& row, int m_warp0,
                                                   int nb, float* stage, int lane, float* out_f32) {
   const bool full_chunk = nb + 16 <= p.N;
+  const int64_t m = row.pix;
+  const bool row_ok = row.ok;
   if (p.raw) {
     uint32_t r[16];
     tmem_ld_32x32b_x16(taddr, r);
@@ -267,7 +327,7 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-    qg_store_f32<PITCH>(p, v, m, row_ok, m_warp0, nb, full_chunk, stage, lane, out_f32);
+    qg_store_f32<PITCH, MAPPED>(p, v, row, m_warp0, nb, full_chunk, stage, lane, out_f32);
     return;
   }
   float hs[16], ls[16];
@@ -340,7 +400,7 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
     }
   }
 
-  if (out_f32 != nullptr) qg_store_f32<PITCH>(p, v, m, row_ok, m_warp0, nb, full_chunk, stage, lane, out_f32);
+  if (out_f32 != nullptr) qg_store_f32<PITCH, MAPPED>(p, v, row, m_warp0, nb, full_chunk, stage, lane, out_f32);
   if (p.out_i8 != nullptr && row_ok && nb < p.ld_i8) {
     uint32_t b[16];
     requant16_x2(v, p.q_scale, p.q_rcp, p.q_c127, b);
@@ -349,7 +409,7 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
       for (int j = 0; j < 16; ++j)
         if (nb + j >= p.N) b[j] = 0u;
     }
-    *reinterpret_cast<uint4*>(p.out_i8 + static_cast<int64_t>(m) * p.ld_i8 + nb) =
+    *reinterpret_cast<uint4*>(p.out_i8 + row.i8 + (nb >> 4) * p.i8_chunk) =
         make_uint4(pack4_i8(b[0], b[1], b[2], b[3]), pack4_i8(b[4], b[5], b[6], b[7]),
                    pack4_i8(b[8], b[9], b[10], b[11]), pack4_i8(b[12], b[13], b[14], b[15]));
   }
@@ -357,11 +417,12 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
 
 // ---------------------------------------------------------------- the kernel
 
-template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK, int RKB = 0>
-__global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::THREADS, 1)
+template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK, int RKB = 0,
+          int PATCH = 0>
+__global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PATCH>::THREADS, 1)
     qgemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ QgParams p) {
-  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>;
+  using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PATCH>;
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
   constexpr uint32_t IDESC = idesc_i8(QG_BM, BN);
@@ -369,7 +430,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sB = smem + Cfg::A_REGION;
   float* staging = reinterpret_cast<float*>(sB + Cfg::B_REGION);
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(staging) + Cfg::STAGING_BYTES);
   uint64_t* empty = full + STAGES;
@@ -378,7 +439,9 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
   uint64_t* drain = tempty + 2;
   uint64_t* pool_bar = drain + 1;   // [2]: all epilogue threads wrote the tile buffer
   uint64_t* bres = pool_bar + 2;    // resident B landed (RKB > 0)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bres + 1);
+  uint64_t* pfull = bres + 1;       // [2]: a halo buffer landed (PATCH)
+  uint64_t* pempty = pfull + 2;     // [2]: the MMAs reading a halo buffer finished (PATCH)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -386,7 +449,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], qg_a_by_tma(AMODE) ? 1 : 1 + 128);
+      mbar_init(&full[s], qg_a_async(AMODE) ? 1 : 1 + 128);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -397,6 +460,10 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
     mbar_init(&pool_bar[0], Cfg::EPI_THREADS);
     mbar_init(&pool_bar[1], Cfg::EPI_THREADS);
     mbar_init(bres, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmB);
@@ -419,18 +486,32 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int issued = 0;
+      int issued = 0, patches = 0;
       bool ok = true;
       if (RKB > 0 && blockIdx.x < num_tiles) {
         // the whole B operand (one column tile, checked by the host) once for the CTA
         mbar_arrive_expect_tx(bres, p.num_kb * B_BYTES);
         for (int kb = 0; kb < p.num_kb; ++kb) tma_load_2d(sB + kb * B_BYTES, &tmB, kb * BK, 0, bres);
       }
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = blockIdx.x, it = 0; t < num_tiles && ok; t += gridDim.x, ++it) {
         const int split = t / mn_tiles, t_mn = t - split * mn_tiles;
         const int m0 = (t_mn / p.n_tiles) * QG_BM;
         const int n0 = (t_mn % p.n_tiles) * BN;
         const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        if (AMODE == QG_A_PATCH) {
+          // the tile's input halo: output slots m0 .. m0 + 127 read input slots m0 - (w + 3) ..
+          // m0 + 127 + (w + 3) of every chunk plane (guards and padding ring are zero)
+          const int pb = it & 1;
+          if (!mbar_wait(&pempty[pb], ((it >> 1) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
+          const uint32_t pbytes = static_cast<uint32_t>(p.g.patch_slots) * 16u;
+          const int planes = p.g.cp >> 4;
+          mbar_arrive_expect_tx(&pfull[pb], planes * pbytes);
+          const int8_t* src = p.A + (static_cast<int64_t>(p.g.guard) + m0 - (p.g.ow + 3)) * 16;
+          for (int c = 0; c < planes; ++c)
+            bulk_load(sA + pb * PATCH + c * pbytes, src + c * p.g.plane * 16, pbytes, &pfull[pb]);
+          ++patches;
+          if (RKB > 0) continue;
+        }
         // im2col: traversal position of the tile's first output pixel
         int iw0 = 0, ih0 = 0, img0 = 0;
         if (AMODE == QG_A_IM2COL) {
@@ -465,6 +546,10 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
           const int idx = issued - i;
           mbar_wait_drain(&full[idx % STAGES], (idx / STAGES) & 1);
         }
+        for (int i = 1; i <= 2 && i <= patches; ++i) {
+          const int idx = patches - i;
+          mbar_wait_drain(&pfull[idx & 1], (idx >> 1) & 1);
+        }
       }
       if (RKB > 0 && blockIdx.x < num_tiles) mbar_wait_drain(bres, 0);
     }
@@ -476,6 +561,8 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
       int it = 0;
       bool ok = true;
       if (RKB > 0 && blockIdx.x < num_tiles && !mbar_wait(bres, 0, abort_flag, QG_TIMEOUT_NS)) ok = false;
+      // PATCH mode with resident weights waits on nothing per K-block: the halo and B are in place
+      constexpr bool kStaged = !(AMODE == QG_A_PATCH && RKB > 0);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
         const int acc = it & 1;
         if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) break;
@@ -483,23 +570,54 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
         const uint32_t d_tmem = tmem_base + acc * BN;
         const int split = t / mn_tiles;
         const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
-          if (!qg_a_by_tma(AMODE)) fence_proxy_async_smem();  // A was written by cp.async (generic proxy)
+        uint32_t halo = 0, plane_bytes = 0;
+        int kbc = 1;
+        if (AMODE == QG_A_PATCH) {
+          if (!mbar_wait(&pfull[it & 1], (it >> 1) & 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + (RKB > 0 ? kb : stage) * B_BYTES);
-          const int rem = p.K - kb * BK;
-          const int nk = rem >= BK ? BK / QG_UMMA_K : (rem + QG_UMMA_K - 1) / QG_UMMA_K;
-          for (int kk = 0; kk < nk; ++kk) {
-            const uint32_t ao = a_addr + kk * QG_UMMA_K, bo = b_addr + kk * QG_UMMA_K;
-            mma_i8(d_tmem, BK == 64 ? smem_desc_k_sw64(ao) : smem_desc_k_sw128(ao),
-                   BK == 64 ? smem_desc_k_sw64(bo) : smem_desc_k_sw128(bo),
-                   IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
-          }
-          mma_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          halo = smem_u32(sA + (it & 1) * PATCH);
+          plane_bytes = static_cast<uint32_t>(p.g.patch_slots) * 16u;
+          kbc = p.g.cp / BK;
         }
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (kStaged) {
+            if (!mbar_wait(&full[stage], phase, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
+            if (!qg_a_async(AMODE)) fence_proxy_async_smem();  // A was written by cp.async (generic proxy)
+            tc_fence_after();
+          }
+          const uint32_t b_addr = smem_u32(sB + (RKB > 0 ? kb : stage) * B_BYTES);
+          if (AMODE == QG_A_PATCH) {
+            // K-block kb = channels [cb * BK, cb * BK + BK) of tap (ti, tj): the A rows are the halo's
+            // slots shifted by the tap, each 16-channel chunk one plane of the halo
+            const int tap = kb / kbc, cb = kb - tap * kbc;
+            const int ti = tap / 3, tj = tap - ti * 3;
+            const uint32_t a_addr =
+                halo + static_cast<uint32_t>(p.g.ow + 3 + (ti - 1) * (p.g.ow + 2) + (tj - 1)) * 16u;
+#pragma unroll
+            for (int kk = 0; kk < BK / QG_UMMA_K; ++kk) {
+              const uint32_t chunk = static_cast<uint32_t>((cb * BK + kk * QG_UMMA_K) >> 4);
+              const uint32_t bo = b_addr + kk * QG_UMMA_K;
+              mma_i8(d_tmem, smem_desc_k_none(a_addr + chunk * plane_bytes, plane_bytes, 128),
+                     BK == 64 ? smem_desc_k_sw64(bo) : smem_desc_k_sw128(bo), IDESC,
+                     (kb != kb0 || kk != 0) ? 1u : 0u);
+            }
+          } else {
+            const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+            const int rem = p.K - kb * BK;
+            const int nk = rem >= BK ? BK / QG_UMMA_K : (rem + QG_UMMA_K - 1) / QG_UMMA_K;
+            for (int kk = 0; kk < nk; ++kk) {
+              const uint32_t ao = a_addr + kk * QG_UMMA_K, bo = b_addr + kk * QG_UMMA_K;
+              mma_i8(d_tmem, BK == 64 ? smem_desc_k_sw64(ao) : smem_desc_k_sw128(ao),
+                     BK == 64 ? smem_desc_k_sw64(bo) : smem_desc_k_sw128(bo),
+                     IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
+            }
+          }
+          if (kStaged) {
+            mma_commit(&empty[stage]);
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          }
+        }
+        if (AMODE == QG_A_PATCH && ok) mma_commit(&pempty[it & 1]);
         if (ok) mma_commit(&tfull[acc]);
       }
       // every MMA issued by this thread has finished once `drain` completes
@@ -524,14 +642,13 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       if (!POOL) {
         const int m_warp0 = t_m * QG_BM + quarter * 32;
-        const int m = m_warp0 + lane;
-        const bool row_ok = m < p.M;
+        const QgRow row = qg_row<AMODE>(p, m_warp0 + lane);
 #pragma unroll 1
         for (int c = group; c < BN / Cfg::CW; c += G) {
           const int nb = n0 + c * Cfg::CW;
           if (nb >= p.N) break;  // warp-uniform
-          qg_epilogue_chunk<ROWCOL, Cfg::STAGE_PITCH>(p, tbase + c * Cfg::CW, m, row_ok, m_warp0, nb, stage, lane,
-                                                      out_f32);
+          qg_epilogue_chunk<ROWCOL, Cfg::STAGE_PITCH, AMODE == QG_A_PATCH>(p, tbase + c * Cfg::CW, row, m_warp0, nb,
+                                                                         stage, lane, out_f32);
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
@@ -602,7 +719,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB>::TH
         }
       }
     }
-  } else if (!qg_a_by_tma(AMODE) && warp >= Cfg::GATHER_WARP0) {
+  } else if (!qg_a_async(AMODE) && warp >= Cfg::GATHER_WARP0) {
     // ------------------------------------------------ im2col gather of A (convolutions)
     const int row = threadIdx.x - 32 * Cfg::GATHER_WARP0;
     const QgConv& g = p.g;

@@ -78,6 +78,58 @@ def row4_entries(ow: int, stride_w: int) -> int:
     return int(ow) + 4 // int(stride_w)
 
 
+def cp_guard(w: int) -> int:
+    """Guard slots in front of the planes of the chunk-planar layout (MIRA_LAYOUT_CP) of width w."""
+    return round_up(int(w) + 3, 8)
+
+
+# bytes of one halo buffer of the chunk-planar conv kernels per input channel count (libmira_cuda's
+# patch_cap): a 3x3 stride-1 conv reads the layout when (128 + 2 (w + 3)) * c fits
+PATCH_CAP = {64: 16384, 128: 24576, 256: 41984, 512: 75776}
+
+
+def patch_fits(c: int, w: int) -> bool:
+    """A 3x3 stride-1 pad-1 conv over [., c, ., w] int8 inputs has a chunk-planar kernel."""
+    cap = PATCH_CAP.get(int(c))
+    return cap is not None and (128 + 2 * (int(w) + 3)) * int(c) <= cap
+
+
+# The chunk-planar conv computes every slot of the zero-padded plane, (h + 2)(w + 2) per image
+# instead of h w, and its epilogue (the conv's bound) runs on all of them: on narrow images that
+# extra work outweighs the cheaper operand loads (measured on ResNet-18: faster at 56 x 56, slower
+# at 28 x 28 and below), so the planner uses it from this width on.
+PATCH_MIN_WIDTH = 40
+
+
+def patch_preferred(c: int, w: int) -> bool:
+    return int(w) >= PATCH_MIN_WIDTH and patch_fits(c, w)
+
+
+def cp_bytes(n: int, h: int, w: int, cp: int) -> int:
+    """Bytes of an int8 [n, h, w, cp] activation in the chunk-planar, zero-padded layout."""
+    g = cp_guard(w)
+    return (2 * g + 128 + (int(cp) // 16) * int(n) * (int(h) + 2) * (int(w) + 2)) * 16
+
+
+def to_cp(x_nhwc: np.ndarray) -> np.ndarray:
+    """int8 NHWC [n, h, w, cp] (cp % 16 == 0) -> its MIRA_LAYOUT_CP bytes (host-side, for tests)."""
+    n, h, w, cp = x_nhwc.shape
+    g = cp_guard(w)
+    planes = np.zeros((cp // 16, n, h + 2, w + 2, 16), np.int8)
+    planes[:, :, 1:h + 1, 1:w + 1, :] = x_nhwc.reshape(n, h, w, cp // 16, 16).transpose(3, 0, 1, 2, 4)
+    out = np.zeros(cp_bytes(n, h, w, cp), np.int8)
+    out[g * 16:g * 16 + planes.size] = planes.ravel()
+    return out
+
+
+def from_cp(buf: np.ndarray, n: int, h: int, w: int, cp: int) -> np.ndarray:
+    """The inverse of to_cp: MIRA_LAYOUT_CP bytes -> int8 NHWC [n, h, w, cp]."""
+    g = cp_guard(w)
+    size = (cp // 16) * n * (h + 2) * (w + 2) * 16
+    planes = np.asarray(buf, np.int8)[g * 16:g * 16 + size].reshape(cp // 16, n, h + 2, w + 2, 16)
+    return np.ascontiguousarray(planes[:, :, 1:h + 1, 1:w + 1, :].transpose(1, 2, 3, 0, 4).reshape(n, h, w, cp))
+
+
 def conv_weight_row4(q_oihw: np.ndarray) -> np.ndarray:
     """Reference qconv2d weight int8 [O, C<=4, KH, KW<=8] -> [O, KH*32] for MIRA_LAYOUT_ROW4 inputs:
     k = i * 32 + j * 4 + c (taps j >= KW and channels c >= C are 0)."""
@@ -114,6 +166,7 @@ class Epi:
     out_i8: object = None
     ld_i8: int = 0
     out_scale: float = 1.0
+    i8_layout: int = 0       # _lib.LAYOUT_NHWC or _lib.LAYOUT_CP (convolutions)
 
     def struct(self) -> _lib.Epilogue:
         e = _lib.Epilogue()
@@ -135,6 +188,7 @@ class Epi:
         e.out_i8 = ptr(self.out_i8).value or 0
         e.ld_i8 = int(self.ld_i8)
         e.out_scale = float(np.float32(self.out_scale))
+        e.i8_layout = int(self.i8_layout)
         return e
 
 
@@ -200,10 +254,10 @@ def qconv2d_maxpool(n: int, h: int, w: int, cp: int, x, o: int, kh: int, kw: int
 
 
 def maxpool2d(n, h, w, c, ldc_in, size, stride, pad, pad_value, x_f32=None, x_i8=None, out_f32=None,
-              ldc_out_f32=0, out_i8=None, ldc_out_i8=0, out_scale=1.0) -> None:
-    _lib.call("mira_cuda_maxpool2d_nhwc", ptr(x_f32), ptr(x_i8), n, h, w, c, ldc_in, size, stride, pad,
+              ldc_out_f32=0, out_i8=None, ldc_out_i8=0, out_scale=1.0, i8_layout: int = 0) -> None:
+    _lib.call("mira_cuda_maxpool2d_nhwc_ex", ptr(x_f32), ptr(x_i8), n, h, w, c, ldc_in, size, stride, pad,
               float(np.float32(pad_value)), ptr(out_f32), ldc_out_f32, ptr(out_i8), ldc_out_i8,
-              float(np.float32(out_scale)))
+              float(np.float32(out_scale)), int(i8_layout))
 
 
 def mean_hw(x, n, hw, c, ldc, out_f32=None, out_i8=None, ld_i8=0, out_scale=1.0) -> None:

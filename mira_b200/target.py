@@ -169,10 +169,11 @@ class CudaDevice:
                 args = (a["n"], a["h"], a["w"], a["cp"], ptr(a["x"]), a["layout"], a["row_entries"], a["o"], a["kh"],
                         a["kw"], ptr(a["wq"]), a["ldw"], sh, sw, ph, pw, dh, dw, C.byref(dq), C.byref(e))
         elif k == "maxpool":
-            fn = L.mira_cuda_maxpool2d_nhwc
+            fn = L.mira_cuda_maxpool2d_nhwc_ex
             args = (ptr(a.get("x_f32")), ptr(a.get("x_i8")), a["n"], a["h"], a["w"], a["c"], a["ldc"], a["size"],
                     a["stride"], a["pad"], float(np.float32(a["pad_value"])), ptr(a.get("out_f32")), a.get("ldo", 0),
-                    ptr(a.get("out_i8")), a.get("ldo_i8", 0), float(np.float32(a.get("scale", 1.0))))
+                    ptr(a.get("out_i8")), a.get("ldo_i8", 0), float(np.float32(a.get("scale", 1.0))),
+                    int(a.get("i8_layout", 0)))
         elif k == "mean_hw":
             fn = L.mira_cuda_mean_hw_nhwc
             args = (ptr(a["x"]), a["n"], a["hw"], a["c"], a["ldc"], ptr(a.get("out_f32")), ptr(a.get("out_i8")),
@@ -269,7 +270,8 @@ class DVal:
     i8: object = None
     i8_scale: Optional[float] = None
     i8_ld: int = 0
-    i8_layout: str = "nhwc"      # or "row4" (MIRA_LAYOUT_ROW4, graph inputs of at most 4 channels)
+    i8_layout: str = "nhwc"      # or "row4" (MIRA_LAYOUT_ROW4, graph inputs of at most 4 channels), or "cp"
+                                 # (MIRA_LAYOUT_CP, read by 3x3 stride-1 convolutions)
     row_entries: int = 0
     i32: object = None           # int32 graph inputs (token ids)
     strides: Optional[tuple] = None   # "rows" layout: element strides of the f32 view (None: row-major)
@@ -473,6 +475,33 @@ class Plan:
                         self.image_values.add(v)
         self._group_qmatmuls()
         self._find_attention()
+        self.cp_values = {v for v in i8_req if self._cp_layout_ok(v)}
+
+    def _cp_layout_ok(self, v) -> bool:
+        """Whether the int8 form of `v` is kept in the chunk-planar layout (MIRA_LAYOUT_CP): every
+        quantized op reading it is a 3x3, stride-1, pad-1 convolution of 64k channels whose halo
+        fits the kernel's buffers, all at one scale, and `v` comes from a convolution epilogue or
+        the f32 max pool (the producers that write the layout)."""
+        if v.type.rank != 4 or v not in self.image_values:
+            return False
+        p = v.producer
+        if p is None or p.kind not in ("qconv2d", "maxpool2d") or p in self.skipped or p in self.conv_into_pool:
+            return False
+        n, c, h, w = v.type.shape
+        if c % 64 or not K.patch_preferred(c, w):
+            return False
+        readers = 0
+        for op in self.users.get(v, []):
+            if op.kind not in QOPS or op.inputs[0] is not v:
+                continue
+            stride, padding, dilation, groups = conv_attrs(op.attrs)
+            kh, kw = np.asarray(op.attrs["q"]).shape[2:]
+            if (op.kind != "qconv2d" or op in self.skipped or _f32(op.attrs["x_scale"]) != self.i8_req[v] or groups != 1
+                    or (kh, kw) != (3, 3) or tuple(stride) != (1, 1) or tuple(padding) != (1, 1)
+                    or tuple(dilation) != (1, 1)):
+                return False
+            readers += 1
+        return readers > 0
 
     def _find_attention(self):
         """matmul(q, k^T) {scale, mask} -> softmax(axis=-1) -> matmul(., v) chains run as one fused
@@ -640,7 +669,12 @@ class Plan:
         if v in self.i8_req:
             dv.i8_scale = self.i8_req[v]
             dv.i8_ld = K.round_up(dv.cols, 16)
-            dv.i8 = self._alloc(dv.rows * dv.i8_ld, zero=True)
+            if v in self.cp_values:
+                n, c, h, w = shape
+                dv.i8_layout = "cp"
+                dv.i8 = self._alloc(K.cp_bytes(n, h, w, dv.i8_ld), zero=True)
+            else:
+                dv.i8 = self._alloc(dv.rows * dv.i8_ld, zero=True)
         self.vals[v] = dv
         return dv
 
@@ -750,6 +784,8 @@ class Plan:
         dv = self.vals[v]
         if dv.i8 is not None and dv.i8_scale == scale and dv.i8_layout == "row4":
             return dv.i8, 4, _lib.LAYOUT_ROW4, dv.row_entries
+        if dv.i8 is not None and dv.i8_scale == scale and dv.i8_layout == "cp":
+            return dv.i8, dv.i8_ld, _lib.LAYOUT_CP, 0
         buf, cp = self._i8_of(v, scale)
         return buf, cp, _lib.LAYOUT_NHWC, 0
 
@@ -811,7 +847,8 @@ class Plan:
             else:
                 steps.append(self._operand_step(fn, bool(swapped), op.inputs[idx], out))
         return K.Epi(steps, out_f32=out.f32, ld_f32=out.cols, out_i8=out.i8, ld_i8=out.i8_ld,
-                     out_scale=out.i8_scale if out.i8 is not None else 1.0)
+                     out_scale=out.i8_scale if out.i8 is not None else 1.0,
+                     i8_layout=_lib.LAYOUT_CP if out.i8_layout == "cp" else _lib.LAYOUT_NHWC)
 
     def _operand_step(self, fn: str, swapped: bool, v, out: DVal) -> K.Step:
         val = self._const(v)
@@ -1014,7 +1051,8 @@ class Plan:
         out = self._new_out(op.result, "nhwc")
         self._launch("maxpool", x_f32=x.f32, n=n, h=h, w=w, c=c, ldc=c, size=op.attrs["size"],
                      stride=op.attrs["stride"], pad=pad, pad_value=pad_value, out_f32=out.f32, ldo=c,
-                     out_i8=out.i8, ldo_i8=out.i8_ld, scale=out.i8_scale or 1.0)
+                     out_i8=out.i8, ldo_i8=out.i8_ld, scale=out.i8_scale or 1.0,
+                     i8_layout=_lib.LAYOUT_CP if out.i8_layout == "cp" else _lib.LAYOUT_NHWC)
 
     def _conv_pool(self, pool, conv, pad: int, pad_value: float) -> None:
         """qconv2d -> (pad) -> maxpool2d as one kernel: the conv epilogue runs on the conv outputs,

@@ -150,7 +150,11 @@ class FakeDevice:
             xn = full[:, :, pad_w:pad_w + w, :].transpose(0, 3, 1, 2)
             wt = wq.view(np.int8, (o, ldw))[:, : kh * 32].reshape(o, kh, 8, 4)[:, :, :kw, :].transpose(0, 3, 1, 2)
             return xn, wt
-        xn = x.view(np.int8, (n, h, w, cp)).transpose(0, 3, 1, 2)
+        if layout == 2:                    # chunk-planar, zero-padded
+            from mira_b200 import kernels as K
+            xn = K.from_cp(x.data[:K.cp_bytes(n, h, w, cp)].view(np.int8), n, h, w, cp).transpose(0, 3, 1, 2)
+        else:
+            xn = x.view(np.int8, (n, h, w, cp)).transpose(0, 3, 1, 2)
         wt = wq.view(np.int8, (o, ldw))[:, : kh * kw * cp].reshape(o, kh, kw, cp).transpose(0, 3, 1, 2)
         return xn, wt
 
@@ -163,7 +167,24 @@ class FakeDevice:
     def _copy(self, dst, src, nbytes):
         dst.data[:nbytes] = src.data[:nbytes]
 
-    def _epi(self, y, epi, M, N):
+    @staticmethod
+    def _put_i8(buf, q, ld, layout, geom):
+        """int8 rows [M, N] into `buf`: rows of ld bytes, or (layout 2) the chunk-planar layout of
+        the [n, oh, ow, ld] activation geom = (n, oh, ow) (its padding stays zero)."""
+        m, nc = q.shape
+        if layout == 2:
+            from mira_b200 import kernels as K
+            n, oh, ow = geom
+            full = np.zeros((n, oh, ow, ld), np.int8)
+            full.reshape(m, ld)[:, :nc] = q
+            enc = K.to_cp(full)
+            buf.data[:enc.size] = enc.view(np.uint8)
+            return
+        rows = buf.view(np.int8, (m, ld))
+        rows[:, :nc] = q
+        rows[:, nc:] = 0
+
+    def _epi(self, y, epi, M, N, geom=None):
         """y: f32 [M, N] dequantized; applies steps and writes the outputs."""
         for s in epi.steps:
             if s.operand == "none":
@@ -181,9 +202,7 @@ class FakeDevice:
         if epi.out_f32 is not None:
             epi.out_f32.view(np.float32, (M, epi.ld_f32))[:, :N] = y
         if epi.out_i8 is not None:
-            q = epi.out_i8.view(np.int8, (M, epi.ld_i8))
-            q[:, :N] = ref.quantize_activation(y, epi.out_scale)
-            q[:, N:] = 0
+            self._put_i8(epi.out_i8, ref.quantize_activation(y, epi.out_scale), epi.ld_i8, epi.i8_layout, geom)
 
     def _dequant(self, acc, dq, N):
         s64 = dq[0].view(np.float64, (N,))
@@ -229,7 +248,7 @@ class FakeDevice:
         acc = ref.int_conv2d(xn, wt, stride, padding, dilation)       # [n, o, oh, ow]
         oh, ow = acc.shape[2:]
         rows = acc.transpose(0, 2, 3, 1).reshape(n * oh * ow, o)
-        self._epi(self._dequant(rows, dq, o), epi, n * oh * ow, o)
+        self._epi(self._dequant(rows, dq, o), epi, n * oh * ow, o, geom=(n, oh, ow))
 
     def _qconv2d_pool(self, n, h, w, cp, x, o, kh, kw, wq, ldw, stride, padding, dilation, pool_size, pool_stride,
                       pool_pad, pool_pad_value, dq, epi, layout=0, row_entries=0):
@@ -254,7 +273,7 @@ class FakeDevice:
             q[:, o:] = 0
 
     def _maxpool(self, n, h, w, c, ldc, size, stride, pad, pad_value, x_f32=None, x_i8=None, out_f32=None, ldo=0,
-                 out_i8=None, ldo_i8=0, scale=1.0):
+                 out_i8=None, ldo_i8=0, scale=1.0, i8_layout=0):
         xv = x_f32.view(np.float32, (n, h, w, ldc))[..., :c].transpose(0, 3, 1, 2)
         y = ref.maxpool2d(xv, size, stride, pad, pad_value)
         oh, ow = y.shape[2:]
@@ -262,7 +281,7 @@ class FakeDevice:
         if out_f32 is not None:
             out_f32.view(np.float32, (n * oh * ow, ldo))[:, :c] = rows
         if out_i8 is not None:
-            out_i8.view(np.int8, (n * oh * ow, ldo_i8))[:, :c] = ref.quantize_activation(rows, scale)
+            self._put_i8(out_i8, ref.quantize_activation(rows, scale), ldo_i8, i8_layout, (n, oh, ow))
 
     def _mean_hw(self, x, n, hw, c, ldc, out_f32=None, out_i8=None, ld_i8=0, scale=1.0):
         xv = x.view(np.float32, (n, hw, ldc))[..., :c].transpose(0, 2, 1)

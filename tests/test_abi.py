@@ -5,6 +5,7 @@ import ctypes as C
 import re
 from pathlib import Path
 
+import numpy as np
 import pytest
 
 from mira_b200 import _lib
@@ -53,3 +54,21 @@ def test_no_gpu_is_an_error_not_a_fallback():
     with pytest.raises(_lib.CudaError):
         _lib.call("mira_cuda_malloc", C.byref(p), C.c_size_t(64))
     assert "device" in _lib.last_error()
+
+
+def test_chunk_planar_layout_helpers_round_trip():
+    """MIRA_LAYOUT_CP on the host: to_cp / from_cp invert each other, the padding ring and the
+    guards are zero, and the byte count matches the header's formula."""
+    from mira_b200 import kernels as K
+    rng = np.random.default_rng(0)
+    for n, h, w, cp in ((2, 5, 7, 32), (1, 56, 56, 64), (3, 1, 1, 16)):
+        x = rng.integers(-127, 128, (n, h, w, cp)).astype(np.int8)
+        b = K.to_cp(x)
+        g = K.cp_guard(w)
+        assert b.size == K.cp_bytes(n, h, w, cp) == (2 * g + 128 + cp // 16 * n * (h + 2) * (w + 2)) * 16
+        assert np.array_equal(K.from_cp(b, n, h, w, cp), x)
+        assert int(np.abs(b.astype(np.int64)).sum()) == int(np.abs(x.astype(np.int64)).sum())
+        # slot (c16, img, y, x) = g + c16 * plane + (img * (h + 2) + y + 1) * (w + 2) + x + 1
+        plane = n * (h + 2) * (w + 2)
+        slot = g + (cp // 16 - 1) * plane + ((n - 1) * (h + 2) + h) * (w + 2) + w
+        assert np.array_equal(b[slot * 16:slot * 16 + 16], x[n - 1, h - 1, w - 1, cp - 16:])

@@ -571,3 +571,130 @@ def test_qgemm_config2_8192_cubed_exact(cuda_device):
     got = yb.download((n, n), np.float32)
     _, want = ref.qgemm_rowcol(a, b.T, rs, cs, bias)
     _same_f32(got, want)
+
+
+# ------------------------------------------------------------------------------ chunk-planar convs
+
+def _run_qconv_cp(n, c, h, w, o, seed, out_layout, residual=False, out_f32=True):
+    """A 3x3 stride-1 pad-1 conv reading the chunk-planar layout (MIRA_LAYOUT_CP): every output
+    against the oracle, int8 output in the chunk-planar or NHWC layout."""
+    from mira_b200 import _lib
+    K, DB = _k()
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    x_scale = float(np.abs(x).max() / 127.0)
+    wt = (rng.standard_normal((o, c, 3, 3)) / np.sqrt(c * 9)).astype(np.float32)
+    q, w_scale = ref.quantize_array(wt, 0)
+    bias = rng.standard_normal((o, 1, 1)).astype(np.float32)
+    res = rng.standard_normal((n, o, h, w)).astype(np.float32)
+    steps_ref, operands = [("add", 1, False)], [bias]
+    if residual:
+        steps_ref.append(("add", 2, False))
+        operands.append(res)
+    steps_ref.append(("relu", None, False))
+    xq, acc, y = ref.qconv2d(x, q, w_scale, x_scale, (1, 1), (1, 1), steps=steps_ref, operands=operands)
+    wq, cp = K.conv_weight(q, K.round_up(c, 64))    # the layout's convs read 64k channels
+    xn = np.zeros((n, h, w, cp), np.int8)
+    xn[..., :c] = xq.transpose(0, 2, 3, 1)
+    xb = DB.from_array(K.to_cp(xn))
+    assert xb.nbytes == _lib.load().mira_cuda_cp_bytes(n, h, w, cp)
+    s64, hi, lo = K.scale_arrays(x_scale, w_scale)
+    keep = [DB.from_array(a) for a in (s64, hi, lo)]
+    bb = DB.from_array(K.pad_channels(bias))
+    steps = [K.Step("add", "channel", ptr=bb)]
+    if residual:
+        rb = DB.from_array(np.ascontiguousarray(res.transpose(0, 2, 3, 1)))
+        steps.append(K.Step("add", "full", ptr=rb, ld=o))
+    steps.append(K.Step("relu"))
+    ldi = K.round_up(o, 16)
+    M = n * h * w
+    yb = DB(M * o * 4) if out_f32 else None
+    cp_out = out_layout == "cp"
+    qb = DB(K.cp_bytes(n, h, w, ldi) if cp_out else M * ldi, zero=True)
+    out_scale = float(np.abs(y).max() / 127.0) or 1.0
+    wb = DB.from_array(wq)
+    K.qconv2d(n, h, w, cp, xb, o, 3, 3, wb, wq.shape[1], (1, 1), (1, 1), (1, 1), K.dequant_channel(*keep),
+              K.Epi(steps, out_f32=yb, ld_f32=o, out_i8=qb, ld_i8=ldi, out_scale=out_scale,
+                    i8_layout=_lib.LAYOUT_CP if cp_out else _lib.LAYOUT_NHWC),
+              layout=_lib.LAYOUT_CP)
+    if out_f32:
+        _same_f32(yb.download((n, h, w, o), np.float32).transpose(0, 3, 1, 2), y)
+    raw = qb.download((qb.nbytes,), np.int8)
+    got_q = K.from_cp(raw, n, h, w, ldi) if cp_out else raw.reshape(n, h, w, ldi)
+    np.testing.assert_array_equal(got_q[..., :o].transpose(0, 3, 1, 2), ref.quantize_activation(y, out_scale))
+    assert not got_q[..., o:].any()
+    if cp_out:   # the padding ring and the guards stay zero
+        assert np.array_equal(K.to_cp(got_q), raw)
+
+
+@pytest.mark.parametrize("case", [
+    dict(n=2, c=64, h=56, w=56, o=64),          # ResNet layer 1 (resident weights)
+    dict(n=3, c=64, h=9, w=13, o=64),           # tiles spanning several images
+    dict(n=1, c=64, h=5, w=5, o=100),           # partial column tile
+    dict(n=2, c=64, h=20, w=20, o=256),
+    dict(n=2, c=128, h=28, w=28, o=128),        # layer 2
+    dict(n=2, c=128, h=11, w=7, o=64),
+    dict(n=2, c=128, h=6, w=6, o=256),
+    dict(n=3, c=256, h=14, w=14, o=256),        # layer 3
+    dict(n=2, c=256, h=9, w=9, o=128),
+    dict(n=4, c=512, h=7, w=7, o=512),          # layer 4
+    dict(n=1, c=48, h=8, w=8, o=32),            # 64 padded channels
+])
+@pytest.mark.parametrize("out_layout", ["cp", "nhwc"])
+def test_qconv2d_chunk_planar_exact(cuda_device, case, out_layout):
+    _run_qconv_cp(**case, seed=case["h"] * 7 + case["o"], out_layout=out_layout)
+
+
+@pytest.mark.parametrize("case", [dict(n=2, c=64, h=56, w=56, o=64), dict(n=3, c=128, h=28, w=28, o=128),
+                                  dict(n=2, c=512, h=7, w=7, o=512)])
+def test_qconv2d_chunk_planar_residual_exact(cuda_device, case):
+    """The block's second conv: bias + residual (full f32 operand read per pixel) + relu, f32 and int8 out."""
+    _run_qconv_cp(**case, seed=5, out_layout="cp", residual=True)
+
+
+def test_qconv2d_chunk_planar_int8_only(cuda_device):
+    _run_qconv_cp(2, 64, 56, 56, 64, seed=9, out_layout="cp", out_f32=False)
+
+
+def test_qconv2d_nhwc_input_chunk_planar_output(cuda_device):
+    """A stride-2 im2col conv writing its int8 output in the chunk-planar layout (the next layer's
+    3x3 convs read it)."""
+    from mira_b200 import _lib
+    K, DB = _k()
+    rng = np.random.default_rng(3)
+    n, c, h, w, o = 2, 64, 15, 13, 128
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    x_scale = float(np.abs(x).max() / 127.0)
+    q, w_scale = ref.quantize_array(rng.standard_normal((o, c, 3, 3)).astype(np.float32), 0)
+    xq, _, y = ref.qconv2d(x, q, w_scale, x_scale, (2, 2), (1, 1), steps=[("relu", None, False)])
+    wq, cp = K.conv_weight(q)
+    xb = DB.from_array(np.ascontiguousarray(xq.transpose(0, 2, 3, 1)))
+    keep = [DB.from_array(a) for a in K.scale_arrays(x_scale, w_scale)]
+    oh, ow = y.shape[2:]
+    qb = DB(K.cp_bytes(n, oh, ow, o), zero=True)
+    out_scale = float(np.abs(y).max() / 127.0)
+    K.qconv2d(n, h, w, cp, xb, o, 3, 3, DB.from_array(wq), wq.shape[1], (2, 2), (1, 1), (1, 1),
+              K.dequant_channel(*keep), K.Epi([K.Step("relu")], out_i8=qb, ld_i8=o, out_scale=out_scale,
+                                             i8_layout=_lib.LAYOUT_CP))
+    got = K.from_cp(qb.download((qb.nbytes,), np.int8), n, oh, ow, o)
+    np.testing.assert_array_equal(got.transpose(0, 3, 1, 2), ref.quantize_activation(y, out_scale))
+
+
+def test_maxpool_chunk_planar_int8_output(cuda_device):
+    """ResNet's stem pool writing the first block's int8 input in the chunk-planar layout."""
+    from mira_b200 import _lib
+    K, DB = _k()
+    rng = np.random.default_rng(4)
+    for n, c, h, w in ((2, 64, 15, 15), (3, 48, 9, 12)):
+        x = np.maximum(rng.standard_normal((n, c, h, w)), 0).astype(np.float32)
+        scale = float(np.abs(x).max() / 127)
+        want = ref.maxpool2d(x, 3, 2, 1)
+        oh, ow = want.shape[2:]
+        cp = K.round_up(c, 16)
+        xb = DB.from_array(np.ascontiguousarray(x.transpose(0, 2, 3, 1)))
+        qb = DB(K.cp_bytes(n, oh, ow, cp), zero=True)
+        K.maxpool2d(n, h, w, c, c, 3, 2, 1, -np.inf, x_f32=xb, out_i8=qb, ldc_out_i8=cp, out_scale=scale,
+                    i8_layout=_lib.LAYOUT_CP)
+        got = K.from_cp(qb.download((qb.nbytes,), np.int8), n, oh, ow, cp)
+        np.testing.assert_array_equal(got[..., :c].transpose(0, 3, 1, 2), ref.quantize_activation(want, scale))
+        assert not got[..., c:].any()

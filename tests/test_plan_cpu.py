@@ -50,6 +50,22 @@ def test_resnet18_small_plan_matches_cpu():
     assert dev.launched.count("quantize_row4") == 1    # the 3-channel image feeds the stem row-expanded
 
 
+def test_resnet18_chunk_planar_plan_matches_cpu(monkeypatch):
+    """With the chunk-planar layout allowed at every width, every 3x3 stride-1 conv reads it
+    (written by the max pool or the previous conv's epilogue) and the stride-2 and 1x1 convs read
+    NHWC; the results stay those of the reference cpu target."""
+    from mira_b200 import _lib
+    from mira_b200 import kernels as K
+    monkeypatch.setattr(K, "PATCH_MIN_WIDTH", 1)
+    cpu, cuda, dev = _pair("resnet18", 2, image=32)
+    _check_same(cpu, cuda)
+    launches = cuda.segments[0].executable.plan.launches
+    convs = [l for l in launches if l.kind == "qconv2d"]
+    assert sum(l.args["layout"] == _lib.LAYOUT_CP for l in convs) == 13
+    assert sum(l.args["epi"].i8_layout == _lib.LAYOUT_CP for l in convs) == 12
+    assert [l.args.get("i8_layout") for l in launches if l.kind == "maxpool"] == [_lib.LAYOUT_CP]
+
+
 def test_resnet18_fused_stem_pool_plan_matches_cpu():
     """With fuse_pool the stem conv runs inside the max-pool kernel (its f32 output never reaches
     HBM)."""
