@@ -116,18 +116,52 @@ __device__ __forceinline__ void dequant4_x2(const uint32_t* r, const float4& hs,
   }
 }
 
+// The dequant of 16 accumulators, the arithmetic of dequant4_x2 two lanes per instruction, with
+// the checks folded into two bitwise accumulations per element: the two ends of each value's
+// uncertainty interval must round to the same float (their bit patterns XOR to 0), and each
+// magic-number conversion 0x4B400000 + acc must keep the exponent of 2^23 (|acc| < 2^22: the bits
+// above the mantissa XOR to 0 against 0x4B000000).  Returns false when some value of the 16 needs
+// the exact f64 path.
+__device__ __forceinline__ bool dequant16_x2(const uint32_t (&r)[16], const float (&hs)[16], const float (&ls)[16],
+                                             float (&v)[16]) {
+  const f2_t magic = f2(-12582912.0f, -12582912.0f);
+  const f2_t e40 = f2(0x1p-40f, 0x1p-40f), ne40 = f2(-0x1p-40f, -0x1p-40f);
+  uint32_t bad = 0, range = 0;
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    const uint32_t x0 = 0x4B400000u + r[j], x1 = 0x4B400000u + r[j + 1];
+    range |= x0 ^ 0x4B000000u;
+    range |= x1 ^ 0x4B000000u;
+    const f2_t a = f2_add(f2(__uint_as_float(x0), __uint_as_float(x1)), magic);
+    const f2_t h = f2(hs[j], hs[j + 1]);
+    const f2_t pl = f2_mul(a, f2(ls[j], ls[j + 1]));
+    const f2_t yl = f2_fma(a, h, f2_fma(a, f2_mul(h, ne40), pl));
+    const f2_t yh = f2_fma(a, h, f2_fma(a, f2_mul(h, e40), pl));
+    float l0, l1, h0, h1;
+    f2_split(yl, l0, l1);
+    f2_split(yh, h0, h1);
+    v[j] = l0;
+    v[j + 1] = l1;
+    bad |= __float_as_uint(l0) ^ __float_as_uint(h0);
+    bad |= __float_as_uint(l1) ^ __float_as_uint(h1);
+  }
+  return (bad | (range & 0xFF800000u)) == 0;
+}
+
 // Requantization of 16 values, two per instruction: clip(round_half_even(RN(y / s)), -127, 127)
 // as bytes.  y is clamped to +-c127 = +-RN(127 s) first, so every quotient lies in [-127, 127]
 // after rounding and no clip is needed afterwards (RN(c127 / s) rounds to 127; infinities map to
 // +-127); then Markstein's correction of RN(y * RN(1/s)) and the 1.5 * 2^23 rounding add.
 // Checked against the reference formula on 3e8 random cases (ties, values next to the clip).
-template <int N>
+// NONNEG: the values are known to be >= 0 (or NaN), so only the upper clamp is applied.
+template <int N, bool NONNEG = false>
 __device__ __forceinline__ void requant_x2(const float (&v)[N], float s, float rcp, float c127, uint32_t (&b)[N]) {
   static_assert(N % 2 == 0, "values come in pairs");
   const f2_t r2 = f2(rcp, rcp), ns = f2(-s, -s), magic = f2(12582912.0f, 12582912.0f);
 #pragma unroll
   for (int j = 0; j < N; j += 2) {
-    const f2_t y = f2(fminf(fmaxf(v[j], -c127), c127), fminf(fmaxf(v[j + 1], -c127), c127));
+    const f2_t y = NONNEG ? f2(fminf(v[j], c127), fminf(v[j + 1], c127))
+                          : f2(fminf(fmaxf(v[j], -c127), c127), fminf(fmaxf(v[j + 1], -c127), c127));
     const f2_t q0 = f2_mul(y, r2);
     const f2_t z = f2_fma(f2_fma(q0, ns, y), r2, q0);
     float t0, t1;

@@ -195,6 +195,14 @@ static int encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner_bytes
 
 // ---------------------------------------------------------------- qgemm dispatch
 
+// The kernels' division by d (1 <= d < 2^31) for dividends below 2^31 (QgDiv).
+static QgDiv make_div(int64_t d) {
+  uint32_t l = 0;
+  while ((int64_t(1) << l) < d) ++l;
+  const uint64_t mul = ((uint64_t(1) << 32) * ((uint64_t(1) << l) - uint64_t(d))) / uint64_t(d) + 1;
+  return QgDiv{static_cast<uint32_t>(mul), l};
+}
+
 template <int BN, int STAGES, int AMODE, bool ROWCOL, int G, bool POOL = false, int BK = QG_BK, int RKB = 0,
           int PATCH = 0>
 static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUtensorMap& tmB, const QgParams& p_in) {
@@ -205,6 +213,8 @@ static int launch_qgemm_cfg(DeviceState* dev, const CUtensorMap& tmA, const CUte
   }
   if (RKB > 0 && (p.n_tiles != 1 || p.k_splits != 1 || p.num_kb > RKB))
     return set_error(MIRA_CUDA_EINVAL, "resident-weight kernel used for a shape it does not cover");
+  p.dv_ntiles = make_div(p.n_tiles);
+  p.dv_mntiles = make_div(int64_t(p.m_tiles) * p.n_tiles);
   using Cfg = QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PATCH>;
   auto kern = qgemm_sm100_kernel<BN, STAGES, AMODE, ROWCOL, G, POOL, BK, RKB, PATCH>;
   static bool attr_set[kMaxDevices] = {};
@@ -255,6 +265,8 @@ static int launch_qgemm_pair_cfg(DeviceState* dev, const CUtensorMap& tmA, const
   QgParams p = p_in;
   p.k_splits = 1;
   p.kb_per_split = p.num_kb;
+  p.dv_ntiles = make_div(p.n_tiles);
+  p.dv_mntiles = make_div(int64_t(p.m_tiles) * p.n_tiles);
   using Cfg = Qg2Cfg<BN, STAGES, G>;
   auto kern = qgemm_pair_kernel<BN, STAGES, ROWCOL, G>;
   static bool attr_set[kMaxDevices] = {};
@@ -413,6 +425,18 @@ static int fill_epilogue(QgParams& p, const mira_dequant* dq, const mira_epilogu
   p.i8_cp = 0;
   p.i8_guard = 0;
   p.i8_chunk = 16;   // rows layout: the next 16 channels are the next 16 bytes (set_i8_layout for CP)
+  // whether the steps end in values that cannot be negative (NaN aside): relu, or maximum with a
+  // scalar >= 0, followed at most by minimum with a scalar >= 0 (ReLU6)
+  bool nonneg = false;
+  for (int s = 0; s < epi->n_steps; ++s) {
+    const mira_epi_step& st = epi->steps[s];
+    const bool scalar = st.operand == MIRA_OPND_SCALAR;
+    if (st.op == MIRA_EPI_RELU) nonneg = true;
+    else if (st.op == MIRA_EPI_MAXIMUM && scalar && st.scalar >= 0.0f) nonneg = true;
+    else if (st.op == MIRA_EPI_MINIMUM && scalar && st.scalar >= 0.0f) nonneg = nonneg;
+    else nonneg = false;
+  }
+  p.nonneg = nonneg ? 1 : 0;
   const QuantScale q = make_qscale(epi->out_i8 != nullptr ? epi->out_scale : 1.0f);
   p.q_scale = q.s;
   p.q_rcp = q.rcp;
@@ -924,9 +948,15 @@ static int conv_setup(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t*
     const int64_t plane = n * (h + 2) * (w + 2);
     MIRA_CHECK_ARG(plane < (int64_t(1) << 31) - 256, "conv too large for the chunk-planar layout");
     p.M = int(plane);
+    p.dv_a = make_div((h + 2) * (w + 2));
+    p.dv_b = make_div(w + 2);
     p.g.guard = int(cp_guard(w));
     p.g.patch_slots = int(QG_BM + 2 * (w + 3));
     p.g.plane = plane;
+  } else {
+    // rows are output pixels: divisors for pixel -> (image, y, x) of a chunk-planar int8 output
+    p.dv_a = make_div(oh * ow);
+    p.dv_b = make_div(ow);
   }
   return set_i8_layout(p, epi, n, oh, ow);
 }

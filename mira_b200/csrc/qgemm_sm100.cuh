@@ -43,6 +43,16 @@ constexpr bool qg_a_by_tma(int amode) { return amode == QG_A_TMA || amode == QG_
 constexpr bool qg_a_patch(int amode) { return amode == QG_A_PATCH; }
 constexpr bool qg_a_async(int amode) { return qg_a_by_tma(amode) || qg_a_patch(amode); }
 
+// n / d for 0 <= n < 2^31 without a divide: q = (hi32(n * mul) + n) >> shr, with shr = ceil(log2 d)
+// and mul = floor(2^32 (2^shr - d) / d) + 1 computed on the host (the round-up multiplier method).
+struct QgDiv {
+  uint32_t mul, shr;
+};
+
+__device__ __forceinline__ int qg_div(int n, QgDiv d) {
+  return static_cast<int>((__umulhi(static_cast<uint32_t>(n), d.mul) + static_cast<uint32_t>(n)) >> d.shr);
+}
+
 struct QgConv {
   int n, h, w, cp;      // input NHWC (cp = padded channels)
   int oh, ow;
@@ -83,6 +93,12 @@ struct QgParams {
   // convolution's output (i8_cp = 1: slot guard + c16 * plane + padded pixel, i8_chunk = plane * 16)
   int i8_cp, i8_guard;
   int64_t i8_chunk;
+  // tile index math: divisors n_tiles and m_tiles * n_tiles; row mapping of convolutions: PATCH rows
+  // by (oh + 2)(ow + 2) and ow + 2, chunk-planar int8 output of other convs by oh * ow and ow
+  QgDiv dv_ntiles, dv_mntiles, dv_a, dv_b;
+  // the epilogue's last steps leave no negative value (relu, maximum with a scalar >= 0, then at
+  // most minimum with a scalar >= 0): requantization clamps from above only
+  int nonneg;
   int* err;
   // fused max pooling (POOL kernels only): window pool_p, stride pool_s, padding pool_pad holding
   // pool_pad_value; a tile is pool_t x pool_t pooled pixels whose conv inputs form a
@@ -176,7 +192,7 @@ __device__ __forceinline__ QgRow qg_row(const QgParams& p, int m) {
   QgRow r;
   if (AMODE == QG_A_PATCH) {
     const int pw = p.g.ow + 2, pimg = (p.g.oh + 2) * pw;
-    const int img = m / pimg, rem = m - img * pimg, yy = rem / pw, xx = rem - yy * pw;
+    const int img = qg_div(m, p.dv_a), rem = m - img * pimg, yy = qg_div(rem, p.dv_b), xx = rem - yy * pw;
     r.ok = m < p.M && yy >= 1 && yy <= p.g.oh && xx >= 1 && xx <= p.g.ow;
     r.pix = r.ok ? (static_cast<int64_t>(img) * p.g.oh + yy - 1) * p.g.ow + xx - 1 : 0;
     r.i8 = p.i8_cp ? (static_cast<int64_t>(p.i8_guard) + m) * 16 : r.pix * p.ld_i8;
@@ -186,7 +202,7 @@ __device__ __forceinline__ QgRow qg_row(const QgParams& p, int m) {
     r.i8 = static_cast<int64_t>(m) * p.ld_i8;
     if (p.i8_cp && r.ok) {
       const int hw = p.g.oh * p.g.ow;
-      const int img = m / hw, rem = m - img * hw, y = rem / p.g.ow, x = rem - y * p.g.ow;
+      const int img = qg_div(m, p.dv_a), rem = m - img * hw, y = qg_div(rem, p.dv_b), x = rem - y * p.g.ow;
       r.i8 = (static_cast<int64_t>(p.i8_guard) +
               (static_cast<int64_t>(img) * (p.g.oh + 2) + y + 1) * (p.g.ow + 2) + x + 1) * 16;
     }
@@ -262,8 +278,9 @@ __device__ __forceinline__ void qg_store_f32(const QgParams& p, const float (&v)
       int64_t pr;
       bool okr;
       if (MAPPED) {
-        pr = __shfl_sync(0xffffffffu, row.pix, rr);
-        okr = __shfl_sync(0xffffffffu, row.ok ? 1 : 0, rr) != 0;
+        // each lane left its row's pixel (-1: a padding slot) in the pad column of its staging row
+        pr = reinterpret_cast<const int*>(stage)[rr * PITCH + 16];
+        okr = pr >= 0;
       } else {
         pr = m_warp0 + rr;
         okr = pr < p.M;
@@ -362,15 +379,11 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
   tmem_ld_wait();
 
   float v[16];
-  uint32_t slow = 0;
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-    dequant4_x2(r + 4 * q, make_float4(hs[4 * q], hs[4 * q + 1], hs[4 * q + 2], hs[4 * q + 3]),
-                make_float4(ls[4 * q], ls[4 * q + 1], ls[4 * q + 2], ls[4 * q + 3]), v + 4 * q, slow, 4 * q);
-  if (__any_sync(0xffffffffu, slow != 0)) {   // rare: about 2 elements in 10^5
+  const bool exact = dequant16_x2(r, hs, ls, v);
+  if (__any_sync(0xffffffffu, !exact)) {   // rare: about 3 chunks in 10^4 have an element to redo
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      if (slow & (1u << j)) {
+      if (!exact) {
         const double s64 = ROWCOL ? static_cast<double>(row_ok ? p.row_scale[m] : 0.0f) *
                                         static_cast<double>((nb + j < p.N) ? p.col_scale[nb + j] : 0.0f)
                                   : p.scale64[nb + j];
@@ -403,7 +416,8 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
   if (out_f32 != nullptr) qg_store_f32<PITCH, MAPPED>(p, v, row, m_warp0, nb, full_chunk, stage, lane, out_f32);
   if (p.out_i8 != nullptr && row_ok && nb < p.ld_i8) {
     uint32_t b[16];
-    requant16_x2(v, p.q_scale, p.q_rcp, p.q_c127, b);
+    if (p.nonneg) requant_x2<16, true>(v, p.q_scale, p.q_rcp, p.q_c127, b);
+    else requant_x2<16, false>(v, p.q_scale, p.q_rcp, p.q_c127, b);
     if (!full_chunk) {
 #pragma unroll
       for (int j = 0; j < 16; ++j)
@@ -494,9 +508,10 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
         for (int kb = 0; kb < p.num_kb; ++kb) tma_load_2d(sB + kb * B_BYTES, &tmB, kb * BK, 0, bres);
       }
       for (int t = blockIdx.x, it = 0; t < num_tiles && ok; t += gridDim.x, ++it) {
-        const int split = t / mn_tiles, t_mn = t - split * mn_tiles;
-        const int m0 = (t_mn / p.n_tiles) * QG_BM;
-        const int n0 = (t_mn % p.n_tiles) * BN;
+        const int split = qg_div(t, p.dv_mntiles), t_mn = t - split * mn_tiles;
+        const int t_m = qg_div(t_mn, p.dv_ntiles);
+        const int m0 = t_m * QG_BM;
+        const int n0 = (t_mn - t_m * p.n_tiles) * BN;
         const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         if (AMODE == QG_A_PATCH) {
           // the tile's input halo: output slots m0 .. m0 + 127 read input slots m0 - (w + 3) ..
@@ -568,7 +583,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
         if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const int split = t / mn_tiles;
+        const int split = qg_div(t, p.dv_mntiles);
         const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         uint32_t halo = 0, plane_bytes = 0;
         int kbc = 1;
@@ -635,14 +650,15 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
       const int acc = it & 1;
       if (!mbar_wait(&tfull[acc], (it >> 1) & 1, abort_flag, QG_TIMEOUT_NS)) break;
       tc_fence_after();
-      const int split = t / mn_tiles, t_mn = t - split * mn_tiles;
-      const int t_m = t_mn / p.n_tiles;
-      const int n0 = (t_mn % p.n_tiles) * BN;
+      const int split = qg_div(t, p.dv_mntiles), t_mn = t - split * mn_tiles;
+      const int t_m = qg_div(t_mn, p.dv_ntiles);
+      const int n0 = (t_mn - t_m * p.n_tiles) * BN;
       float* out_f32 = p.out_f32 != nullptr ? p.out_f32 + split * p.split_stride : nullptr;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       if (!POOL) {
         const int m_warp0 = t_m * QG_BM + quarter * 32;
         const QgRow row = qg_row<AMODE>(p, m_warp0 + lane);
+        if (AMODE == QG_A_PATCH) reinterpret_cast<int*>(stage)[lane * Cfg::STAGE_PITCH + 16] = row.ok ? int(row.pix) : -1;
 #pragma unroll 1
         for (int c = group; c < BN / Cfg::CW; c += G) {
           const int nb = n0 + c * Cfg::CW;
