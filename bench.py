@@ -851,6 +851,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true", help="skip the parity check of the timed output")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM sweep of the headline line")
+    ap.add_argument("--fuse-pool", action="store_true",
+                    help="compute a conv whose only consumer is a max pool inside the pooling kernel")
     ap.add_argument("--profile-case", choices=PROFILE_CASES, default=None,
                     help="launch one kernel on a bounded case a few times (for ncu) and exit")
     args = ap.parse_args()
@@ -884,7 +886,7 @@ def main() -> None:
 
     t0 = time.perf_counter()
     prog = configs.compile_w8a8(args.workload, args.batch, "cuda", calib_batch=args.calib_batch, device=local,
-                                n_calib=wl["n_calib"], build_kw=wl["build_kw"] or None)
+                                n_calib=wl["n_calib"], build_kw=wl["build_kw"] or None, fuse_pool=args.fuse_pool)
     compile_s = time.perf_counter() - t0
     segs = [s for s in prog.segments if s.device == "cuda"]
     assert len(prog.segments) == 1 and len(segs) == 1, "the whole network must be one cuda segment"

@@ -361,6 +361,10 @@ static int launch_qgemm_patch(DeviceState* dev, const int8_t* wq, int64_t ldw, i
   if (rc != MIRA_CUDA_OK) return rc;
   switch (cp) {
     case 64:
+      // 18 warps (16 epilogue warps) cap ptxas at 96 registers and spill; without an f32 output the
+      // 8-warp epilogue (10 warps, no spills) is faster, with one the 16 warps hide the f32 stores
+      if (bn == 64 && p.n_tiles == 1 && p.out_f32 == nullptr)
+        return launch_qgemm_cfg<64, 1, QG_A_PATCH, false, 2, false, 64, 9, 16384>(dev, tmA, tmB, p);
       if (bn == 64 && p.n_tiles == 1)
         return launch_qgemm_cfg<64, 1, QG_A_PATCH, false, 4, false, 64, 9, 16384>(dev, tmA, tmB, p);
       if (bn == 64) return launch_qgemm_cfg<64, 8, QG_A_PATCH, false, 4, false, 64, 0, 16384>(dev, tmA, tmB, p);
@@ -437,6 +441,23 @@ static int fill_epilogue(QgParams& p, const mira_dequant* dq, const mira_epilogu
     else nonneg = false;
   }
   p.nonneg = nonneg ? 1 : 0;
+  // the fused step programs: [add channel] [add full] [relu | maximum scalar, minimum scalar]
+  {
+    const mira_epi_step* st = epi->steps;
+    const int n = epi->n_steps;
+    int i = 0, kind = 0;
+    if (i < n && st[i].op == MIRA_EPI_ADD && st[i].operand == MIRA_OPND_CHANNEL && i == 0) { kind |= QG_EPI_BIAS; ++i; }
+    if (i < n && st[i].op == MIRA_EPI_ADD && st[i].operand == MIRA_OPND_FULL && i == 1) { kind |= QG_EPI_RES; ++i; }
+    if (i < n && st[i].op == MIRA_EPI_RELU) {
+      kind |= QG_EPI_RELU;
+      ++i;
+    } else if (i + 1 < n && st[i].op == MIRA_EPI_MAXIMUM && st[i].operand == MIRA_OPND_SCALAR &&
+               st[i + 1].op == MIRA_EPI_MINIMUM && st[i + 1].operand == MIRA_OPND_SCALAR && i + 2 == n) {
+      kind |= QG_EPI_CLAMP;
+      i += 2;
+    }
+    p.epi_kind = (i == n && n > 0) ? kind : 0;
+  }
   const QuantScale q = make_qscale(epi->out_i8 != nullptr ? epi->out_scale : 1.0f);
   p.q_scale = q.s;
   p.q_rcp = q.rcp;
@@ -997,8 +1018,10 @@ extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, co
   rc = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, uint32_t(bn));
   if (rc != MIRA_CUDA_OK) return rc;
   if (x_layout == MIRA_LAYOUT_ROW4) {
-    if (bn == 64 && p.n_tiles == 1 && p.num_kb <= 2)   // the stem's weights stay in shared memory
-      return launch_qgemm_cfg<64, 7, QG_A_ROW4, false, 4, false, QG_BK, 2>(dev, tmA, tmB, p);
+    // the stem: weights resident in shared memory; 8 epilogue warps (with the 4 gather warps, 16
+    // epilogue warps would cap the registers at 80 and spill)
+    if (bn == 64 && p.n_tiles == 1 && p.num_kb <= 2)
+      return launch_qgemm_cfg<64, 7, QG_A_ROW4, false, 2, false, QG_BK, 2>(dev, tmA, tmB, p);
     return launch_qgemm_bn<QG_A_ROW4, false>(dev, tmA, tmB, p, bn);
   }
   if (cp == 4) return launch_qgemm_bn<QG_A_GATHER4, false>(dev, tmA, tmB, p, bn);
@@ -1061,9 +1084,9 @@ extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_
   std::memset(&tmA, 0, sizeof(tmA));
   rc = encode_2d_i8(&tmB, wq, uint64_t(ldw), uint64_t(o), uint64_t(ldw), QG_BK, 64u);
   if (rc != MIRA_CUDA_OK) return rc;
-  if (x_layout == MIRA_LAYOUT_ROW4) return launch_qgemm_cfg<64, 7, QG_A_ROW4, false, 4, true>(dev, tmA, tmB, p);
-  if (cp == 4) return launch_qgemm_cfg<64, 7, QG_A_GATHER4, false, 4, true>(dev, tmA, tmB, p);
-  return launch_qgemm_cfg<64, 7, QG_A_GATHER16, false, 4, true>(dev, tmA, tmB, p);
+  if (x_layout == MIRA_LAYOUT_ROW4) return launch_qgemm_cfg<64, 7, QG_A_ROW4, false, 2, true>(dev, tmA, tmB, p);
+  if (cp == 4) return launch_qgemm_cfg<64, 7, QG_A_GATHER4, false, 2, true>(dev, tmA, tmB, p);
+  return launch_qgemm_cfg<64, 7, QG_A_GATHER16, false, 2, true>(dev, tmA, tmB, p);
 }
 
 extern "C" int mira_cuda_maxpool2d_nhwc(const float* x_f32, const int8_t* x_i8, int64_t n, int64_t h, int64_t w,

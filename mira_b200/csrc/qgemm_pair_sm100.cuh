@@ -152,6 +152,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Qg2Cfg<BN, STAGES, G
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
+      // descriptors built once, moved by their start-address field (see qgemm_sm100_kernel)
+      constexpr uint32_t KU = QG_UMMA_K >> 4;
+      const uint64_t a_desc0 = smem_desc_k_sw128(smem_u32(sA)), b_desc0 = smem_desc_k_sw128(smem_u32(sB));
       for (int t = cluster; t < num_tiles && ok; t += clusters, ++it) {
         const int acc = it & 1;
         if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) break;
@@ -160,13 +163,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Qg2Cfg<BN, STAGES, G
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          const uint64_t a_d = a_desc0 + static_cast<uint64_t>(stage * (A_BYTES >> 4));
+          const uint64_t b_d = b_desc0 + static_cast<uint64_t>(stage * (B_BYTES >> 4));
           const int rem = p.K - kb * QG_BK;
-          const int nk = rem >= QG_BK ? QG_BK / QG_UMMA_K : (rem + QG_UMMA_K - 1) / QG_UMMA_K;
-          for (int kk = 0; kk < nk; ++kk)
-            mma_i8_pair(d_tmem, smem_desc_k_sw128(a_addr + kk * QG_UMMA_K), smem_desc_k_sw128(b_addr + kk * QG_UMMA_K),
-                        IDESC, (kb != 0 || kk != 0) ? 1u : 0u);
+          if (rem >= QG_BK) {
+#pragma unroll
+            for (int kk = 0; kk < QG_BK / QG_UMMA_K; ++kk)
+              mma_i8_pair(d_tmem, a_d + kk * KU, b_d + kk * KU, IDESC, (kb != 0 || kk != 0) ? 1u : 0u);
+          } else {
+            const int nk = (rem + QG_UMMA_K - 1) / QG_UMMA_K;
+            for (int kk = 0; kk < nk; ++kk)
+              mma_i8_pair(d_tmem, a_d + kk * KU, b_d + kk * KU, IDESC, (kb != 0 || kk != 0) ? 1u : 0u);
+          }
           mma_commit_pair_both(&empty[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }

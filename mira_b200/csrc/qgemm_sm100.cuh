@@ -99,6 +99,8 @@ struct QgParams {
   // the epilogue's last steps leave no negative value (relu, maximum with a scalar >= 0, then at
   // most minimum with a scalar >= 0): requantization clamps from above only
   int nonneg;
+  // a common step sequence run as one fused program (QG_EPI_* flags), 0: the general step loop
+  int epi_kind;
   int* err;
   // fused max pooling (POOL kernels only): window pool_p, stride pool_s, padding pool_pad holding
   // pool_pad_value; a tile is pool_t x pool_t pooled pixels whose conv inputs form a
@@ -128,15 +130,18 @@ __device__ __forceinline__ void pool_row_pixel(const QgParams& p, int t_m, int r
 template <int BN, int STAGES, int AMODE, int G, bool POOL = false, int BK = QG_BK, int RKB = 0, int PATCH = 0>
 struct QgCfg {
   static constexpr int A_BYTES = QG_BM * BK;
-  static constexpr int A_REGION = qg_a_patch(AMODE) ? 2 * PATCH : STAGES * A_BYTES;
   static constexpr int B_BYTES = BN * BK;
+  // TMEM accumulators in flight: the MMA warp can run that many tiles ahead of the epilogue (four
+  // when the tile width leaves room in the 512 columns; POOL kernels pair them with two pooling
+  // buffers)
+  static constexpr int ACCS = (!POOL && BN <= 128) ? 4 : 2;
   static constexpr int CW = 16;                       // epilogue chunk width (columns)
   static constexpr int EPI_WARP0 = 2;
   static constexpr int EPI_WARPS = 4 * G;
   static constexpr int GATHER_WARP0 = EPI_WARP0 + EPI_WARPS;
   static constexpr int THREADS = 32 * (GATHER_WARP0 + (qg_a_async(AMODE) ? 0 : 4));
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr uint32_t TMEM_COLS = ACCS * BN;
   // per epilogue warp: a 32-row x 16-column f32 staging block (row pitch 20 floats)
   static constexpr int STAGE_PITCH = 20;
   // POOL kernels instead keep two 128-row x BN conv-output tiles (row pitch BN + 4 floats)
@@ -144,13 +149,22 @@ struct QgCfg {
   static constexpr int POOL_ROWS = 96;
   static constexpr int STAGING_BYTES = POOL ? 2 * POOL_ROWS * POOL_PITCH * 4 : EPI_WARPS * 32 * STAGE_PITCH * 4;
   static constexpr int B_REGION = RKB > 0 ? RKB * B_BYTES : STAGES * B_BYTES;
-  // the barrier region after the staging: 2 * STAGES + 12 mbarriers, the TMEM address, the abort flag
-  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 12) + 8 <= 256 ? 256 : 512;
-  static constexpr size_t SMEM = 1024 + size_t(A_REGION) + B_REGION + STAGING_BYTES + BAR_BYTES;
+  // the barrier region after the staging: the stage, accumulator and halo barriers, drain, pool,
+  // resident-B, then the TMEM address and the abort flag
+  static constexpr int NBAR = 2 * STAGES + 2 * ACCS + 2 * 6 + 4;
+  static constexpr int BAR_BYTES = 8 * NBAR + 8 <= 256 ? 256 : 512;
+  static constexpr int FIXED_BYTES = 1024 + B_REGION + STAGING_BYTES + BAR_BYTES;
+  // PATCH: halo buffers in flight (the producer fetches up to NHALO - 1 tiles ahead of the MMAs),
+  // as many as shared memory leaves room for, at most 6
+  static constexpr int NHALO_FIT = PATCH > 0 ? (232448 - FIXED_BYTES) / PATCH : 0;
+  static constexpr int NHALO = NHALO_FIT > 6 ? 6 : NHALO_FIT;
+  static constexpr int A_REGION = qg_a_patch(AMODE) ? NHALO * PATCH : STAGES * A_BYTES;
+  static constexpr size_t SMEM = size_t(FIXED_BYTES) + A_REGION;
   static_assert(!POOL || (AMODE != 0 && BN == 64), "fused pooling: convolutions with at most 64 channels");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(8 * (2 * STAGES + 12) + 8 <= BAR_BYTES, "barrier region");
+  static_assert(8 * NBAR + 8 <= BAR_BYTES, "barrier region");
+  static_assert(!qg_a_patch(AMODE) || NHALO >= 2, "at least two halo buffers");
   static_assert(BK == 128 || (BK == 64 && (AMODE == QG_A_IM2COL || AMODE == QG_A_PATCH)),
                 "64-byte K-blocks: convolutions with 64-channel inputs only");
   static_assert(qg_a_patch(AMODE) == (PATCH > 0) && PATCH % 1024 == 0, "halo buffers: PATCH mode only");
@@ -176,6 +190,12 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 }
 
 // ---------------------------------------------------------------- epilogue (one 16-column chunk)
+
+// Fused programs for the step sequences the networks use, in the order they run: add of a
+// per-channel operand (steps[0]), add of a full operand (steps[1]), relu, or maximum then minimum
+// with scalars (ReLU6, the last two steps).  The same IEEE operations in the same order as the
+// general loop, without its per-step dispatch.
+enum : int { QG_EPI_BIAS = 1, QG_EPI_RES = 2, QG_EPI_RELU = 4, QG_EPI_CLAMP = 8 };
 
 // Where GEMM row m of a tile goes: the f32 row (output pixel; operands with rows are read there
 // too), the byte offset of its int8 output row, and whether the row exists.  Plain GEMMs and the
@@ -359,20 +379,26 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
       split_rowcol(rs, cs, hs[j], ls[j]);
     }
   }
-  // one operand that reads memory is fetched before the accumulator so its latency overlaps the
-  // TMEM read: a full-tensor operand (a residual in DRAM) if there is one, else the first
-  // per-channel or per-row one
+  // operands that read memory are fetched before the accumulator so their latency overlaps the
+  // TMEM read: for a fused program its bias and residual, for the general loop one full-tensor
+  // operand (a residual in DRAM) if there is one, else the first per-channel or per-row one
+  const int kind = p.epi_kind;
   int mem0 = -1;
-  for (int s = 0; s < p.n_steps; ++s) {
-    const int kind = p.steps[s].operand;
-    if (kind == MIRA_OPND_FULL) {
-      mem0 = s;
-      break;
+  float o0[16], o1[16];
+  if (kind != 0) {
+    if (kind & QG_EPI_BIAS) ld16(p.steps[0].ptr + nb, o0);
+    if (kind & QG_EPI_RES) qg_operand(p, p.steps[1], m, row_ok, nb, full_chunk, o1);
+  } else {
+    for (int s = 0; s < p.n_steps; ++s) {
+      const int opnd = p.steps[s].operand;
+      if (opnd == MIRA_OPND_FULL) {
+        mem0 = s;
+        break;
+      }
+      if (mem0 < 0 && (opnd == MIRA_OPND_CHANNEL || opnd == MIRA_OPND_ROW)) mem0 = s;
     }
-    if (mem0 < 0 && (kind == MIRA_OPND_CHANNEL || kind == MIRA_OPND_ROW)) mem0 = s;
+    if (mem0 >= 0) qg_operand(p, p.steps[mem0], m, row_ok, nb, full_chunk, o0);
   }
-  float o0[16];
-  if (mem0 >= 0) qg_operand(p, p.steps[mem0], m, row_ok, nb, full_chunk, o0);
 
   uint32_t r[16];
   tmem_ld_32x32b_x16(taddr, r);
@@ -392,7 +418,26 @@ __device__ __forceinline__ void qg_epilogue_chunk(const QgParams& p, uint32_t ta
     }
   }
 
-  for (int s = 0; s < p.n_steps; ++s) {
+  if (kind != 0) {
+    if (kind & QG_EPI_BIAS) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) f2_split(f2_add(f2(v[j], v[j + 1]), f2(o0[j], o0[j + 1])), v[j], v[j + 1]);
+    }
+    if (kind & QG_EPI_RES) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) f2_split(f2_add(f2(v[j], v[j + 1]), f2(o1[j], o1[j + 1])), v[j], v[j + 1]);
+    }
+    if (kind & QG_EPI_RELU) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = np_maximum(v[j], 0.0f);
+    }
+    if (kind & QG_EPI_CLAMP) {
+      const float lo = p.steps[p.n_steps - 2].scalar, hi = p.steps[p.n_steps - 1].scalar;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = np_minimum(np_maximum(v[j], lo), hi);
+    }
+  }
+  for (int s = 0; kind == 0 && s < p.n_steps; ++s) {
     const mira_epi_step& st = p.steps[s];
     if (st.operand == MIRA_OPND_NONE) {
       if (st.op == MIRA_EPI_RELU) {
@@ -449,13 +494,13 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(staging) + Cfg::STAGING_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* tempty = tfull + Cfg::ACCS;
+  uint64_t* drain = tempty + Cfg::ACCS;
   uint64_t* pool_bar = drain + 1;   // [2]: all epilogue threads wrote the tile buffer
   uint64_t* bres = pool_bar + 2;    // resident B landed (RKB > 0)
-  uint64_t* pfull = bres + 1;       // [2]: a halo buffer landed (PATCH)
-  uint64_t* pempty = pfull + 2;     // [2]: the MMAs reading a halo buffer finished (PATCH)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pempty + 2);
+  uint64_t* pfull = bres + 1;       // [NHALO]: a halo buffer landed (PATCH)
+  uint64_t* pempty = pfull + 6;     // [NHALO]: the MMAs reading a halo buffer finished (PATCH)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pempty + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -466,7 +511,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
       mbar_init(&full[s], qg_a_async(AMODE) ? 1 : 1 + 128);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < Cfg::ACCS; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], Cfg::EPI_THREADS);
     }
@@ -474,7 +519,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
     mbar_init(&pool_bar[0], Cfg::EPI_THREADS);
     mbar_init(&pool_bar[1], Cfg::EPI_THREADS);
     mbar_init(bres, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < Cfg::NHALO; ++b) {
       mbar_init(&pfull[b], 1);
       mbar_init(&pempty[b], 1);
     }
@@ -516,8 +561,8 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
         if (AMODE == QG_A_PATCH) {
           // the tile's input halo: output slots m0 .. m0 + 127 read input slots m0 - (w + 3) ..
           // m0 + 127 + (w + 3) of every chunk plane (guards and padding ring are zero)
-          const int pb = it & 1;
-          if (!mbar_wait(&pempty[pb], ((it >> 1) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
+          const int pb = it % Cfg::NHALO;
+          if (!mbar_wait(&pempty[pb], ((it / Cfg::NHALO) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
           const uint32_t pbytes = static_cast<uint32_t>(p.g.patch_slots) * 16u;
           const int planes = p.g.cp >> 4;
           mbar_arrive_expect_tx(&pfull[pb], planes * pbytes);
@@ -561,9 +606,9 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
           const int idx = issued - i;
           mbar_wait_drain(&full[idx % STAGES], (idx / STAGES) & 1);
         }
-        for (int i = 1; i <= 2 && i <= patches; ++i) {
+        for (int i = 1; i <= Cfg::NHALO && i <= patches; ++i) {
           const int idx = patches - i;
-          mbar_wait_drain(&pfull[idx & 1], (idx >> 1) & 1);
+          mbar_wait_drain(&pfull[idx % Cfg::NHALO], (idx / Cfg::NHALO) & 1);
         }
       }
       if (RKB > 0 && blockIdx.x < num_tiles) mbar_wait_drain(bres, 0);
@@ -578,61 +623,85 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
       if (RKB > 0 && blockIdx.x < num_tiles && !mbar_wait(bres, 0, abort_flag, QG_TIMEOUT_NS)) ok = false;
       // PATCH mode with resident weights waits on nothing per K-block: the halo and B are in place
       constexpr bool kStaged = !(AMODE == QG_A_PATCH && RKB > 0);
+      // The operand descriptors are built once: a stage, a K step or a tap shift only moves the start
+      // address field (16-byte units in the low 14 bits; shared addresses stay below 256 KB, so no
+      // carry leaves the field), so each MMA costs one add per operand.  A single thread issues every
+      // MMA, and rebuilding both descriptors per instruction made its dependent integer chain, not the
+      // tensor pipe, the limit of the main loop.
+      constexpr uint32_t KU = QG_UMMA_K >> 4;   // one MMA's K step (32 bytes) in 16-byte units
+      const uint64_t b_desc0 = BK == 64 ? smem_desc_k_sw64(smem_u32(sB)) : smem_desc_k_sw128(smem_u32(sB));
+      const uint64_t a_desc0 =
+          qg_a_patch(AMODE) ? smem_desc_k_none(smem_u32(sA), static_cast<uint32_t>(p.g.patch_slots) * 16u, 128)
+                            : (BK == 64 ? smem_desc_k_sw64(smem_u32(sA)) : smem_desc_k_sw128(smem_u32(sA)));
+      // PATCH: the slot shift of each tap and one halo plane, in descriptor units (16-byte slots)
+      uint32_t tap_u[9];
+      uint32_t plane_u = 0;
+      int kbc = 1;
+      if (AMODE == QG_A_PATCH) {
+#pragma unroll
+        for (int tp = 0; tp < 9; ++tp)
+          tap_u[tp] = static_cast<uint32_t>(p.g.ow + 3 + (tp / 3 - 1) * (p.g.ow + 2) + (tp % 3 - 1));
+        plane_u = static_cast<uint32_t>(p.g.patch_slots);
+        kbc = p.g.cp / BK;
+      }
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
-        const int acc = it & 1;
-        if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) break;
+        const int acc = it % Cfg::ACCS;
+        if (!mbar_wait(&tempty[acc], ((it / Cfg::ACCS) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const int split = qg_div(t, p.dv_mntiles);
-        const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
-        uint32_t halo = 0, plane_bytes = 0;
-        int kbc = 1;
         if (AMODE == QG_A_PATCH) {
-          if (!mbar_wait(&pfull[it & 1], (it >> 1) & 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
+          // K-block (tap, cb) = channels [cb * BK, cb * BK + BK) of tap (tap / 3, tap % 3): the A rows
+          // are the halo's slots shifted by the tap, each 16-channel chunk one plane of the halo
+          const int hb = it % Cfg::NHALO;
+          if (!mbar_wait(&pfull[hb], (it / Cfg::NHALO) & 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
           tc_fence_after();
-          halo = smem_u32(sA + (it & 1) * PATCH);
-          plane_bytes = static_cast<uint32_t>(p.g.patch_slots) * 16u;
-          kbc = p.g.cp / BK;
-        }
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (kStaged) {
+          const uint64_t halo_d = a_desc0 + static_cast<uint64_t>(hb) * (PATCH >> 4);
+          uint32_t accum = 0;
+#pragma unroll
+          for (int tp = 0; tp < 9; ++tp) {
+            for (int cb = 0; cb < kbc && ok; ++cb) {
+              const int kb = tp * kbc + cb;
+              if (kStaged) {
+                if (!mbar_wait(&full[stage], phase, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
+                tc_fence_after();
+              }
+              const uint64_t a_d = halo_d + tap_u[tp] + static_cast<uint64_t>(cb * (BK >> 4)) * plane_u;
+              const uint64_t b_d = b_desc0 + static_cast<uint64_t>((RKB > 0 ? kb : stage) * (B_BYTES >> 4));
+#pragma unroll
+              for (int kk = 0; kk < BK / QG_UMMA_K; ++kk) {
+                mma_i8(d_tmem, a_d + static_cast<uint64_t>(kk * KU) * plane_u, b_d + kk * KU, IDESC, accum);
+                accum = 1;
+              }
+              if (kStaged) {
+                mma_commit(&empty[stage]);
+                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+              }
+            }
+          }
+          if (ok) mma_commit(&pempty[hb]);
+        } else {
+          const int split = qg_div(t, p.dv_mntiles);
+          const int kb0 = split * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+          for (int kb = kb0; kb < kb1; ++kb) {
             if (!mbar_wait(&full[stage], phase, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
             if (!qg_a_async(AMODE)) fence_proxy_async_smem();  // A was written by cp.async (generic proxy)
             tc_fence_after();
-          }
-          const uint32_t b_addr = smem_u32(sB + (RKB > 0 ? kb : stage) * B_BYTES);
-          if (AMODE == QG_A_PATCH) {
-            // K-block kb = channels [cb * BK, cb * BK + BK) of tap (ti, tj): the A rows are the halo's
-            // slots shifted by the tap, each 16-channel chunk one plane of the halo
-            const int tap = kb / kbc, cb = kb - tap * kbc;
-            const int ti = tap / 3, tj = tap - ti * 3;
-            const uint32_t a_addr =
-                halo + static_cast<uint32_t>(p.g.ow + 3 + (ti - 1) * (p.g.ow + 2) + (tj - 1)) * 16u;
-#pragma unroll
-            for (int kk = 0; kk < BK / QG_UMMA_K; ++kk) {
-              const uint32_t chunk = static_cast<uint32_t>((cb * BK + kk * QG_UMMA_K) >> 4);
-              const uint32_t bo = b_addr + kk * QG_UMMA_K;
-              mma_i8(d_tmem, smem_desc_k_none(a_addr + chunk * plane_bytes, plane_bytes, 128),
-                     BK == 64 ? smem_desc_k_sw64(bo) : smem_desc_k_sw128(bo), IDESC,
-                     (kb != kb0 || kk != 0) ? 1u : 0u);
-            }
-          } else {
-            const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+            const uint64_t a_d = a_desc0 + static_cast<uint64_t>(stage * (A_BYTES >> 4));
+            const uint64_t b_d = b_desc0 + static_cast<uint64_t>((RKB > 0 ? kb : stage) * (B_BYTES >> 4));
             const int rem = p.K - kb * BK;
-            const int nk = rem >= BK ? BK / QG_UMMA_K : (rem + QG_UMMA_K - 1) / QG_UMMA_K;
-            for (int kk = 0; kk < nk; ++kk) {
-              const uint32_t ao = a_addr + kk * QG_UMMA_K, bo = b_addr + kk * QG_UMMA_K;
-              mma_i8(d_tmem, BK == 64 ? smem_desc_k_sw64(ao) : smem_desc_k_sw128(ao),
-                     BK == 64 ? smem_desc_k_sw64(bo) : smem_desc_k_sw128(bo),
-                     IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
+            if (rem >= BK) {
+#pragma unroll
+              for (int kk = 0; kk < BK / QG_UMMA_K; ++kk)
+                mma_i8(d_tmem, a_d + kk * KU, b_d + kk * KU, IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
+            } else {
+              const int nk = (rem + QG_UMMA_K - 1) / QG_UMMA_K;
+              for (int kk = 0; kk < nk; ++kk)
+                mma_i8(d_tmem, a_d + kk * KU, b_d + kk * KU, IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
             }
-          }
-          if (kStaged) {
             mma_commit(&empty[stage]);
             if (++stage == STAGES) { stage = 0; phase ^= 1; }
           }
         }
-        if (AMODE == QG_A_PATCH && ok) mma_commit(&pempty[it & 1]);
         if (ok) mma_commit(&tfull[acc]);
       }
       // every MMA issued by this thread has finished once `drain` completes
@@ -647,8 +716,8 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
     float* stage = staging + ew * 32 * Cfg::STAGE_PITCH;
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-      const int acc = it & 1;
-      if (!mbar_wait(&tfull[acc], (it >> 1) & 1, abort_flag, QG_TIMEOUT_NS)) break;
+      const int acc = it % Cfg::ACCS;
+      if (!mbar_wait(&tfull[acc], (it / Cfg::ACCS) & 1, abort_flag, QG_TIMEOUT_NS)) break;
       tc_fence_after();
       const int split = qg_div(t, p.dv_mntiles), t_mn = t - split * mn_tiles;
       const int t_m = qg_div(t_mn, p.dv_ntiles);
