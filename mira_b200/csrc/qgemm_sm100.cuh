@@ -657,8 +657,21 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
           tc_fence_after();
           const uint64_t halo_d = a_desc0 + static_cast<uint64_t>(hb) * (PATCH >> 4);
           uint32_t accum = 0;
+          if (RKB > 0 && BK == 64) {
+            // one 64-channel K-block per tap, weights resident: the tile's 18 MMAs as straight-line
+            // code, each operand one add away from a per-CTA constant
 #pragma unroll
-          for (int tp = 0; tp < 9; ++tp) {
+            for (int tp = 0; tp < 9; ++tp) {
+#pragma unroll
+              for (int kk = 0; kk < BK / QG_UMMA_K; ++kk) {
+                mma_i8(d_tmem, halo_d + tap_u[tp] + kk * KU * plane_u,
+                       b_desc0 + static_cast<uint64_t>(tp * (B_BYTES >> 4) + kk * KU), IDESC, accum);
+                accum = 1;
+              }
+            }
+          }
+#pragma unroll
+          for (int tp = 0; tp < 9 && !(RKB > 0 && BK == 64); ++tp) {
             for (int cb = 0; cb < kbc && ok; ++cb) {
               const int kb = tp * kbc + cb;
               if (kStaged) {
