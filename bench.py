@@ -374,7 +374,8 @@ def gemm_sweep(peak_tops: float | None) -> dict:
                     "seeded; operand sets cycled (more than twice L2 between reuses)"}
 
 
-PROFILE_CASES = ("gemm8192", "conv_l1", "conv_l1_cp", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "maxpool_stem",
+PROFILE_CASES = ("gemm8192", "conv_l1", "conv_l1_cp", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "stem_pool",
+                 "maxpool_stem",
                  "decode_step", "attention_prefill", "layernorm_decode", "layernorm_prefill")
 
 
@@ -389,6 +390,8 @@ def profile_case(name: str, reps: int = 3) -> None:
       quantize_rows the transformer's activation quantization, 65536 x 768 f32 -> int8
       stem          ResNet-18's stem: NCHW f32 64 x 3 x 224 x 224 quantized into the row-expanded layout,
                     then the 7x7/2 conv to 64 channels, bias + relu, f32 out (205 MB)
+      stem_pool     ResNet-18's stem conv fused with its max pool (one kernel), 64 images, pooled f32 and
+                    chunk-planar int8 out
       maxpool_stem  ResNet-18's -inf pad + 3x3/2 max pool on the stem output, 64 x 112 x 112 x 64 f32,
                     f32 and int8 out
       decode_step   `reps` eager steps of the config-5 decode (batch 64, 1024-row caches): every
@@ -483,6 +486,24 @@ def profile_case(name: str, reps: int = 3) -> None:
             K.quantize_nchw_to_row4(x, n, 3, h, h, 0.03, xq, entries, 3, 2)
             K.qconv2d(n, h, h, 4, xq, o, 7, 7, wb, wq.shape[1], (2, 2), (3, 3), (1, 1), K.dequant_channel(*keep), epi,
                       layout=_lib.LAYOUT_ROW4, row_entries=entries)
+    elif name == "stem_pool":
+        n, h, o = 64, 224, 64
+        x = DB.from_array(rng.standard_normal((n, 3, h, h), dtype=np.float32))
+        ow = (h + 2 * 3 - 7) // 2 + 1
+        ph = (ow + 2 - 3) // 2 + 1
+        entries = K.row4_entries(ow, 2)
+        xq = DB(n * h * entries * 16)
+        wq = K.conv_weight_row4(rng.integers(-127, 128, (o, 3, 7, 7)).astype(np.int8))
+        keep = [DB.from_array(a) for a in K.scale_arrays(0.03, rng.uniform(1e-3, 1e-2, o).astype(np.float32))]
+        bias = DB.from_array(K.pad_channels(rng.standard_normal(o).astype(np.float32)))
+        y, yq = DB(n * ph * ph * o * 4), DB(K.cp_bytes(n, ph, ph, o), zero=True)
+        epi = K.Epi([K.Step("add", "channel", ptr=bias), K.Step("relu")], out_f32=y, ld_f32=o, out_i8=yq, ld_i8=o,
+                    out_scale=0.05, i8_layout=_lib.LAYOUT_CP)
+        wb = DB.from_array(wq)
+        K.quantize_nchw_to_row4(x, n, 3, h, h, 0.03, xq, entries, 3, 2)
+        for _ in range(reps):
+            K.qconv2d_maxpool(n, h, h, 4, xq, o, 7, 7, wb, wq.shape[1], (2, 2), (3, 3), (1, 1), 3, 2, 1, -np.inf,
+                              K.dequant_channel(*keep), epi, layout=_lib.LAYOUT_ROW4, row_entries=entries)
     elif name == "attention_prefill":
         b0, b1, t, dh = 8, 12, 1024, 64
         q, k, v = (DB.from_array(rng.standard_normal((b0, b1, t, dh), dtype=np.float32)) for _ in range(3))

@@ -16,6 +16,7 @@
 #include "memory_bound.cuh"
 #include "qgemm_sm100.cuh"
 #include "qgemm_pair_sm100.cuh"
+#include "stem_pool_sm100.cuh"
 #include "runtime.h"
 #include "sequence_ops.cuh"
 
@@ -1028,6 +1029,59 @@ extern "C" int mira_cuda_qconv2d(int64_t n, int64_t h, int64_t w, int64_t cp, co
   return launch_qgemm_bn<QG_A_GATHER16, false>(dev, tmA, tmB, p, bn);
 }
 
+// The stem + pool kernel (stem_pool_sm100.cuh).  Work units are (image, band of pooled rows); the
+// band is chosen so that the units fill whole waves of CTAs with the fewest conv rows computed twice
+// (each band recomputes the conv row it shares with the band above).
+static int launch_stem_pool(DeviceState* dev, const QgParams& qp, int64_t n, int64_t h, int64_t w, int64_t oh,
+                            int64_t ow, int64_t ph, int64_t pw, int64_t kh, int64_t pad_h, int64_t row_entries,
+                            int64_t o, const int8_t* x, const int8_t* wq, int64_t ldw, const mira_epilogue* epi) {
+  MIRA_CHECK_ARG(qp.out_f32 == nullptr || (qp.ld_f32 % 4 == 0 && (reinterpret_cast<uintptr_t>(qp.out_f32) & 15) == 0),
+                 "pooled f32 output: rows of a multiple of 4 floats, 16-byte aligned");
+  MIRA_CHECK_ARG(qp.out_i8 == nullptr || (qp.ld_i8 % 4 == 0 && qp.ld_i8 >= o), "pooled int8 output rows");
+  if (n == 0) return MIRA_CUDA_OK;
+  SpParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.n = int(n); p.h = int(h); p.w = int(w);
+  p.oh = int(oh); p.ow = int(ow); p.ph = int(ph); p.pw = int(pw);
+  p.kh = int(kh); p.pad_h = int(pad_h); p.row_entries = int(row_entries); p.o = int(o);
+  int64_t best_cost = -1;
+  for (int b = 1; b <= 8; ++b) {
+    const int64_t units = n * ((ph + b - 1) / b);
+    const int64_t cost = ((units + dev->sm_count - 1) / dev->sm_count) * (2 * b + 1);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      p.band = b;
+    }
+  }
+  p.bands = int((ph + p.band - 1) / p.band);
+  MIRA_CHECK_ARG(n * p.bands < (int64_t(1) << 31), "too many work units");
+  p.x = x; p.wq = wq; p.ldw = ldw;
+  p.scale64 = qp.scale64; p.scale_hi = qp.scale_hi; p.scale_lo = qp.scale_lo;
+  p.epi_kind = qp.epi_kind; p.n_steps = qp.n_steps;
+  for (int s = 0; s < qp.n_steps; ++s) p.steps[s] = qp.steps[s];
+  p.out_f32 = qp.out_f32; p.ld_f32 = qp.ld_f32;
+  p.out_i8 = qp.out_i8; p.ld_i8 = qp.ld_i8;
+  if (qp.out_i8 != nullptr && epi->i8_layout == MIRA_LAYOUT_CP) {
+    MIRA_CHECK_ARG(qp.ld_i8 % 16 == 0, "chunk-planar int8 output: padded channel count a multiple of 16");
+    p.i8_cp = 1;
+    p.i8_guard = int(cp_guard(pw));
+    p.i8_chunk = n * (ph + 2) * (pw + 2) * 16;
+  }
+  p.q_scale = qp.q_scale; p.q_rcp = qp.q_rcp; p.q_c127 = qp.q_c127; p.nonneg = qp.nonneg;
+  p.err = qp.err;
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[dev->device]) {
+    MIRA_CUDA_TRY(cudaFuncSetAttribute(stem_pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(SpSmem::TOTAL)),
+                  "cudaFuncSetAttribute(stem_pool smem)");
+    attr_set[dev->device] = true;
+  }
+  const int64_t units = n * p.bands;
+  const int grid = int(units < dev->sm_count ? units : dev->sm_count);
+  stem_pool_kernel<<<grid, SP_THREADS, SpSmem::TOTAL, dev->stream>>>(p);
+  return after_launch("stem_pool_kernel");
+}
+
 extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_t cp, const int8_t* x,
                                          int64_t x_layout, int64_t x_row_entries, int64_t o, int64_t kh, int64_t kw,
                                          const int8_t* wq, int64_t ldw, int64_t stride_h, int64_t stride_w,
@@ -1041,8 +1095,6 @@ extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_
                       dil_w, dq, epi, p, oh, ow);
   if (rc != MIRA_CUDA_OK) return rc;
   MIRA_CHECK_ARG(o <= 64, "fused pooling supports convolutions with at most 64 output channels");
-  MIRA_CHECK_ARG(x_layout != MIRA_LAYOUT_CP && (epi->out_i8 == nullptr || epi->i8_layout == MIRA_LAYOUT_NHWC),
-                 "fused pooling reads and writes the NHWC / row-expanded layouts");
   MIRA_CHECK_ARG(pool_size > 0 && pool_stride > 0 && pool_pad >= 0 && pool_pad < pool_size, "bad pool geometry");
   // the kernel pools the int32 accumulators and applies the epilogue to the pooled values, which
   // equals pooling the epilogue's outputs when every step is monotone non-decreasing in its input
@@ -1060,6 +1112,12 @@ extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_
   const int64_t ph = (oh + 2 * pool_pad - pool_size) / pool_stride + 1;
   const int64_t pw = (ow + 2 * pool_pad - pool_size) / pool_stride + 1;
   MIRA_CHECK_ARG(ph > 0 && pw > 0, "pool window larger than the conv output");
+  // the ResNet stem form (row-expanded input, stride 2, 3x3/2 pool with one pixel of padding)
+  if (x_layout == MIRA_LAYOUT_ROW4 && stride_h == 2 && stride_w == 2 && kh <= SP_KH_MAX && pool_size == 3 &&
+      pool_stride == 2 && pool_pad == 1 && ow <= SP_OW_MAX && x_row_entries <= SP_PLANE / 16 && o % 4 == 0)
+    return launch_stem_pool(dev, p, n, h, w, oh, ow, ph, pw, kh, pad_h, x_row_entries, o, x, wq, ldw, epi);
+  MIRA_CHECK_ARG(x_layout != MIRA_LAYOUT_CP && (epi->out_i8 == nullptr || epi->i8_layout == MIRA_LAYOUT_NHWC),
+                 "fused pooling reads and writes the NHWC / row-expanded layouts");
   int T = 0;
   for (int t = 1; t <= 16; ++t) {
     const int64_t span = (t - 1) * pool_stride + pool_size;

@@ -79,6 +79,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// The same bounded wait without the suspend hint: for short waits on a barrier that completes
+// within a few hundred cycles (a warp group meeting), where being woken from suspension costs more
+// than spinning.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ TMA (no multicast anywhere)
 
 // im2col load of a 4-D NHWC tensor: the pixels of one tap for pixelsPerColumn consecutive output

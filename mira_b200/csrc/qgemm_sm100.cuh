@@ -157,7 +157,7 @@ struct QgCfg {
   // PATCH: halo buffers in flight (the producer fetches up to NHALO - 1 tiles ahead of the MMAs),
   // as many as shared memory leaves room for, at most 6
   static constexpr int NHALO_FIT = PATCH > 0 ? (232448 - FIXED_BYTES) / PATCH : 0;
-  static constexpr int NHALO = NHALO_FIT > 6 ? 6 : NHALO_FIT;
+  static constexpr int NHALO = PATCH == 0 ? 1 : (NHALO_FIT > 6 ? 6 : NHALO_FIT);
   static constexpr int A_REGION = qg_a_patch(AMODE) ? NHALO * PATCH : STAGES * A_BYTES;
   static constexpr size_t SMEM = size_t(FIXED_BYTES) + A_REGION;
   static_assert(!POOL || (AMODE != 0 && BN == 64), "fused pooling: convolutions with at most 64 channels");

@@ -439,8 +439,9 @@ class Plan:
                 src = pad_op.inputs[0]
             conv = src.producer
             pad_ok = op not in self.pad_into_pool or self.pad_into_pool[op][2] == float("-inf")
-            if (self.fuse_pool and pad_ok and conv is not None and conv.kind == "qconv2d"
-                    and len(users.get(src, [])) == 1 and src not in g.outputs and self._conv_pool_fusable(conv)):
+            if (pad_ok and conv is not None and conv.kind == "qconv2d" and len(users.get(src, [])) == 1
+                    and src not in g.outputs and self._conv_pool_fusable(conv)
+                    and (self.fuse_pool or self._stem_pool(conv, op))):
                 self.conv_into_pool[op] = conv
                 self.skipped.add(conv)
         fused_convs = set(self.conv_into_pool.values())
@@ -485,7 +486,9 @@ class Plan:
         if v.type.rank != 4 or v not in self.image_values:
             return False
         p = v.producer
-        if p is None or p.kind not in ("qconv2d", "maxpool2d") or p in self.skipped or p in self.conv_into_pool:
+        if p is None or p.kind not in ("qconv2d", "maxpool2d") or p in self.skipped:
+            return False
+        if p in self.conv_into_pool and not self._stem_pool(self.conv_into_pool[p], p):
             return False
         n, c, h, w = v.type.shape
         if c % 64 or not K.patch_preferred(c, w):
@@ -618,6 +621,22 @@ class Plan:
             else:
                 return None
         return tuple(sig)
+
+    def _stem_pool(self, conv, pool) -> bool:
+        """The conv + pool pair has the form of the stem kernel (libmira_cuda stem_pool_kernel, always
+        fused): a stride-2 conv reading the row-expanded layout of a graph input of at most 4
+        channels, at most 8 x 8 taps, 64 or fewer output channels (a multiple of 4), an output row of
+        at most 128 pixels, then a 3x3/2 max pool over one pixel of -inf padding."""
+        stride, padding, dilation, groups = conv_attrs(conv.attrs)
+        o, _, kh, kw = np.asarray(conv.attrs["q"]).shape
+        x = conv.inputs[0]
+        if (groups != 1 or tuple(stride) != (2, 2) or tuple(dilation) != (1, 1) or kh > 8 or kw > 8 or o > 64 or o % 4
+                or conv.result.type.shape[3] > 128 or x.type.rank != 4 or x.type.shape[1] > 4
+                or x.producer is not None or self._row4_geometry(x) is None):
+            return False
+        if pool.attrs["size"] != 3 or pool.attrs["stride"] != 2:
+            return False
+        return pool in self.pad_into_pool and self.pad_into_pool[pool][1] == 1
 
     def _conv_pool_fusable(self, conv) -> bool:
         """A qconv2d whose only consumer is a max pool can run inside the pooling kernel when it has
@@ -1071,6 +1090,7 @@ class Plan:
         epi.out_f32, epi.ld_f32 = out.f32, out.cols
         epi.out_i8, epi.ld_i8 = out.i8, out.i8_ld
         epi.out_scale = out.i8_scale if out.i8 is not None else 1.0
+        epi.i8_layout = _lib.LAYOUT_CP if out.i8_layout == "cp" else _lib.LAYOUT_NHWC
         self._launch("qconv2d_pool", n=n, h=h, w=w, cp=cp, x=xi8, layout=layout, row_entries=entries, o=o, kh=kh,
                      kw=kw, wq=self._upload(wq),
                      ldw=wq.shape[1], stride=stride, padding=padding, dilation=dilation,

@@ -268,9 +268,8 @@ class FakeDevice:
         if epi.out_f32 is not None:
             epi.out_f32.view(np.float32, (n * ph * pw, epi.ld_f32))[:, :o] = flat
         if epi.out_i8 is not None:
-            q = epi.out_i8.view(np.int8, (n * ph * pw, epi.ld_i8))
-            q[:, :o] = ref.quantize_activation(flat, epi.out_scale)
-            q[:, o:] = 0
+            self._put_i8(epi.out_i8, ref.quantize_activation(flat, epi.out_scale), epi.ld_i8, epi.i8_layout,
+                         (n, ph, pw))
 
     def _maxpool(self, n, h, w, c, ldc, size, stride, pad, pad_value, x_f32=None, x_i8=None, out_f32=None, ldo=0,
                  out_i8=None, ldo_i8=0, scale=1.0, i8_layout=0):

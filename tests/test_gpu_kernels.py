@@ -698,3 +698,58 @@ def test_maxpool_chunk_planar_int8_output(cuda_device):
         got = K.from_cp(qb.download((qb.nbytes,), np.int8), n, oh, ow, cp)
         np.testing.assert_array_equal(got[..., :c].transpose(0, 3, 1, 2), ref.quantize_activation(want, scale))
         assert not got[..., c:].any()
+
+
+@pytest.mark.parametrize("case", [
+    dict(n=2, h=224, w=224, o=64, act="relu", cp_out=True),      # the ResNet-18 stem (layer-1 int8 layout)
+    dict(n=5, h=224, w=224, o=64, act="relu", cp_out=False),     # units beyond one wave, NHWC int8
+    dict(n=3, h=57, w=61, o=32, act="relu6", cp_out=False),      # odd sizes: ragged bands, odd conv rows
+    dict(n=1, h=30, w=20, o=12, act="relu", cp_out=True),        # few channels (padded int8 chunk)
+    dict(n=4, h=225, w=254, o=64, act="none", cp_out=False),     # conv rows of 127 pixels, plain bias
+])
+def test_stem_pool_kernel_exact(cuda_device, case):
+    """The stem + pool kernel (7x7/2 conv over the row-expanded input, -inf pad, 3x3/2 max pool,
+    pooled values through the epilogue) against the oracle's qconv2d then maxpool2d, bit for bit."""
+    from mira_b200 import _lib
+    K, DB = _k()
+    n, h, w, o = case["n"], case["h"], case["w"], case["o"]
+    rng = np.random.default_rng(n * 7 + w)
+    x = rng.standard_normal((n, 3, h, w)).astype(np.float32)
+    x_scale = float(np.abs(x).max() / 127.0)
+    q, w_scale = ref.quantize_array(rng.standard_normal((o, 3, 7, 7)).astype(np.float32), 0)
+    bias = rng.standard_normal((o, 1, 1)).astype(np.float32)
+    steps, ops = [("add", 1, False)], [bias]
+    if case["act"] == "relu":
+        steps.append(("relu", None, False))
+    elif case["act"] == "relu6":
+        steps += [("maximum", 2, False), ("minimum", 3, False)]
+        ops += [np.float32(0.0), np.float32(6.0)]
+    _, _, y = ref.qconv2d(x, q, w_scale, x_scale, (2, 2), (3, 3), steps=steps, operands=ops)
+    y = ref.maxpool2d(y, 3, 2, 1, -np.inf)
+    oh, ow = (h + 6 - 7) // 2 + 1, (w + 6 - 7) // 2 + 1
+    entries = K.row4_entries(ow, 2)
+    xb, xq = DB.from_array(x), DB(n * h * entries * 16)
+    K.quantize_nchw_to_row4(xb, n, 3, h, w, x_scale, xq, entries, 3, 2)
+    wq = K.conv_weight_row4(q)
+    bufs = [DB.from_array(a) for a in (wq, *K.scale_arrays(x_scale, w_scale), K.pad_channels(bias))]
+    ph, pw_ = y.shape[2:]
+    ldi = K.round_up(o, 16)
+    yb = DB(n * ph * pw_ * o * 4)
+    qb = DB(K.cp_bytes(n, ph, pw_, ldi) if case["cp_out"] else n * ph * pw_ * ldi, zero=True)
+    out_scale = float(np.abs(y).max() / 127.0)
+    es = [K.Step("add", "channel", ptr=bufs[4])]
+    if case["act"] == "relu":
+        es.append(K.Step("relu"))
+    elif case["act"] == "relu6":
+        es += [K.Step("maximum", "scalar", scalar=0.0), K.Step("minimum", "scalar", scalar=6.0)]
+    epi = K.Epi(es, out_f32=yb, ld_f32=o, out_i8=qb, ld_i8=ldi, out_scale=out_scale,
+                i8_layout=_lib.LAYOUT_CP if case["cp_out"] else _lib.LAYOUT_NHWC)
+    n0 = _lib.launch_count()
+    K.qconv2d_maxpool(n, h, w, 4, xq, o, 7, 7, bufs[0], wq.shape[1], (2, 2), (3, 3), (1, 1), 3, 2, 1, -np.inf,
+                      K.dequant_channel(*bufs[1:4]), epi, layout=_lib.LAYOUT_ROW4, row_entries=entries)
+    assert _lib.launch_count() - n0 == 1
+    _same_f32(yb.download((n, ph, pw_, o), np.float32).transpose(0, 3, 1, 2), y)
+    raw = qb.download((qb.nbytes,), np.int8)
+    got_q = K.from_cp(raw, n, ph, pw_, ldi) if case["cp_out"] else raw.reshape(n, ph, pw_, ldi)
+    np.testing.assert_array_equal(got_q[..., :o].transpose(0, 3, 1, 2), ref.quantize_activation(y, out_scale))
+    assert not got_q[..., o:].any()

@@ -45,8 +45,9 @@ def test_resnet18_small_plan_matches_cpu():
     cpu, cuda, dev = _pair("resnet18", 2, image=32)
     assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
     _check_same(cpu, cuda)
-    assert dev.launched.count("qconv2d") == 20 and dev.launched.count("qgemm") == 1
-    assert dev.launched.count("maxpool") == 1
+    # the stem conv runs inside the pooling kernel (the stem + pool kernel), the rest as convs
+    assert dev.launched.count("qconv2d") == 19 and dev.launched.count("qgemm") == 1
+    assert dev.launched.count("qconv2d_pool") == 1 and dev.launched.count("maxpool") == 0
     assert dev.launched.count("quantize_row4") == 1    # the 3-channel image feeds the stem row-expanded
 
 
@@ -63,7 +64,7 @@ def test_resnet18_chunk_planar_plan_matches_cpu(monkeypatch):
     convs = [l for l in launches if l.kind == "qconv2d"]
     assert sum(l.args["layout"] == _lib.LAYOUT_CP for l in convs) == 13
     assert sum(l.args["epi"].i8_layout == _lib.LAYOUT_CP for l in convs) == 12
-    assert [l.args.get("i8_layout") for l in launches if l.kind == "maxpool"] == [_lib.LAYOUT_CP]
+    assert [l.args["epi"].i8_layout for l in launches if l.kind == "qconv2d_pool"] == [_lib.LAYOUT_CP]
 
 
 def test_resnet18_fused_stem_pool_plan_matches_cpu():
