@@ -1009,10 +1009,12 @@ def main() -> None:
         peak = 2.0 * bf16 if bf16 else None
         # roofline of the int8 tensor-core kernels: the convolutions (ResNet-18, MobileNetV2) or all
         # quantized matmuls (MLP, transformer)
-        kinds = ("qconv2d",) if conv_ops else ("qgemm",)
+        kinds = ("qconv2d", "qconv2d_pool") if conv_ops else ("qgemm",)
         fam_ops = conv_ops if conv_ops else q_ops
         fam_ms, fam_n = time_kernels(exe, kinds)
         achieved = fam_ops / (fam_ms * 1e-3) / 1e12
+        fam_kernels = ("qgemm_sm100_kernel" + (" + stem_pool_kernel" if any(
+            l.kind == "qconv2d_pool" for l in exe.plan.launches) else "")) if conv_ops else "qgemm_sm100_kernel"
         other = {}
         for kind in sorted(set(l.kind for l in exe.plan.launches)):
             ms_k, n_k = time_kernels(exe, (kind,))
@@ -1068,7 +1070,7 @@ def main() -> None:
                             + ("; logits gathered to rank 0 on the device every step" if world > 1 else "")},
             "e2e_blocking": {"value": items / e2e_blocking_s, "unit": wl["unit"],
                              "call": "CompiledProgram.run, one step at a time (copy in, kernels, copy out)"},
-            "roofline": {"bound": "tensor", "kernel": f"qgemm_sm100_kernel ({'/'.join(kinds)}, {fam_n} launches/step)",
+            "roofline": {"bound": "tensor", "kernel": f"{fam_kernels} ({'/'.join(kinds)}, {fam_n} launches/step)",
                          "achieved": achieved, "peak": peak, "unit": "TOPS",
                          "frac": (achieved / peak) if peak else None,
                          "traffic": CONV_DRAM_BYTES_PER_PASS if headline else None,

@@ -116,6 +116,33 @@ __device__ __forceinline__ void dequant4_x2(const uint32_t* r, const float4& hs,
   }
 }
 
+// dequant4_x2 with its checks folded into two bitwise accumulations (as dequant16_x2 below): a
+// value needs the exact f64 path when (bad | (range & 0xFF800000)) != 0 after all are folded in.
+__device__ __forceinline__ void dequant4_fold(const uint32_t* r, const float4& hs, const float4& ls, float* v,
+                                              uint32_t& bad, uint32_t& range) {
+  const f2_t magic = f2(-12582912.0f, -12582912.0f);
+  const f2_t e40 = f2(0x1p-40f, 0x1p-40f), ne40 = f2(-0x1p-40f, -0x1p-40f);
+  const float hv[4] = {hs.x, hs.y, hs.z, hs.w}, lv[4] = {ls.x, ls.y, ls.z, ls.w};
+#pragma unroll
+  for (int j = 0; j < 4; j += 2) {
+    const uint32_t x0 = 0x4B400000u + r[j], x1 = 0x4B400000u + r[j + 1];
+    range |= x0 ^ 0x4B000000u;
+    range |= x1 ^ 0x4B000000u;
+    const f2_t a = f2_add(f2(__uint_as_float(x0), __uint_as_float(x1)), magic);
+    const f2_t h = f2(hv[j], hv[j + 1]);
+    const f2_t pl = f2_mul(a, f2(lv[j], lv[j + 1]));
+    const f2_t yl = f2_fma(a, h, f2_fma(a, f2_mul(h, ne40), pl));
+    const f2_t yh = f2_fma(a, h, f2_fma(a, f2_mul(h, e40), pl));
+    float l0, l1, h0, h1;
+    f2_split(yl, l0, l1);
+    f2_split(yh, h0, h1);
+    v[j] = l0;
+    v[j + 1] = l1;
+    bad |= __float_as_uint(l0) ^ __float_as_uint(h0);
+    bad |= __float_as_uint(l1) ^ __float_as_uint(h1);
+  }
+}
+
 // The dequant of 16 accumulators, the arithmetic of dequant4_x2 two lanes per instruction, with
 // the checks folded into two bitwise accumulations per element: the two ends of each value's
 // uncertainty interval must round to the same float (their bit patterns XOR to 0), and each

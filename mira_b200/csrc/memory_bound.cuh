@@ -84,59 +84,71 @@ __global__ void quantize_nchw_nhwc_kernel(const float* __restrict__ x, int64_t n
 // layout read by the ROW4 convolution gather: for every image row, `entries` 16-byte entries, entry
 // e holding pixels e - pad .. e - pad + 3 with 4 channels each (zero outside the image and for
 // channels >= c).  One thread per entry; neighbouring threads read neighbouring pixels.
+constexpr int Q4_ROWS = 4;   // image rows a thread has in flight (their loads issued before any math)
+
 template <int S>
 __global__ void quantize_nchw_row4_kernel(const float* __restrict__ x, int n, int c, int h, int w, QuantScale q,
                                           int8_t* __restrict__ xq, int entries, int pad) {
-  // blockIdx.y: image rows (n * h, strided over gridDim.y); each warp of the block: 32 entries of the
-  // row.  Entry e holds pixels S*e - pad .. S*e - pad + 3: lane l quantizes the S pixels that start
-  // its entry (lanes 0 .. 4/S - 2 also those of the entries after the block) and the entries are
-  // assembled from 4/S neighbouring lanes by shuffles.  No integer division per element.
+  // blockIdx.y: groups of Q4_ROWS image rows (strided over gridDim.y); each warp of the block: 32
+  // entries of those rows.  Entry e holds pixels S*e - pad .. S*e - pad + 3: lane l quantizes the S
+  // pixels that start its entry (lanes 0 .. 4/S - 2 also those of the entries after the warp) and
+  // the entries are assembled from 4/S neighbouring lanes by shuffles.  All loads of the Q4_ROWS
+  // rows are issued before the first is used, so a thread keeps several rows of reads in flight.
   constexpr int L = 4 / S;
   const int lane = threadIdx.x & 31;
   const int e0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
   if (e0 >= entries) return;   // warp-uniform
   const int64_t rows = int64_t(n) * h;
-  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-    const int img = static_cast<int>(row / h);
-    const int y = static_cast<int>(row - int64_t(img) * h);
-    const float* base = x + (int64_t(img) * c * h + y) * w;
-    const int64_t plane = int64_t(h) * w;
-    // the S pixels from x0 on, 4 channels each (0 outside the image and for channels >= c, which
-    // quantizes to 0), quantized two values per packed instruction
-    auto pixel_words = [&](int x0, uint32_t (&out)[S]) {
-      float v[4 * S];
+  const int64_t plane = int64_t(h) * w;
+  const int x_own = S * (e0 + lane) - pad;
+  const int x_extra = S * (e0 + 32 + lane) - pad;
+  const bool has_extra = lane < L - 1;
+  for (int64_t row0 = int64_t(blockIdx.y) * Q4_ROWS; row0 < rows; row0 += int64_t(gridDim.y) * Q4_ROWS) {
+    float v[Q4_ROWS][4 * S], t[Q4_ROWS][4 * S];
+#pragma unroll
+    for (int r = 0; r < Q4_ROWS; ++r) {
+      const int64_t row = row0 + r;
+      const bool row_ok = row < rows;
+      const int img = row_ok ? static_cast<int>(row / h) : 0;
+      const int y = row_ok ? static_cast<int>(row - int64_t(img) * h) : 0;
+      const float* base = x + (int64_t(img) * c * h + y) * w;
 #pragma unroll
       for (int j = 0; j < S; ++j)
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
-          const int xx = x0 + j;
-          v[4 * j + ch] = (ch < c && xx >= 0 && xx < w) ? __ldg(base + ch * plane + xx) : 0.0f;
+          const int xo = x_own + j, xe = x_extra + j;
+          v[r][4 * j + ch] = (row_ok && ch < c && xo >= 0 && xo < w) ? __ldg(base + ch * plane + xo) : 0.0f;
+          t[r][4 * j + ch] =
+              (row_ok && has_extra && ch < c && xe >= 0 && xe < w) ? __ldg(base + ch * plane + xe) : 0.0f;
         }
-      uint32_t b[4 * S];
-      requant_x2<4 * S>(v, q.s, q.rcp, q.c127, b);
-#pragma unroll
-      for (int j = 0; j < S; ++j) out[j] = pack4_i8(b[4 * j], b[4 * j + 1], b[4 * j + 2], b[4 * j + 3]);
-    };
-    uint32_t own[S], extra[S];
-    pixel_words(S * (e0 + lane) - pad, own);
-    if (lane < L - 1) {
-      pixel_words(S * (e0 + 32 + lane) - pad, extra);
-    } else {
-#pragma unroll
-      for (int j = 0; j < S; ++j) extra[j] = 0u;
     }
-    uint32_t word[4];
 #pragma unroll
-    for (int k = 0; k < L; ++k) {
+    for (int r = 0; r < Q4_ROWS; ++r) {
+      const int64_t row = row0 + r;
+      uint32_t own[S], extra[S];
+      {
+        uint32_t b[4 * S], d[4 * S];
+        requant_x2<4 * S>(v[r], q.s, q.rcp, q.c127, b);
+        requant_x2<4 * S>(t[r], q.s, q.rcp, q.c127, d);
 #pragma unroll
-      for (int j = 0; j < S; ++j) {
-        const uint32_t down = __shfl_down_sync(0xffffffffu, own[j], k);
-        const uint32_t tail = __shfl_sync(0xffffffffu, extra[j], (lane + k - 32) & 31);
-        word[k * S + j] = lane + k < 32 ? down : tail;
+        for (int j = 0; j < S; ++j) {
+          own[j] = pack4_i8(b[4 * j], b[4 * j + 1], b[4 * j + 2], b[4 * j + 3]);
+          extra[j] = pack4_i8(d[4 * j], d[4 * j + 1], d[4 * j + 2], d[4 * j + 3]);
+        }
       }
+      uint32_t word[4];
+#pragma unroll
+      for (int k = 0; k < L; ++k) {
+#pragma unroll
+        for (int j = 0; j < S; ++j) {
+          const uint32_t down = __shfl_down_sync(0xffffffffu, own[j], k);
+          const uint32_t tail = __shfl_sync(0xffffffffu, extra[j], (lane + k - 32) & 31);
+          word[k * S + j] = lane + k < 32 ? down : tail;
+        }
+      }
+      if (row < rows && e0 + lane < entries)
+        reinterpret_cast<uint4*>(xq)[row * entries + e0 + lane] = make_uint4(word[0], word[1], word[2], word[3]);
     }
-    if (e0 + lane < entries)
-      reinterpret_cast<uint4*>(xq)[row * entries + e0 + lane] = make_uint4(word[0], word[1], word[2], word[3]);
   }
 }
 

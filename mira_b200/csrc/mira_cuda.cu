@@ -750,8 +750,8 @@ extern "C" int mira_cuda_quantize_nchw_to_row4(const float* x, int64_t n, int64_
   MIRA_CHECK_ARG(entry_stride == 1 || entry_stride == 2 || entry_stride == 4, "entry stride must be 1, 2 or 4");
   const int64_t warps = (row_entries + 31) / 32;
   const int threads = int(32 * (warps < 8 ? warps : 8));
-  const int64_t rows = n * h;
-  const dim3 grid(unsigned((warps * 32 + threads - 1) / threads), unsigned(rows < 65535 ? rows : 65535));
+  const int64_t groups = (n * h + Q4_ROWS - 1) / Q4_ROWS;
+  const dim3 grid(unsigned((warps * 32 + threads - 1) / threads), unsigned(groups < 65535 ? groups : 65535));
   const QuantScale qs = make_qscale(scale);
   if (entry_stride == 1)
     quantize_nchw_row4_kernel<1><<<grid, threads, 0, dev->stream>>>(x, int(n), int(c), int(h), int(w), qs, xq,
@@ -1114,7 +1114,7 @@ extern "C" int mira_cuda_qconv2d_maxpool(int64_t n, int64_t h, int64_t w, int64_
   MIRA_CHECK_ARG(ph > 0 && pw > 0, "pool window larger than the conv output");
   // the ResNet stem form (row-expanded input, stride 2, 3x3/2 pool with one pixel of padding)
   if (x_layout == MIRA_LAYOUT_ROW4 && stride_h == 2 && stride_w == 2 && kh <= SP_KH_MAX && pool_size == 3 &&
-      pool_stride == 2 && pool_pad == 1 && ow <= SP_OW_MAX && x_row_entries <= SP_PLANE / 16 && o % 4 == 0)
+      pool_stride == 2 && pool_pad == 1 && ow <= SP_OW_MAX && x_row_entries <= SP_ENTRIES_MAX && o % 4 == 0)
     return launch_stem_pool(dev, p, n, h, w, oh, ow, ph, pw, kh, pad_h, x_row_entries, o, x, wq, ldw, epi);
   MIRA_CHECK_ARG(x_layout != MIRA_LAYOUT_CP && (epi->out_i8 == nullptr || epi->i8_layout == MIRA_LAYOUT_NHWC),
                  "fused pooling reads and writes the NHWC / row-expanded layouts");
