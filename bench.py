@@ -612,18 +612,18 @@ def pass_bytes(graph) -> dict:
 
 
 def parity_check(workload: str, batch: int, out: np.ndarray, x: np.ndarray, calib_batch: int, n_calib: int,
-                 n_images: int = 4) -> dict:
+                 n_images: int = 4, **kw) -> dict:
     """The timed program's own output rows against the reference cpu target (MIRA's NumPy golden
     model) run on the same input rows, bit for bit: a batch-1 (MLP: full-batch) cpu program compiled
     with the same calibration, so every activation scale is identical.  Images: first, last and a
     seeded middle pair."""
     from mira_b200 import configs
     if workload == "mlp":
-        cpu = configs.compile_w8a8(workload, batch, "cpu", calib_batch=calib_batch, n_calib=n_calib)
+        cpu = configs.compile_w8a8(workload, batch, "cpu", calib_batch=calib_batch, n_calib=n_calib, **kw)
         want = cpu.run({"x": x})
         bad = int((want != out).any(axis=1).sum())
         return {"images": int(batch), "mismatches": bad, "oracle": "reference cpu target, whole batch"}
-    cpu = configs.compile_w8a8(workload, 1, "cpu", calib_batch=calib_batch, n_calib=n_calib)
+    cpu = configs.compile_w8a8(workload, 1, "cpu", calib_batch=calib_batch, n_calib=n_calib, **kw)
     rng = np.random.default_rng(7)
     idx = sorted({0, batch - 1, *(int(i) for i in rng.choice(batch, size=max(0, n_images - 2), replace=False))})
     bad = [i for i in idx if not np.array_equal(cpu.run({"x": x[i:i + 1]}), out[i:i + 1])]
@@ -872,6 +872,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true", help="skip the parity check of the timed output")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM sweep of the headline line")
+    ap.add_argument("--int8-depthwise", action="store_true",
+                    help="MobileNetV2 in the opt-in int8 depthwise mode (mira_b200.int8_depthwise); the parity "
+                         "check then compares with the reference cpu target compiled in the same mode")
     ap.add_argument("--fuse-pool", action="store_true",
                     help="compute a conv whose only consumer is a max pool inside the pooling kernel")
     ap.add_argument("--profile-case", choices=PROFILE_CASES, default=None,
@@ -906,8 +909,10 @@ def main() -> None:
     from mira_b200 import configs
 
     t0 = time.perf_counter()
+    mode = {"int8_depthwise": True} if args.int8_depthwise else {}
     prog = configs.compile_w8a8(args.workload, args.batch, "cuda", calib_batch=args.calib_batch, device=local,
-                                n_calib=wl["n_calib"], build_kw=wl["build_kw"] or None, fuse_pool=args.fuse_pool)
+                                n_calib=wl["n_calib"], build_kw=wl["build_kw"] or None, fuse_pool=args.fuse_pool,
+                                **mode)
     compile_s = time.perf_counter() - t0
     segs = [s for s in prog.segments if s.device == "cuda"]
     assert len(prog.segments) == 1 and len(segs) == 1, "the whole network must be one cuda segment"
@@ -985,7 +990,7 @@ def main() -> None:
         strong = None
         if strong_batch is not None:
             sprog = configs.compile_w8a8(args.workload, strong_batch, "cuda", calib_batch=args.calib_batch,
-                                         device=local, n_calib=wl["n_calib"], build_kw=wl["build_kw"] or None)
+                                         device=local, n_calib=wl["n_calib"], build_kw=wl["build_kw"] or None, **mode)
             sexe = sprog.segments[0].executable
             sx = sexe.input_array(sprog.graph.inputs[0])
             fill_input(sx, rank)
@@ -1045,7 +1050,7 @@ def main() -> None:
         if not args.no_check and args.workload != "transformer":
             try:
                 parity = parity_check(args.workload, args.batch, outs[-1][exe.g.outputs[0]][:args.batch],
-                                      host_x, args.calib_batch, wl["n_calib"])
+                                      host_x, args.calib_batch, wl["n_calib"], **mode)
             except ImportError as e:
                 parity = {"unavailable": str(e)}
         in_desc = (f"{host_x.nbytes / 1e6:.0f} MB input batch") if host_x.nbytes > 1e6 else "small input batch"
@@ -1061,6 +1066,7 @@ def main() -> None:
                        if host_x.nbytes > 126e6 or args.workload == "transformer"
                        else f"working set near L2 ({in_desc})",
                        "calibration": f"{wl['n_calib']} seeded batches of {args.calib_batch}",
+                       **({"mode": "opt-in int8 depthwise (mira_b200.int8_depthwise)"} if mode else {}),
                        "compile_s": round(compile_s, 1)},
             "e2e": {"value": items / e2e_s, "unit": wl["unit"], "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": int(out.nbytes) * world,

@@ -289,6 +289,18 @@ int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int64_t w, int
                             int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dil_h,
                             int64_t dil_w, const mira_epilogue* epi);
 
+/* W8A8 depthwise convolution, the opt-in int8 depthwise mode: reference _qconv2d_ref
+ * (ops.py:630-634) on a qconv2d with groups == channels (what quantize_w8a8 would produce if
+ * _w8a8_weight, quantize.py:95-115, accepted depthwise weights).  x: int8 NHWC [n, h, w, ldx]
+ * (quantized at the op's x_scale, channels >= c zero); wq: int8 [kh*kw, c] tap-major, 4-byte
+ * aligned; dq: per-channel dequant (scale64/hi/lo of x_scale * w_scale[c]).  Integer sums over the
+ * taps, the exact dequant, then the epilogue on [n*oh*ow, c] (int8 NHWC rows and/or f32).
+ * c must be a multiple of 4. */
+int mira_cuda_qdwconv2d_nhwc(const int8_t* x, int64_t n, int64_t h, int64_t w, int64_t c, int64_t ldx,
+                             const int8_t* wq, int64_t kh, int64_t kw, int64_t stride_h, int64_t stride_w,
+                             int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
+                             const mira_dequant* dq, const mira_epilogue* epi);
+
 /* Layout changes between the reference's NCHW f32 tensors and the device's NHWC. */
 int mira_cuda_nchw_to_nhwc_f32(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
                                float* y, int64_t ldc);

@@ -6,7 +6,7 @@ quantized matmuls and convolutions on hand-written tcgen05 kernels (libmira_cuda
 """
 from __future__ import annotations
 
-__all__ = ["install", "CudaTarget"]
+__all__ = ["install", "CudaTarget", "int8_depthwise"]
 
 
 def install():
@@ -18,4 +18,7 @@ def __getattr__(name):
     if name == "CudaTarget":
         from .target import CudaTarget
         return CudaTarget
+    if name == "int8_depthwise":
+        from .depthwise import int8_depthwise
+        return int8_depthwise
     raise AttributeError(name)

@@ -121,6 +121,8 @@ SIGNATURES: dict[str, tuple] = {
     "mira_cuda_mean_hw_nhwc": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _f32]),
     "mira_cuda_dwconv2d_nhwc": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, C.POINTER(Epilogue)]),
+    "mira_cuda_qdwconv2d_nhwc": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
+                                        _i64, _i64, C.POINTER(Dequant), C.POINTER(Epilogue)]),
     "mira_cuda_nchw_to_nhwc_f32": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64]),
     "mira_cuda_nhwc_to_nchw_f32": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mira_cuda_bmm_f32": (_i32, [_i64, _i64, _i64, _i64, _i64, C.POINTER(View4), C.POINTER(View4),

@@ -280,14 +280,24 @@ _PEAKS: dict = {}
 
 
 def compile_w8a8(name: str, batch: int, target: str, *, seed: int = 0, n_calib: int = 4, calib_seed: int = 100,
-                 calib_batch: Optional[int] = None, build_kw: Optional[dict] = None, **kw):
+                 calib_batch: Optional[int] = None, build_kw: Optional[dict] = None, int8_depthwise: bool = False,
+                 **kw):
     """Build workload `name` at `batch` and compile it W8A8 for `target` through MIRA's compile_ir.
 
     Calibration feeds are `n_calib` seeded N(0, 1) batches.  With `calib_batch` (usually smaller
     than `batch`), calibration runs on the same network built at `calib_batch` - the reference's own
     _calibrate (quantize.py:73-92) over those feeds - and the resulting per-value peaks are carried
     over to the large graph op by op, so large batches do not pay hours of host-side calibration.
-    Those peaks are computed once per process and calibration setting (`_PEAKS`)."""
+    Those peaks are computed once per process and calibration setting (`_PEAKS`).
+    `int8_depthwise`: compile in the opt-in int8 depthwise mode (mira_b200.int8_depthwise)."""
+    if int8_depthwise:
+        from .depthwise import int8_depthwise as mode
+        with mode():
+            return _compile_w8a8(name, batch, target, seed, n_calib, calib_seed, calib_batch, build_kw, True, kw)
+    return _compile_w8a8(name, batch, target, seed, n_calib, calib_seed, calib_batch, build_kw, False, kw)
+
+
+def _compile_w8a8(name, batch, target, seed, n_calib, calib_seed, calib_batch, build_kw, dw_mode, kw):
     if target in ("cuda", "b200"):
         install()
     else:
@@ -311,7 +321,7 @@ def compile_w8a8(name: str, batch: int, target: str, *, seed: int = 0, n_calib: 
     cs, cb = candidates(small), candidates(g)
     if len(cs) != len(cb):
         raise RuntimeError("small and large graphs differ in structure")
-    key = (name, seed, calib_batch, n_calib, calib_seed, tuple(sorted((build_kw or {}).items())))
+    key = (name, seed, calib_batch, n_calib, calib_seed, tuple(sorted((build_kw or {}).items())), dw_mode)
     if key not in _PEAKS:
         cal = [random_inputs(small, calib_seed + i) for i in range(n_calib)]
         peak_small = Q._calibrate(small, cal, {op.inputs[0] for op in cs})

@@ -682,6 +682,127 @@ __global__ void __launch_bounds__(256, 4) dwconv3x3_kernel(const float* __restri
   }
 }
 
+// ---------------------------------------------------------------- K4c: W8A8 depthwise convolution
+
+// The opt-in int8 depthwise mode: reference _qconv2d_ref (ops.py:630-634) with groups = channels.
+// Its per-tap f32 einsum sums of int8 products are exact integers (|sum| <= kh * kw * 127^2 < 2^24),
+// so the device sums int32 products; then the per-channel dequant y = f32(f64(acc) * S[c]) (exact,
+// as in the GEMM epilogue) and the depthwise epilogue.  Inputs: int8 NHWC pixels `ldx` bytes apart
+// (channels padded with zeros), weights as int32 words [kh * kw][c / 4] (4 channels' int8 taps).
+
+__device__ __forceinline__ int32_t sext_byte(uint32_t v, int e) {
+  // byte e of v, sign-extended
+  return static_cast<int32_t>(static_cast<int8_t>(static_cast<uint8_t>(v >> (8 * e))));
+}
+
+struct QdwScales {
+  const float* hi;
+  const float* lo;
+  const double* s64;
+};
+
+template <int T>
+__device__ __forceinline__ void qdw_dequant(const int32_t (&acc)[T][4], const QdwScales& sc, int cg, float (&v)[T][4]) {
+  const float4 hs = __ldg(reinterpret_cast<const float4*>(sc.hi + 4 * cg));
+  const float4 ls = __ldg(reinterpret_cast<const float4*>(sc.lo + 4 * cg));
+  uint32_t bad = 0, range = 0;
+#pragma unroll
+  for (int t = 0; t < T; ++t) dequant4_fold(reinterpret_cast<const uint32_t*>(acc[t]), hs, ls, v[t], bad, range);
+  if ((bad | (range & 0xFF800000u)) != 0) {   // rare: the exact product in f64
+#pragma unroll
+    for (int t = 0; t < T; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[t][e] = __double2float_rn(static_cast<double>(acc[t][e]) * sc.s64[4 * cg + e]);
+  }
+}
+
+// 3 x 3, stride S, dilation 1: 4 channels x OXT output columns per thread (as dwconv3x3_kernel).
+template <int S, int OXT>
+__global__ void __launch_bounds__(256, 4) qdwconv3x3_kernel(const int8_t* __restrict__ x, int64_t ldx,
+                                                         const uint32_t* __restrict__ wt, const QdwScales sc,
+                                                         const __grid_constant__ DwParams p) {
+  constexpr int NIN = (OXT - 1) * S + 3;
+  const int c4 = p.c >> 2;
+  const int ox0 = (blockIdx.x * blockDim.y + threadIdx.y) * OXT;
+  if (ox0 >= p.ow) return;
+  const int64_t rows = int64_t(p.n) * p.oh;
+  for (int64_t orow = blockIdx.y; orow < rows; orow += gridDim.y) {
+    const int img = static_cast<int>(orow / p.oh);
+    const int oy = static_cast<int>(orow - int64_t(img) * p.oh);
+    for (int cg = threadIdx.x; cg < c4; cg += blockDim.x) {
+      int32_t acc[OXT][4];
+#pragma unroll
+      for (int t = 0; t < OXT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        const int iy = oy * S - p.ph + i;
+        const bool row_in = iy >= 0 && iy < p.h;
+        const int8_t* xrow = x + (int64_t(img) * p.h + (row_in ? iy : 0)) * p.w * ldx + 4 * cg;
+        uint32_t xin[NIN];
+#pragma unroll
+        for (int u = 0; u < NIN; ++u) {
+          const int ix = ox0 * S - p.pw + u;
+          xin[u] = row_in && ix >= 0 && ix < p.w ? __ldg(reinterpret_cast<const uint32_t*>(xrow + int64_t(ix) * ldx)) : 0u;
+        }
+        int32_t wv[3][4];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          const uint32_t wword = __ldg(wt + (i * 3 + j) * c4 + cg);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) wv[j][e] = sext_byte(wword, e);
+        }
+#pragma unroll
+        for (int u = 0; u < NIN; ++u) {
+          int32_t xv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xv[e] = sext_byte(xin[u], e);
+#pragma unroll
+          for (int t = 0; t < OXT; ++t) {
+            const int j = u - t * S;
+            if (j < 0 || j > 2) continue;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[t][e] += xv[e] * wv[j][e];
+          }
+        }
+      }
+      float v[OXT][4];
+      qdw_dequant<OXT>(acc, sc, cg, v);
+      dw_epilogue_tile<OXT>(p, orow * p.ow + ox0, cg, p.ow - ox0 < OXT ? p.ow - ox0 : OXT, v);
+    }
+  }
+}
+
+// Any kernel size, stride and dilation: one (output pixel, 4 channels) per thread.
+__global__ void qdwconv4_kernel(const int8_t* __restrict__ x, int64_t ldx, const uint32_t* __restrict__ wt,
+                                const QdwScales sc, const __grid_constant__ DwParams p) {
+  const int c4 = p.c >> 2;
+  const int ox = blockIdx.x * blockDim.y + threadIdx.y;
+  if (ox >= p.ow) return;
+  const int64_t rows = int64_t(p.n) * p.oh;
+  for (int64_t orow = blockIdx.y; orow < rows; orow += gridDim.y) {
+    const int img = static_cast<int>(orow / p.oh);
+    const int oy = static_cast<int>(orow - int64_t(img) * p.oh);
+    for (int cg = threadIdx.x; cg < c4; cg += blockDim.x) {
+      int32_t acc[1][4] = {{0, 0, 0, 0}};
+      for (int i = 0; i < p.kh; ++i) {
+        const int iy = oy * p.sh - p.ph + i * p.dh;
+        if (iy < 0 || iy >= p.h) continue;
+        for (int j = 0; j < p.kw; ++j) {
+          const int ix = ox * p.sw - p.pw + j * p.dw;
+          if (ix < 0 || ix >= p.w) continue;
+          const uint32_t xw = __ldg(reinterpret_cast<const uint32_t*>(x + ((int64_t(img) * p.h + iy) * p.w + ix) * ldx + 4 * cg));
+          const uint32_t ww = __ldg(wt + (i * p.kw + j) * c4 + cg);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[0][e] += sext_byte(xw, e) * sext_byte(ww, e);
+        }
+      }
+      float v[1][4];
+      qdw_dequant<1>(acc, sc, cg, v);
+      dw_epilogue_tile<1>(p, orow * p.ow + ox, cg, 1, v);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- K4b: general f32 convolution
 
 // The patch matrix of an f32 convolution over an NHWC input: row m = output pixel (img, oy, ox),

@@ -17,6 +17,7 @@
 #include "qgemm_sm100.cuh"
 #include "qgemm_pair_sm100.cuh"
 #include "stem_pool_sm100.cuh"
+#include "dw_staged.cuh"
 #include "runtime.h"
 #include "sequence_ops.cuh"
 
@@ -1250,6 +1251,78 @@ extern "C" int mira_cuda_im2col_f32(const float* x, int64_t n, int64_t h, int64_
   return after_launch("im2col_f32_kernel");
 }
 
+// The TMA-staged depthwise 3x3 kernel (dw_staged.cuh) for an NHWC input of elements T (f32 rows of
+// c values, or int8 rows of ldx bytes): picks the unit shape (R output rows x cc channels) so that
+// two input windows fit in shared memory, encodes the 4-D tensor map and launches one persistent
+// CTA per SM (more when the windows are small).  Returns -1 when the shape does not suit it.
+template <typename T>
+static int launch_dw_staged(DeviceState* dev, const T* x, int64_t ldx, const DwParams& p, const void* wt,
+                            const QdwScales& sc) {
+  constexpr int64_t es = sizeof(T);
+  const int S = p.sh;
+  const int oxt = S == 1 ? 4 : 2;
+  const int64_t tiles = (p.ow + oxt - 1) / oxt;
+  const int64_t cols_in = (tiles * oxt - 1) * S + 3;
+  if (cols_in > 256 || (ldx * es) % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return -1;
+  const int64_t unit_c = 16 / es;                               // channels per 16 bytes
+  const int64_t c_pad = (p.c + unit_c - 1) / unit_c * unit_c;
+  const int64_t budget = 55 * 1024;                             // bytes per window buffer (2 CTAs per SM)
+  // the unit shape that re-reads the fewest input rows (R / rows_in largest), with enough tasks
+  // (4-channel groups x column tiles x rows) for the CTA's threads; wider channel chunks on ties
+  int64_t cc = 0, rows = 0;
+  double best = -1.0;
+  for (int64_t c_try = c_pad < 256 ? c_pad : 256; c_try >= unit_c; c_try = c_try > unit_c ? (c_try / 2 + unit_c - 1) / unit_c * unit_c : 0) {
+    for (int64_t r = 8; r >= 1; --r) {
+      const int64_t r_eff = r < p.oh ? r : p.oh;
+      if ((r_eff - 1) * S + 3 > 0 && ((r_eff - 1) * S + 3) * cols_in * c_try * es > budget) continue;
+      const double reuse = double(r_eff) / double((r_eff - 1) * S + 3);
+      const double fill = std::min(1.0, double((c_try / 4) * tiles * r_eff) / DWS_THREADS);
+      const double score = reuse * fill;
+      if (score > best + 1e-9) { best = score; cc = c_try; rows = r_eff; }
+      break;   // the largest r that fits is the best for this chunk width
+    }
+    if (c_try == unit_c) break;
+  }
+  if (rows == 0) return -1;
+  if (rows > p.oh) rows = p.oh;
+  const int64_t rows_in = (rows - 1) * S + 3;
+  DwsParams q;
+  std::memset(&q, 0, sizeof(q));
+  q.p = p;
+  q.sc = sc;
+  q.rows = int(rows); q.cc = int(cc); q.cols_in = int(cols_in); q.rows_in = int(rows_in); q.tiles = int(tiles);
+  q.bands = int((p.oh + rows - 1) / rows);
+  q.chunks = int((p.c + cc - 1) / cc);
+  const int64_t units = int64_t(p.n) * q.bands * q.chunks;
+  if (units >= (int64_t(1) << 31)) return -1;
+  q.units = int(units);
+  q.box_bytes = int(rows_in * cols_in * cc * es);
+  q.err = device_err_ptr();
+  CUtensorMap map;
+  const cuuint64_t dims[4] = {cuuint64_t(ldx), cuuint64_t(p.w), cuuint64_t(p.h), cuuint64_t(p.n)};
+  const cuuint64_t strides[3] = {cuuint64_t(ldx * es), cuuint64_t(ldx * es * p.w), cuuint64_t(ldx * es * p.w * p.h)};
+  const cuuint32_t box[4] = {cuuint32_t(cc), cuuint32_t(cols_in), cuuint32_t(rows_in), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = g_encode_tiled(&map, es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
+                                    const_cast<T*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  const int buf_bytes = (q.box_bytes + 127) & ~127;
+  const int smem = 128 + 2 * buf_bytes + 64;
+  int per_sm = 232448 / (smem + 1024);
+  if (per_sm > 2) per_sm = 2;   // two CTAs of 256 threads at up to 128 registers fill an SM
+  if (per_sm < 1) return -1;
+  const int64_t grid64 = units < int64_t(dev->sm_count) * per_sm ? units : int64_t(dev->sm_count) * per_sm;
+  auto launch = [&](auto kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kernel<<<unsigned(grid64), DWS_THREADS, smem, dev->stream>>>(map, wt, q);
+  };
+  if (S == 1) launch(dw_staged_kernel<T, 1, 4>);
+  else launch(dw_staged_kernel<T, 2, 2>);
+  return after_launch("dw_staged_kernel");
+}
+
 extern "C" int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int64_t w, int64_t c, const float* wt,
                                        int64_t kh, int64_t kw, int64_t stride_h, int64_t stride_w, int64_t pad_h,
                                        int64_t pad_w, int64_t dil_h, int64_t dil_w, const mira_epilogue* epi) {
@@ -1281,6 +1354,12 @@ extern "C" int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int
       vec = vec && (reinterpret_cast<uintptr_t>(st.ptr) & 15) == 0 && (st.operand != MIRA_OPND_FULL || st.ld % 4 == 0);
   }
   if (vec && kh == 3 && kw == 3 && dil_h == 1 && dil_w == 1 && stride_h == stride_w && stride_h <= 2) {
+    // the staged kernel wins on the narrower late layers (measured on MobileNetV2's: 28 x 28 and
+    // smaller outputs); the early wide layers stay on the unstaged one
+    if (oh <= 28) {
+      const int rc = launch_dw_staged<float>(dev, x, c, p, wt, QdwScales{nullptr, nullptr, nullptr});
+      if (rc >= 0) return rc;
+    }
     // threadIdx.x: 4-channel groups (all of them up to 256 threads), threadIdx.y: groups of
     // output columns, so narrow late layers with many channels keep every thread busy
     const int oxt = stride_h == 1 ? 4 : 2;
@@ -1306,6 +1385,73 @@ extern "C" int mira_cuda_dwconv2d_nhwc(const float* x, int64_t n, int64_t h, int
   }
   dwconv_kernel<<<grid_for(dev, n * oh * ow * c, threads), threads, 0, dev->stream>>>(x, wt, p);
   return after_launch("dwconv_kernel");
+}
+
+extern "C" int mira_cuda_qdwconv2d_nhwc(const int8_t* x, int64_t n, int64_t h, int64_t w, int64_t c, int64_t ldx,
+                                        const int8_t* wq, int64_t kh, int64_t kw, int64_t stride_h, int64_t stride_w,
+                                        int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
+                                        const mira_dequant* dq, const mira_epilogue* epi) {
+  MIRA_GET_DEVICE(dev);
+  MIRA_CHECK_ARG(n >= 0 && h > 0 && w > 0 && c > 0 && c % 4 == 0 && ldx >= c && ldx % 4 == 0 && kh > 0 && kw > 0,
+                 "bad int8 depthwise shape (channels must be a multiple of 4)");
+  MIRA_CHECK_ARG(kh * kw * 127 * 127 < (int64_t(1) << 24), "int8 depthwise kernel too large for exact f32 sums");
+  MIRA_CHECK_ARG(stride_h > 0 && stride_w > 0 && dil_h > 0 && dil_w > 0 && pad_h >= 0 && pad_w >= 0,
+                 "bad int8 depthwise geometry");
+  MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 3) == 0 && (reinterpret_cast<uintptr_t>(wq) & 3) == 0,
+                 "int8 depthwise operands must be 4-byte aligned");
+  MIRA_CHECK_ARG(dq != nullptr && dq->scale64 != nullptr && dq->scale_hi != nullptr && dq->scale_lo != nullptr &&
+                     (reinterpret_cast<uintptr_t>(dq->scale_hi) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(dq->scale_lo) & 15) == 0,
+                 "int8 depthwise needs per-channel dequant scales (16-byte aligned)");
+  MIRA_CHECK_ARG(epi != nullptr && epi->n_steps >= 0 && epi->n_steps <= MIRA_EPI_MAX_STEPS, "bad epilogue");
+  MIRA_CHECK_ARG(epi->out_f32 != nullptr || epi->out_i8 != nullptr, "int8 depthwise has no output");
+  MIRA_CHECK_ARG(epi->i8_layout == MIRA_LAYOUT_NHWC, "int8 depthwise writes NHWC rows");
+  if (epi->out_f32 != nullptr)
+    MIRA_CHECK_ARG(epi->ld_f32 % 4 == 0 && (reinterpret_cast<uintptr_t>(epi->out_f32) & 15) == 0,
+                   "f32 output must hold 16-byte aligned rows");
+  if (epi->out_i8 != nullptr)
+    MIRA_CHECK_ARG(epi->ld_i8 % 4 == 0 && (reinterpret_cast<uintptr_t>(epi->out_i8) & 3) == 0,
+                   "int8 output must hold 4-byte aligned rows");
+  for (int s = 0; s < epi->n_steps; ++s) {
+    const mira_epi_step& st = epi->steps[s];
+    if (st.operand == MIRA_OPND_CHANNEL || st.operand == MIRA_OPND_FULL)
+      MIRA_CHECK_ARG((reinterpret_cast<uintptr_t>(st.ptr) & 15) == 0 && (st.operand != MIRA_OPND_FULL || st.ld % 4 == 0),
+                     "epilogue operands must be 16-byte aligned");
+  }
+  const int64_t oh = (h + 2 * pad_h - dil_h * (kh - 1) - 1) / stride_h + 1;
+  const int64_t ow = (w + 2 * pad_w - dil_w * (kw - 1) - 1) / stride_w + 1;
+  MIRA_CHECK_ARG(oh > 0 && ow > 0, "kernel larger than the padded input");
+  if (n == 0) return MIRA_CUDA_OK;
+  DwParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.n = int(n); p.h = int(h); p.w = int(w); p.c = int(c); p.oh = int(oh); p.ow = int(ow);
+  p.kh = int(kh); p.kw = int(kw); p.sh = int(stride_h); p.sw = int(stride_w); p.ph = int(pad_h); p.pw = int(pad_w);
+  p.dh = int(dil_h); p.dw = int(dil_w);
+  p.n_steps = epi->n_steps;
+  for (int s = 0; s < epi->n_steps; ++s) p.steps[s] = epi->steps[s];
+  p.out_f32 = epi->out_f32; p.ld_f32 = epi->ld_f32; p.out_i8 = epi->out_i8; p.ld_i8 = epi->ld_i8;
+  p.q = make_qscale(epi->out_i8 != nullptr ? epi->out_scale : 1.0f);
+  const QdwScales sc{dq->scale_hi, dq->scale_lo, dq->scale64};
+  const uint32_t* wt = reinterpret_cast<const uint32_t*>(wq);
+  const int threads = 256;
+  const int c4 = int(c / 4);
+  const int64_t orows = n * oh;
+  if (kh == 3 && kw == 3 && dil_h == 1 && dil_w == 1 && stride_h == stride_w && stride_h <= 2) {
+    const int oxt = stride_h == 1 ? 4 : 2;
+    const int64_t col_groups = (ow + oxt - 1) / oxt;
+    const int tx = c4 < threads ? c4 : threads;
+    const int ty_max = threads / tx;
+    const int ty = int(col_groups < ty_max ? col_groups : ty_max);
+    const dim3 grid(unsigned((col_groups + ty - 1) / ty), unsigned(orows < 65535 ? orows : 65535));
+    if (stride_h == 1) qdwconv3x3_kernel<1, 4><<<grid, dim3(tx, ty), 0, dev->stream>>>(x, ldx, wt, sc, p);
+    else qdwconv3x3_kernel<2, 2><<<grid, dim3(tx, ty), 0, dev->stream>>>(x, ldx, wt, sc, p);
+    return after_launch("qdwconv3x3_kernel");
+  }
+  const int tx = c4 < 32 ? c4 : 32;
+  const int ty = threads / tx;
+  const dim3 grid(unsigned((ow + ty - 1) / ty), unsigned(orows < 65535 ? orows : 65535));
+  qdwconv4_kernel<<<grid, dim3(tx, ty), 0, dev->stream>>>(x, ldx, wt, sc, p);
+  return after_launch("qdwconv4_kernel");
 }
 
 extern "C" int mira_cuda_nchw_to_nhwc_f32(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, float* y,

@@ -541,13 +541,15 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
   const int num_tiles = mn_tiles * p.k_splits;
 
   if (warp == 0) {
-    // ------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // ------------------------------------------------ TMA producer (lane 0; in PATCH mode the whole
+    // warp, whose lanes issue the halo planes' bulk copies together: a copy costs the issuing thread
+    // several hundred cycles, copies issued by different lanes in one instruction overlap)
+    if (lane == 0 || AMODE == QG_A_PATCH) {
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0, patches = 0;
       bool ok = true;
-      if (RKB > 0 && blockIdx.x < num_tiles) {
+      if (RKB > 0 && blockIdx.x < num_tiles && lane == 0) {
         // the whole B operand (one column tile, checked by the host) once for the CTA
         mbar_arrive_expect_tx(bres, p.num_kb * B_BYTES);
         for (int kb = 0; kb < p.num_kb; ++kb) tma_load_2d(sB + kb * B_BYTES, &tmB, kb * BK, 0, bres);
@@ -562,45 +564,51 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
           // the tile's input halo: output slots m0 .. m0 + 127 read input slots m0 - (w + 3) ..
           // m0 + 127 + (w + 3) of every chunk plane (guards and padding ring are zero)
           const int pb = it % Cfg::NHALO;
-          if (!mbar_wait(&pempty[pb], ((it / Cfg::NHALO) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
+          bool free_buf = true;
+          if (lane == 0) free_buf = mbar_wait(&pempty[pb], ((it / Cfg::NHALO) & 1) ^ 1, abort_flag, QG_TIMEOUT_NS);
+          if (!__shfl_sync(0xffffffffu, free_buf ? 1 : 0, 0)) { ok = false; break; }
           const uint32_t pbytes = static_cast<uint32_t>(p.g.patch_slots) * 16u;
           const int planes = p.g.cp >> 4;
-          mbar_arrive_expect_tx(&pfull[pb], planes * pbytes);
+          if (lane == 0) mbar_arrive_expect_tx(&pfull[pb], planes * pbytes);
+          __syncwarp();
           const int8_t* src = p.A + (static_cast<int64_t>(p.g.guard) + m0 - (p.g.ow + 3)) * 16;
-          for (int c = 0; c < planes; ++c)
+          for (int c = lane; c < planes; c += 32)
             bulk_load(sA + pb * PATCH + c * pbytes, src + c * p.g.plane * 16, pbytes, &pfull[pb]);
           ++patches;
           if (RKB > 0) continue;
         }
-        // im2col: traversal position of the tile's first output pixel
-        int iw0 = 0, ih0 = 0, img0 = 0;
-        if (AMODE == QG_A_IM2COL) {
-          const int hw = p.g.oh * p.g.ow;
-          img0 = m0 / hw;
-          const int rem = m0 - img0 * hw;
-          const int oy = rem / p.g.ow;
-          iw0 = (rem - oy * p.g.ow) * p.g.sw - p.g.pw;
-          ih0 = oy * p.g.sh - p.g.ph;
-        }
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], (qg_a_by_tma(AMODE) ? A_BYTES : 0) + (RKB > 0 ? 0 : B_BYTES));
-          if (AMODE == QG_A_TMA) tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, m0, &full[stage]);
+        if (AMODE != QG_A_PATCH || lane == 0) {   // the K-block stages: lane 0 alone
+          // im2col: traversal position of the tile's first output pixel
+          int iw0 = 0, ih0 = 0, img0 = 0;
           if (AMODE == QG_A_IM2COL) {
-            // K-block kb = channels [c0, c0 + BK) of tap (i, j): k = (i * kw + j) * cp + c
-            const int kbyte = kb * BK;
-            const int tap = kbyte / p.g.cp;
-            const int c0 = kbyte - tap * p.g.cp;
-            const int ti = tap / p.g.kw, tj = tap - ti * p.g.kw;
-            tma_load_im2col_4d(sA + stage * A_BYTES, &tmA, c0, iw0, ih0, img0, static_cast<uint16_t>(tj * p.g.dw),
-                               static_cast<uint16_t>(ti * p.g.dh), &full[stage]);
+            const int hw = p.g.oh * p.g.ow;
+            img0 = m0 / hw;
+            const int rem = m0 - img0 * hw;
+            const int oy = rem / p.g.ow;
+            iw0 = (rem - oy * p.g.ow) * p.g.sw - p.g.pw;
+            ih0 = oy * p.g.sh - p.g.ph;
           }
-          if (RKB == 0) tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, n0, &full[stage]);
-          ++issued;
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          for (int kb = kb0; kb < kb1; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, QG_TIMEOUT_NS)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], (qg_a_by_tma(AMODE) ? A_BYTES : 0) + (RKB > 0 ? 0 : B_BYTES));
+            if (AMODE == QG_A_TMA) tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, m0, &full[stage]);
+            if (AMODE == QG_A_IM2COL) {
+              // K-block kb = channels [c0, c0 + BK) of tap (i, j): k = (i * kw + j) * cp + c
+              const int kbyte = kb * BK;
+              const int tap = kbyte / p.g.cp;
+              const int c0 = kbyte - tap * p.g.cp;
+              const int ti = tap / p.g.kw, tj = tap - ti * p.g.kw;
+              tma_load_im2col_4d(sA + stage * A_BYTES, &tmA, c0, iw0, ih0, img0, static_cast<uint16_t>(tj * p.g.dw),
+                                 static_cast<uint16_t>(ti * p.g.dh), &full[stage]);
+            }
+            if (RKB == 0) tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, n0, &full[stage]);
+            ++issued;
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          }
         }
+        if (AMODE == QG_A_PATCH) ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         // let the copies already issued land before the CTA can exit
         for (int i = 1; i <= STAGES && i <= issued; ++i) {
           const int idx = issued - i;
@@ -611,7 +619,7 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
           mbar_wait_drain(&pfull[idx % Cfg::NHALO], (idx / Cfg::NHALO) & 1);
         }
       }
-      if (RKB > 0 && blockIdx.x < num_tiles) mbar_wait_drain(bres, 0);
+      if (RKB > 0 && blockIdx.x < num_tiles && lane == 0) mbar_wait_drain(bres, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer

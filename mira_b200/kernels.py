@@ -271,6 +271,13 @@ def dwconv2d(x, n, h, w, c, wt, kh, kw, stride, padding, dilation, epi: Epi) -> 
               padding[0], padding[1], dilation[0], dilation[1], C.byref(e))
 
 
+def qdwconv2d(x, ldx, n, h, w, c, wq, kh, kw, stride, padding, dilation, dq, epi: Epi) -> None:
+    """Opt-in int8 depthwise conv: x int8 NHWC (pixels ldx bytes apart), wq int8 [kh * kw, c]."""
+    e = epi.struct()
+    _lib.call("mira_cuda_qdwconv2d_nhwc", ptr(x), n, h, w, c, ldx, ptr(wq), kh, kw, stride[0], stride[1],
+              padding[0], padding[1], dilation[0], dilation[1], C.byref(dq), C.byref(e))
+
+
 def elementwise_f32(op: str, shape4, a: View, out: View, b: Optional[View] = None, scalar: float = 0.0,
                     swapped: bool = False) -> None:
     """out = op(a) (unary) or op(a, b-or-scalar) (op(b, a) when swapped) over a 4-D shape."""

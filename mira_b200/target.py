@@ -185,6 +185,14 @@ class CudaDevice:
             (sh, sw), (ph, pw), (dh, dw) = a["stride"], a["padding"], a["dilation"]
             args = (ptr(a["x"]), a["n"], a["h"], a["w"], a["c"], ptr(a["wt"]), a["kh"], a["kw"], sh, sw, ph, pw, dh, dw,
                     C.byref(e))
+        elif k == "qdwconv":
+            e = a["epi"].struct()
+            dq = K.dequant_channel(*a["dq"])
+            keep += [e, dq]
+            fn = L.mira_cuda_qdwconv2d_nhwc
+            (sh, sw), (ph, pw), (dh, dw) = a["stride"], a["padding"], a["dilation"]
+            args = (ptr(a["x"]), a["n"], a["h"], a["w"], a["c"], a["ldx"], ptr(a["wq"]), a["kh"], a["kw"], sh, sw,
+                    ph, pw, dh, dw, C.byref(dq), C.byref(e))
         elif k == "copy":
             fn = L.mira_cuda_d2d
             args = (ptr(a["dst"]), ptr(a["src"]), C.c_size_t(a["nbytes"]))
@@ -975,12 +983,21 @@ class Plan:
     def _op_qconv2d(self, op) -> None:
         a = op.attrs
         stride, padding, dilation, groups = conv_attrs(a)
-        if groups != 1:
-            raise UnsupportedOnCuda("grouped qconv2d")
         x = self.vals[op.inputs[0]]
         n, c, h, w = x.shape
         q = np.asarray(a["q"])
         o, _, kh, kw = q.shape
+        if groups != 1:
+            if not (groups == c == o and q.shape[1] == 1 and c % 4 == 0):
+                raise UnsupportedOnCuda("grouped qconv2d other than depthwise")
+            # opt-in int8 depthwise: int8 NHWC input, tap-major int8 weights, exact integer sums
+            xi8, ldx = self._i8_of(op.inputs[0], _f32(a["x_scale"]))
+            wtap = np.ascontiguousarray(q[:, 0].reshape(c, kh * kw).T.astype(np.int8))
+            out = self._new_out(op.result, "nhwc")
+            self._launch("qdwconv", x=xi8, ldx=ldx, n=n, h=h, w=w, c=c, wq=self._upload(wtap), kh=kh, kw=kw,
+                         stride=stride, padding=padding, dilation=dilation,
+                         dq=self._scales(a["x_scale"], a["w_scale"]), epi=self._epilogue(op, out))
+            return
         xi8, cp, layout, entries = self._conv_input(op.inputs[0], _f32(a["x_scale"]))
         wq = self._conv_weight(q, cp, layout)
         out = self._new_out(op.result, "nhwc")
@@ -1508,6 +1525,14 @@ def _const_row_slice(v) -> bool:
 def supported_reason(op) -> Optional[str]:
     """None if the cuda target runs `op`, else why not (reference Target.check, base.py:22-23)."""
     k = op.kind
+    if k == "qconv2d" and conv_attrs(op.attrs)[3] != 1:
+        # grouped int8 convs exist only in the opt-in int8 depthwise mode (mira_b200.int8_depthwise)
+        groups = conv_attrs(op.attrs)[3]
+        q = np.asarray(op.attrs["q"])
+        c = op.inputs[0].type.shape[1] if op.inputs[0].type.rank == 4 else -1
+        if not (groups == c == q.shape[0] and q.shape[1] == 1 and c % 4 == 0):
+            return "qconv2d: grouped int8 convolutions run on cuda only as depthwise with 4k channels"
+        return None
     if k in QOPS:
         return None
     if op.is_control:

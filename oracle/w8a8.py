@@ -164,6 +164,37 @@ def qconv2d(x: np.ndarray, q: np.ndarray, w_scale: np.ndarray, x_scale: float, s
     return xq, acc, y
 
 
+def int_dwconv2d(xq: np.ndarray, q: np.ndarray, stride, padding, dilation=(1, 1)) -> np.ndarray:
+    """Exact integer depthwise conv (groups == channels) of NCHW int8 xq with int8 q [c, 1, kh, kw],
+    int64 NCHW result: the grouped branch of reference _conv2d_ref (ops.py:265-276; one einsum term
+    per tap and group, `acc +=`) on int8 operands, whose f32 partial sums are integers below 2^24."""
+    n, c, h, w = xq.shape
+    o, cg, kh, kw = q.shape
+    assert cg == 1 and o == c, "a depthwise conv has one weight per channel and tap"
+    (sh, sw), (ph, pw), (dh, dw) = stride, padding, dilation
+    oh, ow = _conv_out(h, kh, sh, ph, dh), _conv_out(w, kw, sw, pw, dw)
+    xp = np.pad(xq.astype(np.int64), ((0, 0), (0, 0), (ph, ph), (pw, pw)))
+    acc = np.zeros((n, c, oh, ow), np.int64)
+    for i in range(kh):
+        for j in range(kw):
+            xt = xp[:, :, i * dh:i * dh + sh * (oh - 1) + 1:sh, j * dw:j * dw + sw * (ow - 1) + 1:sw]
+            acc += xt * q[:, 0, i, j].astype(np.int64).reshape(1, c, 1, 1)
+    return acc
+
+
+def qdwconv2d(x: np.ndarray, q: np.ndarray, w_scale: np.ndarray, x_scale: float, stride, padding,
+              dilation=(1, 1), steps=(), operands=()):
+    """Reference _qconv2d_ref (ops.py:630-634) of a depthwise qconv2d (the opt-in int8 depthwise
+    mode): quantize x, exact integer sums over the taps, dequant f32(f64(acc) * S[c]), epilogue.
+    Returns (xq, acc, y)."""
+    xq = quantize_activation(x, x_scale)
+    acc = int_dwconv2d(xq, q, stride, padding, dilation)
+    s = combined_scale(x_scale, w_scale).reshape(1, -1, 1, 1)
+    y = (acc.astype(np.float64) * s).astype(np.float32)
+    y = epilogue(y, [x, *operands], steps).astype(np.float32)
+    return xq, acc, y
+
+
 def dwconv2d(x: np.ndarray, w: np.ndarray, stride, padding, dilation=(1, 1), steps=(), operands=()):
     """f32 depthwise conv (groups == channels), reference _conv2d_ref ops.py:265-276: per tap (i, j)
     in order, acc += x_tap * w[c, 0, i, j] in float32 starting from 0."""

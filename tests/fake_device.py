@@ -314,6 +314,14 @@ class FakeDevice:
                 cols.append(xp[:, i * dh:i * dh + sh * (oh - 1) + 1:sh, j * dw:j * dw + sw * (ow - 1) + 1:sw, :])
         out.view(np.float32, (n * oh * ow, ld_out))[:, :kh * kw * c] = np.concatenate(cols, axis=-1).reshape(-1, kh * kw * c)
 
+    def _qdwconv(self, x, ldx, n, h, w, c, wq, kh, kw, stride, padding, dilation, dq, epi):
+        xn = x.view(np.int8, (n, h, w, ldx))[..., :c].transpose(0, 3, 1, 2)
+        q = wq.view(np.int8, (kh * kw, c)).T.reshape(c, 1, kh, kw)
+        acc = ref.int_dwconv2d(xn, q, stride, padding, dilation)
+        oh, ow = acc.shape[2:]
+        rows = acc.transpose(0, 2, 3, 1).reshape(n * oh * ow, c)
+        self._epi(self._dequant(rows, dq, c), epi, n * oh * ow, c, geom=(n, oh, ow))
+
     def _dwconv(self, x, n, h, w, c, wt, kh, kw, stride, padding, dilation, epi):
         xn = x.view(np.float32, (n, h, w, c)).transpose(0, 3, 1, 2)
         wk = wt.view(np.float32, (kh * kw, c)).T.reshape(c, 1, kh, kw)

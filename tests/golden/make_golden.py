@@ -3,6 +3,7 @@
     python tests/golden/make_golden.py path/to/reference      (or set $MIRA_PATH)
     python tests/golden/make_golden.py path/to/reference --only-sequence   (sequence.npz alone)
     python tests/golden/make_golden.py path/to/reference --only-weight-only   (weight_only.npz alone)
+    python tests/golden/make_golden.py path/to/reference --only-depthwise   (qdwconv2d.npz alone)
 
 The reference (a pure-Python package) is imported from the given checkout.  Every expected value comes from the
 reference's own code: mira.ops.evaluate for single ops (ops.py:602-634 quantized ops, 192-199
@@ -255,6 +256,59 @@ def weight_only(ref_path: str) -> None:
     _save("weight_only", **out)
 
 
+def depthwise(ref_path: str) -> None:
+    """qdwconv2d.npz: the reference's qconv2d (ops.py:630-634) with groups == channels, the op the
+    opt-in int8 depthwise mode creates, evaluated by mira.ops.evaluate; and MobileNetV2 compiled in
+    that mode (mira_b200.int8_depthwise around compile_ir) on the reference cpu target."""
+    mira, compiler, ir, O, Q = _import_reference(ref_path)
+    rng = np.random.default_rng(20261204)
+    cases = {}
+    cspecs = [
+        dict(n=2, c=32, h=13, w=11, k=3, s=1, p=1, d=1, epi="bias_relu6"),
+        dict(n=2, c=96, h=12, w=12, k=3, s=2, p=1, d=1, epi="bias_relu6"),
+        dict(n=1, c=16, h=9, w=10, k=5, s=1, p=2, d=1, epi="bias"),
+        dict(n=1, c=8, h=10, w=10, k=3, s=1, p=2, d=2, epi="none"),
+        dict(n=2, c=12, h=7, w=9, k=3, s=2, p=0, d=1, epi="bias_relu6"),
+    ]
+    for i, cs in enumerate(cspecs):
+        x = rng.standard_normal((cs["n"], cs["c"], cs["h"], cs["w"])).astype(np.float32)
+        qw, ws = Q.quantize_array(rng.standard_normal((cs["c"], 1, cs["k"], cs["k"])).astype(np.float32), 0)
+        x_scale = float(np.abs(x).max() / 127.0)
+        attrs = {"stride": (cs["s"], cs["s"]), "padding": (cs["p"], cs["p"]), "groups": cs["c"], "q": qw,
+                 "w_scale": ws, "x_scale": x_scale, "dtype": "f32"}
+        if cs["d"] != 1:
+            attrs["dilation"] = (cs["d"], cs["d"])
+        bias = rng.standard_normal((cs["c"], 1, 1)).astype(np.float32)
+        if cs["epi"] == "bias_relu6":
+            steps = (("add", 1, False), ("maximum", 2, False), ("minimum", 3, False))
+            operands = [bias, np.asarray(np.float32(0)), np.asarray(np.float32(6))]
+        elif cs["epi"] == "bias":
+            steps, operands = (("add", 1, False),), [bias]
+        else:
+            steps, operands = (), []
+        if steps:
+            attrs["epilogue"] = steps
+        y = O.evaluate("qconv2d", [x] + operands, attrs)
+        fns, idx, sw = _epi_arrays(steps)
+        cases.update({f"c{i}_x": x, f"c{i}_q": qw, f"c{i}_w_scale": ws, f"c{i}_x_scale": np.float64(x_scale),
+                      f"c{i}_geom": np.array([cs["s"], cs["p"], cs["d"]], np.int64), f"c{i}_fns": fns,
+                      f"c{i}_idx": idx, f"c{i}_sw": sw, f"c{i}_y": y, f"c{i}_n_operands": np.int64(len(operands))})
+        for j, o in enumerate(operands):
+            cases[f"c{i}_op{j}"] = o
+    sys.path.insert(0, str(ROOT))
+    from mira_b200 import configs
+    from mira_b200.depthwise import int8_depthwise
+    g = configs.BUILDERS["mobilenet_v2"](2, image=32)
+    cal = [configs.random_inputs(g, 100 + i) for i in range(2)]
+    with int8_depthwise():
+        prog = compiler.compile_ir(g, "cpu", quantize="w8a8", calibration=cal, precision=None)
+    feeds = configs.random_inputs(g, 1)
+    cases.update({"mbv2_in": feeds["x"], "mbv2_out": prog.run(feeds),
+                  "mbv2_n_grouped_qconv": np.int64(sum(op.kind == "qconv2d" and op.attrs.get("groups", 1) != 1
+                                                       for op in prog.graph.ops))})
+    _save("qdwconv2d", n_cases=np.int64(len(cspecs)), **cases)
+
+
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     path = args[0] if args else os.environ.get("MIRA_PATH")
@@ -264,5 +318,7 @@ if __name__ == "__main__":
         sequence(path)
     elif "--only-weight-only" in sys.argv:
         weight_only(path)
+    elif "--only-depthwise" in sys.argv:
+        depthwise(path)
     else:
         main(path)

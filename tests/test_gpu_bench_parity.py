@@ -41,15 +41,16 @@ def _x_scales(prog):
 _CPU = {}
 
 
-def _cpu_program(name):
-    if name not in _CPU:
-        _CPU[name] = configs.compile_w8a8(name, 1, "cpu", **CALIB)
-    return _CPU[name]
+def _cpu_program(name, **kw):
+    key = (name, tuple(sorted(kw.items())))
+    if key not in _CPU:
+        _CPU[key] = configs.compile_w8a8(name, 1, "cpu", **CALIB, **kw)
+    return _CPU[key]
 
 
-def _check_rows(name: str, batch: int, n_random: int, seed: int):
-    cpu = _cpu_program(name)
-    cuda = configs.compile_w8a8(name, batch, "cuda", **CALIB)
+def _check_rows(name: str, batch: int, n_random: int, seed: int, **kw):
+    cpu = _cpu_program(name, **kw)
+    cuda = configs.compile_w8a8(name, batch, "cuda", **CALIB, **kw)
     assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
     assert _x_scales(cuda) == _x_scales(cpu), "the two compiles must share their activation scales"
     x = np.random.default_rng(seed).standard_normal((batch, 3, 224, 224), dtype=np.float32)
@@ -63,7 +64,7 @@ def _check_rows(name: str, batch: int, n_random: int, seed: int):
         assert want.shape == (1, got.shape[1]) and want.dtype == got.dtype
         if not np.array_equal(got[i:i + 1], want):
             bad.append((i, int((got[i:i + 1] != want).sum())))
-    print(f"{name} batch {batch}: {len(idx)} images compared bit for bit, mismatching images: {bad}")
+    print(f"{name} batch {batch} {kw}: {len(idx)} images compared bit for bit, mismatching images: {bad}")
     assert not bad, f"images with differing logits (image, values): {bad}"
 
 
@@ -82,3 +83,10 @@ def test_resnet18_batch64_rows_bit_exact(cuda_device):
 def test_mobilenet_v2_batch256_rows_bit_exact(cuda_device):
     """MobileNetV2 W8A8 at batch 256: int8 convs, f32 depthwise, global mean."""
     _check_rows("mobilenet_v2", 256, n_random=26, seed=13)
+
+
+@needs_mira
+def test_mobilenet_v2_int8_depthwise_batch256_rows_bit_exact(cuda_device):
+    """The opt-in int8 depthwise mode at the benchmarked size: both programs compiled inside
+    mira_b200.int8_depthwise, the reference cpu target evaluating its grouped qconv2d itself."""
+    _check_rows("mobilenet_v2", 256, n_random=6, seed=14, int8_depthwise=True)

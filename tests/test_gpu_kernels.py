@@ -395,6 +395,54 @@ def test_dwconv_geometries_bit_exact(cuda_device, n, c, h, w, k, stride, pad, di
     _same_f32(yb.download((n, oh, ow, c), np.float32).transpose(0, 3, 1, 2), want)
 
 
+@pytest.mark.parametrize("n,c,h,w,k,stride,pad,dil,epi", [
+    (2, 32, 13, 11, 3, 1, 1, 1, "bias_relu6"),     # 3x3 stride 1: 4 columns per thread
+    (2, 96, 14, 14, 3, 2, 1, 1, "bias_relu6"),     # 3x3 stride 2: 2 columns per thread
+    (1, 960, 7, 7, 3, 1, 1, 1, "bias_relu6"),      # c / 4 above one block of threads
+    (3, 144, 9, 17, 3, 2, 1, 1, "bias"),           # odd widths: partial column groups
+    (2, 16, 11, 9, 5, 1, 2, 1, "bias_relu6"),      # 5x5: the general kernel
+    (1, 8, 10, 10, 3, 1, 2, 2, "none"),            # dilated
+    (2, 12, 7, 9, 3, 2, 0, 1, "bias_relu6"),       # no padding, stride 2, general kernel (c not 16k)
+])
+def test_qdwconv_bit_exact(cuda_device, n, c, h, w, k, stride, pad, dil, epi):
+    """The opt-in int8 depthwise conv against the oracle's restatement of the reference's grouped
+    qconv2d (itself pinned to the reference's outputs): f32 and int8 outputs bit for bit."""
+    K, DB = _k()
+    rng = np.random.default_rng(n * 1000 + c + k)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    q, ws = ref.quantize_array(rng.standard_normal((c, 1, k, k)).astype(np.float32), 0)
+    x_scale = float(np.abs(x).max() / 127.0)
+    bias = rng.standard_normal((c, 1, 1)).astype(np.float32)
+    if epi == "bias_relu6":
+        steps, operands = [("add", 1, False), ("maximum", 2, False), ("minimum", 3, False)], [bias, np.float32(0),
+                                                                                               np.float32(6)]
+        ksteps = [K.Step("add", "channel", ptr=DB.from_array(K.pad_channels(bias))),
+                  K.Step("maximum", "scalar", scalar=0.0), K.Step("minimum", "scalar", scalar=6.0)]
+    elif epi == "bias":
+        steps, operands = [("add", 1, False)], [bias]
+        ksteps = [K.Step("add", "channel", ptr=DB.from_array(K.pad_channels(bias)))]
+    else:
+        steps, operands, ksteps = [], [], []
+    xq, acc, want = ref.qdwconv2d(x, q, ws, x_scale, (stride, stride), (pad, pad), (dil, dil), steps, operands)
+    oh, ow = want.shape[2:]
+    ldx = K.round_up(c, 16)
+    xh = np.zeros((n, h, w, ldx), np.int8)
+    xh[..., :c] = xq.transpose(0, 2, 3, 1)
+    xb = DB.from_array(xh)
+    wb = DB.from_array(np.ascontiguousarray(q[:, 0].reshape(c, k * k).T))
+    keep = [DB.from_array(a) for a in K.scale_arrays(x_scale, ws)]
+    yb = DB(n * oh * ow * c * 4)
+    qb = DB(n * oh * ow * ldx, zero=True)
+    out_scale = float(np.abs(want).max() / 127.0) or 1.0
+    K.qdwconv2d(xb, ldx, n, h, w, c, wb, k, k, (stride, stride), (pad, pad), (dil, dil), K.dequant_channel(*keep),
+                K.Epi(ksteps, out_f32=yb, ld_f32=c, out_i8=qb, ld_i8=ldx, out_scale=out_scale))
+    got = yb.download((n, oh, ow, c), np.float32).transpose(0, 3, 1, 2)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    qgot = qb.download((n, oh, ow, ldx), np.int8)
+    np.testing.assert_array_equal(qgot[..., :c].transpose(0, 3, 1, 2), ref.quantize_activation(want, out_scale))
+    assert not qgot[..., c:].any()
+
+
 def test_layout_roundtrip(cuda_device):
     K, DB = _k()
     x = np.random.default_rng(0).standard_normal((3, 70, 9, 13)).astype(np.float32)

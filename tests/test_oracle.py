@@ -61,6 +61,18 @@ def test_qconv2d_golden(i):
     _same(y, z[f"c{i}_y"])
 
 
+@pytest.mark.parametrize("i", range(5))
+def test_qdwconv2d_golden(i):
+    """The opt-in int8 depthwise op: the reference's own qconv2d with groups == channels."""
+    z = _load("qdwconv2d")
+    s, p, d = (int(v) for v in z[f"c{i}_geom"])
+    ops = [z[f"c{i}_op{j}"] for j in range(int(z[f"c{i}_n_operands"]))]
+    xq, acc, y = ref.qdwconv2d(z[f"c{i}_x"], z[f"c{i}_q"], z[f"c{i}_w_scale"], float(z[f"c{i}_x_scale"]), (s, s),
+                               (p, p), (d, d), steps=_steps(z, i), operands=ops)
+    assert np.abs(acc).max() < 2 ** 24
+    _same(y, z[f"c{i}_y"])
+
+
 def test_f32_ops_golden():
     z = _load("f32_ops")
     _same(ref.maxpool2d(z["pool_x"], 3, 2, 1, -np.inf), z["pool_pad_3_2"])

@@ -83,6 +83,26 @@ def test_mobilenet_v2_small_plan_matches_cpu():
     assert dev.launched.count("dwconv") == 17
 
 
+def test_mobilenet_v2_int8_depthwise_plan_matches_cpu():
+    """The opt-in int8 depthwise mode: both programs compiled inside mira_b200.int8_depthwise (the
+    reference cpu target evaluates the grouped qconv2d itself), the depthwise convs on
+    mira_cuda_qdwconv2d_nhwc, and the reference's stored output of the same program."""
+    from mira_b200 import int8_depthwise
+    z = np.load(Path(__file__).resolve().parent / "golden" / "qdwconv2d.npz")
+    with int8_depthwise():
+        cpu, cuda, dev = _pair("mobilenet_v2", 2, image=32)
+    grouped = [op for op in cuda.graph.ops if op.kind == "qconv2d" and op.attrs.get("groups", 1) != 1]
+    assert len(grouped) == int(z["mbv2_n_grouped_qconv"]) == 17
+    assert [s.device for s in cuda.segments] == ["cuda"], cuda.summary()
+    _check_same(cpu, cuda)
+    assert dev.launched.count("qdwconv") == 17 and dev.launched.count("dwconv") == 0
+    np.testing.assert_array_equal(cuda.run({"x": z["mbv2_in"]}), z["mbv2_out"])
+    # every expansion conv feeding a depthwise conv now writes int8 only
+    with int8_depthwise():
+        cpu2, _, _ = _pair("mobilenet_v2", 2, image=32)
+    np.testing.assert_array_equal(cpu2.run({"x": z["mbv2_in"]}), z["mbv2_out"])
+
+
 CNN_SRC = """
 fn block(x: f32[N, C, H, W], k: f32[O, C, 3, 3], b: f32[O, 1, 1]) -> f32[N, O, H / 2, W / 2] {
   return maxpool2d(relu(conv2d(x, k, padding=1) + b), size=2)
