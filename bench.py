@@ -551,10 +551,13 @@ def profile_case(name: str, reps: int = 3) -> None:
     print(f"profile case {name}: {reps} launches ok", flush=True)
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the 20 convolution launches of one
-# batch-256 ResNet-18 pass, from one ncu capture of the current kernels: the denominator's traffic
-# counterpart of `achieved` (which is also per pass of those 20 launches).
-CONV_DRAM_BYTES_PER_PASS = 2.535e9
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the largest launch of the conv family,
+# ResNet-18's layer-1 3x3 conv with an f32 and an int8 output at batch 256 (`--profile-case
+# conv_l1_cp`, one ncu capture of that kernel: 58.0 MB read, 208.7 MB written), against its 307 MB
+# of algorithmic bytes (51 MB int8 in, 205 MB f32 + 51 MB int8 out; some writes are still in L2
+# when the kernel ends).  A whole pass at a batch small enough for an ncu capture keeps its
+# activations in the 126 MB L2, so its DRAM bytes say nothing about batch 256.
+CONV_L1_DRAM_BYTES = 58.0e6 + 208.7e6
 
 
 def pass_bytes(graph) -> dict:
@@ -1079,8 +1082,9 @@ def main() -> None:
             "roofline": {"bound": "tensor", "kernel": f"{fam_kernels} ({'/'.join(kinds)}, {fam_n} launches/step)",
                          "achieved": achieved, "peak": peak, "unit": "TOPS",
                          "frac": (achieved / peak) if peak else None,
-                         "traffic": CONV_DRAM_BYTES_PER_PASS if headline else None,
-                         "traffic_unit": "DRAM bytes per pass of the 20 conv launches (batch-32 capture x 8)"
+                         "traffic": CONV_L1_DRAM_BYTES if headline else None,
+                         "traffic_unit": "DRAM bytes of one launch of the family's largest kernel (layer-1 3x3 "
+                                         "conv, f32 + int8 out, batch 256; 307 MB algorithmic)"
                          if headline else None,
                          "peak_source": f"2 x bf16_tflops of {src} (dense int8 issues at twice the bf16 rate)",
                          "int8_ops_per_step": fam_ops, "ms_per_step": fam_ms},
