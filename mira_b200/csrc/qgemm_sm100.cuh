@@ -736,8 +736,25 @@ __global__ void __launch_bounds__(QgCfg<BN, STAGES, AMODE, G, POOL, BK, RKB, PAT
     const int group = ew >> 2;
     float* stage = staging + ew * 32 * Cfg::STAGE_PITCH;
     int it = 0;
+    // a residual operand (one f32 row per output row) is read from DRAM in the epilogue; each
+    // thread asks L2 for its rows of the next tile while this one is processed
+    const bool prefetch_res = !POOL && !p.raw && (p.epi_kind & QG_EPI_RES) != 0 &&
+                              p.steps[1].operand == MIRA_OPND_FULL;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const int acc = it % Cfg::ACCS;
+      if (prefetch_res && t + static_cast<int>(gridDim.x) < num_tiles) {
+        const int tn = t + gridDim.x;
+        const int sn = qg_div(tn, p.dv_mntiles), tn_mn = tn - sn * mn_tiles;
+        const int tn_m = qg_div(tn_mn, p.dv_ntiles);
+        const int n0n = (tn_mn - tn_m * p.n_tiles) * BN;
+        const QgRow rn = qg_row<AMODE>(p, tn_m * QG_BM + quarter * 32 + lane);
+        if (rn.ok) {
+          for (int c = group; c < BN / Cfg::CW; c += G) {
+            const int nb = n0n + c * Cfg::CW;
+            if (nb < p.N) prefetch_l2(p.steps[1].ptr + rn.pix * p.steps[1].ld + nb);
+          }
+        }
+      }
       if (!mbar_wait(&tfull[acc], (it / Cfg::ACCS) & 1, abort_flag, QG_TIMEOUT_NS)) break;
       tc_fence_after();
       const int split = qg_div(t, p.dv_mntiles), t_mn = t - split * mn_tiles;
