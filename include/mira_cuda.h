@@ -398,9 +398,20 @@ typedef struct mira_attention {
   mira_view4 out_f32;       /* ptr may be NULL */
   mira_view4 out_i8;        /* ptr may be NULL: int8 requantized with out_scale */
   float out_scale;
+  void* workspace;          /* device scratch for the tensor-core path (k and v split into bf16 pieces),
+                               128-byte aligned; NULL or smaller than mira_cuda_attention_workspace():
+                               the f32 kernel */
+  int64_t workspace_bytes;
 } mira_attention;
 
 int mira_cuda_attention_f32(const mira_attention* a);
+
+/* Bytes of workspace the tensor-core attention path needs for these sizes (0: the shape takes the
+ * f32 FMA kernel).  Prefill (tq >= 64) with dh == 64 and tk <= 16384 runs on the tensor cores:
+ * q @ k^T and p @ v as sums of bf16 piece products (three pieces per f32 value, exact), f32
+ * accumulation in TMEM, the f32 kernel's online softmax.  MIRA_CUDA_ATTENTION=simt in the
+ * environment selects the f32 kernel for every shape. */
+int64_t mira_cuda_attention_workspace(int64_t batch0, int64_t batch1, int64_t tq, int64_t tk, int64_t dh);
 
 /* *out = max |x| over a [n0, n1, n2, n3] f32 view (NaN counts as +inf); out is device memory. */
 int mira_cuda_absmax_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* x, float* out);

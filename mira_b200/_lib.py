@@ -62,7 +62,8 @@ class Attention(C.Structure):
                 ("q", View4), ("k", View4), ("v", View4), ("scale_op", C.c_int32), ("scale", C.c_float),
                 ("mask", View4), ("tile_max", C.c_void_p), ("kmax", C.c_void_p), ("tile_zero", C.c_void_p),
                 ("out_f32", View4),
-                ("out_i8", View4), ("out_scale", C.c_float)]
+                ("out_i8", View4), ("out_scale", C.c_float), ("workspace", C.c_void_p),
+                ("workspace_bytes", C.c_int64)]
 
 
 _i64, _f32, _vp, _i32 = C.c_int64, C.c_float, C.c_void_p, C.c_int
@@ -142,6 +143,7 @@ SIGNATURES: dict[str, tuple] = {
     "mira_cuda_embed_rows": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64]),
     "mira_cuda_copy_view_f32": (_i32, [_i64, _i64, _i64, _i64, C.POINTER(View4), C.POINTER(View4)]),
     "mira_cuda_attention_f32": (_i32, [C.POINTER(Attention)]),
+    "mira_cuda_attention_workspace": (_i64, [_i64, _i64, _i64, _i64, _i64]),
     "mira_cuda_absmax_f32": (_i32, [_i64, _i64, _i64, _i64, C.POINTER(View4), _vp]),
 }
 

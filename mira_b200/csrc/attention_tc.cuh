@@ -1,0 +1,436 @@
+// Prefill attention on the tensor cores, f32-accurate: o = softmax((q @ k^T) * scale + mask) @ v
+// (reference _matmul_ref ops.py:217-219, _softmax_ref 310-313) for a head dimension of 64.
+//
+// The reference computes in float32.  Every f32 operand x is split into three bf16 pieces,
+// x = x0 + x1 + x2 exactly (8 + 8 + 8 significant bits; bf16 has float32's exponent range), and a
+// product x * y is the sum of the six piece products x_i * y_j with i + j <= 2, each exact in the
+// tensor core's f32 accumulator; the three dropped ones are below 2^-24 of |x * y|.  So q @ k^T
+// and p @ v come out of tcgen05.mma.kind::f16 (bf16 operands, f32 accumulation in TMEM) with about
+// the accuracy of f32 FMA sums, in another summation order.
+//
+// A first kernel splits k and v into their pieces once per (batch0, batch1) entry, in the caller's
+// workspace (k as [piece][key][d] rows, v transposed as [piece][d][key] rows).  Then one CTA per
+// 128 query rows walks the key tiles of 64 keys as a pipeline: one thread loads a tile's six piece
+// tiles with TMA (128-byte swizzle, two tiles in flight), one thread issues the 24 MMAs of a score
+// tile S = q k^T into one of two TMEM buffers ahead of the softmax, the four softmax warps (thread
+// i owns query row i, which is TMEM lane i) read their rows, apply the scale step and the mask,
+// update the running maximum and sum exactly as the f32 kernel does (expf(s - m), rescaled partial
+// sums), and write the probabilities' pieces as the A operand of the 24 MMAs of O_tile = p v (two
+// TMEM buffers), which they add to their f32 output rows one tile later, while the next tile's
+// softmax runs.  Key tiles whose mask is all strongly negative are skipped under the f32 kernel's
+// certificate (|scale| ||q_i||_1 max|k| + tile_max - m_i < -110 for every row; else processed at
+// the end).
+#pragma once
+#include <cuda_bf16.h>
+#include "sequence_ops.cuh"
+
+namespace mira {
+
+constexpr int ATC_BQ = 128, ATC_BK = 64, ATC_DH = 64, ATC_PIECES = 3;
+// warps 0-3 softmax (thread i: query row i = TMEM lane i), warp 4 issues the MMAs, warp 5 the TMA
+// loads (eight warps: two per SM sub-partition, so ptxas allows the softmax rows' 255 registers)
+constexpr int ATC_SOFTMAX = 128, ATC_THREADS = 256;
+constexpr int ATC_MAX_KB = 256;   // key tiles of a row (tk <= 16384)
+constexpr uint64_t ATC_TIMEOUT_NS = 2000000000ull;
+
+struct AtcSmem {
+  // 128-byte-swizzled K-major tiles (rows of 64 bf16 values), one per bf16 piece
+  uint8_t q[ATC_PIECES][ATC_BQ * 128];       // [query][d]
+  uint8_t k[2][ATC_PIECES][ATC_BK * 128];    // [key][d], two tiles in flight
+  uint8_t vt[2][ATC_PIECES][ATC_DH * 128];   // [d][key]
+  uint8_t p[ATC_PIECES][ATC_BQ * 128];       // [query][key]
+  uint64_t kv_full[2], kv_empty[2], s_full[2], s_empty[2], o_full[2], o_empty[2], p_full, p_empty, drain;
+  uint32_t tmem;
+  int abort;
+  float qn1[ATC_BQ];
+  int16_t tiles[ATC_MAX_KB];   // the key tiles that are not skipping candidates, in order
+  uint8_t cand[ATC_MAX_KB];    // 1: a skipping candidate
+  int n_main;
+};
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled tile (8-row atoms of
+// 1 KB, the chunk index XOR the row within the atom): the layout TMA's 128-byte swizzle writes.
+__device__ __forceinline__ int atc_sw128(int row, int chunk) {
+  return (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ void atc_split(float x, uint32_t (&b)[ATC_PIECES]) {
+  const __nv_bfloat16 a0 = __float2bfloat16_rn(x);
+  const float r0 = __fsub_rn(x, __bfloat162float(a0));
+  const __nv_bfloat16 a1 = __float2bfloat16_rn(r0);
+  const float r1 = __fsub_rn(r0, __bfloat162float(a1));
+  const __nv_bfloat16 a2 = __float2bfloat16_rn(r1);
+  b[0] = __bfloat16_as_ushort(a0);
+  b[1] = __bfloat16_as_ushort(a1);
+  b[2] = __bfloat16_as_ushort(a2);
+}
+
+// The three pieces of 8 values as three 16-byte words.
+__device__ __forceinline__ void atc_pack8(const float (&x)[8], uint4 (&w)[ATC_PIECES]) {
+  uint32_t t[ATC_PIECES][4];
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    uint32_t lo[ATC_PIECES], hi[ATC_PIECES];
+    atc_split(x[e], lo);
+    atc_split(x[e + 1], hi);
+#pragma unroll
+    for (int pc = 0; pc < ATC_PIECES; ++pc) t[pc][e >> 1] = lo[pc] | (hi[pc] << 16);
+  }
+#pragma unroll
+  for (int pc = 0; pc < ATC_PIECES; ++pc) w[pc] = make_uint4(t[pc][0], t[pc][1], t[pc][2], t[pc][3]);
+}
+
+// Splits 8 values and stores their pieces as 16-byte chunk `chunk` of row `row` of three
+// consecutive swizzled tiles of `tile_bytes` each.
+__device__ __forceinline__ void atc_store8(uint8_t* base, int tile_bytes, int row, int chunk, const float (&x)[8]) {
+  uint4 w[ATC_PIECES];
+  atc_pack8(x, w);
+  const int off = atc_sw128(row, chunk);
+#pragma unroll
+  for (int pc = 0; pc < ATC_PIECES; ++pc) *reinterpret_cast<uint4*>(base + pc * tile_bytes + off) = w[pc];
+}
+
+// The 24 MMAs of D = A B^T over K = 64: six piece pairs (i + j <= 2) x four K-steps of 16.
+__device__ __forceinline__ void atc_mma(uint32_t d_tmem, const uint8_t* a_tiles, int a_bytes, const uint8_t* b_tiles,
+                                        int b_bytes) {
+  constexpr uint32_t IDESC = idesc_bf16(ATC_BQ, 64);
+  constexpr int PI[6] = {0, 0, 1, 0, 1, 2}, PJ[6] = {0, 1, 0, 2, 1, 0};
+  bool first = true;
+#pragma unroll
+  for (int t = 0; t < 6; ++t) {
+    const uint64_t ad = smem_desc_k_sw128(smem_u32(a_tiles + PI[t] * a_bytes));
+    const uint64_t bd = smem_desc_k_sw128(smem_u32(b_tiles + PJ[t] * b_bytes));
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      mma_bf16(d_tmem, ad + 2 * ks, bd + 2 * ks, IDESC, first ? 0u : 1u);
+      first = false;
+    }
+  }
+}
+
+// k and v of one key tile of one (batch0, batch1) entry into pieces: kpc[((bh * 3 + piece) * tkp +
+// key) * 64 + d] and vtc[((bh * 3 + piece) * 64 + d) * tkp + key] (bf16), keys past tk 0.
+__global__ void __launch_bounds__(256) attention_pieces_kernel(const AttnParams p, int tkp, uint16_t* __restrict__ kpc,
+                                                               uint16_t* __restrict__ vtc) {
+  const int k0 = blockIdx.x * ATC_BK;
+  const int64_t b1 = blockIdx.y, b0 = blockIdx.z, bh = b0 * gridDim.y + b1;
+  const float* kp = p.k + b0 * p.ks[0] + b1 * p.ks[1];
+  const float* vp = p.v + b0 * p.vs[0] + b1 * p.vs[1];
+  for (int task = threadIdx.x; task < ATC_BK * 8; task += blockDim.x) {
+    const int j = task >> 3, ch = task & 7;   // k: key k0 + j, d 8 ch .. 8 ch + 7
+    float x[8];
+    if (k0 + j < p.tk && p.vec) {
+      const float4* src = reinterpret_cast<const float4*>(kp + int64_t(k0 + j) * p.ks[2] + 8 * ch);
+      const float4 a = __ldg(src), c = __ldg(src + 1);
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        x[e] = k0 + j < p.tk ? __ldg(kp + int64_t(k0 + j) * p.ks[2] + int64_t(8 * ch + e) * p.ks[3]) : 0.0f;
+    }
+    uint4 w[ATC_PIECES];
+    atc_pack8(x, w);
+#pragma unroll
+    for (int pc = 0; pc < ATC_PIECES; ++pc)
+      *reinterpret_cast<uint4*>(kpc + ((bh * ATC_PIECES + pc) * tkp + k0 + j) * ATC_DH + 8 * ch) = w[pc];
+  }
+  for (int task = threadIdx.x; task < ATC_DH * 8; task += blockDim.x) {
+    const int n = task & (ATC_DH - 1), kc = task >> 6;   // v: d n, keys k0 + 8 kc .. + 7
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = k0 + 8 * kc + e;
+      x[e] = j < p.tk ? __ldg(vp + int64_t(j) * p.vs[2] + int64_t(n) * p.vs[3]) : 0.0f;
+    }
+    uint4 w[ATC_PIECES];
+    atc_pack8(x, w);
+#pragma unroll
+    for (int pc = 0; pc < ATC_PIECES; ++pc)
+      *reinterpret_cast<uint4*>(vtc + ((bh * ATC_PIECES + pc) * ATC_DH + n) * int64_t(tkp) + k0 + 8 * kc) = w[pc];
+  }
+}
+
+__global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __grid_constant__ CUtensorMap map_k,
+                                                                      const __grid_constant__ CUtensorMap map_vt,
+                                                                      const AttnParams p, int tkp) {
+  extern __shared__ uint8_t atc_raw[];
+  AtcSmem& sm = *reinterpret_cast<AtcSmem*>((reinterpret_cast<uintptr_t>(atc_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int nqb = (p.tq + ATC_BQ - 1) / ATC_BQ, nkb = (p.tk + ATC_BK - 1) / ATC_BK;
+  const int qb = nqb - 1 - static_cast<int>(blockIdx.x);     // the longest rows first
+  const int q0 = qb * ATC_BQ;
+  const int64_t b1 = blockIdx.y, b0 = blockIdx.z;
+  const int64_t bh = b0 * gridDim.y + b1;
+  const float* qp = p.q + b0 * p.qs[0] + b1 * p.qs[1];
+  const float* mp = p.mask != nullptr ? p.mask + b0 * p.ms[0] + b1 * p.ms[1] : nullptr;
+  volatile int* abort_flag = &sm.abort;
+
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.kv_full[b], 1);
+      mbar_init(&sm.kv_empty[b], 1);
+      mbar_init(&sm.s_full[b], 1);
+      mbar_init(&sm.s_empty[b], ATC_SOFTMAX);
+      mbar_init(&sm.o_full[b], 1);
+      mbar_init(&sm.o_empty[b], ATC_SOFTMAX);
+    }
+    mbar_init(&sm.p_full, ATC_SOFTMAX);
+    mbar_init(&sm.p_empty, 1);
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_vt);
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem, 256);   // S buffers in columns 0..127, O_tile buffers in 128..255
+    tmem_relinquish();
+  }
+  // q rows (zero past tq) as pieces; ||q_i||_1 for the skipping certificate
+  for (int task = tid; task < ATC_BQ * 8; task += ATC_THREADS) {
+    const int row = task >> 3, ch = task & 7;
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      x[e] = q0 + row < p.tq ? __ldg(qp + int64_t(q0 + row) * p.qs[2] + int64_t(8 * ch + e) * p.qs[3]) : 0.0f;
+    atc_store8(&sm.q[0][0], sizeof(sm.q[0]), row, ch, x);
+  }
+  if (tid < ATC_BQ) {
+    float a = 0.0f;
+    if (q0 + tid < p.tq)
+      for (int d = 0; d < ATC_DH; ++d) a += fabsf(__ldg(qp + int64_t(q0 + tid) * p.qs[2] + int64_t(d) * p.qs[3]));
+    sm.qn1[tid] = a;
+  }
+  // skipping candidates once, into shared memory: tile_max / tile_zero describe 64 x 64 (query,
+  // key) tiles, this block holds two 64-row halves
+  const bool can_skip = p.tile_max != nullptr && p.kmax != nullptr;
+  const int nqb64 = (p.tq + 63) / 64;
+  auto tile_max = [&](int kb) {
+    float t = __ldg(p.tile_max + int64_t(2 * qb) * nkb + kb);
+    if (2 * qb + 1 < nqb64) t = fmaxf(t, __ldg(p.tile_max + int64_t(2 * qb + 1) * nkb + kb));
+    return t;
+  };
+  for (int kb = tid; kb < nkb; kb += ATC_THREADS) sm.cand[kb] = can_skip && tile_max(kb) <= -200.0f ? 1 : 0;
+  fence_proxy_async_smem();   // generic-proxy writes of q read by tcgen05.mma
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0) {
+    int n = 0;
+    for (int kb = 0; kb < nkb; ++kb)
+      if (!sm.cand[kb]) sm.tiles[n++] = static_cast<int16_t>(kb);
+    sm.n_main = n;
+  }
+  __syncthreads();
+  const uint32_t tmem = sm.tmem;
+
+  // softmax state of query row r = q0 + tid (threads 0..127)
+  const int r = q0 + tid;
+  float m = -INFINITY, l = 0.0f;
+  float o[ATC_DH];
+#pragma unroll
+  for (int d = 0; d < ATC_DH; ++d) o[d] = 0.0f;
+  uint32_t seq = 0;   // tiles through the pipeline so far (mbarrier phases); the same in every role
+
+  // Runs key tiles list(0) .. list(count - 1) through the pipeline (every role calls it with the
+  // same list).
+  auto run = [&](int count, auto list) {
+    if (warp == 5) {
+      // ------------------------------------------------ producer: a tile's six piece tiles by TMA
+      if ((tid & 31) == 0) {
+        int issued = 0;
+        for (int i = 0; i < count; ++i) {
+          const uint32_t sq = seq + i, b = sq & 1;
+          if (!mbar_wait(&sm.kv_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
+          ++issued;
+          const int k0 = list(i) * ATC_BK;
+          mbar_arrive_expect_tx(&sm.kv_full[b], 2 * ATC_PIECES * ATC_BK * 128);
+#pragma unroll
+          for (int pc = 0; pc < ATC_PIECES; ++pc) {
+            tma_load_2d(&sm.k[b][pc][0], &map_k, 0, static_cast<int32_t>((bh * ATC_PIECES + pc) * tkp + k0),
+                        &sm.kv_full[b]);
+            tma_load_2d(&sm.vt[b][pc][0], &map_vt, k0, static_cast<int32_t>((bh * ATC_PIECES + pc) * ATC_DH),
+                        &sm.kv_full[b]);
+          }
+        }
+        if (*abort_flag) {
+          // let the copies still in flight land before the shared memory goes away (bounded)
+          for (int i = issued > 2 ? issued - 2 : 0; i < issued; ++i) {
+            const uint32_t sq = seq + i;
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait_suspend(&sm.kv_full[sq & 1], (sq >> 1) & 1, 1000000u) &&
+                   globaltimer_ns() - t0 < ATC_TIMEOUT_NS) {
+            }
+          }
+        }
+      }
+    } else if (warp == 4) {
+      // ------------------------------------------------ MMA issuer: S one tile ahead of p v
+      if ((tid & 31) == 0) {
+        auto issue_s = [&](uint32_t sq) {
+          const uint32_t b = sq & 1;
+          if (!mbar_wait(&sm.kv_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) return false;
+          if (!mbar_wait(&sm.s_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) return false;
+          tc_fence_after();
+          atc_mma(tmem + 64 * b, &sm.q[0][0], sizeof(sm.q[0]), &sm.k[b][0][0], sizeof(sm.k[0][0]));
+          mma_commit(&sm.s_full[b]);
+          return true;
+        };
+        bool ok = count > 0 ? issue_s(seq) : true;
+        for (int i = 0; i < count && ok; ++i) {
+          const uint32_t sq = seq + i, b = sq & 1;
+          if (i + 1 < count && !issue_s(sq + 1)) break;
+          if (!mbar_wait(&sm.p_full, sq & 1, abort_flag, ATC_TIMEOUT_NS)) break;
+          if (!mbar_wait(&sm.o_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
+          tc_fence_after();
+          atc_mma(tmem + 128 + 64 * b, &sm.p[0][0], sizeof(sm.p[0]), &sm.vt[b][0][0], sizeof(sm.vt[0][0]));
+          mma_commit(&sm.o_full[b]);
+          mma_commit(&sm.p_empty);
+          mma_commit(&sm.kv_empty[b]);
+        }
+      }
+    } else if (warp < 4) {
+      // ------------------------------------------------ softmax rows
+      const uint32_t lane_base = static_cast<uint32_t>(warp) * 32u << 16;
+      const int half = tid >> 6;   // which 64-row half of the block this row is in
+      auto add_o = [&](uint32_t sq) {   // the p v tile of sq into the output row
+        const uint32_t b = sq & 1;
+        if (!mbar_wait(&sm.o_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) return;
+        tc_fence_after();
+        uint32_t raw[32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          tmem_ld_32x32b_x32(tmem + lane_base + 128 + 64 * b + 32 * h, raw);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[32 * h + c] += __uint_as_float(raw[c]);
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.o_empty[b]);
+      };
+      for (int i = 0; i < count; ++i) {
+        const uint32_t sq = seq + i, b = sq & 1;
+        const int kb = list(i), k0 = kb * ATC_BK;
+        // a mask tile of +0 only adds nothing (x + 0 turns -0 into +0, which leaves exp(x - m) alone)
+        const bool zero_mask = p.tile_zero != nullptr && 2 * qb + half < nqb64 &&
+                               __ldg(p.tile_zero + int64_t(2 * qb + half) * nkb + kb) != 0;
+        float s[ATC_BK];
+        if (!mbar_wait(&sm.s_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
+        tc_fence_after();
+        {
+          uint32_t raw[32];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tmem_ld_32x32b_x32(tmem + lane_base + 64 * b + 32 * h, raw);
+            tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) s[32 * h + c] = __uint_as_float(raw[c]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.s_empty[b]);
+        if (p.scale_op == MIRA_EPI_MUL) {
+#pragma unroll
+          for (int c = 0; c < ATC_BK; ++c) s[c] = __fmul_rn(s[c], p.scale);
+        } else if (p.scale_op == MIRA_EPI_DIV) {
+#pragma unroll
+          for (int c = 0; c < ATC_BK; ++c) s[c] = __fdiv_rn(s[c], p.scale);
+        }
+        if (mp != nullptr && !zero_mask && r < p.tq) {
+          // the row's 64 mask values: all loads issued before the first add
+          const float* mrow = mp + int64_t(r) * p.ms[2];
+          float mk[ATC_BK];
+          if (p.ms[3] == 1 && (reinterpret_cast<uintptr_t>(mrow + k0) & 15) == 0 && k0 + ATC_BK <= p.tk) {
+#pragma unroll
+            for (int c = 0; c < ATC_BK; c += 4) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(mrow + k0 + c));
+              mk[c] = t.x; mk[c + 1] = t.y; mk[c + 2] = t.z; mk[c + 3] = t.w;
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < ATC_BK; ++c) mk[c] = k0 + c < p.tk ? __ldg(mrow + int64_t(k0 + c) * p.ms[3]) : 0.0f;
+          }
+#pragma unroll
+          for (int c = 0; c < ATC_BK; ++c) s[c] = __fadd_rn(s[c], mk[c]);
+        }
+        float rmax = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < ATC_BK; ++c) {
+          if (k0 + c >= p.tk) s[c] = -INFINITY;
+          rmax = fmaxf(rmax, s[c]);
+        }
+        const float mnew = fmaxf(m, rmax);
+        const float corr = (mnew == -INFINITY) ? 1.0f : expf(m - mnew);
+        float rsum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < ATC_BK; ++c) {
+          const float e = (mnew == -INFINITY) ? 0.0f : expf(s[c] - mnew);
+          s[c] = e;
+          rsum += e;
+        }
+        l = fmaf(l, corr, rsum);
+        m = mnew;
+        if (!mbar_wait(&sm.p_empty, (sq & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = s[8 * ch + e];
+          atc_store8(&sm.p[0][0], sizeof(sm.p[0]), tid, ch, x);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&sm.p_full);
+        // the previous tile's p v (at the previous maximum), then this tile's rescale
+        if (i > 0) add_o(sq - 1);
+#pragma unroll
+        for (int d = 0; d < ATC_DH; ++d) o[d] *= corr;
+      }
+      if (count > 0 && !*abort_flag) add_o(seq + count - 1);
+    }
+    seq += count;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  };
+
+  run(sm.n_main, [&](int i) { return static_cast<int>(sm.tiles[i]); });
+  if (can_skip && !*abort_flag) {
+    const float kmax = __uint_as_float(__ldg(p.kmax));
+    for (int kb = 0; kb < nkb && !*abort_flag; ++kb) {
+      if (!sm.cand[kb]) continue;
+      bool ok = true;
+      if (tid < ATC_BQ && r < p.tq) {
+        // every score of this tile is at most this bound (the factor covers the products' rounding)
+        const float bound = p.scale_abs * sm.qn1[tid] * kmax * 1.001f + tile_max(kb);
+        ok = bound - m < -110.0f;
+      }
+      if (!__syncthreads_and(ok)) run(1, [&](int) { return kb; });
+    }
+  }
+  if (tid < ATC_BQ && r < p.tq && !*abort_flag) {
+#pragma unroll
+    for (int d = 0; d < ATC_DH; ++d) {
+      const float y = __fdiv_rn(o[d], l);
+      if (p.out != nullptr) p.out[b0 * p.os[0] + b1 * p.os[1] + int64_t(r) * p.os[2] + int64_t(d) * p.os[3]] = y;
+      if (p.out_i8 != nullptr)
+        p.out_i8[b0 * p.is[0] + b1 * p.is[1] + int64_t(r) * p.is[2] + int64_t(d) * p.is[3]] =
+            static_cast<int8_t>(quant_byte(y, p.q8) & 0xff);
+    }
+  }
+  if (tid == ATC_SOFTMAX) {
+    // every MMA this thread issued has finished once `drain` completes (bounded wait)
+    mma_commit(&sm.drain);
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait_suspend(&sm.drain, 0, 1000000u) && globaltimer_ns() - t0 < ATC_TIMEOUT_NS) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+  if (tid == 0 && *abort_flag) atomicExch(p.err, 2);
+}
+
+}  // namespace mira

@@ -20,6 +20,7 @@
 #include "dw_staged.cuh"
 #include "runtime.h"
 #include "sequence_ops.cuh"
+#include "attention_tc.cuh"
 
 // Set by a kernel that gave up on a bounded wait or met an impossible index; read and cleared by
 // mira_cuda_sync.  One copy per device (module global).
@@ -1776,6 +1777,62 @@ static int launch_attention(DeviceState* dev, const AttnParams& p, int64_t b0, i
   return after_launch("attention_f32_kernel");
 }
 
+// Whether the tensor-core kernel takes a shape, and its workspace: k and v as three bf16 pieces.
+static bool attention_tc_shape(int64_t tq, int64_t tk, int64_t dh) {
+  const char* choice = std::getenv("MIRA_CUDA_ATTENTION");   // "simt": the f32 FMA kernel, for comparisons
+  const bool simt = choice != nullptr && std::strcmp(choice, "simt") == 0;
+  return dh == ATC_DH && tq >= 64 && tk > 0 && tk <= int64_t(ATC_MAX_KB) * ATC_BK && !simt;
+}
+
+static int64_t attention_tc_bytes(int64_t b0, int64_t b1, int64_t tk) {
+  const int64_t tkp = (tk + ATC_BK - 1) / ATC_BK * ATC_BK;
+  // the TMA row coordinates of the piece arrays are 32-bit
+  if (b0 * b1 * ATC_PIECES * tkp >= (int64_t(1) << 31)) return 0;
+  return 2 * b0 * b1 * ATC_PIECES * tkp * ATC_DH * 2;
+}
+
+// The tensor-core path (attention_tc.cuh): k and v into pieces, then 128 query rows per CTA.
+static int launch_attention_tc(DeviceState* dev, const AttnParams& p, int64_t b0, int64_t b1, void* ws) {
+  const int smem = static_cast<int>(sizeof(AtcSmem)) + 1024;
+  static bool configured[64] = {};
+  if (!configured[dev->device & 63]) {
+    MIRA_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                  "cudaFuncSetAttribute(attention_tc)");
+    configured[dev->device & 63] = true;
+  }
+  const int64_t tkp = (p.tk + ATC_BK - 1) / ATC_BK * ATC_BK;
+  const int64_t bh = b0 * b1;
+  uint16_t* kpc = static_cast<uint16_t*>(ws);
+  uint16_t* vtc = kpc + bh * ATC_PIECES * tkp * ATC_DH;
+  attention_pieces_kernel<<<dim3(unsigned(tkp / ATC_BK), unsigned(b1), unsigned(b0)), 256, 0, dev->stream>>>(
+      p, int(tkp), kpc, vtc);
+  const int rc = after_launch("attention_pieces_kernel");
+  if (rc != MIRA_CUDA_OK) return rc;
+  CUtensorMap map_k, map_vt;
+  const cuuint32_t estr[2] = {1, 1};
+  {
+    const cuuint64_t dims[2] = {cuuint64_t(ATC_DH), cuuint64_t(bh * ATC_PIECES * tkp)};
+    const cuuint64_t strides[1] = {cuuint64_t(ATC_DH * 2)};
+    const cuuint32_t box[2] = {cuuint32_t(ATC_DH), cuuint32_t(ATC_BK)};
+    const CUresult r = g_encode_tiled(&map_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kpc, dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  }
+  {
+    const cuuint64_t dims[2] = {cuuint64_t(tkp), cuuint64_t(bh * ATC_PIECES * ATC_DH)};
+    const cuuint64_t strides[1] = {cuuint64_t(tkp * 2)};
+    const cuuint32_t box[2] = {cuuint32_t(ATC_BK), cuuint32_t(ATC_DH)};
+    const CUresult r = g_encode_tiled(&map_vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, vtc, dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(MIRA_CUDA_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  }
+  const dim3 grid(unsigned((p.tq + ATC_BQ - 1) / ATC_BQ), unsigned(b1), unsigned(b0));
+  attention_tc_kernel<<<grid, ATC_THREADS, smem, dev->stream>>>(map_k, map_vt, p, int(tkp));
+  return after_launch("attention_tc_kernel");
+}
+
 }  // namespace mira
 
 extern "C" int mira_cuda_attention_f32(const mira_attention* a) {
@@ -1815,6 +1872,7 @@ extern "C" int mira_cuda_attention_f32(const mira_attention* a) {
   p.out = static_cast<float*>(a->out_f32.ptr);
   p.out_i8 = static_cast<int8_t*>(a->out_i8.ptr);
   p.q8 = make_qscale(p.out_i8 != nullptr ? a->out_scale : 1.0f);
+  p.err = device_err_ptr();
   if (p.tq == 1 && p.vec) {       // one query row (a decode step): stream the keys and values once
     const dim3 grid(unsigned(a->batch1), unsigned(a->batch0));
     if (a->dh <= 32) attention_q1_kernel<32><<<grid, ATT1_WARPS * 32, 0, dev->stream>>>(p);
@@ -1822,9 +1880,20 @@ extern "C" int mira_cuda_attention_f32(const mira_attention* a) {
     else attention_q1_kernel<128><<<grid, ATT1_WARPS * 32, 0, dev->stream>>>(p);
     return after_launch("attention_q1_kernel");
   }
+  // prefill with a head dimension of 64 and a workspace: the tensor-core path
+  if (attention_tc_shape(a->tq, a->tk, a->dh) && a->workspace != nullptr &&
+      (reinterpret_cast<uintptr_t>(a->workspace) & 127) == 0 &&
+      attention_tc_bytes(a->batch0, a->batch1, a->tk) > 0 &&
+      a->workspace_bytes >= attention_tc_bytes(a->batch0, a->batch1, a->tk))
+    return launch_attention_tc(dev, p, a->batch0, a->batch1, a->workspace);
   if (a->dh <= 32) return launch_attention<32>(dev, p, a->batch0, a->batch1);
   if (a->dh <= 64) return launch_attention<64>(dev, p, a->batch0, a->batch1);
   return launch_attention<128>(dev, p, a->batch0, a->batch1);
+}
+
+extern "C" int64_t mira_cuda_attention_workspace(int64_t batch0, int64_t batch1, int64_t tq, int64_t tk, int64_t dh) {
+  if (batch0 <= 0 || batch1 <= 0 || !attention_tc_shape(tq, tk, dh)) return 0;
+  return attention_tc_bytes(batch0, batch1, tk);
 }
 
 extern "C" int mira_cuda_absmax_f32(int64_t n0, int64_t n1, int64_t n2, int64_t n3, const mira_view4* x, float* out) {

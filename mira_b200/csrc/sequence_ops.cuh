@@ -721,6 +721,7 @@ struct AttnParams {
   int8_t* out_i8;
   int64_t is[4];
   QuantScale q8;
+  int* err;                 // kernel error record (the tensor-core kernel's bounded waits)
 };
 
 // Row-major tiles with a 4-float pad: a thread reads rows ty + 16u of q and tx + 16v of k as

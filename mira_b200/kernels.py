@@ -447,6 +447,8 @@ class Attn:
     out: Optional[View] = None
     out_i8: Optional[View] = None
     out_scale: float = 1.0
+    workspace: object = None      # scratch of attention_workspace() bytes: the tensor-core path
+    workspace_bytes: int = 0
 
     def struct(self) -> _lib.Attention:
         a = _lib.Attention()
@@ -464,6 +466,8 @@ class Attn:
         if self.out_i8 is not None:
             a.out_i8 = self.out_i8.struct()
         a.out_scale = float(np.float32(self.out_scale))
+        a.workspace = ptr(self.workspace).value or 0
+        a.workspace_bytes = int(self.workspace_bytes)
         return a
 
 
@@ -483,6 +487,11 @@ def mask_tile_zero(mask: np.ndarray, tq: int, tk: int) -> np.ndarray:
     padded = np.ones((nq * ATT_TILE, nk * ATT_TILE), bool)
     padded[:tq, :tk] = plus_zero
     return padded.reshape(nq, ATT_TILE, nk, ATT_TILE).all(axis=(1, 3)).astype(np.uint8)
+
+
+def attention_workspace(batch0: int, batch1: int, tq: int, tk: int, dh: int) -> int:
+    """Bytes of scratch for the tensor-core attention path (0: the f32 kernel takes the shape)."""
+    return int(_lib.load().mira_cuda_attention_workspace(batch0, batch1, tq, tk, dh))
 
 
 def attention_f32(desc: Attn) -> None:

@@ -67,6 +67,9 @@ class CudaDevice:
     def qgemm_workspace(self, m: int, n: int, k: int) -> int:
         return K.qgemm_workspace(m, n, k)
 
+    def attention_workspace(self, b0: int, b1: int, tq: int, tk: int, dh: int) -> int:
+        return K.attention_workspace(b0, b1, tq, tk, dh)
+
     def h2d(self, dst, src: PinnedBuffer, nbytes: int) -> None:
         _lib.call("mira_cuda_h2d", ptr(dst), ptr(src), C.c_size_t(nbytes))
 
@@ -397,6 +400,7 @@ class Plan:
         self.skipped: set = set()
         self.kernel_counts: dict = {}
         self._kmax = None            # device scalar max|k| shared by the attention launches
+        self._attn_ws, self._attn_ws_bytes = None, 0   # tensor-core attention scratch
         self.w8_cache: dict = {}     # weight-only int8 matmul weights: value -> (int8 DVal, scales)
         self.aliases: dict = {}      # dynamic_update_slice result -> the graph input it updated in place
         self._build()
@@ -1217,6 +1221,14 @@ class Plan:
             self._launch("absmax", shape=cshape, x=K.View(kv.buf, cst, kv.offset), out=kmax)
         desc = K.Attn(batch[0], batch[1], tq, tk, dh, qv, kv, vv, info["scale_op"], info["scale"], mask_view,
                       tile_max, kmax, tile_zero)
+        # scratch of the tensor-core path (k and v split into bf16 pieces): one buffer, sized for the
+        # largest attention of the plan, reused by every launch (they run in order on one stream)
+        fn = getattr(self.dev, "attention_workspace", None)
+        ws = int(fn(batch[0], batch[1], tq, tk, dh)) if fn is not None else 0
+        if ws > 0:
+            if self._attn_ws is None or self._attn_ws_bytes < ws:
+                self._attn_ws, self._attn_ws_bytes = self._alloc(ws), ws
+            desc.workspace, desc.workspace_bytes = self._attn_ws, self._attn_ws_bytes
         chain = info["i8_chain"]
         if chain is not None:
             rs = chain[1]

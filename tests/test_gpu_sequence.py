@@ -227,6 +227,9 @@ def _attention_case(K, DB, b0, b1, t, dh, seed, amp=1.0, mask=True, skip=True, s
         K.absmax_f32((b0, b1, t, dh), K.View(kb, st), kmax)
     desc = K.Attn(b0, b1, t, t, dh, K.View(qb, st), K.View(kb, st), K.View(vb, st), scale_op, scale,
                   K.View(mb, (0, 0, t, 1)) if mask else None, tile_max, kmax, tile_zero, out=K.View(ob, st))
+    ws = K.attention_workspace(b0, b1, t, t, dh)      # the tensor-core path where it applies
+    if ws > 0:
+        desc.workspace, desc.workspace_bytes = DB(ws), ws
     qi8 = None
     if i8_scale is not None:
         qi8 = DB(q.size, zero=True)
@@ -280,6 +283,25 @@ def test_single_query_attention_matches_reference_chain(cuda_device, b0, b1, tk,
     got = ob.download(q.shape, np.float32)
     np.testing.assert_allclose(got, want, rtol=0, atol=3e-6 * np.abs(v).max())
     np.testing.assert_array_equal(ib.download(q.shape, np.int8), ref.quantize_activation(got, out_scale))
+
+
+@pytest.mark.parametrize("b0,b1,t", [(1, 12, 1024), (2, 3, 333), (1, 2, 128)])
+@pytest.mark.parametrize("skip", [True, False])
+def test_tensor_core_attention_matches_reference_and_f32_kernel(cuda_device, monkeypatch, b0, b1, t, skip):
+    """The prefill shape of config 5 (d_head 64) runs on the tensor-core path (bf16 three-piece
+    split, f32 accumulation); the same tolerance against the reference's three ops as the f32 FMA
+    kernel, and both kernels within that tolerance of each other."""
+    K, DB = _k()
+    assert K.attention_workspace(b0, b1, t, t, 64) > 0
+    got, want, v, _ = _attention_case(K, DB, b0, b1, t, 64, t + 1, skip=skip)
+    tol = 3e-6 * np.abs(v).max()
+    np.testing.assert_allclose(got, want, rtol=0, atol=tol)
+    monkeypatch.setenv("MIRA_CUDA_ATTENTION", "simt")
+    assert K.attention_workspace(b0, b1, t, t, 64) == 0
+    got_simt, _, _, _ = _attention_case(K, DB, b0, b1, t, 64, t + 1, skip=skip)
+    np.testing.assert_allclose(got, got_simt, rtol=0, atol=tol)
+    print(f"max |tc - ref| {np.abs(got - want).max():.3g}, max |simt - ref| {np.abs(got_simt - want).max():.3g}, "
+          f"max|v| {np.abs(v).max():.3g}")
 
 
 def test_attention_large_scores_are_not_skipped(cuda_device):
