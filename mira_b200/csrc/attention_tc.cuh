@@ -12,8 +12,9 @@
 // workspace (k as [piece][key][d] rows, v transposed as [piece][d][key] rows).  Then one CTA per
 // 128 query rows walks the key tiles of 64 keys as a pipeline: one thread loads a tile's six piece
 // tiles with TMA (128-byte swizzle, two tiles in flight), one thread issues the 24 MMAs of a score
-// tile S = q k^T into one of two TMEM buffers ahead of the softmax, the four softmax warps (thread
-// i owns query row i, which is TMEM lane i) read their rows, apply the scale step and the mask,
+// tile S = q k^T into one of two TMEM buffers ahead of the softmax, the eight softmax warps (two
+// threads per query row, TMEM lane i, each with 32 of the tile's columns; they swap their row
+// maxima through shared memory) read their rows, apply the scale step and the mask,
 // update the running maximum and sum exactly as the f32 kernel does (expf(s - m), rescaled partial
 // sums), and write the probabilities' pieces as the A operand of the 24 MMAs of O_tile = p v (two
 // TMEM buffers), which they add to their f32 output rows one tile later, while the next tile's
@@ -27,9 +28,9 @@
 namespace mira {
 
 constexpr int ATC_BQ = 128, ATC_BK = 64, ATC_DH = 64, ATC_PIECES = 3;
-// warps 0-3 softmax (thread i: query row i = TMEM lane i), warp 4 issues the MMAs, warp 5 the TMA
-// loads (eight warps: two per SM sub-partition, so ptxas allows the softmax rows' 255 registers)
-constexpr int ATC_SOFTMAX = 128, ATC_THREADS = 256;
+// warps 0-7 softmax (thread t: query row t % 128 = TMEM lane, columns 32 (t / 128) .. + 31), warp 8
+// issues the MMAs, warp 9 the TMA loads
+constexpr int ATC_SOFTMAX = 256, ATC_THREADS = 320;
 constexpr int ATC_MAX_KB = 256;   // key tiles of a row (tk <= 16384)
 constexpr uint64_t ATC_TIMEOUT_NS = 2000000000ull;
 
@@ -40,6 +41,9 @@ struct AtcSmem {
   uint8_t vt[2][ATC_PIECES][ATC_DH * 128];   // [d][key]
   uint8_t p[ATC_PIECES][ATC_BQ * 128];       // [query][key]
   uint64_t kv_full[2], kv_empty[2], s_full[2], s_empty[2], o_full[2], o_empty[2], p_full, p_empty, drain;
+  uint64_t mx_bar[2];          // the two halves of a row have swapped their maxima (per tile, double-buffered)
+  float xmax[2][2][ATC_BQ];    // [tile parity][column half][row]
+  float xl[2][ATC_BQ];         // [column half][row]: the halves' sums, combined at the end
   uint32_t tmem;
   int abort;
   float qn1[ATC_BQ];
@@ -175,6 +179,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       mbar_init(&sm.o_empty[b], ATC_SOFTMAX);
     }
     mbar_init(&sm.p_full, ATC_SOFTMAX);
+    mbar_init(&sm.mx_bar[0], ATC_SOFTMAX);
+    mbar_init(&sm.mx_bar[1], ATC_SOFTMAX);
     mbar_init(&sm.p_empty, 1);
     mbar_init(&sm.drain, 1);
     sm.abort = 0;
@@ -224,18 +230,20 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
   __syncthreads();
   const uint32_t tmem = sm.tmem;
 
-  // softmax state of query row r = q0 + tid (threads 0..127)
-  const int r = q0 + tid;
+  // softmax state of query row r = q0 + (tid & 127), columns 32 * chalf .. + 31 (threads 0..255)
+  const int srow = tid & (ATC_BQ - 1), chalf = (tid >> 7) & 1;
+  const int r = q0 + srow;
+  constexpr int HC = ATC_BK / 2;   // columns per thread (of the scores and of the output)
   float m = -INFINITY, l = 0.0f;
-  float o[ATC_DH];
+  float o[HC];
 #pragma unroll
-  for (int d = 0; d < ATC_DH; ++d) o[d] = 0.0f;
+  for (int d = 0; d < HC; ++d) o[d] = 0.0f;
   uint32_t seq = 0;   // tiles through the pipeline so far (mbarrier phases); the same in every role
 
   // Runs key tiles list(0) .. list(count - 1) through the pipeline (every role calls it with the
   // same list).
   auto run = [&](int count, auto list) {
-    if (warp == 5) {
+    if (warp == 9) {
       // ------------------------------------------------ producer: a tile's six piece tiles by TMA
       if ((tid & 31) == 0) {
         int issued = 0;
@@ -264,7 +272,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
           }
         }
       }
-    } else if (warp == 4) {
+    } else if (warp == 8) {
       // ------------------------------------------------ MMA issuer: S one tile ahead of p v
       if ((tid & 31) == 0) {
         auto issue_s = [&](uint32_t sq) {
@@ -289,81 +297,80 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
           mma_commit(&sm.kv_empty[b]);
         }
       }
-    } else if (warp < 4) {
+    } else {
       // ------------------------------------------------ softmax rows
-      const uint32_t lane_base = static_cast<uint32_t>(warp) * 32u << 16;
-      const int half = tid >> 6;   // which 64-row half of the block this row is in
+      const uint32_t lane_base = static_cast<uint32_t>(warp & 3) * 32u << 16;
+      const int half = srow >> 6;   // which 64-row half of the block this row is in
       auto add_o = [&](uint32_t sq) {   // the p v tile of sq into the output row
         const uint32_t b = sq & 1;
         if (!mbar_wait(&sm.o_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) return;
         tc_fence_after();
-        uint32_t raw[32];
+        uint32_t raw[HC];
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + 64 * b + HC * chalf, raw);
+        tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          tmem_ld_32x32b_x32(tmem + lane_base + 128 + 64 * b + 32 * h, raw);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) o[32 * h + c] += __uint_as_float(raw[c]);
-        }
+        for (int c = 0; c < HC; ++c) o[c] += __uint_as_float(raw[c]);
         tc_fence_before();
         mbar_arrive(&sm.o_empty[b]);
       };
       for (int i = 0; i < count; ++i) {
         const uint32_t sq = seq + i, b = sq & 1;
-        const int kb = list(i), k0 = kb * ATC_BK;
+        const int kb = list(i), k0 = kb * ATC_BK + HC * chalf;   // this thread's first column
         // a mask tile of +0 only adds nothing (x + 0 turns -0 into +0, which leaves exp(x - m) alone)
         const bool zero_mask = p.tile_zero != nullptr && 2 * qb + half < nqb64 &&
                                __ldg(p.tile_zero + int64_t(2 * qb + half) * nkb + kb) != 0;
-        float s[ATC_BK];
+        float s[HC];
         if (!mbar_wait(&sm.s_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
         tc_fence_after();
         {
-          uint32_t raw[32];
+          uint32_t raw[HC];
+          tmem_ld_32x32b_x32(tmem + lane_base + 64 * b + HC * chalf, raw);
+          tmem_ld_wait();
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tmem_ld_32x32b_x32(tmem + lane_base + 64 * b + 32 * h, raw);
-            tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) s[32 * h + c] = __uint_as_float(raw[c]);
-          }
+          for (int c = 0; c < HC; ++c) s[c] = __uint_as_float(raw[c]);
         }
         tc_fence_before();
         mbar_arrive(&sm.s_empty[b]);
         if (p.scale_op == MIRA_EPI_MUL) {
 #pragma unroll
-          for (int c = 0; c < ATC_BK; ++c) s[c] = __fmul_rn(s[c], p.scale);
+          for (int c = 0; c < HC; ++c) s[c] = __fmul_rn(s[c], p.scale);
         } else if (p.scale_op == MIRA_EPI_DIV) {
 #pragma unroll
-          for (int c = 0; c < ATC_BK; ++c) s[c] = __fdiv_rn(s[c], p.scale);
+          for (int c = 0; c < HC; ++c) s[c] = __fdiv_rn(s[c], p.scale);
         }
         if (mp != nullptr && !zero_mask && r < p.tq) {
-          // the row's 64 mask values: all loads issued before the first add
+          // the row's mask values: all loads issued before the first add
           const float* mrow = mp + int64_t(r) * p.ms[2];
-          float mk[ATC_BK];
-          if (p.ms[3] == 1 && (reinterpret_cast<uintptr_t>(mrow + k0) & 15) == 0 && k0 + ATC_BK <= p.tk) {
+          float mk[HC];
+          if (p.ms[3] == 1 && (reinterpret_cast<uintptr_t>(mrow + k0) & 15) == 0 && k0 + HC <= p.tk) {
 #pragma unroll
-            for (int c = 0; c < ATC_BK; c += 4) {
+            for (int c = 0; c < HC; c += 4) {
               const float4 t = __ldg(reinterpret_cast<const float4*>(mrow + k0 + c));
               mk[c] = t.x; mk[c + 1] = t.y; mk[c + 2] = t.z; mk[c + 3] = t.w;
             }
           } else {
 #pragma unroll
-            for (int c = 0; c < ATC_BK; ++c) mk[c] = k0 + c < p.tk ? __ldg(mrow + int64_t(k0 + c) * p.ms[3]) : 0.0f;
+            for (int c = 0; c < HC; ++c) mk[c] = k0 + c < p.tk ? __ldg(mrow + int64_t(k0 + c) * p.ms[3]) : 0.0f;
           }
 #pragma unroll
-          for (int c = 0; c < ATC_BK; ++c) s[c] = __fadd_rn(s[c], mk[c]);
+          for (int c = 0; c < HC; ++c) s[c] = __fadd_rn(s[c], mk[c]);
         }
         float rmax = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < ATC_BK; ++c) {
+        for (int c = 0; c < HC; ++c) {
           if (k0 + c >= p.tk) s[c] = -INFINITY;
           rmax = fmaxf(rmax, s[c]);
         }
+        // the other half of the row's maximum
+        sm.xmax[b][chalf][srow] = rmax;
+        mbar_arrive(&sm.mx_bar[b]);
+        if (!mbar_wait(&sm.mx_bar[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
+        rmax = fmaxf(rmax, sm.xmax[b][chalf ^ 1][srow]);
         const float mnew = fmaxf(m, rmax);
         const float corr = (mnew == -INFINITY) ? 1.0f : expf(m - mnew);
         float rsum = 0.0f;
 #pragma unroll
-        for (int c = 0; c < ATC_BK; ++c) {
+        for (int c = 0; c < HC; ++c) {
           const float e = (mnew == -INFINITY) ? 0.0f : expf(s[c] - mnew);
           s[c] = e;
           rsum += e;
@@ -372,18 +379,18 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
         m = mnew;
         if (!mbar_wait(&sm.p_empty, (sq & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
+        for (int ch = 0; ch < HC / 8; ++ch) {
           float x[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) x[e] = s[8 * ch + e];
-          atc_store8(&sm.p[0][0], sizeof(sm.p[0]), tid, ch, x);
+          atc_store8(&sm.p[0][0], sizeof(sm.p[0]), srow, (HC / 8) * chalf + ch, x);
         }
         fence_proxy_async_smem();
         mbar_arrive(&sm.p_full);
         // the previous tile's p v (at the previous maximum), then this tile's rescale
         if (i > 0) add_o(sq - 1);
 #pragma unroll
-        for (int d = 0; d < ATC_DH; ++d) o[d] *= corr;
+        for (int d = 0; d < HC; ++d) o[d] *= corr;
       }
       if (count > 0 && !*abort_flag) add_o(seq + count - 1);
     }
@@ -399,18 +406,23 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
     for (int kb = 0; kb < nkb && !*abort_flag; ++kb) {
       if (!sm.cand[kb]) continue;
       bool ok = true;
-      if (tid < ATC_BQ && r < p.tq) {
+      if (tid < ATC_SOFTMAX && r < p.tq) {
         // every score of this tile is at most this bound (the factor covers the products' rounding)
-        const float bound = p.scale_abs * sm.qn1[tid] * kmax * 1.001f + tile_max(kb);
+        const float bound = p.scale_abs * sm.qn1[srow] * kmax * 1.001f + tile_max(kb);
         ok = bound - m < -110.0f;
       }
       if (!__syncthreads_and(ok)) run(1, [&](int) { return kb; });
     }
   }
-  if (tid < ATC_BQ && r < p.tq && !*abort_flag) {
+  // the row's sum: the two halves' partial sums (both rescaled by the same maxima)
+  if (tid < ATC_SOFTMAX) sm.xl[chalf][srow] = l;
+  __syncthreads();
+  if (tid < ATC_SOFTMAX && r < p.tq && !*abort_flag) {
+    const float lsum = __fadd_rn(sm.xl[0][srow], sm.xl[1][srow]);
 #pragma unroll
-    for (int d = 0; d < ATC_DH; ++d) {
-      const float y = __fdiv_rn(o[d], l);
+    for (int c = 0; c < HC; ++c) {
+      const int d = HC * chalf + c;
+      const float y = __fdiv_rn(o[c], lsum);
       if (p.out != nullptr) p.out[b0 * p.os[0] + b1 * p.os[1] + int64_t(r) * p.os[2] + int64_t(d) * p.os[3]] = y;
       if (p.out_i8 != nullptr)
         p.out_i8[b0 * p.is[0] + b1 * p.is[1] + int64_t(r) * p.is[2] + int64_t(d) * p.is[3]] =
