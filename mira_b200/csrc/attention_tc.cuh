@@ -10,17 +10,20 @@
 //
 // A first kernel splits k and v into their pieces once per (batch0, batch1) entry, in the caller's
 // workspace (k as [piece][key][d] rows, v transposed as [piece][d][key] rows).  Then one CTA per
-// 128 query rows walks the key tiles of 64 keys as a pipeline: one thread loads a tile's six piece
-// tiles with TMA (128-byte swizzle, two tiles in flight), one thread issues the 24 MMAs of a score
-// tile S = q k^T into one of two TMEM buffers ahead of the softmax, the eight softmax warps (two
+// 128 query rows walks the key tiles of 64 keys as a pipeline: one thread loads the k and v piece
+// tiles with TMA (128-byte swizzle; k and v in separate two-stage rings, k one tile ahead, since a k
+// tile is free as soon as its score MMAs are done), one thread issues the 24 MMAs of a score tile
+// S = q k^T into one of two TMEM buffers ahead of the softmax, and the eight softmax warps (two
 // threads per query row, TMEM lane i, each with 32 of the tile's columns; they swap their row
-// maxima through shared memory) read their rows, apply the scale step and the mask,
-// update the running maximum and sum exactly as the f32 kernel does (expf(s - m), rescaled partial
-// sums), and write the probabilities' pieces as the A operand of the 24 MMAs of O_tile = p v (two
-// TMEM buffers), which they add to their f32 output rows one tile later, while the next tile's
-// softmax runs.  Key tiles whose mask is all strongly negative are skipped under the f32 kernel's
-// certificate (|scale| ||q_i||_1 max|k| + tile_max - m_i < -110 for every row; else processed at
-// the end).
+// maxima through shared memory) read their rows, apply the scale step and the mask (loaded a tile
+// ahead), update the running maximum and the rescaled partial sums as the f32 kernel does, with
+// e^(s - m) evaluated as 2^(s log2(e) - m log2(e)) by the ex2.approx instruction (a few ulp), and
+// write the probabilities' pieces as the A operand of the 24 MMAs of O_tile = p v (two TMEM
+// buffers), which they add to their f32 output rows one tile later, while the next tile's softmax
+// runs.  The output rows are divided by the sums (reciprocal and one residual correction) and
+// stored through shared memory as whole rows.  Key tiles whose mask is all strongly negative are
+// skipped under the f32 kernel's certificate (|scale| ||q_i||_1 max|k| + tile_max - m_i < -110
+// for every row; the tiles some row cannot skip are processed at the end).
 #pragma once
 #include <cuda_bf16.h>
 #include "sequence_ops.cuh"
@@ -40,15 +43,22 @@ struct AtcSmem {
   uint8_t k[2][ATC_PIECES][ATC_BK * 128];    // [key][d], two tiles in flight
   uint8_t vt[2][ATC_PIECES][ATC_DH * 128];   // [d][key]
   uint8_t p[ATC_PIECES][ATC_BQ * 128];       // [query][key]
-  uint64_t kv_full[2], kv_empty[2], s_full[2], s_empty[2], o_full[2], o_empty[2], p_full, p_empty, drain;
+  // k and v have stages of their own: a k tile is free once its score MMAs are done, a tile ahead
+  // of the v tile beside it
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full[2], s_empty[2], o_full[2], o_empty[2], p_full, p_empty, drain;
   uint64_t mx_bar[2];          // the two halves of a row have swapped their maxima (per tile, double-buffered)
   float xmax[2][2][ATC_BQ];    // [tile parity][column half][row]
   float xl[2][ATC_BQ];         // [column half][row]: the halves' sums, combined at the end
   uint32_t tmem;
   int abort;
   float qn1[ATC_BQ];
+  float kmax;                  // max |k| (the skipping certificate)
+  float tmax[ATC_MAX_KB];      // the largest mask value of each key tile over the block's rows
   int16_t tiles[ATC_MAX_KB];   // the key tiles that are not skipping candidates, in order
   uint8_t cand[ATC_MAX_KB];    // 1: a skipping candidate
+  uint8_t fail[ATC_MAX_KB];    // 1: a candidate that some row cannot skip
+  uint8_t zmask[2][ATC_MAX_KB];  // [64-row half][key tile] 1: every mask value of the tile is +0
   int n_main;
 };
 
@@ -58,27 +68,28 @@ __device__ __forceinline__ int atc_sw128(int row, int chunk) {
   return (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
-__device__ __forceinline__ void atc_split(float x, uint32_t (&b)[ATC_PIECES]) {
-  const __nv_bfloat16 a0 = __float2bfloat16_rn(x);
-  const float r0 = __fsub_rn(x, __bfloat162float(a0));
-  const __nv_bfloat16 a1 = __float2bfloat16_rn(r0);
-  const float r1 = __fsub_rn(r0, __bfloat162float(a1));
-  const __nv_bfloat16 a2 = __float2bfloat16_rn(r1);
-  b[0] = __bfloat16_as_ushort(a0);
-  b[1] = __bfloat16_as_ushort(a1);
-  b[2] = __bfloat16_as_ushort(a2);
+// a and b rounded to bf16 (to nearest, ties to even), a in the low half of the word
+__device__ __forceinline__ uint32_t atc_bf2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// The three pieces of 8 values as three 16-byte words.
+// The three pieces of 8 values as three 16-byte words: piece 0 is x rounded to bf16, piece 1 the
+// remainder x - x0 (exact in f32) rounded to bf16, piece 2 the remainder after that (exact in
+// bf16: at most 8 significant bits are left); two values per conversion.
 __device__ __forceinline__ void atc_pack8(const float (&x)[8], uint4 (&w)[ATC_PIECES]) {
   uint32_t t[ATC_PIECES][4];
 #pragma unroll
   for (int e = 0; e < 8; e += 2) {
-    uint32_t lo[ATC_PIECES], hi[ATC_PIECES];
-    atc_split(x[e], lo);
-    atc_split(x[e + 1], hi);
-#pragma unroll
-    for (int pc = 0; pc < ATC_PIECES; ++pc) t[pc][e >> 1] = lo[pc] | (hi[pc] << 16);
+    const uint32_t w0 = atc_bf2(x[e], x[e + 1]);
+    const float ra = __fsub_rn(x[e], __uint_as_float(w0 << 16));
+    const float rb = __fsub_rn(x[e + 1], __uint_as_float(w0 & 0xffff0000u));
+    const uint32_t w1 = atc_bf2(ra, rb);
+    const float sa = __fsub_rn(ra, __uint_as_float(w1 << 16));
+    const float sb = __fsub_rn(rb, __uint_as_float(w1 & 0xffff0000u));
+    t[0][e >> 1] = w0;
+    t[1][e >> 1] = w1;
+    t[2][e >> 1] = atc_bf2(sa, sb);
   }
 #pragma unroll
   for (int pc = 0; pc < ATC_PIECES; ++pc) w[pc] = make_uint4(t[pc][0], t[pc][1], t[pc][2], t[pc][3]);
@@ -92,6 +103,30 @@ __device__ __forceinline__ void atc_store8(uint8_t* base, int tile_bytes, int ro
   const int off = atc_sw128(row, chunk);
 #pragma unroll
   for (int pc = 0; pc < ATC_PIECES; ++pc) *reinterpret_cast<uint4*>(base + pc * tile_bytes + off) = w[pc];
+}
+
+// 2^x by the ex2.approx instruction (a few ulp; subnormal results kept).  The softmax weights are
+// computed as e^(s - m) = 2^(s log2(e) - m log2(e)).
+__device__ __forceinline__ float atc_ex2(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float ATC_LOG2E = 1.4426950408889634f;
+
+// The key tiles kb < nkb with flag[kb] == want, in order, into out[]; their number into *n.  Run by
+// one whole warp.
+__device__ __forceinline__ void atc_list(const uint8_t* flag, uint8_t want, int nkb, int16_t* out, int* n) {
+  const int lane = threadIdx.x & 31;
+  int count = 0;
+  for (int base = 0; base < nkb; base += 32) {
+    const int kb = base + lane;
+    const bool f = kb < nkb && flag[kb] == want;
+    const uint32_t bal = __ballot_sync(0xffffffffu, f);
+    if (f) out[count + __popc(bal & ((1u << lane) - 1u))] = static_cast<int16_t>(kb);
+    count += __popc(bal);
+  }
+  if (lane == 0) *n = count;
 }
 
 // The 24 MMAs of D = A B^T over K = 64: six piece pairs (i + j <= 2) x four K-steps of 16.
@@ -171,8 +206,10 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
 
   if (tid == 0) {
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.kv_full[b], 1);
-      mbar_init(&sm.kv_empty[b], 1);
+      mbar_init(&sm.k_full[b], 1);
+      mbar_init(&sm.k_empty[b], 1);
+      mbar_init(&sm.v_full[b], 1);
+      mbar_init(&sm.v_empty[b], 1);
       mbar_init(&sm.s_full[b], 1);
       mbar_init(&sm.s_empty[b], ATC_SOFTMAX);
       mbar_init(&sm.o_full[b], 1);
@@ -192,41 +229,67 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
     tmem_alloc(&sm.tmem, 256);   // S buffers in columns 0..127, O_tile buffers in 128..255
     tmem_relinquish();
   }
-  // q rows (zero past tq) as pieces; ||q_i||_1 for the skipping certificate
-  for (int task = tid; task < ATC_BQ * 8; task += ATC_THREADS) {
-    const int row = task >> 3, ch = task & 7;
-    float x[8];
+  // q rows (zero past tq) as pieces, all loads of a thread in flight at once; ||q_i||_1 for the
+  // skipping certificate (the 8 chunks of a row are 8 consecutive lanes)
+  {
+    constexpr int QT = (ATC_BQ * 8 + ATC_THREADS - 1) / ATC_THREADS;
+    const bool qvec = p.qs[3] == 1 && ((p.qs[0] | p.qs[1] | p.qs[2]) & 3) == 0 &&
+                      (reinterpret_cast<uintptr_t>(qp) & 15) == 0;
+    float x[QT][8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      x[e] = q0 + row < p.tq ? __ldg(qp + int64_t(q0 + row) * p.qs[2] + int64_t(8 * ch + e) * p.qs[3]) : 0.0f;
-    atc_store8(&sm.q[0][0], sizeof(sm.q[0]), row, ch, x);
+    for (int j = 0; j < QT; ++j) {
+      const int task = tid + j * ATC_THREADS, row = task >> 3, ch = task & 7;
+      const bool live = task < ATC_BQ * 8 && q0 + row < p.tq;
+      const float* src = qp + int64_t(q0 + row) * p.qs[2];
+      if (live && qvec) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src + 8 * ch));
+        const float4 c = __ldg(reinterpret_cast<const float4*>(src + 8 * ch + 4));
+        x[j][0] = a.x; x[j][1] = a.y; x[j][2] = a.z; x[j][3] = a.w;
+        x[j][4] = c.x; x[j][5] = c.y; x[j][6] = c.z; x[j][7] = c.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[j][e] = live ? __ldg(src + int64_t(8 * ch + e) * p.qs[3]) : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < QT; ++j) {
+      const int task = tid + j * ATC_THREADS, row = task >> 3, ch = task & 7;
+      float a = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a += fabsf(x[j][e]);
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      a += __shfl_xor_sync(0xffffffffu, a, 2);
+      a += __shfl_xor_sync(0xffffffffu, a, 4);
+      if (task < ATC_BQ * 8) {
+        atc_store8(&sm.q[0][0], sizeof(sm.q[0]), row, ch, x[j]);
+        if (ch == 0) sm.qn1[row] = a;
+      }
+    }
   }
-  if (tid < ATC_BQ) {
-    float a = 0.0f;
-    if (q0 + tid < p.tq)
-      for (int d = 0; d < ATC_DH; ++d) a += fabsf(__ldg(qp + int64_t(q0 + tid) * p.qs[2] + int64_t(d) * p.qs[3]));
-    sm.qn1[tid] = a;
-  }
-  // skipping candidates once, into shared memory: tile_max / tile_zero describe 64 x 64 (query,
-  // key) tiles, this block holds two 64-row halves
+  // skipping candidates and all-zero mask tiles once, into shared memory: tile_max / tile_zero
+  // describe 64 x 64 (query, key) tiles, this block holds two 64-row halves
   const bool can_skip = p.tile_max != nullptr && p.kmax != nullptr;
   const int nqb64 = (p.tq + 63) / 64;
-  auto tile_max = [&](int kb) {
-    float t = __ldg(p.tile_max + int64_t(2 * qb) * nkb + kb);
-    if (2 * qb + 1 < nqb64) t = fmaxf(t, __ldg(p.tile_max + int64_t(2 * qb + 1) * nkb + kb));
-    return t;
-  };
-  for (int kb = tid; kb < nkb; kb += ATC_THREADS) sm.cand[kb] = can_skip && tile_max(kb) <= -200.0f ? 1 : 0;
+  if (tid == 0 && can_skip) sm.kmax = __uint_as_float(__ldg(p.kmax));
+  for (int kb = tid; kb < nkb; kb += ATC_THREADS) {
+    float t = -INFINITY;
+    if (can_skip) {
+      t = __ldg(p.tile_max + int64_t(2 * qb) * nkb + kb);
+      if (2 * qb + 1 < nqb64) t = fmaxf(t, __ldg(p.tile_max + int64_t(2 * qb + 1) * nkb + kb));
+    }
+    sm.tmax[kb] = t;
+    sm.cand[kb] = can_skip && t <= -200.0f ? 1 : 0;
+    sm.fail[kb] = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      sm.zmask[h][kb] = p.tile_zero != nullptr && 2 * qb + h < nqb64 &&
+                        __ldg(p.tile_zero + int64_t(2 * qb + h) * nkb + kb) != 0;
+  }
   fence_proxy_async_smem();   // generic-proxy writes of q read by tcgen05.mma
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (tid == 0) {
-    int n = 0;
-    for (int kb = 0; kb < nkb; ++kb)
-      if (!sm.cand[kb]) sm.tiles[n++] = static_cast<int16_t>(kb);
-    sm.n_main = n;
-  }
+  if (warp == 0) atc_list(sm.cand, 0, nkb, sm.tiles, &sm.n_main);
   __syncthreads();
   const uint32_t tmem = sm.tmem;
 
@@ -234,7 +297,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
   const int srow = tid & (ATC_BQ - 1), chalf = (tid >> 7) & 1;
   const int r = q0 + srow;
   constexpr int HC = ATC_BK / 2;   // columns per thread (of the scores and of the output)
-  float m = -INFINITY, l = 0.0f;
+  float m = -INFINITY, ml = -INFINITY, l = 0.0f;   // ml = m log2(e), rounded once
   float o[HC];
 #pragma unroll
   for (int d = 0; d < HC; ++d) o[d] = 0.0f;
@@ -244,32 +307,52 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
   // same list).
   auto run = [&](int count, auto list) {
     if (warp == 9) {
-      // ------------------------------------------------ producer: a tile's six piece tiles by TMA
+      // ------------------------------------------------ producer: the k and v piece tiles by TMA,
+      // k one tile ahead of v (k(i + 1) is needed by the score MMAs before v(i) by the p v MMAs)
       if ((tid & 31) == 0) {
-        int issued = 0;
-        for (int i = 0; i < count; ++i) {
+        int nk = 0, nv = 0;   // tiles issued
+        auto load_k = [&](int i) {
           const uint32_t sq = seq + i, b = sq & 1;
-          if (!mbar_wait(&sm.kv_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
-          ++issued;
+          if (!mbar_wait(&sm.k_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) return false;
+          ++nk;
           const int k0 = list(i) * ATC_BK;
-          mbar_arrive_expect_tx(&sm.kv_full[b], 2 * ATC_PIECES * ATC_BK * 128);
+          mbar_arrive_expect_tx(&sm.k_full[b], ATC_PIECES * ATC_BK * 128);
 #pragma unroll
-          for (int pc = 0; pc < ATC_PIECES; ++pc) {
+          for (int pc = 0; pc < ATC_PIECES; ++pc)
             tma_load_2d(&sm.k[b][pc][0], &map_k, 0, static_cast<int32_t>((bh * ATC_PIECES + pc) * tkp + k0),
-                        &sm.kv_full[b]);
+                        &sm.k_full[b]);
+          return true;
+        };
+        auto load_v = [&](int i) {
+          const uint32_t sq = seq + i, b = sq & 1;
+          if (!mbar_wait(&sm.v_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) return false;
+          ++nv;
+          const int k0 = list(i) * ATC_BK;
+          mbar_arrive_expect_tx(&sm.v_full[b], ATC_PIECES * ATC_DH * 128);
+#pragma unroll
+          for (int pc = 0; pc < ATC_PIECES; ++pc)
             tma_load_2d(&sm.vt[b][pc][0], &map_vt, k0, static_cast<int32_t>((bh * ATC_PIECES + pc) * ATC_DH),
-                        &sm.kv_full[b]);
-          }
+                        &sm.v_full[b]);
+          return true;
+        };
+        bool ok = count > 0 ? load_k(0) : true;
+        for (int i = 0; i < count && ok; ++i) {
+          if (i + 1 < count && !load_k(i + 1)) break;
+          if (!load_v(i)) break;
         }
         if (*abort_flag) {
           // let the copies still in flight land before the shared memory goes away (bounded)
-          for (int i = issued > 2 ? issued - 2 : 0; i < issued; ++i) {
-            const uint32_t sq = seq + i;
-            const uint64_t t0 = globaltimer_ns();
-            while (!mbar_try_wait_suspend(&sm.kv_full[sq & 1], (sq >> 1) & 1, 1000000u) &&
-                   globaltimer_ns() - t0 < ATC_TIMEOUT_NS) {
+          auto settle = [&](uint64_t* full, int n) {
+            for (int i = n > 2 ? n - 2 : 0; i < n; ++i) {
+              const uint32_t sq = seq + i;
+              const uint64_t t0 = globaltimer_ns();
+              while (!mbar_try_wait_suspend(&full[sq & 1], (sq >> 1) & 1, 1000000u) &&
+                     globaltimer_ns() - t0 < ATC_TIMEOUT_NS) {
+              }
             }
-          }
+          };
+          settle(sm.k_full, nk);
+          settle(sm.v_full, nv);
         }
       }
     } else if (warp == 8) {
@@ -277,24 +360,26 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       if ((tid & 31) == 0) {
         auto issue_s = [&](uint32_t sq) {
           const uint32_t b = sq & 1;
-          if (!mbar_wait(&sm.kv_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) return false;
+          if (!mbar_wait(&sm.k_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) return false;
           if (!mbar_wait(&sm.s_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) return false;
           tc_fence_after();
           atc_mma(tmem + 64 * b, &sm.q[0][0], sizeof(sm.q[0]), &sm.k[b][0][0], sizeof(sm.k[0][0]));
           mma_commit(&sm.s_full[b]);
+          mma_commit(&sm.k_empty[b]);
           return true;
         };
         bool ok = count > 0 ? issue_s(seq) : true;
         for (int i = 0; i < count && ok; ++i) {
           const uint32_t sq = seq + i, b = sq & 1;
           if (i + 1 < count && !issue_s(sq + 1)) break;
+          if (!mbar_wait(&sm.v_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
           if (!mbar_wait(&sm.p_full, sq & 1, abort_flag, ATC_TIMEOUT_NS)) break;
           if (!mbar_wait(&sm.o_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
           tc_fence_after();
           atc_mma(tmem + 128 + 64 * b, &sm.p[0][0], sizeof(sm.p[0]), &sm.vt[b][0][0], sizeof(sm.vt[0][0]));
           mma_commit(&sm.o_full[b]);
           mma_commit(&sm.p_empty);
-          mma_commit(&sm.kv_empty[b]);
+          mma_commit(&sm.v_empty[b]);
         }
       }
     } else {
@@ -313,12 +398,32 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
         tc_fence_before();
         mbar_arrive(&sm.o_empty[b]);
       };
+      // the mask values of tile list(i) in this thread's columns, loaded one tile ahead (a tile of
+      // +0 adds nothing: x + 0 turns -0 into +0, which leaves exp(x - m) alone)
+      float mk[HC];
+      bool mk_on = false;
+      auto fetch_mask = [&](int i) {
+        mk_on = false;
+        if (mp == nullptr || i >= count || r >= p.tq) return;
+        const int kb = list(i), k0 = kb * ATC_BK + HC * chalf;
+        if (sm.zmask[half][kb]) return;
+        mk_on = true;
+        const float* mrow = mp + int64_t(r) * p.ms[2];
+        if (p.ms[3] == 1 && (reinterpret_cast<uintptr_t>(mrow + k0) & 15) == 0 && k0 + HC <= p.tk) {
+#pragma unroll
+          for (int c = 0; c < HC; c += 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(mrow + k0 + c));
+            mk[c] = t.x; mk[c + 1] = t.y; mk[c + 2] = t.z; mk[c + 3] = t.w;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < HC; ++c) mk[c] = k0 + c < p.tk ? __ldg(mrow + int64_t(k0 + c) * p.ms[3]) : 0.0f;
+        }
+      };
+      fetch_mask(0);
       for (int i = 0; i < count; ++i) {
         const uint32_t sq = seq + i, b = sq & 1;
         const int kb = list(i), k0 = kb * ATC_BK + HC * chalf;   // this thread's first column
-        // a mask tile of +0 only adds nothing (x + 0 turns -0 into +0, which leaves exp(x - m) alone)
-        const bool zero_mask = p.tile_zero != nullptr && 2 * qb + half < nqb64 &&
-                               __ldg(p.tile_zero + int64_t(2 * qb + half) * nkb + kb) != 0;
         float s[HC];
         if (!mbar_wait(&sm.s_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
         tc_fence_after();
@@ -338,55 +443,46 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
 #pragma unroll
           for (int c = 0; c < HC; ++c) s[c] = __fdiv_rn(s[c], p.scale);
         }
-        if (mp != nullptr && !zero_mask && r < p.tq) {
-          // the row's mask values: all loads issued before the first add
-          const float* mrow = mp + int64_t(r) * p.ms[2];
-          float mk[HC];
-          if (p.ms[3] == 1 && (reinterpret_cast<uintptr_t>(mrow + k0) & 15) == 0 && k0 + HC <= p.tk) {
-#pragma unroll
-            for (int c = 0; c < HC; c += 4) {
-              const float4 t = __ldg(reinterpret_cast<const float4*>(mrow + k0 + c));
-              mk[c] = t.x; mk[c + 1] = t.y; mk[c + 2] = t.z; mk[c + 3] = t.w;
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < HC; ++c) mk[c] = k0 + c < p.tk ? __ldg(mrow + int64_t(k0 + c) * p.ms[3]) : 0.0f;
-          }
+        if (mk_on) {
 #pragma unroll
           for (int c = 0; c < HC; ++c) s[c] = __fadd_rn(s[c], mk[c]);
         }
+        if (kb * ATC_BK + ATC_BK > p.tk) {   // the ragged last tile: keys past tk do not exist
+#pragma unroll
+          for (int c = 0; c < HC; ++c)
+            if (k0 + c >= p.tk) s[c] = -INFINITY;
+        }
         float rmax = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < HC; ++c) {
-          if (k0 + c >= p.tk) s[c] = -INFINITY;
-          rmax = fmaxf(rmax, s[c]);
-        }
+        for (int c = 0; c < HC; ++c) rmax = fmaxf(rmax, s[c]);
         // the other half of the row's maximum
         sm.xmax[b][chalf][srow] = rmax;
         mbar_arrive(&sm.mx_bar[b]);
-        if (!mbar_wait(&sm.mx_bar[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
+        if (!mbar_wait_spin(&sm.mx_bar[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
         rmax = fmaxf(rmax, sm.xmax[b][chalf ^ 1][srow]);
         const float mnew = fmaxf(m, rmax);
-        const float corr = (mnew == -INFINITY) ? 1.0f : expf(m - mnew);
-        float rsum = 0.0f;
-#pragma unroll
-        for (int c = 0; c < HC; ++c) {
-          const float e = (mnew == -INFINITY) ? 0.0f : expf(s[c] - mnew);
-          s[c] = e;
-          rsum += e;
-        }
-        l = fmaf(l, corr, rsum);
+        const bool dead = mnew == -INFINITY;   // no key of the row so far can carry weight
+        const float mlnew = __fmul_rn(mnew, ATC_LOG2E);
+        const float corr = dead ? 1.0f : atc_ex2(__fsub_rn(ml, mlnew));
         m = mnew;
+        ml = mlnew;
+        // e^(s - m) piece by piece into the p tiles once the previous p v has read them
         if (!mbar_wait(&sm.p_empty, (sq & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
+        float rsum = 0.0f;
 #pragma unroll
         for (int ch = 0; ch < HC / 8; ++ch) {
           float x[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] = s[8 * ch + e];
+          for (int e = 0; e < 8; ++e) {
+            x[e] = dead ? 0.0f : atc_ex2(fmaf(s[8 * ch + e], ATC_LOG2E, -mlnew));
+            rsum += x[e];
+          }
           atc_store8(&sm.p[0][0], sizeof(sm.p[0]), srow, (HC / 8) * chalf + ch, x);
         }
         fence_proxy_async_smem();
         mbar_arrive(&sm.p_full);
+        l = fmaf(l, corr, rsum);
+        fetch_mask(i + 1);
         // the previous tile's p v (at the previous maximum), then this tile's rescale
         if (i > 0) add_o(sq - 1);
 #pragma unroll
@@ -402,38 +498,82 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
 
   run(sm.n_main, [&](int i) { return static_cast<int>(sm.tiles[i]); });
   if (can_skip && !*abort_flag) {
-    const float kmax = __uint_as_float(__ldg(p.kmax));
-    for (int kb = 0; kb < nkb && !*abort_flag; ++kb) {
-      if (!sm.cand[kb]) continue;
-      bool ok = true;
-      if (tid < ATC_SOFTMAX && r < p.tq) {
-        // every score of this tile is at most this bound (the factor covers the products' rounding)
-        const float bound = p.scale_abs * sm.qn1[srow] * kmax * 1.001f + tile_max(kb);
-        ok = bound - m < -110.0f;
+    // every candidate checked once against the row maxima of the main pass; the candidates that some
+    // row cannot skip are processed (exactly), the rest skipped (the maxima only grow, so a tile
+    // skippable now stays skippable)
+    if (tid < ATC_SOFTMAX) {
+      const float kmax = sm.kmax;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!sm.cand[kb]) continue;
+        bool ok = true;
+        if (r < p.tq) {
+          // every score of this tile is at most this bound (the factor covers the products' rounding)
+          const float bound = p.scale_abs * sm.qn1[srow] * kmax * 1.001f + sm.tmax[kb];
+          ok = bound - m < -110.0f;
+        }
+        if (!__all_sync(0xffffffffu, ok) && (tid & 31) == 0) sm.fail[kb] = 1;
       }
-      if (!__syncthreads_and(ok)) run(1, [&](int) { return kb; });
     }
+    __syncthreads();
+    if (warp == 0) atc_list(sm.fail, 1, nkb, sm.tiles, &sm.n_main);
+    __syncthreads();
+    if (sm.n_main > 0) run(sm.n_main, [&](int i) { return static_cast<int>(sm.tiles[i]); });
   }
   // the row's sum: the two halves' partial sums (both rescaled by the same maxima)
   if (tid < ATC_SOFTMAX) sm.xl[chalf][srow] = l;
   __syncthreads();
-  if (tid < ATC_SOFTMAX && r < p.tq && !*abort_flag) {
-    const float lsum = __fadd_rn(sm.xl[0][srow], sm.xl[1][srow]);
+  const bool live = !*abort_flag;
+  float* obase = p.out != nullptr ? p.out + b0 * p.os[0] + b1 * p.os[1] : nullptr;
+  // f32 output rows staged in shared memory (the p tiles' space, idle now) and stored coalesced
+  constexpr int OST = ATC_DH + 4;   // staged row stride in floats
+  static_assert(sizeof(AtcSmem::p) >= ATC_BQ * OST * sizeof(float), "staging space");
+  float* stage = reinterpret_cast<float*>(&sm.p[0][0]);
+  const bool ostage = obase != nullptr && p.os[3] == 1 && ((p.os[0] | p.os[1] | p.os[2]) & 3) == 0 &&
+                      (reinterpret_cast<uintptr_t>(obase) & 15) == 0;
+  if (tid < ATC_SOFTMAX && live) {
+    if (r < p.tq) {
+      // o / l: the product with the rounded reciprocal and one residual correction (Markstein)
+      const float lsum = __fadd_rn(sm.xl[0][srow], sm.xl[1][srow]);
+      const float rl = __frcp_rn(lsum);
 #pragma unroll
-    for (int c = 0; c < HC; ++c) {
-      const int d = HC * chalf + c;
-      const float y = __fdiv_rn(o[c], lsum);
-      if (p.out != nullptr) p.out[b0 * p.os[0] + b1 * p.os[1] + int64_t(r) * p.os[2] + int64_t(d) * p.os[3]] = y;
-      if (p.out_i8 != nullptr)
-        p.out_i8[b0 * p.is[0] + b1 * p.is[1] + int64_t(r) * p.is[2] + int64_t(d) * p.is[3]] =
-            static_cast<int8_t>(quant_byte(y, p.q8) & 0xff);
+      for (int c = 0; c < HC; ++c) {
+        const float y = __fmul_rn(o[c], rl);
+        o[c] = fmaf(fmaf(-lsum, y, o[c]), rl, y);
+      }
+    }
+    if (ostage) {
+#pragma unroll
+      for (int c = 0; c < HC; c += 4)
+        *reinterpret_cast<float4*>(stage + srow * OST + HC * chalf + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+    }
+    if (r < p.tq) {
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+        const int d = HC * chalf + c;
+        if (obase != nullptr && !ostage) obase[int64_t(r) * p.os[2] + int64_t(d) * p.os[3]] = o[c];
+        if (p.out_i8 != nullptr)
+          p.out_i8[b0 * p.is[0] + b1 * p.is[1] + int64_t(r) * p.is[2] + int64_t(d) * p.is[3]] =
+              static_cast<int8_t>(quant_byte(o[c], p.q8) & 0xff);
+      }
+    }
+  }
+  if (ostage) {
+    __syncthreads();
+    if (tid < ATC_SOFTMAX && live) {
+#pragma unroll
+      for (int j = 0; j < ATC_BQ * (ATC_DH / 4) / ATC_SOFTMAX; ++j) {
+        const int idx = tid + j * ATC_SOFTMAX, row = idx >> 4, c4 = idx & 15;
+        if (q0 + row < p.tq)
+          *reinterpret_cast<float4*>(obase + int64_t(q0 + row) * p.os[2] + 4 * c4) =
+              *reinterpret_cast<const float4*>(stage + row * OST + 4 * c4);
+      }
     }
   }
   if (tid == ATC_SOFTMAX) {
     // every MMA this thread issued has finished once `drain` completes (bounded wait)
     mma_commit(&sm.drain);
     const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait_suspend(&sm.drain, 0, 1000000u) && globaltimer_ns() - t0 < ATC_TIMEOUT_NS) {
+    while (!mbar_try_wait(&sm.drain, 0) && globaltimer_ns() - t0 < ATC_TIMEOUT_NS) {
     }
   }
   tc_fence_before();
