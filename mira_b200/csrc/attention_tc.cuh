@@ -26,6 +26,7 @@
 // for every row; the tiles some row cannot skip are processed at the end).
 #pragma once
 #include <cuda_bf16.h>
+#include "qgemm_sm100.cuh"
 #include "sequence_ops.cuh"
 
 namespace mira {
@@ -33,8 +34,13 @@ namespace mira {
 constexpr int ATC_BQ = 128, ATC_BK = 64, ATC_DH = 64, ATC_PIECES = 3;
 // warps 0-7 softmax (thread t: query row t % 128 = TMEM lane, columns 32 (t / 128) .. + 31), warp 8
 // issues the MMAs, warp 9 the TMA loads
-constexpr int ATC_SOFTMAX = 256, ATC_THREADS = 320;
+constexpr int ATC_CG = 4;                                   // threads (column groups) per query row
+constexpr int ATC_SOFTMAX = ATC_BQ * ATC_CG, ATC_THREADS = ATC_SOFTMAX + 64;
+constexpr int ATC_MMA_WARP = ATC_SOFTMAX / 32, ATC_TMA_WARP = ATC_MMA_WARP + 1;
 constexpr int ATC_MAX_KB = 256;   // key tiles of a row (tk <= 16384)
+// TMEM columns: S tiles at 0 and 64, O tiles at 128 and 192, the two p tiles (three bf16 pieces of
+// 32 columns each, two keys per column) at ATC_PCOL and ATC_PCOL + ATC_PCOLS
+constexpr uint32_t ATC_PCOL = 256, ATC_PCOLS = ATC_PIECES * ATC_BK / 2;
 constexpr uint64_t ATC_TIMEOUT_NS = 2000000000ull;
 
 struct AtcSmem {
@@ -42,14 +48,13 @@ struct AtcSmem {
   uint8_t q[ATC_PIECES][ATC_BQ * 128];       // [query][d]
   uint8_t k[2][ATC_PIECES][ATC_BK * 128];    // [key][d], two tiles in flight
   uint8_t vt[2][ATC_PIECES][ATC_DH * 128];   // [d][key]
-  uint8_t p[ATC_PIECES][ATC_BQ * 128];       // [query][key]
   // k and v have stages of their own: a k tile is free once its score MMAs are done, a tile ahead
   // of the v tile beside it
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_empty[2], o_full[2], o_empty[2], p_full, p_empty, drain;
+  uint64_t s_full[2], s_empty[2], o_full[2], o_empty[2], p_full[2], p_empty[2], drain;
   uint64_t mx_bar[2];          // the two halves of a row have swapped their maxima (per tile, double-buffered)
-  float xmax[2][2][ATC_BQ];    // [tile parity][column half][row]
-  float xl[2][ATC_BQ];         // [column half][row]: the halves' sums, combined at the end
+  float xmax[2][ATC_CG][ATC_BQ];  // [tile parity][column group][row]
+  float xl[ATC_CG][ATC_BQ];       // [column group][row]: the groups' sums, combined at the end
   uint32_t tmem;
   int abort;
   float qn1[ATC_BQ];
@@ -113,6 +118,47 @@ __device__ __forceinline__ float atc_ex2(float x) {
   return y;
 }
 constexpr float ATC_LOG2E = 1.4426950408889634f;
+
+// D (TMEM) (+)= A B^T with A (M = 128 rows x K = 16 bf16) in TMEM (row i in lane i, two bf16 per
+// 32-bit column, the lower k in the low half) and B in shared memory.
+__device__ __forceinline__ void mma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Four 32-bit columns of this thread's TMEM lane (warp-collective: lanes 32 (warp % 4) .. + 31).
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, const uint4& v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// The 24 MMAs of O = p v over the 64 keys of a tile: p's three pieces in TMEM (ATC_BK / 2 columns
+// apart), v's as K-major [d][key] tiles in shared memory.
+__device__ __forceinline__ void atc_mma_ts(uint32_t d_tmem, uint32_t p_tmem, const uint8_t* b_tiles, int b_bytes) {
+  constexpr uint32_t IDESC = idesc_bf16(ATC_BQ, 64);
+  constexpr int PI[6] = {0, 0, 1, 0, 1, 2}, PJ[6] = {0, 1, 0, 2, 1, 0};
+  bool first = true;
+#pragma unroll
+  for (int t = 0; t < 6; ++t) {
+    const uint64_t bd = smem_desc_k_sw128(smem_u32(b_tiles + PJ[t] * b_bytes));
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      mma_bf16_tmem_a(d_tmem, p_tmem + PI[t] * (ATC_BK / 2) + 8 * ks, bd + 2 * ks, IDESC, first ? 0u : 1u);
+      first = false;
+    }
+  }
+}
+
+// This thread's lane of TMEM columns taddr .. taddr + N - 1 (warp-collective).
+__device__ __forceinline__ void atc_tmem_ld(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld_32x32b_x32(taddr, r); }
+__device__ __forceinline__ void atc_tmem_ld(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld_32x32b_x16(taddr, r); }
 
 // The key tiles kb < nkb with flag[kb] == want, in order, into out[]; their number into *n.  Run by
 // one whole warp.
@@ -215,10 +261,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       mbar_init(&sm.o_full[b], 1);
       mbar_init(&sm.o_empty[b], ATC_SOFTMAX);
     }
-    mbar_init(&sm.p_full, ATC_SOFTMAX);
+    mbar_init(&sm.p_full[0], ATC_SOFTMAX);
+    mbar_init(&sm.p_full[1], ATC_SOFTMAX);
     mbar_init(&sm.mx_bar[0], ATC_SOFTMAX);
     mbar_init(&sm.mx_bar[1], ATC_SOFTMAX);
-    mbar_init(&sm.p_empty, 1);
+    mbar_init(&sm.p_empty[0], 1);
+    mbar_init(&sm.p_empty[1], 1);
     mbar_init(&sm.drain, 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -226,7 +274,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
     tma_prefetch_desc(&map_vt);
   }
   if (warp == 0) {
-    tmem_alloc(&sm.tmem, 256);   // S buffers in columns 0..127, O_tile buffers in 128..255
+    tmem_alloc(&sm.tmem, 512);   // S buffers in columns 0..127, O_tile 128..255, p 256..447
     tmem_relinquish();
   }
   // q rows (zero past tq) as pieces, all loads of a thread in flight at once; ||q_i||_1 for the
@@ -293,10 +341,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
   __syncthreads();
   const uint32_t tmem = sm.tmem;
 
-  // softmax state of query row r = q0 + (tid & 127), columns 32 * chalf .. + 31 (threads 0..255)
-  const int srow = tid & (ATC_BQ - 1), chalf = (tid >> 7) & 1;
+  // softmax state of query row r = q0 + (tid & 127), columns HC * cg .. + HC - 1
+  const int srow = tid & (ATC_BQ - 1), cg = (tid >> 7) % ATC_CG;
   const int r = q0 + srow;
-  constexpr int HC = ATC_BK / 2;   // columns per thread (of the scores and of the output)
+  constexpr int HC = ATC_BK / ATC_CG;   // columns per thread (of the scores and of the output)
+  static_assert(HC == 16 || HC == 32, "column group width");
   float m = -INFINITY, ml = -INFINITY, l = 0.0f;   // ml = m log2(e), rounded once
   float o[HC];
 #pragma unroll
@@ -306,7 +355,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
   // Runs key tiles list(0) .. list(count - 1) through the pipeline (every role calls it with the
   // same list).
   auto run = [&](int count, auto list) {
-    if (warp == 9) {
+    if (warp == ATC_TMA_WARP) {
       // ------------------------------------------------ producer: the k and v piece tiles by TMA,
       // k one tile ahead of v (k(i + 1) is needed by the score MMAs before v(i) by the p v MMAs)
       if ((tid & 31) == 0) {
@@ -355,7 +404,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
           settle(sm.v_full, nv);
         }
       }
-    } else if (warp == 8) {
+    } else if (warp == ATC_MMA_WARP) {
       // ------------------------------------------------ MMA issuer: S one tile ahead of p v
       if ((tid & 31) == 0) {
         auto issue_s = [&](uint32_t sq) {
@@ -373,12 +422,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
           const uint32_t sq = seq + i, b = sq & 1;
           if (i + 1 < count && !issue_s(sq + 1)) break;
           if (!mbar_wait(&sm.v_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
-          if (!mbar_wait(&sm.p_full, sq & 1, abort_flag, ATC_TIMEOUT_NS)) break;
+          if (!mbar_wait(&sm.p_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
           if (!mbar_wait(&sm.o_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
           tc_fence_after();
-          atc_mma(tmem + 128 + 64 * b, &sm.p[0][0], sizeof(sm.p[0]), &sm.vt[b][0][0], sizeof(sm.vt[0][0]));
+          atc_mma_ts(tmem + 128 + 64 * b, tmem + ATC_PCOL + ATC_PCOLS * b, &sm.vt[b][0][0], sizeof(sm.vt[0][0]));
           mma_commit(&sm.o_full[b]);
-          mma_commit(&sm.p_empty);
+          mma_commit(&sm.p_empty[b]);
           mma_commit(&sm.v_empty[b]);
         }
       }
@@ -391,7 +440,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
         if (!mbar_wait(&sm.o_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) return;
         tc_fence_after();
         uint32_t raw[HC];
-        tmem_ld_32x32b_x32(tmem + lane_base + 128 + 64 * b + HC * chalf, raw);
+        atc_tmem_ld(tmem + lane_base + 128 + 64 * b + HC * cg, raw);
         tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < HC; ++c) o[c] += __uint_as_float(raw[c]);
@@ -405,7 +454,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       auto fetch_mask = [&](int i) {
         mk_on = false;
         if (mp == nullptr || i >= count || r >= p.tq) return;
-        const int kb = list(i), k0 = kb * ATC_BK + HC * chalf;
+        const int kb = list(i), k0 = kb * ATC_BK + HC * cg;
         if (sm.zmask[half][kb]) return;
         mk_on = true;
         const float* mrow = mp + int64_t(r) * p.ms[2];
@@ -423,13 +472,13 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
       fetch_mask(0);
       for (int i = 0; i < count; ++i) {
         const uint32_t sq = seq + i, b = sq & 1;
-        const int kb = list(i), k0 = kb * ATC_BK + HC * chalf;   // this thread's first column
+        const int kb = list(i), k0 = kb * ATC_BK + HC * cg;   // this thread's first column
         float s[HC];
         if (!mbar_wait(&sm.s_full[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
         tc_fence_after();
         {
           uint32_t raw[HC];
-          tmem_ld_32x32b_x32(tmem + lane_base + 64 * b + HC * chalf, raw);
+          atc_tmem_ld(tmem + lane_base + 64 * b + HC * cg, raw);
           tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < HC; ++c) s[c] = __uint_as_float(raw[c]);
@@ -455,20 +504,24 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
         float rmax = -INFINITY;
 #pragma unroll
         for (int c = 0; c < HC; ++c) rmax = fmaxf(rmax, s[c]);
-        // the other half of the row's maximum
-        sm.xmax[b][chalf][srow] = rmax;
+        // the row's maximum over the column groups
+        sm.xmax[b][cg][srow] = rmax;
         mbar_arrive(&sm.mx_bar[b]);
         if (!mbar_wait_spin(&sm.mx_bar[b], (sq >> 1) & 1, abort_flag, ATC_TIMEOUT_NS)) break;
-        rmax = fmaxf(rmax, sm.xmax[b][chalf ^ 1][srow]);
+#pragma unroll
+        for (int g = 0; g < ATC_CG; ++g) rmax = fmaxf(rmax, sm.xmax[b][g][srow]);
         const float mnew = fmaxf(m, rmax);
         const bool dead = mnew == -INFINITY;   // no key of the row so far can carry weight
         const float mlnew = __fmul_rn(mnew, ATC_LOG2E);
         const float corr = dead ? 1.0f : atc_ex2(__fsub_rn(ml, mlnew));
         m = mnew;
         ml = mlnew;
-        // e^(s - m) piece by piece into the p tiles once the previous p v has read them
-        if (!mbar_wait(&sm.p_empty, (sq & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
+        // e^(s - m) piece by piece into this tile's p buffer in TMEM once the p v two tiles back has
+        // read it: the thread's 32 keys are 16 columns of each piece (two bf16 per column)
+        if (!mbar_wait(&sm.p_empty[b], ((sq >> 1) & 1) ^ 1, abort_flag, ATC_TIMEOUT_NS)) break;
+        tc_fence_after();
         float rsum = 0.0f;
+        const uint32_t pcol = tmem + lane_base + ATC_PCOL + ATC_PCOLS * b + (HC / 2) * cg;
 #pragma unroll
         for (int ch = 0; ch < HC / 8; ++ch) {
           float x[8];
@@ -477,10 +530,14 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
             x[e] = dead ? 0.0f : atc_ex2(fmaf(s[8 * ch + e], ATC_LOG2E, -mlnew));
             rsum += x[e];
           }
-          atc_store8(&sm.p[0][0], sizeof(sm.p[0]), srow, (HC / 8) * chalf + ch, x);
+          uint4 w[ATC_PIECES];
+          atc_pack8(x, w);
+#pragma unroll
+          for (int pc = 0; pc < ATC_PIECES; ++pc) tmem_st_32x32b_x4(pcol + pc * (ATC_BK / 2) + 4 * ch, w[pc]);
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&sm.p_full);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[b]);
         l = fmaf(l, corr, rsum);
         fetch_mask(i + 1);
         // the previous tile's p v (at the previous maximum), then this tile's rescale
@@ -520,20 +577,23 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
     if (sm.n_main > 0) run(sm.n_main, [&](int i) { return static_cast<int>(sm.tiles[i]); });
   }
   // the row's sum: the two halves' partial sums (both rescaled by the same maxima)
-  if (tid < ATC_SOFTMAX) sm.xl[chalf][srow] = l;
+  if (tid < ATC_SOFTMAX) sm.xl[cg][srow] = l;
   __syncthreads();
   const bool live = !*abort_flag;
   float* obase = p.out != nullptr ? p.out + b0 * p.os[0] + b1 * p.os[1] : nullptr;
-  // f32 output rows staged in shared memory (the p tiles' space, idle now) and stored coalesced
+  // f32 output rows staged in shared memory and stored coalesced
   constexpr int OST = ATC_DH + 4;   // staged row stride in floats
-  static_assert(sizeof(AtcSmem::p) >= ATC_BQ * OST * sizeof(float), "staging space");
-  float* stage = reinterpret_cast<float*>(&sm.p[0][0]);
+  // (the k tiles' space: every score MMA has completed once the last p v tile has been added)
+  static_assert(sizeof(AtcSmem::k) >= ATC_BQ * OST * sizeof(float), "staging space");
+  float* stage = reinterpret_cast<float*>(&sm.k[0][0][0]);
   const bool ostage = obase != nullptr && p.os[3] == 1 && ((p.os[0] | p.os[1] | p.os[2]) & 3) == 0 &&
                       (reinterpret_cast<uintptr_t>(obase) & 15) == 0;
   if (tid < ATC_SOFTMAX && live) {
     if (r < p.tq) {
       // o / l: the product with the rounded reciprocal and one residual correction (Markstein)
-      const float lsum = __fadd_rn(sm.xl[0][srow], sm.xl[1][srow]);
+      float lsum = sm.xl[0][srow];
+#pragma unroll
+      for (int g = 1; g < ATC_CG; ++g) lsum = __fadd_rn(lsum, sm.xl[g][srow]);
       const float rl = __frcp_rn(lsum);
 #pragma unroll
       for (int c = 0; c < HC; ++c) {
@@ -544,12 +604,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
     if (ostage) {
 #pragma unroll
       for (int c = 0; c < HC; c += 4)
-        *reinterpret_cast<float4*>(stage + srow * OST + HC * chalf + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+        *reinterpret_cast<float4*>(stage + srow * OST + HC * cg + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
     }
     if (r < p.tq) {
 #pragma unroll
       for (int c = 0; c < HC; ++c) {
-        const int d = HC * chalf + c;
+        const int d = HC * cg + c;
         if (obase != nullptr && !ostage) obase[int64_t(r) * p.os[2] + int64_t(d) * p.os[3]] = o[c];
         if (p.out_i8 != nullptr)
           p.out_i8[b0 * p.is[0] + b1 * p.is[1] + int64_t(r) * p.is[2] + int64_t(d) * p.is[3]] =
@@ -580,7 +640,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
   if (tid == 0 && *abort_flag) atomicExch(p.err, 2);
 }
