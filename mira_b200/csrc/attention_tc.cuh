@@ -13,17 +13,17 @@
 // 128 query rows walks the key tiles of 64 keys as a pipeline: one thread loads the k and v piece
 // tiles with TMA (128-byte swizzle; k and v in separate two-stage rings, k one tile ahead, since a k
 // tile is free as soon as its score MMAs are done), one thread issues the 24 MMAs of a score tile
-// S = q k^T into one of two TMEM buffers ahead of the softmax, and the eight softmax warps (two
-// threads per query row, TMEM lane i, each with 32 of the tile's columns; they swap their row
+// S = q k^T into one of two TMEM buffers ahead of the softmax, and sixteen softmax warps (four
+// threads per query row, TMEM lane i, each with 16 of the tile's columns; they swap their row
 // maxima through shared memory) read their rows, apply the scale step and the mask (loaded a tile
 // ahead), update the running maximum and the rescaled partial sums as the f32 kernel does, with
 // e^(s - m) evaluated as 2^(s log2(e) - m log2(e)) by the ex2.approx instruction (a few ulp), and
-// write the probabilities' pieces as the A operand of the 24 MMAs of O_tile = p v (two TMEM
-// buffers), which they add to their f32 output rows one tile later, while the next tile's softmax
-// runs.  The output rows are divided by the sums (reciprocal and one residual correction) and
-// stored through shared memory as whole rows.  Key tiles whose mask is all strongly negative are
-// skipped under the f32 kernel's certificate (|scale| ||q_i||_1 max|k| + tile_max - m_i < -110
-// for every row; the tiles some row cannot skip are processed at the end).
+// store the probabilities' pieces into one of two TMEM p buffers, the A operand of the 24 MMAs of
+// O_tile = p v (two TMEM buffers), which they add to their f32 output rows one tile later, while
+// the next tile's softmax runs.  The output rows are divided by the sums (reciprocal and one
+// residual correction) and stored through shared memory as whole rows.  Key tiles whose mask is
+// all strongly negative are skipped under the f32 kernel's certificate (|scale| ||q_i||_1 max|k| +
+// tile_max - m_i < -110 for every row; the tiles some row cannot skip are processed at the end).
 #pragma once
 #include <cuda_bf16.h>
 #include "qgemm_sm100.cuh"
@@ -32,8 +32,8 @@
 namespace mira {
 
 constexpr int ATC_BQ = 128, ATC_BK = 64, ATC_DH = 64, ATC_PIECES = 3;
-// warps 0-7 softmax (thread t: query row t % 128 = TMEM lane, columns 32 (t / 128) .. + 31), warp 8
-// issues the MMAs, warp 9 the TMA loads
+// warps 0 .. 4 ATC_CG - 1 softmax (thread t: query row t % 128 = TMEM lane, columns HC (t / 128) ..
+// + HC - 1 with HC = 64 / ATC_CG), then one warp that issues the MMAs and one for the TMA loads
 constexpr int ATC_CG = 4;                                   // threads (column groups) per query row
 constexpr int ATC_SOFTMAX = ATC_BQ * ATC_CG, ATC_THREADS = ATC_SOFTMAX + 64;
 constexpr int ATC_MMA_WARP = ATC_SOFTMAX / 32, ATC_TMA_WARP = ATC_MMA_WARP + 1;
