@@ -379,7 +379,7 @@ PROFILE_CASES = ("gemm8192", "conv_l1", "conv_l1_cp", "dwconv_l1", "attention_q1
                  "decode_step", "attention_prefill", "layernorm_decode", "layernorm_prefill")
 
 
-def profile_case(name: str, reps: int = 3) -> None:
+def profile_case(name: str, reps: int = 3, timed: bool = False) -> None:
     """One kernel on a bounded, seeded case, launched `reps` times, for ncu captures (the inputs are
     larger than L2 where the kernel is HBM-bound; a few hundred MB on the device):
       gemm8192      mira_cuda_qgemm 8192^3 on config-2 operands, row/col scales + bias, f32 out
@@ -397,7 +397,8 @@ def profile_case(name: str, reps: int = 3) -> None:
       decode_step   `reps` eager steps of the config-5 decode (batch 64, 1024-row caches): every
                     launch of a step, for a launch list
       attention_prefill  the prefill's fused attention: 8 sequences x 12 heads x 1024 tokens, d_head 64,
-                    causal mask with exact tile skipping
+                    causal mask with exact tile skipping (tensor-core kernel and its piece pass;
+                    MIRA_CUDA_ATTENTION=simt selects the f32 FMA kernel)
       layernorm_decode  a decode step's layernorm: 64 rows x 768, f32 and int8 out
       layernorm_prefill a prefill layernorm: 65536 rows x 768 (201 MB), int8 out"""
     from mira_b200 import _lib, kernels as K
@@ -515,8 +516,28 @@ def profile_case(name: str, reps: int = 3) -> None:
         K.absmax_f32((b0, b1, t, dh), K.View(k, st), km)
         desc = K.Attn(b0, b1, t, t, dh, K.View(q, st), K.View(k, st), K.View(v, st), "mul", 0.125,
                       K.View(mb, (0, 0, t, 1)), tm, km, tz, out=K.View(out, st))
+        # the planner's workspace selects the tensor-core kernel (MIRA_CUDA_ATTENTION=simt: the f32 one)
+        nws = K.attention_workspace(b0, b1, t, t, dh)
+        if nws > 0:
+            ws = DB(nws)
+            desc.workspace, desc.workspace_bytes = ws, nws
         for _ in range(reps):
             K.attention_f32(desc)
+        if timed:   # CUDA events around 20 calls on the library stream, after the calls above
+            a, b = C.c_void_p(), C.c_void_p()
+            _lib.call("mira_cuda_event_create", C.byref(a))
+            _lib.call("mira_cuda_event_create", C.byref(b))
+            _lib.call("mira_cuda_sync")
+            _lib.call("mira_cuda_event_record", a)
+            for _ in range(20):
+                K.attention_f32(desc)
+            _lib.call("mira_cuda_event_record", b)
+            _lib.call("mira_cuda_sync")
+            ms = C.c_float()
+            _lib.call("mira_cuda_event_elapsed", a, b, C.byref(ms))
+            print(json.dumps({"case": name, "us_per_call": ms.value / 20 * 1e3, "calls": 20, "warmup": reps,
+                              "kernel": "simt" if os.environ.get("MIRA_CUDA_ATTENTION") == "simt" else
+                              ("tensor-core" if nws > 0 else "simt")}))
     elif name in ("layernorm_decode", "layernorm_prefill"):
         rows, d = (64, 768) if name == "layernorm_decode" else (65536, 768)
         x = DB.from_array(rng.standard_normal((rows, d), dtype=np.float32))
@@ -882,9 +903,11 @@ def main() -> None:
                     help="compute a conv whose only consumer is a max pool inside the pooling kernel")
     ap.add_argument("--profile-case", choices=PROFILE_CASES, default=None,
                     help="launch one kernel on a bounded case a few times (for ncu) and exit")
+    ap.add_argument("--time-case", action="store_true",
+                    help="with --profile-case attention_prefill: also time 20 calls with CUDA events (not under ncu)")
     args = ap.parse_args()
     if args.profile_case:
-        profile_case(args.profile_case)
+        profile_case(args.profile_case, reps=5 if args.time_case else 3, timed=args.time_case)
         return
     args.warmup = max(args.warmup, 3)
     if args.workload == "decode":

@@ -63,6 +63,32 @@ def test_static_scratch_splitk_matches_workspace_splitk_twice_in_a_row(cuda_devi
         assert np.array_equal(got_s.view(np.uint32), want.view(np.uint32))
 
 
+def test_static_scratch_call_leaves_free_device_memory_unchanged(cuda_device):
+    """The property these callers need: after the first call on a device (which looks up the scratch
+    array's address), a call takes no device memory, so the device's free bytes stay the same."""
+    import torch
+    from mira_b200 import kernels as K
+    from mira_b200.device import DeviceBuffer as DB
+    M, N, Kd = 16, 4096, 4096
+    bufs, lda, _, out_scale = _case(K, DB, M, N, Kd, 4)
+    y, yq = DB(M * N * 4), DB(M * K.round_up(N, 16), zero=True)
+    dq = K.dequant_channel(bufs["s64"], bufs["hi"], bufs["lo"])
+    epi = K.Epi([K.Step("add", "channel", ptr=bufs["bias"]), K.Step("relu")], out_f32=y, ld_f32=N, out_i8=yq,
+                ld_i8=K.round_up(N, 16), out_scale=out_scale).struct()
+    from mira_b200 import _lib
+
+    def call():
+        _lib.call("mira_cuda_qgemm_splitk_static", M, N, Kd, C.c_void_p(bufs["A"].ptr), lda, C.c_void_p(bufs["B"].ptr),
+                  lda, C.byref(dq), C.byref(epi))
+        _lib.call("mira_cuda_sync")
+
+    call()
+    free0 = torch.cuda.mem_get_info(cuda_device)[0]
+    for _ in range(3):
+        call()
+    assert torch.cuda.mem_get_info(cuda_device)[0] == free0
+
+
 def test_static_scratch_rejects_shapes_beyond_its_size(cuda_device):
     from mira_b200 import _lib
     from mira_b200 import kernels as K
