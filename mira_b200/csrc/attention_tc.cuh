@@ -194,39 +194,75 @@ __device__ __forceinline__ void atc_mma(uint32_t d_tmem, const uint8_t* a_tiles,
 }
 
 // k and v of one key tile of one (batch0, batch1) entry into pieces: kpc[((bh * 3 + piece) * tkp +
-// key) * 64 + d] and vtc[((bh * 3 + piece) * 64 + d) * tkp + key] (bf16), keys past tk 0.
-__global__ void __launch_bounds__(256) attention_pieces_kernel(const AttnParams p, int tkp, uint16_t* __restrict__ kpc,
-                                                               uint16_t* __restrict__ vtc) {
-  const int k0 = blockIdx.x * ATC_BK;
+// key) * 64 + d] and vtc[((bh * 3 + piece) * 64 + d) * tkp + key] (bf16), keys past tk 0.  Every
+// thread issues all its loads before the first conversion; v goes through shared memory so that the
+// transposed rows leave as whole 128-byte segments.
+constexpr int ATC_PIECE_THREADS = 256;
+__global__ void __launch_bounds__(ATC_PIECE_THREADS) attention_pieces_kernel(const AttnParams p, int tkp,
+                                                                             uint16_t* __restrict__ kpc,
+                                                                             uint16_t* __restrict__ vtc) {
+  __shared__ float vs[ATC_BK][ATC_DH + 1];   // [key][d], padded against bank conflicts
+  const int k0 = blockIdx.x * ATC_BK, tid = threadIdx.x;
   const int64_t b1 = blockIdx.y, b0 = blockIdx.z, bh = b0 * gridDim.y + b1;
   const float* kp = p.k + b0 * p.ks[0] + b1 * p.ks[1];
   const float* vp = p.v + b0 * p.vs[0] + b1 * p.vs[1];
-  for (int task = threadIdx.x; task < ATC_BK * 8; task += blockDim.x) {
-    const int j = task >> 3, ch = task & 7;   // k: key k0 + j, d 8 ch .. 8 ch + 7
-    float x[8];
-    if (k0 + j < p.tk && p.vec) {
-      const float4* src = reinterpret_cast<const float4*>(kp + int64_t(k0 + j) * p.ks[2] + 8 * ch);
-      const float4 a = __ldg(src), c = __ldg(src + 1);
-      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+  constexpr int KT = ATC_BK * 8 / ATC_PIECE_THREADS;    // k tasks per thread: (key, 8 values of d)
+  constexpr int VT = ATC_BK * 16 / ATC_PIECE_THREADS;   // v loads per thread: (key, 4 values of d)
+  float xk[KT][8];
+  float4 xv[VT];
+#pragma unroll
+  for (int t = 0; t < KT; ++t) {
+    const int task = tid + t * ATC_PIECE_THREADS, j = task >> 3, ch = task & 7;
+    const bool live = k0 + j < p.tk;
+    const float* src = kp + int64_t(k0 + j) * p.ks[2];
+    if (live && p.vec) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(src + 8 * ch));
+      const float4 c = __ldg(reinterpret_cast<const float4*>(src + 8 * ch + 4));
+      xk[t][0] = a.x; xk[t][1] = a.y; xk[t][2] = a.z; xk[t][3] = a.w;
+      xk[t][4] = c.x; xk[t][5] = c.y; xk[t][6] = c.z; xk[t][7] = c.w;
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        x[e] = k0 + j < p.tk ? __ldg(kp + int64_t(k0 + j) * p.ks[2] + int64_t(8 * ch + e) * p.ks[3]) : 0.0f;
+      for (int e = 0; e < 8; ++e) xk[t][e] = live ? __ldg(src + int64_t(8 * ch + e) * p.ks[3]) : 0.0f;
     }
+  }
+#pragma unroll
+  for (int t = 0; t < VT; ++t) {
+    const int task = tid + t * ATC_PIECE_THREADS, j = task >> 4, c4 = task & 15;
+    const bool live = k0 + j < p.tk;
+    const float* src = vp + int64_t(k0 + j) * p.vs[2];
+    if (live && p.vec) {
+      xv[t] = __ldg(reinterpret_cast<const float4*>(src + 4 * c4));
+    } else {
+      xv[t].x = live ? __ldg(src + int64_t(4 * c4) * p.vs[3]) : 0.0f;
+      xv[t].y = live ? __ldg(src + int64_t(4 * c4 + 1) * p.vs[3]) : 0.0f;
+      xv[t].z = live ? __ldg(src + int64_t(4 * c4 + 2) * p.vs[3]) : 0.0f;
+      xv[t].w = live ? __ldg(src + int64_t(4 * c4 + 3) * p.vs[3]) : 0.0f;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < VT; ++t) {
+    const int task = tid + t * ATC_PIECE_THREADS, j = task >> 4, c4 = task & 15;
+    vs[j][4 * c4] = xv[t].x;
+    vs[j][4 * c4 + 1] = xv[t].y;
+    vs[j][4 * c4 + 2] = xv[t].z;
+    vs[j][4 * c4 + 3] = xv[t].w;
+  }
+#pragma unroll
+  for (int t = 0; t < KT; ++t) {
+    const int task = tid + t * ATC_PIECE_THREADS, j = task >> 3, ch = task & 7;
     uint4 w[ATC_PIECES];
-    atc_pack8(x, w);
+    atc_pack8(xk[t], w);
 #pragma unroll
     for (int pc = 0; pc < ATC_PIECES; ++pc)
       *reinterpret_cast<uint4*>(kpc + ((bh * ATC_PIECES + pc) * tkp + k0 + j) * ATC_DH + 8 * ch) = w[pc];
   }
-  for (int task = threadIdx.x; task < ATC_DH * 8; task += blockDim.x) {
-    const int n = task & (ATC_DH - 1), kc = task >> 6;   // v: d n, keys k0 + 8 kc .. + 7
+  __syncthreads();
+#pragma unroll
+  for (int t = 0; t < KT; ++t) {
+    const int task = tid + t * ATC_PIECE_THREADS, n = task >> 3, kc = task & 7;   // v: d n, keys 8 kc .. + 7
     float x[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int j = k0 + 8 * kc + e;
-      x[e] = j < p.tk ? __ldg(vp + int64_t(j) * p.vs[2] + int64_t(n) * p.vs[3]) : 0.0f;
-    }
+    for (int e = 0; e < 8; ++e) x[e] = vs[8 * kc + e][n];
     uint4 w[ATC_PIECES];
     atc_pack8(x, w);
 #pragma unroll
@@ -607,13 +643,23 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attention_tc_kernel(const __gr
         *reinterpret_cast<float4*>(stage + srow * OST + HC * cg + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
     }
     if (r < p.tq) {
+      int8_t* qrow = p.out_i8 != nullptr ? p.out_i8 + b0 * p.is[0] + b1 * p.is[1] + int64_t(r) * p.is[2] : nullptr;
+      // the int8 row's HC bytes as whole 4-byte words where they are contiguous and aligned
+      const bool qvec = qrow != nullptr && p.is[3] == 1 && (reinterpret_cast<uintptr_t>(qrow + HC * cg) & 3) == 0;
+      if (qvec) {
+#pragma unroll
+        for (int c = 0; c < HC; c += 4) {
+          uint32_t w = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) w |= (static_cast<uint32_t>(quant_byte(o[c + e], p.q8)) & 0xffu) << (8 * e);
+          *reinterpret_cast<uint32_t*>(qrow + HC * cg + c) = w;
+        }
+      }
 #pragma unroll
       for (int c = 0; c < HC; ++c) {
         const int d = HC * cg + c;
         if (obase != nullptr && !ostage) obase[int64_t(r) * p.os[2] + int64_t(d) * p.os[3]] = o[c];
-        if (p.out_i8 != nullptr)
-          p.out_i8[b0 * p.is[0] + b1 * p.is[1] + int64_t(r) * p.is[2] + int64_t(d) * p.is[3]] =
-              static_cast<int8_t>(quant_byte(o[c], p.q8) & 0xff);
+        if (qrow != nullptr && !qvec) qrow[int64_t(d) * p.is[3]] = static_cast<int8_t>(quant_byte(o[c], p.q8) & 0xff);
       }
     }
   }

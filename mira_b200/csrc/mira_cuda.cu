@@ -1804,7 +1804,7 @@ static int launch_attention_tc(DeviceState* dev, const AttnParams& p, int64_t b0
   const int64_t bh = b0 * b1;
   uint16_t* kpc = static_cast<uint16_t*>(ws);
   uint16_t* vtc = kpc + bh * ATC_PIECES * tkp * ATC_DH;
-  attention_pieces_kernel<<<dim3(unsigned(tkp / ATC_BK), unsigned(b1), unsigned(b0)), 256, 0, dev->stream>>>(
+  attention_pieces_kernel<<<dim3(unsigned(tkp / ATC_BK), unsigned(b1), unsigned(b0)), ATC_PIECE_THREADS, 0, dev->stream>>>(
       p, int(tkp), kpc, vtc);
   const int rc = after_launch("attention_pieces_kernel");
   if (rc != MIRA_CUDA_OK) return rc;
