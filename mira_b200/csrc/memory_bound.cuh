@@ -717,11 +717,17 @@ __device__ __forceinline__ void qdw_dequant(const int32_t (&acc)[T][4], const Qd
 }
 
 // 3 x 3, stride S, dilation 1: 4 channels x OXT output columns per thread (as dwconv3x3_kernel).
+// The taps run on dp4a: per input row, the NIN pixels' words (4 channels each) are transposed into
+// one byte stream per channel (x[0][c], x[1][c], ...), the three taps of output column t are the
+// stream's bytes S t .. S t + 2 (a funnel shift), and the row's three weights of channel c are one
+// word (w[i][0][c], w[i][1][c], w[i][2][c], 0): one dp4a adds the three products of a row exactly
+// (the fourth byte is multiplied by 0).  The int32 sums are the same as tap-by-tap products.
 template <int S, int OXT>
-__global__ void __launch_bounds__(256, 4) qdwconv3x3_kernel(const int8_t* __restrict__ x, int64_t ldx,
+__global__ void __launch_bounds__(256, 3) qdwconv3x3_kernel(const int8_t* __restrict__ x, int64_t ldx,
                                                          const uint32_t* __restrict__ wt, const QdwScales sc,
                                                          const __grid_constant__ DwParams p) {
   constexpr int NIN = (OXT - 1) * S + 3;
+  static_assert(NIN >= 5 && NIN <= 6, "pixel window of one thread");
   const int c4 = p.c >> 2;
   const int ox0 = (blockIdx.x * blockDim.y + threadIdx.y) * OXT;
   if (ox0 >= p.ow) return;
@@ -730,40 +736,62 @@ __global__ void __launch_bounds__(256, 4) qdwconv3x3_kernel(const int8_t* __rest
     const int img = static_cast<int>(orow / p.oh);
     const int oy = static_cast<int>(orow - int64_t(img) * p.oh);
     for (int cg = threadIdx.x; cg < c4; cg += blockDim.x) {
-      int32_t acc[OXT][4];
-#pragma unroll
-      for (int t = 0; t < OXT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
+      // all three input rows' words in flight at once
+      uint32_t xin[3][NIN];
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
         const int iy = oy * S - p.ph + i;
         const bool row_in = iy >= 0 && iy < p.h;
         const int8_t* xrow = x + (int64_t(img) * p.h + (row_in ? iy : 0)) * p.w * ldx + 4 * cg;
-        uint32_t xin[NIN];
 #pragma unroll
         for (int u = 0; u < NIN; ++u) {
           const int ix = ox0 * S - p.pw + u;
-          xin[u] = row_in && ix >= 0 && ix < p.w ? __ldg(reinterpret_cast<const uint32_t*>(xrow + int64_t(ix) * ldx)) : 0u;
+          xin[i][u] = row_in && ix >= 0 && ix < p.w ? __ldg(reinterpret_cast<const uint32_t*>(xrow + int64_t(ix) * ldx)) : 0u;
         }
-        int32_t wv[3][4];
+      }
+      int32_t acc[OXT][4];
 #pragma unroll
-        for (int j = 0; j < 3; ++j) {
-          const uint32_t wword = __ldg(wt + (i * 3 + j) * c4 + cg);
+      for (int t = 0; t < OXT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) wv[j][e] = sext_byte(wword, e);
+      for (int i = 0; i < 3; ++i) {
+        // weights of row i, one word per channel: (w[i][0][c], w[i][1][c], w[i][2][c], 0)
+        const uint32_t w0 = __ldg(wt + (i * 3 + 0) * c4 + cg);
+        const uint32_t w1 = __ldg(wt + (i * 3 + 1) * c4 + cg);
+        const uint32_t w2 = __ldg(wt + (i * 3 + 2) * c4 + cg);
+        int32_t wr[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t t01 = __byte_perm(w0, w1, c | ((4 + c) << 4));
+          wr[c] = static_cast<int32_t>(__byte_perm(t01, w2, 0x0010u | ((4 + c) << 8)) & 0x00ffffffu);
+        }
+        // channel byte streams: lo[c] = pixels 0..3 of channel c, hi[c] = pixels 4.. of channel c
+        const uint32_t* xr = xin[i];
+        const uint32_t a01l = __byte_perm(xr[0], xr[1], 0x5140), a01h = __byte_perm(xr[0], xr[1], 0x7362);
+        const uint32_t a23l = __byte_perm(xr[2], xr[3], 0x5140), a23h = __byte_perm(xr[2], xr[3], 0x7362);
+        uint32_t lo[4], hi[4];
+        lo[0] = __byte_perm(a01l, a23l, 0x5410);
+        lo[1] = __byte_perm(a01l, a23l, 0x7632);
+        lo[2] = __byte_perm(a01h, a23h, 0x5410);
+        lo[3] = __byte_perm(a01h, a23h, 0x7632);
+        if constexpr (NIN == 6) {
+          const uint32_t b45l = __byte_perm(xr[4], xr[5], 0x5140), b45h = __byte_perm(xr[4], xr[5], 0x7362);
+          hi[0] = b45l;
+          hi[1] = b45l >> 16;
+          hi[2] = b45h;
+          hi[3] = b45h >> 16;
+        } else {
+          hi[0] = xr[4];
+          hi[1] = xr[4] >> 8;
+          hi[2] = xr[4] >> 16;
+          hi[3] = xr[4] >> 24;
         }
 #pragma unroll
-        for (int u = 0; u < NIN; ++u) {
-          int32_t xv[4];
+        for (int t = 0; t < OXT; ++t)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) xv[e] = sext_byte(xin[u], e);
-#pragma unroll
-          for (int t = 0; t < OXT; ++t) {
-            const int j = u - t * S;
-            if (j < 0 || j > 2) continue;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[t][e] += xv[e] * wv[j][e];
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t taps = t == 0 ? lo[c] : __funnelshift_r(lo[c], hi[c], 8 * S * t);
+            acc[t][c] = __dp4a(static_cast<int32_t>(taps), wr[c], acc[t][c]);
           }
-        }
       }
       float v[OXT][4];
       qdw_dequant<OXT>(acc, sc, cg, v);
