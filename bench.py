@@ -374,7 +374,7 @@ def gemm_sweep(peak_tops: float | None) -> dict:
                     "seeded; operand sets cycled (more than twice L2 between reuses)"}
 
 
-PROFILE_CASES = ("gemm8192", "conv_l1", "conv_l1_cp", "dwconv_l1", "attention_q1", "quantize_rows", "stem", "stem_pool",
+PROFILE_CASES = ("gemm8192", "conv_l1", "conv_l1_cp", "dwconv_l1", "qdwconv_l1", "attention_q1", "quantize_rows", "stem", "stem_pool",
                  "maxpool_stem",
                  "decode_step", "attention_prefill", "layernorm_decode", "layernorm_prefill")
 
@@ -386,6 +386,7 @@ def profile_case(name: str, reps: int = 3, timed: bool = False) -> None:
       conv_l1       ResNet-18 layer-1 3x3 conv, batch 256, 56x56x64 -> 64, bias + relu, int8 + f32 out
       conv_l1_cp    the same conv reading and writing int8 in the chunk-planar layout (MIRA_LAYOUT_CP)
       dwconv_l1     MobileNetV2's first depthwise layer, batch 96, 112x112x32, bias + relu6, int8 out
+      qdwconv_l1    the same layer in the opt-in int8 depthwise mode (int8 in, exact sums), int8 out
       attention_q1  a decode step's attention: 64 sequences x 12 heads, 1024 cached rows, d_head 64
       quantize_rows the transformer's activation quantization, 65536 x 768 f32 -> int8
       stem          ResNet-18's stem: NCHW f32 64 x 3 x 224 x 224 quantized into the row-expanded layout,
@@ -452,6 +453,17 @@ def profile_case(name: str, reps: int = 3, timed: bool = False) -> None:
                      K.Step("minimum", "scalar", scalar=6.0)], out_i8=q, ld_i8=K.round_up(c, 16), out_scale=6.0 / 127)
         for _ in range(reps):
             K.dwconv2d(x, n, h, h, c, wt, 3, 3, (1, 1), (1, 1), (1, 1), epi)
+    elif name == "qdwconv_l1":
+        n, h, c = 96, 112, 32
+        x = DB.from_array(rng.integers(-127, 128, (n, h, h, c)).astype(np.int8))
+        wq = DB.from_array(rng.integers(-127, 128, (9, c)).astype(np.int8))
+        keep = [DB.from_array(a) for a in K.scale_arrays(0.02, rng.uniform(1e-3, 1e-2, c).astype(np.float32))]
+        bias = DB.from_array(K.pad_channels(rng.standard_normal(c).astype(np.float32)))
+        q = DB(n * h * h * K.round_up(c, 16))
+        epi = K.Epi([K.Step("add", "channel", ptr=bias), K.Step("maximum", "scalar", scalar=0.0),
+                     K.Step("minimum", "scalar", scalar=6.0)], out_i8=q, ld_i8=K.round_up(c, 16), out_scale=6.0 / 127)
+        for _ in range(reps):
+            K.qdwconv2d(x, c, n, h, h, c, wq, 3, 3, (1, 1), (1, 1), (1, 1), K.dequant_channel(*keep), epi)
     elif name == "attention_q1":
         b, hd, tk, dh = 64, 12, 1024, 64
         q = DB.from_array(rng.standard_normal((b, hd, 1, dh), dtype=np.float32))
